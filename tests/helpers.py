@@ -1,0 +1,69 @@
+"""Shared builders for tests: small seeded models quantized by the oracle (CPU)
+or by the library (GPU), over identical fp32 weights."""
+import numpy as np
+
+import oracle
+from tinybrain_b200.runtime import (LinearLayerWeights, ModelConfig, ModelWeights, QuantizedTensor,
+                                    SeededGenerator, TransformerLayerWeights)
+
+
+def oracle_quantize(w, mode, gs=32):
+    if mode == "perChannel":
+        q, s = oracle.quantize_int8_per_channel(w)
+        return QuantizedTensor(w.shape, q, s, "perChannel", 0, None)
+    p, s, z = oracle.quantize_int4_group(w, gs)
+    return QuantizedTensor(w.shape, p, s, "int4", gs, z)
+
+
+def small_llama(cfg: ModelConfig, seed=0, mode="perChannel", gs=32, quantizer=None, std=0.02):
+    """LLaMA-shaped model drawn like tinybrain_b200.synthetic.make_llama_model."""
+    quantizer = quantizer or (lambda w: oracle_quantize(w, mode, gs))
+    g = SeededGenerator(seed)
+    H, I, V, kvd = cfg.hidden_dim, cfg.intermediate_dim, cfg.vocab_size, cfg.kv_dim
+    emb = g.normal((V, H), 0.0, std)
+    layers = []
+    rng = np.random.default_rng(seed + 100)
+    for _ in range(cfg.num_layers):
+        p = {}
+        for name, shape in (("q", (H, H)), ("k", (H, kvd)), ("v", (H, kvd)), ("o", (H, H)),
+                            ("gate", (H, I)), ("up", (H, I)), ("down", (I, H))):
+            p[name] = LinearLayerWeights(quantizer(g.normal(shape, 0.0, std)))
+        # non-trivial norm weights exercise the fused RMSNorm prologue
+        n1 = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        n2 = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        layers.append(TransformerLayerWeights(query=p["q"], key=p["k"], value=p["v"], output=p["o"],
+                                              gate=p["gate"], up=p["up"], down=p["down"],
+                                              input_norm=n1, post_attention_norm=n2))
+    out = LinearLayerWeights(quantizer(g.normal((H, V), 0.0, std)))
+    fn = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    return ModelWeights(cfg, emb, layers, out, final_norm=fn)
+
+
+def toy_model(cfg: ModelConfig = None, seed=42, quantizer=None):
+    """makeToyModel (ModelWeights.swift:171-244) drawn like synthetic.make_toy_model."""
+    cfg = cfg or ModelConfig(2, 128, 4, 100, 256, 4, 512, "toy")
+    quantizer = quantizer or (lambda w: oracle_quantize(w, "perChannel"))
+    g = SeededGenerator(seed)
+    H, V, kvd = cfg.hidden_dim, cfg.vocab_size, cfg.kv_dim
+    F = 4 * H
+    emb = g.normal((V, H), 0.0, 0.02)
+
+    def proj(n_in, n_out):
+        w = g.normal((n_in, n_out), 0.0, 0.02)
+        b = g.normal((n_out,), 0.0, 0.02)
+        return LinearLayerWeights(quantizer(w), b)
+
+    layers = []
+    for _ in range(cfg.num_layers):
+        q, k, v, o = proj(H, H), proj(H, kvd), proj(H, kvd), proj(H, H)
+        up, down = proj(H, F), proj(F, H)
+        layers.append(TransformerLayerWeights(query=q, key=k, value=v, output=o, up=up, down=down))
+    out = LinearLayerWeights(quantizer(g.normal((H, V), 0.0, 0.02)), np.zeros(V, dtype=np.float32))
+    cfg2 = ModelConfig(cfg.num_layers, H, cfg.num_heads, V, cfg.max_seq_len, cfg.num_kv_heads, F, "toy")
+    return ModelWeights(cfg2, emb, layers, out, final_norm=None)
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))

@@ -1,0 +1,119 @@
+"""Decode-step parity of the whole device path against the CPU oracle.
+
+Logits within relative L2 <= 1e-3; greedy tokens identical to the oracle's
+(the oracle accumulates in fp64; where its top-2 logit gap is below 1e-4 an
+fp32 reordering could legitimately flip the argmax, and the test reports it).
+"""
+import numpy as np
+import pytest
+
+import oracle
+from tests.helpers import rel_l2, small_llama, toy_model
+from tinybrain_b200.runtime import GenerationConfig, ModelConfig, ModelRunner, SamplerConfig
+
+pytestmark = pytest.mark.gpu
+RTOL_L2 = 1e-3
+
+
+def assert_same_tokens(got, want, gaps):
+    for i, (a, b) in enumerate(zip(got, want)):
+        if a != b:
+            assert gaps[i] < 1e-4, f"token {i}: device {a} vs oracle {b} with top-2 gap {gaps[i]}"
+            return
+    assert len(got) == len(want)
+
+
+def small_cfg(**kw):
+    base = dict(num_layers=2, hidden_dim=256, num_heads=8, vocab_size=1000, max_seq_len=128, num_kv_heads=2,
+                intermediate_dim=512)
+    base.update(kw)
+    return ModelConfig(**base)
+
+
+@pytest.mark.parametrize("mode", ["perChannel", "int4"])
+def test_step_logits_and_kv_state(ctx, mode):
+    w = small_llama(small_cfg(), seed=3, mode=mode)
+    r = ModelRunner(w, ctx)
+    o = oracle.OracleModel(w, mode=1)
+    for i, tok in enumerate([5, 17, 999, 0, 512, 3, 3, 77, 100, 42, 7, 8, 9, 10, 11, 12, 13, 14]):
+        logits, am = r.step(tok)
+        ref = o.step(tok)
+        assert rel_l2(logits, ref) <= RTOL_L2, i
+        assert am == int(np.argmax(logits))
+        assert r.kv_cache.length == o.kv_length == i + 1
+        assert r.current_position == o.position
+        assert r.kv_cache.page_allocation_status() == o.page_status()
+    r.reset()
+    o.reset()
+    assert r.kv_cache.length == 0 and r.current_position == 0
+    l1, _ = r.step(5)
+    assert rel_l2(l1, o.step(5)) <= RTOL_L2
+
+
+def test_toy_model_greedy_identity(ctx):
+    w = toy_model()
+    r = ModelRunner(w, ctx)
+    o = oracle.OracleModel(w, mode=1)
+    prompt = [1, 2, 3, 4, 5]
+    want, gaps = o.generate_greedy(prompt, 40)
+    got = r.generate_batch([prompt], 40)[0]
+    assert_same_tokens(got, want, gaps)
+
+
+@pytest.mark.parametrize("mode", ["perChannel", "int4"])
+def test_generate_greedy_identity(ctx, mode):
+    w = small_llama(small_cfg(num_layers=3), seed=4, mode=mode)
+    r = ModelRunner(w, ctx)
+    o = oracle.OracleModel(w, mode=1)
+    prompt = [11, 22, 33, 44, 55, 66, 77, 88, 99, 111, 222, 333, 444, 555, 666, 777, 888]
+    want, gaps = o.generate_greedy(prompt, 48)
+    got = r.generate_batch([prompt], 48)[0]
+    assert_same_tokens(got, want, gaps)
+    assert r.kv_cache.length == len(prompt) - 1 + 48
+
+
+def test_generate_stream_stop_token(ctx):
+    w = small_llama(small_cfg(), seed=5)
+    r = ModelRunner(w, ctx)
+    o = oracle.OracleModel(w, mode=1)
+    want, gaps = o.generate_greedy([1, 2, 3], 20)
+    stop = want[5]
+    outs = list(r.generate_stream([1, 2, 3], GenerationConfig(max_tokens=20, sampler=SamplerConfig(top_k=1),
+                                                              stop_tokens=[stop])))
+    ids = [t.token_id for t in outs]
+    k = want.index(stop)
+    assert ids == want[:k + 1]  # the stop token is yielded, then generation ends
+    assert all(abs(t.probability - 0.9999999) < 1e-6 for t in outs)
+
+
+def test_kv_eviction_parity(ctx):
+    cfg = small_cfg(max_seq_len=48)
+    w = small_llama(cfg, seed=6)
+    r = ModelRunner(w, ctx, max_positions=160)
+    o = oracle.OracleModel(w, mode=1)
+    for i in range(120):
+        tok = (i * 37) % cfg.vocab_size
+        logits, _ = r.step(tok)
+        ref = o.step(tok)
+        assert rel_l2(logits, ref) <= RTOL_L2, i
+        assert r.kv_cache.length == o.kv_length, i
+        assert r.kv_cache.page_allocation_status() == o.page_status(), i
+
+
+def test_batched_sequences_match_independent_runs(ctx):
+    w = small_llama(small_cfg(), seed=7)
+    r = ModelRunner(w, ctx, max_batch=4)
+    prompts = [[1, 2, 3], [10] * 20, [5], [7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 19, 20, 21, 22, 23, 24]]
+    got = r.generate_batch(prompts, 24)
+    for p, g in zip(prompts, got):
+        o = oracle.OracleModel(w, mode=1)
+        want, gaps = o.generate_greedy(p, 24)
+        assert_same_tokens(g, want, gaps)
+
+
+def test_unsupported_sampler_raises(ctx):
+    from tinybrain_b200._lib import TinyBrainError
+    w = small_llama(small_cfg(), seed=8)
+    r = ModelRunner(w, ctx)
+    with pytest.raises(TinyBrainError):
+        list(r.generate_stream([1, 2], GenerationConfig(max_tokens=3, sampler=SamplerConfig(temperature=0.8))))

@@ -1,0 +1,335 @@
+// tb_attention.cu -- single-query decode attention over the HBM paged KV cache.
+//
+// Semantics follow the reference's live CPU path, ModelRunner.swift:519-579:
+// per query head h, kvHead = h / (H/Hkv); scores = (q.k) * 1/sqrt(d); softmax
+// without epsilon; context = sum_j p_j v_j.  Rows of evicted pages read as
+// zeros and are still attended (KVCache.swift:239-253).  The reference's Metal
+// FlashAttention kernel (Shaders/FlashAttention.metal:55-220) is the interface
+// this replaces (AttentionBackend, Backend.swift:205-219), but it works on a
+// contiguous cache; this kernel reads 16-token pages through a page table.
+//
+// Design (sm_100a): grid = (split, kv head, sequence).  A CTA serves all
+// G = H/Hkv query heads of its KV head, so each K/V byte is read once.  One
+// producer warp streams the K and V tiles of each page (16 x d fp32,
+// contiguous) with 1-D bulk copies into an mbarrier ring; four consumer warps
+// compute scores and an online softmax.  Splits write (m, l, acc) partials to
+// scratch; the last CTA of each (sequence, KV head) -- elected with a ticket --
+// combines them in split order (deterministic).
+#include "tb_common.cuh"
+#include "tb_kernels.h"
+
+namespace tb {
+
+namespace {
+
+constexpr int kAttnConsumerWarps = 4;
+constexpr int kAttnThreads = (kAttnConsumerWarps + 1) * 32;
+constexpr int kAttnStages = 4;
+
+template <int G, int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
+    constexpr int TILE = kPageTokens * D;           // floats per K (or V) tile
+    constexpr int DP = 128 / (G * kPageTokens);     // threads per (head, token) score
+    constexpr int CHK = D / DP;                     // dims per score thread
+    constexpr int PVT = G * (D / 4);                // threads active in the PV phase
+    static_assert(DP >= 1 && CHK <= 64, "unsupported head geometry");
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kAttnStages;
+    int* valid = reinterpret_cast<int*>(empty + kAttnStages);            // [stages]
+    float* S = reinterpret_cast<float*>(smem + 128);                    // [2][G][16]
+    float* tiles = reinterpret_cast<float*>(smem + 128 + ((2 * G * kPageTokens * 4 + 127) / 128) * 128);
+    float* flag = S;  // reused after the loop
+
+    const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kAttnStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kAttnConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    pdl_wait();
+
+    const SeqState& sq = p.seq[m];
+    const bool active = p.lens ? true : (sq.active != 0);
+    const int Lq = p.lens ? p.lens[m] : sq.pos + 1;
+    const int npages = active ? (Lq + kPageTokens - 1) / kPageTokens : 0;
+    const int pps = (npages + p.nsplit - 1) / p.nsplit;
+    const int pg0 = min(npages, split * pps);
+    const int pg1 = min(npages, pg0 + pps);
+    const int nun = pg1 - pg0;
+
+    if (warp == kAttnConsumerWarps) {
+        if (lane == 0) {
+            for (int i = 0; i < nun; ++i) {
+                const int st = i % kAttnStages;
+                if (i >= kAttnStages) {
+                    if (!mbar_wait(&empty[st], ((i / kAttnStages) - 1) & 1, p.err)) break;
+                }
+                const int lp = pg0 + i;
+                const int page = p.page_table[(size_t)m * p.ptab_stride + lp];
+                float* kd = tiles + st * 2 * TILE;
+                if (page >= 0) {
+                    valid[st] = 1;
+                    const size_t kbase =
+                        ((((size_t)page * p.num_layers + p.layer) * 2 + 0) * p.Hkv + kvh) * (size_t)TILE;
+                    const size_t vbase =
+                        ((((size_t)page * p.num_layers + p.layer) * 2 + 1) * p.Hkv + kvh) * (size_t)TILE;
+                    mbar_arrive_expect_tx(&full[st], 2u * TILE * 4u);
+                    bulk_g2s(kd, p.kv_pool + kbase, TILE * 4u, &full[st]);
+                    bulk_g2s(kd + TILE, p.kv_pool + vbase, TILE * 4u, &full[st]);
+                } else {
+                    valid[st] = 0;  // evicted page: rows read as zeros
+                    mbar_arrive(&full[st]);
+                }
+            }
+        }
+    } else {
+        const int t = threadIdx.x;  // 0..127
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+        // Score-phase role.
+        const int pair = t / DP, dp = t % DP;
+        const int gq = pair / kPageTokens, j = pair % kPageTokens;
+        const int head = kvh * G + gq;
+        float qrot[CHK];
+        {
+            const float* qh = p.q + (size_t)m * p.ld_q + (size_t)head * D + dp * CHK;
+#pragma unroll
+            for (int e = 0; e < CHK; ++e) qrot[e] = qh[(e + j) % CHK];
+        }
+        // PV-phase role.
+        const bool pv = t < PVT;
+        const int gv = t / (D / 4), dv = (t % (D / 4)) * 4;
+        float run_m = -INFINITY, run_l = 0.0f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+
+        // A timed-out wait marks the CTA bad: every warp still walks the same
+        // barrier sequence (no warp is left waiting on a named barrier), skips
+        // shared-memory reads, and the host sees the recorded error.
+        bool bad = false;
+        for (int i = 0; i < nun; ++i) {
+            const int st = i % kAttnStages;
+            if (!bad && !mbar_wait(&full[st], (i / kAttnStages) & 1, p.err)) bad = true;
+            const float* Kt = tiles + st * 2 * TILE;
+            const float* Vt = Kt + TILE;
+            const bool ok = !bad && valid[st] != 0;
+            float* Sb = S + (i & 1) * G * kPageTokens;
+            {
+                float dot = 0.0f;
+                if (ok) {
+                    const float* kr = Kt + j * D + dp * CHK;
+#pragma unroll
+                    for (int e = 0; e < CHK; ++e) dot = fmaf(qrot[e], kr[(e + j) % CHK], dot);
+                }
+#pragma unroll
+                for (int o = DP / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+                const int tok = (pg0 + i) * kPageTokens + j;
+                if (dp == 0) Sb[gq * kPageTokens + j] = (tok < Lq) ? __fmul_rn(dot, scale) : -INFINITY;
+            }
+            named_bar_sync(1, 128);
+            if (pv) {
+                const float* Sg = Sb + gv * kPageTokens;
+                float pm = Sg[0];
+#pragma unroll
+                for (int jj = 1; jj < kPageTokens; ++jj) pm = fmaxf(pm, Sg[jj]);
+                const float mnew = fmaxf(run_m, pm);
+                const float corr = (run_m == -INFINITY) ? 0.0f : expf(run_m - mnew);
+                float l = run_l * corr;
+                float4 a = make_float4(acc.x * corr, acc.y * corr, acc.z * corr, acc.w * corr);
+#pragma unroll
+                for (int jj = 0; jj < kPageTokens; ++jj) {
+                    const float s = Sg[jj];
+                    const float e = (s == -INFINITY) ? 0.0f : expf(s - mnew);
+                    l += e;
+                    if (ok) {
+                        const float4 v = *reinterpret_cast<const float4*>(Vt + jj * D + dv);
+                        a.x = fmaf(e, v.x, a.x);
+                        a.y = fmaf(e, v.y, a.y);
+                        a.z = fmaf(e, v.z, a.z);
+                        a.w = fmaf(e, v.w, a.w);
+                    }
+                }
+                run_m = mnew;
+                run_l = l;
+                acc = a;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+
+        const size_t pair_idx = (size_t)m * p.Hkv + kvh;
+        float* out = p.out + (size_t)m * p.ld_out + (size_t)(kvh * G + gv) * D + dv;
+        if (p.nsplit == 1) {
+            if (pv) {
+                if (!active) {
+                    *reinterpret_cast<float4*>(out) = make_float4(0.f, 0.f, 0.f, 0.f);
+                } else {
+                    const float il = run_l > 0.0f ? 1.0f / run_l : 0.0f;
+                    *reinterpret_cast<float4*>(out) =
+                        make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
+                }
+            }
+        } else {
+            float* part = p.part + ((pair_idx * p.nsplit + split) * G + gv) * (size_t)(D + 4);
+            if (pv) {
+                *reinterpret_cast<float4*>(part + dv) = acc;
+                if (dv == 0) {
+                    part[D] = run_m;
+                    part[D + 1] = run_l;
+                }
+            }
+            __threadfence();
+            named_bar_sync(1, 128);
+            if (t == 0) {
+                const unsigned int tk = atomicAdd(&p.tickets[pair_idx], 1u);
+                flag[0] = __int_as_float(tk == (unsigned)p.nsplit - 1 ? 1 : 0);
+            }
+            named_bar_sync(1, 128);
+            if (__float_as_int(flag[0]) == 1) {
+                __threadfence();
+                if (pv) {
+                    const float* base = p.part + (pair_idx * p.nsplit) * G * (size_t)(D + 4);
+                    float M = -INFINITY;
+                    for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, base[((size_t)s * G + gv) * (D + 4) + D]);
+                    float den = 0.0f;
+                    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (M != -INFINITY) {
+                        for (int s = 0; s < p.nsplit; ++s) {
+                            const float* ps = base + ((size_t)s * G + gv) * (D + 4);
+                            const float ms = ps[D];
+                            if (ms == -INFINITY) continue;
+                            const float w = expf(ms - M);
+                            den = fmaf(w, ps[D + 1], den);
+                            const float4 a = *reinterpret_cast<const float4*>(ps + dv);
+                            num.x = fmaf(w, a.x, num.x);
+                            num.y = fmaf(w, a.y, num.y);
+                            num.z = fmaf(w, a.z, num.z);
+                            num.w = fmaf(w, a.w, num.w);
+                        }
+                    }
+                    const float il = den > 0.0f ? 1.0f / den : 0.0f;
+                    *reinterpret_cast<float4*>(out) = make_float4(num.x * il, num.y * il, num.z * il, num.w * il);
+                }
+                if (t == 0) p.tickets[pair_idx] = 0u;
+            }
+        }
+    }
+}
+
+template <int G, int D>
+size_t attn_smem() {
+    return 128 + ((2 * G * kPageTokens * 4 + 127) / 128) * 128 + (size_t)kAttnStages * 2 * kPageTokens * D * 4;
+}
+
+template <int G, int D>
+cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t stream, bool pdl) {
+    const size_t smem = attn_smem<G, D>();
+    auto kfn = attn_decode_kernel<G, D>;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)p.nsplit, (unsigned)p.Hkv, (unsigned)p.M);
+    cfg.blockDim = dim3(kAttnThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kfn, p);
+}
+
+// Observer hook: explicit softmax weights [M][H][L] (ModelRunner.swift:544-586).
+__global__ void attn_probs_kernel(const AttnParams p, float* probs, int L) {
+    const int h = blockIdx.x, m = blockIdx.y;
+    const int G = p.H / p.Hkv, kvh = h / G, d = p.d;
+    extern __shared__ float sc[];
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)d));
+    const float* q = p.q + (size_t)m * p.ld_q + (size_t)h * d;
+    for (int j = threadIdx.x; j < L; j += blockDim.x) {
+        const int page = p.page_table[(size_t)m * p.ptab_stride + j / kPageTokens];
+        float dot = 0.0f;
+        if (page >= 0) {
+            const float* k = p.kv_pool +
+                             (((((size_t)page * p.num_layers + p.layer) * 2 + 0) * p.Hkv + kvh) * kPageTokens +
+                              j % kPageTokens) * d;
+            for (int t = 0; t < d; ++t) dot = fmaf(q[t], k[t], dot);
+        }
+        sc[j] = __fmul_rn(dot, scale);
+    }
+    __syncthreads();
+    __shared__ float red[2];
+    if (threadIdx.x == 0) {
+        float mx = -INFINITY;
+        for (int j = 0; j < L; ++j) mx = fmaxf(mx, sc[j]);
+        float sum = 0.0f;
+        for (int j = 0; j < L; ++j) sum += expf(sc[j] - mx);
+        red[0] = mx;
+        red[1] = sum;
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < L; j += blockDim.x)
+        probs[((size_t)m * p.H + h) * L + j] = __fdiv_rn(expf(sc[j] - red[0]), red[1]);
+}
+
+}  // namespace
+
+size_t attention_scratch_bytes(int M, int Hkv, int nsplit, int G, int d) {
+    return (size_t)M * Hkv * nsplit * G * (d + 4) * sizeof(float);
+}
+size_t attention_ticket_count(int M, int Hkv) { return (size_t)M * Hkv; }
+
+int choose_nsplit(int M, int Hkv, int max_pages, int num_sms) {
+    // About two CTAs per SM over the (sequence, KV head) pairs, at least a few
+    // pages per split, at most one split per page.
+    int pairs = M * Hkv;
+    int ns = (2 * num_sms + pairs - 1) / pairs;
+    ns = ns < 1 ? 1 : ns;
+    if (ns > max_pages) ns = max_pages;
+    if (ns > 64) ns = 64;
+    return ns < 1 ? 1 : ns;
+}
+
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
+    const int G = p.H / p.Hkv;
+    if (p.H % p.Hkv != 0) return cudaErrorInvalidValue;
+#define TB_ATTN_CASE(g, dd) \
+    if (G == g && p.d == dd) return launch_attn_t<g, dd>(p, stream, pdl);
+    TB_ATTN_CASE(1, 16)
+    TB_ATTN_CASE(1, 32)
+    TB_ATTN_CASE(1, 64)
+    TB_ATTN_CASE(1, 128)
+    TB_ATTN_CASE(2, 16)
+    TB_ATTN_CASE(2, 32)
+    TB_ATTN_CASE(2, 64)
+    TB_ATTN_CASE(2, 128)
+    TB_ATTN_CASE(4, 16)
+    TB_ATTN_CASE(4, 32)
+    TB_ATTN_CASE(4, 64)
+    TB_ATTN_CASE(4, 128)
+    TB_ATTN_CASE(8, 16)
+    TB_ATTN_CASE(8, 32)
+    TB_ATTN_CASE(8, 64)
+#undef TB_ATTN_CASE
+    return cudaErrorNotSupported;
+}
+
+cudaError_t launch_attention_probs(const AttnParams& p, float* probs, int L, cudaStream_t stream) {
+    size_t smem = (size_t)L * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e =
+            cudaFuncSetAttribute(attn_probs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    attn_probs_kernel<<<dim3(p.H, p.M), 128, smem, stream>>>(p, probs, L);
+    return cudaGetLastError();
+}
+
+}  // namespace tb

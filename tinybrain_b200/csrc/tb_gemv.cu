@@ -1,0 +1,559 @@
+// tb_gemv.cu -- weight-only dequantising GEMV for decode (M <= 8), sm_100a.
+//
+// Replaces the reference's per-output-thread Metal kernels
+// (Sources/TinyBrainMetal/Shaders/Dequant.metal:49-79 matmul_int8_dequant and
+// Shaders/DequantINT4.metal:95-137 matmul_int4_dequant, dispatched from
+// MetalBackend.swift:894-1048) with a streaming design for HBM3e:
+//
+//  * one producer warp per CTA streams 512-byte-per-row slabs of a 32/64-row
+//    block with 1-D bulk async copies (cp.async.bulk, TMA) into a shared-memory
+//    ring guarded by mbarriers; the first stages are issued before the
+//    programmatic-dependent-launch wait, so weights of the next projection are
+//    already in flight while the previous kernel finishes;
+//  * eight consumer warps unpack biased int8 / int4 values to fp32 with byte
+//    permutes and exponent-bias arithmetic (exact), and accumulate with packed
+//    f32x2 FMAs in a fixed order;
+//  * the reduction dimension is split across the CTAs of a thread-block
+//    cluster; partial sums are combined through distributed shared memory in
+//    rank order (deterministic, no atomics);
+//  * fused prologues (embedding gather, RMSNorm: Tensor.swift:1538-1558) and
+//    epilogues (per-column scale, bias, residual add, RoPE + KV-cache append:
+//    ModelRunner.swift:470-517, SiLU*up: ModelRunner.swift:448-453, GELU,
+//    LM-head argmax: Sampler.swift:126-138).
+#include "tb_common.cuh"
+#include "tb_kernels.h"
+
+#include <cstdio>
+
+namespace tb {
+
+QLayout make_qlayout(int precision, int K, int N, int RB) {
+    QLayout L{};
+    L.precision = precision;
+    L.K = K;
+    L.Kp = (K + 31) / 32 * 32;
+    L.N = N;
+    L.RB = RB;
+    L.Np = (N + RB - 1) / RB * RB;
+    L.row_bytes = precision == 8 ? L.Kp : L.Kp / 2;
+    L.slab_k = precision == 8 ? kSlabBytes : 2 * kSlabBytes;
+    L.slabs = (L.row_bytes + kSlabBytes - 1) / kSlabBytes;
+    L.weight_bytes = (size_t)L.Np * L.row_bytes;
+    L.scale_floats = precision == 8 ? (size_t)L.Np : (size_t)(L.Np / 32) * L.slabs * 1024;
+    return L;
+}
+
+namespace {
+
+template <int PREC, int RB>
+struct GemvCfg {
+    static constexpr int RPW = RB / kGemvConsumerWarps;               // rows per warp
+    static constexpr int kWeightStage = RB * kSlabBytes;               // bytes
+    static constexpr int kScaleStage = PREC == 4 ? (RB / 32) * 1024 * 4 : 0;
+    static constexpr int kStageBytes = kWeightStage + kScaleStage;
+    static constexpr int kStages = (kStageBytes <= 20480) ? 4 : (kStageBytes <= 32768 ? 3 : 2);
+    static constexpr int kCH = PREC == 8 ? 16 : 32;                    // k values per lane per slab
+};
+
+// Exponent-bias constants: a biased integer u placed in the low mantissa bits
+// of 2^23 reads as 2^23 + u; subtracting (2^23 + bias * scale) is exact.
+constexpr float kTwo23 = 8388608.0f;
+
+__device__ __forceinline__ float silu_ref(float x) {
+    // Tensor.swift:1135-1142: x / (1 + exp(-x))
+    return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+}
+__device__ __forceinline__ float gelu_ref(float x) {
+    // Tensor.swift:1107-1121 (tanh approximation, fp32)
+    const float s = 0.797884583f;  // Float(sqrt(2.0 / Float.pi))
+    float x3 = __fmul_rn(__fmul_rn(x, x), x);
+    float inner = __fmul_rn(s, __fadd_rn(x, __fmul_rn(0.044715f, x3)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+// Position of k (relative to its slab) in the lane-interleaved x / scale layout.
+template <int CH>
+__device__ __forceinline__ int xperm(int k_in_slab) {
+    const int lane = k_in_slab / CH;
+    const int r = k_in_slab % CH;
+    return ((r >> 2) * 32 + lane) * 4 + (r & 3);
+}
+
+// INT4: per-position scale factor 2^-shift folded into x so that nibble p of
+// a 32-bit word can be extracted in place with a single LOP3.
+__device__ __forceinline__ float int4_pos_scale(int p) {
+    // nibble p sits at bit 4p (p < 5) or, after the >>12, at bit 4(p-3)
+    const int shift = p < 5 ? 4 * p : 4 * (p - 3);
+    return __int_as_float((127 - shift) << 23);
+}
+
+template <int PREC, int RB, int MB>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+    using Cfg = GemvCfg<PREC, RB>;
+    constexpr int STAGES = Cfg::kStages;
+    constexpr int RPW = Cfg::RPW;
+    constexpr int CH = Cfg::kCH;
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + STAGES;
+    float* red = reinterpret_cast<float*>(smem + 128);                  // [RB][MB]
+    float* misc = red + RB * MB;                                          // [64]
+    uint8_t* stage_base = smem + 128 + ((RB * MB + 64) * 4 + 127) / 128 * 128;
+    float* xs = reinterpret_cast<float*>(stage_base + STAGES * Cfg::kStageBytes);
+
+    const QLayout& L = p.L;
+    const int P = p.P;
+    const int rank = (P > 1) ? (int)cluster_ctarank() : 0;
+    const int rb = blockIdx.x / P;
+    const int s0 = rank * L.slabs / P;
+    const int s1 = (rank + 1) * L.slabs / P;
+    const int nunits = s1 - s0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kGemvConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == kGemvConsumerWarps) {
+        // ------------------------------- producer -------------------------------
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            const uint8_t* wrb = p.w + (size_t)rb * RB * L.row_bytes;
+            const float* srb = (PREC == 4) ? p.scales + (size_t)rb * (RB / 32) * L.slabs * 1024 : nullptr;
+            for (int i = 0; i < nunits; ++i) {
+                const int st = i % STAGES;
+                if (i >= STAGES) {
+                    if (!mbar_wait(&empty[st], ((i / STAGES) - 1) & 1, p.err)) break;
+                }
+                const int s = s0 + i;
+                const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
+                const uint32_t wbytes = (uint32_t)(RB * sb);
+                const uint32_t sbytes = (PREC == 4) ? (uint32_t)Cfg::kScaleStage : 0u;
+                uint8_t* dst = stage_base + st * Cfg::kStageBytes;
+                mbar_arrive_expect_tx(&full[st], wbytes + sbytes);
+                bulk_g2s_stream(dst, wrb + (size_t)s * RB * kSlabBytes, wbytes, &full[st], pol);
+                if (PREC == 4)
+                    bulk_g2s_stream(dst + Cfg::kWeightStage, srb + (size_t)s * (RB / 32) * 1024, sbytes, &full[st],
+                                    pol);
+            }
+        }
+    } else {
+        // ------------------------------- consumers -------------------------------
+        pdl_wait();
+        const int ctid = threadIdx.x;  // 0..255
+        const int xstride = (L.slabs + P - 1) / P * L.slab_k;
+        const int kbeg = s0 * L.slab_k;
+        const int kend = min(s1 * L.slab_k, L.Kp);
+
+        // Source rows (embedding gather or activation buffer).
+        const float* srcm[MB];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            if (p.prologue == kProEmbed || p.prologue == kProEmbedRms) {
+                int tok = m < p.M ? p.seq_ro[m].token : 0;
+                if (tok < 0 || tok >= p.vocab) {
+                    record_error(p.err, kDevBadToken);
+                    tok = 0;
+                }
+                srcm[m] = p.embedding + (size_t)tok * p.L.K;
+            } else {
+                srcm[m] = p.src + (size_t)m * p.ld_src;
+            }
+        }
+        // Embedding prologue: CTA 0 materialises the residual stream h.
+        if ((p.prologue == kProEmbed || p.prologue == kProEmbedRms) && blockIdx.x == 0) {
+            for (int m = 0; m < p.M; ++m)
+                for (int k = ctid; k < L.K; k += 256) p.resid[(size_t)m * p.ld_src + k] = srcm[m][k];
+        }
+        float inv[MB];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) inv[m] = 1.0f;
+        if (p.prologue == kProRmsNorm || p.prologue == kProEmbedRms) {
+            // Tensor.swift:1538-1558: ss = sum x^2; inv = 1 / sqrt(ss/H + eps)
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                float ss = 0.0f;
+                if (m < p.M)
+                    for (int k = ctid; k < L.K; k += 256) ss = fmaf(srcm[m][k], srcm[m][k], ss);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                if (lane == 0) misc[m * 8 + warp] = ss;
+            }
+            named_bar_sync(1, 256);
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) ss += misc[m * 8 + w];
+                inv[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)L.K), p.eps)));
+            }
+        }
+        // Stage x[m][kbeg:kend) into shared memory, lane-interleaved per slab.
+        for (int m = 0; m < MB; ++m) {
+            for (int k = kbeg + ctid; k < kend; k += 256) {
+                float v = 0.0f;
+                if (m < p.M && k < L.K) {
+                    v = srcm[m][k];
+                    if (p.prologue == kProRmsNorm || p.prologue == kProEmbedRms)
+                        v = __fmul_rn(__fmul_rn(v, inv[m]), p.norm_w[k]);
+                }
+                if (PREC == 4) v *= int4_pos_scale(k & 7);
+                const int rel = k - kbeg;
+                const int ls = rel / L.slab_k;
+                xs[m * xstride + ls * L.slab_k + xperm<CH>(rel - ls * L.slab_k)] = v;
+            }
+        }
+        named_bar_sync(1, 256);
+
+        float2 acc[RPW][MB];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int m = 0; m < MB; ++m) acc[r][m] = make_float2(0.0f, 0.0f);
+
+        for (int i = 0; i < nunits; ++i) {
+            const int st = i % STAGES;
+            // On a timed-out wait the results are garbage; the error word tells the host.
+            if (!mbar_wait(&full[st], (i / STAGES) & 1, p.err)) break;
+            const int s = s0 + i;
+            const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
+            const uint8_t* wst = stage_base + st * Cfg::kStageBytes;
+            if (lane * 16 < sb) {
+                uint4 wq[RPW];
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) wq[r] = lds128(wst + (warp * RPW + r) * sb + lane * 16);
+                const float* xsl = xs + i * L.slab_k;
+                if (PREC == 8) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        float4 xv[MB];
+#pragma unroll
+                        for (int m = 0; m < MB; ++m) xv[m] = lds128f(xsl + m * xstride + (c * 32 + lane) * 4);
+#pragma unroll
+                        for (int r = 0; r < RPW; ++r) {
+                            const uint32_t wd = c == 0 ? wq[r].x : c == 1 ? wq[r].y : c == 2 ? wq[r].z : wq[r].w;
+                            const float f0 = __uint_as_float(prmt(wd, 0x4B000000u, 0x7440u));
+                            const float f1 = __uint_as_float(prmt(wd, 0x4B000000u, 0x7441u));
+                            const float f2 = __uint_as_float(prmt(wd, 0x4B000000u, 0x7442u));
+                            const float f3 = __uint_as_float(prmt(wd, 0x4B000000u, 0x7443u));
+                            const float2 nb = make_float2(-(kTwo23 + 128.0f), -(kTwo23 + 128.0f));
+                            const float2 v01 = __fadd2_rn(make_float2(f0, f1), nb);
+                            const float2 v23 = __fadd2_rn(make_float2(f2, f3), nb);
+#pragma unroll
+                            for (int m = 0; m < MB; ++m) {
+                                acc[r][m] = __ffma2_rn(v01, make_float2(xv[m].x, xv[m].y), acc[r][m]);
+                                acc[r][m] = __ffma2_rn(v23, make_float2(xv[m].z, xv[m].w), acc[r][m]);
+                            }
+                        }
+                    }
+                } else {
+                    const int grp = (warp * RPW) / 32;
+                    const float* ssl = reinterpret_cast<const float*>(wst + Cfg::kWeightStage) + grp * 1024;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        // word c of the lane's 16 bytes holds k = 32*lane + 8c + p, p = 0..7
+                        float2 xsv[MB][4];
+                        const float4 sa = lds128f(ssl + ((2 * c) * 32 + lane) * 4);
+                        const float4 sbv = lds128f(ssl + ((2 * c + 1) * 32 + lane) * 4);
+#pragma unroll
+                        for (int m = 0; m < MB; ++m) {
+                            const float4 xa = lds128f(xsl + m * xstride + ((2 * c) * 32 + lane) * 4);
+                            const float4 xb = lds128f(xsl + m * xstride + ((2 * c + 1) * 32 + lane) * 4);
+                            xsv[m][0] = __fmul2_rn(make_float2(xa.x, xa.y), make_float2(sa.x, sa.y));
+                            xsv[m][1] = __fmul2_rn(make_float2(xa.z, xa.w), make_float2(sa.z, sa.w));
+                            xsv[m][2] = __fmul2_rn(make_float2(xb.x, xb.y), make_float2(sbv.x, sbv.y));
+                            xsv[m][3] = __fmul2_rn(make_float2(xb.z, xb.w), make_float2(sbv.z, sbv.w));
+                        }
+#pragma unroll
+                        for (int r = 0; r < RPW; ++r) {
+                            const uint32_t wd = c == 0 ? wq[r].x : c == 1 ? wq[r].y : c == 2 ? wq[r].z : wq[r].w;
+                            const uint32_t t = wd >> 12;
+                            const float f0 = __uint_as_float((wd & 0x0000000Fu) | 0x4B000000u);
+                            const float f1 = __uint_as_float((wd & 0x000000F0u) | 0x4B000000u);
+                            const float f2 = __uint_as_float((wd & 0x00000F00u) | 0x4B000000u);
+                            const float f3 = __uint_as_float((wd & 0x0000F000u) | 0x4B000000u);
+                            const float f4 = __uint_as_float((wd & 0x000F0000u) | 0x4B000000u);
+                            const float f5 = __uint_as_float((t & 0x00000F00u) | 0x4B000000u);
+                            const float f6 = __uint_as_float((t & 0x0000F000u) | 0x4B000000u);
+                            const float f7 = __uint_as_float((t & 0x000F0000u) | 0x4B000000u);
+                            const float2 v01 =
+                                __fadd2_rn(make_float2(f0, f1), make_float2(-(kTwo23 + 8.0f), -(kTwo23 + 128.0f)));
+                            const float2 v23 = __fadd2_rn(make_float2(f2, f3),
+                                                          make_float2(-(kTwo23 + 2048.0f), -(kTwo23 + 32768.0f)));
+                            const float2 v45 = __fadd2_rn(make_float2(f4, f5),
+                                                          make_float2(-(kTwo23 + 524288.0f), -(kTwo23 + 2048.0f)));
+                            const float2 v67 = __fadd2_rn(make_float2(f6, f7),
+                                                          make_float2(-(kTwo23 + 32768.0f), -(kTwo23 + 524288.0f)));
+#pragma unroll
+                            for (int m = 0; m < MB; ++m) {
+                                acc[r][m] = __ffma2_rn(v01, xsv[m][0], acc[r][m]);
+                                acc[r][m] = __ffma2_rn(v23, xsv[m][1], acc[r][m]);
+                                acc[r][m] = __ffma2_rn(v45, xsv[m][2], acc[r][m]);
+                                acc[r][m] = __ffma2_rn(v67, xsv[m][3], acc[r][m]);
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        // Warp reduction: every lane ends with the full row sums.
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                float v = acc[r][m].x + acc[r][m].y;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0) red[(warp * RPW + r) * MB + m] = v;
+            }
+    }
+
+    // Make every CTA's partial row sums visible cluster-wide.
+    __syncwarp();
+    if (P > 1)
+        cluster_sync();
+    else
+        __syncthreads();
+
+    if (warp < kGemvConsumerWarps) {
+        const int ctid = threadIdx.x;
+        // Output items handled by this rank: a contiguous chunk.
+        const int nout = (p.epilogue == kEpiQkv) ? RB / 2 : (p.epilogue == kEpiSiluMul ? 32 : RB);
+        const int ob = rank * nout / P, oe = (rank + 1) * nout / P;
+        const int nitems = (oe - ob) * MB;
+        uint32_t rbase[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) rbase[q] = (q < P) ? dsmem_map(red, q) : 0u;
+        auto rowsum = [&](int row, int m) -> float {
+            float s = 0.0f;
+            if (P == 1) return red[row * MB + m];
+            for (int q = 0; q < P; ++q) s += dsmem_ld_f32(rbase[q] + (uint32_t)((row * MB + m) * 4));
+            return s;
+        };
+        auto finish = [&](int gpu_row, float s) -> float {
+            float v = (PREC == 8) ? __fmul_rn(s, p.scales[gpu_row]) : s;
+            if (p.bias) v = __fadd_rn(v, p.bias[gpu_row]);
+            return v;
+        };
+        unsigned long long best_local[MB];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) best_local[m] = 0ull;
+
+        for (int it = ctid; it < nitems; it += 256) {
+            const int m = it % MB;
+            const int o = ob + it / MB;
+            if (m >= p.M) continue;
+            if (p.epilogue == kEpiQkv) {
+                const int n0 = rb * RB + 2 * o;
+                if (n0 >= L.N) continue;
+                const float v0 = finish(n0, rowsum(2 * o, m));
+                const float v1 = finish(n0 + 1, rowsum(2 * o + 1, m));
+                const SeqState& sq = p.seq_ro[m];
+                if (!sq.active) continue;
+                const int pos = sq.pos;
+                const int d = p.head_dim;
+                if (n0 < p.H + p.kv_dim) {
+                    const int i = (n0 < p.H ? n0 : n0 - p.H) % d;
+                    float2 cs = make_float2(1.0f, 0.0f);
+                    if (pos < p.rope_max_pos) cs = p.rope[(size_t)pos * (d / 2) + i / 2];
+                    // ModelRunner.swift:488-489
+                    const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+                    const float r1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+                    if (n0 < p.H) {
+                        p.out[(size_t)m * p.ld_out + n0] = r0;
+                        p.out[(size_t)m * p.ld_out + n0 + 1] = r1;
+                        continue;
+                    }
+                    const int j = n0 - p.H;
+                    const int page = p.page_table[(size_t)m * p.ptab_stride + pos / kPageTokens];
+                    if (page < 0) {
+                        record_error(p.err, kDevBadPage);
+                        continue;
+                    }
+                    const size_t base =
+                        ((((size_t)page * p.num_layers + p.layer) * 2 + 0) * p.Hkv + j / d) * kPageTokens +
+                        pos % kPageTokens;
+                    p.kv_pool[base * d + i] = r0;
+                    p.kv_pool[base * d + i + 1] = r1;
+                } else {
+                    const int j = n0 - p.H - p.kv_dim;
+                    const int page = p.page_table[(size_t)m * p.ptab_stride + pos / kPageTokens];
+                    if (page < 0) {
+                        record_error(p.err, kDevBadPage);
+                        continue;
+                    }
+                    const size_t base =
+                        ((((size_t)page * p.num_layers + p.layer) * 2 + 1) * p.Hkv + j / d) * kPageTokens +
+                        pos % kPageTokens;
+                    p.kv_pool[base * d + j % d] = v0;
+                    p.kv_pool[base * d + j % d + 1] = v1;
+                }
+            } else if (p.epilogue == kEpiSiluMul) {
+                const int n = rb * 32 + o;
+                if (n >= L.N) continue;
+                const float g = finish(rb * RB + o, rowsum(o, m));
+                const float u = finish(rb * RB + 32 + o, rowsum(32 + o, m));
+                p.out[(size_t)m * p.ld_out + n] = __fmul_rn(silu_ref(g), u);
+            } else {
+                const int n = rb * RB + o;
+                if (n >= L.N) continue;
+                const float v = finish(n, rowsum(o, m));
+                if (p.epilogue == kEpiStore) {
+                    p.out[(size_t)m * p.ld_out + n] = v;
+                } else if (p.epilogue == kEpiResidual) {
+                    float* dst = p.out + (size_t)m * p.ld_out + n;
+                    *dst = __fadd_rn(*dst, v);
+                } else if (p.epilogue == kEpiGelu) {
+                    p.out[(size_t)m * p.ld_out + n] = gelu_ref(v);
+                } else {  // kEpiArgmax
+                    if (p.logits) p.logits[(size_t)m * L.N + n] = v;
+                    const unsigned long long key =
+                        ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+#pragma unroll
+                    for (int mm = 0; mm < MB; ++mm)
+                        if (mm == m && key > best_local[mm]) best_local[mm] = key;
+                }
+            }
+        }
+        if (p.epilogue == kEpiArgmax) {
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                unsigned long long b = best_local[m];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+                    b = t > b ? t : b;
+                }
+                if (lane == 0 && b != 0ull && m < p.M) atomicMax(&p.seq[m].best, b);
+            }
+            named_bar_sync(1, 256);
+            if (ctid == 0) {
+                __threadfence();
+                const unsigned int t = atomicAdd(p.ticket, 1u);
+                misc[0] = __int_as_float(t == gridDim.x - 1 ? 1 : 0);
+            }
+            named_bar_sync(1, 256);
+            if (__float_as_int(misc[0]) == 1) {
+                // Last CTA: finish the step for every sequence (ModelRunner.swift:251-292).
+                __threadfence();
+                for (int m = ctid; m < p.M; m += 256) {
+                    SeqState& sq = p.seq[m];
+                    if (!sq.active) continue;
+                    const unsigned long long b = atomicAdd(&sq.best, 0ull);
+                    const int tok = (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
+                    int next;
+                    if (sq.pos >= sq.n_prompt - 1) {
+                        if (sq.n_out < sq.max_out) p.out_tokens[(size_t)m * sq.max_out + sq.n_out] = tok;
+                        sq.n_out += 1;
+                        next = tok;
+                    } else {
+                        next = p.prompt[(size_t)m * p.prompt_stride + sq.pos + 1];
+                    }
+                    sq.token = next;
+                    sq.pos += 1;
+                    sq.best = 0ull;
+                }
+                if (ctid == 0) *p.ticket = 0u;
+            }
+        }
+    }
+    __syncwarp();
+    if (P > 1) cluster_sync();
+}
+
+template <int PREC, int RB, int MB>
+size_t gemv_smem_bytes(const QLayout& L, int P) {
+    using Cfg = GemvCfg<PREC, RB>;
+    size_t head = 128 + ((size_t)(RB * MB + 64) * 4 + 127) / 128 * 128;
+    size_t stages = (size_t)Cfg::kStages * Cfg::kStageBytes;
+    size_t xbytes = (size_t)MB * ((L.slabs + P - 1) / P) * L.slab_k * 4;
+    return head + stages + xbytes;
+}
+
+template <int PREC, int RB, int MB>
+cudaError_t launch_t(const GemvParams& p, cudaStream_t stream, bool pdl) {
+    const size_t smem = gemv_smem_bytes<PREC, RB, MB>(p.L, p.P);
+    auto kfn = gemv_kernel<PREC, RB, MB>;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)(p.L.Np / RB * p.P), 1, 1);
+    cfg.blockDim = dim3(kGemvThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attrs[2];
+    int na = 0;
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = (unsigned)p.P;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+    if (pdl) {
+        attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, kfn, p);
+}
+
+}  // namespace
+
+int choose_ksplit(const QLayout& L, int M, int num_sms) {
+    const int nrb = L.Np / L.RB;
+    int P = 1;
+    // Keep the staged activation slice modest and give every SM about two CTAs.
+    auto xbytes = [&](int q) { return (size_t)M * ((L.slabs + q - 1) / q) * L.slab_k * 4; };
+    while (P < 8 && P * 2 <= L.slabs && (nrb * P < 2 * num_sms || xbytes(P) > 48 * 1024)) P *= 2;
+    while (P < L.slabs && P < 8 && xbytes(P) > 96 * 1024) ++P;
+    return P;
+}
+
+cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream, bool pdl) {
+    const int prec = p.L.precision, RB = p.L.RB;
+    int mb = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : 8;
+    if (p.M > 8) return cudaErrorInvalidValue;
+    if (prec == 8 && RB == 32) {
+        switch (mb) {
+            case 1: return launch_t<8, 32, 1>(p, stream, pdl);
+            case 2: return launch_t<8, 32, 2>(p, stream, pdl);
+            case 4: return launch_t<8, 32, 4>(p, stream, pdl);
+            default: return launch_t<8, 32, 8>(p, stream, pdl);
+        }
+    }
+    if (prec == 8 && RB == 64) {
+        switch (mb) {
+            case 1: return launch_t<8, 64, 1>(p, stream, pdl);
+            case 2: return launch_t<8, 64, 2>(p, stream, pdl);
+            case 4: return launch_t<8, 64, 4>(p, stream, pdl);
+            default: return launch_t<8, 64, 8>(p, stream, pdl);
+        }
+    }
+    if (prec == 4 && RB == 32) {
+        switch (mb) {
+            case 1: return launch_t<4, 32, 1>(p, stream, pdl);
+            case 2: return launch_t<4, 32, 2>(p, stream, pdl);
+            default: return cudaErrorNotSupported;
+        }
+    }
+    if (prec == 4 && RB == 64) {
+        switch (mb) {
+            case 1: return launch_t<4, 64, 1>(p, stream, pdl);
+            case 2: return launch_t<4, 64, 2>(p, stream, pdl);
+            default: return cudaErrorNotSupported;
+        }
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace tb

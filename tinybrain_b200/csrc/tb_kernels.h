@@ -1,0 +1,185 @@
+// tb_kernels.h -- internal kernel parameter blocks and launchers shared by the
+// host runtime (tb_runtime.cu) and the kernel translation units.  Not part of
+// the public C ABI (include/tinybrain_cuda.h).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace tb {
+
+// Device error codes written into the context's error word (first writer wins).
+enum DeviceError : int {
+    kDevOk = 0,
+    kDevWaitTimeout = 1,      // an mbarrier wait exceeded its time limit
+    kDevBadPage = 2,          // KV append found no page mapped for a position
+    kDevBadToken = 3,         // token id outside [0, vocab)
+};
+
+// ----------------------------------------------------------------------------
+// Device weight layout produced by the repack kernels ("GPU layout").
+//
+// The reference stores a quantized projection row-major as [K in][N out]
+// (y = x * W).  The GPU layout is output-row major and tiled for streaming:
+//   * rows (outputs) are grouped in row blocks of RB rows (RB = 32, or 64 for
+//     the fused gate/up matrix whose block is 32 gate rows + 32 up rows);
+//   * the reduction dimension is cut in slabs of 512 bytes per row (512 int8
+//     values or 1024 int4 values); the last slab of a row may be shorter;
+//   * unit (row block, slab) = RB rows x slab bytes, row-major, contiguous;
+//     units of a row block are consecutive, so a row block is one contiguous
+//     range streamed with 1-D bulk copies.
+// INT8 values are stored biased (q + 128 as uint8).  INT4 values are stored
+// biased (q + 8) two per byte, low nibble = even k.  INT4 group scales for the
+// 32 rows of a group and the k range of a slab are stored next to each other
+// per unit, in the lane-interleaved order the kernel reads them
+// ([group][chunk c][lane][4 floats] for k = 32*lane + 4*c + i).
+// ----------------------------------------------------------------------------
+constexpr int kSlabBytes = 512;
+constexpr int kGemvConsumerWarps = 8;
+constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;  // + 1 producer warp
+
+struct QLayout {
+    int precision;       // 8 or 4
+    int K;               // logical reduction length
+    int Kp;              // K padded to a multiple of 32
+    int N;               // logical output rows
+    int Np;              // N padded to a multiple of RB
+    int RB;              // rows per row block (32 or 64)
+    int slabs;           // number of slabs along K
+    int slab_k;          // k values per full slab (512 int8 / 1024 int4)
+    int row_bytes;       // bytes per row (Kp or Kp/2)
+    size_t weight_bytes; // Np * row_bytes
+    size_t scale_floats; // INT8: Np ; INT4: (Np/32) * Kp
+};
+
+QLayout make_qlayout(int precision, int K, int N, int RB);
+
+// Prologue: how the CTA builds its activation slice x[m][k].
+enum GemvPrologue : int {
+    kProNone = 0,      // x = src[m][k]
+    kProRmsNorm = 1,   // x = src[m][k] * inv_rms(src[m]) * norm_w[k]
+    kProEmbed = 2,     // src row = embedding[token[m]]; CTA 0 copies it into resid
+    kProEmbedRms = 3,  // embed, then RMSNorm
+};
+
+// Epilogue: what happens with the finished dot products.
+enum GemvEpilogue : int {
+    kEpiStore = 0,     // out[m][n] = v
+    kEpiResidual = 1,  // out[m][n] += v
+    kEpiQkv = 2,       // q with RoPE -> q_out; k with RoPE, v -> KV cache page
+    kEpiSiluMul = 3,   // RB 64: out[m][n] = silu(gate) * up
+    kEpiGelu = 4,      // out[m][n] = gelu(v)
+    kEpiArgmax = 5,    // logits (optional) + per-sequence argmax + step bookkeeping
+};
+
+// Per-sequence decode state living in device memory.
+struct SeqState {
+    int pos;            // position of the token processed by the current step
+    int token;          // token fed to the current step
+    int n_prompt;       // prompt length (prompt tokens are taken from prompt[])
+    int n_out;          // tokens generated so far
+    int max_out;        // capacity of out_tokens
+    int active;         // 0 = finished / padding slot
+    unsigned long long best;  // packed argmax key of the current step
+};
+
+struct GemvParams {
+    // weights (GPU layout)
+    const uint8_t* w;
+    const float* scales;
+    const float* bias;        // [N] or null
+    QLayout L;
+    int P;                    // cluster size = K split factor
+    int M;                    // batch rows
+    // prologue
+    int prologue;
+    const float* src;         // [M][ld_src]
+    int ld_src;
+    const float* norm_w;      // [K]
+    float eps;
+    const float* embedding;   // [V][K]
+    float* resid;             // embed prologue: copy of the embedding row
+    const SeqState* seq_ro;   // token / pos source
+    // epilogue
+    int epilogue;
+    float* out;               // [M][ld_out]
+    int ld_out;
+    // QKV epilogue
+    int H, Hkv, head_dim, kv_dim;
+    const float2* rope;       // [max_pos][head_dim/2] (cos, sin)
+    int rope_max_pos;
+    float* kv_pool;           // [page][layer][2][Hkv][16][d]
+    const int* page_table;    // [M][ptab_stride]
+    int ptab_stride;
+    int layer, num_layers;
+    // argmax epilogue
+    SeqState* seq;            // [M]
+    float* logits;            // [M][N] or null
+    unsigned int* ticket;     // completion counter for step bookkeeping
+    int* out_tokens;          // [M][max_out]
+    const int* prompt;        // [M][prompt_stride]
+    int prompt_stride;
+    int vocab;
+    int* err;                 // device error word
+};
+
+// Launch the GEMV described by p on `stream` (PDL + cluster attributes).
+cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream, bool pdl);
+// Pick the K-split (cluster size) for a layout and batch.
+int choose_ksplit(const QLayout& L, int M, int num_sms);
+
+// Repack reference-layout quantized weights (device copies of the host
+// arrays) into the GPU layout.  row_offset places the matrix at rows
+// [row_offset, row_offset + N) of a fused destination; for the fused gate/up
+// block, `interleave` = 1 puts this matrix in rows [0,32) of each 64-row block
+// and 2 in rows [32,64).
+struct RepackSrc {
+    int precision;
+    int K, N;
+    int group_size;
+    const void* data;          // INT8: [K][N] int8 ; INT4: packed nibbles of flat [K][N]
+    const float* scales;       // INT8: [N] ; INT4: [K*N/gs]
+    const int8_t* zero_points; // may be null; must be all zero for the fast path
+};
+cudaError_t launch_repack(const RepackSrc& s, const QLayout& L, uint8_t* w_out, float* scales_out,
+                          int row_offset, int interleave, cudaStream_t stream);
+
+// Device quantizers (bit-exact restatements of the reference quantizers).
+cudaError_t launch_quantize_int8_per_channel(const float* W, int64_t K, int64_t N, int8_t* Q, float* scales,
+                                             cudaStream_t stream);
+cudaError_t launch_quantize_int4_group(const float* x, int64_t count, int64_t gs, uint8_t* packed,
+                                       float* scales, int8_t* zp, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------
+// Paged decode attention.
+// ----------------------------------------------------------------------------
+constexpr int kPageTokens = 16;
+
+struct AttnParams {
+    const float* q;           // [M][H*d] (post-RoPE)
+    int ld_q;
+    const float* kv_pool;     // [page][layer][2][Hkv][16][d]
+    const int* page_table;    // [M][ptab_stride], -1 = evicted (reads as zeros)
+    int ptab_stride;
+    const SeqState* seq;      // L = seq.pos + 1 (if lens == null)
+    const int* lens;          // optional explicit lengths [M]
+    int layer, num_layers;
+    int H, Hkv, d;
+    int M;
+    int nsplit;
+    float* out;               // [M][H*d]
+    int ld_out;
+    float* part;              // scratch partials [M][Hkv][nsplit][G][d + 4] (16-byte rows)
+    unsigned int* tickets;    // scratch counters [M][Hkv], zero on entry, left zero
+    int* err;
+};
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
+size_t attention_scratch_bytes(int M, int Hkv, int nsplit, int G, int d);
+size_t attention_ticket_count(int M, int Hkv);
+int choose_nsplit(int M, int Hkv, int max_pages, int num_sms);
+
+// Softmax attention weights for the observer hook: probs[M][H][L].
+cudaError_t launch_attention_probs(const AttnParams& p, float* probs, int L, cudaStream_t stream);
+
+}  // namespace tb

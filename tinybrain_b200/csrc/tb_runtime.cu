@@ -1,0 +1,1675 @@
+// tb_runtime.cu -- host runtime and C ABI of libtinybrain_cuda.
+//
+// Maps the reference's runtime objects onto the device:
+//   ModelWeights (Sources/TinyBrainRuntime/ModelWeights.swift:137-168)
+//       -> tb_model: weights repacked once into HBM, QKV fused, gate/up fused;
+//   ModelRunner (ModelRunner.swift:127-298)
+//       -> tb_runner: one decode step = one CUDA graph of fused kernels;
+//   KVCache + PageAllocator (KVCache.swift:108-356, PageAllocator.swift:35-152)
+//       -> host page tables with the reference's length / eviction rules,
+//          pages living in one HBM pool;
+//   Sampler.greedy (Sampler.swift:126-138)
+//       -> argmax fused into the LM-head GEMV epilogue.
+// There is no CPU compute path: every numeric result comes from a kernel.
+#include "../../include/tinybrain_cuda.h"
+#include "tb_kernels.h"
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <thread>
+#include <vector>
+
+using namespace tb;
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+namespace {
+thread_local std::string g_last_error;
+
+tb_status fail(tb_status s, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return s;
+}
+tb_status ok() { return TB_OK; }
+
+tb_status cuda_fail(cudaError_t e, const char* what) {
+    if (e == cudaErrorMemoryAllocation) return fail(TB_ERR_OUT_OF_MEMORY, "%s: %s", what, cudaGetErrorString(e));
+    return fail(TB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+#define TB_CUDA(call)                                                     \
+    do {                                                                  \
+        cudaError_t e_ = (call);                                          \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);               \
+    } while (0)
+#define TB_CHECK(cond, ...)                                               \
+    do {                                                                  \
+        if (!(cond)) return fail(TB_ERR_INVALID_ARGUMENT, __VA_ARGS__);   \
+    } while (0)
+
+// RAII device buffer.
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) {
+        o.p = nullptr;
+        o.bytes = 0;
+    }
+    DevBuf& operator=(DevBuf&& o) noexcept {
+        if (this != &o) {
+            release();
+            p = o.p;
+            bytes = o.bytes;
+            o.p = nullptr;
+            o.bytes = 0;
+        }
+        return *this;
+    }
+    ~DevBuf() { release(); }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    cudaError_t alloc(size_t n) {
+        release();
+        if (n == 0) return cudaSuccess;
+        cudaError_t e = cudaMalloc(&p, n);
+        if (e == cudaSuccess) bytes = n;
+        return e;
+    }
+    template <class T>
+    T* as() const { return static_cast<T*>(p); }
+};
+
+struct PinnedBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    ~PinnedBuf() {
+        if (p) cudaFreeHost(p);
+    }
+    cudaError_t ensure(size_t n) {
+        if (n <= bytes) return cudaSuccess;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaMallocHost(&p, n);
+        if (e == cudaSuccess) bytes = n;
+        return e;
+    }
+    template <class T>
+    T* as() const { return static_cast<T*>(p); }
+};
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// objects
+// ---------------------------------------------------------------------------
+struct tb_context {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    DevBuf err;          // int device error word
+    DevBuf scratch;      // attention partials
+    DevBuf tickets;      // attention tickets (zeroed)
+    DevBuf io_a, io_b, io_c, io_d;  // staging for host-pointer entry points
+    DevBuf seq_tmp;
+};
+
+struct tb_qweight {
+    tb_context* ctx = nullptr;
+    QLayout L{};
+    DevBuf w, s;
+};
+
+namespace {
+
+struct ProjStage {
+    bool set = false;
+    int precision = 0;
+    int K = 0, N = 0, gs = 0;
+    DevBuf data, scales;
+    std::vector<float> bias;
+};
+
+struct FusedWeight {
+    QLayout L{};
+    DevBuf w, s, bias;
+    bool has_bias = false;
+};
+
+struct Layer {
+    ProjStage stage[7];
+    std::vector<float> in_norm, post_norm;
+    FusedWeight qkv, o, up, down;  // up = fused gate/up (llama) or up (toy)
+    DevBuf in_norm_d, post_norm_d;
+};
+
+}  // namespace
+
+struct tb_model {
+    tb_context* ctx = nullptr;
+    tb_model_config cfg{};
+    int head_dim = 0, kv_dim = 0;
+    std::vector<Layer> layers;
+    ProjStage out_stage;
+    FusedWeight out;
+    DevBuf emb, final_norm;
+    bool has_final_norm = false;
+    bool finalized = false;
+    int64_t weight_bytes = 0;
+};
+
+namespace {
+
+// Host mirror of the reference's per-sequence KVCache bookkeeping.
+struct SeqKV {
+    std::vector<int> map;   // logical page -> pool page, -1 = absent
+    int64_t length = 0;
+    int64_t pos = 0;        // ModelRunner.currentPosition
+    int pages_held = 0;
+};
+
+struct Launch {
+    int kind;  // 0 gemv, 1 attention
+    GemvParams g;
+    AttnParams a;
+    int64_t bytes;  // algorithmic bytes (weights + activations) for roofline
+};
+
+}  // namespace
+
+struct tb_runner {
+    tb_model* m = nullptr;
+    tb_context* ctx = nullptr;
+    int B = 1;                 // batch slots
+    int max_positions = 0;
+    int ptab_stride = 0;
+    int max_pages_per_seq = 0;
+    int total_pages = 0;
+    // device buffers
+    DevBuf seq, ptab, kv, h, q, ctxv, act, logits, rope, prompt, out_tokens, ticket;
+    DevBuf attn_part, attn_tickets;  // runner-owned: captured by the step graph
+    int64_t h2d_bytes = 0, d2h_bytes = 0;  // host<->device traffic of the generate paths
+    int prompt_stride = 0, max_out = 0;
+    // host mirror
+    std::vector<SeqKV> kvh;
+    std::vector<int> free_pages;  // LIFO
+    std::vector<int> ptab_host;
+    std::vector<char> ptab_dirty;
+    PinnedBuf pin_ptab, pin_tokens, pin_seq;
+    // step plan + graph
+    std::vector<Launch> plan;
+    cudaGraphExec_t graph = nullptr;
+    int nsplit = 1;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    ~tb_runner() {
+        if (graph) cudaGraphExecDestroy(graph);
+        if (ev0) cudaEventDestroy(ev0);
+        if (ev1) cudaEventDestroy(ev1);
+    }
+};
+
+// ---------------------------------------------------------------------------
+// misc
+// ---------------------------------------------------------------------------
+extern "C" int32_t tb_abi_version(void) { return TB_ABI_VERSION; }
+extern "C" const char* tb_last_error(void) { return g_last_error.c_str(); }
+extern "C" const char* tb_status_string(tb_status s) {
+    switch (s) {
+        case TB_OK: return "ok";
+        case TB_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case TB_ERR_CUDA: return "CUDA error";
+        case TB_ERR_OUT_OF_MEMORY: return "out of device memory";
+        case TB_ERR_UNSUPPORTED: return "unsupported";
+        case TB_ERR_PAGE_POOL_EXHAUSTED: return "KV page pool exhausted";
+        case TB_ERR_FORMAT: return "format error";
+        case TB_ERR_NO_DEVICE: return "no CUDA device";
+        case TB_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+        case TB_ERR_STATE: return "invalid state";
+        case TB_ERR_DEVICE_FAULT: return "device fault";
+    }
+    return "unknown";
+}
+
+extern "C" tb_status tb_device_count(int32_t* count) {
+    TB_CHECK(count, "count is NULL");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        *count = 0;
+        return fail(TB_ERR_NO_DEVICE, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+    }
+    *count = n;
+    return ok();
+}
+
+// ---- Tensor.random over SeededGenerator ----
+namespace {
+constexpr uint64_t kLcgA = 6364136223846793005ull;  // ModelWeights.swift:26
+constexpr uint64_t kLcgC = 1ull;
+
+// state after n steps of s -> a*s + c (mod 2^64)
+uint64_t lcg_jump(uint64_t s, uint64_t n) {
+    uint64_t A = 1, C = 0, a = kLcgA, c = kLcgC;
+    while (n) {
+        if (n & 1) {
+            A = A * a;
+            C = C * a + c;
+        }
+        c = (a + 1) * c;
+        a = a * a;
+        n >>= 1;
+    }
+    return A * s + C;
+}
+
+// Float.random(in: 0..<1, using:) for a 64-bit generator: the low 24 bits of
+// the 32-bit truncation of next(), times 2^-24.
+inline float unit_float(uint64_t v) { return (float)((uint32_t)v & 0xFFFFFFu) * 5.9604644775390625e-08f; }
+}  // namespace
+
+extern "C" tb_status tb_rng_seed_state(uint64_t seed, uint64_t* state) {
+    TB_CHECK(state, "state is NULL");
+    *state = seed != 0 ? seed : 0xdeadbeefull;  // ModelWeights.swift:21-23
+    return ok();
+}
+
+extern "C" tb_status tb_rng_fill_normal(uint64_t* state, float mean, float stdv, int64_t n, float* out) {
+    TB_CHECK(state && (out || n == 0), "NULL argument");
+    TB_CHECK(n >= 0, "negative count");
+    const int64_t pairs = (n + 1) / 2;
+    const uint64_t s0 = *state;
+    const float sd = stdv;
+    unsigned nt = std::max(1u, std::min(64u, std::thread::hardware_concurrency()));
+    if (pairs < 65536) nt = 1;
+    auto work = [s0, sd, mean, n, out](int64_t pb, int64_t pe) {
+        uint64_t s = lcg_jump(s0, (uint64_t)(2 * pb));
+        const float two_pi = 2.0f * 3.14159265358979323846f;  // 2.0 * Float.pi
+        for (int64_t pi = pb; pi < pe; ++pi) {
+            s = kLcgA * s + kLcgC;
+            float u1 = unit_float(s);
+            s = kLcgA * s + kLcgC;
+            const float u2 = unit_float(s);
+            u1 = std::max(u1, 1.40129846e-45f);  // Float.leastNonzeroMagnitude
+            const float r = sqrtf(-2.0f * logf(u1));
+            const float theta = two_pi * u2;
+            const int64_t i = 2 * pi;
+            out[i] = mean + sd * r * cosf(theta);
+            if (i + 1 < n) out[i + 1] = mean + sd * r * sinf(theta);
+        }
+    };
+    if (nt == 1) {
+        work(0, pairs);
+    } else {
+        std::vector<std::thread> th;
+        for (unsigned t = 0; t < nt; ++t) {
+            int64_t pb = pairs * t / nt, pe = pairs * (t + 1) / nt;
+            th.emplace_back(work, pb, pe);
+        }
+        for (auto& x : th) x.join();
+    }
+    *state = lcg_jump(s0, (uint64_t)(2 * pairs));
+    return ok();
+}
+
+// ---------------------------------------------------------------------------
+// context
+// ---------------------------------------------------------------------------
+extern "C" tb_status tb_context_create(int32_t device, tb_context** out) {
+    TB_CHECK(out, "out is NULL");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return fail(TB_ERR_NO_DEVICE, "no CUDA device visible");
+    TB_CHECK(device >= 0 && device < n, "device %d out of range (%d devices)", device, n);
+    TB_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop{};
+    TB_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10)
+        return fail(TB_ERR_UNSUPPORTED, "device %d is sm_%d%d; libtinybrain_cuda is built for sm_100a", device,
+                    prop.major, prop.minor);
+    auto c = std::make_unique<tb_context>();
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    TB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    TB_CUDA(c->err.alloc(sizeof(int)));
+    TB_CUDA(cudaMemset(c->err.p, 0, sizeof(int)));
+    *out = c.release();
+    return ok();
+}
+
+extern "C" tb_status tb_context_destroy(tb_context* ctx) {
+    if (!ctx) return ok();
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return ok();
+}
+
+extern "C" tb_status tb_context_synchronize(tb_context* ctx) {
+    TB_CHECK(ctx, "ctx is NULL");
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return ok();
+}
+
+extern "C" void* tb_context_stream(tb_context* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+extern "C" tb_status tb_context_check_device(tb_context* ctx) {
+    TB_CHECK(ctx, "ctx is NULL");
+    int v = 0;
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    TB_CUDA(cudaMemcpy(&v, ctx->err.p, sizeof(int), cudaMemcpyDeviceToHost));
+    TB_CUDA(cudaMemset(ctx->err.p, 0, sizeof(int)));
+    if (v == 0) return ok();
+    if (v == kDevWaitTimeout) return fail(TB_ERR_DEVICE_TIMEOUT, "a device-side wait exceeded its time limit");
+    if (v == kDevBadPage) return fail(TB_ERR_STATE, "KV append found no page mapped for the position");
+    if (v == kDevBadToken) return fail(TB_ERR_STATE, "token id outside the vocabulary");
+    return fail(TB_ERR_STATE, "device error code %d", v);
+}
+
+static tb_status ensure(DevBuf& b, size_t bytes) {
+    if (b.bytes >= bytes) return ok();
+    TB_CUDA(b.alloc(bytes));
+    return ok();
+}
+
+// ---------------------------------------------------------------------------
+// quantizers
+// ---------------------------------------------------------------------------
+extern "C" tb_status tb_quantize_int8_per_channel_dev(tb_context* ctx, const float* w, int64_t K, int64_t N,
+                                                      int8_t* q, float* s) {
+    TB_CHECK(ctx && w && q && s, "NULL argument");
+    TB_CHECK(K > 0 && N > 0, "K and N must be positive");
+    TB_CUDA(cudaSetDevice(ctx->device));
+    TB_CUDA(launch_quantize_int8_per_channel(w, K, N, q, s, ctx->stream));
+    return ok();
+}
+
+extern "C" tb_status tb_quantize_int4_group_dev(tb_context* ctx, const float* x, int64_t count, int64_t gs,
+                                                uint8_t* packed, float* s, int8_t* zp) {
+    TB_CHECK(ctx && x && packed && s, "NULL argument");
+    TB_CHECK(count > 0 && gs > 0, "count and group_size must be positive");
+    TB_CUDA(cudaSetDevice(ctx->device));
+    TB_CUDA(launch_quantize_int4_group(x, count, gs, packed, s, zp, ctx->stream));
+    return ok();
+}
+
+extern "C" tb_status tb_quantize_int8_per_channel(tb_context* ctx, const float* w, int64_t K, int64_t N, int8_t* q,
+                                                  float* s) {
+    TB_CHECK(ctx && w && q && s, "NULL argument");
+    TB_CHECK(K > 0 && N > 0, "K and N must be positive");
+    TB_CUDA(cudaSetDevice(ctx->device));
+    const size_t nw = (size_t)K * N;
+    DevBuf dw, dq, ds;
+    TB_CUDA(dw.alloc(nw * 4));
+    TB_CUDA(dq.alloc(nw));
+    TB_CUDA(ds.alloc((size_t)N * 4));
+    TB_CUDA(cudaMemcpyAsync(dw.p, w, nw * 4, cudaMemcpyHostToDevice, ctx->stream));
+    TB_CUDA(launch_quantize_int8_per_channel(dw.as<float>(), K, N, dq.as<int8_t>(), ds.as<float>(), ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(q, dq.p, nw, cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(s, ds.p, (size_t)N * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return ok();
+}
+
+extern "C" tb_status tb_quantize_int4_group(tb_context* ctx, const float* x, int64_t count, int64_t gs,
+                                            uint8_t* packed, float* s, int8_t* zp) {
+    TB_CHECK(ctx && x && packed && s, "NULL argument");
+    TB_CHECK(count > 0 && gs > 0, "count and group_size must be positive");
+    TB_CUDA(cudaSetDevice(ctx->device));
+    const size_t nb = (size_t)(count + 1) / 2, ng = (size_t)((count + gs - 1) / gs);
+    DevBuf dx, dp, ds, dz;
+    TB_CUDA(dx.alloc((size_t)count * 4));
+    TB_CUDA(dp.alloc(nb));
+    TB_CUDA(ds.alloc(ng * 4));
+    TB_CUDA(dz.alloc(ng));
+    TB_CUDA(cudaMemcpyAsync(dx.p, x, (size_t)count * 4, cudaMemcpyHostToDevice, ctx->stream));
+    TB_CUDA(launch_quantize_int4_group(dx.as<float>(), count, gs, dp.as<uint8_t>(), ds.as<float>(),
+                                       dz.as<int8_t>(), ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(packed, dp.p, nb, cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(s, ds.p, ng * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (zp) TB_CUDA(cudaMemcpyAsync(zp, dz.p, ng, cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return ok();
+}
+
+// ---------------------------------------------------------------------------
+// quantized weights
+// ---------------------------------------------------------------------------
+static tb_status validate_desc(const tb_qtensor_desc* d) {
+    TB_CHECK(d, "desc is NULL");
+    TB_CHECK(d->precision == 8 || d->precision == 4, "precision must be 8 or 4 (got %d)", d->precision);
+    TB_CHECK(d->in_features > 0 && d->out_features > 0, "shape must be positive");
+    TB_CHECK(d->in_features < (1 << 30) && d->out_features < (1 << 30), "shape too large");
+    TB_CHECK(d->data && d->scales, "data and scales are required");
+    const int64_t cnt = d->in_features * d->out_features;
+    if (d->precision == 8) {
+        TB_CHECK(d->data_bytes == cnt, "INT8 data must hold K*N = %lld bytes (got %lld)", (long long)cnt,
+                 (long long)d->data_bytes);
+        TB_CHECK(d->num_scales == d->out_features, "INT8 per-channel needs N = %lld scales (got %lld)",
+                 (long long)d->out_features, (long long)d->num_scales);
+        if (d->zero_points)
+            for (int64_t i = 0; i < d->num_zero_points; ++i)
+                if (d->zero_points[i] != 0)
+                    return fail(TB_ERR_UNSUPPORTED, "non-zero INT8 zero points are not supported");
+    } else {
+        const int64_t gs = d->group_size;
+        TB_CHECK(gs > 0, "INT4 group_size must be positive");
+        TB_CHECK(d->data_bytes == (cnt + 1) / 2, "INT4 data must hold ceil(K*N/2) bytes");
+        TB_CHECK(d->num_scales == (cnt + gs - 1) / gs, "INT4 needs ceil(K*N/group_size) scales");
+        if (gs % 32 != 0 || d->out_features % gs != 0)
+            return fail(TB_ERR_UNSUPPORTED,
+                        "INT4 needs group_size %% 32 == 0 and out_features %% group_size == 0 (group %lld, N %lld)",
+                        (long long)gs, (long long)d->out_features);
+        if (d->zero_points)
+            for (int64_t i = 0; i < d->num_zero_points; ++i)
+                if (d->zero_points[i] != 0)
+                    return fail(TB_ERR_UNSUPPORTED, "non-zero INT4 zero points are not supported");
+    }
+    return ok();
+}
+
+static tb_status stage_desc(tb_context* ctx, const tb_qtensor_desc* d, ProjStage& st) {
+    tb_status s = validate_desc(d);
+    if (s != TB_OK) return s;
+    st.precision = d->precision;
+    st.K = (int)d->in_features;
+    st.N = (int)d->out_features;
+    st.gs = (int)d->group_size;
+    TB_CUDA(st.data.alloc((size_t)d->data_bytes));
+    TB_CUDA(st.scales.alloc((size_t)d->num_scales * 4));
+    TB_CUDA(cudaMemcpyAsync(st.data.p, d->data, (size_t)d->data_bytes, cudaMemcpyHostToDevice, ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(st.scales.p, d->scales, (size_t)d->num_scales * 4, cudaMemcpyHostToDevice,
+                            ctx->stream));
+    st.set = true;
+    return ok();
+}
+
+static tb_status alloc_fused(tb_context* ctx, FusedWeight& f, const QLayout& L) {
+    f.L = L;
+    TB_CUDA(f.w.alloc(L.weight_bytes));
+    TB_CUDA(f.s.alloc(L.scale_floats * 4));
+    TB_CUDA(cudaMemsetAsync(f.w.p, L.precision == 8 ? 0x80 : 0x88, L.weight_bytes, ctx->stream));
+    TB_CUDA(cudaMemsetAsync(f.s.p, 0, L.scale_floats * 4, ctx->stream));
+    return ok();
+}
+
+static tb_status repack_into(tb_context* ctx, FusedWeight& f, const ProjStage& st, int row_offset, int interleave) {
+    RepackSrc rs{};
+    rs.precision = st.precision;
+    rs.K = st.K;
+    rs.N = st.N;
+    rs.group_size = st.gs;
+    rs.data = st.data.p;
+    rs.scales = st.scales.as<float>();
+    TB_CUDA(launch_repack(rs, f.L, f.w.as<uint8_t>(), f.s.as<float>(), row_offset, interleave, ctx->stream));
+    return ok();
+}
+
+extern "C" tb_status tb_qweight_upload(tb_context* ctx, const tb_qtensor_desc* d, tb_qweight** out) {
+    TB_CHECK(ctx && out, "NULL argument");
+    *out = nullptr;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    ProjStage st;
+    tb_status s = stage_desc(ctx, d, st);
+    if (s != TB_OK) return s;
+    auto w = std::make_unique<tb_qweight>();
+    w->ctx = ctx;
+    FusedWeight f;
+    s = alloc_fused(ctx, f, make_qlayout(st.precision, st.K, st.N, 32));
+    if (s != TB_OK) return s;
+    s = repack_into(ctx, f, st, 0, 0);
+    if (s != TB_OK) return s;
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    w->L = f.L;
+    std::swap(w->w.p, f.w.p);
+    std::swap(w->w.bytes, f.w.bytes);
+    std::swap(w->s.p, f.s.p);
+    std::swap(w->s.bytes, f.s.bytes);
+    *out = w.release();
+    return ok();
+}
+
+extern "C" tb_status tb_qweight_free(tb_qweight* w) {
+    if (w) {
+        cudaSetDevice(w->ctx->device);
+        delete w;
+    }
+    return ok();
+}
+
+static GemvParams plain_gemv(tb_context* ctx, const QLayout& L, const uint8_t* w, const float* s, int M) {
+    GemvParams p{};
+    p.w = w;
+    p.scales = s;
+    p.L = L;
+    p.M = M;
+    p.P = choose_ksplit(L, M, ctx->num_sms);
+    p.prologue = kProNone;
+    p.ld_src = L.K;
+    p.epilogue = kEpiStore;
+    p.ld_out = L.N;
+    p.err = ctx->err.as<int>();
+    return p;
+}
+
+extern "C" tb_status tb_matmul_quantized_dev(tb_context* ctx, const float* x, int64_t M, const tb_qweight* w,
+                                             float* y) {
+    TB_CHECK(ctx && x && w && y, "NULL argument");
+    TB_CHECK(M >= 1 && M <= 8, "M must be in [1, 8] for the decode GEMV (got %lld)", (long long)M);
+    TB_CUDA(cudaSetDevice(ctx->device));
+    GemvParams p = plain_gemv(ctx, w->L, w->w.as<uint8_t>(), w->s.as<float>(), (int)M);
+    p.src = x;
+    p.out = y;
+    TB_CUDA(launch_gemv(p, ctx->stream, false));
+    return ok();
+}
+
+extern "C" tb_status tb_matmul_quantized(tb_context* ctx, const float* x, int64_t M, const tb_qweight* w,
+                                         float* y) {
+    TB_CHECK(ctx && x && w && y, "NULL argument");
+    TB_CHECK(M >= 1 && M <= 8, "M must be in [1, 8] for the decode GEMV (got %lld)", (long long)M);
+    TB_CUDA(cudaSetDevice(ctx->device));
+    const size_t xb = (size_t)M * w->L.K * 4, yb = (size_t)M * w->L.N * 4;
+    tb_status s = ensure(ctx->io_a, xb);
+    if (s != TB_OK) return s;
+    s = ensure(ctx->io_b, yb);
+    if (s != TB_OK) return s;
+    TB_CUDA(cudaMemcpyAsync(ctx->io_a.p, x, xb, cudaMemcpyHostToDevice, ctx->stream));
+    s = tb_matmul_quantized_dev(ctx, ctx->io_a.as<float>(), M, w, ctx->io_b.as<float>());
+    if (s != TB_OK) return s;
+    TB_CUDA(cudaMemcpyAsync(y, ctx->io_b.p, yb, cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return tb_context_check_device(ctx);
+}
+
+// ---------------------------------------------------------------------------
+// attention entry points
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void pack_kv_contig_kernel(const float* __restrict__ K, const float* __restrict__ V, int64_t L, int Hkv,
+                                      int d, float* __restrict__ pool) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t kvdim = (int64_t)Hkv * d;
+    if (i >= L * kvdim) return;
+    const int64_t pos = i / kvdim, r = i % kvdim;
+    const int64_t head = r / d, e = r % d;
+    const int64_t page = pos / kPageTokens, slot = pos % kPageTokens;
+    const size_t kb = ((((size_t)page * 1 + 0) * 2 + 0) * Hkv + head) * kPageTokens + slot;
+    const size_t vb = ((((size_t)page * 1 + 0) * 2 + 1) * Hkv + head) * kPageTokens + slot;
+    pool[kb * d + e] = K[i];
+    pool[vb * d + e] = V[i];
+}
+__global__ void iota_kernel(int* p, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = i;
+}
+}  // namespace
+
+static tb_status check_heads(int H, int Hkv, int d) {
+    TB_CHECK(H > 0 && Hkv > 0 && d > 0 && H % Hkv == 0, "heads must divide: H %d, Hkv %d", H, Hkv);
+    const int G = H / Hkv;
+    bool okg = (G == 1 && (d == 16 || d == 32 || d == 64 || d == 128)) ||
+               (G == 2 && (d == 16 || d == 32 || d == 64 || d == 128)) ||
+               (G == 4 && (d == 16 || d == 32 || d == 64 || d == 128)) || (G == 8 && (d == 16 || d == 32 || d == 64));
+    if (!okg) return fail(TB_ERR_UNSUPPORTED, "unsupported head geometry G=%d d=%d", G, d);
+    return ok();
+}
+
+static tb_status run_paged_attention(tb_context* ctx, const float* q, int batch, const float* pool,
+                                     const int* ptab, int ptab_stride, const int* lens, int max_len, int layer,
+                                     int num_layers, int H, int Hkv, int d, float* out) {
+    const int G = H / Hkv;
+    const int max_pages = (max_len + kPageTokens - 1) / kPageTokens;
+    const int ns = choose_nsplit(batch, Hkv, std::max(1, max_pages), ctx->num_sms);
+    tb_status s = ensure(ctx->scratch, attention_scratch_bytes(batch, Hkv, ns, G, d));
+    if (s != TB_OK) return s;
+    const size_t tb = attention_ticket_count(batch, Hkv) * 4;
+    if (ctx->tickets.bytes < tb) {
+        s = ensure(ctx->tickets, tb);
+        if (s != TB_OK) return s;
+        TB_CUDA(cudaMemsetAsync(ctx->tickets.p, 0, ctx->tickets.bytes, ctx->stream));
+    }
+    AttnParams a{};
+    a.q = q;
+    a.ld_q = H * d;
+    a.kv_pool = pool;
+    a.page_table = ptab;
+    a.ptab_stride = ptab_stride;
+    a.lens = lens;
+    a.seq = nullptr;
+    a.layer = layer;
+    a.num_layers = num_layers;
+    a.H = H;
+    a.Hkv = Hkv;
+    a.d = d;
+    a.M = batch;
+    a.nsplit = ns;
+    a.out = out;
+    a.ld_out = H * d;
+    a.part = ctx->scratch.as<float>();
+    a.tickets = ctx->tickets.as<unsigned int>();
+    a.err = ctx->err.as<int>();
+    TB_CUDA(launch_attention(a, ctx->stream, false));
+    return ok();
+}
+
+extern "C" tb_status tb_paged_attention_dev(tb_context* ctx, const float* q, int32_t batch, const float* pool,
+                                            const int32_t* ptab, int32_t ptab_stride, const int32_t* lens,
+                                            int32_t max_len, int32_t layer, int32_t num_layers, int32_t H,
+                                            int32_t Hkv, int32_t d, float* out) {
+    TB_CHECK(ctx && q && pool && ptab && lens && out, "NULL argument");
+    TB_CHECK(batch >= 1 && max_len >= 1 && layer >= 0 && layer < num_layers, "bad batch/len/layer");
+    tb_status s = check_heads(H, Hkv, d);
+    if (s != TB_OK) return s;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    return run_paged_attention(ctx, q, batch, pool, ptab, ptab_stride, lens, max_len, layer, num_layers, H, Hkv, d,
+                               out);
+}
+
+extern "C" tb_status tb_attention_decode(tb_context* ctx, const float* q, const float* K, const float* V, int64_t L,
+                                         int32_t H, int32_t Hkv, int32_t d, float* out) {
+    TB_CHECK(ctx && q && K && V && out, "NULL argument");
+    TB_CHECK(L >= 1 && L < (1ll << 24), "L out of range");
+    tb_status s = check_heads(H, Hkv, d);
+    if (s != TB_OK) return s;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    const int64_t kvdim = (int64_t)Hkv * d;
+    const int64_t pages = (L + kPageTokens - 1) / kPageTokens;
+    const size_t pool_b = (size_t)pages * 2 * kvdim * kPageTokens * 4;
+    DevBuf dk, dv, pool, ptab, lens, dq, dout;
+    TB_CUDA(dk.alloc((size_t)L * kvdim * 4));
+    TB_CUDA(dv.alloc((size_t)L * kvdim * 4));
+    TB_CUDA(pool.alloc(pool_b));
+    TB_CUDA(ptab.alloc((size_t)pages * 4));
+    TB_CUDA(lens.alloc(4));
+    TB_CUDA(dq.alloc((size_t)H * d * 4));
+    TB_CUDA(dout.alloc((size_t)H * d * 4));
+    TB_CUDA(cudaMemsetAsync(pool.p, 0, pool_b, ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(dk.p, K, (size_t)L * kvdim * 4, cudaMemcpyHostToDevice, ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(dv.p, V, (size_t)L * kvdim * 4, cudaMemcpyHostToDevice, ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(dq.p, q, (size_t)H * d * 4, cudaMemcpyHostToDevice, ctx->stream));
+    const int l32 = (int)L;
+    TB_CUDA(cudaMemcpyAsync(lens.p, &l32, 4, cudaMemcpyHostToDevice, ctx->stream));
+    const int64_t tot = L * kvdim;
+    pack_kv_contig_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, ctx->stream>>>(
+        dk.as<float>(), dv.as<float>(), L, Hkv, d, pool.as<float>());
+    iota_kernel<<<(unsigned)((pages + 255) / 256), 256, 0, ctx->stream>>>(ptab.as<int>(), (int)pages);
+    TB_CUDA(cudaGetLastError());
+    s = run_paged_attention(ctx, dq.as<float>(), 1, pool.as<float>(), ptab.as<int>(), (int)pages, lens.as<int>(),
+                            (int)L, 0, 1, H, Hkv, d, dout.as<float>());
+    if (s != TB_OK) return s;
+    TB_CUDA(cudaMemcpyAsync(out, dout.p, (size_t)H * d * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return tb_context_check_device(ctx);
+}
+
+// ---------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------
+extern "C" tb_status tb_model_create(tb_context* ctx, const tb_model_config* cfg, tb_model** out) {
+    TB_CHECK(ctx && cfg && out, "NULL argument");
+    *out = nullptr;
+    const tb_model_config& c = *cfg;
+    TB_CHECK(c.num_layers > 0 && c.hidden_dim > 0 && c.num_heads > 0 && c.num_kv_heads > 0 && c.vocab_size > 0 &&
+                 c.max_seq_len > 0 && c.intermediate_dim > 0,
+             "config fields must be positive");
+    TB_CHECK(c.hidden_dim % c.num_heads == 0, "hidden_dim must be a multiple of num_heads");
+    TB_CHECK(c.architecture == TB_ARCH_LLAMA || c.architecture == TB_ARCH_TOY, "unknown architecture %d",
+             c.architecture);
+    const int d = c.hidden_dim / c.num_heads;
+    tb_status s = check_heads(c.num_heads, c.num_kv_heads, d);
+    if (s != TB_OK) return s;
+    TB_CHECK(c.hidden_dim % 32 == 0 && (d * c.num_kv_heads) % 32 == 0,
+             "hidden_dim and kv_dim must be multiples of 32");
+    auto m = std::make_unique<tb_model>();
+    m->ctx = ctx;
+    m->cfg = c;
+    if (m->cfg.rms_eps == 0.0f) m->cfg.rms_eps = 1e-5f;
+    m->head_dim = d;
+    m->kv_dim = d * c.num_kv_heads;
+    m->layers.resize(c.num_layers);
+    *out = m.release();
+    return ok();
+}
+
+extern "C" tb_status tb_model_free(tb_model* m) {
+    if (m) {
+        cudaSetDevice(m->ctx->device);
+        delete m;
+    }
+    return ok();
+}
+
+extern "C" tb_status tb_model_set_embedding(tb_model* m, const float* emb) {
+    TB_CHECK(m && emb, "NULL argument");
+    TB_CHECK(!m->finalized, "model already finalized");
+    TB_CUDA(cudaSetDevice(m->ctx->device));
+    const size_t b = (size_t)m->cfg.vocab_size * m->cfg.hidden_dim * 4;
+    TB_CUDA(m->emb.alloc(b));
+    TB_CUDA(cudaMemcpy(m->emb.p, emb, b, cudaMemcpyHostToDevice));
+    return ok();
+}
+
+extern "C" tb_status tb_model_set_final_norm(tb_model* m, const float* w) {
+    TB_CHECK(m, "NULL model");
+    TB_CHECK(!m->finalized, "model already finalized");
+    TB_CUDA(cudaSetDevice(m->ctx->device));
+    if (!w) {
+        m->has_final_norm = false;
+        return ok();
+    }
+    TB_CUDA(m->final_norm.alloc((size_t)m->cfg.hidden_dim * 4));
+    TB_CUDA(cudaMemcpy(m->final_norm.p, w, (size_t)m->cfg.hidden_dim * 4, cudaMemcpyHostToDevice));
+    m->has_final_norm = true;
+    return ok();
+}
+
+extern "C" tb_status tb_model_set_layer_norms(tb_model* m, int32_t layer, const float* in, const float* post) {
+    TB_CHECK(m && layer >= 0 && layer < m->cfg.num_layers, "bad model/layer");
+    TB_CHECK(!m->finalized, "model already finalized");
+    Layer& L = m->layers[layer];
+    const int H = m->cfg.hidden_dim;
+    L.in_norm.assign(in ? in : (const float*)nullptr, in ? in + H : (const float*)nullptr);
+    L.post_norm.assign(post ? post : (const float*)nullptr, post ? post + H : (const float*)nullptr);
+    return ok();
+}
+
+static tb_status expected_shape(const tb_model* m, int which, int& K, int& N) {
+    const int H = m->cfg.hidden_dim, I = m->cfg.intermediate_dim;
+    switch (which) {
+        case TB_PROJ_Q: K = H; N = H; break;
+        case TB_PROJ_K:
+        case TB_PROJ_V: K = H; N = m->kv_dim; break;
+        case TB_PROJ_O: K = H; N = H; break;
+        case TB_PROJ_GATE:
+        case TB_PROJ_UP: K = H; N = I; break;
+        case TB_PROJ_DOWN: K = I; N = H; break;
+        default: return fail(TB_ERR_INVALID_ARGUMENT, "unknown projection %d", which);
+    }
+    return ok();
+}
+
+extern "C" tb_status tb_model_set_projection(tb_model* m, int32_t layer, int32_t which, const tb_qtensor_desc* d,
+                                             const float* bias) {
+    TB_CHECK(m && layer >= 0 && layer < m->cfg.num_layers, "bad model/layer");
+    TB_CHECK(!m->finalized, "model already finalized");
+    int K = 0, N = 0;
+    tb_status s = expected_shape(m, which, K, N);
+    if (s != TB_OK) return s;
+    TB_CHECK(d && d->in_features == K && d->out_features == N,
+             "projection %d of layer %d must be [%d, %d] (got [%lld, %lld])", which, layer, K, N,
+             d ? (long long)d->in_features : -1ll, d ? (long long)d->out_features : -1ll);
+    TB_CUDA(cudaSetDevice(m->ctx->device));
+    ProjStage& st = m->layers[layer].stage[which];
+    s = stage_desc(m->ctx, d, st);
+    if (s != TB_OK) return s;
+    if (bias)
+        st.bias.assign(bias, bias + N);
+    else
+        st.bias.clear();
+    return ok();
+}
+
+extern "C" tb_status tb_model_set_output(tb_model* m, const tb_qtensor_desc* d, const float* bias) {
+    TB_CHECK(m, "NULL model");
+    TB_CHECK(!m->finalized, "model already finalized");
+    TB_CHECK(d && d->in_features == m->cfg.hidden_dim && d->out_features == m->cfg.vocab_size,
+             "output projection must be [%d, %d]", m->cfg.hidden_dim, m->cfg.vocab_size);
+    TB_CUDA(cudaSetDevice(m->ctx->device));
+    tb_status s = stage_desc(m->ctx, d, m->out_stage);
+    if (s != TB_OK) return s;
+    if (bias)
+        m->out_stage.bias.assign(bias, bias + m->cfg.vocab_size);
+    else
+        m->out_stage.bias.clear();
+    return ok();
+}
+
+// Scatter per-projection biases into the fused GPU row space.
+static tb_status upload_bias(FusedWeight& f, const std::vector<std::pair<const ProjStage*, std::pair<int, int>>>& parts) {
+    bool any = false;
+    for (auto& pr : parts)
+        if (!pr.first->bias.empty()) any = true;
+    f.has_bias = any;
+    if (!any) return ok();
+    std::vector<float> hb((size_t)f.L.Np, 0.0f);
+    for (auto& pr : parts) {
+        const ProjStage* st = pr.first;
+        const int off = pr.second.first, inter = pr.second.second;
+        for (int n = 0; n < (int)st->bias.size(); ++n) {
+            int row = inter == 0 ? off + n : (n / 32) * 64 + (inter == 2 ? 32 : 0) + n % 32;
+            hb[row] = st->bias[n];
+        }
+    }
+    TB_CUDA(f.bias.alloc(hb.size() * 4));
+    TB_CUDA(cudaMemcpy(f.bias.p, hb.data(), hb.size() * 4, cudaMemcpyHostToDevice));
+    return ok();
+}
+
+extern "C" tb_status tb_model_finalize(tb_model* m) {
+    TB_CHECK(m, "NULL model");
+    if (m->finalized) return ok();
+    tb_context* ctx = m->ctx;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    const tb_model_config& c = m->cfg;
+    const int H = c.hidden_dim, I = c.intermediate_dim, kvd = m->kv_dim;
+    const bool llama = c.architecture == TB_ARCH_LLAMA;
+    if (!m->emb.p) return fail(TB_ERR_STATE, "embedding not set");
+    if (!m->out_stage.set) return fail(TB_ERR_STATE, "output projection not set");
+    int64_t wbytes = 0;
+    for (int l = 0; l < c.num_layers; ++l) {
+        Layer& L = m->layers[l];
+        for (int w : {TB_PROJ_Q, TB_PROJ_K, TB_PROJ_V, TB_PROJ_O, TB_PROJ_UP, TB_PROJ_DOWN})
+            if (!L.stage[w].set) return fail(TB_ERR_STATE, "layer %d projection %d not set", l, w);
+        if (llama && !L.stage[TB_PROJ_GATE].set) return fail(TB_ERR_STATE, "layer %d gate projection not set", l);
+        const int pq = L.stage[TB_PROJ_Q].precision;
+        if (L.stage[TB_PROJ_K].precision != pq || L.stage[TB_PROJ_V].precision != pq ||
+            (L.stage[TB_PROJ_K].gs != L.stage[TB_PROJ_Q].gs && pq == 4))
+            return fail(TB_ERR_UNSUPPORTED, "layer %d: q, k, v must share precision", l);
+        tb_status s = alloc_fused(ctx, L.qkv, make_qlayout(pq, H, H + 2 * kvd, 32));
+        if (s != TB_OK) return s;
+        if ((s = repack_into(ctx, L.qkv, L.stage[TB_PROJ_Q], 0, 0)) != TB_OK) return s;
+        if ((s = repack_into(ctx, L.qkv, L.stage[TB_PROJ_K], H, 0)) != TB_OK) return s;
+        if ((s = repack_into(ctx, L.qkv, L.stage[TB_PROJ_V], H + kvd, 0)) != TB_OK) return s;
+        if ((s = upload_bias(L.qkv, {{&L.stage[TB_PROJ_Q], {0, 0}},
+                                     {&L.stage[TB_PROJ_K], {H, 0}},
+                                     {&L.stage[TB_PROJ_V], {H + kvd, 0}}})) != TB_OK)
+            return s;
+        if ((s = alloc_fused(ctx, L.o, make_qlayout(L.stage[TB_PROJ_O].precision, H, H, 32))) != TB_OK) return s;
+        if ((s = repack_into(ctx, L.o, L.stage[TB_PROJ_O], 0, 0)) != TB_OK) return s;
+        if ((s = upload_bias(L.o, {{&L.stage[TB_PROJ_O], {0, 0}}})) != TB_OK) return s;
+        if (llama) {
+            const int pg = L.stage[TB_PROJ_GATE].precision;
+            if (L.stage[TB_PROJ_UP].precision != pg)
+                return fail(TB_ERR_UNSUPPORTED, "layer %d: gate and up must share precision", l);
+            const int Ip = (I + 31) / 32 * 32;
+            QLayout gl = make_qlayout(pg, H, 2 * Ip, 64);
+            gl.N = I;
+            if ((s = alloc_fused(ctx, L.up, gl)) != TB_OK) return s;
+            if ((s = repack_into(ctx, L.up, L.stage[TB_PROJ_GATE], 0, 1)) != TB_OK) return s;
+            if ((s = repack_into(ctx, L.up, L.stage[TB_PROJ_UP], 0, 2)) != TB_OK) return s;
+            if ((s = upload_bias(L.up, {{&L.stage[TB_PROJ_GATE], {0, 1}}, {&L.stage[TB_PROJ_UP], {0, 2}}})) != TB_OK)
+                return s;
+        } else {
+            if ((s = alloc_fused(ctx, L.up, make_qlayout(L.stage[TB_PROJ_UP].precision, H, I, 32))) != TB_OK)
+                return s;
+            if ((s = repack_into(ctx, L.up, L.stage[TB_PROJ_UP], 0, 0)) != TB_OK) return s;
+            if ((s = upload_bias(L.up, {{&L.stage[TB_PROJ_UP], {0, 0}}})) != TB_OK) return s;
+        }
+        if ((s = alloc_fused(ctx, L.down, make_qlayout(L.stage[TB_PROJ_DOWN].precision, I, H, 32))) != TB_OK)
+            return s;
+        if ((s = repack_into(ctx, L.down, L.stage[TB_PROJ_DOWN], 0, 0)) != TB_OK) return s;
+        if ((s = upload_bias(L.down, {{&L.stage[TB_PROJ_DOWN], {0, 0}}})) != TB_OK) return s;
+        if (!L.in_norm.empty()) {
+            TB_CUDA(L.in_norm_d.alloc((size_t)H * 4));
+            TB_CUDA(cudaMemcpy(L.in_norm_d.p, L.in_norm.data(), (size_t)H * 4, cudaMemcpyHostToDevice));
+        }
+        if (!L.post_norm.empty()) {
+            TB_CUDA(L.post_norm_d.alloc((size_t)H * 4));
+            TB_CUDA(cudaMemcpy(L.post_norm_d.p, L.post_norm.data(), (size_t)H * 4, cudaMemcpyHostToDevice));
+        }
+        TB_CUDA(cudaStreamSynchronize(ctx->stream));
+        for (auto& st : L.stage) {
+            st.data.release();
+            st.scales.release();
+        }
+        for (FusedWeight* f : {&L.qkv, &L.o, &L.up, &L.down})
+            wbytes += (int64_t)f->L.weight_bytes + (int64_t)f->L.scale_floats * 4;
+    }
+    tb_status s = alloc_fused(ctx, m->out, make_qlayout(m->out_stage.precision, H, c.vocab_size, 32));
+    if (s != TB_OK) return s;
+    if ((s = repack_into(ctx, m->out, m->out_stage, 0, 0)) != TB_OK) return s;
+    if ((s = upload_bias(m->out, {{&m->out_stage, {0, 0}}})) != TB_OK) return s;
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    m->out_stage.data.release();
+    m->out_stage.scales.release();
+    wbytes += (int64_t)m->out.L.weight_bytes + (int64_t)m->out.L.scale_floats * 4;
+    m->weight_bytes = wbytes;
+    m->finalized = true;
+    return tb_context_check_device(ctx);
+}
+
+extern "C" tb_status tb_model_weight_bytes(const tb_model* m, int64_t* bytes) {
+    TB_CHECK(m && bytes, "NULL argument");
+    *bytes = m->weight_bytes;
+    return ok();
+}
+
+// ---------------------------------------------------------------------------
+// runner
+// ---------------------------------------------------------------------------
+static void fill_gemv_common(tb_runner* r, GemvParams& p, const FusedWeight& f) {
+    p.w = f.w.as<uint8_t>();
+    p.scales = f.s.as<float>();
+    p.bias = f.has_bias ? f.bias.as<float>() : nullptr;
+    p.L = f.L;
+    p.M = r->B;
+    p.P = choose_ksplit(f.L, r->B, r->ctx->num_sms);
+    p.eps = r->m->cfg.rms_eps;
+    p.vocab = r->m->cfg.vocab_size;
+    p.seq_ro = r->seq.as<SeqState>();
+    p.seq = r->seq.as<SeqState>();
+    p.err = r->ctx->err.as<int>();
+}
+
+static int64_t gemv_bytes(const QLayout& L, int M) {
+    // streamed weights + scales + activations in and out (fp32)
+    int64_t w = (int64_t)L.Np * L.row_bytes + (int64_t)L.scale_floats * 4;
+    return w + (int64_t)M * (L.K + L.N) * 4;
+}
+
+static tb_status build_plan(tb_runner* r) {
+    tb_model* m = r->m;
+    const tb_model_config& c = m->cfg;
+    const int H = c.hidden_dim, d = m->head_dim, kvd = m->kv_dim, B = r->B;
+    const bool llama = c.architecture == TB_ARCH_LLAMA;
+    r->plan.clear();
+    for (int l = 0; l < c.num_layers; ++l) {
+        Layer& Ly = m->layers[l];
+        const bool has_in = Ly.in_norm_d.p != nullptr, has_post = Ly.post_norm_d.p != nullptr;
+        {  // fused QKV (+ embedding gather at layer 0) + RoPE + KV append
+            Launch ln{};
+            ln.kind = 0;
+            GemvParams& p = ln.g;
+            fill_gemv_common(r, p, Ly.qkv);
+            if (l == 0)
+                p.prologue = has_in ? kProEmbedRms : kProEmbed;
+            else
+                p.prologue = has_in ? kProRmsNorm : kProNone;
+            p.src = r->h.as<float>();
+            p.ld_src = H;
+            p.norm_w = Ly.in_norm_d.as<float>();
+            p.embedding = m->emb.as<float>();
+            p.resid = r->h.as<float>();
+            p.epilogue = kEpiQkv;
+            p.out = r->q.as<float>();
+            p.ld_out = H;
+            p.H = H;
+            p.Hkv = c.num_kv_heads;
+            p.head_dim = d;
+            p.kv_dim = kvd;
+            p.rope = r->rope.as<float2>();
+            p.rope_max_pos = r->max_positions;
+            p.kv_pool = r->kv.as<float>();
+            p.page_table = r->ptab.as<int>();
+            p.ptab_stride = r->ptab_stride;
+            p.layer = l;
+            p.num_layers = c.num_layers;
+            ln.bytes = gemv_bytes(Ly.qkv.L, B) + (int64_t)B * 2 * kvd * 4;
+            r->plan.push_back(ln);
+        }
+        {  // attention
+            Launch ln{};
+            ln.kind = 1;
+            AttnParams& a = ln.a;
+            a.q = r->q.as<float>();
+            a.ld_q = H;
+            a.kv_pool = r->kv.as<float>();
+            a.page_table = r->ptab.as<int>();
+            a.ptab_stride = r->ptab_stride;
+            a.seq = r->seq.as<SeqState>();
+            a.lens = nullptr;
+            a.layer = l;
+            a.num_layers = c.num_layers;
+            a.H = c.num_heads;
+            a.Hkv = c.num_kv_heads;
+            a.d = d;
+            a.M = B;
+            a.nsplit = r->nsplit;
+            a.out = r->ctxv.as<float>();
+            a.ld_out = H;
+            a.part = r->attn_part.as<float>();
+            a.tickets = r->attn_tickets.as<unsigned int>();
+            a.err = r->ctx->err.as<int>();
+            ln.bytes = 0;  // depends on the context length; accounted by the caller
+            r->plan.push_back(ln);
+        }
+        {  // o_proj + residual
+            Launch ln{};
+            ln.kind = 0;
+            GemvParams& p = ln.g;
+            fill_gemv_common(r, p, Ly.o);
+            p.prologue = kProNone;
+            p.src = r->ctxv.as<float>();
+            p.ld_src = H;
+            p.epilogue = kEpiResidual;
+            p.out = r->h.as<float>();
+            p.ld_out = H;
+            ln.bytes = gemv_bytes(Ly.o.L, B) + (int64_t)B * H * 4;
+            r->plan.push_back(ln);
+        }
+        {  // gate/up (+ post-attention RMSNorm) + SiLU*up, or toy up + GELU
+            Launch ln{};
+            ln.kind = 0;
+            GemvParams& p = ln.g;
+            fill_gemv_common(r, p, Ly.up);
+            p.prologue = has_post ? kProRmsNorm : kProNone;
+            p.src = r->h.as<float>();
+            p.ld_src = H;
+            p.norm_w = Ly.post_norm_d.as<float>();
+            p.epilogue = llama ? kEpiSiluMul : kEpiGelu;
+            p.out = r->act.as<float>();
+            p.ld_out = c.intermediate_dim;
+            ln.bytes = gemv_bytes(Ly.up.L, B);
+            r->plan.push_back(ln);
+        }
+        {  // down + residual
+            Launch ln{};
+            ln.kind = 0;
+            GemvParams& p = ln.g;
+            fill_gemv_common(r, p, Ly.down);
+            p.prologue = kProNone;
+            p.src = r->act.as<float>();
+            p.ld_src = c.intermediate_dim;
+            p.epilogue = kEpiResidual;
+            p.out = r->h.as<float>();
+            p.ld_out = H;
+            ln.bytes = gemv_bytes(Ly.down.L, B) + (int64_t)B * H * 4;
+            r->plan.push_back(ln);
+        }
+    }
+    {  // final norm + LM head + argmax + step bookkeeping
+        Launch ln{};
+        ln.kind = 0;
+        GemvParams& p = ln.g;
+        fill_gemv_common(r, p, m->out);
+        p.prologue = m->has_final_norm ? kProRmsNorm : kProNone;
+        p.src = r->h.as<float>();
+        p.ld_src = H;
+        p.norm_w = m->final_norm.as<float>();
+        p.epilogue = kEpiArgmax;
+        p.out = nullptr;
+        p.logits = r->logits.as<float>();
+        p.ticket = r->ticket.as<unsigned int>();
+        p.out_tokens = r->out_tokens.as<int>();
+        p.prompt = r->prompt.as<int>();
+        p.prompt_stride = r->prompt_stride;
+        ln.bytes = gemv_bytes(m->out.L, B);
+        r->plan.push_back(ln);
+    }
+    return ok();
+}
+
+static tb_status record_plan(tb_runner* r, cudaStream_t st, bool pdl) {
+    for (const Launch& ln : r->plan) {
+        cudaError_t e = ln.kind == 0 ? launch_gemv(ln.g, st, pdl) : launch_attention(ln.a, st, pdl);
+        if (e != cudaSuccess) return cuda_fail(e, ln.kind == 0 ? "launch_gemv" : "launch_attention");
+    }
+    return ok();
+}
+
+static tb_status capture_graph(tb_runner* r) {
+    if (r->graph) return ok();
+    cudaStream_t st = r->ctx->stream;
+    cudaGraph_t g = nullptr;
+    TB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    tb_status s = record_plan(r, st, true);
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (s != TB_OK) {
+        if (g) cudaGraphDestroy(g);
+        return s;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&r->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+    return ok();
+}
+
+extern "C" tb_status tb_runner_create(tb_model* m, int32_t max_batch, int32_t max_positions, tb_runner** out) {
+    TB_CHECK(m && out, "NULL argument");
+    *out = nullptr;
+    TB_CHECK(m->finalized, "model not finalized");
+    TB_CHECK(max_batch >= 1 && max_batch <= 8, "max_batch must be in [1, 8] (got %d)", max_batch);
+    tb_context* ctx = m->ctx;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    const tb_model_config& c = m->cfg;
+    auto r = std::make_unique<tb_runner>();
+    r->m = m;
+    r->ctx = ctx;
+    r->B = max_batch;
+    r->max_positions = std::max(max_positions, c.max_seq_len);
+    r->ptab_stride = (r->max_positions + kPageTokens - 1) / kPageTokens;
+    r->max_pages_per_seq = (c.max_seq_len + kPageTokens - 1) / kPageTokens;
+    r->total_pages = r->max_pages_per_seq * max_batch;
+    const int H = c.hidden_dim, d = m->head_dim, kvd = m->kv_dim, B = max_batch;
+    const size_t page_floats = (size_t)c.num_layers * 2 * kvd * kPageTokens;
+    TB_CUDA(r->seq.alloc(sizeof(SeqState) * B));
+    TB_CUDA(r->ptab.alloc((size_t)B * r->ptab_stride * 4));
+    TB_CUDA(r->kv.alloc((size_t)r->total_pages * page_floats * 4));
+    TB_CUDA(r->h.alloc((size_t)B * H * 4));
+    TB_CUDA(r->q.alloc((size_t)B * H * 4));
+    TB_CUDA(r->ctxv.alloc((size_t)B * H * 4));
+    TB_CUDA(r->act.alloc((size_t)B * c.intermediate_dim * 4));
+    TB_CUDA(r->logits.alloc((size_t)B * c.vocab_size * 4));
+    TB_CUDA(r->ticket.alloc(16));
+    TB_CUDA(cudaMemset(r->ticket.p, 0, 16));
+    TB_CUDA(cudaMemset(r->seq.p, 0, sizeof(SeqState) * B));
+    TB_CUDA(cudaMemset(r->kv.p, 0, r->kv.bytes));
+    // RoPE table with the reference's fp32 formula (ModelRunner.swift:478-486).
+    {
+        std::vector<float2> tab((size_t)r->max_positions * (d / 2));
+        for (int pos = 0; pos < r->max_positions; ++pos)
+            for (int i = 0; i < d; i += 2) {
+                const float freq = (float)i / (float)d;
+                const float theta = powf(10000.0f, -freq);
+                const float angle = (float)pos * theta;
+                tab[(size_t)pos * (d / 2) + i / 2] = make_float2(cosf(angle), sinf(angle));
+            }
+        TB_CUDA(r->rope.alloc(tab.size() * sizeof(float2)));
+        TB_CUDA(cudaMemcpy(r->rope.p, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    }
+    // Host page bookkeeping.
+    r->kvh.assign(B, SeqKV{});
+    for (auto& s : r->kvh) s.map.assign(r->ptab_stride, -1);
+    r->free_pages.resize(r->total_pages);
+    for (int i = 0; i < r->total_pages; ++i) r->free_pages[i] = r->total_pages - 1 - i;
+    r->ptab_host.assign((size_t)B * r->ptab_stride, -1);
+    r->ptab_dirty.assign(B, 1);
+    TB_CUDA(r->pin_ptab.ensure(r->ptab_host.size() * 4));
+    TB_CUDA(r->pin_seq.ensure(sizeof(SeqState) * B));
+    // Attention scratch sized for the longest context.
+    r->nsplit = choose_nsplit(B, c.num_kv_heads, r->ptab_stride, ctx->num_sms);
+    TB_CUDA(r->attn_part.alloc(attention_scratch_bytes(B, c.num_kv_heads, r->nsplit, c.num_heads / c.num_kv_heads, d)));
+    TB_CUDA(r->attn_tickets.alloc(attention_ticket_count(B, c.num_kv_heads) * 4));
+    TB_CUDA(cudaMemset(r->attn_tickets.p, 0, r->attn_tickets.bytes));
+    tb_status s = TB_OK;
+    // Prompt / output buffers start small and grow in generate.
+    r->prompt_stride = 1;
+    r->max_out = 1;
+    TB_CUDA(r->prompt.alloc((size_t)B * 4));
+    TB_CUDA(r->out_tokens.alloc((size_t)B * 4));
+    TB_CUDA(cudaEventCreate(&r->ev0));
+    TB_CUDA(cudaEventCreate(&r->ev1));
+    if ((s = build_plan(r.get())) != TB_OK) return s;
+    TB_CUDA(cudaDeviceSynchronize());
+    *out = r.release();
+    return ok();
+}
+
+extern "C" tb_status tb_runner_free(tb_runner* r) {
+    if (r) {
+        cudaSetDevice(r->ctx->device);
+        cudaStreamSynchronize(r->ctx->stream);
+        delete r;
+    }
+    return ok();
+}
+
+// KVCache.evictOldestPage (KVCache.swift:293-308): drop the lowest logical page.
+static void kv_evict_oldest(tb_runner* r, int s) {
+    SeqKV& k = r->kvh[s];
+    for (size_t i = 0; i < k.map.size(); ++i)
+        if (k.map[i] >= 0) {
+            r->free_pages.push_back(k.map[i]);
+            k.map[i] = -1;
+            k.pages_held -= 1;
+            r->ptab_host[(size_t)s * r->ptab_stride + i] = -1;
+            r->ptab_dirty[s] = 1;
+            return;
+        }
+}
+
+// KVCache.append (KVCache.swift:157-224) bookkeeping for sequence s at its
+// current position: eviction, page allocation (zero-filled), length update.
+static tb_status kv_prepare(tb_runner* r, int s) {
+    SeqKV& k = r->kvh[s];
+    const int64_t maxTokens = r->m->cfg.max_seq_len;
+    const int64_t pos = k.pos;
+    if (pos >= r->max_positions)
+        return fail(TB_ERR_INVALID_ARGUMENT, "position %lld exceeds the runner's max_positions %d", (long long)pos,
+                    r->max_positions);
+    while (k.length >= maxTokens) {
+        kv_evict_oldest(r, s);
+        k.length = std::max<int64_t>(0, k.length - kPageTokens);
+    }
+    const int64_t lp = pos / kPageTokens;
+    if (k.map[lp] < 0) {
+        if (k.pages_held >= r->max_pages_per_seq) kv_evict_oldest(r, s);
+        if (r->free_pages.empty() || k.pages_held >= r->max_pages_per_seq)
+            return fail(TB_ERR_PAGE_POOL_EXHAUSTED, "no free KV page for sequence %d", s);
+        const int pg = r->free_pages.back();
+        r->free_pages.pop_back();
+        k.map[lp] = pg;
+        k.pages_held += 1;
+        r->ptab_host[(size_t)s * r->ptab_stride + lp] = pg;
+        r->ptab_dirty[s] = 1;
+        const tb_model_config& c = r->m->cfg;
+        const size_t page_bytes = (size_t)c.num_layers * 2 * r->m->kv_dim * kPageTokens * 4;
+        TB_CUDA(cudaMemsetAsync(r->kv.as<uint8_t>() + (size_t)pg * page_bytes, 0, page_bytes, r->ctx->stream));
+    }
+    k.length = std::max<int64_t>(k.length, pos + 1);
+    if (k.length > maxTokens) k.length = maxTokens;
+    return ok();
+}
+
+static tb_status flush_ptab(tb_runner* r) {
+    for (int s = 0; s < r->B; ++s) {
+        if (!r->ptab_dirty[s]) continue;
+        int* pin = r->pin_ptab.as<int>() + (size_t)s * r->ptab_stride;
+        memcpy(pin, r->ptab_host.data() + (size_t)s * r->ptab_stride, (size_t)r->ptab_stride * 4);
+        TB_CUDA(cudaMemcpyAsync(r->ptab.as<int>() + (size_t)s * r->ptab_stride, pin, (size_t)r->ptab_stride * 4,
+                                cudaMemcpyHostToDevice, r->ctx->stream));
+        r->h2d_bytes += (int64_t)r->ptab_stride * 4;
+        r->ptab_dirty[s] = 0;
+    }
+    return ok();
+}
+
+static void kv_clear(tb_runner* r, int s) {
+    SeqKV& k = r->kvh[s];
+    for (size_t i = 0; i < k.map.size(); ++i)
+        if (k.map[i] >= 0) {
+            r->free_pages.push_back(k.map[i]);
+            k.map[i] = -1;
+            r->ptab_host[(size_t)s * r->ptab_stride + i] = -1;
+        }
+    k.pages_held = 0;
+    k.length = 0;
+    k.pos = 0;
+    r->ptab_dirty[s] = 1;
+}
+
+extern "C" tb_status tb_runner_reset(tb_runner* r) {
+    TB_CHECK(r, "NULL runner");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    for (int s = 0; s < r->B; ++s) kv_clear(r, s);
+    // Restore the canonical LIFO order (PageAllocator.reset, PageAllocator.swift:131-137).
+    r->free_pages.resize(r->total_pages);
+    for (int i = 0; i < r->total_pages; ++i) r->free_pages[i] = r->total_pages - 1 - i;
+    TB_CUDA(cudaMemsetAsync(r->seq.p, 0, sizeof(SeqState) * r->B, r->ctx->stream));
+    return flush_ptab(r);
+}
+
+extern "C" tb_status tb_runner_position(const tb_runner* r, int32_t seq, int64_t* pos) {
+    TB_CHECK(r && pos && seq >= 0 && seq < r->B, "bad argument");
+    *pos = r->kvh[seq].pos;
+    return ok();
+}
+extern "C" tb_status tb_runner_kv_length(const tb_runner* r, int32_t seq, int64_t* len) {
+    TB_CHECK(r && len && seq >= 0 && seq < r->B, "bad argument");
+    *len = r->kvh[seq].length;
+    return ok();
+}
+extern "C" tb_status tb_runner_max_pages(const tb_runner* r, int64_t* n) {
+    TB_CHECK(r && n, "bad argument");
+    *n = r->max_pages_per_seq;
+    return ok();
+}
+extern "C" tb_status tb_runner_page_status(const tb_runner* r, int32_t seq, uint8_t* status, int64_t n) {
+    TB_CHECK(r && status && seq >= 0 && seq < r->B, "bad argument");
+    for (int64_t i = 0; i < n; ++i)
+        status[i] = (i < (int64_t)r->kvh[seq].map.size() && r->kvh[seq].map[i] >= 0) ? 1 : 0;
+    return ok();
+}
+
+// Write the device SeqState array from the host values in pin_seq.
+static tb_status push_seq(tb_runner* r) {
+    TB_CUDA(cudaMemcpyAsync(r->seq.p, r->pin_seq.p, sizeof(SeqState) * r->B, cudaMemcpyHostToDevice,
+                            r->ctx->stream));
+    r->h2d_bytes += (int64_t)sizeof(SeqState) * r->B;
+    return ok();
+}
+
+static tb_status launch_step(tb_runner* r) {
+    tb_status s = capture_graph(r);
+    if (s != TB_OK) return s;
+    TB_CUDA(cudaGraphLaunch(r->graph, r->ctx->stream));
+    return ok();
+}
+
+extern "C" tb_status tb_runner_step(tb_runner* r, int32_t token, float* logits, int32_t* argmax_out) {
+    TB_CHECK(r, "NULL runner");
+    TB_CHECK(r->B == 1, "tb_runner_step drives batch-1 runners; use tb_runner_generate for batches");
+    const int V = r->m->cfg.vocab_size;
+    TB_CHECK(token >= 0 && token < V, "token %d outside [0, %d)", token, V);
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    tb_status s = kv_prepare(r, 0);
+    if (s != TB_OK) return s;
+    if ((s = flush_ptab(r)) != TB_OK) return s;
+    SeqState* st = r->pin_seq.as<SeqState>();
+    memset(st, 0, sizeof(SeqState));
+    st->pos = (int)r->kvh[0].pos;
+    st->token = token;
+    st->n_prompt = 0;
+    st->n_out = 0;
+    st->max_out = 0;
+    st->active = 1;
+    st->best = 0;
+    if ((s = push_seq(r)) != TB_OK) return s;
+    if ((s = launch_step(r)) != TB_OK) return s;
+    TB_CUDA(cudaMemcpyAsync(r->pin_seq.p, r->seq.p, sizeof(SeqState), cudaMemcpyDeviceToHost, r->ctx->stream));
+    if (logits)
+        TB_CUDA(cudaMemcpyAsync(logits, r->logits.p, (size_t)V * 4, cudaMemcpyDeviceToHost, r->ctx->stream));
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    r->kvh[0].pos += 1;
+    if (argmax_out) *argmax_out = r->pin_seq.as<SeqState>()->token;
+    return tb_context_check_device(r->ctx);
+}
+
+// Generation state kept between the split timing entry points.
+namespace {
+struct GenPlan {
+    std::vector<int> n_prompt;
+    int n_seqs = 0;
+    int max_new = 0;
+};
+}  // namespace
+
+static tb_status gen_setup(tb_runner* r, const int32_t* prompts, const int64_t* offs, int32_t n_seqs,
+                           int32_t max_new, GenPlan& gp) {
+    TB_CHECK(prompts || n_seqs == 0 || (offs && offs[n_seqs] == offs[0]), "prompts is NULL");
+    TB_CHECK(offs, "prompt_offsets is NULL");
+    TB_CHECK(n_seqs >= 1 && n_seqs <= r->B, "n_seqs must be in [1, %d]", r->B);
+    TB_CHECK(max_new >= 0, "max_new_tokens must be >= 0");
+    const int V = r->m->cfg.vocab_size;
+    gp.n_seqs = n_seqs;
+    gp.max_new = max_new;
+    gp.n_prompt.assign(r->B, 0);
+    int maxp = 1;
+    for (int s = 0; s < n_seqs; ++s) {
+        const int64_t n = offs[s + 1] - offs[s];
+        TB_CHECK(n >= 0, "prompt offsets must be non-decreasing");
+        gp.n_prompt[s] = (int)n;
+        maxp = std::max<int>(maxp, (int)n);
+    }
+    // (Re)size prompt/output buffers.
+    if (maxp > r->prompt_stride || r->B * (size_t)maxp * 4 > r->prompt.bytes) {
+        r->prompt_stride = maxp;
+        TB_CUDA(r->prompt.alloc((size_t)r->B * maxp * 4));
+    }
+    const int mo = std::max(1, max_new);
+    if (mo > r->max_out) {
+        r->max_out = mo;
+        TB_CUDA(r->out_tokens.alloc((size_t)r->B * mo * 4));
+        for (Launch& ln : r->plan)
+            if (ln.kind == 0 && ln.g.epilogue == kEpiArgmax) {
+                ln.g.out_tokens = r->out_tokens.as<int>();
+            }
+        if (r->graph) {
+            cudaGraphExecDestroy(r->graph);
+            r->graph = nullptr;
+        }
+    }
+    for (Launch& ln : r->plan)
+        if (ln.kind == 0 && ln.g.epilogue == kEpiArgmax && (ln.g.prompt != r->prompt.as<int>() ||
+                                                            ln.g.prompt_stride != r->prompt_stride)) {
+            ln.g.prompt = r->prompt.as<int>();
+            ln.g.prompt_stride = r->prompt_stride;
+            if (r->graph) {
+                cudaGraphExecDestroy(r->graph);
+                r->graph = nullptr;
+            }
+        }
+    TB_CUDA(r->pin_tokens.ensure((size_t)r->B * std::max(maxp, mo) * 4 + 64));
+    int* pin = r->pin_tokens.as<int>();
+    memset(pin, 0, (size_t)r->B * r->prompt_stride * 4);
+    for (int s = 0; s < n_seqs; ++s)
+        for (int i = 0; i < gp.n_prompt[s]; ++i) {
+            int t = prompts[offs[s] + i];
+            pin[(size_t)s * r->prompt_stride + i] = std::max(0, std::min(t, V - 1));  // ModelRunner.swift:236
+        }
+    TB_CUDA(cudaMemcpyAsync(r->prompt.p, pin, (size_t)r->B * r->prompt_stride * 4, cudaMemcpyHostToDevice,
+                            r->ctx->stream));
+    r->h2d_bytes += (int64_t)r->B * r->prompt_stride * 4;
+    // Fresh sequences (generateStream on a reset runner).
+    for (int s = 0; s < r->B; ++s) kv_clear(r, s);
+    SeqState* st = r->pin_seq.as<SeqState>();
+    memset(st, 0, sizeof(SeqState) * r->B);
+    for (int s = 0; s < n_seqs; ++s) {
+        st[s].pos = 0;
+        st[s].token = gp.n_prompt[s] > 0 ? pin[(size_t)s * r->prompt_stride] : 0;
+        st[s].n_prompt = gp.n_prompt[s];
+        st[s].n_out = 0;
+        st[s].max_out = mo;
+        st[s].active = 1;
+        st[s].best = 0;
+    }
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    return ok();
+}
+
+// Run `steps` graph replays with host-side page bookkeeping.  `active[s]`
+// says which sequences advance in every one of these steps.
+static tb_status run_steps(tb_runner* r, int steps, const std::vector<char>& active) {
+    for (int t = 0; t < steps; ++t) {
+        for (int s = 0; s < r->B; ++s)
+            if (active[s]) {
+                tb_status e = kv_prepare(r, s);
+                if (e != TB_OK) return e;
+            }
+        tb_status e = flush_ptab(r);
+        if (e != TB_OK) return e;
+        if ((e = launch_step(r)) != TB_OK) return e;
+        for (int s = 0; s < r->B; ++s)
+            if (active[s]) r->kvh[s].pos += 1;
+    }
+    return ok();
+}
+
+// Prefill: each sequence steps all but the last prompt token
+// (ModelRunner.swift:240-244).  Sequences with shorter prompts wait (inactive)
+// until every prompt is consumed, so the decode loop runs the whole batch.
+static tb_status gen_prefill(tb_runner* r, const GenPlan& gp) {
+    SeqState* st = r->pin_seq.as<SeqState>();
+    int maxpre = 0;
+    for (int s = 0; s < gp.n_seqs; ++s) maxpre = std::max(maxpre, gp.n_prompt[s] - 1);
+    for (int t = 0; t < maxpre; ++t) {
+        // Activity changes only at prompt boundaries; push the flags when they do.
+        bool changed = (t == 0);
+        std::vector<char> act(r->B, 0);
+        for (int s = 0; s < gp.n_seqs; ++s) {
+            act[s] = (t < gp.n_prompt[s] - 1) ? 1 : 0;
+            if (t > 0 && (t < gp.n_prompt[s] - 1) != (t - 1 < gp.n_prompt[s] - 1)) changed = true;
+        }
+        if (changed) {
+            // The device state of paused sequences is preserved; only `active` changes.
+            TB_CUDA(cudaMemcpyAsync(r->pin_seq.p, r->seq.p, sizeof(SeqState) * r->B, cudaMemcpyDeviceToHost,
+                                    r->ctx->stream));
+            TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+            if (t == 0) {
+                // first prefill step: the host-written initial state is authoritative
+            }
+            for (int s = 0; s < r->B; ++s) st[s].active = act[s];
+            tb_status e = push_seq(r);
+            if (e != TB_OK) return e;
+        }
+        tb_status e = run_steps(r, 1, act);
+        if (e != TB_OK) return e;
+    }
+    return ok();
+}
+
+static tb_status gen_begin(tb_runner* r, const GenPlan& gp) {
+    // Push the initial state, then prefill.
+    tb_status e = push_seq(r);
+    if (e != TB_OK) return e;
+    return gen_prefill(r, gp);
+}
+
+static tb_status gen_activate_all(tb_runner* r, const GenPlan& gp) {
+    SeqState* st = r->pin_seq.as<SeqState>();
+    TB_CUDA(cudaMemcpyAsync(r->pin_seq.p, r->seq.p, sizeof(SeqState) * r->B, cudaMemcpyDeviceToHost,
+                            r->ctx->stream));
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    for (int s = 0; s < r->B; ++s) st[s].active = (s < gp.n_seqs && gp.max_new > 0) ? 1 : 0;
+    return push_seq(r);
+}
+
+static GenPlan g_last_plan;  // for the split timing entry points (single-threaded benchmark use)
+
+extern "C" tb_status tb_runner_generate(tb_runner* r, const int32_t* prompts, const int64_t* offs, int32_t n_seqs,
+                                        int32_t max_new, const int32_t* stop, int32_t n_stop, int32_t* out_tokens,
+                                        int32_t* out_counts, tb_token_callback cb, void* user) {
+    TB_CHECK(r && out_tokens && out_counts, "NULL argument");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    GenPlan gp;
+    tb_status e = gen_setup(r, prompts, offs, n_seqs, max_new, gp);
+    if (e != TB_OK) return e;
+    if ((e = gen_begin(r, gp)) != TB_OK) return e;
+    if ((e = gen_activate_all(r, gp)) != TB_OK) return e;
+    std::vector<char> act(r->B, 0);
+    for (int s = 0; s < n_seqs; ++s) act[s] = max_new > 0;
+    std::vector<int> count(n_seqs, 0);
+    const bool stepwise = (n_stop > 0 && stop) || cb;
+    if (!stepwise) {
+        if ((e = run_steps(r, max_new, act)) != TB_OK) return e;
+        TB_CUDA(cudaMemcpyAsync(r->pin_tokens.p, r->out_tokens.p, (size_t)r->B * r->max_out * 4,
+                                cudaMemcpyDeviceToHost, r->ctx->stream));
+        r->d2h_bytes += (int64_t)r->B * r->max_out * 4;
+        TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+        const int* pt = r->pin_tokens.as<int>();
+        for (int s = 0; s < n_seqs; ++s) {
+            for (int i = 0; i < max_new; ++i) out_tokens[(size_t)s * max_new + i] = pt[(size_t)s * r->max_out + i];
+            out_counts[s] = max_new;
+        }
+        return tb_context_check_device(r->ctx);
+    }
+    // Step-synchronous path: yield every token, honour stop tokens
+    // (ModelRunner.swift:272-292: the stop token is yielded, then the loop ends).
+    SeqState* st = r->pin_seq.as<SeqState>();
+    for (int t = 0; t < max_new; ++t) {
+        bool any = false;
+        for (int s = 0; s < n_seqs; ++s) any = any || act[s];
+        if (!any) break;
+        if ((e = run_steps(r, 1, act)) != TB_OK) return e;
+        TB_CUDA(cudaMemcpyAsync(r->pin_seq.p, r->seq.p, sizeof(SeqState) * r->B, cudaMemcpyDeviceToHost,
+                                r->ctx->stream));
+        r->d2h_bytes += (int64_t)sizeof(SeqState) * r->B;
+        TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+        bool changed = false;
+        for (int s = 0; s < n_seqs; ++s) {
+            if (!act[s]) continue;
+            // After a generating step the device stored the sampled token as the next input.
+            const int tok = st[s].token;
+            out_tokens[(size_t)s * max_new + count[s]] = tok;
+            count[s] += 1;
+            bool stop_now = false;
+            for (int k = 0; k < n_stop; ++k)
+                if (stop[k] == tok) stop_now = true;
+            if (cb && cb(user, s, count[s] - 1, tok) != 0) stop_now = true;
+            if (count[s] >= max_new) stop_now = true;
+            if (stop_now) {
+                act[s] = 0;
+                st[s].active = 0;
+                changed = true;
+            }
+        }
+        if (changed && (e = push_seq(r)) != TB_OK) return e;
+    }
+    for (int s = 0; s < n_seqs; ++s) out_counts[s] = count[s];
+    return tb_context_check_device(r->ctx);
+}
+
+extern "C" tb_status tb_runner_prefill_device(tb_runner* r, const int32_t* prompts, const int64_t* offs,
+                                              int32_t n_seqs, int32_t max_new) {
+    TB_CHECK(r, "NULL runner");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    tb_status e = gen_setup(r, prompts, offs, n_seqs, max_new, g_last_plan);
+    if (e != TB_OK) return e;
+    if ((e = gen_begin(r, g_last_plan)) != TB_OK) return e;
+    if ((e = gen_activate_all(r, g_last_plan)) != TB_OK) return e;
+    if ((e = capture_graph(r)) != TB_OK) return e;
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    return tb_context_check_device(r->ctx);
+}
+
+extern "C" tb_status tb_runner_decode_device(tb_runner* r, int32_t n_steps, float* ms) {
+    TB_CHECK(r && n_steps >= 0, "bad argument");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    std::vector<char> act(r->B, 0);
+    for (int s = 0; s < g_last_plan.n_seqs; ++s) act[s] = 1;
+    // Pre-map the pages these steps touch so the timed loop is pure graph replays.
+    TB_CUDA(cudaEventRecord(r->ev0, r->ctx->stream));
+    tb_status e = run_steps(r, n_steps, act);
+    if (e != TB_OK) return e;
+    TB_CUDA(cudaEventRecord(r->ev1, r->ctx->stream));
+    TB_CUDA(cudaEventSynchronize(r->ev1));
+    float t = 0.0f;
+    TB_CUDA(cudaEventElapsedTime(&t, r->ev0, r->ev1));
+    if (ms) *ms = t;
+    return tb_context_check_device(r->ctx);
+}
+
+extern "C" tb_status tb_runner_read_tokens(tb_runner* r, int32_t* out_tokens, int32_t* out_counts) {
+    TB_CHECK(r && out_tokens && out_counts, "NULL argument");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    TB_CUDA(cudaMemcpyAsync(r->pin_tokens.p, r->out_tokens.p, (size_t)r->B * r->max_out * 4, cudaMemcpyDeviceToHost,
+                            r->ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(r->pin_seq.p, r->seq.p, sizeof(SeqState) * r->B, cudaMemcpyDeviceToHost,
+                            r->ctx->stream));
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    const SeqState* st = r->pin_seq.as<SeqState>();
+    const int* pt = r->pin_tokens.as<int>();
+    const int stride = std::max(1, g_last_plan.max_new);
+    for (int s = 0; s < g_last_plan.n_seqs; ++s) {
+        const int n = std::min(std::min(st[s].n_out, r->max_out), stride);
+        out_counts[s] = n;
+        for (int i = 0; i < n; ++i) out_tokens[(size_t)s * stride + i] = pt[(size_t)s * r->max_out + i];
+    }
+    return ok();
+}
+
+extern "C" tb_status tb_runner_profile_step(tb_runner* r, float* times_ms, int32_t* kinds, int64_t* bytes,
+                                            int32_t* n) {
+    TB_CHECK(r && n && times_ms && kinds && bytes, "NULL argument");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    const int cnt = (int)r->plan.size();
+    TB_CHECK(*n >= cnt, "capacity %d < %d kernels", *n, cnt);
+    std::vector<char> act(r->B, 0);
+    for (int s = 0; s < std::max(1, g_last_plan.n_seqs); ++s) act[s] = 1;
+    for (int s = 0; s < r->B; ++s)
+        if (act[s]) {
+            tb_status e = kv_prepare(r, s);
+            if (e != TB_OK) return e;
+        }
+    tb_status e = flush_ptab(r);
+    if (e != TB_OK) return e;
+    std::vector<cudaEvent_t> ev(cnt + 1);
+    for (auto& x : ev) TB_CUDA(cudaEventCreate(&x));
+    cudaStream_t st = r->ctx->stream;
+    TB_CUDA(cudaEventRecord(ev[0], st));
+    for (int i = 0; i < cnt; ++i) {
+        const Launch& ln = r->plan[i];
+        cudaError_t ce = ln.kind == 0 ? launch_gemv(ln.g, st, false) : launch_attention(ln.a, st, false);
+        if (ce != cudaSuccess) return cuda_fail(ce, "profile launch");
+        TB_CUDA(cudaEventRecord(ev[i + 1], st));
+    }
+    TB_CUDA(cudaEventSynchronize(ev[cnt]));
+    for (int i = 0; i < cnt; ++i) {
+        float t = 0;
+        TB_CUDA(cudaEventElapsedTime(&t, ev[i], ev[i + 1]));
+        times_ms[i] = t;
+        kinds[i] = r->plan[i].kind;
+        bytes[i] = r->plan[i].bytes;
+    }
+    for (auto& x : ev) cudaEventDestroy(x);
+    for (int s = 0; s < r->B; ++s)
+        if (act[s]) r->kvh[s].pos += 1;
+    *n = cnt;
+    return tb_context_check_device(r->ctx);
+}
+
+extern "C" tb_status tb_runner_io_bytes(tb_runner* r, int64_t* h2d, int64_t* d2h, int32_t reset) {
+    TB_CHECK(r && h2d && d2h, "NULL argument");
+    *h2d = r->h2d_bytes;
+    *d2h = r->d2h_bytes;
+    if (reset) r->h2d_bytes = r->d2h_bytes = 0;
+    return ok();
+}

@@ -1,0 +1,507 @@
+"""Host-side mirror of TinyBrain's runtime API over libtinybrain_cuda.
+
+Names and argument meanings follow the reference's Swift API
+(Sources/TinyBrainRuntime): ModelConfig (ModelRunner.swift:27-121),
+QuantizedTensor / Tensor.quantize (QuantizedTensor.swift:31-165, 359-560),
+LinearLayerWeights / ModelWeights (ModelWeights.swift:32-244), ModelRunner
+(ModelRunner.swift:127-298), KVCache.length / pageAllocationStatus
+(KVCache.swift:138-356), SamplerConfig / GenerationConfig / TokenOutput
+(Sampler.swift:46-104, GenerationConfig.swift:35-219).
+
+Every numeric result comes from the CUDA library; nothing here computes a
+projection, an attention or a sample on the CPU.  Unsupported requests
+(e.g. stochastic sampling, which the device sampler does not implement yet)
+raise instead of falling back.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import time
+from dataclasses import dataclass, field
+from typing import Iterator, List, Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import QTensorDesc, TinyBrainError, call
+
+ARCH_LLAMA, ARCH_TOY = 0, 1
+PROJ_Q, PROJ_K, PROJ_V, PROJ_O, PROJ_GATE, PROJ_UP, PROJ_DOWN = range(7)
+
+
+def _ptr(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+# ---------------------------------------------------------------- context --
+class Context:
+    """A CUDA device context (replaces `TinyBrainBackend.metalBackend = MetalBackend()`)."""
+
+    _default = {}
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        call("tb_context_create", device, C.byref(h))
+        self.handle = h
+        self.device = device
+
+    @classmethod
+    def default(cls, device: int = 0) -> "Context":
+        if device not in cls._default:
+            cls._default[device] = Context(device)
+        return cls._default[device]
+
+    def synchronize(self):
+        call("tb_context_synchronize", self.handle)
+
+    def check_device(self):
+        call("tb_context_check_device", self.handle)
+
+    def close(self):
+        if self.handle:
+            _lib.load().tb_context_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def device_count() -> int:
+    n = C.c_int32(0)
+    st = _lib.load().tb_device_count(C.byref(n))
+    return n.value if st == 0 else 0
+
+
+# ------------------------------------------------------------- RNG / data --
+class SeededGenerator:
+    """ModelWeights.swift:18-29 LCG (seed 0 -> 0xdeadbeef) used by Tensor.random."""
+
+    def __init__(self, seed: int):
+        s = C.c_uint64(0)
+        call("tb_rng_seed_state", C.c_uint64(seed), C.byref(s))
+        self.state = s
+
+    def normal(self, shape, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+        """Tensor.random(shape:mean:std:using:) (Tensor.swift:1623-1644)."""
+        n = int(np.prod(shape))
+        out = np.empty(n, dtype=np.float32)
+        call("tb_rng_fill_normal", C.byref(self.state), C.c_float(mean), C.c_float(std), n, _ptr(out))
+        return out.reshape(shape)
+
+
+# ------------------------------------------------------------ quantization --
+@dataclass
+class QuantizedTensor:
+    """QuantizedTensor (QuantizedTensor.swift:62-165) in the reference layout.
+
+    shape = (K in_features, N out_features), row-major, y = x @ dequant(W).
+    mode 'perChannel': data int8 [K*N], scales [N].
+    mode 'int4': data uint8 packed [ceil(K*N/2)] (even flat index = high
+    nibble), scales / zero_points [ceil(K*N/group_size)].
+    """
+
+    shape: tuple
+    data: np.ndarray
+    scales: np.ndarray
+    mode: str = "perChannel"
+    group_size: int = 32
+    zero_points: Optional[np.ndarray] = None
+
+    @property
+    def precision(self) -> int:
+        return 4 if self.mode == "int4" else 8
+
+    def desc(self) -> QTensorDesc:
+        d = QTensorDesc()
+        d.precision = self.precision
+        d.in_features, d.out_features = int(self.shape[0]), int(self.shape[1])
+        d.group_size = int(self.group_size)
+        d.data = self.data.ctypes.data_as(C.c_void_p)
+        d.data_bytes = self.data.nbytes
+        d.scales = self.scales.ctypes.data_as(C.c_void_p)
+        d.num_scales = self.scales.size
+        if self.zero_points is not None:
+            d.zero_points = self.zero_points.ctypes.data_as(C.c_void_p)
+            d.num_zero_points = self.zero_points.size
+        return d
+
+    def dequantize(self) -> np.ndarray:
+        raise TinyBrainError(4, "dequantize() is a host debugging helper in the reference; "
+                                "use the oracle in tests instead")
+
+
+def quantize(w: np.ndarray, mode: str = "perChannel", group_size: int = 32,
+             ctx: Optional[Context] = None) -> QuantizedTensor:
+    """Tensor.quantize(mode:groupSize:) (QuantizedTensor.swift:359-372) on the GPU."""
+    ctx = ctx or Context.default()
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    if w.ndim != 2:
+        raise ValueError("quantize expects a 2-D [in, out] weight")
+    K, N = w.shape
+    if mode == "perChannel":
+        q = np.empty(K * N, dtype=np.int8)
+        s = np.empty(N, dtype=np.float32)
+        call("tb_quantize_int8_per_channel", ctx.handle, _ptr(w), K, N, _ptr(q), _ptr(s))
+        return QuantizedTensor((K, N), q, s, "perChannel", 0, None)
+    if mode == "int4":
+        cnt = K * N
+        ng = (cnt + group_size - 1) // group_size
+        p = np.empty((cnt + 1) // 2, dtype=np.uint8)
+        s = np.empty(ng, dtype=np.float32)
+        z = np.empty(ng, dtype=np.int8)
+        call("tb_quantize_int4_group", ctx.handle, _ptr(w), cnt, group_size, _ptr(p), _ptr(s), _ptr(z))
+        return QuantizedTensor((K, N), p, s, "int4", group_size, z)
+    raise TinyBrainError(4, f"quantization mode {mode!r} is not on the decode path")
+
+
+class QuantizedWeight:
+    """A quantized weight resident in HBM (cachedQuantizedBuffers replacement)."""
+
+    def __init__(self, q: QuantizedTensor, ctx: Optional[Context] = None):
+        self.ctx = ctx or Context.default()
+        self.q = q
+        h = C.c_void_p()
+        d = q.desc()
+        call("tb_qweight_upload", self.ctx.handle, C.byref(d), C.byref(h))
+        self.handle = h
+
+    def matmul(self, x: np.ndarray) -> np.ndarray:
+        """QuantizedMatMulBackend.matmulQuantized (Backend.swift:173-175)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim == 1:
+            x = x[None, :]
+        M = x.shape[0]
+        y = np.empty((M, self.q.shape[1]), dtype=np.float32)
+        call("tb_matmul_quantized", self.ctx.handle, _ptr(x), M, self.handle, _ptr(y))
+        return y
+
+    def __del__(self):
+        try:
+            if self.handle:
+                _lib.load().tb_qweight_free(self.handle)
+        except Exception:
+            pass
+
+
+def attention_decode(q, keys, values, num_heads, num_kv_heads, head_dim, ctx=None) -> np.ndarray:
+    """Single-query decode attention (ModelRunner.swift:519-579 semantics)."""
+    ctx = ctx or Context.default()
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    keys = np.ascontiguousarray(keys, dtype=np.float32)
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    L = keys.shape[0]
+    out = np.empty(num_heads * head_dim, dtype=np.float32)
+    call("tb_attention_decode", ctx.handle, _ptr(q), _ptr(keys), _ptr(values), L, num_heads, num_kv_heads,
+         head_dim, _ptr(out))
+    return out
+
+
+# ------------------------------------------------------------------ model --
+@dataclass
+class ModelConfig:
+    """ModelConfig (ModelRunner.swift:27-121)."""
+
+    num_layers: int
+    hidden_dim: int
+    num_heads: int
+    vocab_size: int
+    max_seq_len: int = 2048
+    num_kv_heads: Optional[int] = None
+    intermediate_dim: Optional[int] = None
+    architecture: str = "llama"
+    rms_eps: float = 1e-5
+
+    def __post_init__(self):
+        if self.num_kv_heads is None:
+            self.num_kv_heads = self.num_heads
+        if self.intermediate_dim is None:
+            self.intermediate_dim = 4 * self.hidden_dim
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_dim // self.num_heads
+
+    @property
+    def kv_dim(self) -> int:
+        return self.head_dim * self.num_kv_heads
+
+    def to_c(self) -> _lib.ModelConfigC:
+        c = _lib.ModelConfigC()
+        c.num_layers, c.hidden_dim, c.num_heads = self.num_layers, self.hidden_dim, self.num_heads
+        c.num_kv_heads, c.vocab_size, c.max_seq_len = self.num_kv_heads, self.vocab_size, self.max_seq_len
+        c.intermediate_dim = self.intermediate_dim
+        c.architecture = ARCH_TOY if self.architecture == "toy" else ARCH_LLAMA
+        c.rms_eps = self.rms_eps
+        return c
+
+
+@dataclass
+class LinearLayerWeights:
+    """LinearLayerWeights (ModelWeights.swift:32-69): quantized weight + optional bias."""
+
+    weights: QuantizedTensor
+    bias: Optional[np.ndarray] = None
+
+
+@dataclass
+class TransformerLayerWeights:
+    """TransformerLayerWeights (ModelWeights.swift:98-134)."""
+
+    query: LinearLayerWeights
+    key: LinearLayerWeights
+    value: LinearLayerWeights
+    output: LinearLayerWeights
+    up: LinearLayerWeights
+    down: LinearLayerWeights
+    gate: Optional[LinearLayerWeights] = None
+    input_norm: Optional[np.ndarray] = None
+    post_attention_norm: Optional[np.ndarray] = None
+
+
+@dataclass
+class ModelWeights:
+    """ModelWeights (ModelWeights.swift:137-168)."""
+
+    config: ModelConfig
+    token_embeddings: np.ndarray  # [vocab, hidden] fp32
+    layers: List[TransformerLayerWeights]
+    output: LinearLayerWeights
+    final_norm: Optional[np.ndarray] = None
+
+    def upload(self, ctx: Optional[Context] = None) -> "DeviceModel":
+        return DeviceModel(self, ctx)
+
+
+class DeviceModel:
+    """ModelWeights uploaded to HBM (fused QKV and gate/up, GPU tile layout)."""
+
+    def __init__(self, w: ModelWeights, ctx: Optional[Context] = None):
+        self.ctx = ctx or Context.default()
+        self.config = w.config
+        cfg = w.config.to_c()
+        h = C.c_void_p()
+        call("tb_model_create", self.ctx.handle, C.byref(cfg), C.byref(h))
+        self.handle = h
+        emb = np.ascontiguousarray(w.token_embeddings, dtype=np.float32)
+        call("tb_model_set_embedding", h, _ptr(emb))
+        if w.final_norm is not None:
+            fn = np.ascontiguousarray(w.final_norm, dtype=np.float32)
+            call("tb_model_set_final_norm", h, _ptr(fn))
+        for i, ly in enumerate(w.layers):
+            ni = None if ly.input_norm is None else np.ascontiguousarray(ly.input_norm, dtype=np.float32)
+            npn = None if ly.post_attention_norm is None else np.ascontiguousarray(ly.post_attention_norm,
+                                                                                    dtype=np.float32)
+            call("tb_model_set_layer_norms", h, i, _ptr(ni), _ptr(npn))
+            for which, lw in ((PROJ_Q, ly.query), (PROJ_K, ly.key), (PROJ_V, ly.value), (PROJ_O, ly.output),
+                              (PROJ_GATE, ly.gate), (PROJ_UP, ly.up), (PROJ_DOWN, ly.down)):
+                if lw is None:
+                    continue
+                d = lw.weights.desc()
+                b = None if lw.bias is None else np.ascontiguousarray(lw.bias, dtype=np.float32)
+                call("tb_model_set_projection", h, i, which, C.byref(d), _ptr(b))
+        d = w.output.weights.desc()
+        b = None if w.output.bias is None else np.ascontiguousarray(w.output.bias, dtype=np.float32)
+        call("tb_model_set_output", h, C.byref(d), _ptr(b))
+        call("tb_model_finalize", h)
+
+    @property
+    def weight_bytes(self) -> int:
+        v = C.c_int64(0)
+        call("tb_model_weight_bytes", self.handle, C.byref(v))
+        return v.value
+
+    def __del__(self):
+        try:
+            if self.handle:
+                _lib.load().tb_model_free(self.handle)
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------- sampling --
+@dataclass
+class SamplerConfig:
+    """SamplerConfig (Sampler.swift:46-104)."""
+
+    temperature: float = 0.7
+    top_k: Optional[int] = None
+    top_p: Optional[float] = None
+    repetition_penalty: float = 1.0
+    seed: Optional[int] = None
+
+    def is_greedy(self) -> bool:
+        return self.top_k == 1
+
+
+@dataclass
+class GenerationConfig:
+    """GenerationConfig (GenerationConfig.swift:35-119)."""
+
+    max_tokens: int = 100
+    sampler: SamplerConfig = field(default_factory=SamplerConfig)
+    stop_tokens: Sequence[int] = ()
+
+
+@dataclass
+class TokenOutput:
+    """TokenOutput (GenerationConfig.swift:149-219)."""
+
+    token_id: int
+    probability: float
+    entropy: float
+    timestamp: float
+    strategy: Optional[str] = None
+
+
+def _greedy_topk1_stats():
+    # Sampler.sampleDetailed with topK = 1: softmax over one finite logit with
+    # the +1e-7 denominator (Tensor.swift:1293), entropy -p*log(p), in fp32.
+    p = np.float32(1.0) / (np.float32(1.0) + np.float32(1e-7))
+    ent = -p * np.log(p, dtype=np.float32)
+    return float(p), float(ent)
+
+
+class KVCacheView:
+    """The runner's KVCache as the reference exposes it (KVCache.swift:138-356)."""
+
+    def __init__(self, runner: "ModelRunner", seq: int = 0):
+        self._r, self._seq = runner, seq
+
+    @property
+    def length(self) -> int:
+        v = C.c_int64(0)
+        call("tb_runner_kv_length", self._r.handle, self._seq, C.byref(v))
+        return v.value
+
+    @property
+    def max_pages(self) -> int:
+        v = C.c_int64(0)
+        call("tb_runner_max_pages", self._r.handle, C.byref(v))
+        return v.value
+
+    def page_allocation_status(self, layer: int = 0) -> List[bool]:
+        n = self.max_pages
+        st = np.zeros(n, dtype=np.uint8)
+        call("tb_runner_page_status", self._r.handle, self._seq, _ptr(st), n)
+        return [bool(x) for x in st]
+
+
+class ModelRunner:
+    """ModelRunner (ModelRunner.swift:127-298) on one GPU.
+
+    `max_batch` > 1 decodes that many independent sequences together
+    (generate_batch); step() drives sequence 0 of a batch-1 runner.
+    """
+
+    def __init__(self, weights, ctx: Optional[Context] = None, max_batch: int = 1,
+                 max_positions: Optional[int] = None):
+        self.model = weights if isinstance(weights, DeviceModel) else DeviceModel(weights, ctx)
+        self.ctx = self.model.ctx
+        self.config = self.model.config
+        self.max_batch = max_batch
+        h = C.c_void_p()
+        call("tb_runner_create", self.model.handle, max_batch, int(max_positions or self.config.max_seq_len),
+             C.byref(h))
+        self.handle = h
+        self.kv_cache = KVCacheView(self, 0)
+        self.observer = None
+
+    # -- ModelRunner.step / reset / currentPosition --
+    def step(self, token_id: int, want_logits: bool = True):
+        """One forward step; returns (logits or None, greedy token)."""
+        logits = np.empty(self.config.vocab_size, dtype=np.float32) if want_logits else None
+        am = C.c_int32(0)
+        call("tb_runner_step", self.handle, int(token_id), _ptr(logits), C.byref(am))
+        return logits, am.value
+
+    def reset(self):
+        call("tb_runner_reset", self.handle)
+
+    @property
+    def current_position(self) -> int:
+        v = C.c_int64(0)
+        call("tb_runner_position", self.handle, 0, C.byref(v))
+        return v.value
+
+    # -- generation --
+    def generate_batch(self, prompts: Sequence[Sequence[int]], max_new_tokens: int,
+                       stop_tokens: Sequence[int] = (), callback=None) -> List[List[int]]:
+        """Greedy generation for independent sequences (generateStream semantics each)."""
+        n = len(prompts)
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(p, dtype=np.int64) for p in prompts])
+                                    .astype(np.int32) if n and sum(len(p) for p in prompts) else
+                                    np.zeros(1, dtype=np.int32))
+        offs = np.zeros(n + 1, dtype=np.int64)
+        offs[1:] = np.cumsum([len(p) for p in prompts])
+        out = np.zeros((n, max(1, max_new_tokens)), dtype=np.int32)
+        counts = np.zeros(n, dtype=np.int32)
+        stops = np.asarray(list(stop_tokens), dtype=np.int32)
+        cb = _lib.TOKEN_CALLBACK(0) if callback is None else _lib.TOKEN_CALLBACK(
+            lambda user, seq, idx, tok: int(bool(callback(seq, idx, tok))))
+        call("tb_runner_generate", self.handle, _ptr(flat), _ptr(offs), n, max_new_tokens,
+             _ptr(stops) if stops.size else None, int(stops.size), _ptr(out), _ptr(counts), cb, None)
+        return [out[i, :counts[i]].tolist() for i in range(n)]
+
+    def generate_stream(self, prompt: Sequence[int], config: Optional[GenerationConfig] = None
+                        ) -> Iterator[TokenOutput]:
+        """ModelRunner.generateStream (ModelRunner.swift:227-298), greedy sampler only."""
+        config = config or GenerationConfig()
+        if not config.sampler.is_greedy():
+            raise TinyBrainError(4, "the device sampler implements greedy decoding (SamplerConfig(top_k=1)); "
+                                    "stochastic sampling is not available")
+        strategy = f"temp={config.sampler.temperature:.2f}, topK=1"
+        if config.sampler.repetition_penalty != 1.0:
+            raise TinyBrainError(4, "repetition penalty is not implemented by the device sampler")
+        p, ent = _greedy_topk1_stats()
+        toks: List[int] = []
+
+        def cb(seq, idx, tok):
+            toks.append(tok)
+            return False
+
+        self.generate_batch([list(prompt)], config.max_tokens, config.stop_tokens, cb)
+        for t in toks:
+            yield TokenOutput(t, p, ent, time.time(), strategy)
+
+    # -- benchmark hooks --
+    def prefill_device(self, prompts: Sequence[Sequence[int]], max_new_tokens: int):
+        n = len(prompts)
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(p, dtype=np.int32) for p in prompts]))
+        offs = np.zeros(n + 1, dtype=np.int64)
+        offs[1:] = np.cumsum([len(p) for p in prompts])
+        call("tb_runner_prefill_device", self.handle, _ptr(flat), _ptr(offs), n, max_new_tokens)
+
+    def decode_device(self, n_steps: int) -> float:
+        ms = C.c_float(0)
+        call("tb_runner_decode_device", self.handle, n_steps, C.byref(ms))
+        return ms.value
+
+    def read_tokens(self, n_seqs: int, max_new_tokens: int) -> List[List[int]]:
+        out = np.zeros((self.max_batch, max(1, max_new_tokens)), dtype=np.int32)
+        counts = np.zeros(self.max_batch, dtype=np.int32)
+        call("tb_runner_read_tokens", self.handle, _ptr(out), _ptr(counts))
+        return [out[i, :counts[i]].tolist() for i in range(n_seqs)]
+
+    def io_bytes(self, reset: bool = False):
+        a, b = C.c_int64(0), C.c_int64(0)
+        call("tb_runner_io_bytes", self.handle, C.byref(a), C.byref(b), int(reset))
+        return a.value, b.value
+
+    def profile_step(self):
+        cap = 4096
+        t = np.zeros(cap, dtype=np.float32)
+        k = np.zeros(cap, dtype=np.int32)
+        b = np.zeros(cap, dtype=np.int64)
+        n = C.c_int32(cap)
+        call("tb_runner_profile_step", self.handle, _ptr(t), _ptr(k), _ptr(b), C.byref(n))
+        return t[:n.value].copy(), k[:n.value].copy(), b[:n.value].copy()
+
+    def __del__(self):
+        try:
+            if self.handle:
+                _lib.load().tb_runner_free(self.handle)
+        except Exception:
+            pass
