@@ -102,9 +102,9 @@ def build_model(ctx, mode="perChannel"):
     return make_llama_model(tl_config(), seed=MODEL_SEED, mode=mode, ctx=ctx)
 
 
-def prompt_ids():
+def prompt_ids(n=PROMPT_LEN):
     from tinybrain_b200.synthetic import random_prompt
-    return random_prompt(PROMPT_LEN, 32000, PROMPT_SEED)
+    return random_prompt(n, 32000, PROMPT_SEED)
 
 
 def cpu_baseline(weights, prompt, budget_s=20.0, max_steps=24):
@@ -193,7 +193,7 @@ def run_ours(args):
     weights = build_model(ctx)
     runner = ModelRunner(weights, ctx, max_batch=1, max_positions=tl_config().max_seq_len)
     build_s = time.perf_counter() - t_build
-    prompt = prompt_ids()
+    prompt = prompt_ids(args.prompt_len)
     W, K = args.warmup, args.steps
     total_new = W + K
 
@@ -268,7 +268,7 @@ def run_ours(args):
         "data": "synthetic (seeded LCG normal std 0.02, uniform prompt ids)",
         "config": {"workload": "TinyLlama-1.1B-shaped INT8, batch 1, greedy decode (BASELINE config 2)",
                    "layers": 22, "hidden": 2048, "heads": "32q/4kv", "vocab": 32000,
-                   "prompt": PROMPT_LEN, "decode_tokens": total_new, "parallelism": f"replicas x{world}",
+                   "prompt": len(prompt), "decode_tokens": total_new, "parallelism": f"replicas x{world}",
                    "l2": "weights streamed per step (1.04 GB) exceed L2; no flush needed"},
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "h2d_bytes_per_step": round(h2d / n_steps_e2e, 1), "d2h_bytes_per_step": round(d2h / n_steps_e2e, 1),
@@ -302,6 +302,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
+                    help="prompt length (default 128 = the config; shorter only for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

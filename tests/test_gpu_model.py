@@ -24,7 +24,7 @@ def assert_same_tokens(got, want, gaps):
 
 
 def small_cfg(**kw):
-    base = dict(num_layers=2, hidden_dim=256, num_heads=8, vocab_size=1000, max_seq_len=128, num_kv_heads=2,
+    base = dict(num_layers=2, hidden_dim=256, num_heads=8, vocab_size=1024, max_seq_len=128, num_kv_heads=2,
                 intermediate_dim=512)
     base.update(kw)
     return ModelConfig(**base)

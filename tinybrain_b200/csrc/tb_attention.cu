@@ -193,20 +193,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             named_bar_sync(1, 128);
             if (__float_as_int(flag[0]) == 1) {
                 __threadfence();
+                // Combine the splits in split order: all (m, l) pairs are loaded in
+                // parallel into shared memory first, so the chain is two L2 round trips.
+                const float* base = p.part + (pair_idx * p.nsplit) * G * (size_t)(D + 4);
+                float* wsm = tiles;  // [nsplit][G] weights, reused ring space
+                float* lsm = tiles + 64 * G;
+                for (int e = t; e < p.nsplit * G; e += 128) {
+                    wsm[e] = base[(size_t)e * (D + 4) + D];
+                    lsm[e] = base[(size_t)e * (D + 4) + D + 1];
+                }
+                named_bar_sync(1, 128);
                 if (pv) {
-                    const float* base = p.part + (pair_idx * p.nsplit) * G * (size_t)(D + 4);
                     float M = -INFINITY;
-                    for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, base[((size_t)s * G + gv) * (D + 4) + D]);
+                    for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, wsm[s * G + gv]);
                     float den = 0.0f;
                     float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (M != -INFINITY) {
+#pragma unroll 4
                         for (int s = 0; s < p.nsplit; ++s) {
-                            const float* ps = base + ((size_t)s * G + gv) * (D + 4);
-                            const float ms = ps[D];
-                            if (ms == -INFINITY) continue;
-                            const float w = expf(ms - M);
-                            den = fmaf(w, ps[D + 1], den);
-                            const float4 a = *reinterpret_cast<const float4*>(ps + dv);
+                            const float ms = wsm[s * G + gv];
+                            const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+                            den = fmaf(w, lsm[s * G + gv], den);
+                            const float4 a = *reinterpret_cast<const float4*>(base + ((size_t)s * G + gv) * (D + 4) + dv);
                             num.x = fmaf(w, a.x, num.x);
                             num.y = fmaf(w, a.y, num.y);
                             num.z = fmaf(w, a.z, num.z);
@@ -287,12 +295,12 @@ size_t attention_scratch_bytes(int M, int Hkv, int nsplit, int G, int d) {
 size_t attention_ticket_count(int M, int Hkv) { return (size_t)M * Hkv; }
 
 int choose_nsplit(int M, int Hkv, int max_pages, int num_sms) {
-    // About two CTAs per SM over the (sequence, KV head) pairs, at least a few
-    // pages per split, at most one split per page.
+    // About one CTA per SM over the (sequence, KV head) pairs at the longest
+    // context, at least 8 pages per split there, at most 64 splits.
     int pairs = M * Hkv;
-    int ns = (2 * num_sms + pairs - 1) / pairs;
-    ns = ns < 1 ? 1 : ns;
-    if (ns > max_pages) ns = max_pages;
+    int ns = (num_sms + pairs - 1) / pairs;
+    const int by_pages = (max_pages + 7) / 8;
+    if (ns > by_pages) ns = by_pages;
     if (ns > 64) ns = 64;
     return ns < 1 ? 1 : ns;
 }

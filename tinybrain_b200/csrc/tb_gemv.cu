@@ -447,7 +447,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                 __threadfence();
                 for (int m = ctid; m < p.M; m += 256) {
                     SeqState& sq = p.seq[m];
-                    if (!sq.active) continue;
+                    if (!sq.active) {
+                        sq.best = 0ull;  // paused slot: drop this step's argmax
+                        continue;
+                    }
                     const unsigned long long b = atomicAdd(&sq.best, 0ull);
                     const int tok = (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
                     int next;

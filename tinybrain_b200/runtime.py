@@ -15,8 +15,10 @@ raise instead of falling back.
 """
 from __future__ import annotations
 
+import atexit
 import ctypes as C
 import time
+import weakref
 from dataclasses import dataclass, field
 from typing import Iterator, List, Optional, Sequence
 
@@ -33,6 +35,22 @@ def _ptr(a: Optional[np.ndarray]):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
 
 
+# Live handles, released children-first when the interpreter exits so no CUDA
+# object outlives its context or the CUDA runtime.
+_LIVE = {"runner": weakref.WeakSet(), "model": weakref.WeakSet(), "qweight": weakref.WeakSet(),
+         "context": weakref.WeakSet()}
+
+
+@atexit.register
+def _release_all():
+    for kind in ("runner", "model", "qweight", "context"):
+        for obj in list(_LIVE[kind]):
+            try:
+                obj.close()
+            except Exception:
+                pass
+
+
 # ---------------------------------------------------------------- context --
 class Context:
     """A CUDA device context (replaces `TinyBrainBackend.metalBackend = MetalBackend()`)."""
@@ -44,6 +62,7 @@ class Context:
         call("tb_context_create", device, C.byref(h))
         self.handle = h
         self.device = device
+        _LIVE["context"].add(self)
 
     @classmethod
     def default(cls, device: int = 0) -> "Context":
@@ -59,6 +78,10 @@ class Context:
 
     def close(self):
         if self.handle:
+            for kind in ("runner", "model", "qweight"):
+                for obj in list(_LIVE[kind]):
+                    if getattr(obj, "ctx", None) is self:
+                        obj.close()
             _lib.load().tb_context_destroy(self.handle)
             self.handle = None
 
@@ -167,6 +190,7 @@ class QuantizedWeight:
         d = q.desc()
         call("tb_qweight_upload", self.ctx.handle, C.byref(d), C.byref(h))
         self.handle = h
+        _LIVE["qweight"].add(self)
 
     def matmul(self, x: np.ndarray) -> np.ndarray:
         """QuantizedMatMulBackend.matmulQuantized (Backend.swift:173-175)."""
@@ -178,10 +202,14 @@ class QuantizedWeight:
         call("tb_matmul_quantized", self.ctx.handle, _ptr(x), M, self.handle, _ptr(y))
         return y
 
+    def close(self):
+        if self.handle:
+            _lib.load().tb_qweight_free(self.handle)
+            self.handle = None
+
     def __del__(self):
         try:
-            if self.handle:
-                _lib.load().tb_qweight_free(self.handle)
+            self.close()
         except Exception:
             pass
 
@@ -285,6 +313,7 @@ class DeviceModel:
         h = C.c_void_p()
         call("tb_model_create", self.ctx.handle, C.byref(cfg), C.byref(h))
         self.handle = h
+        _LIVE["model"].add(self)
         emb = np.ascontiguousarray(w.token_embeddings, dtype=np.float32)
         call("tb_model_set_embedding", h, _ptr(emb))
         if w.final_norm is not None:
@@ -313,10 +342,17 @@ class DeviceModel:
         call("tb_model_weight_bytes", self.handle, C.byref(v))
         return v.value
 
+    def close(self):
+        if self.handle:
+            for r in list(_LIVE["runner"]):
+                if r.model is self:
+                    r.close()
+            _lib.load().tb_model_free(self.handle)
+            self.handle = None
+
     def __del__(self):
         try:
-            if self.handle:
-                _lib.load().tb_model_free(self.handle)
+            self.close()
         except Exception:
             pass
 
@@ -368,7 +404,7 @@ class KVCacheView:
     """The runner's KVCache as the reference exposes it (KVCache.swift:138-356)."""
 
     def __init__(self, runner: "ModelRunner", seq: int = 0):
-        self._r, self._seq = runner, seq
+        self._r, self._seq = weakref.proxy(runner), seq
 
     @property
     def length(self) -> int:
@@ -406,6 +442,7 @@ class ModelRunner:
         call("tb_runner_create", self.model.handle, max_batch, int(max_positions or self.config.max_seq_len),
              C.byref(h))
         self.handle = h
+        _LIVE["runner"].add(self)
         self.kv_cache = KVCacheView(self, 0)
         self.observer = None
 
@@ -499,9 +536,13 @@ class ModelRunner:
         call("tb_runner_profile_step", self.handle, _ptr(t), _ptr(k), _ptr(b), C.byref(n))
         return t[:n.value].copy(), k[:n.value].copy(), b[:n.value].copy()
 
+    def close(self):
+        if self.handle:
+            _lib.load().tb_runner_free(self.handle)
+            self.handle = None
+
     def __del__(self):
         try:
-            if self.handle:
-                _lib.load().tb_runner_free(self.handle)
+            self.close()
         except Exception:
             pass
