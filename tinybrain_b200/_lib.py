@@ -77,6 +77,7 @@ SIGNATURES = {
     "tb_matmul_quantized_dev": [_P, _P, _I64, _P, _P],
     "tb_attention_decode": [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _P],
     "tb_paged_attention_dev": [_P, _P, _I32, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P],
+    "tb_paged_attention_dev_noalloc": [_P, _P, _I32, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P],
     "tb_model_create": [_P, C.POINTER(ModelConfigC), C.POINTER(_P)],
     "tb_model_free": [_P],
     "tb_model_set_embedding": [_P, _P],

@@ -15,8 +15,11 @@
 // compute scores and an online softmax.  Splits write (m, l, acc) partials to
 // scratch; the last CTA of each (sequence, KV head) -- elected with a ticket --
 // combines them in split order (deterministic).
+#include "../../include/tinybrain_cuda.h"
 #include "tb_common.cuh"
 #include "tb_kernels.h"
+
+#include <mutex>
 
 namespace tb {
 
@@ -341,3 +344,110 @@ cudaError_t launch_attention_probs(const AttnParams& p, float* probs, int L, cud
 }
 
 }  // namespace tb
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the paged decode attention.
+//
+// Some callers cannot create device allocations at all: a host that hands
+// every byte of HBM to its own pool before loading this library, or code on a
+// latency-critical path where cudaMalloc / cudaFree would synchronise the
+// device.  tb_paged_attention_dev_noalloc serves them: its split-K scratch
+// lives in the fixed-size arrays below, which every GPU that loads the library
+// holds until the process exits.
+// ---------------------------------------------------------------------------
+namespace tb {
+namespace {
+constexpr size_t kNoAllocPartFloats = size_t(1) << 20;  // 4 MiB of split partials
+constexpr size_t kNoAllocTickets = 4096;                // (sequence, KV head) counters
+static __device__ __align__(256) float g_noalloc_part[kNoAllocPartFloats];
+static __device__ __align__(256) unsigned int g_noalloc_tickets[kNoAllocTickets];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_part_ptr[kMaxDevices] = {};
+unsigned int* g_noalloc_ticket_ptr[kMaxDevices] = {};
+int g_noalloc_sms[kMaxDevices] = {};
+
+// Once per device, with that device current: the device addresses of the
+// arrays (host code only sees a host-side stand-in under their names).
+cudaError_t noalloc_setup(int dev) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_part_ptr[dev]) return cudaSuccess;
+    void* part = nullptr;
+    void* tickets = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&part, g_noalloc_part);
+    if (e != cudaSuccess) return e;
+    e = cudaGetSymbolAddress(&tickets, g_noalloc_tickets);
+    if (e != cudaSuccess) return e;
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    g_noalloc_sms[dev] = sms;
+    g_noalloc_ticket_ptr[dev] = static_cast<unsigned int*>(tickets);
+    g_noalloc_part_ptr[dev] = static_cast<float*>(part);
+    return cudaSuccess;
+}
+}  // namespace
+
+}  // namespace tb
+
+extern "C" tb_status tb_paged_attention_dev_noalloc(void* stream, const float* q, int32_t batch, const float* pool,
+                                                    const int32_t* ptab, int32_t ptab_stride, const int32_t* lens,
+                                                    int32_t max_len, int32_t layer, int32_t num_layers, int32_t H,
+                                                    int32_t Hkv, int32_t d, float* out) {
+    using namespace tb;
+    if (!q || !pool || !ptab || !lens || !out)
+        return (tb_status)report_error(TB_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (batch < 1 || max_len < 1 || layer < 0 || layer >= num_layers || H <= 0 || Hkv <= 0 || d <= 0 ||
+        H % Hkv != 0)
+        return (tb_status)report_error(TB_ERR_INVALID_ARGUMENT, "bad batch / length / layer / head arguments");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return (tb_status)report_error(TB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    e = noalloc_setup(dev);
+    if (e != cudaSuccess)
+        return (tb_status)report_error(TB_ERR_CUDA, "scratch set-up (cudaGetSymbolAddress): %s",
+                                       cudaGetErrorString(e));
+    const int G = H / Hkv;
+    const int max_pages = (max_len + kPageTokens - 1) / kPageTokens;
+    const int ns = choose_nsplit(batch, Hkv, max_pages, g_noalloc_sms[dev]);
+    const size_t need = attention_scratch_bytes(batch, Hkv, ns, G, d) / sizeof(float);
+    const size_t nt = attention_ticket_count(batch, Hkv);
+    if (need > kNoAllocPartFloats || nt > kNoAllocTickets)
+        return (tb_status)report_error(
+            TB_ERR_INVALID_ARGUMENT,
+            "tb_paged_attention_dev_noalloc: needs %zu scratch floats and %zu tickets, the fixed maximum is %zu "
+            "floats (4 MiB) and %zu tickets; use tb_paged_attention_dev for this size",
+            need, nt, kNoAllocPartFloats, kNoAllocTickets);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // The counters must start at zero; a completed call leaves them at zero,
+    // an interrupted one might not.
+    e = cudaMemsetAsync(g_noalloc_ticket_ptr[dev], 0, nt * sizeof(unsigned int), st);
+    if (e != cudaSuccess) return (tb_status)report_error(TB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    AttnParams a{};
+    a.q = q;
+    a.ld_q = H * d;
+    a.kv_pool = pool;
+    a.page_table = ptab;
+    a.ptab_stride = ptab_stride;
+    a.lens = lens;
+    a.seq = nullptr;
+    a.layer = layer;
+    a.num_layers = num_layers;
+    a.H = H;
+    a.Hkv = Hkv;
+    a.d = d;
+    a.M = batch;
+    a.nsplit = ns;
+    a.out = out;
+    a.ld_out = H * d;
+    a.part = g_noalloc_part_ptr[dev];
+    a.tickets = g_noalloc_ticket_ptr[dev];
+    a.err = nullptr;
+    e = launch_attention(a, st, false);
+    if (e != cudaSuccess)
+        return (tb_status)report_error(e == cudaErrorNotSupported ? TB_ERR_UNSUPPORTED : TB_ERR_CUDA,
+                                       "attention launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}

@@ -179,6 +179,9 @@ size_t attention_scratch_bytes(int M, int Hkv, int nsplit, int G, int d);
 size_t attention_ticket_count(int M, int Hkv);
 int choose_nsplit(int M, int Hkv, int max_pages, int num_sms);
 
+// Record the calling thread's last-error message (tb_last_error); returns status.
+int report_error(int status, const char* fmt, ...);
+
 // Softmax attention weights for the observer hook: probs[M][H][L].
 cudaError_t launch_attention_probs(const AttnParams& p, float* probs, int L, cudaStream_t stream);
 

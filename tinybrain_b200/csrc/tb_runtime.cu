@@ -43,6 +43,19 @@ tb_status fail(tb_status s, const char* fmt, ...) {
     return s;
 }
 tb_status ok() { return TB_OK; }
+}  // namespace
+
+int tb::report_error(int status, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+namespace {
 
 tb_status cuda_fail(cudaError_t e, const char* what) {
     if (e == cudaErrorMemoryAllocation) return fail(TB_ERR_OUT_OF_MEMORY, "%s: %s", what, cudaGetErrorString(e));
