@@ -22,6 +22,7 @@
 //    LM-head argmax: Sampler.swift:126-138).
 #include "tb_common.cuh"
 #include "tb_kernels.h"
+#include "tb_unit.cuh"
 
 #include <cstdio>
 
@@ -55,10 +56,6 @@ struct GemvCfg {
     static constexpr int kCH = PREC == 8 ? 16 : 32;                    // k values per lane per slab
 };
 
-// Exponent-bias constants: a biased integer u placed in the low mantissa bits
-// of 2^23 reads as 2^23 + u; subtracting (2^23 + bias * scale) is exact.
-constexpr float kTwo23 = 8388608.0f;
-
 __device__ __forceinline__ float silu_ref(float x) {
     // Tensor.swift:1135-1142: x / (1 + exp(-x))
     return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
@@ -69,22 +66,6 @@ __device__ __forceinline__ float gelu_ref(float x) {
     float x3 = __fmul_rn(__fmul_rn(x, x), x);
     float inner = __fmul_rn(s, __fadd_rn(x, __fmul_rn(0.044715f, x3)));
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
-}
-
-// Position of k (relative to its slab) in the lane-interleaved x / scale layout.
-template <int CH>
-__device__ __forceinline__ int xperm(int k_in_slab) {
-    const int lane = k_in_slab / CH;
-    const int r = k_in_slab % CH;
-    return ((r >> 2) * 32 + lane) * 4 + (r & 3);
-}
-
-// INT4: per-position scale factor 2^-shift folded into x so that nibble p of
-// a 32-bit word can be extracted in place with a single LOP3.
-__device__ __forceinline__ float int4_pos_scale(int p) {
-    // nibble p sits at bit 4p (p < 5) or, after the >>12, at bit 4(p-3)
-    const int shift = p < 5 ? 4 * p : 4 * (p - 3);
-    return __int_as_float((127 - shift) << 23);
 }
 
 template <int PREC, int RB, int MB>
@@ -225,82 +206,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             const int s = s0 + i;
             const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
             const uint8_t* wst = stage_base + st * Cfg::kStageBytes;
-            if (lane * 16 < sb) {
-                uint4 wq[RPW];
-#pragma unroll
-                for (int r = 0; r < RPW; ++r) wq[r] = lds128(wst + (warp * RPW + r) * sb + lane * 16);
-                const float* xsl = xs + i * L.slab_k;
-                if (PREC == 8) {
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        float4 xv[MB];
-#pragma unroll
-                        for (int m = 0; m < MB; ++m) xv[m] = lds128f(xsl + m * xstride + (c * 32 + lane) * 4);
-#pragma unroll
-                        for (int r = 0; r < RPW; ++r) {
-                            const uint32_t wd = c == 0 ? wq[r].x : c == 1 ? wq[r].y : c == 2 ? wq[r].z : wq[r].w;
-                            const float f0 = __uint_as_float(prmt(wd, 0x4B000000u, 0x7440u));
-                            const float f1 = __uint_as_float(prmt(wd, 0x4B000000u, 0x7441u));
-                            const float f2 = __uint_as_float(prmt(wd, 0x4B000000u, 0x7442u));
-                            const float f3 = __uint_as_float(prmt(wd, 0x4B000000u, 0x7443u));
-                            const float2 nb = make_float2(-(kTwo23 + 128.0f), -(kTwo23 + 128.0f));
-                            const float2 v01 = __fadd2_rn(make_float2(f0, f1), nb);
-                            const float2 v23 = __fadd2_rn(make_float2(f2, f3), nb);
-#pragma unroll
-                            for (int m = 0; m < MB; ++m) {
-                                acc[r][m] = __ffma2_rn(v01, make_float2(xv[m].x, xv[m].y), acc[r][m]);
-                                acc[r][m] = __ffma2_rn(v23, make_float2(xv[m].z, xv[m].w), acc[r][m]);
-                            }
-                        }
-                    }
-                } else {
-                    const int grp = (warp * RPW) / 32;
-                    const float* ssl = reinterpret_cast<const float*>(wst + Cfg::kWeightStage) + grp * 1024;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        // word c of the lane's 16 bytes holds k = 32*lane + 8c + p, p = 0..7
-                        float2 xsv[MB][4];
-                        const float4 sa = lds128f(ssl + ((2 * c) * 32 + lane) * 4);
-                        const float4 sbv = lds128f(ssl + ((2 * c + 1) * 32 + lane) * 4);
-#pragma unroll
-                        for (int m = 0; m < MB; ++m) {
-                            const float4 xa = lds128f(xsl + m * xstride + ((2 * c) * 32 + lane) * 4);
-                            const float4 xb = lds128f(xsl + m * xstride + ((2 * c + 1) * 32 + lane) * 4);
-                            xsv[m][0] = __fmul2_rn(make_float2(xa.x, xa.y), make_float2(sa.x, sa.y));
-                            xsv[m][1] = __fmul2_rn(make_float2(xa.z, xa.w), make_float2(sa.z, sa.w));
-                            xsv[m][2] = __fmul2_rn(make_float2(xb.x, xb.y), make_float2(sbv.x, sbv.y));
-                            xsv[m][3] = __fmul2_rn(make_float2(xb.z, xb.w), make_float2(sbv.z, sbv.w));
-                        }
-#pragma unroll
-                        for (int r = 0; r < RPW; ++r) {
-                            const uint32_t wd = c == 0 ? wq[r].x : c == 1 ? wq[r].y : c == 2 ? wq[r].z : wq[r].w;
-                            const uint32_t t = wd >> 12;
-                            const float f0 = __uint_as_float((wd & 0x0000000Fu) | 0x4B000000u);
-                            const float f1 = __uint_as_float((wd & 0x000000F0u) | 0x4B000000u);
-                            const float f2 = __uint_as_float((wd & 0x00000F00u) | 0x4B000000u);
-                            const float f3 = __uint_as_float((wd & 0x0000F000u) | 0x4B000000u);
-                            const float f4 = __uint_as_float((wd & 0x000F0000u) | 0x4B000000u);
-                            const float f5 = __uint_as_float((t & 0x00000F00u) | 0x4B000000u);
-                            const float f6 = __uint_as_float((t & 0x0000F000u) | 0x4B000000u);
-                            const float f7 = __uint_as_float((t & 0x000F0000u) | 0x4B000000u);
-                            const float2 v01 =
-                                __fadd2_rn(make_float2(f0, f1), make_float2(-(kTwo23 + 8.0f), -(kTwo23 + 128.0f)));
-                            const float2 v23 = __fadd2_rn(make_float2(f2, f3),
-                                                          make_float2(-(kTwo23 + 2048.0f), -(kTwo23 + 32768.0f)));
-                            const float2 v45 = __fadd2_rn(make_float2(f4, f5),
-                                                          make_float2(-(kTwo23 + 524288.0f), -(kTwo23 + 2048.0f)));
-                            const float2 v67 = __fadd2_rn(make_float2(f6, f7),
-                                                          make_float2(-(kTwo23 + 32768.0f), -(kTwo23 + 524288.0f)));
-#pragma unroll
-                            for (int m = 0; m < MB; ++m) {
-                                acc[r][m] = __ffma2_rn(v01, xsv[m][0], acc[r][m]);
-                                acc[r][m] = __ffma2_rn(v23, xsv[m][1], acc[r][m]);
-                                acc[r][m] = __ffma2_rn(v45, xsv[m][2], acc[r][m]);
-                                acc[r][m] = __ffma2_rn(v67, xsv[m][3], acc[r][m]);
-                            }
-                        }
-                    }
-                }
+            {
+                const float* ssl = (PREC == 4) ? reinterpret_cast<const float*>(wst + Cfg::kWeightStage) +
+                                                     ((warp * RPW) / 32) * 1024
+                                               : nullptr;
+                unit_dot<PREC, RPW, MB>(wst, sb, warp * RPW, ssl, xs + i * L.slab_k, xstride, lane, acc);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
@@ -416,8 +326,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                     p.out[(size_t)m * p.ld_out + n] = gelu_ref(v);
                 } else {  // kEpiArgmax
                     if (p.logits) p.logits[(size_t)m * L.N + n] = v;
-                    const unsigned long long key =
-                        ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+                    const unsigned long long key = argmax_key(v, n);
 #pragma unroll
                     for (int mm = 0; mm < MB; ++mm)
                         if (mm == m && key > best_local[mm]) best_local[mm] = key;
@@ -451,19 +360,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                         sq.best = 0ull;  // paused slot: drop this step's argmax
                         continue;
                     }
-                    const unsigned long long b = atomicAdd(&sq.best, 0ull);
-                    const int tok = (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
-                    int next;
-                    if (sq.pos >= sq.n_prompt - 1) {
-                        if (sq.n_out < sq.max_out) p.out_tokens[(size_t)m * sq.max_out + sq.n_out] = tok;
-                        sq.n_out += 1;
-                        next = tok;
-                    } else {
-                        next = p.prompt[(size_t)m * p.prompt_stride + sq.pos + 1];
-                    }
-                    sq.token = next;
-                    sq.pos += 1;
-                    sq.best = 0ull;
+                    finish_sequence_step(sq, m, p.out_tokens, p.prompt, p.prompt_stride);
                 }
                 if (ctid == 0) *p.ticket = 0u;
             }
