@@ -213,6 +213,18 @@ tb_status tb_runner_kv_length(const tb_runner *r, int32_t seq, int64_t *length);
 tb_status tb_runner_page_status(const tb_runner *r, int32_t seq, uint8_t *status, int64_t n);
 tb_status tb_runner_max_pages(const tb_runner *r, int64_t *n);
 
+/* Execution mode of a runner's decode step.  Batch-1 LLaMA runners default to
+ * the persistent single-kernel step (one cooperative launch per token streams
+ * every layer's weights through a shared-memory ring); other runners, or
+ * enable = 0, use one fused kernel per projection and attention. */
+tb_status tb_runner_set_persistent(tb_runner *r, int32_t enable);
+tb_status tb_runner_get_persistent(const tb_runner *r, int32_t *enabled);
+/* Copy an internal fp32 buffer of the runner to the host (diagnostics):
+ * 0 h_in, 1 h_mid (persistent step), 2-5 split-K partials (qkv, o, gate/up,
+ * down), 6 attention split partials, 7 logits, 8 residual stream, 9 q,
+ * 10 attention context, 11 SiLU*up activations (per-op step). */
+tb_status tb_runner_debug_read(tb_runner *r, int32_t which, float *out_host, int64_t n);
+
 /* Called once per generated token (TokenOutput, GenerationConfig.swift:149-219);
  * return nonzero to stop that sequence. */
 typedef int32_t (*tb_token_callback)(void *user, int32_t seq, int32_t index, int32_t token_id);

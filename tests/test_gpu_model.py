@@ -30,10 +30,12 @@ def small_cfg(**kw):
     return ModelConfig(**base)
 
 
+@pytest.mark.parametrize("persistent", [True, False])
 @pytest.mark.parametrize("mode", ["perChannel", "int4"])
-def test_step_logits_and_kv_state(ctx, mode):
+def test_step_logits_and_kv_state(ctx, mode, persistent):
     w = small_llama(small_cfg(), seed=3, mode=mode)
     r = ModelRunner(w, ctx)
+    r.persistent = persistent
     o = oracle.OracleModel(w, mode=1)
     for i, tok in enumerate([5, 17, 999, 0, 512, 3, 3, 77, 100, 42, 7, 8, 9, 10, 11, 12, 13, 14]):
         logits, am = r.step(tok)
@@ -60,10 +62,12 @@ def test_toy_model_greedy_identity(ctx):
     assert_same_tokens(got, want, gaps)
 
 
+@pytest.mark.parametrize("persistent", [True, False])
 @pytest.mark.parametrize("mode", ["perChannel", "int4"])
-def test_generate_greedy_identity(ctx, mode):
+def test_generate_greedy_identity(ctx, mode, persistent):
     w = small_llama(small_cfg(num_layers=3), seed=4, mode=mode)
     r = ModelRunner(w, ctx)
+    r.persistent = persistent
     o = oracle.OracleModel(w, mode=1)
     prompt = [11, 22, 33, 44, 55, 66, 77, 88, 99, 111, 222, 333, 444, 555, 666, 777, 888]
     want, gaps = o.generate_greedy(prompt, 48)
@@ -86,10 +90,12 @@ def test_generate_stream_stop_token(ctx):
     assert all(abs(t.probability - 0.9999999) < 1e-6 for t in outs)
 
 
-def test_kv_eviction_parity(ctx):
+@pytest.mark.parametrize("persistent", [True, False])
+def test_kv_eviction_parity(ctx, persistent):
     cfg = small_cfg(max_seq_len=48)
     w = small_llama(cfg, seed=6)
     r = ModelRunner(w, ctx, max_positions=160)
+    r.persistent = persistent
     o = oracle.OracleModel(w, mode=1)
     for i in range(120):
         tok = (i * 37) % cfg.vocab_size
@@ -117,3 +123,28 @@ def test_unsupported_sampler_raises(ctx):
     r = ModelRunner(w, ctx)
     with pytest.raises(TinyBrainError):
         list(r.generate_stream([1, 2], GenerationConfig(max_tokens=3, sampler=SamplerConfig(temperature=0.8))))
+
+
+def test_persistent_is_default_for_batch1_llama_only(ctx):
+    w = small_llama(small_cfg(), seed=9)
+    assert ModelRunner(w, ctx).persistent
+    assert not ModelRunner(w, ctx, max_batch=2).persistent
+    assert not ModelRunner(toy_model(), ctx).persistent
+
+
+@pytest.mark.parametrize("shape", [dict(hidden_dim=512, num_heads=8, num_kv_heads=8, intermediate_dim=1408),
+                                   dict(hidden_dim=256, num_heads=4, num_kv_heads=4, intermediate_dim=704,
+                                        num_layers=1),
+                                   dict(hidden_dim=2048, num_heads=32, num_kv_heads=4, intermediate_dim=5632,
+                                        vocab_size=32000)])
+@pytest.mark.parametrize("mode", ["perChannel", "int4"])
+def test_persistent_other_shapes(ctx, shape, mode):
+    # MHA (G = 1), one layer with a short last slab, and the TinyLlama layer shape
+    cfg = small_cfg(**shape)
+    w = small_llama(cfg, seed=10, mode=mode)
+    r = ModelRunner(w, ctx)
+    assert r.persistent
+    o = oracle.OracleModel(w, mode=1)
+    for i, tok in enumerate([3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8, 9, 7, 9, 3, 2, 3]):
+        logits, _ = r.step(tok)
+        assert rel_l2(logits, o.step(tok)) <= RTOL_L2, i

@@ -101,6 +101,9 @@ SIGNATURES = {
     "tb_runner_read_tokens": [_P, _P, _P],
     "tb_runner_profile_step": [_P, _P, _P, _P, _PI32],
     "tb_runner_io_bytes": [_P, _PI64, _PI64, _I32],
+    "tb_runner_set_persistent": [_P, _I32],
+    "tb_runner_get_persistent": [_P, _PI32],
+    "tb_runner_debug_read": [_P, _I32, _P, _I64],
 }
 _RESTYPES = {
     "tb_abi_version": C.c_int32,

@@ -179,6 +179,51 @@ size_t attention_scratch_bytes(int M, int Hkv, int nsplit, int G, int d);
 size_t attention_ticket_count(int M, int Hkv);
 int choose_nsplit(int M, int Hkv, int max_pages, int num_sms);
 
+// ----------------------------------------------------------------------------
+// Persistent decode step (batch 1): one cooperative launch per token runs all
+// layers and the LM head.  See tb_step.cu.
+// ----------------------------------------------------------------------------
+struct StepLayer {
+    const uint8_t *qkv_w, *o_w, *gu_w, *dn_w;
+    const float *qkv_s, *o_s, *gu_s, *dn_s;
+    const float *qkv_b, *o_b, *gu_b, *dn_b;  // GPU-row-space biases or null
+    const float *in_norm, *post_norm;        // null = no norm
+};
+
+struct StepParams {
+    const StepLayer* layers;  // [num_layers], device memory
+    int num_layers;
+    QLayout Lqkv, Lo, Lgu, Ldn, Llm;  // identical for every layer
+    const uint8_t* lm_w;
+    const float *lm_s, *lm_b, *final_norm;
+    const float* emb;
+    int H, nheads, Hkv, d, kvd, I, V;
+    float eps;
+    const float2* rope;
+    int rope_max_pos;
+    float* kv_pool;
+    const int* ptab;
+    SeqState* seq;
+    int* out_tokens;
+    const int* prompt;
+    int prompt_stride;
+    float* logits;
+    float *hX, *hY;                               // residual stream ping-pong [H]
+    float *part_qkv, *part_o, *part_gu, *part_dn;  // split-K partials [slabs][Np]
+    float* attn_part;                             // [Hkv][A][G][d + 4]
+    int A;                                        // attention splits per KV head
+    unsigned int* bar;                            // grid barrier counter, zero at launch
+    int* err;
+    int nslots, slot_bytes;
+};
+
+constexpr int kStepConsumerWarps = 8;
+constexpr int kStepThreads = (kStepConsumerWarps + 1) * 32;
+
+// Shared memory a launch needs (and its ring geometry), or 0 if unsupported.
+size_t step_smem_bytes(const StepParams& p, int* nslots, int* slot_bytes, int max_smem);
+cudaError_t launch_decode_step(const StepParams& p, int grid, size_t smem, cudaStream_t stream);
+
 // Record the calling thread's last-error message (tb_last_error); returns status.
 int report_error(int status, const char* fmt, ...);
 

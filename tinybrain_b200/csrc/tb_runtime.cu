@@ -229,6 +229,13 @@ struct tb_runner {
     std::vector<Launch> plan;
     cudaGraphExec_t graph = nullptr;
     int nsplit = 1;
+    // persistent single-kernel step (batch 1, LLaMA): see tb_step.cu
+    bool persistent = false;      // in use
+    bool persistent_ok = false;   // supported for this model
+    StepParams sp{};
+    int step_grid = 0;
+    size_t step_smem = 0;
+    DevBuf step_layers, part_qkv, part_o, part_gu, part_dn, step_attn, hX, hY, step_bar;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     ~tb_runner() {
         if (graph) cudaGraphExecDestroy(graph);
@@ -1127,12 +1134,133 @@ static tb_status record_plan(tb_runner* r, cudaStream_t st, bool pdl) {
     return ok();
 }
 
+// Pointers of the persistent step that change when generate() resizes buffers.
+static void refresh_step_params(tb_runner* r) {
+    StepParams& p = r->sp;
+    p.prompt = r->prompt.as<int>();
+    p.prompt_stride = r->prompt_stride;
+    p.out_tokens = r->out_tokens.as<int>();
+}
+
+// Build the persistent-step parameters when the model qualifies (batch 1,
+// LLaMA, one precision and shape for every layer, a supported head shape).
+static tb_status build_step(tb_runner* r) {
+    tb_model* m = r->m;
+    const tb_model_config& c = m->cfg;
+    r->persistent_ok = false;
+    if (r->B != 1 || c.architecture != TB_ARCH_LLAMA || c.hidden_dim > 4096) return ok();
+    const Layer& L0 = m->layers[0];
+    const int prec = L0.qkv.L.precision;
+    auto same = [](const QLayout& a, const QLayout& b) {
+        return a.precision == b.precision && a.K == b.K && a.N == b.N && a.RB == b.RB;
+    };
+    for (const Layer& L : m->layers)
+        if (!same(L.qkv.L, L0.qkv.L) || !same(L.o.L, L0.o.L) || !same(L.up.L, L0.up.L) ||
+            !same(L.down.L, L0.down.L) || L.o.L.precision != prec || L.up.L.precision != prec ||
+            L.down.L.precision != prec)
+            return ok();
+    if (m->out.L.precision != prec) return ok();
+    StepParams& p = r->sp;
+    p = StepParams{};
+    std::vector<StepLayer> hl(c.num_layers);
+    for (int l = 0; l < c.num_layers; ++l) {
+        const Layer& L = m->layers[l];
+        StepLayer& s = hl[l];
+        s.qkv_w = L.qkv.w.as<uint8_t>();
+        s.o_w = L.o.w.as<uint8_t>();
+        s.gu_w = L.up.w.as<uint8_t>();
+        s.dn_w = L.down.w.as<uint8_t>();
+        s.qkv_s = L.qkv.s.as<float>();
+        s.o_s = L.o.s.as<float>();
+        s.gu_s = L.up.s.as<float>();
+        s.dn_s = L.down.s.as<float>();
+        s.qkv_b = L.qkv.has_bias ? L.qkv.bias.as<float>() : nullptr;
+        s.o_b = L.o.has_bias ? L.o.bias.as<float>() : nullptr;
+        s.gu_b = L.up.has_bias ? L.up.bias.as<float>() : nullptr;
+        s.dn_b = L.down.has_bias ? L.down.bias.as<float>() : nullptr;
+        s.in_norm = L.in_norm_d.as<float>();
+        s.post_norm = L.post_norm_d.as<float>();
+    }
+    p.num_layers = c.num_layers;
+    p.Lqkv = L0.qkv.L;
+    p.Lo = L0.o.L;
+    p.Lgu = L0.up.L;
+    p.Ldn = L0.down.L;
+    p.Llm = m->out.L;
+    p.lm_w = m->out.w.as<uint8_t>();
+    p.lm_s = m->out.s.as<float>();
+    p.lm_b = m->out.has_bias ? m->out.bias.as<float>() : nullptr;
+    p.final_norm = m->has_final_norm ? m->final_norm.as<float>() : nullptr;
+    p.emb = m->emb.as<float>();
+    p.H = c.hidden_dim;
+    p.nheads = c.num_heads;
+    p.Hkv = c.num_kv_heads;
+    p.d = m->head_dim;
+    p.kvd = m->kv_dim;
+    p.I = c.intermediate_dim;
+    p.V = c.vocab_size;
+    p.eps = c.rms_eps;
+    p.rope = r->rope.as<float2>();
+    p.rope_max_pos = r->max_positions;
+    p.kv_pool = r->kv.as<float>();
+    p.ptab = r->ptab.as<int>();
+    p.seq = r->seq.as<SeqState>();
+    p.logits = r->logits.as<float>();
+    const int C = r->ctx->num_sms;
+    const int G = c.num_heads / c.num_kv_heads;
+    p.A = std::max(1, std::min(16, C / c.num_kv_heads));
+    int max_smem = 0;
+    TB_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, r->ctx->device));
+    int ns = 0, sb = 0;
+    const size_t smem = step_smem_bytes(p, &ns, &sb, max_smem - 1024);
+    if (smem == 0) return ok();
+    TB_CUDA(r->step_layers.alloc(hl.size() * sizeof(StepLayer)));
+    TB_CUDA(cudaMemcpy(r->step_layers.p, hl.data(), hl.size() * sizeof(StepLayer), cudaMemcpyHostToDevice));
+    p.layers = r->step_layers.as<StepLayer>();
+    auto part = [&](DevBuf& b, const QLayout& L) { return b.alloc((size_t)L.slabs * L.Np * 4); };
+    TB_CUDA(part(r->part_qkv, p.Lqkv));
+    TB_CUDA(part(r->part_o, p.Lo));
+    TB_CUDA(part(r->part_gu, p.Lgu));
+    TB_CUDA(part(r->part_dn, p.Ldn));
+    TB_CUDA(r->step_attn.alloc((size_t)c.num_kv_heads * p.A * G * (m->head_dim + 4) * 4));
+    TB_CUDA(r->hX.alloc((size_t)c.hidden_dim * 4));
+    TB_CUDA(r->hY.alloc((size_t)c.hidden_dim * 4));
+    TB_CUDA(r->step_bar.alloc(64));
+    TB_CUDA(cudaMemset(r->step_bar.p, 0, 64));
+    p.part_qkv = r->part_qkv.as<float>();
+    p.part_o = r->part_o.as<float>();
+    p.part_gu = r->part_gu.as<float>();
+    p.part_dn = r->part_dn.as<float>();
+    p.attn_part = r->step_attn.as<float>();
+    p.hX = r->hX.as<float>();
+    p.hY = r->hY.as<float>();
+    p.bar = r->step_bar.as<unsigned int>();
+    p.err = r->ctx->err.as<int>();
+    p.nslots = ns;
+    p.slot_bytes = sb;
+    r->step_smem = smem;
+    r->step_grid = C;
+    refresh_step_params(r);
+    r->persistent_ok = true;
+    r->persistent = true;
+    return ok();
+}
+
+static tb_status record_step(tb_runner* r, cudaStream_t st) {
+    if (r->persistent) {
+        cudaError_t e = launch_decode_step(r->sp, r->step_grid, r->step_smem, st);
+        if (e != cudaSuccess) return cuda_fail(e, "launch_decode_step");
+        return ok();
+    }
+    return record_plan(r, st, true);
+}
+
 static tb_status capture_graph(tb_runner* r) {
     if (r->graph) return ok();
     cudaStream_t st = r->ctx->stream;
     cudaGraph_t g = nullptr;
     TB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    tb_status s = record_plan(r, st, true);
+    tb_status s = record_step(r, st);
     cudaError_t e = cudaStreamEndCapture(st, &g);
     if (s != TB_OK) {
         if (g) cudaGraphDestroy(g);
@@ -1211,6 +1339,7 @@ extern "C" tb_status tb_runner_create(tb_model* m, int32_t max_batch, int32_t ma
     TB_CUDA(cudaEventCreate(&r->ev0));
     TB_CUDA(cudaEventCreate(&r->ev1));
     if ((s = build_plan(r.get())) != TB_OK) return s;
+    if ((s = build_step(r.get())) != TB_OK) return s;
     TB_CUDA(cudaDeviceSynchronize());
     *out = r.release();
     return ok();
@@ -1430,6 +1559,15 @@ static tb_status gen_setup(tb_runner* r, const int32_t* prompts, const int64_t* 
                 r->graph = nullptr;
             }
         }
+    if (r->persistent_ok &&
+        (r->sp.prompt != r->prompt.as<int>() || r->sp.prompt_stride != r->prompt_stride ||
+         r->sp.out_tokens != r->out_tokens.as<int>())) {
+        refresh_step_params(r);
+        if (r->persistent && r->graph) {
+            cudaGraphExecDestroy(r->graph);
+            r->graph = nullptr;
+        }
+    }
     TB_CUDA(r->pin_tokens.ensure((size_t)r->B * std::max(maxp, mo) * 4 + 64));
     int* pin = r->pin_tokens.as<int>();
     memset(pin, 0, (size_t)r->B * r->prompt_stride * 4);
@@ -1654,6 +1792,28 @@ extern "C" tb_status tb_runner_profile_step(tb_runner* r, float* times_ms, int32
         }
     tb_status e = flush_ptab(r);
     if (e != TB_OK) return e;
+    if (r->persistent) {
+        cudaStream_t st = r->ctx->stream;
+        TB_CUDA(cudaEventRecord(r->ev0, st));
+        cudaError_t ce = launch_decode_step(r->sp, r->step_grid, r->step_smem, st);
+        if (ce != cudaSuccess) return cuda_fail(ce, "launch_decode_step");
+        TB_CUDA(cudaEventRecord(r->ev1, st));
+        TB_CUDA(cudaEventSynchronize(r->ev1));
+        float t = 0;
+        TB_CUDA(cudaEventElapsedTime(&t, r->ev0, r->ev1));
+        times_ms[0] = t;
+        kinds[0] = 2;
+        // algorithmic bytes: every weight + scale once, K/V of the context, the
+        // embedding row and the logits
+        const tb_model_config& c = r->m->cfg;
+        const int64_t L = r->kvh[0].pos + 1;
+        bytes[0] = r->m->weight_bytes + (int64_t)c.num_layers * 2 * L * r->m->kv_dim * 4 +
+                   (int64_t)c.hidden_dim * 4 + (int64_t)c.vocab_size * 4;
+        for (int s2 = 0; s2 < r->B; ++s2)
+            if (act[s2]) r->kvh[s2].pos += 1;
+        *n = 1;
+        return tb_context_check_device(r->ctx);
+    }
     std::vector<cudaEvent_t> ev(cnt + 1);
     for (auto& x : ev) TB_CUDA(cudaEventCreate(&x));
     cudaStream_t st = r->ctx->stream;
@@ -1684,5 +1844,52 @@ extern "C" tb_status tb_runner_io_bytes(tb_runner* r, int64_t* h2d, int64_t* d2h
     *h2d = r->h2d_bytes;
     *d2h = r->d2h_bytes;
     if (reset) r->h2d_bytes = r->d2h_bytes = 0;
+    return ok();
+}
+
+extern "C" tb_status tb_runner_set_persistent(tb_runner* r, int32_t enable) {
+    TB_CHECK(r, "NULL runner");
+    const bool want = enable != 0;
+    if (want && !r->persistent_ok)
+        return fail(TB_ERR_UNSUPPORTED, "the persistent step needs batch 1, a LLaMA model with uniform layers "
+                                        "and a supported head shape");
+    if (want != r->persistent) {
+        r->persistent = want;
+        if (r->graph) {
+            cudaGraphExecDestroy(r->graph);
+            r->graph = nullptr;
+        }
+    }
+    return ok();
+}
+
+extern "C" tb_status tb_runner_get_persistent(const tb_runner* r, int32_t* enabled) {
+    TB_CHECK(r && enabled, "NULL argument");
+    *enabled = r->persistent ? 1 : 0;
+    return ok();
+}
+
+extern "C" tb_status tb_runner_debug_read(tb_runner* r, int32_t which, float* out, int64_t n) {
+    TB_CHECK(r && out && n >= 0, "bad argument");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    const DevBuf* b = nullptr;
+    switch (which) {
+        case 0: b = &r->hX; break;
+        case 1: b = &r->hY; break;
+        case 2: b = &r->part_qkv; break;
+        case 3: b = &r->part_o; break;
+        case 4: b = &r->part_gu; break;
+        case 5: b = &r->part_dn; break;
+        case 6: b = &r->step_attn; break;
+        case 7: b = &r->logits; break;
+        case 8: b = &r->h; break;
+        case 9: b = &r->q; break;
+        case 10: b = &r->ctxv; break;
+        case 11: b = &r->act; break;
+        default: return fail(TB_ERR_INVALID_ARGUMENT, "unknown buffer %d", which);
+    }
+    TB_CHECK((size_t)n * 4 <= b->bytes, "buffer %d holds %zu bytes", which, b->bytes);
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    TB_CUDA(cudaMemcpy(out, b->p, (size_t)n * 4, cudaMemcpyDeviceToHost));
     return ok();
 }

@@ -1,0 +1,884 @@
+// tb_step.cu -- persistent decode step for batch 1 (sm_100a).
+//
+// One cooperative launch per token runs ModelRunner.step
+// (Sources/TinyBrainRuntime/ModelRunner.swift:168-208) end to end: for every
+// layer QKV -> attention -> o_proj -> gate/up -> down (applyLayer,
+// ModelRunner.swift:392-459), then the final norm, LM head and greedy argmax.
+//
+// Why one kernel: a batch-1 decode step streams ~1 GB of weights through ~110
+// dependent matrix products of 4-65 MB each; launched one by one, each product
+// pays launch, ramp-up and drain latencies longer than its own HBM time.  Here
+// one CTA per SM runs the whole step:
+//
+//  * a producer warp walks the CTA's static share of every phase (32-row x
+//    512-byte weight units, INT4 group scales with them, and the KV-cache pages
+//    of its attention split) and streams them with 1-D bulk async copies into a
+//    shared-memory ring.  Weights and cached K/V do not depend on this step's
+//    activations, so the stream never waits on the data dependencies between
+//    phases -- only on free ring slots;
+//  * eight consumer warps run the phases in order.  A phase starts after a
+//    grid-wide barrier (an atomic counter in global memory, bounded spin),
+//    builds its activation vector in shared memory (residual add + RMSNorm,
+//    RoPE, SiLU*up, split-K / attention-split combine -- Tensor.swift:1538-1558,
+//    ModelRunner.swift:470-579), multiplies it against the units already in the
+//    ring, and writes per-segment partial sums that the next phase reduces in a
+//    fixed order (deterministic, no atomics on data);
+//  * the LM-head phase reduces whole row blocks per CTA, writes logits and
+//    folds a packed (value, index) argmax into the sequence state with one
+//    atomicMax per warp (Sampler.swift:126-138); CTA 0 then advances the step.
+//
+// All waits are bounded (2 s of %globaltimer); a timeout records an error code
+// and makes the CTA leave the step early without hanging the device.
+#include "tb_common.cuh"
+#include "tb_kernels.h"
+#include "tb_unit.cuh"
+
+#include <algorithm>
+
+namespace tb {
+
+namespace {
+
+constexpr int kMaxSlots = 24;
+constexpr int kBarRegion = 1024;  // mbarriers + flags
+constexpr int kMiscFloats = 1024;
+constexpr int kConsumers = kStepConsumerWarps * 32;
+
+struct Shared {
+    uint64_t* full;
+    uint64_t* empty;
+    int* valid;             // [kMaxSlots] attention tile present (page not evicted)
+    volatile int* abort;    // set when a wait timed out
+    volatile int* go;       // thread 0's per-phase decision
+    float* misc;            // [kMiscFloats]
+    uint8_t* ring;
+    float* xs;              // activation vector, lane-interleaved per slab
+    float* att;             // attention scratch
+    uint32_t* segmask[4];   // per 32-row block: bit s = a CTA segment starts at slab s (qkv, o, gate/up, down)
+};
+
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned int* p, unsigned int v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// The CTA whose static unit range [c*U/C, (c+1)*U/C) contains unit u.
+__device__ __forceinline__ int owner_of(int u, int U, int C) { return (int)(((long long)u * C + C - 1) / U); }
+
+__device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+
+__device__ __forceinline__ int att_floats(int G, int d, int Hkv, int A) {
+    return max(G * d + 2 * d + 2 * G * kPageTokens, Hkv * G * A);
+}
+
+// Geometry of one 32-row unit u of a GEMV phase (units ordered 32-row block
+// major, slab minor).  A 64-row block (fused gate/up) is two 32-row units.
+struct UnitGeo {
+    int rb32, s, sb;
+    const uint8_t* w;
+    const float* sc;  // INT4 scales of the unit
+};
+__device__ __forceinline__ UnitGeo unit_geo(const QLayout& L, const uint8_t* w, const float* sc, int u) {
+    UnitGeo g;
+    g.rb32 = u / L.slabs;
+    g.s = u % L.slabs;
+    g.sb = min(kSlabBytes, L.row_bytes - g.s * kSlabBytes);
+    const int per = L.RB / 32;
+    const int rbb = g.rb32 / per, half = g.rb32 % per;
+    g.w = w + (size_t)rbb * L.RB * L.row_bytes + (size_t)g.s * L.RB * kSlabBytes + (size_t)half * 32 * g.sb;
+    g.sc = (L.precision == 4) ? sc + (((size_t)rbb * L.slabs + g.s) * per + half) * 1024 : nullptr;
+    return g;
+}
+
+// ------------------------------------------------------------------ producer --
+struct Producer {
+    const StepParams& p;
+    Shared& sh;
+    int it = 0;
+    uint64_t pol;
+    bool dead = false;
+
+    __device__ Producer(const StepParams& p_, Shared& sh_) : p(p_), sh(sh_) { pol = l2_policy_evict_first(); }
+
+    __device__ uint8_t* acquire(int& st) {
+        st = it % p.nslots;
+        if (it >= p.nslots) {
+            const uint32_t par = ((it / p.nslots) - 1) & 1;
+            const uint64_t t0 = global_timer_ns();
+            while (!mbar_try_wait(&sh.empty[st], par)) {
+                if (*sh.abort || global_timer_ns() - t0 > kWaitLimitNs) {
+                    if (!*sh.abort) record_error(p.err, kDevWaitTimeout);
+                    dead = true;
+                    *sh.abort = 1;
+                    return nullptr;
+                }
+            }
+        }
+        return sh.ring + (size_t)st * p.slot_bytes;
+    }
+
+    __device__ void gemv(const QLayout& L, const uint8_t* w, const float* sc, int u0, int u1) {
+        for (int u = u0; u < u1 && !dead; ++u) {
+            const UnitGeo g = unit_geo(L, w, sc, u);
+            int st;
+            uint8_t* dst = acquire(st);
+            if (!dst) return;
+            const uint32_t wb = 32u * g.sb, sbytes = (L.precision == 4) ? 4096u : 0u;
+            mbar_arrive_expect_tx(&sh.full[st], wb + sbytes);
+            bulk_g2s_stream(dst, g.w, wb, &sh.full[st], pol);
+            if (L.precision == 4) bulk_g2s_stream(dst + 16384, g.sc, sbytes, &sh.full[st], pol);
+            ++it;
+        }
+    }
+
+    __device__ void attention(int layer, int head, int pg0, int pg1) {
+        const int tile = kPageTokens * p.d;  // floats
+        for (int pg = pg0; pg < pg1 && !dead; ++pg) {
+            int st;
+            uint8_t* dst = acquire(st);
+            if (!dst) return;
+            const int page = p.ptab[pg];
+            if (page >= 0) {
+                sh.valid[st] = 1;
+                const size_t kb = ((((size_t)page * p.num_layers + layer) * 2 + 0) * p.Hkv + head) * (size_t)tile;
+                const size_t vb = ((((size_t)page * p.num_layers + layer) * 2 + 1) * p.Hkv + head) * (size_t)tile;
+                mbar_arrive_expect_tx(&sh.full[st], 2u * tile * 4u);
+                bulk_g2s(dst, p.kv_pool + kb, tile * 4u, &sh.full[st]);
+                bulk_g2s(dst + tile * 4, p.kv_pool + vb, tile * 4u, &sh.full[st]);
+            } else {
+                sh.valid[st] = 0;  // evicted page: rows read as zeros (KVCache.swift:239-253)
+                mbar_arrive(&sh.full[st]);
+            }
+            ++it;
+        }
+    }
+
+    // After an abort: wait (bounded) until every copy this warp issued has landed.
+    __device__ void drain() {
+        const int first = it > p.nslots ? it - p.nslots : 0;
+        const uint64_t t0 = global_timer_ns();
+        for (int j = first; j < it; ++j) {
+            const int st = j % p.nslots;
+            while (!mbar_try_wait(&sh.full[st], (j / p.nslots) & 1))
+                if (global_timer_ns() - t0 > kWaitLimitNs) return;
+        }
+    }
+};
+
+// ------------------------------------------------------------------ consumer --
+struct Consumer {
+    const StepParams& p;
+    Shared& sh;
+    int it = 0;
+    int ctid, warp, lane, c, C;
+
+    __device__ Consumer(const StepParams& p_, Shared& sh_) : p(p_), sh(sh_) {
+        ctid = threadIdx.x;
+        warp = ctid >> 5;
+        lane = ctid & 31;
+        c = blockIdx.x;
+        C = gridDim.x;
+    }
+
+    __device__ void bar() { named_bar_sync(1, kConsumers); }
+
+    // Grid barrier: wait until every CTA finished phase (phase - 1).  The
+    // go/stop decision is taken by thread 0 and published through sh.go before
+    // the barrier, so every consumer warp takes the same branch.
+    __device__ bool phase_begin(int phase) {
+        if (ctid == 0) {
+            if (phase > 0 && !*sh.abort) {
+                const unsigned int target = (unsigned int)C * (unsigned int)phase;
+                if (ld_acquire(p.bar) < target) {
+                    const uint64_t t0 = global_timer_ns();
+                    while (ld_acquire(p.bar) < target) {
+                        if (global_timer_ns() - t0 > kWaitLimitNs) {
+                            record_error(p.err, kDevWaitTimeout);
+                            *sh.abort = 1;
+                            break;
+                        }
+                    }
+                }
+            }
+            *sh.go = *sh.abort ? 0 : 1;
+        }
+        bar();
+        return *sh.go != 0;
+    }
+    __device__ void phase_end() {
+        bar();
+        if (ctid == 0) {
+            __threadfence();
+            red_release_add(p.bar, 1u);
+        }
+    }
+
+    __device__ const uint8_t* wait_slot(int& st) {
+        st = it % p.nslots;
+        if (*sh.abort) return nullptr;
+        if (!mbar_wait(&sh.full[st], (it / p.nslots) & 1, p.err)) {
+            *sh.abort = 1;
+            return nullptr;
+        }
+        return sh.ring + (size_t)st * p.slot_bytes;
+    }
+    __device__ void release_slot(int st) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.empty[st]);
+        ++it;
+    }
+
+    // Sums of the split-K partials of NJ GPU rows of a phase, scaled and biased.
+    // A partial is stored at the slab where its CTA's segment of the row block
+    // starts; segments are summed in slab order.  All loads are issued before
+    // the first add, so NJ rows cost one L2 round trip, not one per segment.
+    template <int NJ>
+    __device__ void reduce_rows(const QLayout& L, const uint32_t* tab, const float* part, const float* sc,
+                                const float* bias, const int (&n)[NJ], const bool (&use)[NJ], float (&out)[NJ]) {
+        constexpr int SEGMAX = 8;
+        float v[NJ][SEGMAX];
+        uint32_t m0[NJ], rest[NJ];
+        float scv[NJ], bv[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            uint32_t m = use[j] ? tab[n[j] >> 5] : 0u;
+            m0[j] = m;
+#pragma unroll
+            for (int g = 0; g < SEGMAX; ++g) {
+                const int sl = __ffs(m) - 1;  // -1: no segment left
+                v[j][g] = sl >= 0 ? __ldcg(part + (size_t)sl * L.Np + n[j]) : 0.0f;
+                m &= m - 1;
+            }
+            rest[j] = m;
+            scv[j] = (use[j] && L.precision == 8) ? __ldg(sc + n[j]) : 1.0f;
+            bv[j] = (use[j] && bias) ? __ldg(bias + n[j]) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const int cnt = __popc(m0[j]);
+            float t = 0.0f;
+#pragma unroll
+            for (int g = 0; g < SEGMAX; ++g)
+                if (g < cnt) t += v[j][g];
+            for (uint32_t m = rest[j]; m; m &= m - 1) t += __ldcg(part + (size_t)(__ffs(m) - 1) * L.Np + n[j]);
+            float r = (L.precision == 8) ? __fmul_rn(t, scv[j]) : t;
+            if (bias) r = __fadd_rn(r, bv[j]);
+            out[j] = r;
+        }
+    }
+
+    template <int PREC>
+    __device__ void put_x(const QLayout& L, int k, float v) {
+        constexpr int CH = PREC == 8 ? 16 : 32;
+        if (PREC == 4) v *= int4_pos_scale(k & 7);
+        const int s = k / L.slab_k;
+        sh.xs[s * L.slab_k + xperm<CH>(k - s * L.slab_k)] = v;
+    }
+
+    // h = src + (reduced partials of the previous phase); optional store of
+    // this CTA's slice of h; x = RMSNorm(h) * w (or h when norm == null).
+    template <int PREC>
+    __device__ void residual_norm(const float* src, const QLayout* Lp, const uint32_t* tab, const float* part,
+                                  const float* sc, const float* bias, float* store, const float* norm,
+                                  const QLayout& Lnext) {
+        const int H = p.H;
+        constexpr int MAXJ = 16;  // H <= 4096
+        float hv[MAXJ];
+        float ss = 0.0f;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            int n[8];
+            bool use[8];
+            float add[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                n[j] = ctid + kConsumers * (half * 8 + j);
+                use[j] = n[j] < H;
+                if (!use[j]) n[j] = 0;
+                add[j] = 0.0f;
+            }
+            if (Lp) reduce_rows<8>(*Lp, tab, part, sc, bias, n, use, add);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float v = use[j] ? __ldcg(src + n[j]) : 0.0f;
+                if (Lp) v = __fadd_rn(v, add[j]);
+                hv[half * 8 + j] = v;
+                ss = fmaf(v, v, ss);
+            }
+        }
+        if (store) {
+            const int k0 = (int)((long long)c * H / C), k1 = (int)((long long)(c + 1) * H / C);
+#pragma unroll
+            for (int j = 0; j < MAXJ; ++j) {
+                const int k = ctid + kConsumers * j;
+                if (k >= k0 && k < k1) store[k] = hv[j];
+            }
+        }
+        float inv = 1.0f;
+        if (norm) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) sh.misc[warp] = ss;
+            bar();
+            float t = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kStepConsumerWarps; ++w) t += sh.misc[w];
+            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), p.eps)));
+        }
+#pragma unroll
+        for (int j = 0; j < MAXJ; ++j) {
+            const int k = ctid + kConsumers * j;
+            if (k < H) put_x<PREC>(Lnext, k, norm ? __fmul_rn(__fmul_rn(hv[j], inv), __ldg(norm + k)) : hv[j]);
+        }
+        for (int k = H + ctid; k < Lnext.Kp; k += kConsumers) put_x<PREC>(Lnext, k, 0.0f);
+        bar();
+    }
+
+    // Multiply this CTA's units of a GEMV phase; write one partial per row and
+    // segment, at the slab where the segment starts.
+    template <int PREC>
+    __device__ void gemv_units(const QLayout& L, float* part) {
+        const int U = (L.Np / 32) * L.slabs;
+        const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
+        float2 acc[4][1];
+        int cur = -1, s_first = 0;
+        auto flush = [&](int rb32, int slab) {
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                float v = acc[r][0].x + acc[r][0].y;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == r) part[(size_t)slab * L.Np + rb32 * 32 + warp * 4 + r] = v;
+                acc[r][0] = make_float2(0.f, 0.f);
+            }
+        };
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r][0] = make_float2(0.f, 0.f);
+        for (int u = u0; u < u1; ++u) {
+            const int rb32 = u / L.slabs, s = u % L.slabs;
+            if (rb32 != cur) {
+                if (cur >= 0) flush(cur, s_first);
+                cur = rb32;
+                s_first = s;
+            }
+            int st;
+            const uint8_t* slot = wait_slot(st);
+            if (!slot) return;
+            const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
+            const float* ssl = (PREC == 4) ? reinterpret_cast<const float*>(slot + 16384) : nullptr;
+            unit_dot<PREC, 4, 1>(slot, sb, warp * 4, ssl, sh.xs + s * L.slab_k, 0, lane, acc);
+            release_slot(st);
+        }
+        if (cur >= 0) flush(cur, s_first);
+    }
+
+    // ---------------------------------------------------------------- attention
+    template <int G, int D>
+    __device__ void attention(int layer, int pos, int npages) {
+        constexpr int DP = kConsumers / (G * kPageTokens);
+        constexpr int CHK = D / DP;
+        constexpr int PVT = G * (D / 4);
+        static_assert(DP >= 1 && CHK >= 1 && CHK <= 64 && PVT <= kConsumers, "head geometry");
+        const int A = p.A;
+        if (c >= A * p.Hkv) return;  // uniform per CTA
+        const int head = c / A, split = c % A;
+        const int pps = (npages + A - 1) / A;
+        const int pg0 = min(npages, split * pps), pg1 = min(npages, pg0 + pps);
+        float* qs = sh.att;        // [G][D]
+        float* knew = qs + G * D;  // [D]
+        float* vnew = knew + D;    // [D]
+        float* S = vnew + D;       // [2][G][16]
+        const QLayout& L = p.Lqkv;
+        const StepLayer& ly = p.layers[layer];
+        const float2* rope = p.rope + (size_t)min(pos, p.rope_max_pos - 1) * (D / 2);
+        // q (RoPE'd) for the G query heads of this KV head (ModelRunner.swift:499-515).
+        for (int e = ctid; e < G * D / 2; e += kConsumers) {
+            int n[2] = {head * G * D + 2 * e, head * G * D + 2 * e + 1};
+            bool use[2] = {true, true};
+            float v[2];
+            reduce_rows<2>(L, sh.segmask[0], p.part_qkv, ly.qkv_s, ly.qkv_b, n, use, v);
+            const float2 cs = rope[(2 * e % D) / 2];
+            qs[2 * e] = __fsub_rn(__fmul_rn(v[0], cs.x), __fmul_rn(v[1], cs.y));
+            qs[2 * e + 1] = __fadd_rn(__fmul_rn(v[0], cs.y), __fmul_rn(v[1], cs.x));
+        }
+        const bool owner = pg0 < pg1 && pg1 == npages;
+        if (owner) {  // this split holds the current position: append k, v (KVCache.swift:157-224)
+            for (int e = ctid; e < D / 2; e += kConsumers) {
+                const int nk = p.H + head * D + 2 * e;
+                const int nv = p.H + p.kvd + head * D + 2 * e;
+                int n[4] = {nk, nk + 1, nv, nv + 1};
+                bool use[4] = {true, true, true, true};
+                float v[4];
+                reduce_rows<4>(L, sh.segmask[0], p.part_qkv, ly.qkv_s, ly.qkv_b, n, use, v);
+                const float2 cs = rope[e];
+                const float r0 = __fsub_rn(__fmul_rn(v[0], cs.x), __fmul_rn(v[1], cs.y));
+                const float r1 = __fadd_rn(__fmul_rn(v[0], cs.y), __fmul_rn(v[1], cs.x));
+                knew[2 * e] = r0;
+                knew[2 * e + 1] = r1;
+                vnew[2 * e] = v[2];
+                vnew[2 * e + 1] = v[3];
+                const int page = p.ptab[pos / kPageTokens];
+                if (page < 0) {
+                    record_error(p.err, kDevBadPage);
+                } else {
+                    const size_t kb = ((((size_t)page * p.num_layers + layer) * 2 + 0) * p.Hkv + head) * kPageTokens +
+                                      pos % kPageTokens;
+                    const size_t vb = ((((size_t)page * p.num_layers + layer) * 2 + 1) * p.Hkv + head) * kPageTokens +
+                                      pos % kPageTokens;
+                    p.kv_pool[kb * D + 2 * e] = r0;
+                    p.kv_pool[kb * D + 2 * e + 1] = r1;
+                    p.kv_pool[vb * D + 2 * e] = v[2];
+                    p.kv_pool[vb * D + 2 * e + 1] = v[3];
+                }
+            }
+        }
+        bar();
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+        const int pair = ctid / DP, dp = ctid % DP;
+        const int gq = pair / kPageTokens, j = pair % kPageTokens;
+        float qrot[CHK];
+#pragma unroll
+        for (int e = 0; e < CHK; ++e) qrot[e] = qs[gq * D + dp * CHK + (e + j) % CHK];
+        const bool pv = ctid < PVT;
+        const int gv = ctid / (D / 4), dv = (ctid % (D / 4)) * 4;
+        float run_m = -INFINITY, run_l = 0.0f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int cur_row = pos % kPageTokens;
+        for (int i = 0; i < pg1 - pg0; ++i) {
+            // Every warp walks every barrier even after a failed wait (no early exit).
+            int st;
+            const uint8_t* slot = wait_slot(st);
+            const bool have = slot != nullptr;
+            const float* Kt = have ? reinterpret_cast<const float*>(slot) : knew;
+            const float* Vt = have ? Kt + kPageTokens * D : vnew;
+            const bool ok = have && sh.valid[st] != 0;
+            const bool last = have && owner && (pg0 + i == npages - 1);
+            float* Sb = S + (i & 1) * G * kPageTokens;
+            {
+                float dot = 0.0f;
+                const bool cur = last && j == cur_row;
+                const float* kr = cur ? knew + dp * CHK : Kt + j * D + dp * CHK;
+                if (ok || cur) {
+#pragma unroll
+                    for (int e = 0; e < CHK; ++e) dot = fmaf(qrot[e], kr[(e + j) % CHK], dot);
+                }
+#pragma unroll
+                for (int o = DP / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+                const int tok = (pg0 + i) * kPageTokens + j;
+                if (dp == 0) Sb[gq * kPageTokens + j] = (tok <= pos) ? __fmul_rn(dot, scale) : -INFINITY;
+            }
+            bar();
+            if (pv) {
+                const float* Sg = Sb + gv * kPageTokens;
+                float pm = Sg[0];
+#pragma unroll
+                for (int jj = 1; jj < kPageTokens; ++jj) pm = fmaxf(pm, Sg[jj]);
+                const float mnew = fmaxf(run_m, pm);
+                const float corr = (run_m == -INFINITY) ? 0.0f : expf(run_m - mnew);
+                float l = run_l * corr;
+                float4 a = make_float4(acc.x * corr, acc.y * corr, acc.z * corr, acc.w * corr);
+#pragma unroll
+                for (int jj = 0; jj < kPageTokens; ++jj) {
+                    const float s = Sg[jj];
+                    const float e = (s == -INFINITY) ? 0.0f : expf(s - mnew);
+                    l += e;
+                    const bool cur = last && jj == cur_row;
+                    if (ok || cur) {
+                        const float4 v = cur ? *reinterpret_cast<const float4*>(vnew + dv)
+                                             : *reinterpret_cast<const float4*>(Vt + jj * D + dv);
+                        a.x = fmaf(e, v.x, a.x);
+                        a.y = fmaf(e, v.y, a.y);
+                        a.z = fmaf(e, v.z, a.z);
+                        a.w = fmaf(e, v.w, a.w);
+                    }
+                }
+                run_m = mnew;
+                run_l = l;
+                acc = a;
+            }
+            if (have) {
+                release_slot(st);
+            } else {
+                ++it;
+            }
+        }
+        if (pv && !*sh.abort) {
+            float* part = p.attn_part + (((size_t)head * A + split) * G + gv) * (D + 4);
+            *reinterpret_cast<float4*>(part + dv) = acc;
+            if (dv == 0) {
+                part[D] = run_m;
+                part[D + 1] = run_l;
+            }
+        }
+    }
+
+    // Slab range of K touched by this CTA's units of a phase.
+    __device__ void slab_span(const QLayout& L, int& kb, int& ke) {
+        const int U = (L.Np / 32) * L.slabs;
+        const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
+        int smin = L.slabs, smax = -1;
+        if (u1 - u0 >= L.slabs) {
+            smin = 0;
+            smax = L.slabs - 1;
+        } else {
+            for (int u = u0; u < u1; ++u) {
+                smin = min(smin, u % L.slabs);
+                smax = max(smax, u % L.slabs);
+            }
+        }
+        kb = smin * L.slab_k;
+        ke = min((smax + 1) * L.slab_k, L.Kp);
+    }
+
+    // ctx[k] for the slabs this CTA's o_proj units need: combine the attention
+    // splits in split order (softmax rescaling of (m, l, acc) partials).
+    template <int PREC, int G, int D>
+    __device__ void ctx_prologue() {
+        constexpr int AMAX = 16;
+        const QLayout& L = p.Lo;
+        const int A = p.A;
+        float2* ml = reinterpret_cast<float2*>(sh.misc);  // [Hkv][A][G] (m, l)
+        float* wts = sh.att;                              // [Hkv][G][A]
+        const int nml = p.Hkv * A * G;
+        for (int e = ctid; e < nml; e += kConsumers) {
+            const float* q = p.attn_part + (size_t)e * (D + 4) + D;
+            ml[e] = make_float2(__ldcg(q), __ldcg(q + 1));
+        }
+        bar();
+        for (int e = ctid; e < p.Hkv * G; e += kConsumers) {
+            const int hk = e / G, g = e % G;
+            float M = -INFINITY;
+            for (int sp = 0; sp < A; ++sp) M = fmaxf(M, ml[(hk * A + sp) * G + g].x);
+            float den = 0.0f;
+            for (int sp = 0; sp < A; ++sp) {
+                const float2 t = ml[(hk * A + sp) * G + g];
+                const float w = (t.x == -INFINITY || M == -INFINITY) ? 0.0f : expf(t.x - M);
+                wts[e * A + sp] = w;
+                den = fmaf(w, t.y, den);
+            }
+            const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+            for (int sp = 0; sp < A; ++sp) wts[e * A + sp] *= inv;
+        }
+        bar();
+        int kb, ke;
+        slab_span(L, kb, ke);
+        for (int k = kb + ctid; k < ke; k += kConsumers) {
+            float v = 0.0f;
+            if (k < L.K) {
+                const int hq = k / D, i = k % D;
+                const int hk = hq / G, g = hq % G;
+                const float* w = wts + (hk * G + g) * A;
+                float a[AMAX];
+#pragma unroll
+                for (int sp = 0; sp < AMAX; ++sp)
+                    a[sp] = sp < A ? __ldcg(p.attn_part + (((size_t)hk * A + sp) * G + g) * (D + 4) + i) : 0.0f;
+#pragma unroll
+                for (int sp = 0; sp < AMAX; ++sp)
+                    if (sp < A) v = fmaf(w[sp], a[sp], v);
+            }
+            put_x<PREC>(L, k, v);
+        }
+        bar();
+    }
+
+    // act[k] = silu(gate[k]) * up[k] for the slabs this CTA's down units need.
+    template <int PREC>
+    __device__ void act_prologue(const StepLayer& ly) {
+        const QLayout& L = p.Ldn;
+        const QLayout& GL = p.Lgu;
+        int kb, ke;
+        slab_span(L, kb, ke);
+        for (int k0 = kb + ctid; k0 < ke; k0 += 4 * kConsumers) {
+            int n[8];
+            bool use[8];
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int k = k0 + kConsumers * j;
+                const bool ok = k < ke && k < L.K;
+                const int grow = ok ? (k / 32) * 64 + (k % 32) : 0;
+                n[2 * j] = grow;
+                n[2 * j + 1] = grow + 32;
+                use[2 * j] = use[2 * j + 1] = ok;
+            }
+            reduce_rows<8>(GL, sh.segmask[2], p.part_gu, ly.gu_s, ly.gu_b, n, use, v);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int k = k0 + kConsumers * j;
+                if (k < ke) put_x<PREC>(L, k, use[2 * j] ? __fmul_rn(silu_ref(v[2 * j]), v[2 * j + 1]) : 0.0f);
+            }
+        }
+        bar();
+    }
+
+    // LM head: whole row blocks per CTA, logits + argmax (Sampler.swift:126-138).
+    template <int PREC>
+    __device__ void lm_head(unsigned long long* best_out) {
+        const QLayout& L = p.Llm;
+        const int nrb = L.Np / 32;
+        const int r0 = (int)((long long)c * nrb / C), r1 = (int)((long long)(c + 1) * nrb / C);
+        unsigned long long best = 0ull;
+        for (int rb = r0; rb < r1; ++rb) {
+            float2 acc[4][1];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[r][0] = make_float2(0.f, 0.f);
+            for (int s = 0; s < L.slabs; ++s) {
+                int st;
+                const uint8_t* slot = wait_slot(st);
+                if (!slot) return;
+                const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
+                const float* ssl = (PREC == 4) ? reinterpret_cast<const float*>(slot + 16384) : nullptr;
+                unit_dot<PREC, 4, 1>(slot, sb, warp * 4, ssl, sh.xs + s * L.slab_k, 0, lane, acc);
+                release_slot(st);
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                float v = acc[r][0].x + acc[r][0].y;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                const int n = rb * 32 + warp * 4 + r;
+                if (lane == r && n < L.N) {
+                    float lv = (PREC == 8) ? __fmul_rn(v, p.lm_s[n]) : v;
+                    if (p.lm_b) lv = __fadd_rn(lv, p.lm_b[n]);
+                    if (p.logits) p.logits[n] = lv;
+                    const unsigned long long key = argmax_key(lv, n);
+                    best = key > best ? key : best;
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+            best = t > best ? t : best;
+        }
+        if (lane == 0 && best != 0ull) atomicMax(best_out, best);
+    }
+};
+
+template <int PREC, int G, int D>
+__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    Shared sh;
+    sh.full = reinterpret_cast<uint64_t*>(smem);
+    sh.empty = sh.full + kMaxSlots;
+    sh.valid = reinterpret_cast<int*>(sh.empty + kMaxSlots);
+    sh.abort = reinterpret_cast<volatile int*>(sh.valid + kMaxSlots);
+    sh.go = sh.abort + 1;
+    sh.misc = reinterpret_cast<float*>(smem + kBarRegion);
+    sh.ring = smem + kBarRegion + kMiscFloats * 4;
+    sh.xs = reinterpret_cast<float*>(sh.ring + (size_t)p.nslots * p.slot_bytes);
+    const int xfloats = max(max(max(p.Lqkv.slabs * p.Lqkv.slab_k, p.Lo.slabs * p.Lo.slab_k),
+                                max(p.Lgu.slabs * p.Lgu.slab_k, p.Ldn.slabs * p.Ldn.slab_k)),
+                            p.Llm.slabs * p.Llm.slab_k);
+    sh.att = sh.xs + xfloats;
+    {
+        uint32_t* t = reinterpret_cast<uint32_t*>(sh.att + att_floats(G, D, p.Hkv, p.A));
+        const QLayout* Ls[4] = {&p.Lqkv, &p.Lo, &p.Lgu, &p.Ldn};
+        for (int i = 0; i < 4; ++i) {
+            sh.segmask[i] = t;
+            t += (Ls[i]->Np / 32 + 3) / 4 * 4;
+        }
+    }
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int C = gridDim.x, c = blockIdx.x;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.nslots; ++i) {
+            mbar_init(&sh.full[i], 1);
+            mbar_init(&sh.empty[i], kStepConsumerWarps);
+        }
+        *sh.abort = 0;
+        *sh.go = 1;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    const int pos = p.seq->pos;
+    const int npages = pos / kPageTokens + 1;
+    const int A = p.A;
+    const int head = c < A * p.Hkv ? c / A : -1;
+    const int split = c < A * p.Hkv ? c % A : 0;
+    const int pps = (npages + A - 1) / A;
+    const int apg0 = min(npages, split * pps), apg1 = min(npages, apg0 + pps);
+
+    if (warp == kStepConsumerWarps) {
+        if (lane == 0) {
+            Producer pr(p, sh);
+            auto range = [&](const QLayout& L, int& u0, int& u1) {
+                const int U = (L.Np / 32) * L.slabs;
+                u0 = (int)((long long)c * U / C);
+                u1 = (int)((long long)(c + 1) * U / C);
+            };
+            int u0, u1;
+            for (int l = 0; l < p.num_layers && !pr.dead; ++l) {
+                const StepLayer& ly = p.layers[l];
+                range(p.Lqkv, u0, u1);
+                pr.gemv(p.Lqkv, ly.qkv_w, ly.qkv_s, u0, u1);
+                if (head >= 0) pr.attention(l, head, apg0, apg1);
+                range(p.Lo, u0, u1);
+                pr.gemv(p.Lo, ly.o_w, ly.o_s, u0, u1);
+                range(p.Lgu, u0, u1);
+                pr.gemv(p.Lgu, ly.gu_w, ly.gu_s, u0, u1);
+                range(p.Ldn, u0, u1);
+                pr.gemv(p.Ldn, ly.dn_w, ly.dn_s, u0, u1);
+            }
+            if (!pr.dead) {
+                const int nrb = p.Llm.Np / 32;
+                const int r0 = (int)((long long)c * nrb / C), r1 = (int)((long long)(c + 1) * nrb / C);
+                pr.gemv(p.Llm, p.lm_w, p.lm_s, r0 * p.Llm.slabs, r1 * p.Llm.slabs);
+            }
+            if (pr.dead) pr.drain();
+        }
+        return;
+    }
+
+    Consumer cs(p, sh);
+    {
+        // Where the CTA segments of each 32-row block start (bit per slab).
+        const QLayout* Ls[4] = {&p.Lqkv, &p.Lo, &p.Lgu, &p.Ldn};
+        for (int i = 0; i < 4; ++i) {
+            const QLayout& L = *Ls[i];
+            const int nrb = L.Np / 32, U = nrb * L.slabs;
+            for (int rb = threadIdx.x; rb < nrb; rb += kConsumers) {
+                uint32_t m = 1u;
+                for (int s = 1; s < L.slabs; ++s)
+                    if (owner_of(rb * L.slabs + s, U, C) != owner_of(rb * L.slabs + s - 1, U, C)) m |= 1u << s;
+                sh.segmask[i][rb] = m;
+            }
+        }
+    }
+    int phase = 0;
+    for (int l = 0; l < p.num_layers; ++l) {
+        const StepLayer& ly = p.layers[l];
+        // ---- QKV: h_in = (embedding | h_mid(l-1) + down(l-1)); x = RMSNorm(h_in) ----
+        if (!cs.phase_begin(phase++)) return;
+        if (l == 0) {
+            int tok = p.seq->token;
+            if (tok < 0 || tok >= p.V) {
+                if (threadIdx.x == 0) record_error(p.err, kDevBadToken);
+                tok = 0;
+            }
+            cs.residual_norm<PREC>(p.emb + (size_t)tok * p.H, nullptr, nullptr, nullptr, nullptr, nullptr, p.hX,
+                                   ly.in_norm, p.Lqkv);
+        } else {
+            const StepLayer& pl = p.layers[l - 1];
+            cs.residual_norm<PREC>(p.hY, &p.Ldn, sh.segmask[3], p.part_dn, pl.dn_s, pl.dn_b, p.hX, ly.in_norm,
+                                   p.Lqkv);
+        }
+        cs.gemv_units<PREC>(p.Lqkv, p.part_qkv);
+        cs.phase_end();
+        // ---- attention over the paged cache (+ RoPE, KV append) ----
+        if (!cs.phase_begin(phase++)) return;
+        cs.attention<G, D>(l, pos, npages);
+        cs.phase_end();
+        // ---- o_proj ----
+        if (!cs.phase_begin(phase++)) return;
+        cs.ctx_prologue<PREC, G, D>();
+        cs.gemv_units<PREC>(p.Lo, p.part_o);
+        cs.phase_end();
+        // ---- gate/up: h_mid = h_in + o; x = RMSNorm(h_mid) ----
+        if (!cs.phase_begin(phase++)) return;
+        cs.residual_norm<PREC>(p.hX, &p.Lo, sh.segmask[1], p.part_o, ly.o_s, ly.o_b, p.hY, ly.post_norm, p.Lgu);
+        cs.gemv_units<PREC>(p.Lgu, p.part_gu);
+        cs.phase_end();
+        // ---- down ----
+        if (!cs.phase_begin(phase++)) return;
+        cs.act_prologue<PREC>(ly);
+        cs.gemv_units<PREC>(p.Ldn, p.part_dn);
+        cs.phase_end();
+    }
+    // ---- final norm + LM head + argmax ----
+    if (!cs.phase_begin(phase++)) return;
+    {
+        const StepLayer& pl = p.layers[p.num_layers - 1];
+        cs.residual_norm<PREC>(p.hY, &p.Ldn, sh.segmask[3], p.part_dn, pl.dn_s, pl.dn_b, nullptr, p.final_norm,
+                               p.Llm);
+    }
+    cs.lm_head<PREC>(&p.seq->best);
+    cs.phase_end();
+    // ---- CTA 0 advances the step once every CTA folded its argmax ----
+    if (c == 0 && cs.phase_begin(phase)) {
+        if (threadIdx.x == 0) {
+            __threadfence();
+            finish_sequence_step(*p.seq, 0, p.out_tokens, p.prompt, p.prompt_stride);
+            *p.bar = 0u;  // every CTA has passed its last barrier read
+        }
+    }
+}
+
+template <int PREC, int G, int D>
+cudaError_t launch_t(const StepParams& p, int grid, size_t smem, cudaStream_t stream) {
+    auto kfn = decode_step_kernel<PREC, G, D>;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
+    cfg.blockDim = dim3(kStepThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kfn, p);
+}
+
+bool supported(int prec, int G, int d) {
+    if (prec != 8 && prec != 4) return false;
+    return (G == 8 && d == 64) || (G == 1 && (d == 64 || d == 128)) || (G == 4 && d == 32) ||
+           (prec == 8 && ((G == 4 && d == 64) || (G == 2 && d == 64) || (G == 1 && d == 32)));
+}
+
+}  // namespace
+
+size_t step_smem_bytes(const StepParams& p, int* nslots, int* slot_bytes, int max_smem) {
+    const int G = p.nheads / p.Hkv;
+    if (!supported(p.Lqkv.precision, G, p.d)) return 0;
+    if (p.A > 16 || (size_t)p.Hkv * G * p.A * 2 > (size_t)kMiscFloats) return 0;  // (m, l) staging in misc
+    const int slot = p.Lqkv.precision == 4 ? 16384 + 4096 : 16384;
+    const int att_tile = 2 * kPageTokens * p.d * 4;
+    const int sbytes = std::max(slot, att_tile);
+    const int xfloats = std::max(std::max(std::max(p.Lqkv.slabs * p.Lqkv.slab_k, p.Lo.slabs * p.Lo.slab_k),
+                                          std::max(p.Lgu.slabs * p.Lgu.slab_k, p.Ldn.slabs * p.Ldn.slab_k)),
+                                 p.Llm.slabs * p.Llm.slab_k);
+    const size_t att = (size_t)std::max(G * p.d + 2 * p.d + 2 * G * kPageTokens, p.Hkv * G * p.A) * 4;
+    size_t tabs = 0;
+    for (const QLayout* L : {&p.Lqkv, &p.Lo, &p.Lgu, &p.Ldn}) {
+        if (L->slabs > 32) return 0;  // segment masks are 32-bit
+        tabs += (size_t)(L->Np / 32 + 3) / 4 * 4 * 4;
+    }
+    const size_t fixed = kBarRegion + kMiscFloats * 4 + (size_t)xfloats * 4 + att + tabs;
+    if ((size_t)max_smem <= fixed + 2 * (size_t)sbytes) return 0;
+    int ns = (int)((max_smem - fixed) / sbytes);
+    ns = std::min(ns, kMaxSlots);
+    *nslots = ns;
+    *slot_bytes = sbytes;
+    return fixed + (size_t)ns * sbytes;
+}
+
+cudaError_t launch_decode_step(const StepParams& p, int grid, size_t smem, cudaStream_t stream) {
+    const int G = p.nheads / p.Hkv;
+    const int prec = p.Lqkv.precision;
+#define TB_STEP_CASE(pr, g, dd) \
+    if (prec == pr && G == g && p.d == dd) return launch_t<pr, g, dd>(p, grid, smem, stream);
+    TB_STEP_CASE(8, 8, 64)
+    TB_STEP_CASE(4, 8, 64)
+    TB_STEP_CASE(8, 1, 128)
+    TB_STEP_CASE(4, 1, 128)
+    TB_STEP_CASE(8, 1, 64)
+    TB_STEP_CASE(4, 1, 64)
+    TB_STEP_CASE(8, 4, 32)
+    TB_STEP_CASE(4, 4, 32)
+    TB_STEP_CASE(8, 4, 64)
+    TB_STEP_CASE(8, 2, 64)
+    TB_STEP_CASE(8, 1, 32)
+#undef TB_STEP_CASE
+    return cudaErrorNotSupported;
+}
+
+}  // namespace tb

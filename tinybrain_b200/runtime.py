@@ -522,6 +522,22 @@ class ModelRunner:
         call("tb_runner_read_tokens", self.handle, _ptr(out), _ptr(counts))
         return [out[i, :counts[i]].tolist() for i in range(n_seqs)]
 
+    @property
+    def persistent(self) -> bool:
+        """True when each decode step is one persistent cooperative kernel."""
+        v = C.c_int32(0)
+        call("tb_runner_get_persistent", self.handle, C.byref(v))
+        return bool(v.value)
+
+    @persistent.setter
+    def persistent(self, enable: bool):
+        call("tb_runner_set_persistent", self.handle, int(bool(enable)))
+
+    def debug_read(self, which: int, n: int) -> np.ndarray:
+        out = np.empty(n, dtype=np.float32)
+        call("tb_runner_debug_read", self.handle, which, _ptr(out), n)
+        return out
+
     def io_bytes(self, reset: bool = False):
         a, b = C.c_int64(0), C.c_int64(0)
         call("tb_runner_io_bytes", self.handle, C.byref(a), C.byref(b), int(reset))
