@@ -225,6 +225,12 @@ tb_status tb_runner_get_persistent(const tb_runner *r, int32_t *enabled);
  * 10 attention context, 11 SiLU*up activations (per-op step). */
 tb_status tb_runner_debug_read(tb_runner *r, int32_t which, float *out_host, int64_t n);
 
+/* Diagnostics: run one persistent step recording, per CTA and phase,
+ * out[(cta * phases + phase) * 8 + i]: %globaltimer (ns) at the phase start
+ * (i = 0), its end (1) and the end of its prologue (2); ns spent waiting for
+ * weight tiles (3) and in unit products (4), as seen by consumer thread 0. */
+tb_status tb_runner_trace_step(tb_runner *r, uint64_t *out, int64_t n, int32_t *ctas, int32_t *phases);
+
 /* Called once per generated token (TokenOutput, GenerationConfig.swift:149-219);
  * return nonzero to stop that sequence. */
 typedef int32_t (*tb_token_callback)(void *user, int32_t seq, int32_t index, int32_t token_id);

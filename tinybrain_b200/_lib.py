@@ -104,6 +104,7 @@ SIGNATURES = {
     "tb_runner_set_persistent": [_P, _I32],
     "tb_runner_get_persistent": [_P, _PI32],
     "tb_runner_debug_read": [_P, _I32, _P, _I64],
+    "tb_runner_trace_step": [_P, _P, _I64, _PI32, _PI32],
 }
 _RESTYPES = {
     "tb_abi_version": C.c_int32,

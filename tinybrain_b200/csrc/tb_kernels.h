@@ -215,6 +215,8 @@ struct StepParams {
     unsigned int* bar;                            // grid barrier counter, zero at launch
     int* err;
     int nslots, slot_bytes;
+    int nflight;                // producer copies in flight at most
+    unsigned long long* trace;  // optional [C][phases][8] diagnostics
 };
 
 constexpr int kStepConsumerWarps = 8;

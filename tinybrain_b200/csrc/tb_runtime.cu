@@ -235,7 +235,7 @@ struct tb_runner {
     StepParams sp{};
     int step_grid = 0;
     size_t step_smem = 0;
-    DevBuf step_layers, part_qkv, part_o, part_gu, part_dn, step_attn, hX, hY, step_bar;
+    DevBuf step_layers, part_qkv, part_o, part_gu, part_dn, step_attn, hX, hY, step_bar, step_trace;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     ~tb_runner() {
         if (graph) cudaGraphExecDestroy(graph);
@@ -1148,7 +1148,7 @@ static tb_status build_step(tb_runner* r) {
     tb_model* m = r->m;
     const tb_model_config& c = m->cfg;
     r->persistent_ok = false;
-    if (r->B != 1 || c.architecture != TB_ARCH_LLAMA || c.hidden_dim > 4096) return ok();
+    if (r->B != 1 || c.architecture != TB_ARCH_LLAMA || c.hidden_dim > 4096 || c.intermediate_dim % 4 != 0) return ok();
     const Layer& L0 = m->layers[0];
     const int prec = L0.qkv.L.precision;
     auto same = [](const QLayout& a, const QLayout& b) {
@@ -1238,6 +1238,8 @@ static tb_status build_step(tb_runner* r) {
     p.err = r->ctx->err.as<int>();
     p.nslots = ns;
     p.slot_bytes = sb;
+    p.nflight = std::min(ns, 4);
+    if (const char* e = getenv("TB_STEP_INFLIGHT")) p.nflight = std::max(1, std::min(ns, atoi(e)));
     r->step_smem = smem;
     r->step_grid = C;
     refresh_step_params(r);
@@ -1892,4 +1894,28 @@ extern "C" tb_status tb_runner_debug_read(tb_runner* r, int32_t which, float* ou
     TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
     TB_CUDA(cudaMemcpy(out, b->p, (size_t)n * 4, cudaMemcpyDeviceToHost));
     return ok();
+}
+
+extern "C" tb_status tb_runner_trace_step(tb_runner* r, uint64_t* out, int64_t n, int32_t* ctas, int32_t* phases) {
+    TB_CHECK(r && out && ctas && phases, "NULL argument");
+    TB_CHECK(r->persistent, "tracing needs the persistent step");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    const int nph = 5 * r->m->cfg.num_layers + 1;
+    const size_t cnt = (size_t)r->step_grid * nph * 8;
+    TB_CHECK((size_t)n >= cnt, "need %zu entries", cnt);
+    if (r->step_trace.bytes < cnt * 8) TB_CUDA(r->step_trace.alloc(cnt * 8));
+    tb_status s = kv_prepare(r, 0);
+    if (s != TB_OK) return s;
+    if ((s = flush_ptab(r)) != TB_OK) return s;
+    StepParams p = r->sp;
+    p.trace = r->step_trace.as<unsigned long long>();
+    TB_CUDA(cudaMemsetAsync(r->step_trace.p, 0, cnt * 8, r->ctx->stream));
+    cudaError_t ce = launch_decode_step(p, r->step_grid, r->step_smem, r->ctx->stream);
+    if (ce != cudaSuccess) return cuda_fail(ce, "launch_decode_step");
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    r->kvh[0].pos += 1;
+    TB_CUDA(cudaMemcpy(out, r->step_trace.p, cnt * 8, cudaMemcpyDeviceToHost));
+    *ctas = r->step_grid;
+    *phases = nph;
+    return tb_context_check_device(r->ctx);
 }

@@ -54,6 +54,7 @@ struct Shared {
     uint8_t* ring;
     float* xs;              // activation vector, lane-interleaved per slab
     float* att;             // attention scratch
+    float* hs;              // [2][H] residual stream and norm weights of a prologue
     uint32_t* segmask[4];   // per 32-row block: bit s = a CTA segment starts at slab s (qkv, o, gate/up, down)
 };
 
@@ -97,14 +98,33 @@ __device__ __forceinline__ UnitGeo unit_geo(const QLayout& L, const uint8_t* w, 
 // ------------------------------------------------------------------ producer --
 struct Producer {
     const StepParams& p;
-    Shared& sh;
+    Shared sh;  // by value: the pointers stay in registers, not in local memory
     int it = 0;
     uint64_t pol;
     bool dead = false;
 
-    __device__ Producer(const StepParams& p_, Shared& sh_) : p(p_), sh(sh_) { pol = l2_policy_evict_first(); }
+    __device__ Producer(const StepParams& p_, const Shared& sh_) : p(p_), sh(sh_) { pol = l2_policy_evict_first(); }
+
+    // Keep at most p.nflight copies outstanding: enough to keep HBM busy, few
+    // enough not to inflate the latency of the consumers' activation loads.
+    __device__ bool throttle() {
+        if (it < p.nflight) return true;
+        const int j = it - p.nflight;
+        const int st = j % p.nslots;
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&sh.full[st], (j / p.nslots) & 1)) {
+            if (*sh.abort || global_timer_ns() - t0 > kWaitLimitNs) {
+                if (!*sh.abort) record_error(p.err, kDevWaitTimeout);
+                dead = true;
+                *sh.abort = 1;
+                return false;
+            }
+        }
+        return true;
+    }
 
     __device__ uint8_t* acquire(int& st) {
+        if (!throttle()) return nullptr;
         st = it % p.nslots;
         if (it >= p.nslots) {
             const uint32_t par = ((it / p.nslots) - 1) & 1;
@@ -172,11 +192,31 @@ struct Producer {
 // ------------------------------------------------------------------ consumer --
 struct Consumer {
     const StepParams& p;
-    Shared& sh;
+    Shared sh;  // by value: the pointers stay in registers, not in local memory
     int it = 0;
     int ctid, warp, lane, c, C;
+    int nph = 0;                     // phases per step (trace stride)
+    int cur_phase = 0;
+    unsigned long long waited = 0;   // thread 0: ns waiting for ring slots in this phase
+    unsigned long long dotted = 0;   // thread 0: ns in unit products in this phase
 
-    __device__ Consumer(const StepParams& p_, Shared& sh_) : p(p_), sh(sh_) {
+    // Diagnostics (p.trace != null): per CTA and phase, %globaltimer at the
+    // start (0), end (1), end of the prologue (2); ns waiting for tiles (3) and
+    // in unit products (4).
+    __device__ void trace(int phase, int which) {
+        if (!p.trace || ctid != 0) return;
+        unsigned long long* t = p.trace + ((size_t)c * nph + phase) * 8;
+        t[which] = global_timer_ns();
+        if (which == 0) {
+            waited = dotted = 0;
+            cur_phase = phase;
+        } else if (which == 1) {
+            t[3] = waited;
+            t[4] = dotted;
+        }
+    }
+
+    __device__ Consumer(const StepParams& p_, const Shared& sh_) : p(p_), sh(sh_) {
         ctid = threadIdx.x;
         warp = ctid >> 5;
         lane = ctid & 31;
@@ -205,13 +245,15 @@ struct Consumer {
                 }
             }
             *sh.go = *sh.abort ? 0 : 1;
+            if (phase < nph) trace(phase, 0);
         }
         bar();
         return *sh.go != 0;
     }
-    __device__ void phase_end() {
+    __device__ void phase_end(int phase) {
         bar();
         if (ctid == 0) {
+            trace(phase, 1);
             __threadfence();
             red_release_add(p.bar, 1u);
         }
@@ -220,7 +262,11 @@ struct Consumer {
     __device__ const uint8_t* wait_slot(int& st) {
         st = it % p.nslots;
         if (*sh.abort) return nullptr;
-        if (!mbar_wait(&sh.full[st], (it / p.nslots) & 1, p.err)) {
+        const bool tr = p.trace && ctid == 0;
+        const uint64_t w0 = tr ? global_timer_ns() : 0;
+        const bool okw = mbar_wait(&sh.full[st], (it / p.nslots) & 1, p.err);
+        if (tr) waited += global_timer_ns() - w0;
+        if (!okw) {
             *sh.abort = 1;
             return nullptr;
         }
@@ -236,10 +282,9 @@ struct Consumer {
     // A partial is stored at the slab where its CTA's segment of the row block
     // starts; segments are summed in slab order.  All loads are issued before
     // the first add, so NJ rows cost one L2 round trip, not one per segment.
-    template <int NJ>
+    template <int NJ, int SEGMAX = 4>
     __device__ void reduce_rows(const QLayout& L, const uint32_t* tab, const float* part, const float* sc,
                                 const float* bias, const int (&n)[NJ], const bool (&use)[NJ], float (&out)[NJ]) {
-        constexpr int SEGMAX = 8;
         float v[NJ][SEGMAX];
         uint32_t m0[NJ], rest[NJ];
         float scv[NJ], bv[NJ];
@@ -271,51 +316,124 @@ struct Consumer {
         }
     }
 
+    // Vector form of reduce_rows: NG groups of 4 consecutive GPU rows (same
+    // 32-row block), one float4 load per segment.
+    template <int NG, int SEGMAX = 4>
+    __device__ void reduce4(const QLayout& L, const uint32_t* tab, const float* part, const float* sc,
+                            const float* bias, const int (&n0)[NG], const bool (&use)[NG], float4 (&out)[NG]) {
+        float4 v[NG][SEGMAX];
+        uint32_t m0[NG], rest[NG];
+        float4 scv[NG], bv[NG];
+#pragma unroll
+        for (int j = 0; j < NG; ++j) {
+            uint32_t m = use[j] ? tab[n0[j] >> 5] : 0u;
+            m0[j] = m;
+#pragma unroll
+            for (int g = 0; g < SEGMAX; ++g) {
+                const int sl = __ffs(m) - 1;
+                v[j][g] = sl >= 0 ? __ldcg(reinterpret_cast<const float4*>(part + (size_t)sl * L.Np + n0[j]))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                m &= m - 1;
+            }
+            rest[j] = m;
+            scv[j] = (use[j] && L.precision == 8) ? __ldg(reinterpret_cast<const float4*>(sc + n0[j]))
+                                                   : make_float4(1.f, 1.f, 1.f, 1.f);
+            bv[j] = (use[j] && bias) ? __ldg(reinterpret_cast<const float4*>(bias + n0[j]))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < NG; ++j) {
+            const int cnt = __popc(m0[j]);
+            float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int g = 0; g < SEGMAX; ++g)
+                if (g < cnt) {
+                    t.x += v[j][g].x;
+                    t.y += v[j][g].y;
+                    t.z += v[j][g].z;
+                    t.w += v[j][g].w;
+                }
+            for (uint32_t m = rest[j]; m; m &= m - 1) {
+                const float4 q = __ldcg(reinterpret_cast<const float4*>(part + (size_t)(__ffs(m) - 1) * L.Np + n0[j]));
+                t.x += q.x;
+                t.y += q.y;
+                t.z += q.z;
+                t.w += q.w;
+            }
+            if (L.precision == 8) {
+                t.x = __fmul_rn(t.x, scv[j].x);
+                t.y = __fmul_rn(t.y, scv[j].y);
+                t.z = __fmul_rn(t.z, scv[j].z);
+                t.w = __fmul_rn(t.w, scv[j].w);
+            }
+            if (bias) {
+                t.x = __fadd_rn(t.x, bv[j].x);
+                t.y = __fadd_rn(t.y, bv[j].y);
+                t.z = __fadd_rn(t.z, bv[j].z);
+                t.w = __fadd_rn(t.w, bv[j].w);
+            }
+            out[j] = t;
+        }
+    }
+
     template <int PREC>
     __device__ void put_x(const QLayout& L, int k, float v) {
         constexpr int CH = PREC == 8 ? 16 : 32;
+        constexpr int SK = PREC == 8 ? kSlabBytes : 2 * kSlabBytes;  // == L.slab_k
         if (PREC == 4) v *= int4_pos_scale(k & 7);
-        const int s = k / L.slab_k;
-        sh.xs[s * L.slab_k + xperm<CH>(k - s * L.slab_k)] = v;
+        const int s = k / SK;
+        sh.xs[s * SK + xperm<CH>(k - s * SK)] = v;
     }
 
     // h = src + (reduced partials of the previous phase); optional store of
-    // this CTA's slice of h; x = RMSNorm(h) * w (or h when norm == null).
+    // this CTA's slice of h; x = RMSNorm(h) * w (or h when norm == null).  The
+    // source rows, norm weights and partials are loaded as float4 in one batch
+    // per chunk; h is parked in shared memory (sh.hs) until the norm is known.
     template <int PREC>
     __device__ void residual_norm(const float* src, const QLayout* Lp, const uint32_t* tab, const float* part,
                                   const float* sc, const float* bias, float* store, const float* norm,
                                   const QLayout& Lnext) {
-        const int H = p.H;
-        constexpr int MAXJ = 16;  // H <= 4096
-        float hv[MAXJ];
+        const int H = p.H;  // multiple of 32
+        const int k0 = (int)((long long)c * H / C), k1 = (int)((long long)(c + 1) * H / C);
         float ss = 0.0f;
+        // thread t owns rows 4t..4t+3 of every 1024-row chunk
+        for (int base = 0; base < H; base += 4 * 2 * kConsumers) {
+            int n0[2];
+            bool use[2];
+            float4 add[2], sv[2], nw[2];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            int n[8];
-            bool use[8];
-            float add[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                n[j] = ctid + kConsumers * (half * 8 + j);
-                use[j] = n[j] < H;
-                if (!use[j]) n[j] = 0;
-                add[j] = 0.0f;
+            for (int j = 0; j < 2; ++j) {
+                n0[j] = base + 4 * (ctid + kConsumers * j);
+                use[j] = n0[j] < H;
+                if (!use[j]) n0[j] = 0;
+                sv[j] = use[j] ? __ldcg(reinterpret_cast<const float4*>(src + n0[j])) : make_float4(0.f, 0.f, 0.f, 0.f);
+                nw[j] = (use[j] && norm) ? __ldg(reinterpret_cast<const float4*>(norm + n0[j]))
+                                         : make_float4(1.f, 1.f, 1.f, 1.f);
+                add[j] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            if (Lp) reduce_rows<8>(*Lp, tab, part, sc, bias, n, use, add);
+            if (Lp) reduce4<2>(*Lp, tab, part, sc, bias, n0, use, add);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                float v = use[j] ? __ldcg(src + n[j]) : 0.0f;
-                if (Lp) v = __fadd_rn(v, add[j]);
-                hv[half * 8 + j] = v;
-                ss = fmaf(v, v, ss);
-            }
-        }
-        if (store) {
-            const int k0 = (int)((long long)c * H / C), k1 = (int)((long long)(c + 1) * H / C);
+            for (int j = 0; j < 2; ++j) {
+                if (!use[j]) continue;
+                float4 v = sv[j];
+                if (Lp) {
+                    v.x = __fadd_rn(v.x, add[j].x);
+                    v.y = __fadd_rn(v.y, add[j].y);
+                    v.z = __fadd_rn(v.z, add[j].z);
+                    v.w = __fadd_rn(v.w, add[j].w);
+                }
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
+                *reinterpret_cast<float4*>(sh.hs + n0[j]) = v;
+                *reinterpret_cast<float4*>(sh.hs + H + n0[j]) = nw[j];
+                if (store) {
+                    const float e4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int j = 0; j < MAXJ; ++j) {
-                const int k = ctid + kConsumers * j;
-                if (k >= k0 && k < k1) store[k] = hv[j];
+                    for (int e = 0; e < 4; ++e)
+                        if (n0[j] + e >= k0 && n0[j] + e < k1) store[n0[j] + e] = e4[e];
+                }
             }
         }
         float inv = 1.0f;
@@ -329,10 +447,13 @@ struct Consumer {
             for (int w = 0; w < kStepConsumerWarps; ++w) t += sh.misc[w];
             inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), p.eps)));
         }
+        // each thread re-reads the rows it parked itself: no barrier needed
+        for (int n = 4 * ctid; n < H; n += 4 * kConsumers) {
 #pragma unroll
-        for (int j = 0; j < MAXJ; ++j) {
-            const int k = ctid + kConsumers * j;
-            if (k < H) put_x<PREC>(Lnext, k, norm ? __fmul_rn(__fmul_rn(hv[j], inv), __ldg(norm + k)) : hv[j]);
+            for (int e = 0; e < 4; ++e) {
+                const float v = sh.hs[n + e];
+                put_x<PREC>(Lnext, n + e, norm ? __fmul_rn(__fmul_rn(v, inv), sh.hs[H + n + e]) : v);
+            }
         }
         for (int k = H + ctid; k < Lnext.Kp; k += kConsumers) put_x<PREC>(Lnext, k, 0.0f);
         bar();
@@ -342,6 +463,7 @@ struct Consumer {
     // segment, at the slab where the segment starts.
     template <int PREC>
     __device__ void gemv_units(const QLayout& L, float* part) {
+        trace(cur_phase, 2);
         const int U = (L.Np / 32) * L.slabs;
         const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
         float2 acc[4][1];
@@ -370,7 +492,13 @@ struct Consumer {
             if (!slot) return;
             const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
             const float* ssl = (PREC == 4) ? reinterpret_cast<const float*>(slot + 16384) : nullptr;
+            const uint64_t td = (p.trace && ctid == 0) ? global_timer_ns() : 0;
             unit_dot<PREC, 4, 1>(slot, sb, warp * 4, ssl, sh.xs + s * L.slab_k, 0, lane, acc);
+            if (p.trace && ctid == 0) {
+                volatile float sink = acc[0][0].x;
+                (void)sink;
+                dotted += global_timer_ns() - td;
+            }
             release_slot(st);
         }
         if (cur >= 0) flush(cur, s_first);
@@ -516,22 +644,23 @@ struct Consumer {
         }
     }
 
-    // Slab range of K touched by this CTA's units of a phase.
-    __device__ void slab_span(const QLayout& L, int& kb, int& ke) {
+    // Slabs of K touched by this CTA's units of a phase (bit per slab).
+    __device__ uint32_t slab_set(const QLayout& L) {
         const int U = (L.Np / 32) * L.slabs;
         const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
-        int smin = L.slabs, smax = -1;
-        if (u1 - u0 >= L.slabs) {
-            smin = 0;
-            smax = L.slabs - 1;
-        } else {
-            for (int u = u0; u < u1; ++u) {
-                smin = min(smin, u % L.slabs);
-                smax = max(smax, u % L.slabs);
-            }
-        }
-        kb = smin * L.slab_k;
-        ke = min((smax + 1) * L.slab_k, L.Kp);
+        if (u1 - u0 >= L.slabs) return L.slabs >= 32 ? 0xFFFFFFFFu : ((1u << L.slabs) - 1u);
+        uint32_t m = 0;
+        for (int u = u0; u < u1; ++u) m |= 1u << (u % L.slabs);
+        return m;
+    }
+    // The e-th k of the slabs in `set` (slab-major); -1 past the set, -2 past Kp.
+    __device__ __forceinline__ int kth_in_set(const QLayout& L, uint32_t set, int e) {
+        const int si = e / L.slab_k;
+        uint32_t m = set;
+        for (int i = 0; i < si && m; ++i) m &= m - 1;
+        if (!m) return -1;
+        const int k = (__ffs(m) - 1) * L.slab_k + e % L.slab_k;
+        return k < L.Kp ? k : -2;
     }
 
     // ctx[k] for the slabs this CTA's o_proj units need: combine the attention
@@ -564,9 +693,11 @@ struct Consumer {
             for (int sp = 0; sp < A; ++sp) wts[e * A + sp] *= inv;
         }
         bar();
-        int kb, ke;
-        slab_span(L, kb, ke);
-        for (int k = kb + ctid; k < ke; k += kConsumers) {
+        const uint32_t set = slab_set(L);
+        const int total = __popc(set) * L.slab_k;
+        for (int e = ctid; e < total; e += kConsumers) {
+            const int k = kth_in_set(L, set, e);
+            if (k < 0) continue;
             float v = 0.0f;
             if (k < L.K) {
                 const int hq = k / D, i = k % D;
@@ -585,31 +716,40 @@ struct Consumer {
         bar();
     }
 
-    // act[k] = silu(gate[k]) * up[k] for the slabs this CTA's down units need.
+    // act[k] = silu(gate[k]) * up[k] for the slabs this CTA's down units need;
+    // groups of 4 consecutive k, up to 4 groups per thread per batch of loads.
     template <int PREC>
     __device__ void act_prologue(const StepLayer& ly) {
+        constexpr int NG = 4;
         const QLayout& L = p.Ldn;
         const QLayout& GL = p.Lgu;
-        int kb, ke;
-        slab_span(L, kb, ke);
-        for (int k0 = kb + ctid; k0 < ke; k0 += 4 * kConsumers) {
-            int n[8];
-            bool use[8];
-            float v[8];
+        const uint32_t set = slab_set(L);
+        const int total = __popc(set) * L.slab_k;  // multiple of 4
+        for (int e0 = 0; e0 < total; e0 += 4 * NG * kConsumers) {
+            int n0[2 * NG], kk[NG];
+            bool use[2 * NG];
+            float4 v[2 * NG];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int k = k0 + kConsumers * j;
-                const bool ok = k < ke && k < L.K;
+            for (int j = 0; j < NG; ++j) {
+                const int e = e0 + 4 * (ctid + kConsumers * j);
+                const int k = e < total ? kth_in_set(L, set, e) : -1;
+                kk[j] = k;
+                const bool ok = k >= 0 && k < L.K;  // K % 4 == 0
                 const int grow = ok ? (k / 32) * 64 + (k % 32) : 0;
-                n[2 * j] = grow;
-                n[2 * j + 1] = grow + 32;
+                n0[2 * j] = grow;
+                n0[2 * j + 1] = grow + 32;
                 use[2 * j] = use[2 * j + 1] = ok;
             }
-            reduce_rows<8>(GL, sh.segmask[2], p.part_gu, ly.gu_s, ly.gu_b, n, use, v);
+            reduce4<2 * NG, 2>(GL, sh.segmask[2], p.part_gu, ly.gu_s, ly.gu_b, n0, use, v);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int k = k0 + kConsumers * j;
-                if (k < ke) put_x<PREC>(L, k, use[2 * j] ? __fmul_rn(silu_ref(v[2 * j]), v[2 * j + 1]) : 0.0f);
+            for (int j = 0; j < NG; ++j) {
+                if (kk[j] < 0) continue;
+                const float4 g = v[2 * j], u = v[2 * j + 1];
+                const bool ok = use[2 * j];
+                put_x<PREC>(L, kk[j] + 0, ok ? __fmul_rn(silu_ref(g.x), u.x) : 0.0f);
+                put_x<PREC>(L, kk[j] + 1, ok ? __fmul_rn(silu_ref(g.y), u.y) : 0.0f);
+                put_x<PREC>(L, kk[j] + 2, ok ? __fmul_rn(silu_ref(g.z), u.z) : 0.0f);
+                put_x<PREC>(L, kk[j] + 3, ok ? __fmul_rn(silu_ref(g.w), u.w) : 0.0f);
             }
         }
         bar();
@@ -675,8 +815,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                                 max(p.Lgu.slabs * p.Lgu.slab_k, p.Ldn.slabs * p.Ldn.slab_k)),
                             p.Llm.slabs * p.Llm.slab_k);
     sh.att = sh.xs + xfloats;
+    sh.hs = sh.att + att_floats(G, D, p.Hkv, p.A);
     {
-        uint32_t* t = reinterpret_cast<uint32_t*>(sh.att + att_floats(G, D, p.Hkv, p.A));
+        uint32_t* t = reinterpret_cast<uint32_t*>(sh.hs + 2 * p.H);
         const QLayout* Ls[4] = {&p.Lqkv, &p.Lo, &p.Lgu, &p.Ldn};
         for (int i = 0; i < 4; ++i) {
             sh.segmask[i] = t;
@@ -737,6 +878,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     }
 
     Consumer cs(p, sh);
+    cs.nph = 5 * p.num_layers + 1;
     {
         // Where the CTA segments of each 32-row block start (bit per slab).
         const QLayout* Ls[4] = {&p.Lqkv, &p.Lo, &p.Lgu, &p.Ldn};
@@ -770,26 +912,26 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                                    p.Lqkv);
         }
         cs.gemv_units<PREC>(p.Lqkv, p.part_qkv);
-        cs.phase_end();
+        cs.phase_end(phase - 1);
         // ---- attention over the paged cache (+ RoPE, KV append) ----
         if (!cs.phase_begin(phase++)) return;
         cs.attention<G, D>(l, pos, npages);
-        cs.phase_end();
+        cs.phase_end(phase - 1);
         // ---- o_proj ----
         if (!cs.phase_begin(phase++)) return;
         cs.ctx_prologue<PREC, G, D>();
         cs.gemv_units<PREC>(p.Lo, p.part_o);
-        cs.phase_end();
+        cs.phase_end(phase - 1);
         // ---- gate/up: h_mid = h_in + o; x = RMSNorm(h_mid) ----
         if (!cs.phase_begin(phase++)) return;
         cs.residual_norm<PREC>(p.hX, &p.Lo, sh.segmask[1], p.part_o, ly.o_s, ly.o_b, p.hY, ly.post_norm, p.Lgu);
         cs.gemv_units<PREC>(p.Lgu, p.part_gu);
-        cs.phase_end();
+        cs.phase_end(phase - 1);
         // ---- down ----
         if (!cs.phase_begin(phase++)) return;
         cs.act_prologue<PREC>(ly);
         cs.gemv_units<PREC>(p.Ldn, p.part_dn);
-        cs.phase_end();
+        cs.phase_end(phase - 1);
     }
     // ---- final norm + LM head + argmax ----
     if (!cs.phase_begin(phase++)) return;
@@ -799,7 +941,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                                p.Llm);
     }
     cs.lm_head<PREC>(&p.seq->best);
-    cs.phase_end();
+    cs.phase_end(phase - 1);
     // ---- CTA 0 advances the step once every CTA folded its argmax ----
     if (c == 0 && cs.phase_begin(phase)) {
         if (threadIdx.x == 0) {
@@ -852,10 +994,11 @@ size_t step_smem_bytes(const StepParams& p, int* nslots, int* slot_bytes, int ma
         if (L->slabs > 32) return 0;  // segment masks are 32-bit
         tabs += (size_t)(L->Np / 32 + 3) / 4 * 4 * 4;
     }
-    const size_t fixed = kBarRegion + kMiscFloats * 4 + (size_t)xfloats * 4 + att + tabs;
+    const size_t fixed = kBarRegion + kMiscFloats * 4 + (size_t)xfloats * 4 + att + (size_t)2 * p.H * 4 + tabs;
     if ((size_t)max_smem <= fixed + 2 * (size_t)sbytes) return 0;
     int ns = (int)((max_smem - fixed) / sbytes);
     ns = std::min(ns, kMaxSlots);
+    ns = std::min(ns, 10);  // leave L1 room for the few register spills
     *nslots = ns;
     *slot_bytes = sbytes;
     return fixed + (size_t)ns * sbytes;
