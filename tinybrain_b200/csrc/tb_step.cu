@@ -43,6 +43,7 @@ constexpr int kMaxSlots = 24;
 constexpr int kBarRegion = 1024;  // mbarriers + flags
 constexpr int kMiscFloats = 1024;
 constexpr int kConsumers = kStepConsumerWarps * 32;
+constexpr int kRowBlocksCached = 16;  // per-warp scale/bias cache of a GEMV phase (row blocks)
 
 struct Shared {
     uint64_t* full;
@@ -55,6 +56,7 @@ struct Shared {
     float* xs;              // activation vector, lane-interleaved per slab
     float* att;             // attention scratch
     float* hs;              // [2][H] residual stream and norm weights of a prologue
+    float* rows;            // [warp][kRowBlocksCached][8]: INT8 scales (4) and biases (4) of the warp's rows
     uint32_t* segmask[4];   // per 32-row block: bit s = a CTA segment starts at slab s (qkv, o, gate/up, down)
 };
 
@@ -66,6 +68,11 @@ __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
 __device__ __forceinline__ void red_release_add(unsigned int* p, unsigned int v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// 4-byte asynchronous copy global -> shared (does not stall the issuing warp).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // The CTA whose static unit range [c*U/C, (c+1)*U/C) contains unit u.
 __device__ __forceinline__ int owner_of(int u, int U, int C) { return (int)(((long long)u * C + C - 1) / U); }
@@ -113,6 +120,7 @@ struct Producer {
         const int st = j % p.nslots;
         const uint64_t t0 = global_timer_ns();
         while (!mbar_try_wait(&sh.full[st], (j / p.nslots) & 1)) {
+            __nanosleep(64);
             if (*sh.abort || global_timer_ns() - t0 > kWaitLimitNs) {
                 if (!*sh.abort) record_error(p.err, kDevWaitTimeout);
                 dead = true;
@@ -130,6 +138,7 @@ struct Producer {
             const uint32_t par = ((it / p.nslots) - 1) & 1;
             const uint64_t t0 = global_timer_ns();
             while (!mbar_try_wait(&sh.empty[st], par)) {
+                __nanosleep(64);
                 if (*sh.abort || global_timer_ns() - t0 > kWaitLimitNs) {
                     if (!*sh.abort) record_error(p.err, kDevWaitTimeout);
                     dead = true;
@@ -202,7 +211,8 @@ struct Consumer {
 
     // Diagnostics (p.trace != null): per CTA and phase, %globaltimer at the
     // start (0), end (1), end of the prologue (2); ns waiting for tiles (3) and
-    // in unit products (4).
+    // in unit products (4); the prologue's loads landed (5), the last unit
+    // product done (6), the phase-end barrier entered (7).
     __device__ void trace(int phase, int which) {
         if (!p.trace || ctid != 0) return;
         unsigned long long* t = p.trace + ((size_t)c * nph + phase) * 8;
@@ -216,6 +226,10 @@ struct Consumer {
         }
     }
 
+    __device__ __forceinline__ void mark(int which) {
+        if (p.trace && ctid == 0) p.trace[((size_t)c * nph + cur_phase) * 8 + which] = global_timer_ns();
+    }
+
     __device__ Consumer(const StepParams& p_, const Shared& sh_) : p(p_), sh(sh_) {
         ctid = threadIdx.x;
         warp = ctid >> 5;
@@ -226,9 +240,12 @@ struct Consumer {
 
     __device__ void bar() { named_bar_sync(1, kConsumers); }
 
-    // Grid barrier: wait until every CTA finished phase (phase - 1).  The
-    // go/stop decision is taken by thread 0 and published through sh.go before
-    // the barrier, so every consumer warp takes the same branch.
+    // Grid barrier: wait until every CTA finished phase (phase - 1).  Arrival
+    // is one release-add on a counter, the wait an acquire poll by thread 0
+    // (measured cheaper on this part than per-CTA flags polled by a warp,
+    // whose loads crowd the L2 slices holding the flags).  The go/stop
+    // decision is published through sh.go before the CTA barrier, so every
+    // consumer warp takes the same branch.
     __device__ bool phase_begin(int phase) {
         if (ctid == 0) {
             if (phase > 0 && !*sh.abort) {
@@ -251,12 +268,30 @@ struct Consumer {
         return *sh.go != 0;
     }
     __device__ void phase_end(int phase) {
+        mark(7);
         bar();
         if (ctid == 0) {
             trace(phase, 1);
-            __threadfence();
-            red_release_add(p.bar, 1u);
+            red_release_add(p.bar, 1u);  // release: orders the CTA's writes (bar.sync above) before the arrival
         }
+    }
+
+    // Issue asynchronous copies of the INT8 scales and the biases of this
+    // warp's rows of every row block in the CTA's range of a GEMV phase; the
+    // first flush of the phase waits for them.
+    __device__ void prefetch_rows(const QLayout& L, const float* sc, const float* bias) {
+        const int U = (L.Np / 32) * L.slabs;
+        const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
+        if (u1 <= u0) return;
+        const int rb0 = u0 / L.slabs, nrb = min((u1 - 1) / L.slabs - rb0 + 1, kRowBlocksCached);
+        float* rs = sh.rows + warp * kRowBlocksCached * 8;
+        for (int e = lane; e < nrb * 8; e += 32) {
+            const int i = e >> 3, q = e & 7;
+            const int row = (rb0 + i) * 32 + warp * 4 + (q & 3);
+            const float* src = q < 4 ? (L.precision == 8 ? sc : nullptr) : bias;
+            if (src) cp_async4(rs + e, src + row);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
     }
 
     __device__ const uint8_t* wait_slot(int& st) {
@@ -278,16 +313,16 @@ struct Consumer {
         ++it;
     }
 
-    // Sums of the split-K partials of NJ GPU rows of a phase, scaled and biased.
-    // A partial is stored at the slab where its CTA's segment of the row block
-    // starts; segments are summed in slab order.  All loads are issued before
+    // Sums of the split-K partials of NJ GPU rows of a phase.  A partial is
+    // stored (already scaled; the slab-0 segment carries the bias) at the slab
+    // where its CTA's segment of the row block starts; segments are summed in
+    // slab order.  All loads are issued before
     // the first add, so NJ rows cost one L2 round trip, not one per segment.
     template <int NJ, int SEGMAX = 4>
-    __device__ void reduce_rows(const QLayout& L, const uint32_t* tab, const float* part, const float* sc,
-                                const float* bias, const int (&n)[NJ], const bool (&use)[NJ], float (&out)[NJ]) {
+    __device__ void reduce_rows(const QLayout& L, const uint32_t* tab, const float* part, const int (&n)[NJ],
+                                const bool (&use)[NJ], float (&out)[NJ]) {
         float v[NJ][SEGMAX];
         uint32_t m0[NJ], rest[NJ];
-        float scv[NJ], bv[NJ];
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
             uint32_t m = use[j] ? tab[n[j] >> 5] : 0u;
@@ -299,8 +334,6 @@ struct Consumer {
                 m &= m - 1;
             }
             rest[j] = m;
-            scv[j] = (use[j] && L.precision == 8) ? __ldg(sc + n[j]) : 1.0f;
-            bv[j] = (use[j] && bias) ? __ldg(bias + n[j]) : 0.0f;
         }
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
@@ -310,20 +343,17 @@ struct Consumer {
             for (int g = 0; g < SEGMAX; ++g)
                 if (g < cnt) t += v[j][g];
             for (uint32_t m = rest[j]; m; m &= m - 1) t += __ldcg(part + (size_t)(__ffs(m) - 1) * L.Np + n[j]);
-            float r = (L.precision == 8) ? __fmul_rn(t, scv[j]) : t;
-            if (bias) r = __fadd_rn(r, bv[j]);
-            out[j] = r;
+            out[j] = t;
         }
     }
 
     // Vector form of reduce_rows: NG groups of 4 consecutive GPU rows (same
     // 32-row block), one float4 load per segment.
     template <int NG, int SEGMAX = 4>
-    __device__ void reduce4(const QLayout& L, const uint32_t* tab, const float* part, const float* sc,
-                            const float* bias, const int (&n0)[NG], const bool (&use)[NG], float4 (&out)[NG]) {
+    __device__ void reduce4(const QLayout& L, const uint32_t* tab, const float* part, const int (&n0)[NG],
+                            const bool (&use)[NG], float4 (&out)[NG]) {
         float4 v[NG][SEGMAX];
         uint32_t m0[NG], rest[NG];
-        float4 scv[NG], bv[NG];
 #pragma unroll
         for (int j = 0; j < NG; ++j) {
             uint32_t m = use[j] ? tab[n0[j] >> 5] : 0u;
@@ -336,10 +366,6 @@ struct Consumer {
                 m &= m - 1;
             }
             rest[j] = m;
-            scv[j] = (use[j] && L.precision == 8) ? __ldg(reinterpret_cast<const float4*>(sc + n0[j]))
-                                                   : make_float4(1.f, 1.f, 1.f, 1.f);
-            bv[j] = (use[j] && bias) ? __ldg(reinterpret_cast<const float4*>(bias + n0[j]))
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int j = 0; j < NG; ++j) {
@@ -360,18 +386,6 @@ struct Consumer {
                 t.z += q.z;
                 t.w += q.w;
             }
-            if (L.precision == 8) {
-                t.x = __fmul_rn(t.x, scv[j].x);
-                t.y = __fmul_rn(t.y, scv[j].y);
-                t.z = __fmul_rn(t.z, scv[j].z);
-                t.w = __fmul_rn(t.w, scv[j].w);
-            }
-            if (bias) {
-                t.x = __fadd_rn(t.x, bv[j].x);
-                t.y = __fadd_rn(t.y, bv[j].y);
-                t.z = __fadd_rn(t.z, bv[j].z);
-                t.w = __fadd_rn(t.w, bv[j].w);
-            }
             out[j] = t;
         }
     }
@@ -391,8 +405,7 @@ struct Consumer {
     // per chunk; h is parked in shared memory (sh.hs) until the norm is known.
     template <int PREC>
     __device__ void residual_norm(const float* src, const QLayout* Lp, const uint32_t* tab, const float* part,
-                                  const float* sc, const float* bias, float* store, const float* norm,
-                                  const QLayout& Lnext) {
+                                  float* store, const float* norm, const QLayout& Lnext) {
         const int H = p.H;  // multiple of 32
         const int k0 = (int)((long long)c * H / C), k1 = (int)((long long)(c + 1) * H / C);
         float ss = 0.0f;
@@ -411,7 +424,7 @@ struct Consumer {
                                          : make_float4(1.f, 1.f, 1.f, 1.f);
                 add[j] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            if (Lp) reduce4<2>(*Lp, tab, part, sc, bias, n0, use, add);
+            if (Lp) reduce4<2>(*Lp, tab, part, n0, use, add);
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 if (!use[j]) continue;
@@ -435,6 +448,11 @@ struct Consumer {
                         if (n0[j] + e >= k0 && n0[j] + e < k1) store[n0[j] + e] = e4[e];
                 }
             }
+        }
+        if (p.trace && ctid == 0) {
+            volatile float sink = ss;
+            (void)sink;
+            mark(5);
         }
         float inv = 1.0f;
         if (norm) {
@@ -462,19 +480,38 @@ struct Consumer {
     // Multiply this CTA's units of a GEMV phase; write one partial per row and
     // segment, at the slab where the segment starts.
     template <int PREC>
-    __device__ void gemv_units(const QLayout& L, float* part) {
+    __device__ void gemv_units(const QLayout& L, float* part, const float* sc, const float* bias) {
         trace(cur_phase, 2);
+        prefetch_rows(L, sc, bias);
         const int U = (L.Np / 32) * L.slabs;
         const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
         float2 acc[4][1];
         int cur = -1, s_first = 0;
+        // The per-row INT8 scale is applied to each partial; the segment that
+        // starts at slab 0 also carries the bias, so readers only add.  Scales
+        // and biases come from the warp's prefetched row cache.
+        const int rb0 = u0 / L.slabs;
+        const float* rs = sh.rows + warp * kRowBlocksCached * 8;
+        bool cached = false;
         auto flush = [&](int rb32, int slab) {
+            const int i = rb32 - rb0;
+            if (!cached) {
+                cp_async_wait_all();
+                __syncwarp();
+                cached = true;
+            }
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 float v = acc[r][0].x + acc[r][0].y;
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == r) part[(size_t)slab * L.Np + rb32 * 32 + warp * 4 + r] = v;
+                const int n = rb32 * 32 + warp * 4 + r;
+                if (lane == r) {
+                    const bool hit = i < kRowBlocksCached;
+                    if (L.precision == 8) v = __fmul_rn(v, hit ? rs[i * 8 + r] : __ldg(sc + n));
+                    if (bias && slab == 0) v = __fadd_rn(v, hit ? rs[i * 8 + 4 + r] : __ldg(bias + n));
+                    part[(size_t)slab * L.Np + n] = v;
+                }
                 acc[r][0] = make_float2(0.f, 0.f);
             }
         };
@@ -501,6 +538,7 @@ struct Consumer {
             }
             release_slot(st);
         }
+        mark(6);
         if (cur >= 0) flush(cur, s_first);
     }
 
@@ -528,7 +566,7 @@ struct Consumer {
             int n[2] = {head * G * D + 2 * e, head * G * D + 2 * e + 1};
             bool use[2] = {true, true};
             float v[2];
-            reduce_rows<2>(L, sh.segmask[0], p.part_qkv, ly.qkv_s, ly.qkv_b, n, use, v);
+            reduce_rows<2>(L, sh.segmask[0], p.part_qkv, n, use, v);
             const float2 cs = rope[(2 * e % D) / 2];
             qs[2 * e] = __fsub_rn(__fmul_rn(v[0], cs.x), __fmul_rn(v[1], cs.y));
             qs[2 * e + 1] = __fadd_rn(__fmul_rn(v[0], cs.y), __fmul_rn(v[1], cs.x));
@@ -541,7 +579,7 @@ struct Consumer {
                 int n[4] = {nk, nk + 1, nv, nv + 1};
                 bool use[4] = {true, true, true, true};
                 float v[4];
-                reduce_rows<4>(L, sh.segmask[0], p.part_qkv, ly.qkv_s, ly.qkv_b, n, use, v);
+                reduce_rows<4>(L, sh.segmask[0], p.part_qkv, n, use, v);
                 const float2 cs = rope[e];
                 const float r0 = __fsub_rn(__fmul_rn(v[0], cs.x), __fmul_rn(v[1], cs.y));
                 const float r1 = __fadd_rn(__fmul_rn(v[0], cs.y), __fmul_rn(v[1], cs.x));
@@ -664,7 +702,10 @@ struct Consumer {
     }
 
     // ctx[k] for the slabs this CTA's o_proj units need: combine the attention
-    // splits in split order (softmax rescaling of (m, l, acc) partials).
+    // splits in split order (softmax rescaling of (m, l, acc) partials).  Each
+    // thread owns groups of 4 consecutive k; the acc loads of its first group
+    // are issued together with the (m, l) loads, so the common case costs one
+    // round trip.
     template <int PREC, int G, int D>
     __device__ void ctx_prologue() {
         constexpr int AMAX = 16;
@@ -672,6 +713,42 @@ struct Consumer {
         const int A = p.A;
         float2* ml = reinterpret_cast<float2*>(sh.misc);  // [Hkv][A][G] (m, l)
         float* wts = sh.att;                              // [Hkv][G][A]
+        const uint32_t set = slab_set(L);
+        const int total = __popc(set) * L.slab_k;  // multiple of 4
+        auto group_loads = [&](int e, int& k, float4 (&a)[AMAX]) {
+            k = e < total ? kth_in_set(L, set, e) : -1;
+            const bool ok = k >= 0 && k < L.K;
+            const int hq = ok ? k / D : 0, i = ok ? k % D : 0;
+            const int hk = hq / G, g = hq % G;
+#pragma unroll
+            for (int sp = 0; sp < AMAX; ++sp)
+                a[sp] = (ok && sp < A) ? __ldcg(reinterpret_cast<const float4*>(
+                                             p.attn_part + (((size_t)hk * A + sp) * G + g) * (D + 4) + i))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        };
+        auto group_put = [&](int k, const float4 (&a)[AMAX]) {
+            if (k < 0) return;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k < L.K) {
+                const int hq = k / D;
+                const float* w = wts + ((hq / G) * G + hq % G) * A;
+#pragma unroll
+                for (int sp = 0; sp < AMAX; ++sp)
+                    if (sp < A) {
+                        v.x = fmaf(w[sp], a[sp].x, v.x);
+                        v.y = fmaf(w[sp], a[sp].y, v.y);
+                        v.z = fmaf(w[sp], a[sp].z, v.z);
+                        v.w = fmaf(w[sp], a[sp].w, v.w);
+                    }
+            }
+            put_x<PREC>(L, k + 0, v.x);
+            put_x<PREC>(L, k + 1, v.y);
+            put_x<PREC>(L, k + 2, v.z);
+            put_x<PREC>(L, k + 3, v.w);
+        };
+        int k0;
+        float4 a0[AMAX];
+        group_loads(4 * ctid, k0, a0);
         const int nml = p.Hkv * A * G;
         for (int e = ctid; e < nml; e += kConsumers) {
             const float* q = p.attn_part + (size_t)e * (D + 4) + D;
@@ -693,25 +770,13 @@ struct Consumer {
             for (int sp = 0; sp < A; ++sp) wts[e * A + sp] *= inv;
         }
         bar();
-        const uint32_t set = slab_set(L);
-        const int total = __popc(set) * L.slab_k;
-        for (int e = ctid; e < total; e += kConsumers) {
-            const int k = kth_in_set(L, set, e);
-            if (k < 0) continue;
-            float v = 0.0f;
-            if (k < L.K) {
-                const int hq = k / D, i = k % D;
-                const int hk = hq / G, g = hq % G;
-                const float* w = wts + (hk * G + g) * A;
-                float a[AMAX];
-#pragma unroll
-                for (int sp = 0; sp < AMAX; ++sp)
-                    a[sp] = sp < A ? __ldcg(p.attn_part + (((size_t)hk * A + sp) * G + g) * (D + 4) + i) : 0.0f;
-#pragma unroll
-                for (int sp = 0; sp < AMAX; ++sp)
-                    if (sp < A) v = fmaf(w[sp], a[sp], v);
-            }
-            put_x<PREC>(L, k, v);
+        mark(5);
+        group_put(k0, a0);
+        for (int e = 4 * (ctid + kConsumers); e < total; e += 4 * kConsumers) {
+            int k;
+            float4 a[AMAX];
+            group_loads(e, k, a);
+            group_put(k, a);
         }
         bar();
     }
@@ -740,7 +805,12 @@ struct Consumer {
                 n0[2 * j + 1] = grow + 32;
                 use[2 * j] = use[2 * j + 1] = ok;
             }
-            reduce4<2 * NG, 2>(GL, sh.segmask[2], p.part_gu, ly.gu_s, ly.gu_b, n0, use, v);
+            reduce4<2 * NG, 2>(GL, sh.segmask[2], p.part_gu, n0, use, v);
+            if (e0 == 0 && p.trace && ctid == 0) {
+                volatile float sink = v[0].x;
+                (void)sink;
+                mark(5);
+            }
 #pragma unroll
             for (int j = 0; j < NG; ++j) {
                 if (kk[j] < 0) continue;
@@ -823,6 +893,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             sh.segmask[i] = t;
             t += (Ls[i]->Np / 32 + 3) / 4 * 4;
         }
+        sh.rows = reinterpret_cast<float*>(t);
     }
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -904,14 +975,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 if (threadIdx.x == 0) record_error(p.err, kDevBadToken);
                 tok = 0;
             }
-            cs.residual_norm<PREC>(p.emb + (size_t)tok * p.H, nullptr, nullptr, nullptr, nullptr, nullptr, p.hX,
-                                   ly.in_norm, p.Lqkv);
+            cs.residual_norm<PREC>(p.emb + (size_t)tok * p.H, nullptr, nullptr, nullptr, p.hX, ly.in_norm, p.Lqkv);
         } else {
             const StepLayer& pl = p.layers[l - 1];
-            cs.residual_norm<PREC>(p.hY, &p.Ldn, sh.segmask[3], p.part_dn, pl.dn_s, pl.dn_b, p.hX, ly.in_norm,
-                                   p.Lqkv);
+            cs.residual_norm<PREC>(p.hY, &p.Ldn, sh.segmask[3], p.part_dn, p.hX, ly.in_norm, p.Lqkv);
         }
-        cs.gemv_units<PREC>(p.Lqkv, p.part_qkv);
+        cs.gemv_units<PREC>(p.Lqkv, p.part_qkv, ly.qkv_s, ly.qkv_b);
         cs.phase_end(phase - 1);
         // ---- attention over the paged cache (+ RoPE, KV append) ----
         if (!cs.phase_begin(phase++)) return;
@@ -920,25 +989,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         // ---- o_proj ----
         if (!cs.phase_begin(phase++)) return;
         cs.ctx_prologue<PREC, G, D>();
-        cs.gemv_units<PREC>(p.Lo, p.part_o);
+        cs.gemv_units<PREC>(p.Lo, p.part_o, ly.o_s, ly.o_b);
         cs.phase_end(phase - 1);
         // ---- gate/up: h_mid = h_in + o; x = RMSNorm(h_mid) ----
         if (!cs.phase_begin(phase++)) return;
-        cs.residual_norm<PREC>(p.hX, &p.Lo, sh.segmask[1], p.part_o, ly.o_s, ly.o_b, p.hY, ly.post_norm, p.Lgu);
-        cs.gemv_units<PREC>(p.Lgu, p.part_gu);
+        cs.residual_norm<PREC>(p.hX, &p.Lo, sh.segmask[1], p.part_o, p.hY, ly.post_norm, p.Lgu);
+        cs.gemv_units<PREC>(p.Lgu, p.part_gu, ly.gu_s, ly.gu_b);
         cs.phase_end(phase - 1);
         // ---- down ----
         if (!cs.phase_begin(phase++)) return;
         cs.act_prologue<PREC>(ly);
-        cs.gemv_units<PREC>(p.Ldn, p.part_dn);
+        cs.gemv_units<PREC>(p.Ldn, p.part_dn, ly.dn_s, ly.dn_b);
         cs.phase_end(phase - 1);
     }
     // ---- final norm + LM head + argmax ----
     if (!cs.phase_begin(phase++)) return;
     {
         const StepLayer& pl = p.layers[p.num_layers - 1];
-        cs.residual_norm<PREC>(p.hY, &p.Ldn, sh.segmask[3], p.part_dn, pl.dn_s, pl.dn_b, nullptr, p.final_norm,
-                               p.Llm);
+        cs.residual_norm<PREC>(p.hY, &p.Ldn, sh.segmask[3], p.part_dn, nullptr, p.final_norm, p.Llm);
     }
     cs.lm_head<PREC>(&p.seq->best);
     cs.phase_end(phase - 1);
@@ -994,7 +1062,9 @@ size_t step_smem_bytes(const StepParams& p, int* nslots, int* slot_bytes, int ma
         if (L->slabs > 32) return 0;  // segment masks are 32-bit
         tabs += (size_t)(L->Np / 32 + 3) / 4 * 4 * 4;
     }
-    const size_t fixed = kBarRegion + kMiscFloats * 4 + (size_t)xfloats * 4 + att + (size_t)2 * p.H * 4 + tabs;
+    const size_t rows = (size_t)kStepConsumerWarps * kRowBlocksCached * 8 * 4;
+    const size_t fixed =
+        kBarRegion + kMiscFloats * 4 + (size_t)xfloats * 4 + att + (size_t)2 * p.H * 4 + tabs + rows;
     if ((size_t)max_smem <= fixed + 2 * (size_t)sbytes) return 0;
     int ns = (int)((max_smem - fixed) / sbytes);
     ns = std::min(ns, kMaxSlots);
