@@ -22,6 +22,7 @@
 //    LM-head argmax: Sampler.swift:126-138).
 #include "tb_common.cuh"
 #include "tb_kernels.h"
+#include "tb_tc.cuh"
 #include "tb_unit.cuh"
 
 #include <cstdio>
@@ -32,13 +33,23 @@ QLayout make_qlayout(int precision, int K, int N, int RB) {
     QLayout L{};
     L.precision = precision;
     L.K = K;
-    L.Kp = (K + 31) / 32 * 32;
     L.N = N;
-    L.RB = RB;
-    L.Np = (N + RB - 1) / RB * RB;
-    L.row_bytes = precision == 8 ? L.Kp : L.Kp / 2;
-    L.slab_k = precision == 8 ? kSlabBytes : 2 * kSlabBytes;
-    L.slabs = (L.row_bytes + kSlabBytes - 1) / kSlabBytes;
+    L.fused_gu = RB == 64 ? 1 : 0;
+    if (precision == 8) {
+        L.Kp = (K + kTcUnitK - 1) / kTcUnitK * kTcUnitK;
+        L.RB = kTcTileRows;
+        L.slab_k = kTcUnitK;
+        L.slab_bytes = kTcUnitK;
+        L.row_bytes = L.Kp;
+    } else {
+        L.Kp = (K + 31) / 32 * 32;
+        L.RB = RB;
+        L.slab_k = 2 * kSlabBytes;
+        L.slab_bytes = kSlabBytes;
+        L.row_bytes = L.Kp / 2;
+    }
+    L.Np = (N + L.RB - 1) / L.RB * L.RB;
+    L.slabs = (L.row_bytes + L.slab_bytes - 1) / L.slab_bytes;
     L.weight_bytes = (size_t)L.Np * L.row_bytes;
     L.scale_floats = precision == 8 ? (size_t)L.Np : (size_t)(L.Np / 32) * L.slabs * 1024;
     return L;
@@ -48,13 +59,15 @@ namespace {
 
 template <int PREC, int RB>
 struct GemvCfg {
-    static constexpr int RPW = RB / kGemvConsumerWarps;               // rows per warp
-    static constexpr int kWeightStage = RB * kSlabBytes;               // bytes
+    static constexpr int RPW = RB / kGemvConsumerWarps;               // rows per warp (INT4)
+    static constexpr int kWeightStage = PREC == 8 ? kTcUnitBytes : RB * kSlabBytes;  // bytes
     static constexpr int kScaleStage = PREC == 4 ? (RB / 32) * 1024 * 4 : 0;
     static constexpr int kStageBytes = kWeightStage + kScaleStage;
-    static constexpr int kStages = (kStageBytes <= 20480) ? 4 : (kStageBytes <= 32768 ? 3 : 2);
-    static constexpr int kCH = PREC == 8 ? 16 : 32;                    // k values per lane per slab
+    static constexpr int kStages = PREC == 8 ? 6 : (kStageBytes <= 20480) ? 4 : (kStageBytes <= 32768 ? 3 : 2);
+    static constexpr int kCH = 32;                                     // INT4 k values per lane per slab
 };
+// Digit rows of the INT8 B operand for MB batch rows (4 digits each; N >= 8, 16-multiples past 8).
+__host__ __device__ constexpr int tc_nb(int mb) { return mb <= 2 ? 8 : (4 * mb + 15) / 16 * 16; }
 
 __device__ __forceinline__ float silu_ref(float x) {
     // Tensor.swift:1135-1142: x / (1 + exp(-x))
@@ -74,14 +87,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     constexpr int STAGES = Cfg::kStages;
     constexpr int RPW = Cfg::RPW;
     constexpr int CH = Cfg::kCH;
+    constexpr int NB = tc_nb(MB);
 
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + STAGES;
-    float* red = reinterpret_cast<float*>(smem + 128);                  // [RB][MB]
-    float* misc = red + RB * MB;                                          // [64]
-    uint8_t* stage_base = smem + 128 + ((RB * MB + 64) * 4 + 127) / 128 * 128;
-    float* xs = reinterpret_cast<float*>(stage_base + STAGES * Cfg::kStageBytes);
+    uint64_t* done = empty + STAGES;                                      // INT8: accumulator complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    float* red = reinterpret_cast<float*>(smem + 256);                    // [RB][MB]
+    float* misc = red + RB * MB;                                          // [2][MB][8]
+    uint8_t* stage_base = smem + (256 + (RB * MB + 16 * MB) * 4 + 1023) / 1024 * 1024;
+    uint8_t* xbuf = stage_base + STAGES * Cfg::kStageBytes;
+    float* xs = reinterpret_cast<float*>(xbuf);   // INT4: lane-interleaved fp32 activations
+    uint8_t* xd = xbuf;                           // INT8: digit operand [k/16][NB][16]
 
     const QLayout& L = p.L;
     const int P = p.P;
@@ -95,11 +113,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kGemvConsumerWarps);
+            mbar_init(&empty[i], PREC == 8 ? 1 : kGemvConsumerWarps);  // INT8: released by tcgen05.commit
         }
+        mbar_init(done, 1);
         fence_barrier_init();
     }
+    if (PREC == 8 && warp == 0) tmem_alloc(tmem_slot, 32);
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
     pdl_launch_dependents();
 
     if (warp == kGemvConsumerWarps) {
@@ -114,15 +136,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                     if (!mbar_wait(&empty[st], ((i / STAGES) - 1) & 1, p.err)) break;
                 }
                 const int s = s0 + i;
-                const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-                const uint32_t wbytes = (uint32_t)(RB * sb);
-                const uint32_t sbytes = (PREC == 4) ? (uint32_t)Cfg::kScaleStage : 0u;
                 uint8_t* dst = stage_base + st * Cfg::kStageBytes;
-                mbar_arrive_expect_tx(&full[st], wbytes + sbytes);
-                bulk_g2s_stream(dst, wrb + (size_t)s * RB * kSlabBytes, wbytes, &full[st], pol);
-                if (PREC == 4)
+                if (PREC == 8) {
+                    mbar_arrive_expect_tx(&full[st], kTcUnitBytes);
+                    bulk_g2s_stream(dst, wrb + (size_t)s * kTcUnitBytes, kTcUnitBytes, &full[st], pol);
+                } else {
+                    const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
+                    const uint32_t wbytes = (uint32_t)(RB * sb);
+                    const uint32_t sbytes = (uint32_t)Cfg::kScaleStage;
+                    mbar_arrive_expect_tx(&full[st], wbytes + sbytes);
+                    bulk_g2s_stream(dst, wrb + (size_t)s * RB * kSlabBytes, wbytes, &full[st], pol);
                     bulk_g2s_stream(dst + Cfg::kWeightStage, srb + (size_t)s * (RB / 32) * 1024, sbytes, &full[st],
                                     pol);
+                }
             }
         }
     } else {
@@ -132,6 +158,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         const int xstride = (L.slabs + P - 1) / P * L.slab_k;
         const int kbeg = s0 * L.slab_k;
         const int kend = min(s1 * L.slab_k, L.Kp);
+        const bool rms = p.prologue == kProRmsNorm || p.prologue == kProEmbedRms;
 
         // Source rows (embedding gather or activation buffer).
         const float* srcm[MB];
@@ -153,78 +180,154 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             for (int m = 0; m < p.M; ++m)
                 for (int k = ctid; k < L.K; k += 256) p.resid[(size_t)m * p.ld_src + k] = srcm[m][k];
         }
+        // Tensor.swift:1538-1558: ss = sum x^2; inv = 1 / sqrt(ss/H + eps).  The
+        // INT8 path also needs max |x| over this CTA's k range (digit scale).
         float inv[MB];
+        int ex[MB];
 #pragma unroll
-        for (int m = 0; m < MB; ++m) inv[m] = 1.0f;
-        if (p.prologue == kProRmsNorm || p.prologue == kProEmbedRms) {
-            // Tensor.swift:1538-1558: ss = sum x^2; inv = 1 / sqrt(ss/H + eps)
+        for (int m = 0; m < MB; ++m) {
+            inv[m] = 1.0f;
+            ex[m] = 0;
+        }
+        if (rms || PREC == 8) {
 #pragma unroll
             for (int m = 0; m < MB; ++m) {
-                float ss = 0.0f;
-                if (m < p.M)
-                    for (int k = ctid; k < L.K; k += 256) ss = fmaf(srcm[m][k], srcm[m][k], ss);
+                float ss = 0.0f, mx = 0.0f;
+                if (m < p.M) {
+                    if (rms)
+                        for (int k = ctid; k < L.K; k += 256) ss = fmaf(srcm[m][k], srcm[m][k], ss);
+                    if (PREC == 8)
+                        for (int k = kbeg + ctid; k < min(kend, L.K); k += 256)
+                            mx = fmaxf(mx, fabsf(rms ? __fmul_rn(srcm[m][k], p.norm_w[k]) : srcm[m][k]));
+                }
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-                if (lane == 0) misc[m * 8 + warp] = ss;
+                for (int o = 16; o > 0; o >>= 1) {
+                    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                }
+                if (lane == 0) {
+                    misc[m * 8 + warp] = ss;
+                    misc[(MB + m) * 8 + warp] = mx;
+                }
             }
             named_bar_sync(1, 256);
 #pragma unroll
             for (int m = 0; m < MB; ++m) {
-                float ss = 0.0f;
+                float ss = 0.0f, mx = 0.0f;
 #pragma unroll
-                for (int w = 0; w < 8; ++w) ss += misc[m * 8 + w];
-                inv[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)L.K), p.eps)));
-            }
-        }
-        // Stage x[m][kbeg:kend) into shared memory, lane-interleaved per slab.
-        for (int m = 0; m < MB; ++m) {
-            for (int k = kbeg + ctid; k < kend; k += 256) {
-                float v = 0.0f;
-                if (m < p.M && k < L.K) {
-                    v = srcm[m][k];
-                    if (p.prologue == kProRmsNorm || p.prologue == kProEmbedRms)
-                        v = __fmul_rn(__fmul_rn(v, inv[m]), p.norm_w[k]);
+                for (int w = 0; w < 8; ++w) {
+                    ss += misc[m * 8 + w];
+                    mx = fmaxf(mx, misc[(MB + m) * 8 + w]);
                 }
-                if (PREC == 4) v *= int4_pos_scale(k & 7);
-                const int rel = k - kbeg;
-                const int ls = rel / L.slab_k;
-                xs[m * xstride + ls * L.slab_k + xperm<CH>(rel - ls * L.slab_k)] = v;
+                if (rms) inv[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)L.K), p.eps)));
+                // x = src * w * inv and inv > 0: max |x| = max |src * w| * inv (one rounding above)
+                ex[m] = digit_exponent(__fmul_rn(mx, inv[m]) * 1.0000002f);
             }
         }
-        named_bar_sync(1, 256);
-
-        float2 acc[RPW][MB];
-#pragma unroll
-        for (int r = 0; r < RPW; ++r)
-#pragma unroll
-            for (int m = 0; m < MB; ++m) acc[r][m] = make_float2(0.0f, 0.0f);
-
-        for (int i = 0; i < nunits; ++i) {
-            const int st = i % STAGES;
-            // On a timed-out wait the results are garbage; the error word tells the host.
-            if (!mbar_wait(&full[st], (i / STAGES) & 1, p.err)) break;
-            const int s = s0 + i;
-            const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-            const uint8_t* wst = stage_base + st * Cfg::kStageBytes;
-            {
-                const float* ssl = (PREC == 4) ? reinterpret_cast<const float*>(wst + Cfg::kWeightStage) +
-                                                     ((warp * RPW) / 32) * 1024
-                                               : nullptr;
-                unit_dot<PREC, RPW, MB>(wst, sb, warp * RPW, ssl, xs + i * L.slab_k, xstride, lane, acc);
+        auto xval = [&](int m, int k) -> float {
+            float v = 0.0f;
+            if (m < p.M && k < L.K) {
+                v = srcm[m][k];
+                if (rms) v = __fmul_rn(__fmul_rn(v, inv[m]), p.norm_w[k]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
-        }
-        // Warp reduction: every lane ends with the full row sums.
+            return v;
+        };
+
+        if constexpr (PREC == 8) {
+            // Digits of x[m][kbeg:kend) into the B operand, 4 consecutive k per thread.
+            const int ngroups = (kend - kbeg) / 4;
+            for (int g = ctid; g < ngroups; g += 256) {
+                const int k = kbeg + 4 * g;
 #pragma unroll
-        for (int r = 0; r < RPW; ++r)
+                for (int m = 0; m < MB; ++m) {
+                    const float4 v = make_float4(xval(m, k), xval(m, k + 1), xval(m, k + 2), xval(m, k + 3));
+                    put_digits4(xd, NB, 4 * g, m, v, __int_as_float((127 - ex[m]) << 23));
+                }
+                if (NB > kTcDigits * MB) {  // unused digit rows read as zero
+                    uint8_t* base = xd + (size_t)(g >> 2) * NB * 16 + (4 * g & 15);
+                    for (int row = kTcDigits * MB; row < NB; ++row)
+                        *reinterpret_cast<uint32_t*>(base + (row >> 3) * 128 + (row & 7) * 16) = 0u;
+                }
+            }
+            fence_proxy_async_shared();
+            named_bar_sync(1, 256);
+            const uint32_t tmem = *tmem_slot;
+            if (warp == 0) {
+                tc_fence_after();
+                if (lane == 0) {
+                    for (int i = 0; i < nunits; ++i) {
+                        const int st = i % STAGES;
+                        if (!mbar_wait(&full[st], (i / STAGES) & 1, p.err)) break;
+                        tc_fence_after();
+                        tc_unit_mma(tmem, smem_u32(stage_base + st * Cfg::kStageBytes),
+                                    smem_u32(xd + (size_t)i * (kTcUnitK / 16) * NB * 16), NB, i > 0);
+                        tc_commit(&empty[st]);
+                    }
+                    tc_commit(done);
+                }
+                __syncwarp();
+            } else if (warp >= 4) {
+                // Epilogue warps: TMEM lanes 32 * (warp - 4) .. +31 = tile rows.
+                const bool okd = mbar_wait(done, 0, p.err);
+                tc_fence_after();
+                int d[NB];
 #pragma unroll
+                for (int c8 = 0; c8 < NB / 8; ++c8) {
+                    int t[8];
+                    tmem_ld8(tmem + ((uint32_t)(32 * (warp - 4)) << 16) + 8 * c8, t);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) d[8 * c8 + i] = t[i];
+                }
+                tmem_ld_wait();
+                const int row = 32 * (warp - 4) + lane;
+#pragma unroll
+                for (int m = 0; m < MB; ++m) red[row * MB + m] = okd ? combine_digits(d + kTcDigits * m, ex[m]) : 0.0f;
+                tc_fence_before();
+            }
+        } else {
+            // Stage x[m][kbeg:kend) into shared memory, lane-interleaved per slab.
             for (int m = 0; m < MB; ++m) {
-                float v = acc[r][m].x + acc[r][m].y;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0) red[(warp * RPW + r) * MB + m] = v;
+                for (int k = kbeg + ctid; k < kend; k += 256) {
+                    float v = xval(m, k) * int4_pos_scale(k & 7);
+                    const int rel = k - kbeg;
+                    const int ls = rel / L.slab_k;
+                    xs[m * xstride + ls * L.slab_k + xperm<CH>(rel - ls * L.slab_k)] = v;
+                }
             }
+            named_bar_sync(1, 256);
+
+            float2 acc[RPW][MB];
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+#pragma unroll
+                for (int m = 0; m < MB; ++m) acc[r][m] = make_float2(0.0f, 0.0f);
+
+            for (int i = 0; i < nunits; ++i) {
+                const int st = i % STAGES;
+                // On a timed-out wait the results are garbage; the error word tells the host.
+                if (!mbar_wait(&full[st], (i / STAGES) & 1, p.err)) break;
+                const int s = s0 + i;
+                const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
+                const uint8_t* wst = stage_base + st * Cfg::kStageBytes;
+                {
+                    const float* ssl = reinterpret_cast<const float*>(wst + Cfg::kWeightStage) +
+                                       ((warp * RPW) / 32) * 1024;
+                    unit_dot<PREC, RPW, MB>(wst, sb, warp * RPW, ssl, xs + i * L.slab_k, xstride, lane, acc);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);
+            }
+            // Warp reduction: every lane ends with the full row sums.
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    float v = acc[r][m].x + acc[r][m].y;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (lane == 0) red[(warp * RPW + r) * MB + m] = v;
+                }
+        }
     }
 
     // Make every CTA's partial row sums visible cluster-wide.
@@ -233,11 +336,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         cluster_sync();
     else
         __syncthreads();
+    if (PREC == 8 && warp == 0) {  // every tcgen05.ld of the epilogue completed before the barrier
+        tc_fence_after();
+        tmem_dealloc(*tmem_slot, 32);
+    }
 
     if (warp < kGemvConsumerWarps) {
         const int ctid = threadIdx.x;
         // Output items handled by this rank: a contiguous chunk.
-        const int nout = (p.epilogue == kEpiQkv) ? RB / 2 : (p.epilogue == kEpiSiluMul ? 32 : RB);
+        constexpr int HALF = RB / 2;  // fused gate/up: gate rows [0, HALF), up rows [HALF, RB)
+        const int nout = (p.epilogue == kEpiQkv || p.epilogue == kEpiSiluMul) ? HALF : RB;
         const int ob = rank * nout / P, oe = (rank + 1) * nout / P;
         const int nitems = (oe - ob) * MB;
         uint32_t rbase[8];
@@ -308,10 +416,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                     p.kv_pool[base * d + j % d + 1] = v1;
                 }
             } else if (p.epilogue == kEpiSiluMul) {
-                const int n = rb * 32 + o;
+                const int n = rb * HALF + o;
                 if (n >= L.N) continue;
                 const float g = finish(rb * RB + o, rowsum(o, m));
-                const float u = finish(rb * RB + 32 + o, rowsum(32 + o, m));
+                const float u = finish(rb * RB + HALF + o, rowsum(HALF + o, m));
                 p.out[(size_t)m * p.ld_out + n] = __fmul_rn(silu_ref(g), u);
             } else {
                 const int n = rb * RB + o;
@@ -373,9 +481,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 template <int PREC, int RB, int MB>
 size_t gemv_smem_bytes(const QLayout& L, int P) {
     using Cfg = GemvCfg<PREC, RB>;
-    size_t head = 128 + ((size_t)(RB * MB + 64) * 4 + 127) / 128 * 128;
+    size_t head = (256 + (size_t)(RB * MB + 16 * MB) * 4 + 1023) / 1024 * 1024;
     size_t stages = (size_t)Cfg::kStages * Cfg::kStageBytes;
-    size_t xbytes = (size_t)MB * ((L.slabs + P - 1) / P) * L.slab_k * 4;
+    const size_t per_k = PREC == 8 ? (size_t)tc_nb(MB) : (size_t)MB * 4;
+    size_t xbytes = ((L.slabs + P - 1) / P) * (size_t)L.slab_k * per_k;
     return head + stages + xbytes;
 }
 
@@ -413,7 +522,8 @@ int choose_ksplit(const QLayout& L, int M, int num_sms) {
     const int nrb = L.Np / L.RB;
     int P = 1;
     // Keep the staged activation slice modest and give every SM about two CTAs.
-    auto xbytes = [&](int q) { return (size_t)M * ((L.slabs + q - 1) / q) * L.slab_k * 4; };
+    const size_t per_k = L.precision == 8 ? (size_t)tc_nb(M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8) : (size_t)M * 4;
+    auto xbytes = [&](int q) { return ((L.slabs + q - 1) / q) * (size_t)L.slab_k * per_k; };
     while (P < 8 && P * 2 <= L.slabs && (nrb * P < 2 * num_sms || xbytes(P) > 48 * 1024)) P *= 2;
     while (P < L.slabs && P < 8 && xbytes(P) > 96 * 1024) ++P;
     return P;
@@ -423,20 +533,12 @@ cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream, bool pdl) {
     const int prec = p.L.precision, RB = p.L.RB;
     int mb = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : 8;
     if (p.M > 8) return cudaErrorInvalidValue;
-    if (prec == 8 && RB == 32) {
+    if (prec == 8) {
         switch (mb) {
-            case 1: return launch_t<8, 32, 1>(p, stream, pdl);
-            case 2: return launch_t<8, 32, 2>(p, stream, pdl);
-            case 4: return launch_t<8, 32, 4>(p, stream, pdl);
-            default: return launch_t<8, 32, 8>(p, stream, pdl);
-        }
-    }
-    if (prec == 8 && RB == 64) {
-        switch (mb) {
-            case 1: return launch_t<8, 64, 1>(p, stream, pdl);
-            case 2: return launch_t<8, 64, 2>(p, stream, pdl);
-            case 4: return launch_t<8, 64, 4>(p, stream, pdl);
-            default: return launch_t<8, 64, 8>(p, stream, pdl);
+            case 1: return launch_t<8, 128, 1>(p, stream, pdl);
+            case 2: return launch_t<8, 128, 2>(p, stream, pdl);
+            case 4: return launch_t<8, 128, 4>(p, stream, pdl);
+            default: return launch_t<8, 128, 8>(p, stream, pdl);
         }
     }
     if (prec == 4 && RB == 32) {

@@ -18,22 +18,28 @@ enum DeviceError : int {
 };
 
 // ----------------------------------------------------------------------------
-// Device weight layout produced by the repack kernels ("GPU layout").
+// Device weight layouts produced by the repack kernels ("GPU layout").
 //
 // The reference stores a quantized projection row-major as [K in][N out]
-// (y = x * W).  The GPU layout is output-row major and tiled for streaming:
-//   * rows (outputs) are grouped in row blocks of RB rows (RB = 32, or 64 for
-//     the fused gate/up matrix whose block is 32 gate rows + 32 up rows);
-//   * the reduction dimension is cut in slabs of 512 bytes per row (512 int8
-//     values or 1024 int4 values); the last slab of a row may be shorter;
-//   * unit (row block, slab) = RB rows x slab bytes, row-major, contiguous;
-//     units of a row block are consecutive, so a row block is one contiguous
-//     range streamed with 1-D bulk copies.
-// INT8 values are stored biased (q + 128 as uint8).  INT4 values are stored
-// biased (q + 8) two per byte, low nibble = even k.  INT4 group scales for the
-// 32 rows of a group and the k range of a slab are stored next to each other
-// per unit, in the lane-interleaved order the kernel reads them
-// ([group][chunk c][lane][4 floats] for k = 32*lane + 4*c + i).
+// (y = x * W).  The GPU layouts are output-row major and cut into "units" that
+// are streamed with 1-D bulk copies; the units of a row block are consecutive
+// (row-block major, k minor).
+//
+// INT8 (tensor-core path, tb_tc.cuh): row blocks ("tiles") of 128 rows, units
+// of 128 k = 16 KB, values stored as signed int8, each unit in the canonical
+// K-major no-swizzle operand layout of tcgen05.mma ([16 row groups][8 k-chunks
+// of 16 bytes][8 rows][16 bytes]).  K is padded to a multiple of 128 and N to
+// a multiple of 128 with zero weights.  The fused gate/up matrix puts 64 gate
+// rows and the matching 64 up rows in each tile.
+//
+// INT4 (CUDA-core path, tb_unit.cuh): row blocks of RB = 32 rows (or 64 for the
+// fused gate/up matrix: 32 gate + 32 up rows), the reduction dimension cut in
+// slabs of 512 bytes per row (1024 int4 values; the last slab may be shorter);
+// unit = 32 rows x slab bytes, row-major.  Values stored biased (q + 8) two per
+// byte, low nibble = even k.  Group scales for the 32 rows of a group and the k
+// range of a slab are stored next to each other per unit, in the
+// lane-interleaved order the kernel reads them ([group][chunk c][lane][4
+// floats] for k = 32*lane + 4*c + i).
 // ----------------------------------------------------------------------------
 constexpr int kSlabBytes = 512;
 constexpr int kGemvConsumerWarps = 8;
@@ -42,17 +48,28 @@ constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;  // + 1 producer war
 struct QLayout {
     int precision;       // 8 or 4
     int K;               // logical reduction length
-    int Kp;              // K padded to a multiple of 32
+    int Kp;              // K padded (INT8: multiple of 128, INT4: multiple of 32)
     int N;               // logical output rows
     int Np;              // N padded to a multiple of RB
-    int RB;              // rows per row block (32 or 64)
-    int slabs;           // number of slabs along K
-    int slab_k;          // k values per full slab (512 int8 / 1024 int4)
+    int RB;              // rows per row block (INT8: 128; INT4: 32, or 64 for gate/up)
+    int slabs;           // units along K per row block
+    int slab_k;          // k values per full unit (INT8 128, INT4 1024)
+    int slab_bytes;      // bytes per row of a full unit (INT8 128, INT4 512)
     int row_bytes;       // bytes per row (Kp or Kp/2)
+    int fused_gu;        // 1: gate/up interleaved by half row blocks
     size_t weight_bytes; // Np * row_bytes
     size_t scale_floats; // INT8: Np ; INT4: (Np/32) * Kp
 };
 
+// GPU row of logical row n of a matrix placed at (row_offset, interleave) in a
+// fused layout (interleave 1: gate half of each row block, 2: up half).
+__host__ __device__ inline int fused_row(const QLayout& L, int n, int row_offset, int interleave) {
+    if (interleave == 0) return row_offset + n;
+    const int half = L.RB / 2;
+    return (n / half) * L.RB + (interleave == 2 ? half : 0) + n % half;
+}
+
+// RB = 64 requests the fused gate/up arrangement (INT8 tiles stay 128 rows).
 QLayout make_qlayout(int precision, int K, int N, int RB);
 
 // Prologue: how the CTA builds its activation slice x[m][k].

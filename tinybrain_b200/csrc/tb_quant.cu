@@ -5,9 +5,10 @@
 // roundf (round half away from zero, as Swift's `round`), clamp, then the
 // integer conversion.  The repack converts the reference's [K in][N out]
 // row-major storage (INT8 per-column scales, INT4 flat groups packed high
-// nibble first) into the streamed layout documented in tb_kernels.h.
+// nibble first) into the streamed layouts documented in tb_kernels.h.
 #include "tb_common.cuh"
 #include "tb_kernels.h"
+#include "tb_tc.cuh"
 
 namespace tb {
 
@@ -73,25 +74,19 @@ __global__ void q4_pack_kernel(const float* __restrict__ x, int64_t count, int64
 
 // ---- repack ----
 
-__device__ __forceinline__ int dst_row_of(int n, int row_offset, int interleave) {
-    if (interleave == 0) return row_offset + n;
-    return (n / 32) * 64 + (interleave == 2 ? 32 : 0) + (n % 32);
-}
-
-// INT8: one thread per (destination row n, 16-value k chunk).  Threads with
+// INT8: one thread per (destination row, 16-value k chunk): 16 signed bytes
+// into the tensor-core operand layout of the row's 128-row tile.  Threads with
 // consecutive n read consecutive source bytes of row k.
 __global__ void repack_q8_kernel(const int8_t* __restrict__ src, int K, int N, QLayout L, uint8_t* __restrict__ dst,
                                  int row_offset, int interleave) {
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     const int kc = blockIdx.y;  // 16-value chunk
     if (n >= N) return;
-    const int drow = dst_row_of(n, row_offset, interleave);
-    const int rb = drow / L.RB, r = drow % L.RB;
+    const int drow = fused_row(L, n, row_offset, interleave);
+    const int tile = drow / kTcTileRows, r = drow % kTcTileRows;
     const int k0 = kc * 16;
-    const int s = k0 / kSlabBytes;
-    const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-    uint8_t* out = dst + (size_t)rb * L.RB * L.row_bytes + (size_t)s * L.RB * kSlabBytes + (size_t)r * sb +
-                   (k0 - s * kSlabBytes);
+    const int unit = k0 / kTcUnitK, c = (k0 % kTcUnitK) / 16;
+    uint8_t* out = dst + ((size_t)tile * L.slabs + unit) * kTcUnitBytes + ((r / 8) * 8 + c) * 128 + (r % 8) * 16;
     uint32_t w[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -100,18 +95,18 @@ __global__ void repack_q8_kernel(const int8_t* __restrict__ src, int K, int N, Q
         for (int b = 0; b < 4; ++b) {
             const int k = k0 + q * 4 + b;
             const int v = (k < K) ? (int)src[(size_t)k * N + n] : 0;
-            word |= ((uint32_t)((v + 128) & 0xFF)) << (8 * b);
+            word |= ((uint32_t)(v & 0xFF)) << (8 * b);
         }
         w[q] = word;
     }
     *reinterpret_cast<uint4*>(out) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-__global__ void repack_scales_q8_kernel(const float* __restrict__ src, int N, float* __restrict__ dst, int row_offset,
-                                        int interleave) {
+__global__ void repack_scales_q8_kernel(const float* __restrict__ src, int N, QLayout L, float* __restrict__ dst,
+                                        int row_offset, int interleave) {
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     if (n >= N) return;
-    dst[dst_row_of(n, row_offset, interleave)] = src[n];
+    dst[fused_row(L, n, row_offset, interleave)] = src[n];
 }
 
 __device__ __forceinline__ int src_nibble(const uint8_t* packed, int64_t i) {
@@ -126,7 +121,7 @@ __global__ void repack_q4_kernel(const uint8_t* __restrict__ src, int K, int N, 
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     const int kc = blockIdx.y;  // 32-value chunk
     if (n >= N) return;
-    const int drow = dst_row_of(n, row_offset, interleave);
+    const int drow = fused_row(L, n, row_offset, interleave);
     const int rb = drow / L.RB, r = drow % L.RB;
     const int k0 = kc * 32;
     const int byte0 = k0 / 2;
@@ -159,7 +154,7 @@ __global__ void repack_scales_q4_kernel(const float* __restrict__ src, int K, in
     if (e >= L.slabs * 1024) return;
     const int n0 = g32 * 32;
     if (n0 >= N) return;
-    const int drow = dst_row_of(n0, row_offset, interleave);
+    const int drow = fused_row(L, n0, row_offset, interleave);
     const int rb = drow / L.RB, grp = (drow % L.RB) / 32;
     const int s = e / 1024, w = e % 1024;
     const int i = w & 3, lane = (w >> 2) & 31, c = w >> 7;
@@ -195,7 +190,7 @@ cudaError_t launch_repack(const RepackSrc& s, const QLayout& L, uint8_t* w_out, 
     if (s.precision == 8) {
         repack_q8_kernel<<<dim3(nb, (unsigned)(L.Kp / 16)), 128, 0, stream>>>(
             (const int8_t*)s.data, s.K, s.N, L, w_out, row_offset, interleave);
-        repack_scales_q8_kernel<<<nb, 128, 0, stream>>>(s.scales, s.N, scales_out, row_offset, interleave);
+        repack_scales_q8_kernel<<<nb, 128, 0, stream>>>(s.scales, s.N, L, scales_out, row_offset, interleave);
     } else {
         repack_q4_kernel<<<dim3(nb, (unsigned)(L.Kp / 32)), 128, 0, stream>>>(
             (const uint8_t*)s.data, s.K, s.N, L, w_out, row_offset, interleave);

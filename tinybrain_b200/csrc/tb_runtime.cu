@@ -524,7 +524,8 @@ static tb_status alloc_fused(tb_context* ctx, FusedWeight& f, const QLayout& L) 
     f.L = L;
     TB_CUDA(f.w.alloc(L.weight_bytes));
     TB_CUDA(f.s.alloc(L.scale_floats * 4));
-    TB_CUDA(cudaMemsetAsync(f.w.p, L.precision == 8 ? 0x80 : 0x88, L.weight_bytes, ctx->stream));
+    // padding reads as zero weights: INT8 stores q itself, INT4 stores q + 8
+    TB_CUDA(cudaMemsetAsync(f.w.p, L.precision == 8 ? 0x00 : 0x88, L.weight_bytes, ctx->stream));
     TB_CUDA(cudaMemsetAsync(f.s.p, 0, L.scale_floats * 4, ctx->stream));
     return ok();
 }
@@ -873,7 +874,7 @@ static tb_status upload_bias(FusedWeight& f, const std::vector<std::pair<const P
         const ProjStage* st = pr.first;
         const int off = pr.second.first, inter = pr.second.second;
         for (int n = 0; n < (int)st->bias.size(); ++n) {
-            int row = inter == 0 ? off + n : (n / 32) * 64 + (inter == 2 ? 32 : 0) + n % 32;
+            const int row = fused_row(f.L, n, off, inter);
             hb[row] = st->bias[n];
         }
     }
@@ -918,7 +919,8 @@ extern "C" tb_status tb_model_finalize(tb_model* m) {
             const int pg = L.stage[TB_PROJ_GATE].precision;
             if (L.stage[TB_PROJ_UP].precision != pg)
                 return fail(TB_ERR_UNSUPPORTED, "layer %d: gate and up must share precision", l);
-            const int Ip = (I + 31) / 32 * 32;
+            const int half = make_qlayout(pg, H, 64, 64).RB / 2;  // gate rows per row block
+            const int Ip = (I + half - 1) / half * half;
             QLayout gl = make_qlayout(pg, H, 2 * Ip, 64);
             gl.N = I;
             if ((s = alloc_fused(ctx, L.up, gl)) != TB_OK) return s;
@@ -1151,6 +1153,7 @@ static tb_status build_step(tb_runner* r) {
     if (r->B != 1 || c.architecture != TB_ARCH_LLAMA || c.hidden_dim > 4096 || c.intermediate_dim % 4 != 0) return ok();
     const Layer& L0 = m->layers[0];
     const int prec = L0.qkv.L.precision;
+    if (prec == 8) return ok();  // INT8 persistent step: tensor-core rewrite pending
     auto same = [](const QLayout& a, const QLayout& b) {
         return a.precision == b.precision && a.K == b.K && a.N == b.N && a.RB == b.RB;
     };

@@ -34,6 +34,7 @@
 #include "tb_unit.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace tb {
 
@@ -83,43 +84,34 @@ __device__ __forceinline__ int att_floats(int G, int d, int Hkv, int A) {
     return max(G * d + 2 * d + 2 * G * kPageTokens, Hkv * G * A);
 }
 
-// Geometry of one 32-row unit u of a GEMV phase (units ordered 32-row block
-// major, slab minor).  A 64-row block (fused gate/up) is two 32-row units.
-struct UnitGeo {
-    int rb32, s, sb;
-    const uint8_t* w;
-    const float* sc;  // INT4 scales of the unit
+// Ring position (slot, phase parity) advanced without divisions.
+struct Cursor {
+    int st = 0;
+    uint32_t ph = 0;
+    __device__ __forceinline__ void next(int n) {
+        if (++st == n) {
+            st = 0;
+            ph ^= 1u;
+        }
+    }
 };
-__device__ __forceinline__ UnitGeo unit_geo(const QLayout& L, const uint8_t* w, const float* sc, int u) {
-    UnitGeo g;
-    g.rb32 = u / L.slabs;
-    g.s = u % L.slabs;
-    g.sb = min(kSlabBytes, L.row_bytes - g.s * kSlabBytes);
-    const int per = L.RB / 32;
-    const int rbb = g.rb32 / per, half = g.rb32 % per;
-    g.w = w + (size_t)rbb * L.RB * L.row_bytes + (size_t)g.s * L.RB * kSlabBytes + (size_t)half * 32 * g.sb;
-    g.sc = (L.precision == 4) ? sc + (((size_t)rbb * L.slabs + g.s) * per + half) * 1024 : nullptr;
-    return g;
-}
 
 // ------------------------------------------------------------------ producer --
 struct Producer {
     const StepParams& p;
     Shared sh;  // by value: the pointers stay in registers, not in local memory
-    int it = 0;
+    int it = 0;        // copies issued
+    Cursor cur;        // slot of copy `it`
+    Cursor thr;        // slot of copy `it - nflight` (throttle)
     uint64_t pol;
     bool dead = false;
 
     __device__ Producer(const StepParams& p_, const Shared& sh_) : p(p_), sh(sh_) { pol = l2_policy_evict_first(); }
 
-    // Keep at most p.nflight copies outstanding: enough to keep HBM busy, few
-    // enough not to inflate the latency of the consumers' activation loads.
-    __device__ bool throttle() {
-        if (it < p.nflight) return true;
-        const int j = it - p.nflight;
-        const int st = j % p.nslots;
+    __device__ bool spin(uint64_t* bar, uint32_t par) {
+        if (mbar_try_wait(bar, par)) return true;
         const uint64_t t0 = global_timer_ns();
-        while (!mbar_try_wait(&sh.full[st], (j / p.nslots) & 1)) {
+        while (!mbar_try_wait(bar, par)) {
             __nanosleep(64);
             if (*sh.abort || global_timer_ns() - t0 > kWaitLimitNs) {
                 if (!*sh.abort) record_error(p.err, kDevWaitTimeout);
@@ -131,36 +123,47 @@ struct Producer {
         return true;
     }
 
+    // Keep at most p.nflight copies outstanding: enough to keep HBM busy, few
+    // enough not to inflate the latency of the consumers' activation loads.
     __device__ uint8_t* acquire(int& st) {
-        if (!throttle()) return nullptr;
-        st = it % p.nslots;
-        if (it >= p.nslots) {
-            const uint32_t par = ((it / p.nslots) - 1) & 1;
-            const uint64_t t0 = global_timer_ns();
-            while (!mbar_try_wait(&sh.empty[st], par)) {
-                __nanosleep(64);
-                if (*sh.abort || global_timer_ns() - t0 > kWaitLimitNs) {
-                    if (!*sh.abort) record_error(p.err, kDevWaitTimeout);
-                    dead = true;
-                    *sh.abort = 1;
-                    return nullptr;
-                }
-            }
+        if (it >= p.nflight) {
+            if (!spin(&sh.full[thr.st], thr.ph)) return nullptr;
+            thr.next(p.nslots);
         }
+        st = cur.st;
+        if (it >= p.nslots && !spin(&sh.empty[st], cur.ph ^ 1u)) return nullptr;
         return sh.ring + (size_t)st * p.slot_bytes;
     }
+    __device__ __forceinline__ void issued() {
+        ++it;
+        cur.next(p.nslots);
+    }
 
+    // Units [u0, u1) of a GEMV phase (32-row block major, slab minor; a 64-row
+    // block of the fused gate/up matrix is two 32-row units).
     __device__ void gemv(const QLayout& L, const uint8_t* w, const float* sc, int u0, int u1) {
+        if (u1 <= u0) return;
+        const int hshift = L.RB == 64 ? 1 : 0;
+        int rb32 = u0 / L.slabs, s = u0 - rb32 * L.slabs;
         for (int u = u0; u < u1 && !dead; ++u) {
-            const UnitGeo g = unit_geo(L, w, sc, u);
+            const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
+            const int rbb = rb32 >> hshift, half = rb32 & hshift;
+            const uint8_t* src =
+                w + (size_t)rbb * L.RB * L.row_bytes + (size_t)s * L.RB * kSlabBytes + (size_t)half * 32 * sb;
             int st;
             uint8_t* dst = acquire(st);
             if (!dst) return;
-            const uint32_t wb = 32u * g.sb, sbytes = (L.precision == 4) ? 4096u : 0u;
+            const uint32_t wb = 32u * sb, sbytes = (L.precision == 4) ? 4096u : 0u;
             mbar_arrive_expect_tx(&sh.full[st], wb + sbytes);
-            bulk_g2s_stream(dst, g.w, wb, &sh.full[st], pol);
-            if (L.precision == 4) bulk_g2s_stream(dst + 16384, g.sc, sbytes, &sh.full[st], pol);
-            ++it;
+            bulk_g2s_stream(dst, src, wb, &sh.full[st], pol);
+            if (L.precision == 4)
+                bulk_g2s_stream(dst + 16384, sc + (((size_t)rbb * L.slabs + s) * (L.RB / 32) + half) * 1024, sbytes,
+                                &sh.full[st], pol);
+            issued();
+            if (++s == L.slabs) {
+                s = 0;
+                ++rb32;
+            }
         }
     }
 
@@ -182,7 +185,7 @@ struct Producer {
                 sh.valid[st] = 0;  // evicted page: rows read as zeros (KVCache.swift:239-253)
                 mbar_arrive(&sh.full[st]);
             }
-            ++it;
+            issued();
         }
     }
 
@@ -202,17 +205,17 @@ struct Producer {
 struct Consumer {
     const StepParams& p;
     Shared sh;  // by value: the pointers stay in registers, not in local memory
-    int it = 0;
+    Cursor rc;  // next ring slot to consume
     int ctid, warp, lane, c, C;
     int nph = 0;                     // phases per step (trace stride)
     int cur_phase = 0;
-    unsigned long long waited = 0;   // thread 0: ns waiting for ring slots in this phase
-    unsigned long long dotted = 0;   // thread 0: ns in unit products in this phase
+    unsigned long long waited = 0;   // thread 0: cycles waiting for ring slots in this phase
+    unsigned long long dotted = 0;   // thread 0: cycles in unit products in this phase
 
     // Diagnostics (p.trace != null): per CTA and phase, %globaltimer at the
     // start (0), end (1), end of the prologue (2); ns waiting for tiles (3) and
-    // in unit products (4); the prologue's loads landed (5), the last unit
-    // product done (6), the phase-end barrier entered (7).
+    // in unit products (4) (SM cycles); the prologue's loads landed (5); SM
+    // cycles (6) and ns (7) of the unit loop of a GEMV phase.
     __device__ void trace(int phase, int which) {
         if (!p.trace || ctid != 0) return;
         unsigned long long* t = p.trace + ((size_t)c * nph + phase) * 8;
@@ -268,7 +271,6 @@ struct Consumer {
         return *sh.go != 0;
     }
     __device__ void phase_end(int phase) {
-        mark(7);
         bar();
         if (ctid == 0) {
             trace(phase, 1);
@@ -295,12 +297,12 @@ struct Consumer {
     }
 
     __device__ const uint8_t* wait_slot(int& st) {
-        st = it % p.nslots;
+        st = rc.st;
         if (*sh.abort) return nullptr;
         const bool tr = p.trace && ctid == 0;
-        const uint64_t w0 = tr ? global_timer_ns() : 0;
-        const bool okw = mbar_wait(&sh.full[st], (it / p.nslots) & 1, p.err);
-        if (tr) waited += global_timer_ns() - w0;
+        const long long w0 = tr ? clock64() : 0;
+        const bool okw = mbar_wait(&sh.full[st], rc.ph, p.err);
+        if (tr) waited += clock64() - w0;
         if (!okw) {
             *sh.abort = 1;
             return nullptr;
@@ -310,7 +312,7 @@ struct Consumer {
     __device__ void release_slot(int st) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.empty[st]);
-        ++it;
+        rc.next(p.nslots);
     }
 
     // Sums of the split-K partials of NJ GPU rows of a phase.  A partial is
@@ -517,8 +519,10 @@ struct Consumer {
         };
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[r][0] = make_float2(0.f, 0.f);
-        for (int u = u0; u < u1; ++u) {
-            const int rb32 = u / L.slabs, s = u % L.slabs;
+        const long long loop_c0 = (p.trace && ctid == 0) ? clock64() : 0;
+        const uint64_t loop_t0 = (p.trace && ctid == 0) ? global_timer_ns() : 0;
+        int rb32 = u0 / L.slabs, s = u0 - (u0 / L.slabs) * L.slabs;
+        for (int u = u0; u < u1; ++u, (++s == L.slabs ? (s = 0, ++rb32) : 0)) {
             if (rb32 != cur) {
                 if (cur >= 0) flush(cur, s_first);
                 cur = rb32;
@@ -529,16 +533,20 @@ struct Consumer {
             if (!slot) return;
             const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
             const float* ssl = (PREC == 4) ? reinterpret_cast<const float*>(slot + 16384) : nullptr;
-            const uint64_t td = (p.trace && ctid == 0) ? global_timer_ns() : 0;
+            const long long td = (p.trace && ctid == 0) ? clock64() : 0;
             unit_dot<PREC, 4, 1>(slot, sb, warp * 4, ssl, sh.xs + s * L.slab_k, 0, lane, acc);
             if (p.trace && ctid == 0) {
-                volatile float sink = acc[0][0].x;
+                volatile float sink = acc[0][0].x + acc[1][0].x + acc[2][0].x + acc[3][0].x;
                 (void)sink;
-                dotted += global_timer_ns() - td;
+                dotted += clock64() - td;
             }
             release_slot(st);
         }
-        mark(6);
+        if (p.trace && ctid == 0) {
+            unsigned long long* t = p.trace + ((size_t)c * nph + cur_phase) * 8;
+            t[6] = clock64() - loop_c0;
+            t[7] = global_timer_ns() - loop_t0;
+        }
         if (cur >= 0) flush(cur, s_first);
     }
 
@@ -669,7 +677,7 @@ struct Consumer {
             if (have) {
                 release_slot(st);
             } else {
-                ++it;
+                rc.next(p.nslots);
             }
         }
         if (pv && !*sh.abort) {
@@ -1069,6 +1077,7 @@ size_t step_smem_bytes(const StepParams& p, int* nslots, int* slot_bytes, int ma
     int ns = (int)((max_smem - fixed) / sbytes);
     ns = std::min(ns, kMaxSlots);
     ns = std::min(ns, 10);  // leave L1 room for the few register spills
+    if (const char* e = getenv("TB_STEP_SLOTS")) ns = std::max(2, std::min(ns, atoi(e)));
     *nslots = ns;
     *slot_bytes = sbytes;
     return fixed + (size_t)ns * sbytes;

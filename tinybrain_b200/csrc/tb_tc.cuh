@@ -1,0 +1,144 @@
+// tb_tc.cuh -- 5th-generation tensor-core (tcgen05) helpers for the INT8
+// weight-only GEMV (sm_100a only).
+//
+// An INT8 projection y = W x (W: q[n][k] * scale[n]) runs on the integer
+// tensor cores exactly:
+//   * the activation slice x is scaled by a power of two 2^-e chosen so that
+//     |x| * 2^-e < 127, and split into four signed 8-bit digits
+//         u = x * 2^-e = d0 + d1 2^-7 + d2 2^-14 + d3 2^-21 (+ |r| <= 2^-22);
+//     every step is exact in fp32 (power-of-two scaling, round-to-integer,
+//     exact subtraction), so the digits carry x to 2^-29 of max|x|;
+//   * tcgen05.mma kind::i8 multiplies a 128-row weight tile (A, K-major in
+//     shared memory) by the digit matrix (B: N = 8 rows per batch row pair,
+//     K-major) into int32 accumulators in tensor memory -- exact integer sums;
+//   * the epilogue reads one row per thread (tcgen05.ld 32x32b), combines the
+//     digit columns in int64 (D0 2^21 + D1 2^14 + D2 2^7 + D3), converts once
+//     to fp32 and applies 2^(e-21), the per-row weight scale and the bias.
+// The result equals the fp32 dot product of the reference
+// (Sources/TinyBrainRuntime/QuantizedTensor.swift:430-460: dequantised
+// weights times x, fp32 accumulation) to ~1e-7 relative, with a single
+// rounding instead of K sequential ones.
+//
+// Shared-memory operand layouts (no swizzle, "interleaved" canonical K-major):
+//   A (weights, one 16 KB unit = 128 rows x 128 k): [16 row groups][8 k-chunks of
+//     16 bytes][8 rows][16 bytes]; core matrix (8 rows x 16 bytes) = 128
+//     contiguous bytes; LBO (next 16-byte k-chunk) = 128 B, SBO (next 8-row
+//     group) = 1024 B.  The GPU weight layout stores units in exactly this
+//     form so a 1-D bulk copy lands it ready for the tensor core.
+//   B (digits, NB rows): [k-chunk of 16][NB/8 row groups][8 rows][16 bytes];
+//     LBO = NB * 16 B, SBO = 128 B.  Row n = 4 * m + j holds digit j of batch
+//     row m.
+#pragma once
+
+#include "tb_common.cuh"
+
+namespace tb {
+
+constexpr int kTcTileRows = 128;    // A tile rows (M of the MMA)
+constexpr int kTcUnitK = 128;       // k per weight unit
+constexpr int kTcUnitBytes = kTcTileRows * kTcUnitK;  // 16 KB
+constexpr int kTcDigits = 4;
+
+// ---- tensor memory ----
+// Allocate `ncols` TMEM columns (power of two >= 32); the whole warp executes.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (sm_100 format: start, LBO, SBO in 16-byte
+// units; version 1; no swizzle).
+__device__ __forceinline__ uint64_t tc_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor: kind::i8, D s32, A s8, B s8, both K-major, M = 128.
+__host__ __device__ constexpr uint32_t tc_idesc_i8(int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcTileRows >> 4) << 24);
+}
+// D[tmem] (+)= A * B^T for one K = 32 step; issued by a single thread.
+__device__ __forceinline__ void tc_mma_i8(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+// Arrive once on `bar` when every tcgen05 operation issued so far by this thread completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// Issue the four K = 32 steps of one 16 KB weight unit (A at `a_saddr`)
+// against the digit columns of its k range (B at `b_saddr`).
+__device__ __forceinline__ void tc_unit_mma(uint32_t dtmem, uint32_t a_saddr, uint32_t b_saddr, int nb,
+                                            bool accumulate) {
+    const uint32_t idesc = tc_idesc_i8(nb);
+#pragma unroll
+    for (int s = 0; s < kTcUnitK / 32; ++s) {
+        const uint64_t ad = tc_sdesc(a_saddr + s * 256, 128, 1024);
+        const uint64_t bd = tc_sdesc(b_saddr + s * 2 * nb * 16, nb * 16, 128);
+        tc_mma_i8(dtmem, ad, bd, idesc, accumulate || s > 0);
+    }
+}
+
+// Warp-collective load of 8 / 16 / 32 consecutive accumulator columns of the
+// warp's 32 TMEM lanes (lane i of the warp gets row (32 * (warp % 4) + i)).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---- activation digits ----
+// Exponent e with max_abs * 2^-e < 127 (0 for max_abs == 0).
+__device__ __forceinline__ int digit_exponent(float max_abs) {
+    int e = 0;
+    (void)frexpf(max_abs * (1.0f / 127.0f), &e);
+    // max/127 = f 2^e, f in [0.5, 1): max 2^-e < 127.  The product with 1/127
+    // may round up across a power of two; that only makes e larger (still safe).
+    return e;
+}
+// Four digits of u = x * 2^-e (|u| < 127), returned as the four bytes of a word.
+__device__ __forceinline__ void split_digits(float x, float inv_scale, int (&d)[kTcDigits]) {
+    float u = x * inv_scale;  // exact: power-of-two scaling
+#pragma unroll
+    for (int j = 0; j < kTcDigits; ++j) {
+        const float r = rintf(u);
+        d[j] = (int)r;
+        u = (u - r) * 128.0f;  // exact
+    }
+}
+// Digit words of four consecutive k (k0 % 4 == 0) of batch row m, written to
+// the B operand: word j = bytes (d_j(x0), d_j(x1), d_j(x2), d_j(x3)).
+__device__ __forceinline__ void put_digits4(uint8_t* xd, int nb, int k0_rel, int m, float4 v, float inv_scale) {
+    int a[kTcDigits], b[kTcDigits], c[kTcDigits], e[kTcDigits];
+    split_digits(v.x, inv_scale, a);
+    split_digits(v.y, inv_scale, b);
+    split_digits(v.z, inv_scale, c);
+    split_digits(v.w, inv_scale, e);
+    uint8_t* base = xd + (size_t)(k0_rel >> 4) * nb * 16 + (k0_rel & 15);
+#pragma unroll
+    for (int j = 0; j < kTcDigits; ++j) {
+        const int row = m * kTcDigits + j;
+        const uint32_t w = (uint32_t)(a[j] & 0xFF) | ((uint32_t)(b[j] & 0xFF) << 8) | ((uint32_t)(c[j] & 0xFF) << 16) |
+                           ((uint32_t)(e[j] & 0xFF) << 24);
+        *reinterpret_cast<uint32_t*>(base + ((row >> 3) * 128) + (row & 7) * 16) = w;
+    }
+}
+// Combined accumulator of one batch row: digits at columns 4m .. 4m+3.
+__device__ __forceinline__ float combine_digits(const int* d, int e) {
+    const long long v = ((long long)d[0] << 21) + ((long long)d[1] << 14) + ((long long)d[2] << 7) + (long long)d[3];
+    return ldexpf(__ll2float_rn(v), e - 21);
+}
+
+}  // namespace tb
