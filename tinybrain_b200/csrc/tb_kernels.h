@@ -240,7 +240,7 @@ constexpr int kStepConsumerWarps = 8;
 constexpr int kStepThreads = (kStepConsumerWarps + 1) * 32;
 
 // Shared memory a launch needs (and its ring geometry), or 0 if unsupported.
-size_t step_smem_bytes(const StepParams& p, int* nslots, int* slot_bytes, int max_smem);
+size_t step_smem_bytes(const StepParams& p, int grid, int* nslots, int* slot_bytes, int max_smem);
 cudaError_t launch_decode_step(const StepParams& p, int grid, size_t smem, cudaStream_t stream);
 
 // Record the calling thread's last-error message (tb_last_error); returns status.

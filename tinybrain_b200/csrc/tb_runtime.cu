@@ -1153,7 +1153,6 @@ static tb_status build_step(tb_runner* r) {
     if (r->B != 1 || c.architecture != TB_ARCH_LLAMA || c.hidden_dim > 4096 || c.intermediate_dim % 4 != 0) return ok();
     const Layer& L0 = m->layers[0];
     const int prec = L0.qkv.L.precision;
-    if (prec == 8) return ok();  // INT8 persistent step: tensor-core rewrite pending
     auto same = [](const QLayout& a, const QLayout& b) {
         return a.precision == b.precision && a.K == b.K && a.N == b.N && a.RB == b.RB;
     };
@@ -1215,7 +1214,7 @@ static tb_status build_step(tb_runner* r) {
     int max_smem = 0;
     TB_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, r->ctx->device));
     int ns = 0, sb = 0;
-    const size_t smem = step_smem_bytes(p, &ns, &sb, max_smem - 1024);
+    const size_t smem = step_smem_bytes(p, C, &ns, &sb, max_smem - 1024);
     if (smem == 0) return ok();
     TB_CUDA(r->step_layers.alloc(hl.size() * sizeof(StepLayer)));
     TB_CUDA(cudaMemcpy(r->step_layers.p, hl.data(), hl.size() * sizeof(StepLayer), cudaMemcpyHostToDevice));

@@ -10,9 +10,9 @@
 // pays launch, ramp-up and drain latencies longer than its own HBM time.  Here
 // one CTA per SM runs the whole step:
 //
-//  * a producer warp walks the CTA's static share of every phase (32-row x
-//    512-byte weight units, INT4 group scales with them, and the KV-cache pages
-//    of its attention split) and streams them with 1-D bulk async copies into a
+//  * a producer warp walks the CTA's static share of every phase (16 KB weight
+//    units, INT4 group scales with them, and the KV-cache pages of its
+//    attention split) and streams them with 1-D bulk async copies into a
 //    shared-memory ring.  Weights and cached K/V do not depend on this step's
 //    activations, so the stream never waits on the data dependencies between
 //    phases -- only on free ring slots;
@@ -20,17 +20,27 @@
 //    grid-wide barrier (an atomic counter in global memory, bounded spin),
 //    builds its activation vector in shared memory (residual add + RMSNorm,
 //    RoPE, SiLU*up, split-K / attention-split combine -- Tensor.swift:1538-1558,
-//    ModelRunner.swift:470-579), multiplies it against the units already in the
-//    ring, and writes per-segment partial sums that the next phase reduces in a
+//    ModelRunner.swift:470-579), multiplies it against the units in the ring,
+//    and writes per-segment partial sums that the next phase reduces in a
 //    fixed order (deterministic, no atomics on data);
+//  * INT8 products run on the tensor cores (tb_tc.cuh): one thread issues
+//    tcgen05.mma kind::i8 per unit (128 rows x 128 k) against the exact 4-digit
+//    split of the activations, accumulating each segment (a run of units of one
+//    128-row tile) in its own tensor-memory block; tcgen05.commit releases the
+//    ring slot when the tensor core has read it and signals the segment's
+//    barrier, and four epilogue warps (one tile row per thread) read the
+//    accumulators back, combine the digits and apply scale and bias.  INT4
+//    products run on the CUDA cores (tb_unit.cuh, 32-row units);
 //  * the LM-head phase reduces whole row blocks per CTA, writes logits and
 //    folds a packed (value, index) argmax into the sequence state with one
 //    atomicMax per warp (Sampler.swift:126-138); CTA 0 then advances the step.
 //
 // All waits are bounded (2 s of %globaltimer); a timeout records an error code
-// and makes the CTA leave the step early without hanging the device.
+// and makes the CTA leave the step early (after its tensor-core work drained and
+// its tensor memory was freed) without hanging the device.
 #include "tb_common.cuh"
 #include "tb_kernels.h"
+#include "tb_tc.cuh"
 #include "tb_unit.cuh"
 
 #include <algorithm>
@@ -41,24 +51,29 @@ namespace tb {
 namespace {
 
 constexpr int kMaxSlots = 24;
-constexpr int kBarRegion = 1024;  // mbarriers + flags
-constexpr int kMiscFloats = 1024;
+constexpr int kMaxSegs = 16;                 // INT8: accumulator blocks per CTA and phase
+constexpr int kTmemCols = kMaxSegs * 8;      // 8 TMEM columns (4 digits + 4 zero) per block
+constexpr int kBarRegion = 1024;             // mbarriers + flags
+constexpr int kMiscFloats = 2048;
 constexpr int kConsumers = kStepConsumerWarps * 32;
-constexpr int kRowBlocksCached = 16;  // per-warp scale/bias cache of a GEMV phase (row blocks)
+constexpr int kMaxTileSegs = 32;             // split-K segments per row block (table width)
 
 struct Shared {
     uint64_t* full;
     uint64_t* empty;
+    uint64_t* seg;          // [kMaxSegs] INT8 segment accumulators complete
+    uint64_t* fin;          // INT8: all tensor-core work of the CTA complete
     int* valid;             // [kMaxSlots] attention tile present (page not evicted)
     volatile int* abort;    // set when a wait timed out
     volatile int* go;       // thread 0's per-phase decision
+    uint32_t* tmem;         // tensor-memory base address
     float* misc;            // [kMiscFloats]
     uint8_t* ring;
-    float* xs;              // activation vector, lane-interleaved per slab
+    float* xs;              // INT4: fp32 lane-interleaved activations; INT8: digit operand (bytes)
     float* att;             // attention scratch
-    float* hs;              // [2][H] residual stream and norm weights of a prologue
-    float* rows;            // [warp][kRowBlocksCached][8]: INT8 scales (4) and biases (4) of the warp's rows
-    uint32_t* segmask[4];   // per 32-row block: bit s = a CTA segment starts at slab s (qkv, o, gate/up, down)
+    float* hs;              // staging: residual + norm weights [2][H], combined activations
+    uint8_t* seglist[4];    // per row block: units where CTA segments start, ascending [rb][kMaxTileSegs]
+    uint8_t* segcnt[4];     // per row block: number of segments
 };
 
 __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
@@ -69,19 +84,23 @@ __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
 __device__ __forceinline__ void red_release_add(unsigned int* p, unsigned int v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// 4-byte asynchronous copy global -> shared (does not stall the issuing warp).
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // The CTA whose static unit range [c*U/C, (c+1)*U/C) contains unit u.
-__device__ __forceinline__ int owner_of(int u, int U, int C) { return (int)(((long long)u * C + C - 1) / U); }
+__host__ __device__ inline int owner_of(int u, int U, int C) { return (int)(((long long)u * C + C - 1) / U); }
 
 __device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
 
 __device__ __forceinline__ int att_floats(int G, int d, int Hkv, int A) {
     return max(G * d + 2 * d + 2 * G * kPageTokens, Hkv * G * A);
+}
+
+// Rows per streamed unit: INT8 128-row tiles, INT4 32-row units.
+__host__ __device__ constexpr int unit_rows(int prec) { return prec == 8 ? kTcTileRows : 32; }
+__host__ __device__ inline int phase_units(const QLayout& L) { return (L.Np / unit_rows(L.precision)) * L.slabs; }
+// Segment table bytes of a phase: [rb][kMaxTileSegs] unit indices + [rb] counts (16-byte rounded).
+__host__ __device__ inline int seg_table_bytes(const QLayout& L) {
+    const int nrb = L.Np / unit_rows(L.precision);
+    return (nrb * kMaxTileSegs + nrb + 15) / 16 * 16;
 }
 
 // Ring position (slot, phase parity) advanced without divisions.
@@ -93,6 +112,11 @@ struct Cursor {
             st = 0;
             ph ^= 1u;
         }
+    }
+    __device__ __forceinline__ void advance(int k, int n) {
+        const int t = st + k;
+        ph ^= (uint32_t)((t / n) & 1);
+        st = t % n;
     }
 };
 
@@ -139,10 +163,23 @@ struct Producer {
         cur.next(p.nslots);
     }
 
-    // Units [u0, u1) of a GEMV phase (32-row block major, slab minor; a 64-row
-    // block of the fused gate/up matrix is two 32-row units).
+    // Units [u0, u1) of a GEMV phase (row-block major, unit minor; an INT4
+    // 64-row gate/up block is two 32-row units).
+    template <int PREC>
     __device__ void gemv(const QLayout& L, const uint8_t* w, const float* sc, int u0, int u1) {
         if (u1 <= u0) return;
+        if (PREC == 8) {
+            // INT8 units are consecutive 16 KB blocks in memory.
+            for (int u = u0; u < u1 && !dead; ++u) {
+                int st;
+                uint8_t* dst = acquire(st);
+                if (!dst) return;
+                mbar_arrive_expect_tx(&sh.full[st], kTcUnitBytes);
+                bulk_g2s_stream(dst, w + (size_t)u * kTcUnitBytes, kTcUnitBytes, &sh.full[st], pol);
+                issued();
+            }
+            return;
+        }
         const int hshift = L.RB == 64 ? 1 : 0;
         int rb32 = u0 / L.slabs, s = u0 - rb32 * L.slabs;
         for (int u = u0; u < u1 && !dead; ++u) {
@@ -153,12 +190,11 @@ struct Producer {
             int st;
             uint8_t* dst = acquire(st);
             if (!dst) return;
-            const uint32_t wb = 32u * sb, sbytes = (L.precision == 4) ? 4096u : 0u;
-            mbar_arrive_expect_tx(&sh.full[st], wb + sbytes);
+            const uint32_t wb = 32u * sb;
+            mbar_arrive_expect_tx(&sh.full[st], wb + 4096u);
             bulk_g2s_stream(dst, src, wb, &sh.full[st], pol);
-            if (L.precision == 4)
-                bulk_g2s_stream(dst + 16384, sc + (((size_t)rbb * L.slabs + s) * (L.RB / 32) + half) * 1024, sbytes,
-                                &sh.full[st], pol);
+            bulk_g2s_stream(dst + 16384, sc + (((size_t)rbb * L.slabs + s) * (L.RB / 32) + half) * 1024, 4096u,
+                            &sh.full[st], pol);
             issued();
             if (++s == L.slabs) {
                 s = 0;
@@ -209,13 +245,17 @@ struct Consumer {
     int ctid, warp, lane, c, C;
     int nph = 0;                     // phases per step (trace stride)
     int cur_phase = 0;
+    int xexp = 0;                    // INT8: digit exponent of the current activation vector
+    uint32_t tmem = 0;               // INT8: tensor-memory base
+    uint32_t segpar = 0;             // INT8 epilogue: next parity of each segment barrier
+    bool issued_mma = false;         // INT8 issuer: tensor-core work outstanding
     unsigned long long waited = 0;   // thread 0: cycles waiting for ring slots in this phase
     unsigned long long dotted = 0;   // thread 0: cycles in unit products in this phase
 
     // Diagnostics (p.trace != null): per CTA and phase, %globaltimer at the
-    // start (0), end (1), end of the prologue (2); ns waiting for tiles (3) and
-    // in unit products (4) (SM cycles); the prologue's loads landed (5); SM
-    // cycles (6) and ns (7) of the unit loop of a GEMV phase.
+    // start (0), end (1), end of the prologue (2); cycles waiting for tiles (3)
+    // and in unit products (4); the prologue's loads landed (5); SM cycles (6)
+    // and ns (7) of the unit loop of a GEMV phase.
     __device__ void trace(int phase, int which) {
         if (!p.trace || ctid != 0) return;
         unsigned long long* t = p.trace + ((size_t)c * nph + phase) * 8;
@@ -228,7 +268,6 @@ struct Consumer {
             t[4] = dotted;
         }
     }
-
     __device__ __forceinline__ void mark(int which) {
         if (p.trace && ctid == 0) p.trace[((size_t)c * nph + cur_phase) * 8 + which] = global_timer_ns();
     }
@@ -244,11 +283,9 @@ struct Consumer {
     __device__ void bar() { named_bar_sync(1, kConsumers); }
 
     // Grid barrier: wait until every CTA finished phase (phase - 1).  Arrival
-    // is one release-add on a counter, the wait an acquire poll by thread 0
-    // (measured cheaper on this part than per-CTA flags polled by a warp,
-    // whose loads crowd the L2 slices holding the flags).  The go/stop
-    // decision is published through sh.go before the CTA barrier, so every
-    // consumer warp takes the same branch.
+    // is one release-add on a counter, the wait an acquire poll by thread 0.
+    // The go/stop decision is published through sh.go before the CTA barrier,
+    // so every consumer warp takes the same branch.
     __device__ bool phase_begin(int phase) {
         if (ctid == 0) {
             if (phase > 0 && !*sh.abort) {
@@ -278,24 +315,6 @@ struct Consumer {
         }
     }
 
-    // Issue asynchronous copies of the INT8 scales and the biases of this
-    // warp's rows of every row block in the CTA's range of a GEMV phase; the
-    // first flush of the phase waits for them.
-    __device__ void prefetch_rows(const QLayout& L, const float* sc, const float* bias) {
-        const int U = (L.Np / 32) * L.slabs;
-        const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
-        if (u1 <= u0) return;
-        const int rb0 = u0 / L.slabs, nrb = min((u1 - 1) / L.slabs - rb0 + 1, kRowBlocksCached);
-        float* rs = sh.rows + warp * kRowBlocksCached * 8;
-        for (int e = lane; e < nrb * 8; e += 32) {
-            const int i = e >> 3, q = e & 7;
-            const int row = (rb0 + i) * 32 + warp * 4 + (q & 3);
-            const float* src = q < 4 ? (L.precision == 8 ? sc : nullptr) : bias;
-            if (src) cp_async4(rs + e, src + row);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    }
-
     __device__ const uint8_t* wait_slot(int& st) {
         st = rc.st;
         if (*sh.abort) return nullptr;
@@ -309,108 +328,136 @@ struct Consumer {
         }
         return sh.ring + (size_t)st * p.slot_bytes;
     }
-    __device__ void release_slot(int st) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.empty[st]);
+    // Every consumer thread calls this once per slot (a CTA barrier inside).
+    __device__ void release_slot(int st, bool have) {
+        bar();
+        if (ctid == 0 && have) mbar_arrive(&sh.empty[st]);
         rc.next(p.nslots);
     }
 
-    // Sums of the split-K partials of NJ GPU rows of a phase.  A partial is
-    // stored (already scaled; the slab-0 segment carries the bias) at the slab
-    // where its CTA's segment of the row block starts; segments are summed in
-    // slab order.  All loads are issued before
-    // the first add, so NJ rows cost one L2 round trip, not one per segment.
-    template <int NJ, int SEGMAX = 4>
-    __device__ void reduce_rows(const QLayout& L, const uint32_t* tab, const float* part, const int (&n)[NJ],
-                                const bool (&use)[NJ], float (&out)[NJ]) {
-        float v[NJ][SEGMAX];
-        uint32_t m0[NJ], rest[NJ];
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-            uint32_t m = use[j] ? tab[n[j] >> 5] : 0u;
-            m0[j] = m;
-#pragma unroll
-            for (int g = 0; g < SEGMAX; ++g) {
-                const int sl = __ffs(m) - 1;  // -1: no segment left
-                v[j][g] = sl >= 0 ? __ldcg(part + (size_t)sl * L.Np + n[j]) : 0.0f;
-                m &= m - 1;
-            }
-            rest[j] = m;
-        }
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-            const int cnt = __popc(m0[j]);
-            float t = 0.0f;
-#pragma unroll
-            for (int g = 0; g < SEGMAX; ++g)
-                if (g < cnt) t += v[j][g];
-            for (uint32_t m = rest[j]; m; m &= m - 1) t += __ldcg(part + (size_t)(__ffs(m) - 1) * L.Np + n[j]);
-            out[j] = t;
-        }
-    }
-
-    // Vector form of reduce_rows: NG groups of 4 consecutive GPU rows (same
-    // 32-row block), one float4 load per segment.
-    template <int NG, int SEGMAX = 4>
-    __device__ void reduce4(const QLayout& L, const uint32_t* tab, const float* part, const int (&n0)[NG],
+    // Sums of the split-K partials of NG groups of 4 consecutive GPU rows (same
+    // row block).  A partial is stored (scaled; the segment starting at unit 0
+    // carries the bias) at the unit where its CTA's segment of the row block
+    // starts; segments are summed in unit order.  The first NL partials of
+    // every group are loaded before the first add (one L2 round trip for all
+    // groups); further segments, if any, follow group by group.
+    template <int NG, int NL>
+    __device__ void reduce4(const QLayout& L, int which, const float* part, const int (&n0)[NG],
                             const bool (&use)[NG], float4 (&out)[NG]) {
-        float4 v[NG][SEGMAX];
-        uint32_t m0[NG], rest[NG];
+        const int ru = unit_rows(L.precision);
+        float4 v[NG][NL];
+        int cnt[NG];
+        const uint8_t* lst[NG];
 #pragma unroll
         for (int j = 0; j < NG; ++j) {
-            uint32_t m = use[j] ? tab[n0[j] >> 5] : 0u;
-            m0[j] = m;
+            const int rb = n0[j] / ru;
+            cnt[j] = use[j] ? sh.segcnt[which][rb] : 0;
+            lst[j] = sh.seglist[which] + rb * kMaxTileSegs;
 #pragma unroll
-            for (int g = 0; g < SEGMAX; ++g) {
-                const int sl = __ffs(m) - 1;
-                v[j][g] = sl >= 0 ? __ldcg(reinterpret_cast<const float4*>(part + (size_t)sl * L.Np + n0[j]))
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-                m &= m - 1;
-            }
-            rest[j] = m;
+            for (int g = 0; g < NL; ++g)
+                v[j][g] = g < cnt[j] ? __ldcg(reinterpret_cast<const float4*>(part + (size_t)lst[j][g] * L.Np + n0[j]))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int j = 0; j < NG; ++j) {
-            const int cnt = __popc(m0[j]);
-            float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 a = v[j][0];
 #pragma unroll
-            for (int g = 0; g < SEGMAX; ++g)
-                if (g < cnt) {
-                    t.x += v[j][g].x;
-                    t.y += v[j][g].y;
-                    t.z += v[j][g].z;
-                    t.w += v[j][g].w;
+            for (int g = 1; g < NL; ++g)
+                if (g < cnt[j]) {
+                    a.x += v[j][g].x;
+                    a.y += v[j][g].y;
+                    a.z += v[j][g].z;
+                    a.w += v[j][g].w;
                 }
-            for (uint32_t m = rest[j]; m; m &= m - 1) {
-                const float4 q = __ldcg(reinterpret_cast<const float4*>(part + (size_t)(__ffs(m) - 1) * L.Np + n0[j]));
-                t.x += q.x;
-                t.y += q.y;
-                t.z += q.z;
-                t.w += q.w;
+            for (int g = NL; g < cnt[j]; ++g) {
+                const float4 q = __ldcg(reinterpret_cast<const float4*>(part + (size_t)lst[j][g] * L.Np + n0[j]));
+                a.x += q.x;
+                a.y += q.y;
+                a.z += q.z;
+                a.w += q.w;
             }
-            out[j] = t;
+            out[j] = a;
+        }
+    }
+    // Scalar form for single rows.
+    template <int NJ, int NL>
+    __device__ void reduce_rows(const QLayout& L, int which, const float* part, const int (&n)[NJ],
+                                float (&out)[NJ]) {
+        const int ru = unit_rows(L.precision);
+        float v[NJ][NL];
+        int cnt[NJ];
+        const uint8_t* lst[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const int rb = n[j] / ru;
+            cnt[j] = sh.segcnt[which][rb];
+            lst[j] = sh.seglist[which] + rb * kMaxTileSegs;
+#pragma unroll
+            for (int g = 0; g < NL; ++g) v[j][g] = g < cnt[j] ? __ldcg(part + (size_t)lst[j][g] * L.Np + n[j]) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            float a = v[j][0];
+#pragma unroll
+            for (int g = 1; g < NL; ++g)
+                if (g < cnt[j]) a += v[j][g];
+            for (int g = NL; g < cnt[j]; ++g) a += __ldcg(part + (size_t)lst[j][g] * L.Np + n[j]);
+            out[j] = a;
         }
     }
 
-    template <int PREC>
-    __device__ void put_x(const QLayout& L, int k, float v) {
-        constexpr int CH = PREC == 8 ? 16 : 32;
-        constexpr int SK = PREC == 8 ? kSlabBytes : 2 * kSlabBytes;  // == L.slab_k
-        if (PREC == 4) v *= int4_pos_scale(k & 7);
+    // INT4: fp32 activation, lane-interleaved per slab, nibble-position scaled.
+    __device__ void put_x4(int k, float v) {
+        constexpr int SK = 2 * kSlabBytes;  // == L.slab_k
+        v *= int4_pos_scale(k & 7);
         const int s = k / SK;
-        sh.xs[s * SK + xperm<CH>(k - s * SK)] = v;
+        sh.xs[s * SK + xperm<32>(k - s * SK)] = v;
+    }
+    // Four consecutive activations (k % 4 == 0) into the phase's operand.
+    template <int PREC>
+    __device__ __forceinline__ void put_x_group(int k, float4 v) {
+        if (PREC == 8) {
+            put_digits4(reinterpret_cast<uint8_t*>(sh.xs), 8, k, 0, v, __int_as_float((127 - xexp) << 23));
+        } else {
+            put_x4(k + 0, v.x);
+            put_x4(k + 1, v.y);
+            put_x4(k + 2, v.z);
+            put_x4(k + 3, v.w);
+        }
+    }
+    // Zero activations for k in [k0, Kp) (multiple-of-4 bounds).
+    template <int PREC>
+    __device__ void zero_tail(const QLayout& L, int k0) {
+        for (int k = k0 + 4 * ctid; k < L.Kp; k += 4 * kConsumers) put_x_group<PREC>(k, make_float4(0.f, 0.f, 0.f, 0.f));
+    }
+    // Block-wide max of a per-thread value; sets xexp (all consumer threads).
+    __device__ void set_digit_exponent(float mx, float factor) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) sh.misc[32 + warp] = mx;
+        bar();
+        float t = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kStepConsumerWarps; ++w) t = fmaxf(t, sh.misc[32 + w]);
+        xexp = digit_exponent(__fmul_rn(t, factor) * 1.0000002f);
+    }
+    // End of a prologue: make INT8 digits visible to the tensor core.
+    template <int PREC>
+    __device__ void prologue_done() {
+        if (PREC == 8) fence_proxy_async_shared();
+        bar();
     }
 
     // h = src + (reduced partials of the previous phase); optional store of
     // this CTA's slice of h; x = RMSNorm(h) * w (or h when norm == null).  The
-    // source rows, norm weights and partials are loaded as float4 in one batch
-    // per chunk; h is parked in shared memory (sh.hs) until the norm is known.
+    // source rows, norm weights and partials are loaded as float4 per group of
+    // 4 rows; h is parked in shared memory (sh.hs) until the norm is known.
     template <int PREC>
-    __device__ void residual_norm(const float* src, const QLayout* Lp, const uint32_t* tab, const float* part,
-                                  float* store, const float* norm, const QLayout& Lnext) {
+    __device__ void residual_norm(const float* src, const QLayout* Lp, int which, const float* part, float* store,
+                                  const float* norm, const QLayout& Lnext) {
         const int H = p.H;  // multiple of 32
         const int k0 = (int)((long long)c * H / C), k1 = (int)((long long)(c + 1) * H / C);
-        float ss = 0.0f;
+        float ss = 0.0f, mx = 0.0f;
         // thread t owns rows 4t..4t+3 of every 1024-row chunk
         for (int base = 0; base < H; base += 4 * 2 * kConsumers) {
             int n0[2];
@@ -426,7 +473,7 @@ struct Consumer {
                                          : make_float4(1.f, 1.f, 1.f, 1.f);
                 add[j] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            if (Lp) reduce4<2>(*Lp, tab, part, n0, use, add);
+            if (Lp) reduce4<2, 10>(*Lp, which, part, n0, use, add);
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 if (!use[j]) continue;
@@ -441,6 +488,12 @@ struct Consumer {
                 ss = fmaf(v.y, v.y, ss);
                 ss = fmaf(v.z, v.z, ss);
                 ss = fmaf(v.w, v.w, ss);
+                if (PREC == 8) {
+                    mx = fmaxf(mx, fabsf(__fmul_rn(v.x, nw[j].x)));
+                    mx = fmaxf(mx, fabsf(__fmul_rn(v.y, nw[j].y)));
+                    mx = fmaxf(mx, fabsf(__fmul_rn(v.z, nw[j].z)));
+                    mx = fmaxf(mx, fabsf(__fmul_rn(v.w, nw[j].w)));
+                }
                 *reinterpret_cast<float4*>(sh.hs + n0[j]) = v;
                 *reinterpret_cast<float4*>(sh.hs + H + n0[j]) = nw[j];
                 if (store) {
@@ -467,41 +520,108 @@ struct Consumer {
             for (int w = 0; w < kStepConsumerWarps; ++w) t += sh.misc[w];
             inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), p.eps)));
         }
-        // each thread re-reads the rows it parked itself: no barrier needed
+        if (PREC == 8) set_digit_exponent(mx, inv);
+        // each thread re-reads the rows it parked itself
         for (int n = 4 * ctid; n < H; n += 4 * kConsumers) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float v = sh.hs[n + e];
-                put_x<PREC>(Lnext, n + e, norm ? __fmul_rn(__fmul_rn(v, inv), sh.hs[H + n + e]) : v);
+            const float4 v = *reinterpret_cast<const float4*>(sh.hs + n);
+            float4 x = v;
+            if (norm) {
+                const float4 w = *reinterpret_cast<const float4*>(sh.hs + H + n);
+                x = make_float4(__fmul_rn(__fmul_rn(v.x, inv), w.x), __fmul_rn(__fmul_rn(v.y, inv), w.y),
+                                __fmul_rn(__fmul_rn(v.z, inv), w.z), __fmul_rn(__fmul_rn(v.w, inv), w.w));
             }
+            put_x_group<PREC>(n, x);
         }
-        for (int k = H + ctid; k < Lnext.Kp; k += kConsumers) put_x<PREC>(Lnext, k, 0.0f);
-        bar();
+        zero_tail<PREC>(Lnext, H);
+        prologue_done<PREC>();
     }
 
-    // Multiply this CTA's units of a GEMV phase; write one partial per row and
-    // segment, at the slab where the segment starts.
-    template <int PREC>
-    __device__ void gemv_units(const QLayout& L, float* part, const float* sc, const float* bias) {
+    // ---------------------------------------------------------- GEMV phases --
+    // INT8: warp 0 lane 0 issues the tensor-core products of this CTA's units;
+    // warps 4-7 read each finished segment accumulator (one tile row per
+    // thread), combine the digits, apply scale (and the bias on the segment
+    // that starts at unit 0) and store one partial per row and segment at the
+    // unit where the segment starts.
+    __device__ void gemv_tc(const QLayout& L, float* part, const float* sc, const float* bias) {
         trace(cur_phase, 2);
-        prefetch_rows(L, sc, bias);
-        const int U = (L.Np / 32) * L.slabs;
+        const int U = phase_units(L);
+        const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
+        const uint8_t* xd = reinterpret_cast<const uint8_t*>(sh.xs);
+        if (warp == 0) {
+            if (lane == 0 && u1 > u0) {
+                const long long lc0 = p.trace ? clock64() : 0;
+                const uint64_t lt0 = p.trace ? global_timer_ns() : 0;
+                Cursor q = rc;
+                int s = u0 % L.slabs, sfirst = s, j = 0;
+                tc_fence_after();
+                for (int u = u0; u < u1; ++u) {
+                    if (*sh.abort) break;
+                    const long long w0 = p.trace ? clock64() : 0;
+                    if (!mbar_wait(&sh.full[q.st], q.ph, p.err)) {
+                        *sh.abort = 1;
+                        break;
+                    }
+                    if (p.trace) waited += clock64() - w0;
+                    tc_fence_after();
+                    tc_unit_mma(tmem + 8 * j, smem_u32(sh.ring + (size_t)q.st * p.slot_bytes),
+                                smem_u32(xd + (size_t)s * (kTcUnitK / 16) * 128), 8, s != sfirst);
+                    tc_commit(&sh.empty[q.st]);
+                    issued_mma = true;
+                    q.next(p.nslots);
+                    if (u + 1 == u1 || s + 1 == L.slabs) {
+                        tc_commit(&sh.seg[j]);
+                        ++j;
+                    }
+                    if (++s == L.slabs) {
+                        s = 0;
+                        sfirst = 0;
+                    }
+                }
+                if (p.trace) {
+                    unsigned long long* t = p.trace + ((size_t)c * nph + cur_phase) * 8;
+                    t[6] = clock64() - lc0;
+                    t[7] = global_timer_ns() - lt0;
+                }
+            }
+            __syncwarp();
+        } else if (warp >= 4) {
+            const int row = 32 * (warp - 4) + lane;
+            const uint32_t lane_base = (uint32_t)(32 * (warp - 4)) << 16;
+            int j = 0;
+            for (int u = u0; u < u1; ++j) {
+                const int T = u / L.slabs, sfirst = u - T * L.slabs;
+                const int uend = min(u1, (T + 1) * L.slabs);
+                const int n = T * kTcTileRows + row;
+                const float scv = __ldg(sc + n);
+                const float bv = (bias && sfirst == 0) ? __ldg(bias + n) : 0.0f;
+                const uint32_t par = (segpar >> j) & 1u;
+                segpar ^= 1u << j;
+                const bool ok = !*sh.abort && mbar_wait(&sh.seg[j], par, p.err);
+                if (!ok) *sh.abort = 1;
+                tc_fence_after();
+                int d[8];
+                tmem_ld8(tmem + lane_base + 8 * j, d);
+                tmem_ld_wait();
+                if (ok) {
+                    float v = __fmul_rn(combine_digits(d, xexp), scv);
+                    if (bias && sfirst == 0) v = __fadd_rn(v, bv);
+                    part[(size_t)sfirst * L.Np + n] = v;
+                }
+                u = uend;
+            }
+            tc_fence_before();
+        }
+        rc.advance(u1 - u0, p.nslots);
+    }
+
+    // INT4: 32-row units on the CUDA cores; each warp owns 4 rows of a unit.
+    __device__ void gemv_cc(const QLayout& L, float* part, const float* bias) {
+        trace(cur_phase, 2);
+        const int U = phase_units(L);
         const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
         float2 acc[4][1];
         int cur = -1, s_first = 0;
-        // The per-row INT8 scale is applied to each partial; the segment that
-        // starts at slab 0 also carries the bias, so readers only add.  Scales
-        // and biases come from the warp's prefetched row cache.
-        const int rb0 = u0 / L.slabs;
-        const float* rs = sh.rows + warp * kRowBlocksCached * 8;
-        bool cached = false;
         auto flush = [&](int rb32, int slab) {
-            const int i = rb32 - rb0;
-            if (!cached) {
-                cp_async_wait_all();
-                __syncwarp();
-                cached = true;
-            }
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 float v = acc[r][0].x + acc[r][0].y;
@@ -509,9 +629,7 @@ struct Consumer {
                 for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                 const int n = rb32 * 32 + warp * 4 + r;
                 if (lane == r) {
-                    const bool hit = i < kRowBlocksCached;
-                    if (L.precision == 8) v = __fmul_rn(v, hit ? rs[i * 8 + r] : __ldg(sc + n));
-                    if (bias && slab == 0) v = __fadd_rn(v, hit ? rs[i * 8 + 4 + r] : __ldg(bias + n));
+                    if (bias && slab == 0) v = __fadd_rn(v, __ldg(bias + n));
                     part[(size_t)slab * L.Np + n] = v;
                 }
                 acc[r][0] = make_float2(0.f, 0.f);
@@ -530,17 +648,18 @@ struct Consumer {
             }
             int st;
             const uint8_t* slot = wait_slot(st);
-            if (!slot) return;
-            const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-            const float* ssl = (PREC == 4) ? reinterpret_cast<const float*>(slot + 16384) : nullptr;
-            const long long td = (p.trace && ctid == 0) ? clock64() : 0;
-            unit_dot<PREC, 4, 1>(slot, sb, warp * 4, ssl, sh.xs + s * L.slab_k, 0, lane, acc);
-            if (p.trace && ctid == 0) {
-                volatile float sink = acc[0][0].x + acc[1][0].x + acc[2][0].x + acc[3][0].x;
-                (void)sink;
-                dotted += clock64() - td;
+            if (slot) {
+                const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
+                const float* ssl = reinterpret_cast<const float*>(slot + 16384);
+                const long long td = (p.trace && ctid == 0) ? clock64() : 0;
+                unit_dot<4, 4, 1>(slot, sb, warp * 4, ssl, sh.xs + s * L.slab_k, 0, lane, acc);
+                if (p.trace && ctid == 0) {
+                    volatile float sink = acc[0][0].x + acc[1][0].x + acc[2][0].x + acc[3][0].x;
+                    (void)sink;
+                    dotted += clock64() - td;
+                }
             }
-            release_slot(st);
+            release_slot(st, slot != nullptr);
         }
         if (p.trace && ctid == 0) {
             unsigned long long* t = p.trace + ((size_t)c * nph + cur_phase) * 8;
@@ -548,6 +667,14 @@ struct Consumer {
             t[7] = global_timer_ns() - loop_t0;
         }
         if (cur >= 0) flush(cur, s_first);
+    }
+
+    template <int PREC>
+    __device__ void gemv_units(const QLayout& L, float* part, const float* sc, const float* bias) {
+        if (PREC == 8)
+            gemv_tc(L, part, sc, bias);
+        else
+            gemv_cc(L, part, bias);
     }
 
     // ---------------------------------------------------------------- attention
@@ -567,14 +694,12 @@ struct Consumer {
         float* vnew = knew + D;    // [D]
         float* S = vnew + D;       // [2][G][16]
         const QLayout& L = p.Lqkv;
-        const StepLayer& ly = p.layers[layer];
         const float2* rope = p.rope + (size_t)min(pos, p.rope_max_pos - 1) * (D / 2);
         // q (RoPE'd) for the G query heads of this KV head (ModelRunner.swift:499-515).
         for (int e = ctid; e < G * D / 2; e += kConsumers) {
             int n[2] = {head * G * D + 2 * e, head * G * D + 2 * e + 1};
-            bool use[2] = {true, true};
             float v[2];
-            reduce_rows<2>(L, sh.segmask[0], p.part_qkv, n, use, v);
+            reduce_rows<2, 10>(L, 0, p.part_qkv, n, v);
             const float2 cs = rope[(2 * e % D) / 2];
             qs[2 * e] = __fsub_rn(__fmul_rn(v[0], cs.x), __fmul_rn(v[1], cs.y));
             qs[2 * e + 1] = __fadd_rn(__fmul_rn(v[0], cs.y), __fmul_rn(v[1], cs.x));
@@ -585,9 +710,8 @@ struct Consumer {
                 const int nk = p.H + head * D + 2 * e;
                 const int nv = p.H + p.kvd + head * D + 2 * e;
                 int n[4] = {nk, nk + 1, nv, nv + 1};
-                bool use[4] = {true, true, true, true};
                 float v[4];
-                reduce_rows<4>(L, sh.segmask[0], p.part_qkv, n, use, v);
+                reduce_rows<4, 10>(L, 0, p.part_qkv, n, v);
                 const float2 cs = rope[e];
                 const float r0 = __fsub_rn(__fmul_rn(v[0], cs.x), __fmul_rn(v[1], cs.y));
                 const float r1 = __fadd_rn(__fmul_rn(v[0], cs.y), __fmul_rn(v[1], cs.x));
@@ -674,11 +798,7 @@ struct Consumer {
                 run_l = l;
                 acc = a;
             }
-            if (have) {
-                release_slot(st);
-            } else {
-                rc.next(p.nslots);
-            }
+            release_slot(st, have);
         }
         if (pv && !*sh.abort) {
             float* part = p.attn_part + (((size_t)head * A + split) * G + gv) * (D + 4);
@@ -690,41 +810,41 @@ struct Consumer {
         }
     }
 
-    // Slabs of K touched by this CTA's units of a phase (bit per slab).
-    __device__ uint32_t slab_set(const QLayout& L) {
-        const int U = (L.Np / 32) * L.slabs;
+    // Units of K touched by this CTA's units of a phase: a cyclic run of
+    // `count` units starting at unit `first` (units are row-block major).
+    __device__ void unit_run(const QLayout& L, int& first, int& count) {
+        const int U = phase_units(L);
         const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
-        if (u1 - u0 >= L.slabs) return L.slabs >= 32 ? 0xFFFFFFFFu : ((1u << L.slabs) - 1u);
-        uint32_t m = 0;
-        for (int u = u0; u < u1; ++u) m |= 1u << (u % L.slabs);
-        return m;
+        first = u0 % L.slabs;
+        count = min(u1 - u0, L.slabs);
     }
-    // The e-th k of the slabs in `set` (slab-major); -1 past the set, -2 past Kp.
-    __device__ __forceinline__ int kth_in_set(const QLayout& L, uint32_t set, int e) {
-        const int si = e / L.slab_k;
-        uint32_t m = set;
-        for (int i = 0; i < si && m; ++i) m &= m - 1;
-        if (!m) return -1;
-        const int k = (__ffs(m) - 1) * L.slab_k + e % L.slab_k;
+    // The e-th k of that run; -1 past the run, -2 past Kp.
+    __device__ __forceinline__ int kth_in_run(const QLayout& L, int first, int count, int e) {
+        const int i = e / L.slab_k;
+        if (i >= count) return -1;
+        int s = first + i;
+        if (s >= L.slabs) s -= L.slabs;
+        const int k = s * L.slab_k + (e - i * L.slab_k);
         return k < L.Kp ? k : -2;
     }
 
-    // ctx[k] for the slabs this CTA's o_proj units need: combine the attention
+    // ctx[k] for the units this CTA's o_proj units need: combine the attention
     // splits in split order (softmax rescaling of (m, l, acc) partials).  Each
     // thread owns groups of 4 consecutive k; the acc loads of its first group
     // are issued together with the (m, l) loads, so the common case costs one
-    // round trip.
+    // round trip.  INT8 stages the values (sh.hs) until their maximum is known.
     template <int PREC, int G, int D>
     __device__ void ctx_prologue() {
         constexpr int AMAX = 16;
         const QLayout& L = p.Lo;
         const int A = p.A;
-        float2* ml = reinterpret_cast<float2*>(sh.misc);  // [Hkv][A][G] (m, l)
-        float* wts = sh.att;                              // [Hkv][G][A]
-        const uint32_t set = slab_set(L);
-        const int total = __popc(set) * L.slab_k;  // multiple of 4
+        float2* ml = reinterpret_cast<float2*>(sh.misc + 64);  // [Hkv][A][G] (m, l)
+        float* wts = sh.att;                                     // [Hkv][G][A]
+        int first, count;
+        unit_run(L, first, count);
+        const int total = count * L.slab_k;  // multiple of 4
         auto group_loads = [&](int e, int& k, float4 (&a)[AMAX]) {
-            k = e < total ? kth_in_set(L, set, e) : -1;
+            k = e < total ? kth_in_run(L, first, count, e) : -1;
             const bool ok = k >= 0 && k < L.K;
             const int hq = ok ? k / D : 0, i = ok ? k % D : 0;
             const int hk = hq / G, g = hq % G;
@@ -734,10 +854,9 @@ struct Consumer {
                                              p.attn_part + (((size_t)hk * A + sp) * G + g) * (D + 4) + i))
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
         };
-        auto group_put = [&](int k, const float4 (&a)[AMAX]) {
-            if (k < 0) return;
+        auto group_value = [&](int k, const float4 (&a)[AMAX]) -> float4 {
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (k < L.K) {
+            if (k >= 0 && k < L.K) {
                 const int hq = k / D;
                 const float* w = wts + ((hq / G) * G + hq % G) * A;
 #pragma unroll
@@ -749,10 +868,7 @@ struct Consumer {
                         v.w = fmaf(w[sp], a[sp].w, v.w);
                     }
             }
-            put_x<PREC>(L, k + 0, v.x);
-            put_x<PREC>(L, k + 1, v.y);
-            put_x<PREC>(L, k + 2, v.z);
-            put_x<PREC>(L, k + 3, v.w);
+            return v;
         };
         int k0;
         float4 a0[AMAX];
@@ -779,25 +895,50 @@ struct Consumer {
         }
         bar();
         mark(5);
-        group_put(k0, a0);
-        for (int e = 4 * (ctid + kConsumers); e < total; e += 4 * kConsumers) {
-            int k;
-            float4 a[AMAX];
-            group_loads(e, k, a);
-            group_put(k, a);
+        if (PREC == 8) {
+            float mx = 0.0f;
+            for (int e = 4 * ctid; e < total; e += 4 * kConsumers) {
+                float4 v;
+                if (e == 4 * ctid) {
+                    v = group_value(k0, a0);
+                } else {
+                    int k;
+                    float4 a[AMAX];
+                    group_loads(e, k, a);
+                    v = group_value(k, a);
+                }
+                *reinterpret_cast<float4*>(sh.hs + e) = v;
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            }
+            set_digit_exponent(mx, 1.0f);
+            for (int e = 4 * ctid; e < total; e += 4 * kConsumers) {
+                const int k = kth_in_run(L, first, count, e);
+                if (k >= 0) put_x_group<PREC>(k, *reinterpret_cast<const float4*>(sh.hs + e));
+            }
+        } else {
+            if (k0 >= 0) put_x_group<PREC>(k0, group_value(k0, a0));
+            for (int e = 4 * (ctid + kConsumers); e < total; e += 4 * kConsumers) {
+                int k;
+                float4 a[AMAX];
+                group_loads(e, k, a);
+                if (k >= 0) put_x_group<PREC>(k, group_value(k, a));
+            }
         }
-        bar();
+        prologue_done<PREC>();
     }
 
-    // act[k] = silu(gate[k]) * up[k] for the slabs this CTA's down units need;
-    // groups of 4 consecutive k, up to 4 groups per thread per batch of loads.
+    // act[k] = silu(gate[k]) * up[k] for the units this CTA's down units need;
+    // groups of 4 consecutive k, up to 2 groups per thread per batch of loads.
     template <int PREC>
-    __device__ void act_prologue(const StepLayer& ly) {
-        constexpr int NG = 4;
+    __device__ void act_prologue() {
+        constexpr int NG = 2;
         const QLayout& L = p.Ldn;
         const QLayout& GL = p.Lgu;
-        const uint32_t set = slab_set(L);
-        const int total = __popc(set) * L.slab_k;  // multiple of 4
+        int first, count;
+        unit_run(L, first, count);
+        const int total = count * L.slab_k;  // multiple of 4
+        const int half = GL.RB / 2;
+        float mx = 0.0f;
         for (int e0 = 0; e0 < total; e0 += 4 * NG * kConsumers) {
             int n0[2 * NG], kk[NG];
             bool use[2 * NG];
@@ -805,15 +946,15 @@ struct Consumer {
 #pragma unroll
             for (int j = 0; j < NG; ++j) {
                 const int e = e0 + 4 * (ctid + kConsumers * j);
-                const int k = e < total ? kth_in_set(L, set, e) : -1;
+                const int k = e < total ? kth_in_run(L, first, count, e) : -1;
                 kk[j] = k;
                 const bool ok = k >= 0 && k < L.K;  // K % 4 == 0
-                const int grow = ok ? (k / 32) * 64 + (k % 32) : 0;
+                const int grow = ok ? fused_row(GL, k, 0, 1) : 0;
                 n0[2 * j] = grow;
-                n0[2 * j + 1] = grow + 32;
+                n0[2 * j + 1] = grow + half;
                 use[2 * j] = use[2 * j + 1] = ok;
             }
-            reduce4<2 * NG, 2>(GL, sh.segmask[2], p.part_gu, n0, use, v);
+            reduce4<2 * NG, 4>(GL, 2, p.part_gu, n0, use, v);
             if (e0 == 0 && p.trace && ctid == 0) {
                 volatile float sink = v[0].x;
                 (void)sink;
@@ -824,18 +965,93 @@ struct Consumer {
                 if (kk[j] < 0) continue;
                 const float4 g = v[2 * j], u = v[2 * j + 1];
                 const bool ok = use[2 * j];
-                put_x<PREC>(L, kk[j] + 0, ok ? __fmul_rn(silu_ref(g.x), u.x) : 0.0f);
-                put_x<PREC>(L, kk[j] + 1, ok ? __fmul_rn(silu_ref(g.y), u.y) : 0.0f);
-                put_x<PREC>(L, kk[j] + 2, ok ? __fmul_rn(silu_ref(g.z), u.z) : 0.0f);
-                put_x<PREC>(L, kk[j] + 3, ok ? __fmul_rn(silu_ref(g.w), u.w) : 0.0f);
+                const float4 a = ok ? make_float4(__fmul_rn(silu_ref(g.x), u.x), __fmul_rn(silu_ref(g.y), u.y),
+                                                  __fmul_rn(silu_ref(g.z), u.z), __fmul_rn(silu_ref(g.w), u.w))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (PREC == 8) {
+                    *reinterpret_cast<float4*>(sh.hs + e0 + 4 * (ctid + kConsumers * j)) = a;
+                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+                } else {
+                    put_x_group<PREC>(kk[j], a);
+                }
             }
         }
-        bar();
+        if (PREC == 8) {
+            set_digit_exponent(mx, 1.0f);
+            for (int e = 4 * ctid; e < total; e += 4 * kConsumers) {
+                const int k = kth_in_run(L, first, count, e);
+                if (k >= 0) put_x_group<PREC>(k, *reinterpret_cast<const float4*>(sh.hs + e));
+            }
+        }
+        prologue_done<PREC>();
     }
 
     // LM head: whole row blocks per CTA, logits + argmax (Sampler.swift:126-138).
-    template <int PREC>
-    __device__ void lm_head(unsigned long long* best_out) {
+    __device__ void lm_head_tc(unsigned long long* best_out) {
+        const QLayout& L = p.Llm;
+        const int nt = L.Np / kTcTileRows;
+        const int t0 = (int)((long long)c * nt / C), t1 = (int)((long long)(c + 1) * nt / C);
+        const uint8_t* xd = reinterpret_cast<const uint8_t*>(sh.xs);
+        if (warp == 0) {
+            if (lane == 0 && t1 > t0) {
+                Cursor q = rc;
+                tc_fence_after();
+                for (int t = t0; t < t1 && !*sh.abort; ++t) {
+                    for (int s = 0; s < L.slabs; ++s) {
+                        if (!mbar_wait(&sh.full[q.st], q.ph, p.err)) {
+                            *sh.abort = 1;
+                            break;
+                        }
+                        tc_fence_after();
+                        tc_unit_mma(tmem + 8 * (t - t0), smem_u32(sh.ring + (size_t)q.st * p.slot_bytes),
+                                    smem_u32(xd + (size_t)s * (kTcUnitK / 16) * 128), 8, s > 0);
+                        tc_commit(&sh.empty[q.st]);
+                        issued_mma = true;
+                        q.next(p.nslots);
+                    }
+                    if (*sh.abort) break;
+                    tc_commit(&sh.seg[t - t0]);
+                }
+            }
+            __syncwarp();
+        } else if (warp >= 4) {
+            const int row = 32 * (warp - 4) + lane;
+            const uint32_t lane_base = (uint32_t)(32 * (warp - 4)) << 16;
+            unsigned long long best = 0ull;
+            for (int t = t0; t < t1; ++t) {
+                const int j = t - t0;
+                const int n = t * kTcTileRows + row;
+                const bool inr = n < L.N;
+                const float scv = inr ? __ldg(p.lm_s + n) : 0.0f;
+                const float bv = (inr && p.lm_b) ? __ldg(p.lm_b + n) : 0.0f;
+                const uint32_t par = (segpar >> j) & 1u;
+                segpar ^= 1u << j;
+                const bool ok = !*sh.abort && mbar_wait(&sh.seg[j], par, p.err);
+                if (!ok) *sh.abort = 1;
+                tc_fence_after();
+                int d[8];
+                tmem_ld8(tmem + lane_base + 8 * j, d);
+                tmem_ld_wait();
+                if (ok && inr) {
+                    float lv = __fmul_rn(combine_digits(d, xexp), scv);
+                    if (p.lm_b) lv = __fadd_rn(lv, bv);
+                    if (p.logits) p.logits[n] = lv;
+                    const unsigned long long key = argmax_key(lv, n);
+                    best = key > best ? key : best;
+                }
+            }
+            tc_fence_before();
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+                best = t > best ? t : best;
+            }
+            if (lane == 0 && best != 0ull) atomicMax(best_out, best);
+        }
+        rc.advance((t1 - t0) * L.slabs, p.nslots);
+    }
+
+    __device__ void lm_head_cc(unsigned long long* best_out) {
         const QLayout& L = p.Llm;
         const int nrb = L.Np / 32;
         const int r0 = (int)((long long)c * nrb / C), r1 = (int)((long long)(c + 1) * nrb / C);
@@ -847,11 +1063,12 @@ struct Consumer {
             for (int s = 0; s < L.slabs; ++s) {
                 int st;
                 const uint8_t* slot = wait_slot(st);
-                if (!slot) return;
-                const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-                const float* ssl = (PREC == 4) ? reinterpret_cast<const float*>(slot + 16384) : nullptr;
-                unit_dot<PREC, 4, 1>(slot, sb, warp * 4, ssl, sh.xs + s * L.slab_k, 0, lane, acc);
-                release_slot(st);
+                if (slot) {
+                    const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
+                    const float* ssl = reinterpret_cast<const float*>(slot + 16384);
+                    unit_dot<4, 4, 1>(slot, sb, warp * 4, ssl, sh.xs + s * L.slab_k, 0, lane, acc);
+                }
+                release_slot(st, slot != nullptr);
             }
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
@@ -859,8 +1076,8 @@ struct Consumer {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                 const int n = rb * 32 + warp * 4 + r;
-                if (lane == r && n < L.N) {
-                    float lv = (PREC == 8) ? __fmul_rn(v, p.lm_s[n]) : v;
+                if (lane == r && n < L.N && !*sh.abort) {
+                    float lv = v;
                     if (p.lm_b) lv = __fadd_rn(lv, p.lm_b[n]);
                     if (p.logits) p.logits[n] = lv;
                     const unsigned long long key = argmax_key(lv, n);
@@ -875,103 +1092,32 @@ struct Consumer {
         }
         if (lane == 0 && best != 0ull) atomicMax(best_out, best);
     }
+
+    template <int PREC>
+    __device__ void lm_head(unsigned long long* best_out) {
+        if (PREC == 8)
+            lm_head_tc(best_out);
+        else
+            lm_head_cc(best_out);
+    }
 };
 
+// Segment tables: for every row block of a phase, the units (ascending) where
+// a CTA's unit range starts a segment of that row block.
+__device__ void build_seglist(uint8_t* list, uint8_t* cnt, const QLayout& L, int C, int tid, int nthreads) {
+    const int ru = unit_rows(L.precision);
+    const int nrb = L.Np / ru, U = nrb * L.slabs;
+    for (int rb = tid; rb < nrb; rb += nthreads) {
+        int n = 0;
+        for (int s = 0; s < L.slabs && n < kMaxTileSegs; ++s)
+            if (s == 0 || owner_of(rb * L.slabs + s, U, C) != owner_of(rb * L.slabs + s - 1, U, C))
+                list[rb * kMaxTileSegs + n++] = (uint8_t)s;
+        cnt[rb] = (uint8_t)n;
+    }
+}
+
 template <int PREC, int G, int D>
-__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    Shared sh;
-    sh.full = reinterpret_cast<uint64_t*>(smem);
-    sh.empty = sh.full + kMaxSlots;
-    sh.valid = reinterpret_cast<int*>(sh.empty + kMaxSlots);
-    sh.abort = reinterpret_cast<volatile int*>(sh.valid + kMaxSlots);
-    sh.go = sh.abort + 1;
-    sh.misc = reinterpret_cast<float*>(smem + kBarRegion);
-    sh.ring = smem + kBarRegion + kMiscFloats * 4;
-    sh.xs = reinterpret_cast<float*>(sh.ring + (size_t)p.nslots * p.slot_bytes);
-    const int xfloats = max(max(max(p.Lqkv.slabs * p.Lqkv.slab_k, p.Lo.slabs * p.Lo.slab_k),
-                                max(p.Lgu.slabs * p.Lgu.slab_k, p.Ldn.slabs * p.Ldn.slab_k)),
-                            p.Llm.slabs * p.Llm.slab_k);
-    sh.att = sh.xs + xfloats;
-    sh.hs = sh.att + att_floats(G, D, p.Hkv, p.A);
-    {
-        uint32_t* t = reinterpret_cast<uint32_t*>(sh.hs + 2 * p.H);
-        const QLayout* Ls[4] = {&p.Lqkv, &p.Lo, &p.Lgu, &p.Ldn};
-        for (int i = 0; i < 4; ++i) {
-            sh.segmask[i] = t;
-            t += (Ls[i]->Np / 32 + 3) / 4 * 4;
-        }
-        sh.rows = reinterpret_cast<float*>(t);
-    }
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int C = gridDim.x, c = blockIdx.x;
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < p.nslots; ++i) {
-            mbar_init(&sh.full[i], 1);
-            mbar_init(&sh.empty[i], kStepConsumerWarps);
-        }
-        *sh.abort = 0;
-        *sh.go = 1;
-        fence_barrier_init();
-    }
-    __syncthreads();
-
-    const int pos = p.seq->pos;
-    const int npages = pos / kPageTokens + 1;
-    const int A = p.A;
-    const int head = c < A * p.Hkv ? c / A : -1;
-    const int split = c < A * p.Hkv ? c % A : 0;
-    const int pps = (npages + A - 1) / A;
-    const int apg0 = min(npages, split * pps), apg1 = min(npages, apg0 + pps);
-
-    if (warp == kStepConsumerWarps) {
-        if (lane == 0) {
-            Producer pr(p, sh);
-            auto range = [&](const QLayout& L, int& u0, int& u1) {
-                const int U = (L.Np / 32) * L.slabs;
-                u0 = (int)((long long)c * U / C);
-                u1 = (int)((long long)(c + 1) * U / C);
-            };
-            int u0, u1;
-            for (int l = 0; l < p.num_layers && !pr.dead; ++l) {
-                const StepLayer& ly = p.layers[l];
-                range(p.Lqkv, u0, u1);
-                pr.gemv(p.Lqkv, ly.qkv_w, ly.qkv_s, u0, u1);
-                if (head >= 0) pr.attention(l, head, apg0, apg1);
-                range(p.Lo, u0, u1);
-                pr.gemv(p.Lo, ly.o_w, ly.o_s, u0, u1);
-                range(p.Lgu, u0, u1);
-                pr.gemv(p.Lgu, ly.gu_w, ly.gu_s, u0, u1);
-                range(p.Ldn, u0, u1);
-                pr.gemv(p.Ldn, ly.dn_w, ly.dn_s, u0, u1);
-            }
-            if (!pr.dead) {
-                const int nrb = p.Llm.Np / 32;
-                const int r0 = (int)((long long)c * nrb / C), r1 = (int)((long long)(c + 1) * nrb / C);
-                pr.gemv(p.Llm, p.lm_w, p.lm_s, r0 * p.Llm.slabs, r1 * p.Llm.slabs);
-            }
-            if (pr.dead) pr.drain();
-        }
-        return;
-    }
-
-    Consumer cs(p, sh);
-    cs.nph = 5 * p.num_layers + 1;
-    {
-        // Where the CTA segments of each 32-row block start (bit per slab).
-        const QLayout* Ls[4] = {&p.Lqkv, &p.Lo, &p.Lgu, &p.Ldn};
-        for (int i = 0; i < 4; ++i) {
-            const QLayout& L = *Ls[i];
-            const int nrb = L.Np / 32, U = nrb * L.slabs;
-            for (int rb = threadIdx.x; rb < nrb; rb += kConsumers) {
-                uint32_t m = 1u;
-                for (int s = 1; s < L.slabs; ++s)
-                    if (owner_of(rb * L.slabs + s, U, C) != owner_of(rb * L.slabs + s - 1, U, C)) m |= 1u << s;
-                sh.segmask[i][rb] = m;
-            }
-        }
-    }
+__device__ void run_layers(Consumer& cs, const StepParams& p, int pos, int npages) {
     int phase = 0;
     for (int l = 0; l < p.num_layers; ++l) {
         const StepLayer& ly = p.layers[l];
@@ -983,10 +1129,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 if (threadIdx.x == 0) record_error(p.err, kDevBadToken);
                 tok = 0;
             }
-            cs.residual_norm<PREC>(p.emb + (size_t)tok * p.H, nullptr, nullptr, nullptr, p.hX, ly.in_norm, p.Lqkv);
+            cs.residual_norm<PREC>(p.emb + (size_t)tok * p.H, nullptr, 3, nullptr, p.hX, ly.in_norm, p.Lqkv);
         } else {
-            const StepLayer& pl = p.layers[l - 1];
-            cs.residual_norm<PREC>(p.hY, &p.Ldn, sh.segmask[3], p.part_dn, p.hX, ly.in_norm, p.Lqkv);
+            cs.residual_norm<PREC>(p.hY, &p.Ldn, 3, p.part_dn, p.hX, ly.in_norm, p.Lqkv);
         }
         cs.gemv_units<PREC>(p.Lqkv, p.part_qkv, ly.qkv_s, ly.qkv_b);
         cs.phase_end(phase - 1);
@@ -1001,30 +1146,143 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         cs.phase_end(phase - 1);
         // ---- gate/up: h_mid = h_in + o; x = RMSNorm(h_mid) ----
         if (!cs.phase_begin(phase++)) return;
-        cs.residual_norm<PREC>(p.hX, &p.Lo, sh.segmask[1], p.part_o, p.hY, ly.post_norm, p.Lgu);
+        cs.residual_norm<PREC>(p.hX, &p.Lo, 1, p.part_o, p.hY, ly.post_norm, p.Lgu);
         cs.gemv_units<PREC>(p.Lgu, p.part_gu, ly.gu_s, ly.gu_b);
         cs.phase_end(phase - 1);
         // ---- down ----
         if (!cs.phase_begin(phase++)) return;
-        cs.act_prologue<PREC>(ly);
+        cs.act_prologue<PREC>();
         cs.gemv_units<PREC>(p.Ldn, p.part_dn, ly.dn_s, ly.dn_b);
         cs.phase_end(phase - 1);
     }
     // ---- final norm + LM head + argmax ----
     if (!cs.phase_begin(phase++)) return;
-    {
-        const StepLayer& pl = p.layers[p.num_layers - 1];
-        cs.residual_norm<PREC>(p.hY, &p.Ldn, sh.segmask[3], p.part_dn, nullptr, p.final_norm, p.Llm);
-    }
+    cs.residual_norm<PREC>(p.hY, &p.Ldn, 3, p.part_dn, nullptr, p.final_norm, p.Llm);
     cs.lm_head<PREC>(&p.seq->best);
     cs.phase_end(phase - 1);
     // ---- CTA 0 advances the step once every CTA folded its argmax ----
-    if (c == 0 && cs.phase_begin(phase)) {
+    if (cs.c == 0 && cs.phase_begin(phase)) {
         if (threadIdx.x == 0) {
             __threadfence();
             finish_sequence_step(*p.seq, 0, p.out_tokens, p.prompt, p.prompt_stride);
             *p.bar = 0u;  // every CTA has passed its last barrier read
         }
+    }
+}
+
+template <int PREC, int G, int D>
+__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    Shared sh;
+    sh.full = reinterpret_cast<uint64_t*>(smem);
+    sh.empty = sh.full + kMaxSlots;
+    sh.seg = sh.empty + kMaxSlots;
+    sh.fin = sh.seg + kMaxSegs;
+    sh.valid = reinterpret_cast<int*>(sh.fin + 1);
+    sh.abort = reinterpret_cast<volatile int*>(sh.valid + kMaxSlots);
+    sh.go = sh.abort + 1;
+    sh.tmem = reinterpret_cast<uint32_t*>(const_cast<int*>(sh.go + 1));
+    sh.misc = reinterpret_cast<float*>(smem + kBarRegion);
+    sh.ring = smem + kBarRegion + kMiscFloats * 4;
+    sh.xs = reinterpret_cast<float*>(sh.ring + (size_t)p.nslots * p.slot_bytes);
+    const QLayout* Ls[5] = {&p.Lqkv, &p.Lo, &p.Lgu, &p.Ldn, &p.Llm};
+    int kmax = 0;
+    for (int i = 0; i < 5; ++i) kmax = max(kmax, Ls[i]->slabs * Ls[i]->slab_k);
+    const int xbytes = PREC == 8 ? kmax * 8 : kmax * 4;
+    sh.att = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sh.xs) + xbytes);
+    sh.hs = sh.att + att_floats(G, D, p.Hkv, p.A);
+    {
+        uint8_t* t = reinterpret_cast<uint8_t*>(sh.hs + max(2 * p.H, p.Ldn.Kp));
+        for (int i = 0; i < 4; ++i) {
+            const int nrb = Ls[i]->Np / unit_rows(PREC);
+            sh.seglist[i] = t;
+            sh.segcnt[i] = t + nrb * kMaxTileSegs;
+            t += seg_table_bytes(*Ls[i]);
+        }
+    }
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int C = gridDim.x, c = blockIdx.x;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.nslots; ++i) {
+            mbar_init(&sh.full[i], 1);
+            mbar_init(&sh.empty[i], 1);
+        }
+        for (int i = 0; i < kMaxSegs; ++i) mbar_init(&sh.seg[i], 1);
+        mbar_init(sh.fin, 1);
+        *sh.abort = 0;
+        *sh.go = 1;
+        fence_barrier_init();
+    }
+    if (PREC == 8 && warp == 0) tmem_alloc(sh.tmem, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    const int pos = p.seq->pos;
+    const int npages = pos / kPageTokens + 1;
+    const int A = p.A;
+    const int head = c < A * p.Hkv ? c / A : -1;
+    const int split = c < A * p.Hkv ? c % A : 0;
+    const int pps = (npages + A - 1) / A;
+    const int apg0 = min(npages, split * pps), apg1 = min(npages, apg0 + pps);
+
+    if (warp == kStepConsumerWarps) {
+        if (lane == 0) {
+            Producer pr(p, sh);
+            auto range = [&](const QLayout& L, int& u0, int& u1) {
+                const int U = phase_units(L);
+                u0 = (int)((long long)c * U / C);
+                u1 = (int)((long long)(c + 1) * U / C);
+            };
+            int u0, u1;
+            for (int l = 0; l < p.num_layers && !pr.dead; ++l) {
+                const StepLayer& ly = p.layers[l];
+                range(p.Lqkv, u0, u1);
+                pr.gemv<PREC>(p.Lqkv, ly.qkv_w, ly.qkv_s, u0, u1);
+                if (head >= 0) pr.attention(l, head, apg0, apg1);
+                range(p.Lo, u0, u1);
+                pr.gemv<PREC>(p.Lo, ly.o_w, ly.o_s, u0, u1);
+                range(p.Lgu, u0, u1);
+                pr.gemv<PREC>(p.Lgu, ly.gu_w, ly.gu_s, u0, u1);
+                range(p.Ldn, u0, u1);
+                pr.gemv<PREC>(p.Ldn, ly.dn_w, ly.dn_s, u0, u1);
+            }
+            if (!pr.dead) {
+                const int nrb = p.Llm.Np / unit_rows(PREC);
+                const int r0 = (int)((long long)c * nrb / C), r1 = (int)((long long)(c + 1) * nrb / C);
+                pr.gemv<PREC>(p.Llm, p.lm_w, p.lm_s, r0 * p.Llm.slabs, r1 * p.Llm.slabs);
+            }
+            if (pr.dead) pr.drain();
+        }
+        return;
+    }
+
+    Consumer cs(p, sh);
+    cs.nph = 5 * p.num_layers + 1;
+    for (int i = 0; i < 4; ++i) build_seglist(sh.seglist[i], sh.segcnt[i], *Ls[i], C, threadIdx.x, kConsumers);
+    if (PREC == 8) {
+        // digit rows 4..7 of the operand stay zero for the whole step
+        uint32_t* x = reinterpret_cast<uint32_t*>(sh.xs);
+        for (int i = threadIdx.x; i < xbytes / 4; i += kConsumers) x[i] = 0u;
+        cs.tmem = *sh.tmem;
+    }
+    cs.bar();
+    run_layers<PREC, G, D>(cs, p, pos, npages);
+
+    // Teardown: wait (bounded) for this CTA's tensor-core work, free TMEM.
+    if (PREC == 8) {
+        if (warp == 0) {
+            if (lane == 0 && cs.issued_mma) {
+                tc_commit(sh.fin);
+                (void)mbar_wait(sh.fin, 0, nullptr);
+            }
+            __syncwarp();
+        }
+        tc_fence_before();
+        cs.bar();
+        tc_fence_after();
+        if (warp == 0) tmem_dealloc(cs.tmem, kTmemCols);
     }
 }
 
@@ -1052,31 +1310,69 @@ bool supported(int prec, int G, int d) {
            (prec == 8 && ((G == 4 && d == 64) || (G == 2 && d == 64) || (G == 1 && d == 32)));
 }
 
+// Largest number of CTA segments any row block of a phase is split into.
+int max_tile_segments(const QLayout& L, int C) {
+    const int nrb = L.Np / unit_rows(L.precision), U = nrb * L.slabs;
+    int best = 0;
+    for (int rb = 0; rb < nrb; ++rb) {
+        int n = 0;
+        for (int s = 0; s < L.slabs; ++s)
+            if (s == 0 || owner_of(rb * L.slabs + s, U, C) != owner_of(rb * L.slabs + s - 1, U, C)) ++n;
+        best = std::max(best, n);
+    }
+    return best;
+}
+
+// Largest number of row blocks any CTA's unit range of a phase touches.
+int max_segments(const QLayout& L, int C, bool whole_blocks) {
+    const int nrb = L.Np / unit_rows(L.precision);
+    int best = 0;
+    for (int c = 0; c < C; ++c) {
+        int n;
+        if (whole_blocks) {
+            n = (int)((long long)(c + 1) * nrb / C) - (int)((long long)c * nrb / C);
+        } else {
+            const int U = nrb * L.slabs;
+            const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
+            n = u1 > u0 ? (u1 - 1) / L.slabs - u0 / L.slabs + 1 : 0;
+        }
+        best = std::max(best, n);
+    }
+    return best;
+}
+
 }  // namespace
 
-size_t step_smem_bytes(const StepParams& p, int* nslots, int* slot_bytes, int max_smem) {
+size_t step_smem_bytes(const StepParams& p, int grid, int* nslots, int* slot_bytes, int max_smem) {
     const int G = p.nheads / p.Hkv;
-    if (!supported(p.Lqkv.precision, G, p.d)) return 0;
-    if (p.A > 16 || (size_t)p.Hkv * G * p.A * 2 > (size_t)kMiscFloats) return 0;  // (m, l) staging in misc
-    const int slot = p.Lqkv.precision == 4 ? 16384 + 4096 : 16384;
+    const int prec = p.Lqkv.precision;
+    if (!supported(prec, G, p.d)) return 0;
+    if (p.A > 16 || (size_t)p.Hkv * G * p.A * 2 + 64 > (size_t)kMiscFloats) return 0;  // (m, l) staging in misc
+    const QLayout* Ls[5] = {&p.Lqkv, &p.Lo, &p.Lgu, &p.Ldn, &p.Llm};
+    if (prec == 8) {
+        for (int i = 0; i < 4; ++i)
+            if (max_segments(*Ls[i], grid, false) > kMaxSegs) return 0;
+        if (max_segments(p.Llm, grid, true) > kMaxSegs) return 0;
+    }
+    const int slot = prec == 4 ? 16384 + 4096 : kTcUnitBytes;
     const int att_tile = 2 * kPageTokens * p.d * 4;
     const int sbytes = std::max(slot, att_tile);
-    const int xfloats = std::max(std::max(std::max(p.Lqkv.slabs * p.Lqkv.slab_k, p.Lo.slabs * p.Lo.slab_k),
-                                          std::max(p.Lgu.slabs * p.Lgu.slab_k, p.Ldn.slabs * p.Ldn.slab_k)),
-                                 p.Llm.slabs * p.Llm.slab_k);
+    int kmax = 0;
+    for (const QLayout* L : Ls) kmax = std::max(kmax, L->slabs * L->slab_k);
+    const size_t xbytes = (size_t)kmax * (prec == 8 ? 8 : 4);
     const size_t att = (size_t)std::max(G * p.d + 2 * p.d + 2 * G * kPageTokens, p.Hkv * G * p.A) * 4;
     size_t tabs = 0;
-    for (const QLayout* L : {&p.Lqkv, &p.Lo, &p.Lgu, &p.Ldn}) {
-        if (L->slabs > 32) return 0;  // segment masks are 32-bit
-        tabs += (size_t)(L->Np / 32 + 3) / 4 * 4 * 4;
+    for (int i = 0; i < 4; ++i) {
+        tabs += (size_t)seg_table_bytes(*Ls[i]);
+        if (max_tile_segments(*Ls[i], grid) > kMaxTileSegs) return 0;
     }
-    const size_t rows = (size_t)kStepConsumerWarps * kRowBlocksCached * 8 * 4;
-    const size_t fixed =
-        kBarRegion + kMiscFloats * 4 + (size_t)xfloats * 4 + att + (size_t)2 * p.H * 4 + tabs + rows;
+    // staging: [2][H] residual + norm weights; combined ctx / act values of a CTA's units
+    const size_t stage = (size_t)std::max(2 * p.H, p.Ldn.Kp) * 4;
+    const size_t fixed = kBarRegion + kMiscFloats * 4 + xbytes + att + stage + tabs;
     if ((size_t)max_smem <= fixed + 2 * (size_t)sbytes) return 0;
     int ns = (int)((max_smem - fixed) / sbytes);
     ns = std::min(ns, kMaxSlots);
-    ns = std::min(ns, 10);  // leave L1 room for the few register spills
+    ns = std::min(ns, 10);
     if (const char* e = getenv("TB_STEP_SLOTS")) ns = std::max(2, std::min(ns, atoi(e)));
     *nslots = ns;
     *slot_bytes = sbytes;
