@@ -51,8 +51,9 @@ namespace tb {
 namespace {
 
 constexpr int kMaxSlots = 24;
-constexpr int kMaxSegs = 16;                 // INT8: accumulator blocks per CTA and phase
-constexpr int kTmemCols = kMaxSegs * 8;      // 8 TMEM columns (4 digits + 4 zero) per block
+constexpr int kMaxSegs = 16;                 // INT8: segments per CTA and phase
+constexpr int kIssuers = 2;                  // INT8: threads issuing tensor-core products (alternate units)
+constexpr int kTmemCols = kMaxSegs * kIssuers * 8;  // 8 TMEM columns (4 digits + 4 zero) per block
 constexpr int kBarRegion = 1024;             // mbarriers + flags
 constexpr int kMiscFloats = 2048;
 constexpr int kConsumers = kStepConsumerWarps * 32;
@@ -62,7 +63,7 @@ struct Shared {
     uint64_t* full;
     uint64_t* empty;
     uint64_t* seg;          // [kMaxSegs] INT8 segment accumulators complete
-    uint64_t* fin;          // INT8: all tensor-core work of the CTA complete
+    uint64_t* fin;          // [kIssuers] INT8: all tensor-core work of an issuer complete
     int* valid;             // [kMaxSlots] attention tile present (page not evicted)
     volatile int* abort;    // set when a wait timed out
     volatile int* go;       // thread 0's per-phase decision
@@ -474,6 +475,7 @@ struct Consumer {
                 add[j] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
             if (Lp) reduce4<2, 10>(*Lp, which, part, n0, use, add);
+
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 if (!use[j]) continue;
@@ -537,50 +539,49 @@ struct Consumer {
     }
 
     // ---------------------------------------------------------- GEMV phases --
-    // INT8: warp 0 lane 0 issues the tensor-core products of this CTA's units;
-    // warps 4-7 read each finished segment accumulator (one tile row per
-    // thread), combine the digits, apply scale (and the bias on the segment
-    // that starts at unit 0) and store one partial per row and segment at the
-    // unit where the segment starts.
+    // INT8: lane 0 of warps 0 and 1 issue the tensor-core products of this
+    // CTA's units (alternate units: one thread's issue latency would bound the
+    // stream), each into its own accumulator block of the segment; warps 4-7
+    // read each finished segment (one tile row per thread), add the blocks,
+    // combine the digits, apply scale (and the bias on the segment that starts
+    // at unit 0) and store one partial per row and segment at the unit where
+    // the segment starts.
     __device__ void gemv_tc(const QLayout& L, float* part, const float* sc, const float* bias) {
         trace(cur_phase, 2);
         const int U = phase_units(L);
         const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
         const uint8_t* xd = reinterpret_cast<const uint8_t*>(sh.xs);
-        if (warp == 0) {
+        if (warp < kIssuers) {
             if (lane == 0 && u1 > u0) {
-                const long long lc0 = p.trace ? clock64() : 0;
-                const uint64_t lt0 = p.trace ? global_timer_ns() : 0;
                 Cursor q = rc;
-                int s = u0 % L.slabs, sfirst = s, j = 0;
+                int s = u0 % L.slabs, j = 0;
+                bool fresh = true;  // next product of this issuer starts its block of the segment
                 tc_fence_after();
                 for (int u = u0; u < u1; ++u) {
                     if (*sh.abort) break;
-                    const long long w0 = p.trace ? clock64() : 0;
-                    if (!mbar_wait(&sh.full[q.st], q.ph, p.err)) {
-                        *sh.abort = 1;
-                        break;
+                    if (((u - u0) & (kIssuers - 1)) == warp) {
+                        const long long w0 = p.trace ? clock64() : 0;
+                        if (!mbar_wait(&sh.full[q.st], q.ph, p.err)) {
+                            *sh.abort = 1;
+                            break;
+                        }
+                        const long long d0 = p.trace ? clock64() : 0;
+                        if (p.trace) waited += d0 - w0;
+                        tc_fence_after();
+                        tc_unit_mma(tmem + 8 * (kIssuers * j + warp), smem_u32(sh.ring + (size_t)q.st * p.slot_bytes),
+                                    smem_u32(xd + (size_t)s * (kTcUnitK / 16) * 128), 8, !fresh);
+                        tc_commit(&sh.empty[q.st]);
+                        issued_mma = true;
+                        fresh = false;
+                        if (p.trace) dotted += clock64() - d0;
                     }
-                    if (p.trace) waited += clock64() - w0;
-                    tc_fence_after();
-                    tc_unit_mma(tmem + 8 * j, smem_u32(sh.ring + (size_t)q.st * p.slot_bytes),
-                                smem_u32(xd + (size_t)s * (kTcUnitK / 16) * 128), 8, s != sfirst);
-                    tc_commit(&sh.empty[q.st]);
-                    issued_mma = true;
                     q.next(p.nslots);
                     if (u + 1 == u1 || s + 1 == L.slabs) {
                         tc_commit(&sh.seg[j]);
                         ++j;
+                        fresh = true;
                     }
-                    if (++s == L.slabs) {
-                        s = 0;
-                        sfirst = 0;
-                    }
-                }
-                if (p.trace) {
-                    unsigned long long* t = p.trace + ((size_t)c * nph + cur_phase) * 8;
-                    t[6] = clock64() - lc0;
-                    t[7] = global_timer_ns() - lt0;
+                    if (++s == L.slabs) s = 0;
                 }
             }
             __syncwarp();
@@ -599,9 +600,15 @@ struct Consumer {
                 const bool ok = !*sh.abort && mbar_wait(&sh.seg[j], par, p.err);
                 if (!ok) *sh.abort = 1;
                 tc_fence_after();
-                int d[8];
-                tmem_ld8(tmem + lane_base + 8 * j, d);
+                int d[8], e[8];
+                tmem_ld8(tmem + lane_base + 8 * (kIssuers * j), d);
+                tmem_ld8(tmem + lane_base + 8 * (kIssuers * j + 1), e);
                 tmem_ld_wait();
+                // block 1 holds data only if the segment has a unit at odd position
+                const bool two = uend - u >= 2 || ((u - u0) & 1);
+                const bool one = uend - u >= 2 || !((u - u0) & 1);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) d[i] = (one ? d[i] : 0) + (two ? e[i] : 0);
                 if (ok) {
                     float v = __fmul_rn(combine_digits(d, xexp), scv);
                     if (bias && sfirst == 0) v = __fadd_rn(v, bv);
@@ -879,19 +886,21 @@ struct Consumer {
             ml[e] = make_float2(__ldcg(q), __ldcg(q + 1));
         }
         bar();
-        for (int e = ctid; e < p.Hkv * G; e += kConsumers) {
+        // weights of the splits: 16 lanes per (kv head, query head) pair, one split each
+        for (int base = 0; base < p.Hkv * G * 16; base += kConsumers) {
+            const int e = (base + ctid) >> 4, sp = ctid & 15;
+            const bool live = e < p.Hkv * G && sp < A;
             const int hk = e / G, g = e % G;
-            float M = -INFINITY;
-            for (int sp = 0; sp < A; ++sp) M = fmaxf(M, ml[(hk * A + sp) * G + g].x);
-            float den = 0.0f;
-            for (int sp = 0; sp < A; ++sp) {
-                const float2 t = ml[(hk * A + sp) * G + g];
-                const float w = (t.x == -INFINITY || M == -INFINITY) ? 0.0f : expf(t.x - M);
-                wts[e * A + sp] = w;
-                den = fmaf(w, t.y, den);
-            }
+            const float2 t = live ? ml[(hk * A + sp) * G + g] : make_float2(-INFINITY, 0.0f);
+            float M = t.x;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            const float w = (t.x == -INFINITY || M == -INFINITY) ? 0.0f : expf(t.x - M);
+            float den = w * t.y;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
             const float inv = den > 0.0f ? 1.0f / den : 0.0f;
-            for (int sp = 0; sp < A; ++sp) wts[e * A + sp] *= inv;
+            if (live) wts[e * A + sp] = w * inv;
         }
         bar();
         mark(5);
@@ -992,21 +1001,27 @@ struct Consumer {
         const int nt = L.Np / kTcTileRows;
         const int t0 = (int)((long long)c * nt / C), t1 = (int)((long long)(c + 1) * nt / C);
         const uint8_t* xd = reinterpret_cast<const uint8_t*>(sh.xs);
-        if (warp == 0) {
+        if (warp < kIssuers) {
             if (lane == 0 && t1 > t0) {
                 Cursor q = rc;
                 tc_fence_after();
+                int v = 0;  // unit position in this CTA's range
                 for (int t = t0; t < t1 && !*sh.abort; ++t) {
-                    for (int s = 0; s < L.slabs; ++s) {
-                        if (!mbar_wait(&sh.full[q.st], q.ph, p.err)) {
-                            *sh.abort = 1;
-                            break;
+                    bool fresh = true;
+                    for (int s = 0; s < L.slabs; ++s, ++v) {
+                        if ((v & (kIssuers - 1)) == warp) {
+                            if (!mbar_wait(&sh.full[q.st], q.ph, p.err)) {
+                                *sh.abort = 1;
+                                break;
+                            }
+                            tc_fence_after();
+                            tc_unit_mma(tmem + 8 * (kIssuers * (t - t0) + warp),
+                                        smem_u32(sh.ring + (size_t)q.st * p.slot_bytes),
+                                        smem_u32(xd + (size_t)s * (kTcUnitK / 16) * 128), 8, !fresh);
+                            tc_commit(&sh.empty[q.st]);
+                            issued_mma = true;
+                            fresh = false;
                         }
-                        tc_fence_after();
-                        tc_unit_mma(tmem + 8 * (t - t0), smem_u32(sh.ring + (size_t)q.st * p.slot_bytes),
-                                    smem_u32(xd + (size_t)s * (kTcUnitK / 16) * 128), 8, s > 0);
-                        tc_commit(&sh.empty[q.st]);
-                        issued_mma = true;
                         q.next(p.nslots);
                     }
                     if (*sh.abort) break;
@@ -1029,9 +1044,15 @@ struct Consumer {
                 const bool ok = !*sh.abort && mbar_wait(&sh.seg[j], par, p.err);
                 if (!ok) *sh.abort = 1;
                 tc_fence_after();
-                int d[8];
-                tmem_ld8(tmem + lane_base + 8 * j, d);
+                int d[8], e[8];
+                tmem_ld8(tmem + lane_base + 8 * (kIssuers * j), d);
+                tmem_ld8(tmem + lane_base + 8 * (kIssuers * j + 1), e);
                 tmem_ld_wait();
+                const int v0 = j * L.slabs;  // position of the tile's first unit
+                const bool one = L.slabs >= 2 || !(v0 & 1);
+                const bool two = L.slabs >= 2 || (v0 & 1);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) d[i] = (one ? d[i] : 0) + (two ? e[i] : 0);
                 if (ok && inr) {
                     float lv = __fmul_rn(combine_digits(d, xexp), scv);
                     if (p.lm_b) lv = __fadd_rn(lv, bv);
@@ -1178,7 +1199,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     sh.empty = sh.full + kMaxSlots;
     sh.seg = sh.empty + kMaxSlots;
     sh.fin = sh.seg + kMaxSegs;
-    sh.valid = reinterpret_cast<int*>(sh.fin + 1);
+    sh.valid = reinterpret_cast<int*>(sh.fin + kIssuers);
     sh.abort = reinterpret_cast<volatile int*>(sh.valid + kMaxSlots);
     sh.go = sh.abort + 1;
     sh.tmem = reinterpret_cast<uint32_t*>(const_cast<int*>(sh.go + 1));
@@ -1208,8 +1229,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             mbar_init(&sh.full[i], 1);
             mbar_init(&sh.empty[i], 1);
         }
-        for (int i = 0; i < kMaxSegs; ++i) mbar_init(&sh.seg[i], 1);
-        mbar_init(sh.fin, 1);
+        for (int i = 0; i < kMaxSegs; ++i) mbar_init(&sh.seg[i], kIssuers);
+        for (int i = 0; i < kIssuers; ++i) mbar_init(&sh.fin[i], 1);
         *sh.abort = 0;
         *sh.go = 1;
         fence_barrier_init();
@@ -1272,10 +1293,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
     // Teardown: wait (bounded) for this CTA's tensor-core work, free TMEM.
     if (PREC == 8) {
-        if (warp == 0) {
+        if (warp < kIssuers) {
             if (lane == 0 && cs.issued_mma) {
-                tc_commit(sh.fin);
-                (void)mbar_wait(sh.fin, 0, nullptr);
+                tc_commit(&sh.fin[warp]);
+                (void)mbar_wait(&sh.fin[warp], 0, nullptr);
             }
             __syncwarp();
         }

@@ -108,31 +108,32 @@ __device__ __forceinline__ int digit_exponent(float max_abs) {
     // may round up across a power of two; that only makes e larger (still safe).
     return e;
 }
-// Four digits of u = x * 2^-e (|u| < 127), returned as the four bytes of a word.
-__device__ __forceinline__ void split_digits(float x, float inv_scale, int (&d)[kTcDigits]) {
-    float u = x * inv_scale;  // exact: power-of-two scaling
-#pragma unroll
-    for (int j = 0; j < kTcDigits; ++j) {
-        const float r = rintf(u);
-        d[j] = (int)r;
-        u = (u - r) * 128.0f;  // exact
-    }
-}
 // Digit words of four consecutive k (k0 % 4 == 0) of batch row m, written to
 // the B operand: word j = bytes (d_j(x0), d_j(x1), d_j(x2), d_j(x3)).
+// Round-to-integer by the 1.5 * 2^23 magic constant (IEEE round-to-nearest-
+// even, the same rounding as rintf): t = u + M holds rint(u) in its low
+// mantissa bits, so the digit byte is the low byte of t's bit pattern; the
+// remainder u' = 128 u - 128 (t - M) is computed exactly by two FMAs.
 __device__ __forceinline__ void put_digits4(uint8_t* xd, int nb, int k0_rel, int m, float4 v, float inv_scale) {
-    int a[kTcDigits], b[kTcDigits], c[kTcDigits], e[kTcDigits];
-    split_digits(v.x, inv_scale, a);
-    split_digits(v.y, inv_scale, b);
-    split_digits(v.z, inv_scale, c);
-    split_digits(v.w, inv_scale, e);
+    constexpr float kM = 12582912.0f;  // 1.5 * 2^23
+    const float2 sc = make_float2(inv_scale, inv_scale);
+    float2 u01 = __fmul2_rn(make_float2(v.x, v.y), sc);  // exact: power-of-two scaling
+    float2 u23 = __fmul2_rn(make_float2(v.z, v.w), sc);
     uint8_t* base = xd + (size_t)(k0_rel >> 4) * nb * 16 + (k0_rel & 15);
 #pragma unroll
     for (int j = 0; j < kTcDigits; ++j) {
+        const float2 t01 = __fadd2_rn(u01, make_float2(kM, kM));
+        const float2 t23 = __fadd2_rn(u23, make_float2(kM, kM));
+        const uint32_t lo = prmt(__float_as_uint(t01.x), __float_as_uint(t01.y), 0x0040u);
+        const uint32_t hi = prmt(__float_as_uint(t23.x), __float_as_uint(t23.y), 0x0040u);
         const int row = m * kTcDigits + j;
-        const uint32_t w = (uint32_t)(a[j] & 0xFF) | ((uint32_t)(b[j] & 0xFF) << 8) | ((uint32_t)(c[j] & 0xFF) << 16) |
-                           ((uint32_t)(e[j] & 0xFF) << 24);
-        *reinterpret_cast<uint32_t*>(base + ((row >> 3) * 128) + (row & 7) * 16) = w;
+        *reinterpret_cast<uint32_t*>(base + ((row >> 3) * 128) + (row & 7) * 16) = prmt(lo, hi, 0x5410u);
+        if (j + 1 < kTcDigits) {
+            const float2 n01 = __ffma2_rn(t01, make_float2(-128.0f, -128.0f), make_float2(128.0f * kM, 128.0f * kM));
+            const float2 n23 = __ffma2_rn(t23, make_float2(-128.0f, -128.0f), make_float2(128.0f * kM, 128.0f * kM));
+            u01 = __ffma2_rn(u01, make_float2(128.0f, 128.0f), n01);
+            u23 = __ffma2_rn(u23, make_float2(128.0f, 128.0f), n23);
+        }
     }
 }
 // Combined accumulator of one batch row: digits at columns 4m .. 4m+3.
