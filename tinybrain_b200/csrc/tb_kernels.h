@@ -234,6 +234,15 @@ struct StepParams {
     int nslots, slot_bytes;
     int nflight;                // producer copies in flight at most
     unsigned long long* trace;  // optional [C][phases][8] diagnostics
+    // dataflow step (tb_flow.cu): 64-bit (fp32 bits, tag) words
+    int flow;                            // 1: launch the dataflow kernel
+    uint64_t* f_h[2];                    // residual stream h_in, h_mid [H]
+    uint64_t* f_ss[2];                   // per-CTA sums of h^2 [C]
+    uint64_t *f_qkv, *f_o, *f_gu, *f_dn;  // split-K partials [units][Np]
+    uint64_t* f_att;                     // attention partials [Hkv][A][G][d + 2]
+    uint64_t *f_dbqkv, *f_dbgu;          // segment doorbells [row blocks][units]
+    unsigned int* f_epoch;               // steps completed (tag base)
+    unsigned int* f_ticket;              // LM-head completion counter, zero between steps
 };
 
 constexpr int kStepConsumerWarps = 8;
@@ -242,6 +251,11 @@ constexpr int kStepThreads = (kStepConsumerWarps + 1) * 32;
 // Shared memory a launch needs (and its ring geometry), or 0 if unsupported.
 size_t step_smem_bytes(const StepParams& p, int grid, int* nslots, int* slot_bytes, int max_smem);
 cudaError_t launch_decode_step(const StepParams& p, int grid, size_t smem, cudaStream_t stream);
+// Dataflow variant (INT8 only); 0 if unsupported.
+size_t flow_smem_bytes(const StepParams& p, int grid, int* nslots, int* slot_bytes, int max_smem);
+cudaError_t launch_decode_flow(const StepParams& p, int grid, size_t smem, cudaStream_t stream);
+// Phases per step of a launch (diagnostic trace rows).
+inline int step_phases(const StepParams& p) { return p.flow ? 7 * p.num_layers + 2 : 5 * p.num_layers + 1; }
 
 // Record the calling thread's last-error message (tb_last_error); returns status.
 int report_error(int status, const char* fmt, ...);

@@ -236,6 +236,7 @@ struct tb_runner {
     int step_grid = 0;
     size_t step_smem = 0;
     DevBuf step_layers, part_qkv, part_o, part_gu, part_dn, step_attn, hX, hY, step_bar, step_trace;
+    DevBuf flow_buf;  // dataflow step: tagged words + epoch / ticket
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     ~tb_runner() {
         if (graph) cudaGraphExecDestroy(graph);
@@ -1214,7 +1215,13 @@ static tb_status build_step(tb_runner* r) {
     int max_smem = 0;
     TB_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, r->ctx->device));
     int ns = 0, sb = 0;
-    const size_t smem = step_smem_bytes(p, C, &ns, &sb, max_smem - 1024);
+    size_t smem = 0;
+    // INT8: the dataflow kernel (tagged words, no grid barriers) unless disabled
+    const char* sel = getenv("TB_STEP_KERNEL");
+    const bool try_flow = prec == 8 && !(sel && std::string(sel) == "barrier");
+    if (try_flow) smem = flow_smem_bytes(p, C, &ns, &sb, max_smem - 1024);
+    p.flow = smem > 0 ? 1 : 0;
+    if (!p.flow) smem = step_smem_bytes(p, C, &ns, &sb, max_smem - 1024);
     if (smem == 0) return ok();
     TB_CUDA(r->step_layers.alloc(hl.size() * sizeof(StepLayer)));
     TB_CUDA(cudaMemcpy(r->step_layers.p, hl.data(), hl.size() * sizeof(StepLayer), cudaMemcpyHostToDevice));
@@ -1237,6 +1244,43 @@ static tb_status build_step(tb_runner* r) {
     p.hX = r->hX.as<float>();
     p.hY = r->hY.as<float>();
     p.bar = r->step_bar.as<unsigned int>();
+    if (p.flow) {
+        // tagged words start at tag 0, which no step produces
+        const int H = c.hidden_dim;
+        size_t off[12], total = 0;
+        const size_t words[11] = {(size_t)H,
+                                 (size_t)H,
+                                 (size_t)C,
+                                 (size_t)C,
+                                 (size_t)p.Lqkv.slabs * p.Lqkv.Np,
+                                 (size_t)p.Lo.slabs * p.Lo.Np,
+                                 (size_t)p.Lgu.slabs * p.Lgu.Np,
+                                 (size_t)p.Ldn.slabs * p.Ldn.Np,
+                                 (size_t)c.num_kv_heads * p.A * G * (m->head_dim + 2),
+                                 (size_t)(p.Lqkv.Np / p.Lqkv.RB) * p.Lqkv.slabs,
+                                 (size_t)(p.Lgu.Np / p.Lgu.RB) * p.Lgu.slabs};
+        for (int i = 0; i < 11; ++i) {
+            off[i] = total;
+            total += (words[i] + 1) / 2 * 2;  // 16-byte aligned sections
+        }
+        off[11] = total;
+        TB_CUDA(r->flow_buf.alloc(total * 8 + 64));
+        TB_CUDA(cudaMemset(r->flow_buf.p, 0, total * 8 + 64));
+        uint64_t* b = r->flow_buf.as<uint64_t>();
+        p.f_h[0] = b + off[0];
+        p.f_h[1] = b + off[1];
+        p.f_ss[0] = b + off[2];
+        p.f_ss[1] = b + off[3];
+        p.f_qkv = b + off[4];
+        p.f_o = b + off[5];
+        p.f_gu = b + off[6];
+        p.f_dn = b + off[7];
+        p.f_att = b + off[8];
+        p.f_dbqkv = b + off[9];
+        p.f_dbgu = b + off[10];
+        p.f_epoch = reinterpret_cast<unsigned int*>(b + off[11]);
+        p.f_ticket = p.f_epoch + 1;
+    }
     p.err = r->ctx->err.as<int>();
     p.nslots = ns;
     p.slot_bytes = sb;
@@ -1902,7 +1946,7 @@ extern "C" tb_status tb_runner_trace_step(tb_runner* r, uint64_t* out, int64_t n
     TB_CHECK(r && out && ctas && phases, "NULL argument");
     TB_CHECK(r->persistent, "tracing needs the persistent step");
     TB_CUDA(cudaSetDevice(r->ctx->device));
-    const int nph = 5 * r->m->cfg.num_layers + 1;
+    const int nph = step_phases(r->sp);
     const size_t cnt = (size_t)r->step_grid * nph * 8;
     TB_CHECK((size_t)n >= cnt, "need %zu entries", cnt);
     if (r->step_trace.bytes < cnt * 8) TB_CUDA(r->step_trace.alloc(cnt * 8));
