@@ -192,8 +192,7 @@ def run_ours(args):
     t_build = time.perf_counter()
     weights = build_model(ctx)
     runner = ModelRunner(weights, ctx, max_batch=1, max_positions=tl_config().max_seq_len)
-    if args.per_op:
-        runner.persistent = False
+    runner.persistent = bool(args.persistent)
     build_s = time.perf_counter() - t_build
     prompt = prompt_ids(args.prompt_len)
     W, K = args.warmup, args.steps
@@ -307,7 +306,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--per-op", action="store_true", help="one kernel per projection instead of the persistent step")
+    ap.add_argument("--persistent", action="store_true",
+                    help="one persistent kernel per step (TB_STEP_KERNEL=flow|barrier picks the variant) "
+                         "instead of the default per-projection launch chain")
+    ap.add_argument("--per-op", action="store_true", help="the default per-projection launch chain (kept for scripts)")
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
                     help="prompt length (default 128 = the config; shorter only for profiling captures)")
     args = ap.parse_args()

@@ -62,12 +62,14 @@ def test_toy_model_greedy_identity(ctx):
     assert_same_tokens(got, want, gaps)
 
 
-@pytest.mark.parametrize("persistent", [True, False])
+@pytest.mark.parametrize("persistent", ["flow", "barrier", False])
 @pytest.mark.parametrize("mode", ["perChannel", "int4"])
-def test_generate_greedy_identity(ctx, mode, persistent):
+def test_generate_greedy_identity(ctx, mode, persistent, monkeypatch):
+    if persistent:  # INT4 always takes the grid-barrier persistent kernel
+        monkeypatch.setenv("TB_STEP_KERNEL", persistent)
     w = small_llama(small_cfg(num_layers=3), seed=4, mode=mode)
     r = ModelRunner(w, ctx)
-    r.persistent = persistent
+    r.persistent = bool(persistent)
     o = oracle.OracleModel(w, mode=1)
     prompt = [11, 22, 33, 44, 55, 66, 77, 88, 99, 111, 222, 333, 444, 555, 666, 777, 888]
     want, gaps = o.generate_greedy(prompt, 48)
@@ -125,11 +127,16 @@ def test_unsupported_sampler_raises(ctx):
         list(r.generate_stream([1, 2], GenerationConfig(max_tokens=3, sampler=SamplerConfig(temperature=0.8))))
 
 
-def test_persistent_is_default_for_batch1_llama_only(ctx):
+def test_persistent_available_for_batch1_llama_only(ctx):
+    from tinybrain_b200._lib import TinyBrainError
     w = small_llama(small_cfg(), seed=9)
-    assert ModelRunner(w, ctx).persistent
-    assert not ModelRunner(w, ctx, max_batch=2).persistent
-    assert not ModelRunner(toy_model(), ctx).persistent
+    r = ModelRunner(w, ctx)
+    assert not r.persistent  # the per-projection launch chain is the default
+    r.persistent = True
+    assert r.persistent
+    for other in (ModelRunner(w, ctx, max_batch=2), ModelRunner(toy_model(), ctx)):
+        with pytest.raises(TinyBrainError):
+            other.persistent = True
 
 
 @pytest.mark.parametrize("shape", [dict(hidden_dim=512, num_heads=8, num_kv_heads=8, intermediate_dim=1408),
@@ -137,13 +144,15 @@ def test_persistent_is_default_for_batch1_llama_only(ctx):
                                         num_layers=1),
                                    dict(hidden_dim=2048, num_heads=32, num_kv_heads=4, intermediate_dim=5632,
                                         vocab_size=32000)])
-@pytest.mark.parametrize("mode", ["perChannel", "int4"])
-def test_persistent_other_shapes(ctx, shape, mode):
-    # MHA (G = 1), one layer with a short last slab, and the TinyLlama layer shape
+@pytest.mark.parametrize("mode,kernel", [("perChannel", "flow"), ("perChannel", "barrier"), ("int4", "barrier")])
+def test_persistent_other_shapes(ctx, shape, mode, kernel, monkeypatch):
+    # MHA (G = 1), one layer with a short last slab, and the TinyLlama layer
+    # shape; INT8 through both persistent kernels (dataflow and grid-barrier)
+    monkeypatch.setenv("TB_STEP_KERNEL", kernel)
     cfg = small_cfg(**shape)
     w = small_llama(cfg, seed=10, mode=mode)
     r = ModelRunner(w, ctx)
-    assert r.persistent
+    r.persistent = True
     o = oracle.OracleModel(w, mode=1)
     for i, tok in enumerate([3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8, 9, 7, 9, 3, 2, 3]):
         logits, _ = r.step(tok)

@@ -1290,7 +1290,11 @@ static tb_status build_step(tb_runner* r) {
     r->step_grid = C;
     refresh_step_params(r);
     r->persistent_ok = true;
-    r->persistent = true;
+    // The per-projection launch chain (CUDA graph + programmatic dependent
+    // launch) measured faster than both persistent kernels on TinyLlama-shaped
+    // batch-1 decode, so it stays the default; TB_PERSISTENT=1 flips it.
+    const char* dflt = getenv("TB_PERSISTENT");
+    r->persistent = dflt && std::string(dflt) == "1";
     return ok();
 }
 
