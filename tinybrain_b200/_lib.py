@@ -75,6 +75,7 @@ SIGNATURES = {
     "tb_qweight_free": [_P],
     "tb_matmul_quantized": [_P, _P, _I64, _P, _P],
     "tb_matmul_quantized_dev": [_P, _P, _I64, _P, _P],
+    "tb_qgemv_stream_time": [_P, _P, _I32, _P, _I64, _P, _I32, _I32, _PF],
     "tb_attention_decode": [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _P],
     "tb_paged_attention_dev": [_P, _P, _I32, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P],
     "tb_paged_attention_dev_noalloc": [_P, _P, _I32, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P],

@@ -590,6 +590,58 @@ static GemvParams plain_gemv(tb_context* ctx, const QLayout& L, const uint8_t* w
     return p;
 }
 
+// A timed stream of independent GEMVs (BASELINE config 1 measurement): one
+// CUDA graph launches every weight once (in order, programmatic dependent launch
+// between them so each kernel's weight stream overlaps its predecessor's tail);
+// the graph is replayed `reps` times after one warm-up replay.  All weights
+// share K; y must hold M x max(N).  Returns milliseconds per replay.
+extern "C" tb_status tb_qgemv_stream_time(tb_context* ctx, const tb_qweight* const* ws, int32_t n, const float* x,
+                                          int64_t M, float* y, int32_t reps, int32_t pdl, float* ms_out) {
+    TB_CHECK(ctx && ws && x && y && ms_out && n > 0 && reps > 0, "invalid argument");
+    TB_CHECK(M >= 1 && M <= 8, "M must be in [1, 8] (got %lld)", (long long)M);
+    TB_CUDA(cudaSetDevice(ctx->device));
+    for (int i = 0; i < n; ++i) {
+        TB_CHECK(ws[i], "NULL weight %d", i);
+        TB_CHECK(ws[i]->L.K == ws[0]->L.K, "weights must share K");
+    }
+    cudaStream_t st = ctx->stream;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    TB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    cudaError_t le = cudaSuccess;
+    for (int i = 0; i < n && le == cudaSuccess; ++i) {
+        GemvParams p = plain_gemv(ctx, ws[i]->L, ws[i]->w.as<uint8_t>(), ws[i]->s.as<float>(), (int)M);
+        p.src = x;
+        p.out = y;
+        le = launch_gemv(p, st, pdl != 0 && i > 0);
+    }
+    cudaError_t ce = cudaStreamEndCapture(st, &g);
+    if (le != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return cuda_fail(le, "launch_gemv");
+    }
+    TB_CUDA(ce);
+    ce = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    TB_CUDA(ce);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    ce = cudaGraphLaunch(ge, st);
+    if (ce == cudaSuccess) ce = cudaEventRecord(e0, st);
+    for (int r = 0; r < reps && ce == cudaSuccess; ++r) ce = cudaGraphLaunch(ge, st);
+    if (ce == cudaSuccess) ce = cudaEventRecord(e1, st);
+    if (ce == cudaSuccess) ce = cudaEventSynchronize(e1);
+    float ms = 0.0f;
+    if (ce == cudaSuccess) ce = cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaGraphExecDestroy(ge);
+    TB_CUDA(ce);
+    *ms_out = ms / (float)reps;
+    return tb_context_check_device(ctx);
+}
+
 extern "C" tb_status tb_matmul_quantized_dev(tb_context* ctx, const float* x, int64_t M, const tb_qweight* w,
                                              float* y) {
     TB_CHECK(ctx && x && w && y, "NULL argument");

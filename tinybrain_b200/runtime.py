@@ -214,6 +214,20 @@ class QuantizedWeight:
             pass
 
 
+def gemv_stream_time(weights: Sequence["QuantizedWeight"], x_dev: int, M: int, y_dev: int, reps: int = 20,
+                     pdl: bool = True) -> float:
+    """Milliseconds per pass of one GEMV per weight (device pointers x [M][K],
+    y [M][max N]); the single-GEMV HBM measurement of BASELINE config 1."""
+    if not weights:
+        raise ValueError("no weights")
+    ctx = weights[0].ctx
+    arr = (C.c_void_p * len(weights))(*[w.handle for w in weights])
+    ms = C.c_float(0.0)
+    call("tb_qgemv_stream_time", ctx.handle, arr, len(weights), C.c_void_p(x_dev), M, C.c_void_p(y_dev), reps,
+         int(bool(pdl)), C.byref(ms))
+    return float(ms.value)
+
+
 def attention_decode(q, keys, values, num_heads, num_kv_heads, head_dim, ctx=None) -> np.ndarray:
     """Single-query decode attention (ModelRunner.swift:519-579 semantics)."""
     ctx = ctx or Context.default()
