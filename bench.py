@@ -97,9 +97,11 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def build_model(ctx, mode="perChannel"):
-    from tinybrain_b200.synthetic import make_llama_model
-    return make_llama_model(tl_config(), seed=MODEL_SEED, mode=mode, ctx=ctx)
+def build_model(ctx, mode="perChannel", max_seq_len=None):
+    from tinybrain_b200.runtime import ModelConfig
+    from tinybrain_b200.synthetic import TINYLLAMA, make_llama_model
+    cfg = ModelConfig(**{**TINYLLAMA, **({"max_seq_len": max_seq_len} if max_seq_len else {})})
+    return make_llama_model(cfg, seed=MODEL_SEED, mode=mode, ctx=ctx)
 
 
 def prompt_ids(n=PROMPT_LEN):
@@ -190,12 +192,21 @@ def run_ours(args):
 
     ctx = Context(local)
     t_build = time.perf_counter()
-    weights = build_model(ctx)
-    runner = ModelRunner(weights, ctx, max_batch=1, max_positions=tl_config().max_seq_len)
+    cfg3 = args.config == 3
+    weights = build_model(ctx, mode="int4" if cfg3 else "perChannel")
+    # RoPE table covers the config's context plus the few extra profiling steps
+    runner = ModelRunner(weights, ctx, max_batch=1, max_positions=tl_config().max_seq_len + 64)
     runner.persistent = bool(args.persistent)
     build_s = time.perf_counter() - t_build
-    prompt = prompt_ids(args.prompt_len)
-    W, K = args.warmup, args.steps
+    if cfg3:
+        # config 3: prompt 1920 ids (seed 3), 128 greedy steps, context 1921..2048 (no eviction)
+        from tinybrain_b200.synthetic import random_prompt
+        prompt = random_prompt(args.prompt_len if args.prompt_len != PROMPT_LEN else 1920, 32000, 3)
+        W = args.warmup
+        K = min(args.steps, 128 - W)
+    else:
+        prompt = prompt_ids(args.prompt_len)
+        W, K = args.warmup, args.steps
     total_new = W + K
 
     # ---- device-resident timing (value) ----
@@ -232,7 +243,7 @@ def run_ours(args):
         extra = {}
     else:
         gm = kinds == 0
-        kern = "gemv_kernel<8,*,1> (all projections + LM head of one step)"
+        kern = ("gemv_kernel<4,*,1>" if cfg3 else "gemv_kernel<8,128,1>") + " (all projections + LM head of one step)"
         dom_bytes, dom_ms, n_dom = float(nbytes[gm].sum()), float(tmean[gm].sum()), int(gm.sum())
         extra = {"gemv_ms_per_step": dom_ms, "attention_ms_per_step": float(tmean[~gm].sum())}
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
@@ -270,9 +281,12 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": 1000.0 * t_dev / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8 weights x fp32 activations (fp32 accumulate)",
+        "dtype": ("int4-g32 weights x fp32 activations (fp32 accumulate)" if cfg3 else
+                  "int8 weights x fp32 activations (exact integer tensor-core products, fp32 epilogue)"),
         "data": "synthetic (seeded LCG normal std 0.02, uniform prompt ids)",
-        "config": {"workload": "TinyLlama-1.1B-shaped INT8, batch 1, greedy decode (BASELINE config 2)",
+        "config": {"workload": ("TinyLlama-1.1B-shaped INT4-g32, batch 1, prompt 1920, greedy decode "
+                                "(BASELINE config 3)") if cfg3 else
+                               "TinyLlama-1.1B-shaped INT8, batch 1, greedy decode (BASELINE config 2)",
                    "layers": 22, "hidden": 2048, "heads": "32q/4kv", "vocab": 32000,
                    "prompt": len(prompt), "decode_tokens": total_new, "parallelism": f"replicas x{world}",
                    "l2": "weights streamed per step (1.04 GB) exceed L2; no flush needed"},
@@ -353,6 +367,99 @@ def run_gemv_config1(args):
     return 0
 
 
+def run_config4(args):
+    """TinyLlama INT8, 64 independent sequences, prompt lengths
+    ~ U[512, 4096] and ids ~ U[0, 32000) (numpy PCG64 seed 4), 128 greedy steps
+    each, max_seq_len 4224 (no eviction).  Data parallel over the ranks: sequences
+    assigned longest-first to the least-loaded rank, one batch per GPU, no
+    collective on the data path.  value = 64 x timed steps / max over ranks."""
+    import numpy as np
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl")
+    from tinybrain_b200.runtime import Context, ModelRunner
+    n_seqs, n_new = 64, 128
+    rng = np.random.default_rng(4)
+    lens = rng.integers(512, 4097, size=n_seqs)
+    prompts = [rng.integers(0, 32000, size=int(n)).tolist() for n in lens]
+    load = [0] * world
+    mine = []
+    for i in sorted(range(n_seqs), key=lambda i: -lens[i]):
+        r = min(range(world), key=lambda q: load[q])
+        load[r] += int(lens[i])
+        if r == rank:
+            mine.append(i)
+    ctx = Context(local)
+    weights = build_model(ctx, max_seq_len=4224)  # >= 4096 + 128: no eviction
+    runner = ModelRunner(weights, ctx, max_batch=len(mine), max_positions=4224 + 64)
+    my_prompts = [prompts[i] for i in mine]
+    W = args.warmup
+    K = min(args.steps, n_new - W)
+    t0 = time.perf_counter()
+    runner.prefill_device(my_prompts, W + K)
+    prefill_s = time.perf_counter() - t0
+    runner.decode_device(W)
+    clocks = ClockSampler(local)
+    if dist:
+        dist.barrier()
+    clocks.start()
+    ms = runner.decode_device(K)
+    clk = clocks.stop()
+    t_dev = ms / 1000.0
+    if dist:
+        import torch
+        t = torch.tensor([t_dev], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_dev = float(t.item())
+    value = n_seqs * K / t_dev
+    times, kinds, nbytes = [], None, None
+    for _ in range(3):
+        t, k, b = runner.profile_step()
+        times.append(t)
+        kinds, nbytes = k, b
+    tmean = np.mean(np.stack(times[1:]), axis=0)
+    peak, peak_kind = measured_peaks()
+    gm = kinds == 0
+    parts = {"gemv": (float(nbytes[gm].sum()), float(tmean[gm].sum()), int(gm.sum())),
+             "attention": (float(nbytes[~gm].sum()), float(tmean[~gm].sum()), int((~gm).sum()))}
+    dom = max(parts, key=lambda k: parts[k][1])
+    db, dms, dn = parts[dom]
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": 1000.0 * t_dev / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8 weights x fp32 activations (exact integer tensor-core products, fp32 epilogue)",
+        "data": "synthetic (seeded LCG normal std 0.02 weights; numpy PCG64 seed 4 prompt lengths and ids)",
+        "config": {"workload": "TinyLlama-1.1B-shaped INT8, 64 sequences, prompts U[512,4096], 128 greedy steps "
+                               "(BASELINE config 4)", "parallelism": f"dp{world} (longest-first assignment)",
+                   "batch_per_gpu": len(mine), "prefill_s_rank0": round(prefill_s, 1),
+                   "l2": "weights (1.04 GB) and KV (GBs) per step exceed L2; no flush needed"},
+        "e2e": None,
+        "roofline": {"bound": "hbm", "achieved": db / (dms / 1000.0) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": db / (dms / 1000.0) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs (burst copy)",
+                     "kernel": "attn_decode_kernel (paged KV, all layers)" if dom == "attention" else
+                               "gemv_kernel<8,128,16> (all projections + LM head)",
+                     "bytes_per_launch": db / dn, "launches_per_step": dn, "ms_per_launch": dms / dn,
+                     "traffic": None,
+                     "gemv_ms_per_step": parts["gemv"][1], "attention_ms_per_step": parts["attention"][1]},
+        "gpu_launches": int(len(kinds)) * K,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -366,8 +473,9 @@ def main():
     ap.add_argument("--per-op", action="store_true", help="the default per-projection launch chain (kept for scripts)")
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
                     help="prompt length (default 128 = the config; shorter only for profiling captures)")
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2],
-                    help="BASELINE config: 2 = TinyLlama INT8 decode (default), 1 = single-GEMV HBM bandwidth")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
+                    help="BASELINE config: 2 = TinyLlama INT8 decode (default), 1 = single-GEMV HBM bandwidth, "
+                         "3 = TinyLlama INT4-g32 decode at context ~2k, 4 = 64 sequences data-parallel")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -375,6 +483,8 @@ def main():
         return run_reference(args)
     if args.config == 1:
         return run_gemv_config1(args)
+    if args.config == 4:
+        return run_config4(args)
     return run_ours(args)
 
 

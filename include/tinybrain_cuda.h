@@ -120,7 +120,7 @@ typedef struct {
 tb_status tb_qweight_upload(tb_context *ctx, const tb_qtensor_desc *desc, tb_qweight **out);
 tb_status tb_qweight_free(tb_qweight *w);
 /* QuantizedMatMulBackend.matmulQuantized (Backend.swift:173-175,
- * MetalBackend.swift:894-1048): y[M][N] = x[M][K] * dequant(W), fp32, M <= 8.
+ * MetalBackend.swift:894-1048): y[M][N] = x[M][K] * dequant(W), fp32, M <= 64.
  * Synchronous, host buffers. */
 tb_status tb_matmul_quantized(tb_context *ctx, const float *x_host, int64_t M, const tb_qweight *w,
                               float *y_host);

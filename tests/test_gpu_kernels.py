@@ -67,7 +67,8 @@ def test_gemv_cfg1(ctx, mode):
 
 
 @pytest.mark.parametrize("K,N,M", [(100, 70, 1), (48, 33, 3), (5632, 2048, 1), (2048, 5632, 2),
-                                   (11008, 4096, 1), (4096, 32000, 1), (2048, 256, 8), (1024, 512, 5)])
+                                   (11008, 4096, 1), (4096, 32000, 1), (2048, 256, 8), (1024, 512, 5),
+                                   (2048, 2560, 16), (5632, 2048, 33), (2048, 11264, 64), (200, 130, 17)])
 def test_gemv_int8_shapes(ctx, K, N, M):
     g = SeededGenerator(K * 7 + N)
     w = g.normal((K, N), 0.0, 0.02)
@@ -81,7 +82,7 @@ def test_gemv_int8_shapes(ctx, K, N, M):
 
 
 @pytest.mark.parametrize("K,N,M,gs", [(2048, 4096, 1, 32), (11008, 4096, 1, 32), (1000, 64, 1, 32),
-                                      (4096, 256, 2, 128), (5632, 2048, 1, 32)])
+                                      (4096, 256, 2, 128), (5632, 2048, 1, 32), (1024, 512, 7, 32)])
 def test_gemv_int4_shapes(ctx, K, N, M, gs):
     g = SeededGenerator(K * 3 + N)
     w = g.normal((K, N), 0.0, 0.02)

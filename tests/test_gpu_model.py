@@ -119,6 +119,35 @@ def test_batched_sequences_match_independent_runs(ctx):
         assert_same_tokens(g, want, gaps)
 
 
+@pytest.mark.parametrize("mode", ["perChannel", "int4"])
+def test_batch_of_twenty_sequences(ctx, mode):
+    # more sequences than one GEMV CTA holds (INT8 16 rows, INT4 2): batch rows
+    # are split over the grid; every sequence must match its own oracle run
+    w = small_llama(small_cfg(num_layers=2), seed=12, mode=mode)
+    r = ModelRunner(w, ctx, max_batch=20)
+    rng = np.random.default_rng(77)
+    prompts = [[int(v) for v in rng.integers(1, 200, size=1 + (i * 7) % 23)] for i in range(20)]
+    got = r.generate_batch(prompts, 12)
+    for p, gt in zip(prompts, got):
+        o = oracle.OracleModel(w, mode=1)
+        want, gaps = o.generate_greedy(p, 12)
+        assert_same_tokens(gt, want, gaps)
+
+
+def test_batched_eviction_parity(ctx):
+    # two sequences whose contexts run past max_seq_len (reference FIFO page
+    # eviction, KVCache.swift:157-224) next to a short one, decoded together
+    cfg = small_cfg(max_seq_len=48)
+    w = small_llama(cfg, seed=13)
+    r = ModelRunner(w, ctx, max_batch=3, max_positions=128)
+    prompts = [list(range(1, 41)), [7, 8, 9], list(range(50, 90))]
+    got = r.generate_batch(prompts, 30)
+    for p, gt in zip(prompts, got):
+        o = oracle.OracleModel(w, mode=1)
+        want, gaps = o.generate_greedy(p, 30)
+        assert_same_tokens(gt, want, gaps)
+
+
 def test_unsupported_sampler_raises(ctx):
     from tinybrain_b200._lib import TinyBrainError
     w = small_llama(small_cfg(), seed=8)

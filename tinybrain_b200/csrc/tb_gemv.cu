@@ -25,6 +25,7 @@
 #include "tb_tc.cuh"
 #include "tb_unit.cuh"
 
+#include <algorithm>
 #include <cstdio>
 
 namespace tb {
@@ -109,6 +110,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     const int s1 = (rank + 1) * L.slabs / P;
     const int nunits = s1 - s0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // batch rows [m0, m0 + Mloc) of this CTA (grid y splits batches larger than MB)
+    const int m0 = blockIdx.y * MB;
+    const int Mloc = min(MB, p.M - m0);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
@@ -165,20 +169,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
             if (p.prologue == kProEmbed || p.prologue == kProEmbedRms) {
-                int tok = m < p.M ? p.seq_ro[m].token : 0;
+                int tok = m < Mloc ? p.seq_ro[m0 + m].token : 0;
                 if (tok < 0 || tok >= p.vocab) {
                     record_error(p.err, kDevBadToken);
                     tok = 0;
                 }
                 srcm[m] = p.embedding + (size_t)tok * p.L.K;
             } else {
-                srcm[m] = p.src + (size_t)m * p.ld_src;
+                srcm[m] = p.src + (size_t)(m0 + m) * p.ld_src;
             }
         }
         // Embedding prologue: CTA 0 materialises the residual stream h.
         if ((p.prologue == kProEmbed || p.prologue == kProEmbedRms) && blockIdx.x == 0) {
-            for (int m = 0; m < p.M; ++m)
-                for (int k = ctid; k < L.K; k += 256) p.resid[(size_t)m * p.ld_src + k] = srcm[m][k];
+            for (int m = 0; m < Mloc; ++m)
+                for (int k = ctid; k < L.K; k += 256) p.resid[(size_t)(m0 + m) * p.ld_src + k] = srcm[m][k];
         }
         // Tensor.swift:1538-1558: ss = sum x^2; inv = 1 / sqrt(ss/H + eps).  The
         // INT8 path also needs max |x| over this CTA's k range (digit scale).
@@ -193,7 +197,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 #pragma unroll
             for (int m = 0; m < MB; ++m) {
                 float ss = 0.0f, mx = 0.0f;
-                if (m < p.M) {
+                if (m < Mloc) {
                     if (rms)
                         for (int k = ctid; k < L.K; k += 256) ss = fmaf(srcm[m][k], srcm[m][k], ss);
                     if (PREC == 8)
@@ -226,7 +230,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         }
         auto xval = [&](int m, int k) -> float {
             float v = 0.0f;
-            if (m < p.M && k < L.K) {
+            if (m < Mloc && k < L.K) {
                 v = srcm[m][k];
                 if (rms) v = __fmul_rn(__fmul_rn(v, inv[m]), p.norm_w[k]);
             }
@@ -369,13 +373,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         for (int it = ctid; it < nitems; it += 256) {
             const int m = it % MB;
             const int o = ob + it / MB;
-            if (m >= p.M) continue;
+            if (m >= Mloc) continue;
+            const int gm = m0 + m;  // batch row
             if (p.epilogue == kEpiQkv) {
                 const int n0 = rb * RB + 2 * o;
                 if (n0 >= L.N) continue;
                 const float v0 = finish(n0, rowsum(2 * o, m));
                 const float v1 = finish(n0 + 1, rowsum(2 * o + 1, m));
-                const SeqState& sq = p.seq_ro[m];
+                const SeqState& sq = p.seq_ro[gm];
                 if (!sq.active) continue;
                 const int pos = sq.pos;
                 const int d = p.head_dim;
@@ -387,12 +392,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                     const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
                     const float r1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
                     if (n0 < p.H) {
-                        p.out[(size_t)m * p.ld_out + n0] = r0;
-                        p.out[(size_t)m * p.ld_out + n0 + 1] = r1;
+                        p.out[(size_t)gm * p.ld_out + n0] = r0;
+                        p.out[(size_t)gm * p.ld_out + n0 + 1] = r1;
                         continue;
                     }
                     const int j = n0 - p.H;
-                    const int page = p.page_table[(size_t)m * p.ptab_stride + pos / kPageTokens];
+                    const int page = p.page_table[(size_t)gm * p.ptab_stride + pos / kPageTokens];
                     if (page < 0) {
                         record_error(p.err, kDevBadPage);
                         continue;
@@ -404,7 +409,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                     p.kv_pool[base * d + i + 1] = r1;
                 } else {
                     const int j = n0 - p.H - p.kv_dim;
-                    const int page = p.page_table[(size_t)m * p.ptab_stride + pos / kPageTokens];
+                    const int page = p.page_table[(size_t)gm * p.ptab_stride + pos / kPageTokens];
                     if (page < 0) {
                         record_error(p.err, kDevBadPage);
                         continue;
@@ -420,20 +425,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                 if (n >= L.N) continue;
                 const float g = finish(rb * RB + o, rowsum(o, m));
                 const float u = finish(rb * RB + HALF + o, rowsum(HALF + o, m));
-                p.out[(size_t)m * p.ld_out + n] = __fmul_rn(silu_ref(g), u);
+                p.out[(size_t)gm * p.ld_out + n] = __fmul_rn(silu_ref(g), u);
             } else {
                 const int n = rb * RB + o;
                 if (n >= L.N) continue;
                 const float v = finish(n, rowsum(o, m));
                 if (p.epilogue == kEpiStore) {
-                    p.out[(size_t)m * p.ld_out + n] = v;
+                    p.out[(size_t)gm * p.ld_out + n] = v;
                 } else if (p.epilogue == kEpiResidual) {
-                    float* dst = p.out + (size_t)m * p.ld_out + n;
+                    float* dst = p.out + (size_t)gm * p.ld_out + n;
                     *dst = __fadd_rn(*dst, v);
                 } else if (p.epilogue == kEpiGelu) {
-                    p.out[(size_t)m * p.ld_out + n] = gelu_ref(v);
+                    p.out[(size_t)gm * p.ld_out + n] = gelu_ref(v);
                 } else {  // kEpiArgmax
-                    if (p.logits) p.logits[(size_t)m * L.N + n] = v;
+                    if (p.logits) p.logits[(size_t)gm * L.N + n] = v;
                     const unsigned long long key = argmax_key(v, n);
 #pragma unroll
                     for (int mm = 0; mm < MB; ++mm)
@@ -450,13 +455,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                     unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
                     b = t > b ? t : b;
                 }
-                if (lane == 0 && b != 0ull && m < p.M) atomicMax(&p.seq[m].best, b);
+                if (lane == 0 && b != 0ull && m < Mloc) atomicMax(&p.seq[m0 + m].best, b);
             }
             named_bar_sync(1, 256);
             if (ctid == 0) {
                 __threadfence();
                 const unsigned int t = atomicAdd(p.ticket, 1u);
-                misc[0] = __int_as_float(t == gridDim.x - 1 ? 1 : 0);
+                misc[0] = __int_as_float(t == gridDim.x * gridDim.y - 1 ? 1 : 0);
             }
             named_bar_sync(1, 256);
             if (__float_as_int(misc[0]) == 1) {
@@ -495,7 +500,7 @@ cudaError_t launch_t(const GemvParams& p, cudaStream_t stream, bool pdl) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)(p.L.Np / RB * p.P), 1, 1);
+    cfg.gridDim = dim3((unsigned)(p.L.Np / RB * p.P), (unsigned)((p.M + MB - 1) / MB), 1);
     cfg.blockDim = dim3(kGemvThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -522,39 +527,31 @@ int choose_ksplit(const QLayout& L, int M, int num_sms) {
     const int nrb = L.Np / L.RB;
     int P = 1;
     // Keep the staged activation slice modest and give every SM about two CTAs.
-    const size_t per_k = L.precision == 8 ? (size_t)tc_nb(M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8) : (size_t)M * 4;
+    const int mb = L.precision == 8 ? (M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16) : std::min(M, 2);
+    const size_t per_k = L.precision == 8 ? (size_t)tc_nb(mb) : (size_t)mb * 4;
     auto xbytes = [&](int q) { return ((L.slabs + q - 1) / q) * (size_t)L.slab_k * per_k; };
-    while (P < 8 && P * 2 <= L.slabs && (nrb * P < 2 * num_sms || xbytes(P) > 48 * 1024)) P *= 2;
+    const int splits = (M + mb - 1) / mb;  // grid y
+    while (P < 8 && P * 2 <= L.slabs && (nrb * P * splits < 2 * num_sms || xbytes(P) > 48 * 1024)) P *= 2;
     while (P < L.slabs && P < 8 && xbytes(P) > 96 * 1024) ++P;
     return P;
 }
 
 cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream, bool pdl) {
     const int prec = p.L.precision, RB = p.L.RB;
-    int mb = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : 8;
-    if (p.M > 8) return cudaErrorInvalidValue;
+    // batches beyond one CTA's rows (INT8 16, INT4 2) are split over grid y
+    int mb = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : p.M <= 8 ? 8 : 16;
+    if (p.M < 1 || p.M > kMaxGemvBatch) return cudaErrorInvalidValue;
     if (prec == 8) {
         switch (mb) {
             case 1: return launch_t<8, 128, 1>(p, stream, pdl);
             case 2: return launch_t<8, 128, 2>(p, stream, pdl);
             case 4: return launch_t<8, 128, 4>(p, stream, pdl);
-            default: return launch_t<8, 128, 8>(p, stream, pdl);
+            case 8: return launch_t<8, 128, 8>(p, stream, pdl);
+            default: return launch_t<8, 128, 16>(p, stream, pdl);
         }
     }
-    if (prec == 4 && RB == 32) {
-        switch (mb) {
-            case 1: return launch_t<4, 32, 1>(p, stream, pdl);
-            case 2: return launch_t<4, 32, 2>(p, stream, pdl);
-            default: return cudaErrorNotSupported;
-        }
-    }
-    if (prec == 4 && RB == 64) {
-        switch (mb) {
-            case 1: return launch_t<4, 64, 1>(p, stream, pdl);
-            case 2: return launch_t<4, 64, 2>(p, stream, pdl);
-            default: return cudaErrorNotSupported;
-        }
-    }
+    if (prec == 4 && RB == 32) return mb == 1 ? launch_t<4, 32, 1>(p, stream, pdl) : launch_t<4, 32, 2>(p, stream, pdl);
+    if (prec == 4 && RB == 64) return mb == 1 ? launch_t<4, 64, 1>(p, stream, pdl) : launch_t<4, 64, 2>(p, stream, pdl);
     return cudaErrorInvalidValue;
 }
 

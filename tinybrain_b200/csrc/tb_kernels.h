@@ -44,6 +44,7 @@ enum DeviceError : int {
 constexpr int kSlabBytes = 512;
 constexpr int kGemvConsumerWarps = 8;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;  // + 1 producer warp
+constexpr int kMaxGemvBatch = 64;  // batch rows of one GEMV launch (grid y splits rows beyond a CTA's)
 
 struct QLayout {
     int precision;       // 8 or 4

@@ -223,6 +223,7 @@ struct tb_runner {
     std::vector<SeqKV> kvh;
     std::vector<int> free_pages;  // LIFO
     std::vector<int> ptab_host;
+    std::vector<cudaEvent_t> ptab_ev;  // last upload from each sequence's pinned staging row
     std::vector<char> ptab_dirty;
     PinnedBuf pin_ptab, pin_tokens, pin_seq;
     // step plan + graph
@@ -239,6 +240,8 @@ struct tb_runner {
     DevBuf flow_buf;  // dataflow step: tagged words + epoch / ticket
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     ~tb_runner() {
+        for (cudaEvent_t e : ptab_ev)
+            if (e) cudaEventDestroy(e);
         if (graph) cudaGraphExecDestroy(graph);
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
@@ -598,7 +601,7 @@ static GemvParams plain_gemv(tb_context* ctx, const QLayout& L, const uint8_t* w
 extern "C" tb_status tb_qgemv_stream_time(tb_context* ctx, const tb_qweight* const* ws, int32_t n, const float* x,
                                           int64_t M, float* y, int32_t reps, int32_t pdl, float* ms_out) {
     TB_CHECK(ctx && ws && x && y && ms_out && n > 0 && reps > 0, "invalid argument");
-    TB_CHECK(M >= 1 && M <= 8, "M must be in [1, 8] (got %lld)", (long long)M);
+    TB_CHECK(M >= 1 && M <= kMaxGemvBatch, "M must be in [1, %d] (got %lld)", kMaxGemvBatch, (long long)M);
     TB_CUDA(cudaSetDevice(ctx->device));
     for (int i = 0; i < n; ++i) {
         TB_CHECK(ws[i], "NULL weight %d", i);
@@ -645,7 +648,8 @@ extern "C" tb_status tb_qgemv_stream_time(tb_context* ctx, const tb_qweight* con
 extern "C" tb_status tb_matmul_quantized_dev(tb_context* ctx, const float* x, int64_t M, const tb_qweight* w,
                                              float* y) {
     TB_CHECK(ctx && x && w && y, "NULL argument");
-    TB_CHECK(M >= 1 && M <= 8, "M must be in [1, 8] for the decode GEMV (got %lld)", (long long)M);
+    TB_CHECK(M >= 1 && M <= kMaxGemvBatch, "M must be in [1, %d] for the decode GEMV (got %lld)", kMaxGemvBatch,
+             (long long)M);
     TB_CUDA(cudaSetDevice(ctx->device));
     GemvParams p = plain_gemv(ctx, w->L, w->w.as<uint8_t>(), w->s.as<float>(), (int)M);
     p.src = x;
@@ -657,7 +661,8 @@ extern "C" tb_status tb_matmul_quantized_dev(tb_context* ctx, const float* x, in
 extern "C" tb_status tb_matmul_quantized(tb_context* ctx, const float* x, int64_t M, const tb_qweight* w,
                                          float* y) {
     TB_CHECK(ctx && x && w && y, "NULL argument");
-    TB_CHECK(M >= 1 && M <= 8, "M must be in [1, 8] for the decode GEMV (got %lld)", (long long)M);
+    TB_CHECK(M >= 1 && M <= kMaxGemvBatch, "M must be in [1, %d] for the decode GEMV (got %lld)", kMaxGemvBatch,
+             (long long)M);
     TB_CUDA(cudaSetDevice(ctx->device));
     const size_t xb = (size_t)M * w->L.K * 4, yb = (size_t)M * w->L.N * 4;
     tb_status s = ensure(ctx->io_a, xb);
@@ -1381,7 +1386,8 @@ extern "C" tb_status tb_runner_create(tb_model* m, int32_t max_batch, int32_t ma
     TB_CHECK(m && out, "NULL argument");
     *out = nullptr;
     TB_CHECK(m->finalized, "model not finalized");
-    TB_CHECK(max_batch >= 1 && max_batch <= 8, "max_batch must be in [1, 8] (got %d)", max_batch);
+    TB_CHECK(max_batch >= 1 && max_batch <= kMaxGemvBatch, "max_batch must be in [1, %d] (got %d)", kMaxGemvBatch,
+             max_batch);
     tb_context* ctx = m->ctx;
     TB_CUDA(cudaSetDevice(ctx->device));
     const tb_model_config& c = m->cfg;
@@ -1506,12 +1512,19 @@ static tb_status kv_prepare(tb_runner* r, int s) {
 }
 
 static tb_status flush_ptab(tb_runner* r) {
+    if (r->ptab_ev.size() != (size_t)r->B) r->ptab_ev.assign(r->B, nullptr);
     for (int s = 0; s < r->B; ++s) {
         if (!r->ptab_dirty[s]) continue;
         int* pin = r->pin_ptab.as<int>() + (size_t)s * r->ptab_stride;
+        // The previous upload from this staging row may still be queued behind
+        // earlier steps: wait for it before overwriting the row, or an older
+        // step would read a newer table (with pages evicted after it).
+        if (r->ptab_ev[s]) TB_CUDA(cudaEventSynchronize(r->ptab_ev[s]));
         memcpy(pin, r->ptab_host.data() + (size_t)s * r->ptab_stride, (size_t)r->ptab_stride * 4);
         TB_CUDA(cudaMemcpyAsync(r->ptab.as<int>() + (size_t)s * r->ptab_stride, pin, (size_t)r->ptab_stride * 4,
                                 cudaMemcpyHostToDevice, r->ctx->stream));
+        if (!r->ptab_ev[s]) TB_CUDA(cudaEventCreateWithFlags(&r->ptab_ev[s], cudaEventDisableTiming));
+        TB_CUDA(cudaEventRecord(r->ptab_ev[s], r->ctx->stream));
         r->h2d_bytes += (int64_t)r->ptab_stride * 4;
         r->ptab_dirty[s] = 0;
     }
