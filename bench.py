@@ -387,6 +387,8 @@ def run_config4(args):
     n_seqs, n_new = 64, 128
     rng = np.random.default_rng(4)
     lens = rng.integers(512, 4097, size=n_seqs)
+    if args.prompt_len != PROMPT_LEN:  # profiling captures only: cap the prompt lengths
+        lens = np.minimum(lens, args.prompt_len)
     prompts = [rng.integers(0, 32000, size=int(n)).tolist() for n in lens]
     load = [0] * world
     mine = []

@@ -97,7 +97,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     float* red = reinterpret_cast<float*>(smem + 256);                    // [RB][MB]
     float* misc = red + RB * MB;                                          // [2][MB][8]
-    uint8_t* stage_base = smem + (256 + (RB * MB + 16 * MB) * 4 + 1023) / 1024 * 1024;
+    float* rowsc = misc + 16 * MB;                                        // [RB] row scales (1 for INT4)
+    float* rowbias = rowsc + RB;                                          // [RB] row biases (0 if none)
+    int* seqinfo = reinterpret_cast<int*>(rowbias + RB);                  // [3][MB] pos, active, page
+    uint8_t* stage_base = smem + (256 + (RB * MB + 16 * MB + 2 * RB + 3 * MB) * 4 + 1023) / 1024 * 1024;
     uint8_t* xbuf = stage_base + STAGES * Cfg::kStageBytes;
     float* xs = reinterpret_cast<float*>(xbuf);   // INT4: lane-interleaved fp32 activations
     uint8_t* xd = xbuf;                           // INT8: digit operand [k/16][NB][16]
@@ -122,7 +125,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         mbar_init(done, 1);
         fence_barrier_init();
     }
-    if (PREC == 8 && warp == 0) tmem_alloc(tmem_slot, 32);
+    // accumulator: NB int32 columns (4 digit rows per batch row); allocation is a power of two >= 32
+    constexpr uint32_t kTmemCols = NB <= 32 ? 32u : NB <= 64 ? 64u : NB <= 128 ? 128u : 256u;
+    static_assert(PREC != 8 || NB <= 256, "tcgen05 N is at most 256");
+    if (PREC == 8 && warp == 0) tmem_alloc(tmem_slot, kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -157,8 +163,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         }
     } else {
         // ------------------------------- consumers -------------------------------
-        pdl_wait();
         const int ctid = threadIdx.x;  // 0..255
+        // weights-side epilogue constants do not depend on the previous kernel
+        for (int i = ctid; i < RB; i += 256) {
+            const int grow = rb * RB + i;
+            rowsc[i] = PREC == 8 ? __ldg(p.scales + grow) : 1.0f;
+            rowbias[i] = p.bias ? __ldg(p.bias + grow) : 0.0f;
+        }
+        pdl_wait();
+        if (p.epilogue == kEpiQkv && ctid < Mloc) {
+            const SeqState& sq = p.seq_ro[m0 + ctid];
+            const int pos = sq.pos;
+            seqinfo[ctid] = pos;
+            seqinfo[MB + ctid] = sq.active;
+            seqinfo[2 * MB + ctid] = sq.active ? p.page_table[(size_t)(m0 + ctid) * p.ptab_stride + pos / kPageTokens] : -1;
+        }
         const int xstride = (L.slabs + P - 1) / P * L.slab_k;
         const int kbeg = s0 * L.slab_k;
         const int kend = min(s1 * L.slab_k, L.Kp);
@@ -193,16 +212,43 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             inv[m] = 1.0f;
             ex[m] = 0;
         }
+        // rows are read as float4 when K and the row stride allow it
+        const bool v4 = (L.K % 4 == 0) && (p.prologue == kProEmbed || p.prologue == kProEmbedRms || p.ld_src % 4 == 0);
         if (rms || PREC == 8) {
 #pragma unroll
             for (int m = 0; m < MB; ++m) {
                 float ss = 0.0f, mx = 0.0f;
                 if (m < Mloc) {
-                    if (rms)
-                        for (int k = ctid; k < L.K; k += 256) ss = fmaf(srcm[m][k], srcm[m][k], ss);
-                    if (PREC == 8)
-                        for (int k = kbeg + ctid; k < min(kend, L.K); k += 256)
-                            mx = fmaxf(mx, fabsf(rms ? __fmul_rn(srcm[m][k], p.norm_w[k]) : srcm[m][k]));
+                    if (rms) {
+                        if (v4) {
+                            for (int k = 4 * ctid; k < L.K; k += 1024) {
+                                const float4 a = *reinterpret_cast<const float4*>(srcm[m] + k);
+                                ss = fmaf(a.x, a.x, ss);
+                                ss = fmaf(a.y, a.y, ss);
+                                ss = fmaf(a.z, a.z, ss);
+                                ss = fmaf(a.w, a.w, ss);
+                            }
+                        } else {
+                            for (int k = ctid; k < L.K; k += 256) ss = fmaf(srcm[m][k], srcm[m][k], ss);
+                        }
+                    }
+                    if (PREC == 8) {
+                        const int kl = min(kend, L.K);
+                        if (v4) {
+                            for (int k = kbeg + 4 * ctid; k < kl; k += 1024) {
+                                float4 a = *reinterpret_cast<const float4*>(srcm[m] + k);
+                                if (rms) {
+                                    const float4 w = __ldg(reinterpret_cast<const float4*>(p.norm_w + k));
+                                    a = make_float4(__fmul_rn(a.x, w.x), __fmul_rn(a.y, w.y), __fmul_rn(a.z, w.z),
+                                                    __fmul_rn(a.w, w.w));
+                                }
+                                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+                            }
+                        } else {
+                            for (int k = kbeg + ctid; k < kl; k += 256)
+                                mx = fmaxf(mx, fabsf(rms ? __fmul_rn(srcm[m][k], p.norm_w[k]) : srcm[m][k]));
+                        }
+                    }
                 }
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
@@ -236,6 +282,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             }
             return v;
         };
+        // four consecutive k (k % 4 == 0)
+        auto xval4 = [&](int m, int k) -> float4 {
+            if (v4 && m < Mloc && k + 3 < L.K) {
+                float4 a = *reinterpret_cast<const float4*>(srcm[m] + k);
+                if (rms) {
+                    const float4 w = __ldg(reinterpret_cast<const float4*>(p.norm_w + k));
+                    a = make_float4(__fmul_rn(__fmul_rn(a.x, inv[m]), w.x), __fmul_rn(__fmul_rn(a.y, inv[m]), w.y),
+                                    __fmul_rn(__fmul_rn(a.z, inv[m]), w.z), __fmul_rn(__fmul_rn(a.w, inv[m]), w.w));
+                }
+                return a;
+            }
+            return make_float4(xval(m, k), xval(m, k + 1), xval(m, k + 2), xval(m, k + 3));
+        };
 
         if constexpr (PREC == 8) {
             // Digits of x[m][kbeg:kend) into the B operand, 4 consecutive k per thread.
@@ -244,8 +303,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                 const int k = kbeg + 4 * g;
 #pragma unroll
                 for (int m = 0; m < MB; ++m) {
-                    const float4 v = make_float4(xval(m, k), xval(m, k + 1), xval(m, k + 2), xval(m, k + 3));
-                    put_digits4(xd, NB, 4 * g, m, v, __int_as_float((127 - ex[m]) << 23));
+                    put_digits4(xd, NB, 4 * g, m, xval4(m, k), __int_as_float((127 - ex[m]) << 23));
                 }
                 if (NB > kTcDigits * MB) {  // unused digit rows read as zero
                     uint8_t* base = xd + (size_t)(g >> 2) * NB * 16 + (4 * g & 15);
@@ -342,7 +400,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         __syncthreads();
     if (PREC == 8 && warp == 0) {  // every tcgen05.ld of the epilogue completed before the barrier
         tc_fence_after();
-        tmem_dealloc(*tmem_slot, 32);
+        tmem_dealloc(*tmem_slot, kTmemCols);
     }
 
     if (warp < kGemvConsumerWarps) {
@@ -362,79 +420,111 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             return s;
         };
         auto finish = [&](int gpu_row, float s) -> float {
-            float v = (PREC == 8) ? __fmul_rn(s, p.scales[gpu_row]) : s;
-            if (p.bias) v = __fadd_rn(v, p.bias[gpu_row]);
+            const int i = gpu_row - rb * RB;
+            float v = (PREC == 8) ? __fmul_rn(s, rowsc[i]) : s;
+            if (p.bias) v = __fadd_rn(v, rowbias[i]);
             return v;
         };
         unsigned long long best_local[MB];
 #pragma unroll
         for (int m = 0; m < MB; ++m) best_local[m] = 0ull;
 
-        for (int it = ctid; it < nitems; it += 256) {
+        // Two phases so that every global load of a thread's items is in flight
+        // together: (1) reduce, scale, issue the loads the stores need (RoPE
+        // table, the residual); (2) finish and store.
+        constexpr int JMAX = (RB * MB + 255) / 256;
+        float va[JMAX], vb[JMAX], old[JMAX];
+        float2 cs[JMAX];
+#pragma unroll
+        for (int j = 0; j < JMAX; ++j) {
+            va[j] = vb[j] = old[j] = 0.0f;
+            cs[j] = make_float2(1.0f, 0.0f);
+            const int it = ctid + 256 * j;
+            if (it >= nitems) continue;
+            const int m = it % MB;
+            const int o = ob + it / MB;
+            if (m >= Mloc) continue;
+            if (p.epilogue == kEpiQkv) {
+                const int n0 = rb * RB + 2 * o;
+                if (n0 >= L.N) continue;
+                va[j] = finish(n0, rowsum(2 * o, m));
+                vb[j] = finish(n0 + 1, rowsum(2 * o + 1, m));
+                const int pos = seqinfo[m];
+                if (seqinfo[MB + m] && n0 < p.H + p.kv_dim && pos < p.rope_max_pos) {
+                    const int i = (n0 < p.H ? n0 : n0 - p.H) % p.head_dim;
+                    cs[j] = p.rope[(size_t)pos * (p.head_dim / 2) + i / 2];
+                }
+            } else if (p.epilogue == kEpiSiluMul) {
+                if (rb * HALF + o >= L.N) continue;
+                va[j] = finish(rb * RB + o, rowsum(o, m));
+                vb[j] = finish(rb * RB + HALF + o, rowsum(HALF + o, m));
+            } else {
+                const int n = rb * RB + o;
+                if (n >= L.N) continue;
+                va[j] = finish(n, rowsum(o, m));
+                if (p.epilogue == kEpiResidual) old[j] = p.out[(size_t)(m0 + m) * p.ld_out + n];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < JMAX; ++j) {
+            const int it = ctid + 256 * j;
+            if (it >= nitems) continue;
             const int m = it % MB;
             const int o = ob + it / MB;
             if (m >= Mloc) continue;
             const int gm = m0 + m;  // batch row
             if (p.epilogue == kEpiQkv) {
                 const int n0 = rb * RB + 2 * o;
-                if (n0 >= L.N) continue;
-                const float v0 = finish(n0, rowsum(2 * o, m));
-                const float v1 = finish(n0 + 1, rowsum(2 * o + 1, m));
-                const SeqState& sq = p.seq_ro[gm];
-                if (!sq.active) continue;
-                const int pos = sq.pos;
+                if (n0 >= L.N || !seqinfo[MB + m]) continue;
+                const int pos = seqinfo[m];
                 const int d = p.head_dim;
+                const float v0 = va[j], v1 = vb[j];
                 if (n0 < p.H + p.kv_dim) {
                     const int i = (n0 < p.H ? n0 : n0 - p.H) % d;
-                    float2 cs = make_float2(1.0f, 0.0f);
-                    if (pos < p.rope_max_pos) cs = p.rope[(size_t)pos * (d / 2) + i / 2];
                     // ModelRunner.swift:488-489
-                    const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
-                    const float r1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+                    const float r0 = __fsub_rn(__fmul_rn(v0, cs[j].x), __fmul_rn(v1, cs[j].y));
+                    const float r1 = __fadd_rn(__fmul_rn(v0, cs[j].y), __fmul_rn(v1, cs[j].x));
                     if (n0 < p.H) {
                         p.out[(size_t)gm * p.ld_out + n0] = r0;
                         p.out[(size_t)gm * p.ld_out + n0 + 1] = r1;
                         continue;
                     }
-                    const int j = n0 - p.H;
-                    const int page = p.page_table[(size_t)gm * p.ptab_stride + pos / kPageTokens];
+                    const int jj = n0 - p.H;
+                    const int page = seqinfo[2 * MB + m];
                     if (page < 0) {
                         record_error(p.err, kDevBadPage);
                         continue;
                     }
                     const size_t base =
-                        ((((size_t)page * p.num_layers + p.layer) * 2 + 0) * p.Hkv + j / d) * kPageTokens +
+                        ((((size_t)page * p.num_layers + p.layer) * 2 + 0) * p.Hkv + jj / d) * kPageTokens +
                         pos % kPageTokens;
                     p.kv_pool[base * d + i] = r0;
                     p.kv_pool[base * d + i + 1] = r1;
                 } else {
-                    const int j = n0 - p.H - p.kv_dim;
-                    const int page = p.page_table[(size_t)gm * p.ptab_stride + pos / kPageTokens];
+                    const int jj = n0 - p.H - p.kv_dim;
+                    const int page = seqinfo[2 * MB + m];
                     if (page < 0) {
                         record_error(p.err, kDevBadPage);
                         continue;
                     }
                     const size_t base =
-                        ((((size_t)page * p.num_layers + p.layer) * 2 + 1) * p.Hkv + j / d) * kPageTokens +
+                        ((((size_t)page * p.num_layers + p.layer) * 2 + 1) * p.Hkv + jj / d) * kPageTokens +
                         pos % kPageTokens;
-                    p.kv_pool[base * d + j % d] = v0;
-                    p.kv_pool[base * d + j % d + 1] = v1;
+                    p.kv_pool[base * d + jj % d] = v0;
+                    p.kv_pool[base * d + jj % d + 1] = v1;
                 }
             } else if (p.epilogue == kEpiSiluMul) {
                 const int n = rb * HALF + o;
                 if (n >= L.N) continue;
-                const float g = finish(rb * RB + o, rowsum(o, m));
-                const float u = finish(rb * RB + HALF + o, rowsum(HALF + o, m));
-                p.out[(size_t)gm * p.ld_out + n] = __fmul_rn(silu_ref(g), u);
+                p.out[(size_t)gm * p.ld_out + n] = __fmul_rn(silu_ref(va[j]), vb[j]);
             } else {
                 const int n = rb * RB + o;
                 if (n >= L.N) continue;
-                const float v = finish(n, rowsum(o, m));
+                const float v = va[j];
                 if (p.epilogue == kEpiStore) {
                     p.out[(size_t)gm * p.ld_out + n] = v;
                 } else if (p.epilogue == kEpiResidual) {
-                    float* dst = p.out + (size_t)gm * p.ld_out + n;
-                    *dst = __fadd_rn(*dst, v);
+                    p.out[(size_t)gm * p.ld_out + n] = __fadd_rn(old[j], v);
                 } else if (p.epilogue == kEpiGelu) {
                     p.out[(size_t)gm * p.ld_out + n] = gelu_ref(v);
                 } else {  // kEpiArgmax
@@ -486,7 +576,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 template <int PREC, int RB, int MB>
 size_t gemv_smem_bytes(const QLayout& L, int P) {
     using Cfg = GemvCfg<PREC, RB>;
-    size_t head = (256 + (size_t)(RB * MB + 16 * MB) * 4 + 1023) / 1024 * 1024;
+    size_t head = (256 + (size_t)(RB * MB + 16 * MB + 2 * RB + 3 * MB) * 4 + 1023) / 1024 * 1024;
     size_t stages = (size_t)Cfg::kStages * Cfg::kStageBytes;
     const size_t per_k = PREC == 8 ? (size_t)tc_nb(MB) : (size_t)MB * 4;
     size_t xbytes = ((L.slabs + P - 1) / P) * (size_t)L.slab_k * per_k;
