@@ -216,6 +216,16 @@ tb_status tb_runner_reset(tb_runner *r);
  * batch-1 runner: logits_host [vocab] may be NULL; argmax_out receives the
  * greedy token (Sampler.greedy, Sampler.swift:126-138). */
 tb_status tb_runner_step(tb_runner *r, int32_t token, float *logits_host, int32_t *argmax_out);
+/* ModelRunner.step with the InferenceObserver hooks (InferenceObserver.swift:
+ * 40-84): as tb_runner_step, plus (any may be NULL) layer_norms[num_layers] =
+ * ||h||_2 at each layer's entry (didEnterLayer), attn_weights[num_layers][stride]
+ * = each layer's softmax weights, num_heads x L flattened head-major with L =
+ * position + 1 (didComputeAttention), final_hidden[hidden_dim] = the normalised
+ * hidden state before the LM head (didComputeFinalHiddenState).  Logits are
+ * didComputeLogits.  Batch-1 runners; the step runs launch by launch (no graph). */
+tb_status tb_runner_step_observed(tb_runner *r, int32_t token, float *logits, int32_t *argmax_out,
+                                  float *layer_norms, float *attn_weights, int64_t attn_stride,
+                                  float *final_hidden);
 tb_status tb_runner_position(const tb_runner *r, int32_t seq, int64_t *pos);
 /* KVCache.length (KVCache.swift:138-143) and pageAllocationStatus (:352-356). */
 tb_status tb_runner_kv_length(const tb_runner *r, int32_t seq, int64_t *length);

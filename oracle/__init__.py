@@ -58,6 +58,7 @@ def load():
         "orc_runner_free": ([P], None),
         "orc_runner_reset": ([P], None),
         "orc_runner_step": ([P, I64, P], None),
+        "orc_runner_set_observer": ([P, P, P, I64, P], None),
         "orc_runner_position": ([P], I64),
         "orc_runner_kv_length": ([P], I64),
         "orc_runner_max_pages": ([P], I64),
@@ -229,11 +230,29 @@ class OracleModel:
         lib.orc_model_set_output(self.m, C.byref(s), _p(weights.output.bias))
         self.r = lib.orc_runner_create(self.m, mode, threads)
         self.vocab = c.vocab_size
+        self.cfg = c
 
     def step(self, token):
         logits = np.empty(self.vocab, dtype=np.float32)
         load().orc_runner_step(self.r, int(token), _p(logits))
         return logits
+
+    def step_observed(self, token):
+        """step() plus the InferenceObserver values of this step:
+        (logits, layer-entry norms [layers], attention weights per layer
+        [layers][heads * L], final hidden state [hidden])."""
+        c = self.cfg
+        L = self.position + 1
+        norms = np.empty(c.num_layers, dtype=np.float32)
+        attn = np.empty((c.num_layers, c.num_heads * L), dtype=np.float32)
+        fin = np.empty(c.hidden_dim, dtype=np.float32)
+        lib = load()
+        lib.orc_runner_set_observer(self.r, _p(norms), _p(attn), c.num_heads * L, _p(fin))
+        try:
+            logits = self.step(token)
+        finally:
+            lib.orc_runner_set_observer(self.r, None, None, 0, None)
+        return logits, norms, attn, fin
 
     def reset(self):
         load().orc_runner_reset(self.r)

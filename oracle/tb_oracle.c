@@ -411,7 +411,19 @@ struct orc_runner {
     /* scratch */
     float *h, *x, *q, *k, *v, *ctx, *tmp, *ff1, *ff2, *K, *V;
     int64_t kv_gather_cap;
+    /* InferenceObserver hooks (InferenceObserver.swift:40-84), NULL = off */
+    float *obs_norms;        /* [num_layers] layer-entry ||h||_2 */
+    float *obs_attn;         /* [num_layers][attn_stride] = [H][L] per layer */
+    int64_t obs_attn_stride;
+    float *obs_final;        /* [H] final hidden state (post-norm, pre-projection) */
 };
+
+void orc_runner_set_observer(orc_runner *r, float *norms, float *attn, int64_t attn_stride, float *final_hidden) {
+    r->obs_norms = norms;
+    r->obs_attn = attn;
+    r->obs_attn_stride = attn_stride;
+    r->obs_final = final_hidden;
+}
 
 static void kv_layer_reset(orc_runner *r, orc_kvlayer *L) {
     L->nfree = r->max_pages;
@@ -576,6 +588,11 @@ void orc_runner_step(orc_runner *r, int64_t token, float *logits) {
     memcpy(r->h, m->emb + token * H, sizeof(float) * (size_t)H);
     for (int64_t l = 0; l < c->num_layers; ++l) {
         const orc_layer *ly = &m->layers[l];
+        if (r->obs_norms) { /* ModelRunner.swift:395-399: sqrt(reduce(0) { $0 + $1*$1 }) */
+            float ss = 0.0f;
+            for (int64_t i = 0; i < H; ++i) ss = ss + r->h[i] * r->h[i];
+            r->obs_norms[l] = sqrtf(ss);
+        }
         const float *xin = r->h;
         if (ly->in_norm) {
             orc_rmsnorm(r->h, ly->in_norm, H, c->rms_eps, r->x);
@@ -588,7 +605,9 @@ void orc_runner_step(orc_runner *r, int64_t token, float *logits) {
         orc_rope(r->k, d, c->num_kv_heads, r->pos, d);
         kv_append(r, l, r->k, r->v, r->pos);
         kv_gather(r, l, L_, r->K, r->V);
-        orc_attention(r->q, r->K, r->V, L_, c->num_heads, c->num_kv_heads, d, r->ctx, NULL);
+        /* ModelRunner.swift:582-586: weights flattened numHeads x seqLen */
+        orc_attention(r->q, r->K, r->V, L_, c->num_heads, c->num_kv_heads, d, r->ctx,
+                      r->obs_attn ? r->obs_attn + l * r->obs_attn_stride : NULL);
         apply_proj(r, &ly->p[ORC_O], r->ctx, r->tmp);
         for (int64_t i = 0; i < H; ++i) r->h[i] = r->h[i] + r->tmp[i]; /* residual1 */
         const float *x2 = r->h;
@@ -614,6 +633,7 @@ void orc_runner_step(orc_runner *r, int64_t token, float *logits) {
         orc_rmsnorm(r->h, m->final_norm, H, c->rms_eps, r->x);
         hf = r->x;
     }
+    if (r->obs_final) memcpy(r->obs_final, hf, sizeof(float) * (size_t)H); /* ModelRunner.swift:195 */
     apply_proj(r, &m->out, hf, logits);
     r->pos += 1;
 }

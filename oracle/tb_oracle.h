@@ -96,9 +96,13 @@ void orc_model_set_proj(orc_model *m, int64_t layer, int32_t which,
 orc_runner *orc_runner_create(const orc_model *m, int32_t mode, int32_t nthreads);
 void orc_runner_free(orc_runner *r);
 void orc_runner_reset(orc_runner *r);
-/* logits [vocab]; attn_probs (may be NULL) receives layer `probe_layer`'s [H, L]
- * attention weights; hidden_norms (may be NULL) [num_layers] layer-entry norms. */
+/* logits [vocab]. */
 void orc_runner_step(orc_runner *r, int64_t token, float *logits);
+/* InferenceObserver (InferenceObserver.swift:40-84) outputs of later steps, any
+ * may be NULL: norms [num_layers] layer-entry ||h||_2; attn [num_layers][stride]
+ * with each layer's [num_heads][L] softmax weights (L = position + 1);
+ * final_hidden [hidden] post-norm, pre-projection. */
+void orc_runner_set_observer(orc_runner *r, float *norms, float *attn, int64_t attn_stride, float *final_hidden);
 int64_t orc_runner_position(const orc_runner *r);
 int64_t orc_runner_kv_length(const orc_runner *r);
 /* KVCache.pageAllocationStatus(layer:) -- status has max_pages entries. */

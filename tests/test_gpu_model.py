@@ -186,3 +186,61 @@ def test_persistent_other_shapes(ctx, shape, mode, kernel, monkeypatch):
     for i, tok in enumerate([3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8, 9, 7, 9, 3, 2, 3]):
         logits, _ = r.step(tok)
         assert rel_l2(logits, o.step(tok)) <= RTOL_L2, i
+
+
+class _Recorder:
+    """InferenceObserver (InferenceObserver.swift:40-84) that records every call."""
+
+    def __init__(self):
+        self.calls = []
+
+    def did_enter_layer(self, layer, norm, position):
+        self.calls.append(("enter", layer, position, norm))
+
+    def did_compute_attention(self, layer, weights, position):
+        self.calls.append(("attn", layer, position, weights))
+
+    def did_compute_final_hidden_state(self, hidden, position):
+        self.calls.append(("final", None, position, hidden))
+
+    def did_compute_logits(self, logits, position):
+        self.calls.append(("logits", None, position, logits))
+
+
+@pytest.mark.parametrize("mode", ["perChannel", "int4"])
+def test_observer_hooks_match_oracle(ctx, mode):
+    cfg = small_cfg(num_layers=3)
+    w = small_llama(cfg, seed=21, mode=mode)
+    r = ModelRunner(w, ctx)
+    rec = _Recorder()
+    r.observer = rec
+    o = oracle.OracleModel(w, mode=1)
+    for i, tok in enumerate([5, 17, 3, 99, 42, 7, 11, 250, 1, 64, 33, 2, 8, 19, 600, 4, 12, 90]):
+        rec.calls.clear()
+        logits, _ = r.step(tok)
+        ol, on, oa, of = o.step_observed(tok)
+        kinds = [c[0] for c in rec.calls]
+        assert kinds == ["enter", "attn"] * cfg.num_layers + ["final", "logits"]  # the reference's order
+        assert all(c[2] == i for c in rec.calls)  # currentPosition
+        norms = np.array([c[3] for c in rec.calls if c[0] == "enter"], dtype=np.float32)
+        assert rel_l2(norms, on) <= 1e-5
+        for l, c in enumerate([c for c in rec.calls if c[0] == "attn"]):
+            assert c[3].shape == (cfg.num_heads * (i + 1),)
+            assert np.allclose(c[3], oa[l], atol=1e-5, rtol=5e-4)
+            assert np.allclose(c[3].reshape(cfg.num_heads, -1).sum(axis=1), 1.0, atol=1e-5)
+        assert rel_l2(rec.calls[-2][3], of) <= 1e-5
+        assert rel_l2(rec.calls[-1][3], ol) <= RTOL_L2
+        assert rel_l2(logits, ol) <= RTOL_L2
+
+
+def test_observer_generate_stream_same_tokens(ctx):
+    w = small_llama(small_cfg(), seed=22)
+    prompt = [3, 1, 4, 1, 5, 9, 2, 6]
+    plain = [t.token_id for t in ModelRunner(w, ctx).generate_stream(prompt, GenerationConfig(max_tokens=12, sampler=SamplerConfig(top_k=1)))]
+    r = ModelRunner(w, ctx)
+    rec = _Recorder()
+    r.observer = rec
+    seen = [t.token_id for t in r.generate_stream(prompt, GenerationConfig(max_tokens=12, sampler=SamplerConfig(top_k=1)))]
+    assert seen == plain
+    # one didComputeLogits per step: 7 prefill steps + 12 decode steps
+    assert sum(1 for c in rec.calls if c[0] == "logits") == len(prompt) - 1 + 12

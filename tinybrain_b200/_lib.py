@@ -92,6 +92,7 @@ SIGNATURES = {
     "tb_runner_free": [_P],
     "tb_runner_reset": [_P],
     "tb_runner_step": [_P, _I32, _P, _PI32],
+    "tb_runner_step_observed": [_P, _I32, _P, _PI32, _P, _P, _I64, _P],
     "tb_runner_position": [_P, _I32, _PI64],
     "tb_runner_kv_length": [_P, _I32, _PI64],
     "tb_runner_page_status": [_P, _I32, _P, _I64],

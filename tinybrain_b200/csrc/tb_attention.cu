@@ -290,6 +290,46 @@ __global__ void attn_probs_kernel(const AttnParams p, float* probs, int L) {
         probs[((size_t)m * p.H + h) * L + j] = __fdiv_rn(expf(sc[j] - red[0]), red[1]);
 }
 
+// Observer hook: L2 norm of each hidden row (ModelRunner.swift:395-399).
+__global__ void row_norm_kernel(const float* h, int H, int ld, float* out) {
+    const float* x = h + (size_t)blockIdx.x * ld;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+    __shared__ float red[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+        out[blockIdx.x] = __fsqrt_rn(t);
+    }
+}
+
+// Observer hook: final hidden state, RMSNorm(h) * w (Tensor.swift:1538-1558),
+// or h itself when the model has no final norm.
+__global__ void rmsnorm_rows_kernel(const float* h, const float* w, int H, int ld, float eps, float* out) {
+    const float* x = h + (size_t)blockIdx.x * ld;
+    float* y = out + (size_t)blockIdx.x * H;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+    __shared__ float red[32];
+    __shared__ float inv_s;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int q = 0; q < (int)(blockDim.x >> 5); ++q) t += red[q];
+        inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), eps)));
+    }
+    __syncthreads();
+    const float inv = inv_s;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) y[i] = w ? __fmul_rn(__fmul_rn(x[i], inv), w[i]) : x[i];
+}
+
 }  // namespace
 
 size_t attention_scratch_bytes(int M, int Hkv, int nsplit, int G, int d) {
@@ -330,6 +370,16 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl)
     TB_ATTN_CASE(8, 64)
 #undef TB_ATTN_CASE
     return cudaErrorNotSupported;
+}
+
+cudaError_t launch_row_norm(const float* h, int H, int ld, int M, float* out, cudaStream_t stream) {
+    row_norm_kernel<<<M, 256, 0, stream>>>(h, H, ld, out);
+    return cudaGetLastError();
+}
+cudaError_t launch_rmsnorm_rows(const float* h, const float* w, int H, int ld, int M, float eps, float* out,
+                                cudaStream_t stream) {
+    rmsnorm_rows_kernel<<<M, 256, 0, stream>>>(h, w, H, ld, eps, out);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_attention_probs(const AttnParams& p, float* probs, int L, cudaStream_t stream) {

@@ -263,5 +263,9 @@ int report_error(int status, const char* fmt, ...);
 
 // Softmax attention weights for the observer hook: probs[M][H][L].
 cudaError_t launch_attention_probs(const AttnParams& p, float* probs, int L, cudaStream_t stream);
+// Observer hooks: per-row L2 norm; RMSNorm(h) * w per row (w null: copy).
+cudaError_t launch_row_norm(const float* h, int H, int ld, int M, float* out, cudaStream_t stream);
+cudaError_t launch_rmsnorm_rows(const float* h, const float* w, int H, int ld, int M, float eps, float* out,
+                                cudaStream_t stream);
 
 }  // namespace tb

@@ -238,6 +238,7 @@ struct tb_runner {
     size_t step_smem = 0;
     DevBuf step_layers, part_qkv, part_o, part_gu, part_dn, step_attn, hX, hY, step_bar, step_trace;
     DevBuf flow_buf;  // dataflow step: tagged words + epoch / ticket
+    DevBuf obs_buf;   // observer outputs: attention weights, layer norms, final hidden
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     ~tb_runner() {
         for (cudaEvent_t e : ptab_ev)
@@ -1617,6 +1618,70 @@ extern "C" tb_status tb_runner_step(tb_runner* r, int32_t token, float* logits, 
     if (logits)
         TB_CUDA(cudaMemcpyAsync(logits, r->logits.p, (size_t)V * 4, cudaMemcpyDeviceToHost, r->ctx->stream));
     TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    r->kvh[0].pos += 1;
+    if (argmax_out) *argmax_out = r->pin_seq.as<SeqState>()->token;
+    return tb_context_check_device(r->ctx);
+}
+
+// ModelRunner.step with the InferenceObserver hooks (InferenceObserver.swift:40-84,
+// ModelRunner.swift:195-202, 395-399, 582-586): the per-projection plan runs
+// launch by launch with three observer kernels in between -- the L2 norm of h
+// after each layer's QKV launch (h at layer entry; layer 0's embedding row is
+// gathered by that launch), the softmax weights after each attention launch,
+// and RMSNorm(h) * w before the LM head.  Batch-1 runners, sequence 0.
+extern "C" tb_status tb_runner_step_observed(tb_runner* r, int32_t token, float* logits, int32_t* argmax_out,
+                                             float* layer_norms, float* attn_weights, int64_t attn_stride,
+                                             float* final_hidden) {
+    TB_CHECK(r, "NULL runner");
+    TB_CHECK(r->B == 1, "tb_runner_step_observed drives batch-1 runners");
+    tb_model* m = r->m;
+    const tb_model_config& c = m->cfg;
+    const int V = c.vocab_size, H = c.hidden_dim, NL = c.num_layers;
+    TB_CHECK(token >= 0 && token < V, "token %d outside [0, %d)", token, V);
+    const int64_t Lc = r->kvh[0].pos + 1;
+    TB_CHECK(!attn_weights || attn_stride >= (int64_t)c.num_heads * Lc, "attn_stride %lld < num_heads * L = %lld",
+             (long long)attn_stride, (long long)(c.num_heads * Lc));
+    TB_CHECK(r->plan.size() == (size_t)(5 * NL + 1), "observer needs the per-projection plan");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    tb_status s = kv_prepare(r, 0);
+    if (s != TB_OK) return s;
+    if ((s = flush_ptab(r)) != TB_OK) return s;
+    SeqState* st = r->pin_seq.as<SeqState>();
+    memset(st, 0, sizeof(SeqState));
+    st->pos = (int)r->kvh[0].pos;
+    st->token = token;
+    st->active = 1;
+    if ((s = push_seq(r)) != TB_OK) return s;
+    const size_t probs_floats = (size_t)NL * c.num_heads * Lc;
+    if (r->obs_buf.bytes < (probs_floats + NL + H) * 4) TB_CUDA(r->obs_buf.alloc((probs_floats + NL + H) * 4));
+    float* d_probs = r->obs_buf.as<float>();
+    float* d_norms = d_probs + probs_floats;
+    float* d_final = d_norms + NL;
+    cudaStream_t sm = r->ctx->stream;
+    for (size_t i = 0; i < r->plan.size(); ++i) {
+        const Launch& ln = r->plan[i];
+        const int l = (int)(i / 5);
+        if (i + 1 == r->plan.size()) {
+            cudaError_t e = launch_rmsnorm_rows(r->h.as<float>(), m->has_final_norm ? m->final_norm.as<float>() : nullptr,
+                                                H, H, 1, c.rms_eps, d_final, sm);
+            if (e != cudaSuccess) return cuda_fail(e, "launch_rmsnorm_rows");
+        }
+        cudaError_t e = ln.kind == 0 ? launch_gemv(ln.g, sm, false) : launch_attention(ln.a, sm, false);
+        if (e != cudaSuccess) return cuda_fail(e, ln.kind == 0 ? "launch_gemv" : "launch_attention");
+        if (i + 1 < r->plan.size() && i % 5 == 0) e = launch_row_norm(r->h.as<float>(), H, H, 1, d_norms + l, sm);
+        if (i + 1 < r->plan.size() && i % 5 == 1)
+            e = launch_attention_probs(ln.a, d_probs + (size_t)l * c.num_heads * Lc, (int)Lc, sm);
+        if (e != cudaSuccess) return cuda_fail(e, "observer kernel");
+    }
+    TB_CUDA(cudaMemcpyAsync(r->pin_seq.p, r->seq.p, sizeof(SeqState), cudaMemcpyDeviceToHost, sm));
+    if (logits) TB_CUDA(cudaMemcpyAsync(logits, r->logits.p, (size_t)V * 4, cudaMemcpyDeviceToHost, sm));
+    if (layer_norms) TB_CUDA(cudaMemcpyAsync(layer_norms, d_norms, (size_t)NL * 4, cudaMemcpyDeviceToHost, sm));
+    if (final_hidden) TB_CUDA(cudaMemcpyAsync(final_hidden, d_final, (size_t)H * 4, cudaMemcpyDeviceToHost, sm));
+    if (attn_weights)
+        for (int l = 0; l < NL; ++l)
+            TB_CUDA(cudaMemcpyAsync(attn_weights + (size_t)l * attn_stride, d_probs + (size_t)l * c.num_heads * Lc,
+                                    (size_t)c.num_heads * Lc * 4, cudaMemcpyDeviceToHost, sm));
+    TB_CUDA(cudaStreamSynchronize(sm));
     r->kvh[0].pos += 1;
     if (argmax_out) *argmax_out = r->pin_seq.as<SeqState>()->token;
     return tb_context_check_device(r->ctx);

@@ -462,10 +462,39 @@ class ModelRunner:
 
     # -- ModelRunner.step / reset / currentPosition --
     def step(self, token_id: int, want_logits: bool = True):
-        """One forward step; returns (logits or None, greedy token)."""
+        """One forward step; returns (logits or None, greedy token).  With an
+        observer attached (``runner.observer``, the InferenceObserver of
+        InferenceObserver.swift:40-84) the step reports its internals through
+        the observer's methods, in the reference's order: per layer
+        ``did_enter_layer(layer, hidden_state_norm, position)`` and
+        ``did_compute_attention(layer, weights, position)`` (weights flattened
+        num_heads x L), then ``did_compute_final_hidden_state(hidden, position)``
+        (optional method) and ``did_compute_logits(logits, position)``."""
+        if self.observer is not None:
+            return self._step_observed(int(token_id))
         logits = np.empty(self.config.vocab_size, dtype=np.float32) if want_logits else None
         am = C.c_int32(0)
         call("tb_runner_step", self.handle, int(token_id), _ptr(logits), C.byref(am))
+        return logits, am.value
+
+    def _step_observed(self, token_id: int):
+        c = self.config
+        pos = self.current_position()
+        L = pos + 1
+        logits = np.empty(c.vocab_size, dtype=np.float32)
+        norms = np.empty(c.num_layers, dtype=np.float32)
+        attn = np.empty((c.num_layers, c.num_heads * L), dtype=np.float32)
+        fin = np.empty(c.hidden_dim, dtype=np.float32)
+        am = C.c_int32(0)
+        call("tb_runner_step_observed", self.handle, token_id, _ptr(logits), C.byref(am), _ptr(norms), _ptr(attn),
+             c.num_heads * L, _ptr(fin))
+        ob = self.observer
+        for layer in range(c.num_layers):
+            ob.did_enter_layer(layer, float(norms[layer]), pos)
+            ob.did_compute_attention(layer, attn[layer].copy(), pos)
+        if hasattr(ob, "did_compute_final_hidden_state"):
+            ob.did_compute_final_hidden_state(fin, pos)
+        ob.did_compute_logits(logits.copy(), pos)
         return logits, am.value
 
     def reset(self):
@@ -507,6 +536,23 @@ class ModelRunner:
         if config.sampler.repetition_penalty != 1.0:
             raise TinyBrainError(4, "repetition penalty is not implemented by the device sampler")
         p, ent = _greedy_topk1_stats()
+        if self.observer is not None:
+            # observed generation runs step by step so every step reports to the
+            # observer (ModelRunner.swift:236-298: clamp, prefill all but the
+            # last prompt token, then step + sample; a stop token is yielded)
+            V = self.config.vocab_size
+            ids = [min(max(int(t), 0), V - 1) for t in prompt] or [0]
+            for t in ids[:-1]:
+                self.step(t)
+            cur = ids[-1]
+            stops = set(config.stop_tokens)
+            for _ in range(config.max_tokens):
+                _, nxt = self.step(cur)
+                yield TokenOutput(nxt, p, ent, time.time(), strategy)
+                if nxt in stops:
+                    break
+                cur = nxt
+            return
         toks: List[int] = []
 
         def cb(seq, idx, tok):
