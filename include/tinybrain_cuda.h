@@ -192,6 +192,17 @@ typedef struct {
  * (QKV concatenated, gate/up interleaved) at tb_model_finalize. */
 tb_status tb_model_create(tb_context *ctx, const tb_model_config *cfg, tb_model **out);
 tb_status tb_model_free(tb_model *m);
+/* Tensor parallelism (new; the reference runs on one device).  Rank 0 draws
+ * a 128-byte NCCL unique id, every rank receives it out of band and joins
+ * the communicator on its context; the model is then told its shard before
+ * any projection is set.  Projections are passed pre-sliced: q, k, v and
+ * gate, up as column shards [hidden, out/world] (this rank's heads / rows),
+ * o_proj and down_proj as row shards [in/world, hidden].  The step adds an
+ * in-place fp32 all-reduce of the residual stream after o_proj and
+ * down_proj; the LM head is replicated. */
+tb_status tb_tp_unique_id(uint8_t *id /* [128] */);
+tb_status tb_context_init_tp(tb_context *ctx, const uint8_t *id /* [128] */, int32_t rank, int32_t world);
+tb_status tb_model_set_tensor_parallel(tb_model *m, int32_t rank, int32_t world);
 tb_status tb_model_set_embedding(tb_model *m, const float *emb_host /* [vocab][hidden] */);
 tb_status tb_model_set_final_norm(tb_model *m, const float *w_host /* [hidden] */);
 tb_status tb_model_set_layer_norms(tb_model *m, int32_t layer, const float *input_norm_host,

@@ -11,7 +11,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libtinybrain_cuda.so")
-SOURCES = ["tb_gemv.cu", "tb_attention.cu", "tb_quant.cu", "tb_step.cu", "tb_flow.cu", "tb_runtime.cu"]
+SOURCES = ["tb_gemv.cu", "tb_attention.cu", "tb_quant.cu", "tb_step.cu", "tb_flow.cu", "tb_nccl.cu", "tb_runtime.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -54,7 +54,7 @@ def build(verbose=False, force=False, jobs=None):
     if failed:
         raise RuntimeError("nvcc failed for: " + ", ".join(failed))
     if force or _stale([LIB], objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs, "-lpthread"]
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs, "-lpthread", "-ldl"]
         subprocess.check_call(cmd)
     return LIB
 

@@ -13,6 +13,7 @@
 // There is no CPU compute path: every numeric result comes from a kernel.
 #include "../../include/tinybrain_cuda.h"
 #include "tb_kernels.h"
+#include "tb_nccl.h"
 
 #include <algorithm>
 #include <atomic>
@@ -141,6 +142,9 @@ struct tb_context {
     DevBuf tickets;      // attention tickets (zeroed)
     DevBuf io_a, io_b, io_c, io_d;  // staging for host-pointer entry points
     DevBuf seq_tmp;
+    // tensor parallelism: NCCL communicator over the ranks sharing a model
+    void* comm = nullptr;
+    int tp_rank = 0, tp_world = 1;
 };
 
 struct tb_qweight {
@@ -176,8 +180,10 @@ struct Layer {
 
 struct tb_model {
     tb_context* ctx = nullptr;
-    tb_model_config cfg{};
-    int head_dim = 0, kv_dim = 0;
+    tb_model_config cfg{};   // this rank's shard: heads, kv heads, intermediate are local counts
+    tb_model_config full{};  // the whole model
+    int head_dim = 0, kv_dim = 0, q_dim = 0;  // kv_dim, q_dim: local
+    int tp_rank = 0, tp_world = 1;
     std::vector<Layer> layers;
     ProjStage out_stage;
     FusedWeight out;
@@ -198,7 +204,7 @@ struct SeqKV {
 };
 
 struct Launch {
-    int kind;  // 0 gemv, 1 attention
+    int kind;  // 0 gemv, 1 attention, 3 all-reduce of the residual stream over the tensor-parallel ranks
     GemvParams g;
     AttnParams a;
     int64_t bytes;  // algorithmic bytes (weights + activations) for roofline
@@ -381,6 +387,7 @@ extern "C" tb_status tb_context_destroy(tb_context* ctx) {
     if (!ctx) return ok();
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
+    if (ctx->comm) nccl_comm_destroy(ctx->comm);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
     return ok();
@@ -823,8 +830,58 @@ extern "C" tb_status tb_model_create(tb_context* ctx, const tb_model_config* cfg
     if (m->cfg.rms_eps == 0.0f) m->cfg.rms_eps = 1e-5f;
     m->head_dim = d;
     m->kv_dim = d * c.num_kv_heads;
+    m->q_dim = c.hidden_dim;
+    m->full = m->cfg;
     m->layers.resize(c.num_layers);
     *out = m.release();
+    return ok();
+}
+
+extern "C" tb_status tb_tp_unique_id(uint8_t* id) {
+    TB_CHECK(id, "NULL argument");
+    std::string why;
+    if (nccl_unique_id(id, why)) return fail(TB_ERR_UNSUPPORTED, "%s", why.c_str());
+    return ok();
+}
+
+extern "C" tb_status tb_context_init_tp(tb_context* ctx, const uint8_t* id, int32_t rank, int32_t world) {
+    TB_CHECK(ctx && id, "NULL argument");
+    TB_CHECK(world >= 1 && rank >= 0 && rank < world, "rank %d / world %d", rank, world);
+    TB_CHECK(!ctx->comm, "context already has a tensor-parallel communicator");
+    TB_CUDA(cudaSetDevice(ctx->device));
+    if (world > 1) {
+        std::string why;
+        if (nccl_comm_init(&ctx->comm, id, rank, world, why)) return fail(TB_ERR_UNSUPPORTED, "%s", why.c_str());
+    }
+    ctx->tp_rank = rank;
+    ctx->tp_world = world;
+    return ok();
+}
+
+extern "C" tb_status tb_model_set_tensor_parallel(tb_model* m, int32_t rank, int32_t world) {
+    TB_CHECK(m, "NULL model");
+    TB_CHECK(!m->finalized, "model already finalized");
+    TB_CHECK(m->tp_world == 1, "tensor parallelism already set");
+    for (const Layer& L : m->layers)
+        for (const ProjStage& st : L.stage) TB_CHECK(!st.set, "set tensor parallelism before the projections");
+    TB_CHECK(world >= 1 && rank >= 0 && rank < world, "rank %d / world %d", rank, world);
+    TB_CHECK(m->ctx->tp_world == world && m->ctx->tp_rank == rank,
+             "context is rank %d of %d (tb_context_init_tp), model asks for rank %d of %d", m->ctx->tp_rank,
+             m->ctx->tp_world, rank, world);
+    const tb_model_config& f = m->full;
+    TB_CHECK(f.num_heads % world == 0 && f.num_kv_heads % world == 0 && f.intermediate_dim % world == 0,
+             "heads %d, kv heads %d and intermediate %d must divide by %d ranks", f.num_heads, f.num_kv_heads,
+             f.intermediate_dim, world);
+    const int hl = f.num_heads / world, kl = f.num_kv_heads / world, il = f.intermediate_dim / world;
+    TB_CHECK((hl * m->head_dim) % 32 == 0 && (kl * m->head_dim) % 32 == 0 && il % 32 == 0,
+             "per-rank q, kv and intermediate widths must be multiples of 32");
+    m->cfg.num_heads = hl;
+    m->cfg.num_kv_heads = kl;
+    m->cfg.intermediate_dim = il;
+    m->q_dim = hl * m->head_dim;
+    m->kv_dim = kl * m->head_dim;
+    m->tp_rank = rank;
+    m->tp_world = world;
     return ok();
 }
 
@@ -871,12 +928,12 @@ extern "C" tb_status tb_model_set_layer_norms(tb_model* m, int32_t layer, const 
 }
 
 static tb_status expected_shape(const tb_model* m, int which, int& K, int& N) {
-    const int H = m->cfg.hidden_dim, I = m->cfg.intermediate_dim;
+    const int H = m->cfg.hidden_dim, I = m->cfg.intermediate_dim, qd = m->q_dim;
     switch (which) {
-        case TB_PROJ_Q: K = H; N = H; break;
+        case TB_PROJ_Q: K = H; N = qd; break;
         case TB_PROJ_K:
         case TB_PROJ_V: K = H; N = m->kv_dim; break;
-        case TB_PROJ_O: K = H; N = H; break;
+        case TB_PROJ_O: K = qd; N = H; break;
         case TB_PROJ_GATE:
         case TB_PROJ_UP: K = H; N = I; break;
         case TB_PROJ_DOWN: K = I; N = H; break;
@@ -948,7 +1005,7 @@ extern "C" tb_status tb_model_finalize(tb_model* m) {
     tb_context* ctx = m->ctx;
     TB_CUDA(cudaSetDevice(ctx->device));
     const tb_model_config& c = m->cfg;
-    const int H = c.hidden_dim, I = c.intermediate_dim, kvd = m->kv_dim;
+    const int H = c.hidden_dim, I = c.intermediate_dim, kvd = m->kv_dim, qd = m->q_dim;
     const bool llama = c.architecture == TB_ARCH_LLAMA;
     if (!m->emb.p) return fail(TB_ERR_STATE, "embedding not set");
     if (!m->out_stage.set) return fail(TB_ERR_STATE, "output projection not set");
@@ -962,16 +1019,16 @@ extern "C" tb_status tb_model_finalize(tb_model* m) {
         if (L.stage[TB_PROJ_K].precision != pq || L.stage[TB_PROJ_V].precision != pq ||
             (L.stage[TB_PROJ_K].gs != L.stage[TB_PROJ_Q].gs && pq == 4))
             return fail(TB_ERR_UNSUPPORTED, "layer %d: q, k, v must share precision", l);
-        tb_status s = alloc_fused(ctx, L.qkv, make_qlayout(pq, H, H + 2 * kvd, 32));
+        tb_status s = alloc_fused(ctx, L.qkv, make_qlayout(pq, H, qd + 2 * kvd, 32));
         if (s != TB_OK) return s;
         if ((s = repack_into(ctx, L.qkv, L.stage[TB_PROJ_Q], 0, 0)) != TB_OK) return s;
-        if ((s = repack_into(ctx, L.qkv, L.stage[TB_PROJ_K], H, 0)) != TB_OK) return s;
-        if ((s = repack_into(ctx, L.qkv, L.stage[TB_PROJ_V], H + kvd, 0)) != TB_OK) return s;
+        if ((s = repack_into(ctx, L.qkv, L.stage[TB_PROJ_K], qd, 0)) != TB_OK) return s;
+        if ((s = repack_into(ctx, L.qkv, L.stage[TB_PROJ_V], qd + kvd, 0)) != TB_OK) return s;
         if ((s = upload_bias(L.qkv, {{&L.stage[TB_PROJ_Q], {0, 0}},
-                                     {&L.stage[TB_PROJ_K], {H, 0}},
-                                     {&L.stage[TB_PROJ_V], {H + kvd, 0}}})) != TB_OK)
+                                     {&L.stage[TB_PROJ_K], {qd, 0}},
+                                     {&L.stage[TB_PROJ_V], {qd + kvd, 0}}})) != TB_OK)
             return s;
-        if ((s = alloc_fused(ctx, L.o, make_qlayout(L.stage[TB_PROJ_O].precision, H, H, 32))) != TB_OK) return s;
+        if ((s = alloc_fused(ctx, L.o, make_qlayout(L.stage[TB_PROJ_O].precision, qd, H, 32))) != TB_OK) return s;
         if ((s = repack_into(ctx, L.o, L.stage[TB_PROJ_O], 0, 0)) != TB_OK) return s;
         if ((s = upload_bias(L.o, {{&L.stage[TB_PROJ_O], {0, 0}}})) != TB_OK) return s;
         if (llama) {
@@ -1058,8 +1115,21 @@ static int64_t gemv_bytes(const QLayout& L, int M) {
 static tb_status build_plan(tb_runner* r) {
     tb_model* m = r->m;
     const tb_model_config& c = m->cfg;
-    const int H = c.hidden_dim, d = m->head_dim, kvd = m->kv_dim, B = r->B;
+    const int H = c.hidden_dim, d = m->head_dim, kvd = m->kv_dim, qd = m->q_dim, B = r->B;
     const bool llama = c.architecture == TB_ARCH_LLAMA;
+    // Tensor parallel: QKV and gate/up are column shards (local heads, local
+    // intermediate rows), o_proj and down row shards whose partial sums meet
+    // in an all-reduce of the residual stream.  Rank 0 adds its partial to the
+    // residual, the other ranks store theirs, so the sum is h + sum_r y_r.
+    const bool tp = m->tp_world > 1;
+    const int row_epi = tp && m->tp_rank != 0 ? kEpiStore : kEpiResidual;
+    auto push_allreduce = [&]() {
+        if (!tp) return;
+        Launch ln{};
+        ln.kind = 3;
+        ln.bytes = (int64_t)B * H * 4;
+        r->plan.push_back(ln);
+    };
     r->plan.clear();
     for (int l = 0; l < c.num_layers; ++l) {
         Layer& Ly = m->layers[l];
@@ -1080,8 +1150,8 @@ static tb_status build_plan(tb_runner* r) {
             p.resid = r->h.as<float>();
             p.epilogue = kEpiQkv;
             p.out = r->q.as<float>();
-            p.ld_out = H;
-            p.H = H;
+            p.ld_out = qd;
+            p.H = qd;
             p.Hkv = c.num_kv_heads;
             p.head_dim = d;
             p.kv_dim = kvd;
@@ -1100,7 +1170,7 @@ static tb_status build_plan(tb_runner* r) {
             ln.kind = 1;
             AttnParams& a = ln.a;
             a.q = r->q.as<float>();
-            a.ld_q = H;
+            a.ld_q = qd;
             a.kv_pool = r->kv.as<float>();
             a.page_table = r->ptab.as<int>();
             a.ptab_stride = r->ptab_stride;
@@ -1114,7 +1184,7 @@ static tb_status build_plan(tb_runner* r) {
             a.M = B;
             a.nsplit = r->nsplit;
             a.out = r->ctxv.as<float>();
-            a.ld_out = H;
+            a.ld_out = qd;
             a.part = r->attn_part.as<float>();
             a.tickets = r->attn_tickets.as<unsigned int>();
             a.err = r->ctx->err.as<int>();
@@ -1128,12 +1198,13 @@ static tb_status build_plan(tb_runner* r) {
             fill_gemv_common(r, p, Ly.o);
             p.prologue = kProNone;
             p.src = r->ctxv.as<float>();
-            p.ld_src = H;
-            p.epilogue = kEpiResidual;
+            p.ld_src = qd;
+            p.epilogue = row_epi;
             p.out = r->h.as<float>();
             p.ld_out = H;
             ln.bytes = gemv_bytes(Ly.o.L, B) + (int64_t)B * H * 4;
             r->plan.push_back(ln);
+            push_allreduce();
         }
         {  // gate/up (+ post-attention RMSNorm) + SiLU*up, or toy up + GELU
             Launch ln{};
@@ -1158,11 +1229,12 @@ static tb_status build_plan(tb_runner* r) {
             p.prologue = kProNone;
             p.src = r->act.as<float>();
             p.ld_src = c.intermediate_dim;
-            p.epilogue = kEpiResidual;
+            p.epilogue = row_epi;
             p.out = r->h.as<float>();
             p.ld_out = H;
             ln.bytes = gemv_bytes(Ly.down.L, B) + (int64_t)B * H * 4;
             r->plan.push_back(ln);
+            push_allreduce();
         }
     }
     {  // final norm + LM head + argmax + step bookkeeping
@@ -1187,10 +1259,24 @@ static tb_status build_plan(tb_runner* r) {
     return ok();
 }
 
+// One launch of the plan on `st`.
+static tb_status launch_op(tb_runner* r, const Launch& ln, cudaStream_t st, bool pdl) {
+    cudaError_t e;
+    if (ln.kind == 3) {
+        std::string why;
+        e = nccl_allreduce_sum_f32(r->ctx->comm, r->h.as<float>(), (size_t)r->B * r->m->cfg.hidden_dim, st, why);
+        if (e != cudaSuccess) return fail(TB_ERR_CUDA, "tensor-parallel all-reduce: %s", why.c_str());
+        return ok();
+    }
+    e = ln.kind == 0 ? launch_gemv(ln.g, st, pdl) : launch_attention(ln.a, st, pdl);
+    if (e != cudaSuccess) return cuda_fail(e, ln.kind == 0 ? "launch_gemv" : "launch_attention");
+    return ok();
+}
+
 static tb_status record_plan(tb_runner* r, cudaStream_t st, bool pdl) {
     for (const Launch& ln : r->plan) {
-        cudaError_t e = ln.kind == 0 ? launch_gemv(ln.g, st, pdl) : launch_attention(ln.a, st, pdl);
-        if (e != cudaSuccess) return cuda_fail(e, ln.kind == 0 ? "launch_gemv" : "launch_attention");
+        tb_status s = launch_op(r, ln, st, pdl);
+        if (s != TB_OK) return s;
     }
     return ok();
 }
@@ -1209,7 +1295,7 @@ static tb_status build_step(tb_runner* r) {
     tb_model* m = r->m;
     const tb_model_config& c = m->cfg;
     r->persistent_ok = false;
-    if (r->B != 1 || c.architecture != TB_ARCH_LLAMA || c.hidden_dim > 4096 || c.intermediate_dim % 4 != 0) return ok();
+    if (r->B != 1 || m->tp_world > 1 || c.architecture != TB_ARCH_LLAMA || c.hidden_dim > 4096 || c.intermediate_dim % 4 != 0) return ok();
     const Layer& L0 = m->layers[0];
     const int prec = L0.qkv.L.precision;
     auto same = [](const QLayout& a, const QLayout& b) {
@@ -1451,6 +1537,17 @@ extern "C" tb_status tb_runner_create(tb_model* m, int32_t max_batch, int32_t ma
     TB_CUDA(cudaEventCreate(&r->ev1));
     if ((s = build_plan(r.get())) != TB_OK) return s;
     if ((s = build_step(r.get())) != TB_OK) return s;
+    TB_CHECK(m->tp_world == 1 || (ctx->comm && ctx->tp_world == m->tp_world), "tensor-parallel model on a context "
+             "without its communicator (tb_context_init_tp)");
+    if (m->tp_world > 1) {
+        // One all-reduce of the step's size outside any graph capture, so the
+        // communicator's connections exist before the step graph records it.
+        TB_CUDA(cudaMemsetAsync(r->h.p, 0, (size_t)B * H * 4, ctx->stream));
+        std::string why;
+        cudaError_t e = nccl_allreduce_sum_f32(ctx->comm, r->h.as<float>(), (size_t)B * H, ctx->stream, why);
+        if (e != cudaSuccess) return fail(TB_ERR_CUDA, "tensor-parallel all-reduce: %s", why.c_str());
+        TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    }
     TB_CUDA(cudaDeviceSynchronize());
     *out = r.release();
     return ok();
@@ -1633,6 +1730,7 @@ extern "C" tb_status tb_runner_step_observed(tb_runner* r, int32_t token, float*
                                              float* layer_norms, float* attn_weights, int64_t attn_stride,
                                              float* final_hidden) {
     TB_CHECK(r, "NULL runner");
+    if (r->m->tp_world > 1) return fail(TB_ERR_UNSUPPORTED, "observer hooks need the whole model on one GPU");
     TB_CHECK(r->B == 1, "tb_runner_step_observed drives batch-1 runners");
     tb_model* m = r->m;
     const tb_model_config& c = m->cfg;
@@ -2001,9 +2099,8 @@ extern "C" tb_status tb_runner_profile_step(tb_runner* r, float* times_ms, int32
     cudaStream_t st = r->ctx->stream;
     TB_CUDA(cudaEventRecord(ev[0], st));
     for (int i = 0; i < cnt; ++i) {
-        const Launch& ln = r->plan[i];
-        cudaError_t ce = ln.kind == 0 ? launch_gemv(ln.g, st, false) : launch_attention(ln.a, st, false);
-        if (ce != cudaSuccess) return cuda_fail(ce, "profile launch");
+        tb_status ls = launch_op(r, r->plan[i], st, false);
+        if (ls != TB_OK) return ls;
         TB_CUDA(cudaEventRecord(ev[i + 1], st));
     }
     TB_CUDA(cudaEventSynchronize(ev[cnt]));

@@ -76,6 +76,15 @@ class Context:
     def check_device(self):
         call("tb_context_check_device", self.handle)
 
+    def init_tensor_parallel(self, unique_id: bytes, rank: int, world: int):
+        """Join the tensor-parallel communicator (`unique_id` from rank 0's
+        tp_unique_id(), shared out of band, e.g. a torch.distributed broadcast)."""
+        if len(unique_id) != 128:
+            raise ValueError("unique_id must be 128 bytes")
+        buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
+        call("tb_context_init_tp", self.handle, buf, int(rank), int(world))
+        self.tp = (int(rank), int(world))
+
     def close(self):
         if self.handle:
             for kind in ("runner", "model", "qweight"):
@@ -90,6 +99,13 @@ class Context:
             self.close()
         except Exception:
             pass
+
+
+def tp_unique_id() -> bytes:
+    """A fresh 128-byte NCCL communicator id (rank 0 draws it)."""
+    buf = (C.c_uint8 * 128)()
+    call("tb_tp_unique_id", buf)
+    return bytes(buf)
 
 
 def device_count() -> int:
@@ -178,6 +194,60 @@ def quantize(w: np.ndarray, mode: str = "perChannel", group_size: int = 32,
         call("tb_quantize_int4_group", ctx.handle, _ptr(w), cnt, group_size, _ptr(p), _ptr(s), _ptr(z))
         return QuantizedTensor((K, N), p, s, "int4", group_size, z)
     raise TinyBrainError(4, f"quantization mode {mode!r} is not on the decode path")
+
+
+def _unpack_nibbles(q: "QuantizedTensor") -> np.ndarray:
+    n = q.shape[0] * q.shape[1]
+    nib = np.empty(2 * q.data.size, dtype=np.uint8)
+    nib[0::2] = q.data >> 4
+    nib[1::2] = q.data & 0x0F
+    return nib[:n]
+
+
+def _pack_nibbles(nib: np.ndarray) -> np.ndarray:
+    if nib.size % 2:
+        nib = np.concatenate([nib, np.zeros(1, dtype=np.uint8)])
+    return ((nib[0::2] << 4) | nib[1::2]).astype(np.uint8)
+
+
+def shard_quantized(q: QuantizedTensor, axis: int, rank: int, world: int) -> QuantizedTensor:
+    """Slice of a quantized [in, out] weight for tensor-parallel rank `rank`:
+    axis 1 = a column shard (out features), axis 0 = a row shard (in features).
+
+    The slice is taken from the quantized bytes, so every kept element,
+    scale and zero point is bit-identical to the unsharded tensor.  INT4
+    groups run along the out dimension of the row-major [in][out] data
+    (QuantizedTensor.swift:502-560, groups of consecutive flat elements):
+    a shard must cut whole groups."""
+    K, N = q.shape
+    if axis not in (0, 1):
+        raise ValueError("axis must be 0 (rows) or 1 (columns)")
+    D = N if axis == 1 else K
+    if D % world:
+        raise ValueError(f"dimension {D} does not split over {world} ranks")
+    w = D // world
+    a, b = rank * w, (rank + 1) * w
+    if q.mode == "perChannel":
+        m = q.data.reshape(K, N)
+        if axis == 1:
+            return QuantizedTensor((K, w), np.ascontiguousarray(m[:, a:b]).ravel(),
+                                   np.ascontiguousarray(q.scales[a:b]), q.mode, q.group_size, None)
+        return QuantizedTensor((w, N), np.ascontiguousarray(m[a:b]).ravel(), q.scales.copy(), q.mode,
+                               q.group_size, None)
+    if q.mode != "int4":
+        raise TinyBrainError(4, f"cannot shard mode {q.mode!r}")
+    gs = q.group_size
+    if N % gs or (axis == 1 and w % gs):
+        raise ValueError(f"INT4 shard must cut whole groups of {gs} out features")
+    nib = _unpack_nibbles(q).reshape(K, N)
+    sc = q.scales[:K * N // gs].reshape(K, N // gs)
+    zp = q.zero_points[:K * N // gs].reshape(K, N // gs)
+    if axis == 1:
+        nb, s2, z2, shape = nib[:, a:b], sc[:, a // gs:b // gs], zp[:, a // gs:b // gs], (K, w)
+    else:
+        nb, s2, z2, shape = nib[a:b], sc[a:b], zp[a:b], (w, N)
+    return QuantizedTensor(shape, _pack_nibbles(np.ascontiguousarray(nb).ravel()),
+                           np.ascontiguousarray(s2).ravel(), "int4", gs, np.ascontiguousarray(z2).ravel())
 
 
 class QuantizedWeight:
@@ -313,27 +383,65 @@ class ModelWeights:
     output: LinearLayerWeights
     final_norm: Optional[np.ndarray] = None
 
-    def upload(self, ctx: Optional[Context] = None) -> "DeviceModel":
-        return DeviceModel(self, ctx)
+    def upload(self, ctx: Optional[Context] = None, tp: Optional[tuple] = None) -> "DeviceModel":
+        return DeviceModel(self, ctx, tp)
+
+
+# Which axis of each projection a tensor-parallel rank keeps: 1 = column
+# shard (heads / intermediate rows), 0 = row shard (partial sums).
+TP_AXIS = {"query": 1, "key": 1, "value": 1, "gate": 1, "up": 1, "output": 0, "down": 0}
+
+
+def shard_linear(lw: "LinearLayerWeights", axis: int, rank: int, world: int) -> "LinearLayerWeights":
+    """Tensor-parallel slice of a projection; a row shard's bias stays on rank 0
+    (the partial sums of all ranks are added up once)."""
+    b = lw.bias
+    if b is not None:
+        if axis == 1:
+            w = b.size // world
+            b = np.ascontiguousarray(b[rank * w:(rank + 1) * w])
+        elif rank != 0:
+            b = None
+    return LinearLayerWeights(shard_quantized(lw.weights, axis, rank, world), b)
+
+
+def shard_layer(ly: "TransformerLayerWeights", rank: int, world: int) -> "TransformerLayerWeights":
+    kw = {}
+    for name, axis in TP_AXIS.items():
+        lw = getattr(ly, name)
+        kw[name] = None if lw is None else shard_linear(lw, axis, rank, world)
+    return TransformerLayerWeights(input_norm=ly.input_norm, post_attention_norm=ly.post_attention_norm, **kw)
 
 
 class DeviceModel:
-    """ModelWeights uploaded to HBM (fused QKV and gate/up, GPU tile layout)."""
+    """ModelWeights uploaded to HBM (fused QKV and gate/up, GPU tile layout).
 
-    def __init__(self, w: ModelWeights, ctx: Optional[Context] = None):
+    tp=(rank, world): this GPU's tensor-parallel shard.  `w` holds either the
+    whole model (sliced here) or layers already sharded for this rank
+    (w.tp == tp, as make_llama_model(shard=...) builds them); the context
+    must have joined the communicator (Context.init_tensor_parallel)."""
+
+    def __init__(self, w: ModelWeights, ctx: Optional[Context] = None, tp: Optional[tuple] = None):
         self.ctx = ctx or Context.default()
         self.config = w.config
+        self.tp = tuple(tp) if tp else (0, 1)
         cfg = w.config.to_c()
         h = C.c_void_p()
         call("tb_model_create", self.ctx.handle, C.byref(cfg), C.byref(h))
         self.handle = h
         _LIVE["model"].add(self)
+        rank, world = self.tp
+        pre_sharded = getattr(w, "tp", (0, 1)) == self.tp and world > 1
+        if world > 1:
+            call("tb_model_set_tensor_parallel", h, rank, world)
         emb = np.ascontiguousarray(w.token_embeddings, dtype=np.float32)
         call("tb_model_set_embedding", h, _ptr(emb))
         if w.final_norm is not None:
             fn = np.ascontiguousarray(w.final_norm, dtype=np.float32)
             call("tb_model_set_final_norm", h, _ptr(fn))
         for i, ly in enumerate(w.layers):
+            if world > 1 and not pre_sharded:
+                ly = shard_layer(ly, rank, world)
             ni = None if ly.input_norm is None else np.ascontiguousarray(ly.input_norm, dtype=np.float32)
             npn = None if ly.post_attention_norm is None else np.ascontiguousarray(ly.post_attention_norm,
                                                                                     dtype=np.float32)
@@ -479,7 +587,7 @@ class ModelRunner:
 
     def _step_observed(self, token_id: int):
         c = self.config
-        pos = self.current_position()
+        pos = self.current_position
         L = pos + 1
         logits = np.empty(c.vocab_size, dtype=np.float32)
         norms = np.empty(c.num_layers, dtype=np.float32)

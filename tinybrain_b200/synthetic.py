@@ -18,8 +18,8 @@ from typing import Optional
 
 import numpy as np
 
-from .runtime import (Context, LinearLayerWeights, ModelConfig, ModelWeights, SeededGenerator,
-                      TransformerLayerWeights, quantize)
+from .runtime import (TP_AXIS, Context, LinearLayerWeights, ModelConfig, ModelWeights, SeededGenerator,
+                      TransformerLayerWeights, quantize, shard_linear)
 
 TINYLLAMA = dict(num_layers=22, hidden_dim=2048, num_heads=32, num_kv_heads=4, vocab_size=32000,
                  intermediate_dim=5632, max_seq_len=2048)
@@ -29,14 +29,20 @@ TOY = dict(num_layers=2, hidden_dim=128, num_heads=4, num_kv_heads=4, vocab_size
            intermediate_dim=512, max_seq_len=256, architecture="toy")
 
 
+_FIELD = {"q": "query", "k": "key", "v": "value", "o": "output", "gate": "gate", "up": "up", "down": "down"}
+
+
 def _q(w, mode, group_size, ctx):
     return quantize(w, mode, group_size, ctx)
 
 
 def make_llama_model(config: ModelConfig, seed: int = 0, mode: str = "perChannel", group_size: int = 32,
                      std: float = 0.02, ctx: Optional[Context] = None,
-                     keep_float: bool = False) -> ModelWeights:
-    """LLaMA-shaped decoder with N(0, std) weights drawn in the documented order."""
+                     keep_float: bool = False, shard: Optional[tuple] = None) -> ModelWeights:
+    """LLaMA-shaped decoder with N(0, std) weights drawn in the documented order.
+
+    shard=(rank, world) keeps only that tensor-parallel rank's slice of every
+    layer projection (the draws are the same; the model's .tp says so)."""
     ctx = ctx or Context.default()
     g = SeededGenerator(seed)
     H, I, V, kvd = config.hidden_dim, config.intermediate_dim, config.vocab_size, config.kv_dim
@@ -50,7 +56,10 @@ def make_llama_model(config: ModelConfig, seed: int = 0, mode: str = "perChannel
             w = g.normal(shape, 0.0, std)
             if keep_float:
                 floats[(li, name)] = w
-            proj[name] = LinearLayerWeights(_q(w, mode, group_size, ctx))
+            lw = LinearLayerWeights(_q(w, mode, group_size, ctx))
+            if shard and shard[1] > 1:
+                lw = shard_linear(lw, TP_AXIS[_FIELD[name]], shard[0], shard[1])
+            proj[name] = lw
         ones = np.ones(H, dtype=np.float32)
         layers.append(TransformerLayerWeights(query=proj["q"], key=proj["k"], value=proj["v"], output=proj["o"],
                                               gate=proj["gate"], up=proj["up"], down=proj["down"],
@@ -62,6 +71,8 @@ def make_llama_model(config: ModelConfig, seed: int = 0, mode: str = "perChannel
                          final_norm=np.ones(H, dtype=np.float32))
     if keep_float:
         model.float_weights = floats
+    if shard and shard[1] > 1:
+        model.tp = tuple(shard)
     return model
 
 
