@@ -82,7 +82,9 @@ def test_gemv_int8_shapes(ctx, K, N, M):
 
 
 @pytest.mark.parametrize("K,N,M,gs", [(2048, 4096, 1, 32), (11008, 4096, 1, 32), (1000, 64, 1, 32),
-                                      (4096, 256, 2, 128), (5632, 2048, 1, 32), (1024, 512, 7, 32)])
+                                      (4096, 256, 2, 128), (5632, 2048, 1, 32), (1024, 512, 7, 32),
+                                      (100, 96, 3, 32), (4096, 22016, 1, 32), (2048, 2560, 16, 32),
+                                      (1376, 4096, 33, 32), (2048, 1024, 64, 64), (4096, 32000, 4, 32)])
 def test_gemv_int4_shapes(ctx, K, N, M, gs):
     g = SeededGenerator(K * 3 + N)
     w = g.normal((K, N), 0.0, 0.02)

@@ -30,8 +30,7 @@ def small_cfg(**kw):
     return ModelConfig(**base)
 
 
-@pytest.mark.parametrize("persistent", [True, False])
-@pytest.mark.parametrize("mode", ["perChannel", "int4"])
+@pytest.mark.parametrize("mode,persistent", [("perChannel", True), ("perChannel", False), ("int4", False)])
 def test_step_logits_and_kv_state(ctx, mode, persistent):
     w = small_llama(small_cfg(), seed=3, mode=mode)
     r = ModelRunner(w, ctx)
@@ -62,10 +61,10 @@ def test_toy_model_greedy_identity(ctx):
     assert_same_tokens(got, want, gaps)
 
 
-@pytest.mark.parametrize("persistent", ["flow", "barrier", False])
-@pytest.mark.parametrize("mode", ["perChannel", "int4"])
+@pytest.mark.parametrize("mode,persistent", [("perChannel", "flow"), ("perChannel", "barrier"),
+                                             ("perChannel", False), ("int4", False)])
 def test_generate_greedy_identity(ctx, mode, persistent, monkeypatch):
-    if persistent:  # INT4 always takes the grid-barrier persistent kernel
+    if persistent:
         monkeypatch.setenv("TB_STEP_KERNEL", persistent)
     w = small_llama(small_cfg(num_layers=3), seed=4, mode=mode)
     r = ModelRunner(w, ctx)
@@ -163,7 +162,9 @@ def test_persistent_available_for_batch1_llama_only(ctx):
     assert not r.persistent  # the per-projection launch chain is the default
     r.persistent = True
     assert r.persistent
-    for other in (ModelRunner(w, ctx, max_batch=2), ModelRunner(toy_model(), ctx)):
+    # batch > 1, the toy architecture and INT4 weights keep the launch chain
+    w4 = small_llama(small_cfg(), seed=9, mode="int4")
+    for other in (ModelRunner(w, ctx, max_batch=2), ModelRunner(toy_model(), ctx), ModelRunner(w4, ctx)):
         with pytest.raises(TinyBrainError):
             other.persistent = True
 
@@ -173,7 +174,7 @@ def test_persistent_available_for_batch1_llama_only(ctx):
                                         num_layers=1),
                                    dict(hidden_dim=2048, num_heads=32, num_kv_heads=4, intermediate_dim=5632,
                                         vocab_size=32000)])
-@pytest.mark.parametrize("mode,kernel", [("perChannel", "flow"), ("perChannel", "barrier"), ("int4", "barrier")])
+@pytest.mark.parametrize("mode,kernel", [("perChannel", "flow"), ("perChannel", "barrier")])
 def test_persistent_other_shapes(ctx, shape, mode, kernel, monkeypatch):
     # MHA (G = 1), one layer with a short last slab, and the TinyLlama layer
     # shape; INT8 through both persistent kernels (dataflow and grid-barrier)

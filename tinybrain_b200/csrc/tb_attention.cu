@@ -55,9 +55,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         }
         fence_barrier_init();
     }
+    if (threadIdx.x == 0) {
+        trace_min(p.trace, 0);
+        trace_max(p.trace, 1);
+    }
     __syncthreads();
     pdl_launch_dependents();
     pdl_wait();
+    if (threadIdx.x == 0) trace_max(p.trace, 2);
 
     const SeqState& sq = p.seq[m];
     const bool active = p.lens ? true : (sq.active != 0);
@@ -231,6 +236,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             }
         }
     }
+    if (threadIdx.x == 0) trace_max(p.trace, 6);
 }
 
 template <int G, int D>

@@ -31,6 +31,14 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     return t;
 }
 
+// Timeline probes (launch tracing): earliest / latest event over the CTAs.
+__device__ __forceinline__ void trace_min(unsigned long long* t, int i) {
+    if (t) atomicMin(t + i, (unsigned long long)global_timer_ns());
+}
+__device__ __forceinline__ void trace_max(unsigned long long* t, int i) {
+    if (t) atomicMax(t + i, (unsigned long long)global_timer_ns());
+}
+
 __device__ __forceinline__ void record_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
 }

@@ -36,23 +36,23 @@ QLayout make_qlayout(int precision, int K, int N, int RB) {
     L.K = K;
     L.N = N;
     L.fused_gu = RB == 64 ? 1 : 0;
-    if (precision == 8) {
-        L.Kp = (K + kTcUnitK - 1) / kTcUnitK * kTcUnitK;
-        L.RB = kTcTileRows;
-        L.slab_k = kTcUnitK;
-        L.slab_bytes = kTcUnitK;
-        L.row_bytes = L.Kp;
-    } else {
-        L.Kp = (K + 31) / 32 * 32;
-        L.RB = RB;
-        L.slab_k = 2 * kSlabBytes;
-        L.slab_bytes = kSlabBytes;
-        L.row_bytes = L.Kp / 2;
-    }
+    // Both precisions: 128-row tiles streamed in units of 128 k (tb_tc.cuh).
+    L.Kp = (K + kTcUnitK - 1) / kTcUnitK * kTcUnitK;
+    L.RB = kTcTileRows;
+    L.slab_k = kTcUnitK;
+    L.slab_bytes = precision == 8 ? kTcUnitK : kTcUnitK / 2;
+    L.row_bytes = precision == 8 ? L.Kp : L.Kp / 2;
     L.Np = (N + L.RB - 1) / L.RB * L.RB;
-    L.slabs = (L.row_bytes + L.slab_bytes - 1) / L.slab_bytes;
-    L.weight_bytes = (size_t)L.Np * L.row_bytes;
-    L.scale_floats = precision == 8 ? (size_t)L.Np : (size_t)(L.Np / 32) * L.slabs * 1024;
+    L.slabs = L.Kp / kTcUnitK;
+    if (precision == 8) {
+        L.weight_bytes = (size_t)L.Np * L.row_bytes;
+        L.scale_floats = (size_t)L.Np;  // per-row scales
+    } else {
+        // units carry their group scales inline; the scale buffer holds the
+        // per-(32-row group, unit) maximum |scale|
+        L.weight_bytes = (size_t)(L.Np / kTcTileRows) * L.slabs * kQ4UnitBytes;
+        L.scale_floats = (size_t)(L.Np / 32) * L.slabs;
+    }
     return L;
 }
 
@@ -60,15 +60,26 @@ namespace {
 
 template <int PREC, int RB>
 struct GemvCfg {
-    static constexpr int RPW = RB / kGemvConsumerWarps;               // rows per warp (INT4)
-    static constexpr int kWeightStage = PREC == 8 ? kTcUnitBytes : RB * kSlabBytes;  // bytes
-    static constexpr int kScaleStage = PREC == 4 ? (RB / 32) * 1024 * 4 : 0;
-    static constexpr int kStageBytes = kWeightStage + kScaleStage;
-    static constexpr int kStages = PREC == 8 ? 6 : (kStageBytes <= 20480) ? 4 : (kStageBytes <= 32768 ? 3 : 2);
-    static constexpr int kCH = 32;                                     // INT4 k values per lane per slab
+    static constexpr int kStageBytes = PREC == 8 ? kTcUnitBytes : kQ4UnitBytes;
+    static constexpr int kStages = PREC == 8 ? 6 : 8;
 };
-// Digit rows of the INT8 B operand for MB batch rows (4 digits each; N >= 8, 16-multiples past 8).
+// Digit rows of the B operand for MB batch rows: INT8 4 digits per row (N >= 8,
+// 16-multiples past 8); INT4 4 digits per (row, 32-row weight group).
 __host__ __device__ constexpr int tc_nb(int mb) { return mb <= 2 ? 8 : (4 * mb + 15) / 16 * 16; }
+__host__ __device__ constexpr int q4_nb(int mb) { return 16 * mb; }
+// INT4 tensor memory: A slots [2 warpgroups][2] x 32 columns, then one
+// accumulator of max(NB, 32) columns per warpgroup.
+constexpr int kQ4ASlots = 2;
+__host__ __device__ constexpr int q4_dcols(int mb) { return q4_nb(mb) < 32 ? 32 : q4_nb(mb); }
+// At most 256 columns: two CTAs of any GEMV variant fit one SM's 512 together,
+// so a CTA never waits in tcgen05.alloc for another one to finish.
+__host__ __device__ constexpr int q4_tmem_cols(int mb) { return 256; }
+// Batch rows handled by one CTA.
+inline int gemv_mb(int prec, int M) {
+    const int cap = prec == 8 ? 16 : 4;  // INT4: A slots + two accumulators fit 256 TMEM columns
+    const int mb = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16;
+    return std::min(mb, cap);
+}
 
 __device__ __forceinline__ float silu_ref(float x) {
     // Tensor.swift:1135-1142: x / (1 + exp(-x))
@@ -85,16 +96,21 @@ __device__ __forceinline__ float gelu_ref(float x) {
 template <int PREC, int RB, int MB>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
     using Cfg = GemvCfg<PREC, RB>;
+    static_assert(RB == kTcTileRows, "tensor-core tiles are 128 rows");
     constexpr int STAGES = Cfg::kStages;
-    constexpr int RPW = Cfg::RPW;
-    constexpr int CH = Cfg::kCH;
-    constexpr int NB = tc_nb(MB);
+    constexpr int NB = PREC == 8 ? tc_nb(MB) : q4_nb(MB);
+    static_assert(NB <= 256, "tcgen05 N is at most 256");
+    // accumulator (INT8: NB columns; INT4: A slots + two accumulators), a power of two >= 32
+    static_assert(PREC != 4 || 2 * kQ4ASlots * 32 + 2 * q4_dcols(MB) <= q4_tmem_cols(MB), "INT4 TMEM budget");
+    constexpr uint32_t kTmemCols = PREC == 4 ? (uint32_t)q4_tmem_cols(MB)
+                                             : (NB <= 32 ? 32u : NB <= 64 ? 64u : NB <= 128 ? 128u : 256u);
 
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + STAGES;
-    uint64_t* done = empty + STAGES;                                      // INT8: accumulator complete
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* done = empty + STAGES;                                      // [2] accumulators complete
+    uint64_t* afree = done + 2;                                           // INT4: [2 warpgroups][kQ4ASlots]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(afree + 2 * kQ4ASlots);
     float* red = reinterpret_cast<float*>(smem + 256);                    // [RB][MB]
     float* misc = red + RB * MB;                                          // [2][MB][8]
     float* rowsc = misc + 16 * MB;                                        // [RB] row scales (1 for INT4)
@@ -102,8 +118,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     int* seqinfo = reinterpret_cast<int*>(rowbias + RB);                  // [3][MB] pos, active, page
     uint8_t* stage_base = smem + (256 + (RB * MB + 16 * MB + 2 * RB + 3 * MB) * 4 + 1023) / 1024 * 1024;
     uint8_t* xbuf = stage_base + STAGES * Cfg::kStageBytes;
-    float* xs = reinterpret_cast<float*>(xbuf);   // INT4: lane-interleaved fp32 activations
-    uint8_t* xd = xbuf;                           // INT8: digit operand [k/16][NB][16]
+    uint8_t* xd = xbuf;  // INT8: digit operand [k/16][NB][16]
 
     const QLayout& L = p.L;
     const int P = p.P;
@@ -116,19 +131,29 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     // batch rows [m0, m0 + Mloc) of this CTA (grid y splits batches larger than MB)
     const int m0 = blockIdx.y * MB;
     const int Mloc = min(MB, p.M - m0);
+    // INT4 staging (after the stage ring): x [MB][kspan] fp32, B slots
+    // [2][kQ4ASlots][NB * 128], per-unit max |x| [nunits][MB], per-unit max
+    // |scale| [4][nunits], digit exponents [MB][4]
+    const int kspan = ((L.slabs + P - 1) / P) * kTcUnitK;
+    float* xs = reinterpret_cast<float*>(xbuf);
+    uint8_t* bslots = xbuf + (size_t)MB * kspan * 4;
+    float* xmax = reinterpret_cast<float*>(bslots + 2 * kQ4ASlots * NB * 128);
+    float* smaxs = xmax + (size_t)(kspan / kTcUnitK) * MB;
+    int* ex4 = reinterpret_cast<int*>(smaxs + kQ4Groups * (kspan / kTcUnitK));
 
     if (threadIdx.x == 0) {
+        trace_min(p.trace, 0);
+        trace_max(p.trace, 1);
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], PREC == 8 ? 1 : kGemvConsumerWarps);  // INT8: released by tcgen05.commit
+            mbar_init(&empty[i], 1);  // released by tcgen05.commit
         }
-        mbar_init(done, 1);
+        mbar_init(&done[0], 1);
+        mbar_init(&done[1], 1);
+        for (int i = 0; i < 2 * kQ4ASlots; ++i) mbar_init(&afree[i], 1);
         fence_barrier_init();
     }
-    // accumulator: NB int32 columns (4 digit rows per batch row); allocation is a power of two >= 32
-    constexpr uint32_t kTmemCols = NB <= 32 ? 32u : NB <= 64 ? 64u : NB <= 128 ? 128u : 256u;
-    static_assert(PREC != 8 || NB <= 256, "tcgen05 N is at most 256");
-    if (PREC == 8 && warp == 0) tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -138,27 +163,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         // ------------------------------- producer -------------------------------
         if (lane == 0) {
             const uint64_t pol = l2_policy_evict_first();
-            const uint8_t* wrb = p.w + (size_t)rb * RB * L.row_bytes;
-            const float* srb = (PREC == 4) ? p.scales + (size_t)rb * (RB / 32) * L.slabs * 1024 : nullptr;
+            const uint8_t* wrb = p.w + (size_t)rb * L.slabs * Cfg::kStageBytes;
             for (int i = 0; i < nunits; ++i) {
                 const int st = i % STAGES;
                 if (i >= STAGES) {
                     if (!mbar_wait(&empty[st], ((i / STAGES) - 1) & 1, p.err)) break;
                 }
-                const int s = s0 + i;
                 uint8_t* dst = stage_base + st * Cfg::kStageBytes;
-                if (PREC == 8) {
-                    mbar_arrive_expect_tx(&full[st], kTcUnitBytes);
-                    bulk_g2s_stream(dst, wrb + (size_t)s * kTcUnitBytes, kTcUnitBytes, &full[st], pol);
-                } else {
-                    const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-                    const uint32_t wbytes = (uint32_t)(RB * sb);
-                    const uint32_t sbytes = (uint32_t)Cfg::kScaleStage;
-                    mbar_arrive_expect_tx(&full[st], wbytes + sbytes);
-                    bulk_g2s_stream(dst, wrb + (size_t)s * RB * kSlabBytes, wbytes, &full[st], pol);
-                    bulk_g2s_stream(dst + Cfg::kWeightStage, srb + (size_t)s * (RB / 32) * 1024, sbytes, &full[st],
-                                    pol);
-                }
+                mbar_arrive_expect_tx(&full[st], Cfg::kStageBytes);
+                bulk_g2s_stream(dst, wrb + (size_t)(s0 + i) * Cfg::kStageBytes, Cfg::kStageBytes, &full[st], pol);
             }
         }
     } else {
@@ -170,7 +183,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             rowsc[i] = PREC == 8 ? __ldg(p.scales + grow) : 1.0f;
             rowbias[i] = p.bias ? __ldg(p.bias + grow) : 0.0f;
         }
+        if (PREC == 4)
+            for (int i = ctid; i < kQ4Groups * nunits; i += 256) {
+                const int g = i / nunits, u = i - g * nunits;
+                smaxs[g * nunits + u] = __ldg(p.scales + ((size_t)rb * kQ4Groups + g) * L.slabs + s0 + u);
+            }
         pdl_wait();
+        if (ctid == 0) trace_max(p.trace, 2);
         if (p.epilogue == kEpiQkv && ctid < Mloc) {
             const SeqState& sq = p.seq_ro[m0 + ctid];
             const int pos = sq.pos;
@@ -178,7 +197,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             seqinfo[MB + ctid] = sq.active;
             seqinfo[2 * MB + ctid] = sq.active ? p.page_table[(size_t)(m0 + ctid) * p.ptab_stride + pos / kPageTokens] : -1;
         }
-        const int xstride = (L.slabs + P - 1) / P * L.slab_k;
         const int kbeg = s0 * L.slab_k;
         const int kend = min(s1 * L.slab_k, L.Kp);
         const bool rms = p.prologue == kProRmsNorm || p.prologue == kProEmbedRms;
@@ -313,6 +331,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             }
             fence_proxy_async_shared();
             named_bar_sync(1, 256);
+            if (ctid == 0) trace_max(p.trace, 3);
             const uint32_t tmem = *tmem_slot;
             if (warp == 0) {
                 tc_fence_after();
@@ -320,17 +339,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                     for (int i = 0; i < nunits; ++i) {
                         const int st = i % STAGES;
                         if (!mbar_wait(&full[st], (i / STAGES) & 1, p.err)) break;
+                        if (i == 0) trace_max(p.trace, 7);
                         tc_fence_after();
                         tc_unit_mma(tmem, smem_u32(stage_base + st * Cfg::kStageBytes),
                                     smem_u32(xd + (size_t)i * (kTcUnitK / 16) * NB * 16), NB, i > 0);
                         tc_commit(&empty[st]);
                     }
-                    tc_commit(done);
+                    tc_commit(&done[0]);
                 }
                 __syncwarp();
             } else if (warp >= 4) {
                 // Epilogue warps: TMEM lanes 32 * (warp - 4) .. +31 = tile rows.
-                const bool okd = mbar_wait(done, 0, p.err);
+                const bool okd = mbar_wait(&done[0], 0, p.err);
+                if (warp == 4 && lane == 0) trace_max(p.trace, 4);
                 tc_fence_after();
                 int d[NB];
 #pragma unroll
@@ -347,48 +368,129 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                 tc_fence_before();
             }
         } else {
-            // Stage x[m][kbeg:kend) into shared memory, lane-interleaved per slab.
-            for (int m = 0; m < MB; ++m) {
-                for (int k = kbeg + ctid; k < kend; k += 256) {
-                    float v = xval(m, k) * int4_pos_scale(k & 7);
-                    const int rel = k - kbeg;
-                    const int ls = rel / L.slab_k;
-                    xs[m * xstride + ls * L.slab_k + xperm<CH>(rel - ls * L.slab_k)] = v;
+            // ---- INT4 on the tensor cores ----
+            // (1) x[m][kbeg:kend) (normalised) into shared memory, and the
+            //     largest |x| of every unit (one warp covers one unit per pass).
+            const int ngroups = kspan / 4;
+            for (int g = ctid; g < ngroups; g += 256) {
+                const int k = kbeg + 4 * g;
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    const float4 v = k < kend ? xval4(m, k) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    *reinterpret_cast<float4*>(xs + (size_t)m * kspan + 4 * g) = v;
+                    float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    const int u = g >> 5;  // 32 float4 per unit
+                    if (lane == 0 && u < nunits) xmax[u * MB + m] = mx;
                 }
             }
             named_bar_sync(1, 256);
-
-            float2 acc[RPW][MB];
-#pragma unroll
-            for (int r = 0; r < RPW; ++r)
-#pragma unroll
-                for (int m = 0; m < MB; ++m) acc[r][m] = make_float2(0.0f, 0.0f);
-
-            for (int i = 0; i < nunits; ++i) {
-                const int st = i % STAGES;
-                // On a timed-out wait the results are garbage; the error word tells the host.
-                if (!mbar_wait(&full[st], (i / STAGES) & 1, p.err)) break;
-                const int s = s0 + i;
-                const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-                const uint8_t* wst = stage_base + st * Cfg::kStageBytes;
-                {
-                    const float* ssl = reinterpret_cast<const float*>(wst + Cfg::kWeightStage) +
-                                       ((warp * RPW) / 32) * 1024;
-                    unit_dot<PREC, RPW, MB>(wst, sb, warp * RPW, ssl, xs + i * L.slab_k, xstride, lane, acc);
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[st]);
+            // (2) digit exponent of every (batch row, row group): |scale * x| is
+            //     bounded by the per-unit maxima (one rounding margin).
+            if (ctid < MB * kQ4Groups) {
+                const int m = ctid >> 2, g = ctid & 3;
+                float b = 0.0f;
+                for (int u = 0; u < nunits; ++u) b = fmaxf(b, __fmul_rn(smaxs[g * nunits + u], xmax[u * MB + m]));
+                ex4[ctid] = digit_exponent(b * 1.0000004f);
             }
-            // Warp reduction: every lane ends with the full row sums.
+            named_bar_sync(1, 256);
+            if (ctid == 0) trace_max(p.trace, 3);
+            // (3) units alternate between the two warpgroups; each expands its
+            //     unit's nibbles into the A slot in tensor memory, writes the
+            //     digits of scale * x into its B slot, and its leader issues
+            //     the four K = 32 products into the warpgroup's accumulator.
+            const uint32_t tmem = *tmem_slot;
+            const int wg = warp >> 2, wq = warp & 3;
+            const int t = ctid & 127;
+            const uint32_t lane_base = (uint32_t)(32 * wq) << 16;
+            const uint32_t dcol = (uint32_t)(2 * kQ4ASlots * 32 + wg * q4_dcols(MB));
+            const uint32_t idesc = tc_idesc_i8(NB);
+            // One thread per warpgroup waits (bounded) and tells the others
+            // through `okflag`, so a timed-out wait ends the loop of the whole
+            // warpgroup together (its named barriers stay matched).
+            volatile int* okflag = reinterpret_cast<volatile int*>(misc) + 2 + wg;
+            int j = 0;
+            for (int i = wg; i < nunits; i += 2, ++j) {
+                const int st = i % STAGES;
+                const int slot = j & 1;
+                if (t == 0) {
+                    bool ok = mbar_wait(&full[st], (i / STAGES) & 1, p.err);
+                    if (ok && j >= kQ4ASlots) ok = mbar_wait(&afree[wg * kQ4ASlots + slot], ((j >> 1) - 1) & 1, p.err);
+                    *okflag = ok ? 1 : 0;
+                }
+                named_bar_sync(2 + wg, 128);
+                if (!*okflag) break;
+                tc_fence_after();
+                const uint8_t* ust = stage_base + st * Cfg::kStageBytes;
+                // B: 4 consecutive k (quad q) of row group gq for every batch row
+                {
+                    const int q = t & 31, gq = t >> 5;
+                    const float4 sc = *reinterpret_cast<const float4*>(ust + kQ4UnitNibBytes + (gq * kTcUnitK + 4 * q) * 4);
+                    uint8_t* bs = bslots + (size_t)(wg * kQ4ASlots + slot) * NB * 128;
 #pragma unroll
-            for (int r = 0; r < RPW; ++r)
+                    for (int m = 0; m < MB; ++m) {
+                        const float4 x = *reinterpret_cast<const float4*>(xs + (size_t)m * kspan + i * kTcUnitK + 4 * q);
+                        const float4 v = make_float4(__fmul_rn(sc.x, x.x), __fmul_rn(sc.y, x.y), __fmul_rn(sc.z, x.z),
+                                                     __fmul_rn(sc.w, x.w));
+                        put_digits4(bs, NB, 4 * q, m * kQ4Groups + gq, v,
+                                    __int_as_float((127 - ex4[m * kQ4Groups + gq]) << 23));
+                    }
+                }
+                // A: this thread's row (TMEM lane) = 32 * wq + lane
+                {
+                    uint32_t a[32];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint4 w = *reinterpret_cast<const uint4*>(ust + (c * kTcTileRows + 32 * wq + lane) * 16);
+                        q4_expand(w.x, a[8 * c + 0], a[8 * c + 1]);
+                        q4_expand(w.y, a[8 * c + 2], a[8 * c + 3]);
+                        q4_expand(w.z, a[8 * c + 4], a[8 * c + 5]);
+                        q4_expand(w.w, a[8 * c + 6], a[8 * c + 7]);
+                    }
+                    tmem_st32(tmem + lane_base + (uint32_t)((wg * kQ4ASlots + slot) * 32), a);
+                }
+                tmem_st_wait();
+                fence_proxy_async_shared();
+                tc_fence_before();
+                named_bar_sync(2 + wg, 128);
+                if (t == 0) {
+                    tc_fence_after();
+                    const uint32_t acol = tmem + (uint32_t)((wg * kQ4ASlots + slot) * 32);
+                    const uint32_t bsa = smem_u32(bslots + (size_t)(wg * kQ4ASlots + slot) * NB * 128);
+#pragma unroll
+                    for (int s = 0; s < kTcUnitK / 32; ++s)
+                        tc_mma_i8_ts(tmem + dcol, acol + 8 * s, tc_sdesc(bsa + s * 2 * NB * 16, NB * 16, 128), idesc,
+                                     j > 0 || s > 0);
+                    tc_commit(&empty[st]);
+                    tc_commit(&afree[wg * kQ4ASlots + slot]);
+                }
+            }
+            if (t == 0 && j > 0) tc_commit(&done[wg]);
+            // (4) epilogue: warpgroup 0 reads both accumulators; lane row
+            //     32 * wq + lane belongs to row group wq.
+            if (wg == 0) {
+                const bool h0 = nunits > 0, h1 = nunits > 1;
+                bool okd = true;
+                if (h0) okd = mbar_wait(&done[0], 0, p.err) && okd;
+                if (h1) okd = mbar_wait(&done[1], 0, p.err) && okd;
+                if (t == 0) trace_max(p.trace, 4);
+                tc_fence_after();
+                const int row = 32 * wq + lane;
 #pragma unroll
                 for (int m = 0; m < MB; ++m) {
-                    float v = acc[r][m].x + acc[r][m].y;
+                    const uint32_t c = (uint32_t)((m * kQ4Groups + wq) * kTcDigits);
+                    int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
+                    if (h0) tmem_ld4(tmem + lane_base + (uint32_t)(2 * kQ4ASlots * 32) + c, d0);
+                    if (h1) tmem_ld4(tmem + lane_base + (uint32_t)(2 * kQ4ASlots * 32 + q4_dcols(MB)) + c, d1);
+                    tmem_ld_wait();
+                    int d[4];
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                    if (lane == 0) red[(warp * RPW + r) * MB + m] = v;
+                    for (int e = 0; e < 4; ++e) d[e] = d0[e] + d1[e];
+                    red[row * MB + m] = okd ? combine_digits(d, ex4[m * kQ4Groups + wq]) : 0.0f;
                 }
+                tc_fence_before();
+            }
         }
     }
 
@@ -398,13 +500,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         cluster_sync();
     else
         __syncthreads();
-    if (PREC == 8 && warp == 0) {  // every tcgen05.ld of the epilogue completed before the barrier
+    if (warp == 0) {  // every tcgen05.ld of the epilogue completed before the barrier
         tc_fence_after();
         tmem_dealloc(*tmem_slot, kTmemCols);
     }
 
     if (warp < kGemvConsumerWarps) {
         const int ctid = threadIdx.x;
+        if (ctid == 0) trace_max(p.trace, 5);
         // Output items handled by this rank: a contiguous chunk.
         constexpr int HALF = RB / 2;  // fused gate/up: gate rows [0, HALF), up rows [HALF, RB)
         const int nout = (p.epilogue == kEpiQkv || p.epilogue == kEpiSiluMul) ? HALF : RB;
@@ -570,7 +673,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         }
     }
     __syncwarp();
+    if (threadIdx.x == 0) trace_max(p.trace, 6);
     if (P > 1) cluster_sync();
+}
+
+// Staged activation bytes of a CTA: INT8 digits (NB per k); INT4 fp32 x,
+// B slots, per-unit maxima and exponents.
+inline size_t gemv_xbytes(int prec, int mb, const QLayout& L, int P) {
+    const size_t units = (size_t)((L.slabs + P - 1) / P);
+    if (prec == 8) return units * kTcUnitK * (size_t)tc_nb(mb);
+    return units * kTcUnitK * mb * 4 + (size_t)2 * kQ4ASlots * q4_nb(mb) * 128 + units * (mb + kQ4Groups) * 4 +
+           (size_t)mb * kQ4Groups * 4;
 }
 
 template <int PREC, int RB, int MB>
@@ -578,9 +691,7 @@ size_t gemv_smem_bytes(const QLayout& L, int P) {
     using Cfg = GemvCfg<PREC, RB>;
     size_t head = (256 + (size_t)(RB * MB + 16 * MB + 2 * RB + 3 * MB) * 4 + 1023) / 1024 * 1024;
     size_t stages = (size_t)Cfg::kStages * Cfg::kStageBytes;
-    const size_t per_k = PREC == 8 ? (size_t)tc_nb(MB) : (size_t)MB * 4;
-    size_t xbytes = ((L.slabs + P - 1) / P) * (size_t)L.slab_k * per_k;
-    return head + stages + xbytes;
+    return head + stages + gemv_xbytes(PREC, MB, L, P);
 }
 
 template <int PREC, int RB, int MB>
@@ -614,23 +725,42 @@ cudaError_t launch_t(const GemvParams& p, cudaStream_t stream, bool pdl) {
 }  // namespace
 
 int choose_ksplit(const QLayout& L, int M, int num_sms) {
+    // Pick the cluster size P (k split) so that every CTA of the launch is
+    // resident at once (no second wave: a wave boundary costs a whole CTA
+    // lifetime) while each CTA streams as few units as possible.
     const int nrb = L.Np / L.RB;
-    int P = 1;
-    // Keep the staged activation slice modest and give every SM about two CTAs.
-    const int mb = L.precision == 8 ? (M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16) : std::min(M, 2);
-    const size_t per_k = L.precision == 8 ? (size_t)tc_nb(mb) : (size_t)mb * 4;
-    auto xbytes = [&](int q) { return ((L.slabs + q - 1) / q) * (size_t)L.slab_k * per_k; };
+    const int mb = gemv_mb(L.precision, M);
     const int splits = (M + mb - 1) / mb;  // grid y
-    while (P < 8 && P * 2 <= L.slabs && (nrb * P * splits < 2 * num_sms || xbytes(P) > 48 * 1024)) P *= 2;
-    while (P < L.slabs && P < 8 && xbytes(P) > 96 * 1024) ++P;
-    return P;
+    const size_t head = (256 + (size_t)(L.RB * mb + 16 * mb + 2 * L.RB + 3 * mb) * 4 + 1023) / 1024 * 1024;
+    const size_t stages = L.precision == 8 ? (size_t)GemvCfg<8, 128>::kStages * GemvCfg<8, 128>::kStageBytes
+                                           : (size_t)GemvCfg<4, 128>::kStages * GemvCfg<4, 128>::kStageBytes;
+    constexpr size_t kSmPerSm = 228 * 1024;  // shared memory per SM, 1 KB reserved per CTA
+    int best = 0;
+    long long best_cost = 0, best_waves = 0;
+    for (int P = 1; P <= std::min(8, L.slabs); ++P) {
+        const size_t xb = gemv_xbytes(L.precision, mb, L, P);
+        if (xb > 96 * 1024) continue;
+        const size_t smem = head + stages + xb;
+        const int occ = (int)std::min<size_t>(2, kSmPerSm / (smem + 1024));  // TMEM and registers: at most 2
+        if (occ < 1) continue;
+        const long long ctas = (long long)nrb * P * splits;
+        const long long cap = (long long)occ * num_sms;
+        const long long waves = (ctas + cap - 1) / cap;
+        const long long cost = waves * ((L.slabs + P - 1) / P);
+        if (best == 0 || cost < best_cost || (cost == best_cost && waves < best_waves)) {
+            best = P;
+            best_cost = cost;
+            best_waves = waves;
+        }
+    }
+    return best > 0 ? best : std::min(8, L.slabs);
 }
 
 cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream, bool pdl) {
-    const int prec = p.L.precision, RB = p.L.RB;
-    // batches beyond one CTA's rows (INT8 16, INT4 2) are split over grid y
-    int mb = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : p.M <= 8 ? 8 : 16;
-    if (p.M < 1 || p.M > kMaxGemvBatch) return cudaErrorInvalidValue;
+    const int prec = p.L.precision;
+    // batches beyond one CTA's rows (INT8 16, INT4 4) are split over grid y
+    const int mb = gemv_mb(prec, p.M);
+    if (p.M < 1 || p.M > kMaxGemvBatch || p.L.RB != kTcTileRows) return cudaErrorInvalidValue;
     if (prec == 8) {
         switch (mb) {
             case 1: return launch_t<8, 128, 1>(p, stream, pdl);
@@ -640,8 +770,13 @@ cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream, bool pdl) {
             default: return launch_t<8, 128, 16>(p, stream, pdl);
         }
     }
-    if (prec == 4 && RB == 32) return mb == 1 ? launch_t<4, 32, 1>(p, stream, pdl) : launch_t<4, 32, 2>(p, stream, pdl);
-    if (prec == 4 && RB == 64) return mb == 1 ? launch_t<4, 64, 1>(p, stream, pdl) : launch_t<4, 64, 2>(p, stream, pdl);
+    if (prec == 4) {
+        switch (mb) {
+            case 1: return launch_t<4, 128, 1>(p, stream, pdl);
+            case 2: return launch_t<4, 128, 2>(p, stream, pdl);
+            default: return launch_t<4, 128, 4>(p, stream, pdl);
+        }
+    }
     return cudaErrorInvalidValue;
 }
 

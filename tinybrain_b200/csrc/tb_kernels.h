@@ -102,7 +102,14 @@ struct SeqState {
     unsigned long long best;  // packed argmax key of the current step
 };
 
+// Optional device timeline of one launch (globaltimer ns; nullptr = off):
+// [0] first CTA entry (min), [1] last CTA entry, [2] last dependency release,
+// [3] last prologue done, [4] last accumulator complete, [5] last partial-sum
+// exchange done, [6] last CTA exit, [7] last first-weight-unit arrival.
+constexpr int kTracePoints = 8;
+
 struct GemvParams {
+    unsigned long long* trace;
     // weights (GPU layout)
     const uint8_t* w;
     const float* scales;
@@ -175,6 +182,7 @@ cudaError_t launch_quantize_int4_group(const float* x, int64_t count, int64_t gs
 constexpr int kPageTokens = 16;
 
 struct AttnParams {
+    unsigned long long* trace;  // see GemvParams::trace ([0], [1], [2], [6])
     const float* q;           // [M][H*d] (post-RoPE)
     int ld_q;
     const float* kv_pool;     // [page][layer][2][Hkv][16][d]

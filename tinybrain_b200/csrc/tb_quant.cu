@@ -115,52 +115,68 @@ __device__ __forceinline__ int src_nibble(const uint8_t* packed, int64_t i) {
     return raw > 7 ? raw - 16 : raw;
 }
 
-// INT4: one thread per (destination row n, 32-value k chunk = 16 bytes).
+// INT4: one thread per (destination row n, 32-value k chunk = 16 bytes) of
+// the tensor-core unit layout (tb_tc.cuh): chunk c of unit s of tile t at
+// ((t * slabs + s) * kQ4UnitBytes) + (c * 128 + row) * 16; in word j, byte i =
+// (q[k 8j+i] + 8) | (q[k 8j+i+4] + 8) << 4.
 __global__ void repack_q4_kernel(const uint8_t* __restrict__ src, int K, int N, QLayout L, uint8_t* __restrict__ dst,
                                  int row_offset, int interleave) {
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     const int kc = blockIdx.y;  // 32-value chunk
     if (n >= N) return;
     const int drow = fused_row(L, n, row_offset, interleave);
-    const int rb = drow / L.RB, r = drow % L.RB;
-    const int k0 = kc * 32;
-    const int byte0 = k0 / 2;
-    const int s = byte0 / kSlabBytes;
-    const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-    uint8_t* out = dst + (size_t)rb * L.RB * L.row_bytes + (size_t)s * L.RB * kSlabBytes + (size_t)r * sb +
-                   (byte0 - s * kSlabBytes);
+    const int tile = drow / kTcTileRows, r = drow % kTcTileRows;
+    const int s = kc >> 2, c = kc & 3;
+    uint8_t* out = dst + ((size_t)tile * L.slabs + s) * kQ4UnitBytes + (size_t)(c * kTcTileRows + r) * 16;
     uint32_t w[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int j = 0; j < 4; ++j) {
         uint32_t word = 0;
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
-            const int k = k0 + q * 8 + p;
-            const int v = (k < K) ? src_nibble(src, (int64_t)k * N + n) : 0;
-            word |= ((uint32_t)((v + 8) & 0xF)) << (4 * p);
+        for (int i = 0; i < 4; ++i) {
+            const int k = kc * 32 + 8 * j + i;
+            const int lo = (k < K) ? src_nibble(src, (int64_t)k * N + n) : 0;
+            const int hi = (k + 4 < K) ? src_nibble(src, (int64_t)(k + 4) * N + n) : 0;
+            word |= ((uint32_t)((lo + 8) & 0xF) | ((uint32_t)((hi + 8) & 0xF) << 4)) << (8 * i);
         }
-        w[q] = word;
+        w[j] = word;
     }
     *reinterpret_cast<uint4*>(out) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// INT4 scales: destination [rb][slab][grp][c][lane][4] for the 32-row group
-// starting at destination row rb*RB + grp*32; value = scale of the source group
-// containing flat index k*N + n0 (all 32 rows share it: gs % 32 == 0, N % gs == 0).
+// INT4 group scales into the unit's scale block [4 row groups][128 k]: one
+// thread per (k, 32-row source group); the value is the scale of the
+// reference group holding flat index k*N + n0 (32 | gs, gs | N: all 32 rows
+// of the group share it, QuantizedTensor.swift:502-535).
 __global__ void repack_scales_q4_kernel(const float* __restrict__ src, int K, int N, int gs, QLayout L,
-                                        float* __restrict__ dst, int row_offset, int interleave) {
-    const int g32 = blockIdx.y;           // source 32-row group index
-    const int e = blockIdx.x * blockDim.x + threadIdx.x;  // element within (slabs * 1024)
-    if (e >= L.slabs * 1024) return;
+                                        uint8_t* __restrict__ dst, int row_offset, int interleave) {
+    const int g32 = blockIdx.y;
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= L.slabs * kTcUnitK) return;
     const int n0 = g32 * 32;
     if (n0 >= N) return;
     const int drow = fused_row(L, n0, row_offset, interleave);
-    const int rb = drow / L.RB, grp = (drow % L.RB) / 32;
-    const int s = e / 1024, w = e % 1024;
-    const int i = w & 3, lane = (w >> 2) & 31, c = w >> 7;
-    const int k = s * 1024 + lane * 32 + c * 4 + i;
-    const float v = (k < K) ? src[((int64_t)k * N + n0) / gs] : 0.0f;
-    dst[(((size_t)rb * L.slabs + s) * (L.RB / 32) + grp) * 1024 + w] = v;
+    const int tile = drow / kTcTileRows, grp = (drow % kTcTileRows) / 32;
+    const int s = k / kTcUnitK, kk = k % kTcUnitK;
+    float* sc = reinterpret_cast<float*>(dst + ((size_t)tile * L.slabs + s) * kQ4UnitBytes + kQ4UnitNibBytes);
+    sc[grp * kTcUnitK + kk] = (k < K) ? src[((int64_t)k * N + n0) / gs] : 0.0f;
+}
+
+// Largest |scale| of every (32-row group, unit): bounds the B-operand digits.
+// Table layout [tile][4 groups][slabs].
+__global__ void scale_max_q4_kernel(const uint8_t* __restrict__ w, int N, QLayout L, float* __restrict__ smax,
+                                    int row_offset, int interleave) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    const int g32 = blockIdx.y;
+    if (s >= L.slabs || g32 * 32 >= N) return;
+    const int drow = fused_row(L, g32 * 32, row_offset, interleave);
+    const int tile = drow / kTcTileRows, grp = (drow % kTcTileRows) / 32;
+    const float* sc =
+        reinterpret_cast<const float*>(w + ((size_t)tile * L.slabs + s) * kQ4UnitBytes + kQ4UnitNibBytes) +
+        grp * kTcUnitK;
+    float m = 0.0f;
+    for (int kk = 0; kk < kTcUnitK; ++kk) m = fmaxf(m, fabsf(sc[kk]));
+    smax[((size_t)tile * kQ4Groups + grp) * L.slabs + s] = m;
 }
 
 }  // namespace
@@ -194,9 +210,12 @@ cudaError_t launch_repack(const RepackSrc& s, const QLayout& L, uint8_t* w_out, 
     } else {
         repack_q4_kernel<<<dim3(nb, (unsigned)(L.Kp / 32)), 128, 0, stream>>>(
             (const uint8_t*)s.data, s.K, s.N, L, w_out, row_offset, interleave);
-        const unsigned ne = (unsigned)((L.slabs * 1024 + 255) / 256);
-        repack_scales_q4_kernel<<<dim3(ne, (unsigned)((s.N + 31) / 32)), 256, 0, stream>>>(
-            s.scales, s.K, s.N, s.group_size, L, scales_out, row_offset, interleave);
+        const unsigned ng = (unsigned)((s.N + 31) / 32);
+        const unsigned ne = (unsigned)((L.slabs * kTcUnitK + 255) / 256);
+        repack_scales_q4_kernel<<<dim3(ne, ng), 256, 0, stream>>>(s.scales, s.K, s.N, s.group_size, L, w_out,
+                                                                  row_offset, interleave);
+        scale_max_q4_kernel<<<dim3((unsigned)((L.slabs + 127) / 128), ng), 128, 0, stream>>>(
+            w_out, s.N, L, scales_out, row_offset, interleave);
     }
     return cudaGetLastError();
 }

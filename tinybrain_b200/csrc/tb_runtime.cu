@@ -1108,7 +1108,7 @@ static void fill_gemv_common(tb_runner* r, GemvParams& p, const FusedWeight& f) 
 
 static int64_t gemv_bytes(const QLayout& L, int M) {
     // streamed weights + scales + activations in and out (fp32)
-    int64_t w = (int64_t)L.Np * L.row_bytes + (int64_t)L.scale_floats * 4;
+    int64_t w = (int64_t)L.weight_bytes + (int64_t)L.scale_floats * 4;
     return w + (int64_t)M * (L.K + L.N) * 4;
 }
 
@@ -1298,6 +1298,7 @@ static tb_status build_step(tb_runner* r) {
     if (r->B != 1 || m->tp_world > 1 || c.architecture != TB_ARCH_LLAMA || c.hidden_dim > 4096 || c.intermediate_dim % 4 != 0) return ok();
     const Layer& L0 = m->layers[0];
     const int prec = L0.qkv.L.precision;
+    if (prec != 8) return ok();  // INT4 decodes through the per-op tensor-core GEMVs
     auto same = [](const QLayout& a, const QLayout& b) {
         return a.precision == b.precision && a.K == b.K && a.N == b.N && a.RB == b.RB;
     };
@@ -2035,6 +2036,43 @@ extern "C" tb_status tb_runner_decode_device(tb_runner* r, int32_t n_steps, floa
     float t = 0.0f;
     TB_CUDA(cudaEventElapsedTime(&t, r->ev0, r->ev1));
     if (ms) *ms = t;
+    return tb_context_check_device(r->ctx);
+}
+
+// Device timeline of one graph-replayed decode step (per launch: kTracePoints
+// globaltimer stamps, see GemvParams::trace) -- where the step's time goes
+// between launch, dependency release, prologue, tensor-core work and exit.
+extern "C" tb_status tb_runner_trace_launches(tb_runner* r, uint64_t* stamps, int32_t* kinds, int32_t* n) {
+    TB_CHECK(r && stamps && kinds && n, "NULL argument");
+    TB_CHECK(!r->persistent, "tracing covers the per-launch step");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    const int cnt = (int)r->plan.size();
+    TB_CHECK(*n >= cnt, "capacity %d < %d launches", *n, cnt);
+    DevBuf buf;
+    TB_CUDA(buf.alloc((size_t)cnt * kTracePoints * 8));
+    std::vector<uint64_t> init((size_t)cnt * kTracePoints, 0ull);
+    for (int i = 0; i < cnt; ++i) init[(size_t)i * kTracePoints] = ~0ull;
+    TB_CUDA(cudaMemcpy(buf.p, init.data(), init.size() * 8, cudaMemcpyHostToDevice));
+    auto set = [&](bool on) {
+        for (int i = 0; i < cnt; ++i) {
+            unsigned long long* t = on ? buf.as<unsigned long long>() + (size_t)i * kTracePoints : nullptr;
+            r->plan[i].g.trace = t;
+            r->plan[i].a.trace = t;
+        }
+        if (r->graph) cudaGraphExecDestroy(r->graph);
+        r->graph = nullptr;
+    };
+    std::vector<char> act(r->B, 0);
+    for (int s = 0; s < std::max(1, g_last_plan.n_seqs); ++s) act[s] = 1;
+    set(true);
+    tb_status e = run_steps(r, 1, act);
+    cudaError_t ce = cudaStreamSynchronize(r->ctx->stream);
+    set(false);
+    if (e != TB_OK) return e;
+    if (ce != cudaSuccess) return cuda_fail(ce, "trace step");
+    TB_CUDA(cudaMemcpy(stamps, buf.p, (size_t)cnt * kTracePoints * 8, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < cnt; ++i) kinds[i] = r->plan[i].kind;
+    *n = cnt;
     return tb_context_check_device(r->ctx);
 }
 

@@ -1145,10 +1145,11 @@ cudaError_t launch_t(const StepParams& p, int grid, size_t smem, cudaStream_t st
     return cudaLaunchKernelEx(&cfg, kfn, p);
 }
 
+// INT8 weights only: INT4 projections stream through the per-op tensor-core GEMV.
 bool supported(int prec, int G, int d) {
-    if (prec != 8 && prec != 4) return false;
+    if (prec != 8) return false;
     return (G == 8 && d == 64) || (G == 1 && (d == 64 || d == 128)) || (G == 4 && d == 32) ||
-           (prec == 8 && ((G == 4 && d == 64) || (G == 2 && d == 64) || (G == 1 && d == 32)));
+           (G == 4 && d == 64) || (G == 2 && d == 64) || (G == 1 && d == 32);
 }
 
 }  // namespace
@@ -1196,13 +1197,9 @@ cudaError_t launch_decode_step(const StepParams& p, int grid, size_t smem, cudaS
 #define TB_STEP_CASE(pr, g, dd) \
     if (prec == pr && G == g && p.d == dd) return launch_t<pr, g, dd>(p, grid, smem, stream);
     TB_STEP_CASE(8, 8, 64)
-    TB_STEP_CASE(4, 8, 64)
     TB_STEP_CASE(8, 1, 128)
-    TB_STEP_CASE(4, 1, 128)
     TB_STEP_CASE(8, 1, 64)
-    TB_STEP_CASE(4, 1, 64)
     TB_STEP_CASE(8, 4, 32)
-    TB_STEP_CASE(4, 4, 32)
     TB_STEP_CASE(8, 4, 64)
     TB_STEP_CASE(8, 2, 64)
     TB_STEP_CASE(8, 1, 32)

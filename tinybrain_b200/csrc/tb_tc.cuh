@@ -90,11 +90,61 @@ __device__ __forceinline__ void tc_unit_mma(uint32_t dtmem, uint32_t a_saddr, ui
     }
 }
 
+// D[tmem] (+)= A[tmem] * B^T for one K = 32 step, A read from tensor memory
+// (lane = row, 32-bit column c = k 4c .. 4c+3 as bytes, low k in the low byte).
+__device__ __forceinline__ void tc_mma_i8_ts(uint32_t dtmem, uint32_t atmem, uint64_t bdesc, uint32_t idesc,
+                                             bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(dtmem),
+        "r"(atmem), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+// Warp-collective store of 32 consecutive 32-bit columns of the warp's 32 TMEM
+// lanes (lane i of the warp writes row 32 * (warp % 4) + i).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// ---- INT4 weights on the integer tensor cores ----
+// A 128-row x 128-k INT4 unit in HBM / shared memory (10 KB):
+//   nibbles: [4 k-chunks of 32][128 rows][16 bytes]; in word j (k 8j .. 8j+7
+//     of the chunk) byte i holds k 8j+i in its low and k 8j+i+4 in its high
+//     nibble, each biased by +8 (value q in [-8, 7] stored as q + 8);
+//   scales: [4 row groups of 32][128 k] fp32 (the reference's group scale of
+//     those 32 rows at that k).
+// Expanded to int8 in registers and stored to tensor memory as the A operand;
+// the scales go into the B operand (digits of scale * x per row group).
+constexpr int kQ4UnitNibBytes = kTcTileRows * kTcUnitK / 2;                 // 8 KB
+constexpr int kQ4UnitBytes = kQ4UnitNibBytes + 4 * kTcUnitK * 4;            // + 2 KB of scales
+constexpr int kQ4Groups = kTcTileRows / 32;                                  // row groups per tile
+
+// One nibble word -> the int8 words of k 8j..8j+3 (lo) and 8j+4..8j+7 (hi).
+// b + 0x78 stays inside its byte for b <= 15, and ^0x80 then yields b - 8 in
+// two's complement.
+__device__ __forceinline__ void q4_expand(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    lo = ((w & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+    hi = (((w >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+}
+
 // Warp-collective load of 8 / 16 / 32 consecutive accumulator columns of the
 // warp's 32 TMEM lanes (lane i of the warp gets row (32 * (warp % 4) + i)).
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&v)[8]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, int (&v)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
                  : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

@@ -720,6 +720,15 @@ class ModelRunner:
         call("tb_runner_profile_step", self.handle, _ptr(t), _ptr(k), _ptr(b), C.byref(n))
         return t[:n.value].copy(), k[:n.value].copy(), b[:n.value].copy()
 
+    def trace_launches(self):
+        """Device timeline of one decode step: (stamps [n][8] ns, kinds [n])."""
+        cap = 4096
+        st = np.zeros((cap, 8), dtype=np.uint64)
+        k = np.zeros(cap, dtype=np.int32)
+        n = C.c_int32(cap)
+        call("tb_runner_trace_launches", self.handle, _ptr(st), _ptr(k), C.byref(n))
+        return st[:n.value].copy(), k[:n.value].copy()
+
     def close(self):
         if self.handle:
             _lib.load().tb_runner_free(self.handle)
