@@ -12,9 +12,14 @@
 // G = H/Hkv query heads of its KV head, so each K/V byte is read once.  One
 // producer warp streams the K and V tiles of each page (16 x d fp32,
 // contiguous) with 1-D bulk copies into an mbarrier ring; four consumer warps
-// compute scores and an online softmax.  Splits write (m, l, acc) partials to
-// scratch; the last CTA of each (sequence, KV head) -- elected with a ticket --
-// combines them in split order (deterministic).
+// compute scores and an online softmax.  The splits of one (sequence, KV
+// head) form a thread-block cluster: each keeps its (m, l, acc) partial in
+// shared memory and, after a cluster barrier, combines a slice of the outputs
+// from all splits' partials through distributed shared memory, in split order
+// (deterministic; no global scratch, no tickets).  Pages older than the
+// current position are complete before the step starts, so their copies are
+// issued before the programmatic-dependent-launch wait; only the page holding
+// the row the preceding QKV kernel appends waits for it.
 #include "../../include/tinybrain_cuda.h"
 #include "tb_common.cuh"
 #include "tb_kernels.h"
@@ -43,7 +48,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     int* valid = reinterpret_cast<int*>(empty + kAttnStages);            // [stages]
     float* S = reinterpret_cast<float*>(smem + 128);                    // [2][G][16]
     float* tiles = reinterpret_cast<float*>(smem + 128 + ((2 * G * kPageTokens * 4 + 127) / 128) * 128);
-    float* flag = S;  // reused after the loop
+    float* cpart = tiles + kAttnStages * 2 * TILE;  // [G][D + 4]: acc, m, l of this split
 
     const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -61,9 +66,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     }
     __syncthreads();
     pdl_launch_dependents();
-    pdl_wait();
-    if (threadIdx.x == 0) trace_max(p.trace, 2);
 
+    // The sequence state and page table are written before the step starts
+    // (the previous step's last kernel, host uploads): readable before the wait.
     const SeqState& sq = p.seq[m];
     const bool active = p.lens ? true : (sq.active != 0);
     const int Lq = p.lens ? p.lens[m] : sq.pos + 1;
@@ -75,12 +80,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 
     if (warp == kAttnConsumerWarps) {
         if (lane == 0) {
+            bool waited = false;
             for (int i = 0; i < nun; ++i) {
                 const int st = i % kAttnStages;
                 if (i >= kAttnStages) {
                     if (!mbar_wait(&empty[st], ((i / kAttnStages) - 1) & 1, p.err)) break;
                 }
                 const int lp = pg0 + i;
+                if (lp == npages - 1 && !waited) {  // the page the preceding kernel appends to
+                    pdl_wait();
+                    waited = true;
+                }
                 const int page = p.page_table[(size_t)m * p.ptab_stride + lp];
                 float* kd = tiles + st * 2 * TILE;
                 if (page >= 0) {
@@ -99,6 +109,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             }
         }
     } else {
+        pdl_wait();
+        if (threadIdx.x == 0) trace_max(p.trace, 2);
         const int t = threadIdx.x;  // 0..127
         const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
         // Score-phase role.
@@ -171,77 +183,74 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             if (lane == 0) mbar_arrive(&empty[st]);
         }
 
-        const size_t pair_idx = (size_t)m * p.Hkv + kvh;
-        float* out = p.out + (size_t)m * p.ld_out + (size_t)(kvh * G + gv) * D + dv;
-        if (p.nsplit == 1) {
-            if (pv) {
-                if (!active) {
-                    *reinterpret_cast<float4*>(out) = make_float4(0.f, 0.f, 0.f, 0.f);
-                } else {
-                    const float il = run_l > 0.0f ? 1.0f / run_l : 0.0f;
-                    *reinterpret_cast<float4*>(out) =
-                        make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
-                }
-            }
-        } else {
-            float* part = p.part + ((pair_idx * p.nsplit + split) * G + gv) * (size_t)(D + 4);
-            if (pv) {
-                *reinterpret_cast<float4*>(part + dv) = acc;
-                if (dv == 0) {
-                    part[D] = run_m;
-                    part[D + 1] = run_l;
-                }
-            }
-            __threadfence();
-            named_bar_sync(1, 128);
-            if (t == 0) {
-                const unsigned int tk = atomicAdd(&p.tickets[pair_idx], 1u);
-                flag[0] = __int_as_float(tk == (unsigned)p.nsplit - 1 ? 1 : 0);
-            }
-            named_bar_sync(1, 128);
-            if (__float_as_int(flag[0]) == 1) {
-                __threadfence();
-                // Combine the splits in split order: all (m, l) pairs are loaded in
-                // parallel into shared memory first, so the chain is two L2 round trips.
-                const float* base = p.part + (pair_idx * p.nsplit) * G * (size_t)(D + 4);
-                float* wsm = tiles;  // [nsplit][G] weights, reused ring space
-                float* lsm = tiles + 64 * G;
-                for (int e = t; e < p.nsplit * G; e += 128) {
-                    wsm[e] = base[(size_t)e * (D + 4) + D];
-                    lsm[e] = base[(size_t)e * (D + 4) + D + 1];
-                }
-                named_bar_sync(1, 128);
-                if (pv) {
-                    float M = -INFINITY;
-                    for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, wsm[s * G + gv]);
-                    float den = 0.0f;
-                    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (M != -INFINITY) {
-#pragma unroll 4
-                        for (int s = 0; s < p.nsplit; ++s) {
-                            const float ms = wsm[s * G + gv];
-                            const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-                            den = fmaf(w, lsm[s * G + gv], den);
-                            const float4 a = *reinterpret_cast<const float4*>(base + ((size_t)s * G + gv) * (D + 4) + dv);
-                            num.x = fmaf(w, a.x, num.x);
-                            num.y = fmaf(w, a.y, num.y);
-                            num.z = fmaf(w, a.z, num.z);
-                            num.w = fmaf(w, a.w, num.w);
-                        }
-                    }
-                    const float il = den > 0.0f ? 1.0f / den : 0.0f;
-                    *reinterpret_cast<float4*>(out) = make_float4(num.x * il, num.y * il, num.z * il, num.w * il);
-                }
-                if (t == 0) p.tickets[pair_idx] = 0u;
+        if (pv) {
+            float* cp = cpart + gv * (D + 4);
+            *reinterpret_cast<float4*>(cp + dv) = acc;
+            if (dv == 0) {
+                cp[D] = run_m;
+                cp[D + 1] = run_l;
             }
         }
     }
+    // Combine the splits (cluster ranks) in split order; CTA `split` produces
+    // output items [split * Q / ns, (split + 1) * Q / ns), Q = G * D / 4 float4s.
+    const int ns = p.nsplit;
+    if (ns > 1) cluster_sync();
+    else __syncthreads();
+    {
+        constexpr int Q = G * (D / 4);
+        const int t = threadIdx.x;
+        const int i0 = split * Q / ns, i1 = (split + 1) * Q / ns;
+        if (t < kAttnConsumerWarps * 32 && i0 + t < i1) {
+            const int item = i0 + t;
+            const int g = item / (D / 4), d4 = (item % (D / 4)) * 4;
+            float* out = p.out + (size_t)m * p.ld_out + (size_t)(kvh * G + g) * D + d4;
+            // every split's (m, l, acc) loaded first (one DSMEM round trip),
+            // then combined in split order
+            float mq[kMaxAttnSplits], lq[kMaxAttnSplits];
+            float4 aq[kMaxAttnSplits];
+#pragma unroll
+            for (int q = 0; q < kMaxAttnSplits; ++q) {
+                if (q < ns) {
+                    const uint32_t base = dsmem_map(cpart + g * (D + 4), (uint32_t)q);
+                    mq[q] = dsmem_ld_f32(base + D * 4);
+                    lq[q] = dsmem_ld_f32(base + (D + 1) * 4);
+                    aq[q] = dsmem_ld_f32x4(base + d4 * 4);
+                } else {
+                    mq[q] = -INFINITY;
+                    lq[q] = 0.0f;
+                    aq[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            float M = -INFINITY;
+#pragma unroll
+            for (int q = 0; q < kMaxAttnSplits; ++q) M = fmaxf(M, mq[q]);
+            float den = 0.0f;
+            float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (M != -INFINITY) {
+#pragma unroll
+                for (int q = 0; q < kMaxAttnSplits; ++q) {
+                    if (q >= ns) continue;
+                    const float w = (mq[q] == -INFINITY) ? 0.0f : expf(mq[q] - M);
+                    den = fmaf(w, lq[q], den);
+                    num.x = fmaf(w, aq[q].x, num.x);
+                    num.y = fmaf(w, aq[q].y, num.y);
+                    num.z = fmaf(w, aq[q].z, num.z);
+                    num.w = fmaf(w, aq[q].w, num.w);
+                }
+            }
+            const float il = den > 0.0f ? 1.0f / den : 0.0f;
+            *reinterpret_cast<float4*>(out) = make_float4(num.x * il, num.y * il, num.z * il, num.w * il);
+        }
+    }
+    if (ns > 1) cluster_sync();  // partials stay readable until every rank has combined
     if (threadIdx.x == 0) trace_max(p.trace, 6);
 }
 
 template <int G, int D>
 size_t attn_smem() {
-    return 128 + ((2 * G * kPageTokens * 4 + 127) / 128) * 128 + (size_t)kAttnStages * 2 * kPageTokens * D * 4;
+    return 128 + ((2 * G * kPageTokens * 4 + 127) / 128) * 128 + (size_t)kAttnStages * 2 * kPageTokens * D * 4 +
+           (size_t)G * (D + 4) * 4;
 }
 
 template <int G, int D>
@@ -255,11 +264,16 @@ cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t stream, bool pdl) {
     cfg.blockDim = dim3(kAttnThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    if (p.nsplit < 1 || p.nsplit > kMaxAttnSplits) return cudaErrorInvalidValue;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;  // the splits of a (sequence, KV head)
+    attr[0].val.clusterDim.x = (unsigned)p.nsplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = pdl ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kfn, p);
 }
 
@@ -345,12 +359,12 @@ size_t attention_ticket_count(int M, int Hkv) { return (size_t)M * Hkv; }
 
 int choose_nsplit(int M, int Hkv, int max_pages, int num_sms) {
     // About one CTA per SM over the (sequence, KV head) pairs at the longest
-    // context, at least 8 pages per split there, at most 64 splits.
+    // context, at least 8 pages per split there, at most one cluster (8) of splits.
     int pairs = M * Hkv;
     int ns = (num_sms + pairs - 1) / pairs;
     const int by_pages = (max_pages + 7) / 8;
     if (ns > by_pages) ns = by_pages;
-    if (ns > 64) ns = 64;
+    if (ns > kMaxAttnSplits) ns = kMaxAttnSplits;
     return ns < 1 ? 1 : ns;
 }
 

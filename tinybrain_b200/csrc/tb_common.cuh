@@ -129,7 +129,16 @@ __device__ __forceinline__ uint32_t dsmem_map(const void* p, uint32_t rank) {
 }
 __device__ __forceinline__ float dsmem_ld_f32(uint32_t addr) {
     float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    // volatile keeps the load after the cluster barrier; no memory clobber, so
+    // independent loads issue back to back
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float4 dsmem_ld_f32x4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr));
     return v;
 }
 

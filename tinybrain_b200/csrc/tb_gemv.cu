@@ -61,7 +61,8 @@ namespace {
 template <int PREC, int RB>
 struct GemvCfg {
     static constexpr int kStageBytes = PREC == 8 ? kTcUnitBytes : kQ4UnitBytes;
-    static constexpr int kStages = PREC == 8 ? 6 : 8;
+    // 2 CTAs per SM x 4 (6) units in flight cover HBM latency many times over
+    static constexpr int kStages = PREC == 8 ? 4 : 6;
 };
 // Digit rows of the B operand for MB batch rows: INT8 4 digits per row (N >= 8,
 // 16-multiples past 8); INT4 4 digits per (row, 32-row weight group).
@@ -131,12 +132,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     // batch rows [m0, m0 + Mloc) of this CTA (grid y splits batches larger than MB)
     const int m0 = blockIdx.y * MB;
     const int Mloc = min(MB, p.M - m0);
-    // INT4 staging (after the stage ring): x [MB][kspan] fp32, B slots
-    // [2][kQ4ASlots][NB * 128], per-unit max |x| [nunits][MB], per-unit max
-    // |scale| [4][nunits], digit exponents [MB][4]
+    // Activation staging after the stage ring, kspan = the CTA's k range:
+    //   INT8: digits [kspan/16][NB][16], x [MB][kspan] fp32, norm weights [kspan];
+    //   INT4: x [MB][kspan] fp32, norm weights [kspan], B slots
+    //   [2][kQ4ASlots][NB * 128], per-unit max |x| [nunits][MB], per-unit max
+    //   |scale| [4][nunits], digit exponents [MB][4].
     const int kspan = ((L.slabs + P - 1) / P) * kTcUnitK;
-    float* xs = reinterpret_cast<float*>(xbuf);
-    uint8_t* bslots = xbuf + (size_t)MB * kspan * 4;
+    float* xs = reinterpret_cast<float*>(PREC == 8 ? xbuf + (size_t)kspan * NB : xbuf);
+    float* wstage = xs + (size_t)MB * kspan;
+    uint8_t* bslots = reinterpret_cast<uint8_t*>(wstage + kspan);
     float* xmax = reinterpret_cast<float*>(bslots + 2 * kQ4ASlots * NB * 128);
     float* smaxs = xmax + (size_t)(kspan / kTcUnitK) * MB;
     int* ex4 = reinterpret_cast<int*>(smaxs + kQ4Groups * (kspan / kTcUnitK));
@@ -183,6 +187,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             rowsc[i] = PREC == 8 ? __ldg(p.scales + grow) : 1.0f;
             rowbias[i] = p.bias ? __ldg(p.bias + grow) : 0.0f;
         }
+        const int kbeg = s0 * L.slab_k;
+        const int kend = min(s1 * L.slab_k, L.Kp);
+        const bool rms = p.prologue == kProRmsNorm || p.prologue == kProEmbedRms;
+        if (rms)  // RMSNorm weights of the CTA's k range (zero past K)
+            for (int k = ctid; k < kspan; k += 256) wstage[k] = kbeg + k < L.K ? __ldg(p.norm_w + kbeg + k) : 0.0f;
         if (PREC == 4)
             for (int i = ctid; i < kQ4Groups * nunits; i += 256) {
                 const int g = i / nunits, u = i - g * nunits;
@@ -197,10 +206,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             seqinfo[MB + ctid] = sq.active;
             seqinfo[2 * MB + ctid] = sq.active ? p.page_table[(size_t)(m0 + ctid) * p.ptab_stride + pos / kPageTokens] : -1;
         }
-        const int kbeg = s0 * L.slab_k;
-        const int kend = min(s1 * L.slab_k, L.Kp);
-        const bool rms = p.prologue == kProRmsNorm || p.prologue == kProEmbedRms;
-
         // Source rows (embedding gather or activation buffer).
         const float* srcm[MB];
 #pragma unroll
@@ -223,6 +228,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         }
         // Tensor.swift:1538-1558: ss = sum x^2; inv = 1 / sqrt(ss/H + eps).  The
         // INT8 path also needs max |x| over this CTA's k range (digit scale).
+        // One pass over the source: the sum of squares over the whole row and
+        // the CTA's k range staged into shared memory (zero past K), so the
+        // digit pass reads no global memory.
         float inv[MB];
         int ex[MB];
 #pragma unroll
@@ -232,42 +240,53 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         }
         // rows are read as float4 when K and the row stride allow it
         const bool v4 = (L.K % 4 == 0) && (p.prologue == kProEmbed || p.prologue == kProEmbedRms || p.ld_src % 4 == 0);
-        if (rms || PREC == 8) {
+        const int kq = kspan / 4;  // float4 groups of the staged range
+        __syncwarp();
+        named_bar_sync(1, 256);  // norm weights staged
 #pragma unroll
-            for (int m = 0; m < MB; ++m) {
-                float ss = 0.0f, mx = 0.0f;
-                if (m < Mloc) {
-                    if (rms) {
-                        if (v4) {
-                            for (int k = 4 * ctid; k < L.K; k += 1024) {
-                                const float4 a = *reinterpret_cast<const float4*>(srcm[m] + k);
-                                ss = fmaf(a.x, a.x, ss);
-                                ss = fmaf(a.y, a.y, ss);
-                                ss = fmaf(a.z, a.z, ss);
-                                ss = fmaf(a.w, a.w, ss);
-                            }
-                        } else {
-                            for (int k = ctid; k < L.K; k += 256) ss = fmaf(srcm[m][k], srcm[m][k], ss);
+        for (int m = 0; m < MB; ++m) {
+            float ss = 0.0f, mx = 0.0f;
+            float* xr = xs + (size_t)m * kspan;
+            if (m < Mloc) {
+                if (rms) {
+                    if (v4) {
+                        for (int k = 4 * ctid; k < L.K; k += 1024) {
+                            const float4 a = *reinterpret_cast<const float4*>(srcm[m] + k);
+                            ss = fmaf(a.x, a.x, ss);
+                            ss = fmaf(a.y, a.y, ss);
+                            ss = fmaf(a.z, a.z, ss);
+                            ss = fmaf(a.w, a.w, ss);
                         }
-                    }
-                    if (PREC == 8) {
-                        const int kl = min(kend, L.K);
-                        if (v4) {
-                            for (int k = kbeg + 4 * ctid; k < kl; k += 1024) {
-                                float4 a = *reinterpret_cast<const float4*>(srcm[m] + k);
-                                if (rms) {
-                                    const float4 w = __ldg(reinterpret_cast<const float4*>(p.norm_w + k));
-                                    a = make_float4(__fmul_rn(a.x, w.x), __fmul_rn(a.y, w.y), __fmul_rn(a.z, w.z),
-                                                    __fmul_rn(a.w, w.w));
-                                }
-                                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
-                            }
-                        } else {
-                            for (int k = kbeg + ctid; k < kl; k += 256)
-                                mx = fmaxf(mx, fabsf(rms ? __fmul_rn(srcm[m][k], p.norm_w[k]) : srcm[m][k]));
-                        }
+                    } else {
+                        for (int k = ctid; k < L.K; k += 256) ss = fmaf(srcm[m][k], srcm[m][k], ss);
                     }
                 }
+                for (int g = ctid; g < kq; g += 256) {
+                    const int k = kbeg + 4 * g;
+                    float4 a;
+                    if (v4 && k + 3 < L.K) {
+                        a = *reinterpret_cast<const float4*>(srcm[m] + k);
+                    } else {
+                        a.x = k < L.K ? srcm[m][k] : 0.0f;
+                        a.y = k + 1 < L.K ? srcm[m][k + 1] : 0.0f;
+                        a.z = k + 2 < L.K ? srcm[m][k + 2] : 0.0f;
+                        a.w = k + 3 < L.K ? srcm[m][k + 3] : 0.0f;
+                    }
+                    *reinterpret_cast<float4*>(xr + 4 * g) = a;
+                    if (PREC == 8) {
+                        if (rms) {
+                            const float4 w = *reinterpret_cast<const float4*>(wstage + 4 * g);
+                            a = make_float4(__fmul_rn(a.x, w.x), __fmul_rn(a.y, w.y), __fmul_rn(a.z, w.z),
+                                            __fmul_rn(a.w, w.w));
+                        }
+                        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+                    }
+                }
+            } else {
+                for (int g = ctid; g < kq; g += 256)
+                    *reinterpret_cast<float4*>(xr + 4 * g) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (rms || PREC == 8) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
                     ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -278,7 +297,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                     misc[(MB + m) * 8 + warp] = mx;
                 }
             }
-            named_bar_sync(1, 256);
+        }
+        named_bar_sync(1, 256);
+        if (rms || PREC == 8) {
 #pragma unroll
             for (int m = 0; m < MB; ++m) {
                 float ss = 0.0f, mx = 0.0f;
@@ -292,36 +313,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                 ex[m] = digit_exponent(__fmul_rn(mx, inv[m]) * 1.0000002f);
             }
         }
-        auto xval = [&](int m, int k) -> float {
-            float v = 0.0f;
-            if (m < Mloc && k < L.K) {
-                v = srcm[m][k];
-                if (rms) v = __fmul_rn(__fmul_rn(v, inv[m]), p.norm_w[k]);
+        // four consecutive staged k (g = (k - kbeg) / 4), normalised as the
+        // reference does: (x * inv) * w
+        auto xval4 = [&](int m, int g) -> float4 {
+            float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * kspan + 4 * g);
+            if (rms) {
+                const float4 w = *reinterpret_cast<const float4*>(wstage + 4 * g);
+                a = make_float4(__fmul_rn(__fmul_rn(a.x, inv[m]), w.x), __fmul_rn(__fmul_rn(a.y, inv[m]), w.y),
+                                __fmul_rn(__fmul_rn(a.z, inv[m]), w.z), __fmul_rn(__fmul_rn(a.w, inv[m]), w.w));
             }
-            return v;
-        };
-        // four consecutive k (k % 4 == 0)
-        auto xval4 = [&](int m, int k) -> float4 {
-            if (v4 && m < Mloc && k + 3 < L.K) {
-                float4 a = *reinterpret_cast<const float4*>(srcm[m] + k);
-                if (rms) {
-                    const float4 w = __ldg(reinterpret_cast<const float4*>(p.norm_w + k));
-                    a = make_float4(__fmul_rn(__fmul_rn(a.x, inv[m]), w.x), __fmul_rn(__fmul_rn(a.y, inv[m]), w.y),
-                                    __fmul_rn(__fmul_rn(a.z, inv[m]), w.z), __fmul_rn(__fmul_rn(a.w, inv[m]), w.w));
-                }
-                return a;
-            }
-            return make_float4(xval(m, k), xval(m, k + 1), xval(m, k + 2), xval(m, k + 3));
+            return a;
         };
 
         if constexpr (PREC == 8) {
             // Digits of x[m][kbeg:kend) into the B operand, 4 consecutive k per thread.
             const int ngroups = (kend - kbeg) / 4;
             for (int g = ctid; g < ngroups; g += 256) {
-                const int k = kbeg + 4 * g;
 #pragma unroll
                 for (int m = 0; m < MB; ++m) {
-                    put_digits4(xd, NB, 4 * g, m, xval4(m, k), __int_as_float((127 - ex[m]) << 23));
+                    put_digits4(xd, NB, 4 * g, m, xval4(m, g), __int_as_float((127 - ex[m]) << 23));
                 }
                 if (NB > kTcDigits * MB) {  // unused digit rows read as zero
                     uint8_t* base = xd + (size_t)(g >> 2) * NB * 16 + (4 * g & 15);
@@ -373,10 +383,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             //     largest |x| of every unit (one warp covers one unit per pass).
             const int ngroups = kspan / 4;
             for (int g = ctid; g < ngroups; g += 256) {
-                const int k = kbeg + 4 * g;
 #pragma unroll
                 for (int m = 0; m < MB; ++m) {
-                    const float4 v = k < kend ? xval4(m, k) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    const float4 v = xval4(m, g);  // zero past K (and past this CTA's units)
                     *reinterpret_cast<float4*>(xs + (size_t)m * kspan + 4 * g) = v;
                     float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
@@ -516,10 +525,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         uint32_t rbase[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) rbase[q] = (q < P) ? dsmem_map(red, q) : 0u;
+        // Partial sums of a row from every rank: all loads issued before the
+        // first add (one DSMEM round trip), then summed in rank order.
         auto rowsum = [&](int row, int m) -> float {
-            float s = 0.0f;
             if (P == 1) return red[row * MB + m];
-            for (int q = 0; q < P; ++q) s += dsmem_ld_f32(rbase[q] + (uint32_t)((row * MB + m) * 4));
+            float v[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) v[q] = q < P ? dsmem_ld_f32(rbase[q] + (uint32_t)((row * MB + m) * 4)) : 0.0f;
+            float s = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if (q < P) s += v[q];
             return s;
         };
         auto finish = [&](int gpu_row, float s) -> float {
@@ -681,9 +697,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 // B slots, per-unit maxima and exponents.
 inline size_t gemv_xbytes(int prec, int mb, const QLayout& L, int P) {
     const size_t units = (size_t)((L.slabs + P - 1) / P);
-    if (prec == 8) return units * kTcUnitK * (size_t)tc_nb(mb);
-    return units * kTcUnitK * mb * 4 + (size_t)2 * kQ4ASlots * q4_nb(mb) * 128 + units * (mb + kQ4Groups) * 4 +
-           (size_t)mb * kQ4Groups * 4;
+    const size_t xw = units * kTcUnitK * (mb + 1) * 4;  // x and norm weights, fp32
+    if (prec == 8) return units * kTcUnitK * (size_t)tc_nb(mb) + xw;
+    return xw + (size_t)2 * kQ4ASlots * q4_nb(mb) * 128 + units * (mb + kQ4Groups) * 4 + (size_t)mb * kQ4Groups * 4;
 }
 
 template <int PREC, int RB, int MB>
@@ -735,8 +751,12 @@ int choose_ksplit(const QLayout& L, int M, int num_sms) {
     const size_t stages = L.precision == 8 ? (size_t)GemvCfg<8, 128>::kStages * GemvCfg<8, 128>::kStageBytes
                                            : (size_t)GemvCfg<4, 128>::kStages * GemvCfg<4, 128>::kStageBytes;
     constexpr size_t kSmPerSm = 228 * 1024;  // shared memory per SM, 1 KB reserved per CTA
+    // Time model (us): a wave costs a CTA lifetime of fixed latency (launch,
+    // prologue, reduction, epilogue: ~4 us measured), and an SM streams a
+    // 16 KB unit in ~0.35 us at its share of HBM bandwidth.
+    constexpr double kWaveUs = 4.0, kUnitUs = 0.35;
     int best = 0;
-    long long best_cost = 0, best_waves = 0;
+    double best_cost = 0.0;
     for (int P = 1; P <= std::min(8, L.slabs); ++P) {
         const size_t xb = gemv_xbytes(L.precision, mb, L, P);
         if (xb > 96 * 1024) continue;
@@ -746,11 +766,11 @@ int choose_ksplit(const QLayout& L, int M, int num_sms) {
         const long long ctas = (long long)nrb * P * splits;
         const long long cap = (long long)occ * num_sms;
         const long long waves = (ctas + cap - 1) / cap;
-        const long long cost = waves * ((L.slabs + P - 1) / P);
-        if (best == 0 || cost < best_cost || (cost == best_cost && waves < best_waves)) {
+        const long long per_sm = (ctas + num_sms - 1) / num_sms;
+        const double cost = waves * kWaveUs + (double)per_sm * ((L.slabs + P - 1) / P) * kUnitUs;
+        if (best == 0 || cost < best_cost) {
             best = P;
             best_cost = cost;
-            best_waves = waves;
         }
     }
     return best > 0 ? best : std::min(8, L.slabs);

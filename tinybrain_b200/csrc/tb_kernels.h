@@ -201,6 +201,7 @@ struct AttnParams {
     int* err;
 };
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
+constexpr int kMaxAttnSplits = 8;  // the splits of a (sequence, KV head) form one cluster
 size_t attention_scratch_bytes(int M, int Hkv, int nsplit, int G, int d);
 size_t attention_ticket_count(int M, int Hkv);
 int choose_nsplit(int M, int Hkv, int max_pages, int num_sms);
