@@ -291,11 +291,14 @@ tb_status tb_runner_io_bytes(tb_runner *r, int64_t *h2d_bytes, int64_t *d2h_byte
  * times_ms[n] receives the kernel durations, kinds[n] 0 = GEMV, 1 = attention;
  * *n in: capacity, out: count. */
 tb_status tb_runner_profile_step(tb_runner *r, float *times_ms, int32_t *kinds, int64_t *bytes, int32_t *n);
-/* Device timeline of one graph-replayed decode step: stamps[n][8] globaltimer
- * nanoseconds per launch (first CTA entry, last CTA entry, last dependency
- * release, last prologue done, last accumulator complete, last partial-sum
- * exchange, last exit, last first-weight arrival; 0 where a point does not
- * apply), kinds[n] as in tb_runner_profile_step. */
+/* Device timeline of one graph-replayed decode step: stamps[n][16] per launch:
+ * globaltimer nanoseconds [0..7] (first CTA entry, last CTA entry, last
+ * dependency release, last prologue done, last accumulator complete, last
+ * partial-sum exchange, last exit, last first-weight arrival) and, for INT4
+ * GEMVs, [8..15] SM-cycle sums of CTA 0's unit pipeline (stage waits, slot
+ * waits, nibble expansion, tensor-memory store, issue waits for A and B, B
+ * digit writes, units); 0 where a point does not apply.  kinds[n] as in
+ * tb_runner_profile_step. */
 tb_status tb_runner_trace_launches(tb_runner *r, uint64_t *stamps, int32_t *kinds, int32_t *n);
 
 #ifdef __cplusplus

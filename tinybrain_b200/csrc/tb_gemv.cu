@@ -27,6 +27,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 
 namespace tb {
 
@@ -68,10 +69,15 @@ struct GemvCfg {
 // 16-multiples past 8); INT4 4 digits per (row, 32-row weight group).
 __host__ __device__ constexpr int tc_nb(int mb) { return mb <= 2 ? 8 : (4 * mb + 15) / 16 * 16; }
 __host__ __device__ constexpr int q4_nb(int mb) { return 16 * mb; }
-// INT4 tensor memory: A slots [2 warpgroups][2] x 32 columns, then one
-// accumulator of max(NB, 32) columns per warpgroup.
-constexpr int kQ4ASlots = 2;
+// INT4 pipeline slots: kQ4Slots A operands in tensor memory (32 columns each)
+// and B operands in shared memory, then one accumulator of NB columns.
+constexpr int kQ4Slots = 4;
+constexpr int kGemvBarBytes = 512;  // mbarriers + tensor-memory address at the start of shared memory
+// red [RB][MB], misc [16 MB], row scales and biases [2 RB], seqinfo [3 MB], rowinv / rowex [2 MB]
+__host__ __device__ constexpr int gemv_head_floats(int rb, int mb) { return rb * mb + 16 * mb + 2 * rb + 5 * mb; }
 __host__ __device__ constexpr int q4_dcols(int mb) { return q4_nb(mb) < 32 ? 32 : q4_nb(mb); }
+// INT4 CTAs add a tensor-core issue warp to the producer and 8 consumer warps.
+__host__ __device__ constexpr int gemv_threads(int prec) { return prec == 4 ? kGemvThreads + 32 : kGemvThreads; }
 // At most 256 columns: two CTAs of any GEMV variant fit one SM's 512 together,
 // so a CTA never waits in tcgen05.alloc for another one to finish.
 __host__ __device__ constexpr int q4_tmem_cols(int mb) { return 256; }
@@ -95,14 +101,14 @@ __device__ __forceinline__ float gelu_ref(float x) {
 }
 
 template <int PREC, int RB, int MB>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __grid_constant__ GemvParams p) {
     using Cfg = GemvCfg<PREC, RB>;
     static_assert(RB == kTcTileRows, "tensor-core tiles are 128 rows");
     constexpr int STAGES = Cfg::kStages;
     constexpr int NB = PREC == 8 ? tc_nb(MB) : q4_nb(MB);
     static_assert(NB <= 256, "tcgen05 N is at most 256");
     // accumulator (INT8: NB columns; INT4: A slots + two accumulators), a power of two >= 32
-    static_assert(PREC != 4 || 2 * kQ4ASlots * 32 + 2 * q4_dcols(MB) <= q4_tmem_cols(MB), "INT4 TMEM budget");
+    static_assert(PREC != 4 || kQ4Slots * 32 + q4_dcols(MB) <= q4_tmem_cols(MB), "INT4 TMEM budget");
     constexpr uint32_t kTmemCols = PREC == 4 ? (uint32_t)q4_tmem_cols(MB)
                                              : (NB <= 32 ? 32u : NB <= 64 ? 64u : NB <= 128 ? 128u : 256u);
 
@@ -110,14 +116,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + STAGES;
     uint64_t* done = empty + STAGES;                                      // [2] accumulators complete
-    uint64_t* afree = done + 2;                                           // INT4: [2 warpgroups][kQ4ASlots]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(afree + 2 * kQ4ASlots);
-    float* red = reinterpret_cast<float*>(smem + 256);                    // [RB][MB]
+    uint64_t* a_ready = done + 2;                                         // INT4: [kQ4Slots] A in tensor memory
+    uint64_t* b_ready = a_ready + kQ4Slots;                               // INT4: [kQ4Slots] B in shared memory
+    uint64_t* s_free = b_ready + kQ4Slots;                                // INT4: [kQ4Slots] products done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + kQ4Slots);
+    static_assert((2 * STAGES + 2 + 3 * kQ4Slots) * 8 + 4 <= kGemvBarBytes, "barrier region");
+    float* red = reinterpret_cast<float*>(smem + kGemvBarBytes);          // [RB][MB]
     float* misc = red + RB * MB;                                          // [2][MB][8]
     float* rowsc = misc + 16 * MB;                                        // [RB] row scales (1 for INT4)
     float* rowbias = rowsc + RB;                                          // [RB] row biases (0 if none)
     int* seqinfo = reinterpret_cast<int*>(rowbias + RB);                  // [3][MB] pos, active, page
-    uint8_t* stage_base = smem + (256 + (RB * MB + 16 * MB + 2 * RB + 3 * MB) * 4 + 1023) / 1024 * 1024;
+    float* rowinv = reinterpret_cast<float*>(seqinfo + 3 * MB);           // [MB] 1/rms of each batch row
+    int* rowex = reinterpret_cast<int*>(rowinv + MB);                     // [MB] INT8 digit exponents
+    uint8_t* stage_base = smem + (kGemvBarBytes + gemv_head_floats(RB, MB) * 4 + 1023) / 1024 * 1024;
     uint8_t* xbuf = stage_base + STAGES * Cfg::kStageBytes;
     uint8_t* xd = xbuf;  // INT8: digit operand [k/16][NB][16]
 
@@ -135,13 +146,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     // Activation staging after the stage ring, kspan = the CTA's k range:
     //   INT8: digits [kspan/16][NB][16], x [MB][kspan] fp32, norm weights [kspan];
     //   INT4: x [MB][kspan] fp32, norm weights [kspan], B slots
-    //   [2][kQ4ASlots][NB * 128], per-unit max |x| [nunits][MB], per-unit max
+    //   [kQ4Slots][NB * 128], per-unit max |x| [nunits][MB], per-unit max
     //   |scale| [4][nunits], digit exponents [MB][4].
     const int kspan = ((L.slabs + P - 1) / P) * kTcUnitK;
     float* xs = reinterpret_cast<float*>(PREC == 8 ? xbuf + (size_t)kspan * NB : xbuf);
     float* wstage = xs + (size_t)MB * kspan;
     uint8_t* bslots = reinterpret_cast<uint8_t*>(wstage + kspan);
-    float* xmax = reinterpret_cast<float*>(bslots + 2 * kQ4ASlots * NB * 128);
+    float* xmax = reinterpret_cast<float*>(bslots + kQ4Slots * NB * 128);
     float* smaxs = xmax + (size_t)(kspan / kTcUnitK) * MB;
     int* ex4 = reinterpret_cast<int*>(smaxs + kQ4Groups * (kspan / kTcUnitK));
 
@@ -150,11 +161,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         trace_max(p.trace, 1);
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);  // released by tcgen05.commit
+            // INT8: released by tcgen05.commit; INT4: by the 8 consumer warps after reading it
+            mbar_init(&empty[i], PREC == 8 ? 1 : kGemvConsumerWarps);
         }
         mbar_init(&done[0], 1);
         mbar_init(&done[1], 1);
-        for (int i = 0; i < 2 * kQ4ASlots; ++i) mbar_init(&afree[i], 1);
+        for (int i = 0; i < kQ4Slots; ++i) {
+            mbar_init(&a_ready[i], 4);
+            mbar_init(&b_ready[i], 4);
+            mbar_init(&s_free[i], 1);
+        }
         fence_barrier_init();
     }
     if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
@@ -163,7 +179,37 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     tc_fence_after();
     pdl_launch_dependents();
 
-    if (warp == kGemvConsumerWarps) {
+    if (PREC == 4 && warp == kGemvConsumerWarps + 1) {
+        // ------------------------- INT4 tensor-core issue -------------------------
+        if (lane == 0) {
+            const uint32_t tmem = *tmem_slot;
+            const uint32_t idesc = tc_idesc_i8(NB);
+            int i = 0;
+            unsigned long long* prb = (p.trace && blockIdx.x == 0 && blockIdx.y == 0) ? p.trace : nullptr;
+            for (; i < nunits; ++i) {
+                const int sl = i % kQ4Slots;
+                const uint32_t par = (uint32_t)(i / kQ4Slots) & 1u;
+                long long c0 = prb ? clock64() : 0;
+                if (!mbar_wait(&a_ready[sl], par, p.err)) break;
+                if (prb) {
+                    atomicAdd(prb + 12, (unsigned long long)(clock64() - c0));
+                    c0 = clock64();
+                }
+                if (!mbar_wait(&b_ready[sl], par, p.err)) break;
+                if (prb) atomicAdd(prb + 13, (unsigned long long)(clock64() - c0));
+                tc_fence_after();
+                const uint32_t acol = tmem + (uint32_t)(sl * 32);
+                const uint32_t bsa = smem_u32(bslots + (size_t)sl * NB * 128);
+#pragma unroll
+                for (int s = 0; s < kTcUnitK / 32; ++s)
+                    tc_mma_i8_ts(tmem + (uint32_t)(kQ4Slots * 32), acol + 8 * s,
+                                 tc_sdesc(bsa + s * 2 * NB * 16, NB * 16, 128), idesc, i > 0 || s > 0);
+                tc_commit(&s_free[sl]);
+            }
+            tc_commit(&done[0]);
+        }
+        __syncwarp();
+    } else if (warp == kGemvConsumerWarps) {
         // ------------------------------- producer -------------------------------
         if (lane == 0) {
             const uint64_t pol = l2_policy_evict_first();
@@ -206,71 +252,69 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             seqinfo[MB + ctid] = sq.active;
             seqinfo[2 * MB + ctid] = sq.active ? p.page_table[(size_t)(m0 + ctid) * p.ptab_stride + pos / kPageTokens] : -1;
         }
-        // Source rows (embedding gather or activation buffer).
-        const float* srcm[MB];
-#pragma unroll
-        for (int m = 0; m < MB; ++m) {
-            if (p.prologue == kProEmbed || p.prologue == kProEmbedRms) {
+        // Source row m (embedding gather or activation buffer).
+        const bool embed = p.prologue == kProEmbed || p.prologue == kProEmbedRms;
+        auto srcrow = [&](int m) -> const float* {
+            if (embed) {
                 int tok = m < Mloc ? p.seq_ro[m0 + m].token : 0;
                 if (tok < 0 || tok >= p.vocab) {
                     record_error(p.err, kDevBadToken);
                     tok = 0;
                 }
-                srcm[m] = p.embedding + (size_t)tok * p.L.K;
-            } else {
-                srcm[m] = p.src + (size_t)(m0 + m) * p.ld_src;
+                return p.embedding + (size_t)tok * p.L.K;
             }
-        }
+            return p.src + (size_t)(m0 + m) * p.ld_src;
+        };
         // Embedding prologue: CTA 0 materialises the residual stream h.
-        if ((p.prologue == kProEmbed || p.prologue == kProEmbedRms) && blockIdx.x == 0) {
-            for (int m = 0; m < Mloc; ++m)
-                for (int k = ctid; k < L.K; k += 256) p.resid[(size_t)(m0 + m) * p.ld_src + k] = srcm[m][k];
+        if (embed && blockIdx.x == 0) {
+            for (int m = 0; m < Mloc; ++m) {
+                const float* sr = srcrow(m);
+                for (int k = ctid; k < L.K; k += 256) p.resid[(size_t)(m0 + m) * p.ld_src + k] = sr[k];
+            }
         }
         // Tensor.swift:1538-1558: ss = sum x^2; inv = 1 / sqrt(ss/H + eps).  The
         // INT8 path also needs max |x| over this CTA's k range (digit scale).
-        // One pass over the source: the sum of squares over the whole row and
-        // the CTA's k range staged into shared memory (zero past K), so the
-        // digit pass reads no global memory.
-        float inv[MB];
-        int ex[MB];
-#pragma unroll
-        for (int m = 0; m < MB; ++m) {
-            inv[m] = 1.0f;
-            ex[m] = 0;
-        }
+        // One pass over the source, rows in parallel (WPR warps per row, each a
+        // slice of it): the sum of squares over the whole row and the CTA's k
+        // range staged into shared memory (zero past K), so the digit pass
+        // reads no global memory.  Per-row 1/rms and digit exponents go to
+        // shared memory (rowinv, rowex).
         // rows are read as float4 when K and the row stride allow it
-        const bool v4 = (L.K % 4 == 0) && (p.prologue == kProEmbed || p.prologue == kProEmbedRms || p.ld_src % 4 == 0);
+        const bool v4 = (L.K % 4 == 0) && (embed || p.ld_src % 4 == 0);
         const int kq = kspan / 4;  // float4 groups of the staged range
+        constexpr int WPR = MB >= 8 ? 1 : 8 / MB;
+        constexpr int RS = 8 / WPR;  // rows in flight
+        const int sw = warp % WPR;
         __syncwarp();
         named_bar_sync(1, 256);  // norm weights staged
-#pragma unroll
-        for (int m = 0; m < MB; ++m) {
+        for (int m = warp / WPR; m < MB; m += RS) {
             float ss = 0.0f, mx = 0.0f;
             float* xr = xs + (size_t)m * kspan;
             if (m < Mloc) {
+                const float* sr = srcrow(m);
                 if (rms) {
                     if (v4) {
-                        for (int k = 4 * ctid; k < L.K; k += 1024) {
-                            const float4 a = *reinterpret_cast<const float4*>(srcm[m] + k);
+                        for (int k = 4 * (sw * 32 + lane); k < L.K; k += 128 * WPR) {
+                            const float4 a = *reinterpret_cast<const float4*>(sr + k);
                             ss = fmaf(a.x, a.x, ss);
                             ss = fmaf(a.y, a.y, ss);
                             ss = fmaf(a.z, a.z, ss);
                             ss = fmaf(a.w, a.w, ss);
                         }
                     } else {
-                        for (int k = ctid; k < L.K; k += 256) ss = fmaf(srcm[m][k], srcm[m][k], ss);
+                        for (int k = sw * 32 + lane; k < L.K; k += 32 * WPR) ss = fmaf(sr[k], sr[k], ss);
                     }
                 }
-                for (int g = ctid; g < kq; g += 256) {
+                for (int g = sw * 32 + lane; g < kq; g += 32 * WPR) {
                     const int k = kbeg + 4 * g;
                     float4 a;
                     if (v4 && k + 3 < L.K) {
-                        a = *reinterpret_cast<const float4*>(srcm[m] + k);
+                        a = *reinterpret_cast<const float4*>(sr + k);
                     } else {
-                        a.x = k < L.K ? srcm[m][k] : 0.0f;
-                        a.y = k + 1 < L.K ? srcm[m][k + 1] : 0.0f;
-                        a.z = k + 2 < L.K ? srcm[m][k + 2] : 0.0f;
-                        a.w = k + 3 < L.K ? srcm[m][k + 3] : 0.0f;
+                        a.x = k < L.K ? sr[k] : 0.0f;
+                        a.y = k + 1 < L.K ? sr[k + 1] : 0.0f;
+                        a.z = k + 2 < L.K ? sr[k + 2] : 0.0f;
+                        a.w = k + 3 < L.K ? sr[k + 3] : 0.0f;
                     }
                     *reinterpret_cast<float4*>(xr + 4 * g) = a;
                     if (PREC == 8) {
@@ -283,44 +327,42 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                     }
                 }
             } else {
-                for (int g = ctid; g < kq; g += 256)
+                for (int g = sw * 32 + lane; g < kq; g += 32 * WPR)
                     *reinterpret_cast<float4*>(xr + 4 * g) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            if (rms || PREC == 8) {
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    ss += __shfl_xor_sync(0xffffffffu, ss, o);
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                }
-                if (lane == 0) {
-                    misc[m * 8 + warp] = ss;
-                    misc[(MB + m) * 8 + warp] = mx;
-                }
+            for (int o = 16; o > 0; o >>= 1) {
+                ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            }
+            if (lane == 0) {
+                misc[m * 8 + sw] = ss;
+                misc[(MB + m) * 8 + sw] = mx;
             }
         }
         named_bar_sync(1, 256);
-        if (rms || PREC == 8) {
-#pragma unroll
-            for (int m = 0; m < MB; ++m) {
-                float ss = 0.0f, mx = 0.0f;
-#pragma unroll
-                for (int w = 0; w < 8; ++w) {
-                    ss += misc[m * 8 + w];
-                    mx = fmaxf(mx, misc[(MB + m) * 8 + w]);
-                }
-                if (rms) inv[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)L.K), p.eps)));
-                // x = src * w * inv and inv > 0: max |x| = max |src * w| * inv (one rounding above)
-                ex[m] = digit_exponent(__fmul_rn(mx, inv[m]) * 1.0000002f);
+        if (ctid < MB) {
+            const int m = ctid;
+            float ss = 0.0f, mx = 0.0f;
+            for (int w = 0; w < WPR; ++w) {
+                ss += misc[m * 8 + w];
+                mx = fmaxf(mx, misc[(MB + m) * 8 + w]);
             }
+            const float iv = rms ? __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)L.K), p.eps))) : 1.0f;
+            rowinv[m] = iv;
+            // x = src * w * inv and inv > 0: max |x| = max |src * w| * inv (one rounding above)
+            rowex[m] = digit_exponent(__fmul_rn(mx, iv) * 1.0000002f);
         }
+        named_bar_sync(1, 256);
         // four consecutive staged k (g = (k - kbeg) / 4), normalised as the
         // reference does: (x * inv) * w
         auto xval4 = [&](int m, int g) -> float4 {
             float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * kspan + 4 * g);
             if (rms) {
                 const float4 w = *reinterpret_cast<const float4*>(wstage + 4 * g);
-                a = make_float4(__fmul_rn(__fmul_rn(a.x, inv[m]), w.x), __fmul_rn(__fmul_rn(a.y, inv[m]), w.y),
-                                __fmul_rn(__fmul_rn(a.z, inv[m]), w.z), __fmul_rn(__fmul_rn(a.w, inv[m]), w.w));
+                const float iv = rowinv[m];
+                a = make_float4(__fmul_rn(__fmul_rn(a.x, iv), w.x), __fmul_rn(__fmul_rn(a.y, iv), w.y),
+                                __fmul_rn(__fmul_rn(a.z, iv), w.z), __fmul_rn(__fmul_rn(a.w, iv), w.w));
             }
             return a;
         };
@@ -331,7 +373,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             for (int g = ctid; g < ngroups; g += 256) {
 #pragma unroll
                 for (int m = 0; m < MB; ++m) {
-                    put_digits4(xd, NB, 4 * g, m, xval4(m, g), __int_as_float((127 - ex[m]) << 23));
+                    put_digits4(xd, NB, 4 * g, m, xval4(m, g), __int_as_float((127 - rowex[m]) << 23));
                 }
                 if (NB > kTcDigits * MB) {  // unused digit rows read as zero
                     uint8_t* base = xd + (size_t)(g >> 2) * NB * 16 + (4 * g & 15);
@@ -374,7 +416,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                 tmem_ld_wait();
                 const int row = 32 * (warp - 4) + lane;
 #pragma unroll
-                for (int m = 0; m < MB; ++m) red[row * MB + m] = okd ? combine_digits(d + kTcDigits * m, ex[m]) : 0.0f;
+                for (int m = 0; m < MB; ++m) red[row * MB + m] = okd ? combine_digits(d + kTcDigits * m, rowex[m]) : 0.0f;
                 tc_fence_before();
             }
         } else {
@@ -405,50 +447,41 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
             }
             named_bar_sync(1, 256);
             if (ctid == 0) trace_max(p.trace, 3);
-            // (3) units alternate between the two warpgroups; each expands its
-            //     unit's nibbles into the A slot in tensor memory, writes the
-            //     digits of scale * x into its B slot, and its leader issues
-            //     the four K = 32 products into the warpgroup's accumulator.
+            // (3) a four-deep slot pipeline: warps 0-3 expand each unit's
+            //     nibbles into an A slot in tensor memory (warp w owns TMEM
+            //     lanes 32w..32w+31 = tile rows), warps 4-7 write the digits of
+            //     scale * x into the matching B slot, and the issue warp runs
+            //     the four K = 32 products once both are ready.  Lane 0 of each
+            //     warp waits (bounded) and broadcasts the outcome, so a timed-out
+            //     wait ends the warp's loop as a whole.
             const uint32_t tmem = *tmem_slot;
-            const int wg = warp >> 2, wq = warp & 3;
-            const int t = ctid & 127;
+            const int wq = warp & 3;
+            const bool arole = warp < 4;
             const uint32_t lane_base = (uint32_t)(32 * wq) << 16;
-            const uint32_t dcol = (uint32_t)(2 * kQ4ASlots * 32 + wg * q4_dcols(MB));
-            const uint32_t idesc = tc_idesc_i8(NB);
-            // One thread per warpgroup waits (bounded) and tells the others
-            // through `okflag`, so a timed-out wait ends the loop of the whole
-            // warpgroup together (its named barriers stay matched).
-            volatile int* okflag = reinterpret_cast<volatile int*>(misc) + 2 + wg;
-            int j = 0;
-            for (int i = wg; i < nunits; i += 2, ++j) {
+            // pipeline probes: CTA 0, lane 0 of warps 0 (A) and 4 (B)
+            unsigned long long* prb =
+                (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && (warp == 0 || warp == 4) && lane == 0) ? p.trace
+                                                                                                      : nullptr;
+            long long c0 = 0;
+            uint32_t a[32];  // A role: the unit's int8 row, stored to tensor memory
+            for (int i = 0; i < nunits; ++i) {
                 const int st = i % STAGES;
-                const int slot = j & 1;
-                if (t == 0) {
-                    bool ok = mbar_wait(&full[st], (i / STAGES) & 1, p.err);
-                    if (ok && j >= kQ4ASlots) ok = mbar_wait(&afree[wg * kQ4ASlots + slot], ((j >> 1) - 1) & 1, p.err);
-                    *okflag = ok ? 1 : 0;
+                const int sl = i % kQ4Slots;
+                int ok = 1;
+                if (lane == 0) {
+                    if (prb) c0 = clock64();
+                    ok = mbar_wait(&full[st], (i / STAGES) & 1, p.err) ? 1 : 0;
+                    if (prb && arole) atomicAdd(prb + 8, (unsigned long long)(clock64() - c0));
+                    if (prb) c0 = clock64();
+                    if (ok && i >= kQ4Slots) ok = mbar_wait(&s_free[sl], ((i / kQ4Slots) - 1) & 1, p.err) ? 1 : 0;
+                    if (prb && arole) atomicAdd(prb + 9, (unsigned long long)(clock64() - c0));
+                    if (prb) c0 = clock64();
                 }
-                named_bar_sync(2 + wg, 128);
-                if (!*okflag) break;
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
                 tc_fence_after();
                 const uint8_t* ust = stage_base + st * Cfg::kStageBytes;
-                // B: 4 consecutive k (quad q) of row group gq for every batch row
-                {
-                    const int q = t & 31, gq = t >> 5;
-                    const float4 sc = *reinterpret_cast<const float4*>(ust + kQ4UnitNibBytes + (gq * kTcUnitK + 4 * q) * 4);
-                    uint8_t* bs = bslots + (size_t)(wg * kQ4ASlots + slot) * NB * 128;
-#pragma unroll
-                    for (int m = 0; m < MB; ++m) {
-                        const float4 x = *reinterpret_cast<const float4*>(xs + (size_t)m * kspan + i * kTcUnitK + 4 * q);
-                        const float4 v = make_float4(__fmul_rn(sc.x, x.x), __fmul_rn(sc.y, x.y), __fmul_rn(sc.z, x.z),
-                                                     __fmul_rn(sc.w, x.w));
-                        put_digits4(bs, NB, 4 * q, m * kQ4Groups + gq, v,
-                                    __int_as_float((127 - ex4[m * kQ4Groups + gq]) << 23));
-                    }
-                }
-                // A: this thread's row (TMEM lane) = 32 * wq + lane
-                {
-                    uint32_t a[32];
+                if (arole) {
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         const uint4 w = *reinterpret_cast<const uint4*>(ust + (c * kTcTileRows + 32 * wq + lane) * 16);
@@ -457,45 +490,68 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                         q4_expand(w.z, a[8 * c + 4], a[8 * c + 5]);
                         q4_expand(w.w, a[8 * c + 6], a[8 * c + 7]);
                     }
-                    tmem_st32(tmem + lane_base + (uint32_t)((wg * kQ4ASlots + slot) * 32), a);
-                }
-                tmem_st_wait();
-                fence_proxy_async_shared();
-                tc_fence_before();
-                named_bar_sync(2 + wg, 128);
-                if (t == 0) {
-                    tc_fence_after();
-                    const uint32_t acol = tmem + (uint32_t)((wg * kQ4ASlots + slot) * 32);
-                    const uint32_t bsa = smem_u32(bslots + (size_t)(wg * kQ4ASlots + slot) * NB * 128);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+                    if (prb) {
+                        atomicAdd(prb + 10, (unsigned long long)(clock64() - c0));
+                        c0 = clock64();
+                    }
+                    // complete the previous unit's store (its latency overlapped
+                    // this unit's waits and expansion), then issue this one's
+                    if (i > 0) {
+                        tmem_st_wait();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&a_ready[(i - 1) % kQ4Slots]);
+                    }
+                    tmem_st32(tmem + lane_base + (uint32_t)(sl * 32), a);
+                    if (prb) {
+                        atomicAdd(prb + 11, (unsigned long long)(clock64() - c0));
+                        atomicAdd(prb + 15, 1ull);
+                    }
+                } else {
+                    // 4 consecutive k (quad q) of row group wq for every batch row
+                    const int q = lane;
+                    const float4 sc =
+                        *reinterpret_cast<const float4*>(ust + kQ4UnitNibBytes + (wq * kTcUnitK + 4 * q) * 4);
+                    uint8_t* bs = bslots + (size_t)sl * NB * 128;
 #pragma unroll
-                    for (int s = 0; s < kTcUnitK / 32; ++s)
-                        tc_mma_i8_ts(tmem + dcol, acol + 8 * s, tc_sdesc(bsa + s * 2 * NB * 16, NB * 16, 128), idesc,
-                                     j > 0 || s > 0);
-                    tc_commit(&empty[st]);
-                    tc_commit(&afree[wg * kQ4ASlots + slot]);
+                    for (int m = 0; m < MB; ++m) {
+                        const float4 x = *reinterpret_cast<const float4*>(xs + (size_t)m * kspan + i * kTcUnitK + 4 * q);
+                        const float4 v = make_float4(__fmul_rn(sc.x, x.x), __fmul_rn(sc.y, x.y), __fmul_rn(sc.z, x.z),
+                                                     __fmul_rn(sc.w, x.w));
+                        put_digits4(bs, NB, 4 * q, m * kQ4Groups + wq, v,
+                                    __int_as_float((127 - ex4[m * kQ4Groups + wq]) << 23));
+                    }
+                    fence_proxy_async_shared();
+                    __syncwarp();  // every lane has used its scales: the stage may be refilled
+                    if (lane == 0) {
+                        mbar_arrive(&empty[st]);
+                        mbar_arrive(&b_ready[sl]);
+                    }
+                    if (prb) atomicAdd(prb + 14, (unsigned long long)(clock64() - c0));
                 }
             }
-            if (t == 0 && j > 0) tc_commit(&done[wg]);
-            // (4) epilogue: warpgroup 0 reads both accumulators; lane row
-            //     32 * wq + lane belongs to row group wq.
-            if (wg == 0) {
-                const bool h0 = nunits > 0, h1 = nunits > 1;
+            if (arole && nunits > 0) {  // the last unit's store
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_ready[(nunits - 1) % kQ4Slots]);
+            }
+            // (4) epilogue: warps 0-3 read the accumulator; lane row 32 * wq +
+            //     lane belongs to row group wq.
+            if (arole) {
                 bool okd = true;
-                if (h0) okd = mbar_wait(&done[0], 0, p.err) && okd;
-                if (h1) okd = mbar_wait(&done[1], 0, p.err) && okd;
-                if (t == 0) trace_max(p.trace, 4);
+                if (nunits > 0) okd = mbar_wait(&done[0], 0, p.err);
+                if (lane == 0) trace_max(p.trace, 4);
                 tc_fence_after();
                 const int row = 32 * wq + lane;
 #pragma unroll
                 for (int m = 0; m < MB; ++m) {
-                    const uint32_t c = (uint32_t)((m * kQ4Groups + wq) * kTcDigits);
-                    int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
-                    if (h0) tmem_ld4(tmem + lane_base + (uint32_t)(2 * kQ4ASlots * 32) + c, d0);
-                    if (h1) tmem_ld4(tmem + lane_base + (uint32_t)(2 * kQ4ASlots * 32 + q4_dcols(MB)) + c, d1);
+                    int d[4] = {0, 0, 0, 0};
+                    if (nunits > 0)
+                        tmem_ld4(tmem + lane_base + (uint32_t)(kQ4Slots * 32 + (m * kQ4Groups + wq) * kTcDigits), d);
                     tmem_ld_wait();
-                    int d[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) d[e] = d0[e] + d1[e];
                     red[row * MB + m] = okd ? combine_digits(d, ex4[m * kQ4Groups + wq]) : 0.0f;
                 }
                 tc_fence_before();
@@ -699,13 +755,13 @@ inline size_t gemv_xbytes(int prec, int mb, const QLayout& L, int P) {
     const size_t units = (size_t)((L.slabs + P - 1) / P);
     const size_t xw = units * kTcUnitK * (mb + 1) * 4;  // x and norm weights, fp32
     if (prec == 8) return units * kTcUnitK * (size_t)tc_nb(mb) + xw;
-    return xw + (size_t)2 * kQ4ASlots * q4_nb(mb) * 128 + units * (mb + kQ4Groups) * 4 + (size_t)mb * kQ4Groups * 4;
+    return xw + (size_t)kQ4Slots * q4_nb(mb) * 128 + units * (mb + kQ4Groups) * 4 + (size_t)mb * kQ4Groups * 4;
 }
 
 template <int PREC, int RB, int MB>
 size_t gemv_smem_bytes(const QLayout& L, int P) {
     using Cfg = GemvCfg<PREC, RB>;
-    size_t head = (256 + (size_t)(RB * MB + 16 * MB + 2 * RB + 3 * MB) * 4 + 1023) / 1024 * 1024;
+    size_t head = (kGemvBarBytes + (size_t)gemv_head_floats(RB, MB) * 4 + 1023) / 1024 * 1024;
     size_t stages = (size_t)Cfg::kStages * Cfg::kStageBytes;
     return head + stages + gemv_xbytes(PREC, MB, L, P);
 }
@@ -716,9 +772,13 @@ cudaError_t launch_t(const GemvParams& p, cudaStream_t stream, bool pdl) {
     auto kfn = gemv_kernel<PREC, RB, MB>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
+    // All of the SM's unified L1/shared storage as shared memory, so that two
+    // CTAs (of this launch, or of this and the next launch) fit side by side.
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)(p.L.Np / RB * p.P), (unsigned)((p.M + MB - 1) / MB), 1);
-    cfg.blockDim = dim3(kGemvThreads, 1, 1);
+    cfg.blockDim = dim3(gemv_threads(PREC), 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attrs[2];
@@ -741,20 +801,28 @@ cudaError_t launch_t(const GemvParams& p, cudaStream_t stream, bool pdl) {
 }  // namespace
 
 int choose_ksplit(const QLayout& L, int M, int num_sms) {
+    if (const char* e = getenv("TB_GEMV_P")) {  // tuning override: a fixed cluster size
+        const int f = atoi(e);
+        if (f > 0) return std::max(1, std::min(std::min(8, L.slabs), f));
+    }
     // Pick the cluster size P (k split) so that every CTA of the launch is
     // resident at once (no second wave: a wave boundary costs a whole CTA
     // lifetime) while each CTA streams as few units as possible.
     const int nrb = L.Np / L.RB;
     const int mb = gemv_mb(L.precision, M);
     const int splits = (M + mb - 1) / mb;  // grid y
-    const size_t head = (256 + (size_t)(L.RB * mb + 16 * mb + 2 * L.RB + 3 * mb) * 4 + 1023) / 1024 * 1024;
+    const size_t head = (kGemvBarBytes + (size_t)gemv_head_floats(L.RB, mb) * 4 + 1023) / 1024 * 1024;
     const size_t stages = L.precision == 8 ? (size_t)GemvCfg<8, 128>::kStages * GemvCfg<8, 128>::kStageBytes
                                            : (size_t)GemvCfg<4, 128>::kStages * GemvCfg<4, 128>::kStageBytes;
     constexpr size_t kSmPerSm = 228 * 1024;  // shared memory per SM, 1 KB reserved per CTA
     // Time model (us): a wave costs a CTA lifetime of fixed latency (launch,
-    // prologue, reduction, epilogue: ~4 us measured), and an SM streams a
-    // 16 KB unit in ~0.35 us at its share of HBM bandwidth.
-    constexpr double kWaveUs = 4.0, kUnitUs = 0.35;
+    // prologue, reduction, epilogue: ~4 us measured); within it a CTA needs
+    // max(its own unit pipeline: ~0.15 us per INT8 unit, ~0.42 us per INT4
+    // unit, measured; the SM's share of HBM bandwidth, ~44 KB/us, for the
+    // units of all CTAs on that SM).
+    constexpr double kWaveUs = 4.0, kSmKBperUs = 44.0;
+    const double unit_us = L.precision == 8 ? 0.15 : 0.42;
+    const double unit_kb = (L.precision == 8 ? kTcUnitBytes : kQ4UnitBytes) / 1024.0;
     int best = 0;
     double best_cost = 0.0;
     for (int P = 1; P <= std::min(8, L.slabs); ++P) {
@@ -767,7 +835,8 @@ int choose_ksplit(const QLayout& L, int M, int num_sms) {
         const long long cap = (long long)occ * num_sms;
         const long long waves = (ctas + cap - 1) / cap;
         const long long per_sm = (ctas + num_sms - 1) / num_sms;
-        const double cost = waves * kWaveUs + (double)per_sm * ((L.slabs + P - 1) / P) * kUnitUs;
+        const int units = (L.slabs + P - 1) / P;
+        const double cost = waves * (kWaveUs + std::max(units * unit_us, (double)per_sm * units * unit_kb / kSmKBperUs));
         if (best == 0 || cost < best_cost) {
             best = P;
             best_cost = cost;

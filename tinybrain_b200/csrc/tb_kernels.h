@@ -105,8 +105,11 @@ struct SeqState {
 // Optional device timeline of one launch (globaltimer ns; nullptr = off):
 // [0] first CTA entry (min), [1] last CTA entry, [2] last dependency release,
 // [3] last prologue done, [4] last accumulator complete, [5] last partial-sum
-// exchange done, [6] last CTA exit, [7] last first-weight-unit arrival.
-constexpr int kTracePoints = 8;
+// exchange done, [6] last CTA exit, [7] last first-weight-unit arrival;
+// [8..15] INT4 pipeline of CTA 0, SM cycles summed over its units: [8] stage
+// waits, [9] slot waits, [10] nibble expansion, [11] tensor-memory store, [12]
+// issue waits for A, [13] for B, [14] B digit writes, [15] units.
+constexpr int kTracePoints = 16;
 
 struct GemvParams {
     unsigned long long* trace;

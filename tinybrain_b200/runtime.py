@@ -721,9 +721,9 @@ class ModelRunner:
         return t[:n.value].copy(), k[:n.value].copy(), b[:n.value].copy()
 
     def trace_launches(self):
-        """Device timeline of one decode step: (stamps [n][8] ns, kinds [n])."""
+        """Device timeline of one decode step: (stamps [n][16], kinds [n])."""
         cap = 4096
-        st = np.zeros((cap, 8), dtype=np.uint64)
+        st = np.zeros((cap, 16), dtype=np.uint64)
         k = np.zeros(cap, dtype=np.int32)
         n = C.c_int32(cap)
         call("tb_runner_trace_launches", self.handle, _ptr(st), _ptr(k), C.byref(n))
