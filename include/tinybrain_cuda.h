@@ -159,13 +159,12 @@ tb_status tb_paged_attention_dev(tb_context *ctx, const float *q_dev, int32_t ba
  * computation and arguments as tb_paged_attention_dev, for callers that cannot
  * allocate device memory -- a host that has given all HBM to its own pool, or
  * a latency-critical path where cudaMalloc/cudaFree would synchronise the
- * device.  It allocates nothing: the split-K scratch is a fixed 4 MiB array
- * (plus 4096 counters) that every GPU loading the library keeps until exit.
- * Runs on `stream` (a cudaStream_t, NULL = default stream) of the current
- * device.  The first call on a device looks up the array's device address and
- * should come before any stream capture.  Sizes whose scratch exceeds the
- * array are rejected with TB_ERR_INVALID_ARGUMENT.  All calls share the array:
- * calls that overlap on the GPU (other streams, other host threads) race. */
+ * device.  It allocates nothing: the splits of each (sequence, KV head) are
+ * combined inside their thread-block cluster, with no scratch memory, so any
+ * batch size is accepted and concurrent calls are independent.  Runs on
+ * `stream` (a cudaStream_t, NULL = default stream) of the current device.  The
+ * first call on a device reads its SM count and should come before any stream
+ * capture. */
 tb_status tb_paged_attention_dev_noalloc(void *stream, const float *q_dev, int32_t batch, const float *kv_pool_dev,
                                          const int32_t *page_table_dev, int32_t ptab_stride,
                                          const int32_t *seq_lens_dev, int32_t max_len, int32_t layer,

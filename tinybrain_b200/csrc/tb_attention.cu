@@ -352,10 +352,6 @@ __global__ void rmsnorm_rows_kernel(const float* h, const float* w, int H, int l
 
 }  // namespace
 
-size_t attention_scratch_bytes(int M, int Hkv, int nsplit, int G, int d) {
-    return (size_t)M * Hkv * nsplit * G * (d + 4) * sizeof(float);
-}
-size_t attention_ticket_count(int M, int Hkv) { return (size_t)M * Hkv; }
 
 int choose_nsplit(int M, int Hkv, int max_pages, int num_sms) {
     // About one CTA per SM over the (sequence, KV head) pairs at the longest
@@ -421,40 +417,23 @@ cudaError_t launch_attention_probs(const AttnParams& p, float* probs, int L, cud
 // Some callers cannot create device allocations at all: a host that hands
 // every byte of HBM to its own pool before loading this library, or code on a
 // latency-critical path where cudaMalloc / cudaFree would synchronise the
-// device.  tb_paged_attention_dev_noalloc serves them: its split-K scratch
-// lives in the fixed-size arrays below, which every GPU that loads the library
-// holds until the process exits.
+// device.  tb_paged_attention_dev_noalloc serves them: the split partials are
+// combined inside each CTA cluster through distributed shared memory, so the
+// kernel needs no global scratch; the entry point only caches the SM count.
 // ---------------------------------------------------------------------------
 namespace tb {
 namespace {
-constexpr size_t kNoAllocPartFloats = size_t(1) << 20;  // 4 MiB of split partials
-constexpr size_t kNoAllocTickets = 4096;                // (sequence, KV head) counters
-static __device__ __align__(256) float g_noalloc_part[kNoAllocPartFloats];
-static __device__ __align__(256) unsigned int g_noalloc_tickets[kNoAllocTickets];
-
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
-float* g_noalloc_part_ptr[kMaxDevices] = {};
-unsigned int* g_noalloc_ticket_ptr[kMaxDevices] = {};
 int g_noalloc_sms[kMaxDevices] = {};
 
-// Once per device, with that device current: the device addresses of the
-// arrays (host code only sees a host-side stand-in under their names).
 cudaError_t noalloc_setup(int dev) {
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (g_noalloc_part_ptr[dev]) return cudaSuccess;
-    void* part = nullptr;
-    void* tickets = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&part, g_noalloc_part);
-    if (e != cudaSuccess) return e;
-    e = cudaGetSymbolAddress(&tickets, g_noalloc_tickets);
-    if (e != cudaSuccess) return e;
+    if (g_noalloc_sms[dev]) return cudaSuccess;
     int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     g_noalloc_sms[dev] = sms;
-    g_noalloc_ticket_ptr[dev] = static_cast<unsigned int*>(tickets);
-    g_noalloc_part_ptr[dev] = static_cast<float*>(part);
     return cudaSuccess;
 }
 }  // namespace
@@ -477,24 +456,10 @@ extern "C" tb_status tb_paged_attention_dev_noalloc(void* stream, const float* q
         return (tb_status)report_error(TB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
     e = noalloc_setup(dev);
     if (e != cudaSuccess)
-        return (tb_status)report_error(TB_ERR_CUDA, "scratch set-up (cudaGetSymbolAddress): %s",
-                                       cudaGetErrorString(e));
-    const int G = H / Hkv;
+        return (tb_status)report_error(TB_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
     const int max_pages = (max_len + kPageTokens - 1) / kPageTokens;
     const int ns = choose_nsplit(batch, Hkv, max_pages, g_noalloc_sms[dev]);
-    const size_t need = attention_scratch_bytes(batch, Hkv, ns, G, d) / sizeof(float);
-    const size_t nt = attention_ticket_count(batch, Hkv);
-    if (need > kNoAllocPartFloats || nt > kNoAllocTickets)
-        return (tb_status)report_error(
-            TB_ERR_INVALID_ARGUMENT,
-            "tb_paged_attention_dev_noalloc: needs %zu scratch floats and %zu tickets, the fixed maximum is %zu "
-            "floats (4 MiB) and %zu tickets; use tb_paged_attention_dev for this size",
-            need, nt, kNoAllocPartFloats, kNoAllocTickets);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // The counters must start at zero; a completed call leaves them at zero,
-    // an interrupted one might not.
-    e = cudaMemsetAsync(g_noalloc_ticket_ptr[dev], 0, nt * sizeof(unsigned int), st);
-    if (e != cudaSuccess) return (tb_status)report_error(TB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
     AttnParams a{};
     a.q = q;
     a.ld_q = H * d;
@@ -512,8 +477,6 @@ extern "C" tb_status tb_paged_attention_dev_noalloc(void* stream, const float* q
     a.nsplit = ns;
     a.out = out;
     a.ld_out = H * d;
-    a.part = g_noalloc_part_ptr[dev];
-    a.tickets = g_noalloc_ticket_ptr[dev];
     a.err = nullptr;
     e = launch_attention(a, st, false);
     if (e != cudaSuccess)

@@ -199,14 +199,10 @@ struct AttnParams {
     int nsplit;
     float* out;               // [M][H*d]
     int ld_out;
-    float* part;              // scratch partials [M][Hkv][nsplit][G][d + 4] (16-byte rows)
-    unsigned int* tickets;    // scratch counters [M][Hkv], zero on entry, left zero
     int* err;
 };
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
 constexpr int kMaxAttnSplits = 8;  // the splits of a (sequence, KV head) form one cluster
-size_t attention_scratch_bytes(int M, int Hkv, int nsplit, int G, int d);
-size_t attention_ticket_count(int M, int Hkv);
 int choose_nsplit(int M, int Hkv, int max_pages, int num_sms);
 
 // ----------------------------------------------------------------------------

@@ -138,8 +138,6 @@ struct tb_context {
     int num_sms = 148;
     cudaStream_t stream = nullptr;
     DevBuf err;          // int device error word
-    DevBuf scratch;      // attention partials
-    DevBuf tickets;      // attention tickets (zeroed)
     DevBuf io_a, io_b, io_c, io_d;  // staging for host-pointer entry points
     DevBuf seq_tmp;
     // tensor parallelism: NCCL communicator over the ranks sharing a model
@@ -222,7 +220,6 @@ struct tb_runner {
     int total_pages = 0;
     // device buffers
     DevBuf seq, ptab, kv, h, q, ctxv, act, logits, rope, prompt, out_tokens, ticket;
-    DevBuf attn_part, attn_tickets;  // runner-owned: captured by the step graph
     int64_t h2d_bytes = 0, d2h_bytes = 0;  // host<->device traffic of the generate paths
     int prompt_stride = 0, max_out = 0;
     // host mirror
@@ -721,17 +718,8 @@ static tb_status check_heads(int H, int Hkv, int d) {
 static tb_status run_paged_attention(tb_context* ctx, const float* q, int batch, const float* pool,
                                      const int* ptab, int ptab_stride, const int* lens, int max_len, int layer,
                                      int num_layers, int H, int Hkv, int d, float* out) {
-    const int G = H / Hkv;
     const int max_pages = (max_len + kPageTokens - 1) / kPageTokens;
     const int ns = choose_nsplit(batch, Hkv, std::max(1, max_pages), ctx->num_sms);
-    tb_status s = ensure(ctx->scratch, attention_scratch_bytes(batch, Hkv, ns, G, d));
-    if (s != TB_OK) return s;
-    const size_t tb = attention_ticket_count(batch, Hkv) * 4;
-    if (ctx->tickets.bytes < tb) {
-        s = ensure(ctx->tickets, tb);
-        if (s != TB_OK) return s;
-        TB_CUDA(cudaMemsetAsync(ctx->tickets.p, 0, ctx->tickets.bytes, ctx->stream));
-    }
     AttnParams a{};
     a.q = q;
     a.ld_q = H * d;
@@ -749,8 +737,6 @@ static tb_status run_paged_attention(tb_context* ctx, const float* q, int batch,
     a.nsplit = ns;
     a.out = out;
     a.ld_out = H * d;
-    a.part = ctx->scratch.as<float>();
-    a.tickets = ctx->tickets.as<unsigned int>();
     a.err = ctx->err.as<int>();
     TB_CUDA(launch_attention(a, ctx->stream, false));
     return ok();
@@ -1185,8 +1171,6 @@ static tb_status build_plan(tb_runner* r) {
             a.nsplit = r->nsplit;
             a.out = r->ctxv.as<float>();
             a.ld_out = qd;
-            a.part = r->attn_part.as<float>();
-            a.tickets = r->attn_tickets.as<unsigned int>();
             a.err = r->ctx->err.as<int>();
             ln.bytes = 0;  // depends on the context length; accounted by the caller
             r->plan.push_back(ln);
@@ -1523,11 +1507,8 @@ extern "C" tb_status tb_runner_create(tb_model* m, int32_t max_batch, int32_t ma
     r->ptab_dirty.assign(B, 1);
     TB_CUDA(r->pin_ptab.ensure(r->ptab_host.size() * 4));
     TB_CUDA(r->pin_seq.ensure(sizeof(SeqState) * B));
-    // Attention scratch sized for the longest context.
+    // Attention splits per (sequence, KV head), sized for the longest context.
     r->nsplit = choose_nsplit(B, c.num_kv_heads, r->ptab_stride, ctx->num_sms);
-    TB_CUDA(r->attn_part.alloc(attention_scratch_bytes(B, c.num_kv_heads, r->nsplit, c.num_heads / c.num_kv_heads, d)));
-    TB_CUDA(r->attn_tickets.alloc(attention_ticket_count(B, c.num_kv_heads) * 4));
-    TB_CUDA(cudaMemset(r->attn_tickets.p, 0, r->attn_tickets.bytes));
     tb_status s = TB_OK;
     // Prompt / output buffers start small and grow in generate.
     r->prompt_stride = 1;
