@@ -428,8 +428,12 @@ def run_config4(args):
     tmean = np.mean(np.stack(times[1:]), axis=0)
     peak, peak_kind = measured_peaks()
     gm = kinds == 0
+    # attention reads every position's K and V rows once per layer (fp32, kv_dim
+    # 256): context of the profiled steps = prompt + W + K + about 2
+    kvd = 256
+    att_bytes_layer = sum((len(p) + W + K + 2) * kvd * 2 * 4 for p in my_prompts)
     parts = {"gemv": (float(nbytes[gm].sum()), float(tmean[gm].sum()), int(gm.sum())),
-             "attention": (float(nbytes[~gm].sum()), float(tmean[~gm].sum()), int((~gm).sum()))}
+             "attention": (float(att_bytes_layer * int((~gm).sum())), float(tmean[~gm].sum()), int((~gm).sum()))}
     dom = max(parts, key=lambda k: parts[k][1])
     db, dms, dn = parts[dom]
     if rank != 0:

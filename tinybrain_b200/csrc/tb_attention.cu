@@ -32,7 +32,10 @@ namespace {
 
 constexpr int kAttnConsumerWarps = 4;
 constexpr int kAttnThreads = (kAttnConsumerWarps + 1) * 32;
-constexpr int kAttnStages = 4;
+// K/V ring depth: 96 KB (d = 64) or 128 KB (d = 128) of pages in flight per
+// CTA, enough for one or two CTAs to keep an SM's share of HBM busy.
+__host__ __device__ constexpr int attn_stages(int d) { return d >= 128 ? 8 : 12; }
+constexpr int kAttnHead = 512;  // mbarriers + valid flags
 
 template <int G, int D>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
@@ -41,13 +44,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     constexpr int CHK = D / DP;                     // dims per score thread
     constexpr int PVT = G * (D / 4);                // threads active in the PV phase
     static_assert(DP >= 1 && CHK <= 64, "unsupported head geometry");
+    constexpr int kAttnStages = attn_stages(D);
+    static_assert(kAttnStages * 20 <= kAttnHead, "ring barriers exceed the header");
 
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kAttnStages;
     int* valid = reinterpret_cast<int*>(empty + kAttnStages);            // [stages]
-    float* S = reinterpret_cast<float*>(smem + 128);                    // [2][G][16]
-    float* tiles = reinterpret_cast<float*>(smem + 128 + ((2 * G * kPageTokens * 4 + 127) / 128) * 128);
+    float* S = reinterpret_cast<float*>(smem + kAttnHead);              // [2][G][16]
+    float* tiles = reinterpret_cast<float*>(smem + kAttnHead + ((2 * G * kPageTokens * 4 + 127) / 128) * 128);
     float* cpart = tiles + kAttnStages * 2 * TILE;  // [G][D + 4]: acc, m, l of this split
 
     const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
@@ -249,7 +254,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 
 template <int G, int D>
 size_t attn_smem() {
-    return 128 + ((2 * G * kPageTokens * 4 + 127) / 128) * 128 + (size_t)kAttnStages * 2 * kPageTokens * D * 4 +
+    return kAttnHead + ((2 * G * kPageTokens * 4 + 127) / 128) * 128 + (size_t)attn_stages(D) * 2 * kPageTokens * D * 4 +
            (size_t)G * (D + 4) * 4;
 }
 
@@ -258,6 +263,8 @@ cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t stream, bool pdl) {
     const size_t smem = attn_smem<G, D>();
     auto kfn = attn_decode_kernel<G, D>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)p.nsplit, (unsigned)p.Hkv, (unsigned)p.M);
