@@ -128,10 +128,13 @@ tb_status tb_matmul_quantized(tb_context *ctx, const float *x_host, int64_t M, c
 tb_status tb_matmul_quantized_dev(tb_context *ctx, const float *x_dev, int64_t M, const tb_qweight *w,
                                   float *y_dev);
 
-/* A timed stream of independent GEMVs y = x W_i (i = 0..n-1, shared K, device
- * x [M][K] and y [M][max N]): one CUDA graph launches each weight once with
- * programmatic dependent launch between consecutive kernels (pdl != 0), replayed
- * `reps` times after one warm-up replay; *ms_out = milliseconds per replay.
+/* A timed stream of GEMVs y = x W_i (i = 0..n-1, shared K, device x [M][K] and
+ * y [M][max N]): one CUDA graph launches each weight once, replayed `reps`
+ * times after one warm-up replay; *ms_out = milliseconds per replay.  pdl = 0:
+ * plain stream order; 1: programmatic dependent launch, each GEMV waits for
+ * the previous one to finish before reading x (a dependent chain, as inside a
+ * decode step); 2: the GEMVs are treated as independent (no wait), so their
+ * executions overlap the way independent projections can.
  * Measurement helper for the single-GEMV HBM benchmark (
  * cycle through more weight copies than fit in L2). */
 tb_status tb_qgemv_stream_time(tb_context *ctx, const tb_qweight *const *ws, int32_t n, const float *x_dev,

@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
                 const int g = i / nunits, u = i - g * nunits;
                 smaxs[g * nunits + u] = __ldg(p.scales + ((size_t)rb * kQ4Groups + g) * L.slabs + s0 + u);
             }
-        pdl_wait();
+        if (!p.independent) pdl_wait();
         if (ctid == 0) trace_max(p.trace, 2);
         if (p.epilogue == kEpiQkv && ctid < Mloc) {
             const SeqState& sq = p.seq_ro[m0 + ctid];

@@ -113,6 +113,7 @@ constexpr int kTracePoints = 16;
 
 struct GemvParams {
     unsigned long long* trace;
+    int independent;  // 1: reads nothing the preceding launch writes (skip the dependency wait)
     // weights (GPU layout)
     const uint8_t* w;
     const float* scales;

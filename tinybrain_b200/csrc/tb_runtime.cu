@@ -621,6 +621,7 @@ extern "C" tb_status tb_qgemv_stream_time(tb_context* ctx, const tb_qweight* con
         GemvParams p = plain_gemv(ctx, ws[i]->L, ws[i]->w.as<uint8_t>(), ws[i]->s.as<float>(), (int)M);
         p.src = x;
         p.out = y;
+        p.independent = pdl == 2 ? 1 : 0;  // independent GEMVs overlap their launches
         le = launch_gemv(p, st, pdl != 0 && i > 0);
     }
     cudaError_t ce = cudaStreamEndCapture(st, &g);

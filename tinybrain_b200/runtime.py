@@ -287,14 +287,16 @@ class QuantizedWeight:
 def gemv_stream_time(weights: Sequence["QuantizedWeight"], x_dev: int, M: int, y_dev: int, reps: int = 20,
                      pdl: bool = True) -> float:
     """Milliseconds per pass of one GEMV per weight (device pointers x [M][K],
-    y [M][max N]); the single-GEMV HBM measurement of BASELINE config 1."""
+    y [M][max N]); the single-GEMV HBM measurement of BASELINE config 1.
+    pdl: 0 / False stream order, 1 / True dependent chain, 2 independent
+    (overlapping) GEMVs."""
     if not weights:
         raise ValueError("no weights")
     ctx = weights[0].ctx
     arr = (C.c_void_p * len(weights))(*[w.handle for w in weights])
     ms = C.c_float(0.0)
     call("tb_qgemv_stream_time", ctx.handle, arr, len(weights), C.c_void_p(x_dev), M, C.c_void_p(y_dev), reps,
-         int(bool(pdl)), C.byref(ms))
+         int(pdl), C.byref(ms))
     return float(ms.value)
 
 
