@@ -122,11 +122,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         const int pair = t / DP, dp = t % DP;
         const int gq = pair / kPageTokens, j = pair % kPageTokens;
         const int head = kvh * G + gq;
+        // q slice rotated by 4j (token j's start offset) so the 16 rows of a
+        // page are read as conflict-spread float4s
+        constexpr bool kVec = CHK % 4 == 0;
+        const int rot = kVec ? (4 * j) % CHK : j % CHK;
         float qrot[CHK];
         {
             const float* qh = p.q + (size_t)m * p.ld_q + (size_t)head * D + dp * CHK;
 #pragma unroll
-            for (int e = 0; e < CHK; ++e) qrot[e] = qh[(e + j) % CHK];
+            for (int e = 0; e < CHK; ++e) qrot[e] = qh[(e + rot) % CHK];
         }
         // PV-phase role.
         const bool pv = t < PVT;
@@ -148,9 +152,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             {
                 float dot = 0.0f;
                 if (ok) {
+                    // four partial sums (independent FMA chains), added pairwise
                     const float* kr = Kt + j * D + dp * CHK;
+                    if constexpr (kVec) {
+                        float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
 #pragma unroll
-                    for (int e = 0; e < CHK; ++e) dot = fmaf(qrot[e], kr[(e + j) % CHK], dot);
+                        for (int e = 0; e < CHK; e += 4) {
+                            const float4 k4 = *reinterpret_cast<const float4*>(kr + (e + rot) % CHK);
+                            d0 = fmaf(qrot[e], k4.x, d0);
+                            d1 = fmaf(qrot[e + 1], k4.y, d1);
+                            d2 = fmaf(qrot[e + 2], k4.z, d2);
+                            d3 = fmaf(qrot[e + 3], k4.w, d3);
+                        }
+                        dot = (d0 + d1) + (d2 + d3);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < CHK; ++e) dot = fmaf(qrot[e], kr[(e + rot) % CHK], dot);
+                    }
                 }
 #pragma unroll
                 for (int o = DP / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
@@ -210,23 +228,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             const int item = i0 + t;
             const int g = item / (D / 4), d4 = (item % (D / 4)) * 4;
             float* out = p.out + (size_t)m * p.ld_out + (size_t)(kvh * G + g) * D + d4;
-            // every split's (m, l, acc) loaded first (one DSMEM round trip),
-            // then combined in split order
-            float mq[kMaxAttnSplits], lq[kMaxAttnSplits];
-            float4 aq[kMaxAttnSplits];
+            // every split's m first (one DSMEM round trip), then (l, acc) in
+            // groups of 8 splits, combined in split order
+            float mq[kMaxAttnSplits];
 #pragma unroll
-            for (int q = 0; q < kMaxAttnSplits; ++q) {
-                if (q < ns) {
-                    const uint32_t base = dsmem_map(cpart + g * (D + 4), (uint32_t)q);
-                    mq[q] = dsmem_ld_f32(base + D * 4);
-                    lq[q] = dsmem_ld_f32(base + (D + 1) * 4);
-                    aq[q] = dsmem_ld_f32x4(base + d4 * 4);
-                } else {
-                    mq[q] = -INFINITY;
-                    lq[q] = 0.0f;
-                    aq[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-            }
+            for (int q = 0; q < kMaxAttnSplits; ++q)
+                mq[q] = q < ns ? dsmem_ld_f32(dsmem_map(cpart + g * (D + 4) + D, (uint32_t)q)) : -INFINITY;
             float M = -INFINITY;
 #pragma unroll
             for (int q = 0; q < kMaxAttnSplits; ++q) M = fmaxf(M, mq[q]);
@@ -234,14 +241,33 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
             if (M != -INFINITY) {
 #pragma unroll
-                for (int q = 0; q < kMaxAttnSplits; ++q) {
-                    if (q >= ns) continue;
-                    const float w = (mq[q] == -INFINITY) ? 0.0f : expf(mq[q] - M);
-                    den = fmaf(w, lq[q], den);
-                    num.x = fmaf(w, aq[q].x, num.x);
-                    num.y = fmaf(w, aq[q].y, num.y);
-                    num.z = fmaf(w, aq[q].z, num.z);
-                    num.w = fmaf(w, aq[q].w, num.w);
+                for (int q0 = 0; q0 < kMaxAttnSplits; q0 += 8) {
+                    if (q0 >= ns) break;
+                    float lq[8];
+                    float4 aq[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int q = q0 + u;
+                        if (q < ns) {
+                            const uint32_t base = dsmem_map(cpart + g * (D + 4), (uint32_t)q);
+                            lq[u] = dsmem_ld_f32(base + (D + 1) * 4);
+                            aq[u] = dsmem_ld_f32x4(base + d4 * 4);
+                        } else {
+                            lq[u] = 0.0f;
+                            aq[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int q = q0 + u;
+                        if (q >= ns) continue;
+                        const float w = (mq[q] == -INFINITY) ? 0.0f : expf(mq[q] - M);
+                        den = fmaf(w, lq[u], den);
+                        num.x = fmaf(w, aq[u].x, num.x);
+                        num.y = fmaf(w, aq[u].y, num.y);
+                        num.z = fmaf(w, aq[u].z, num.z);
+                        num.w = fmaf(w, aq[u].w, num.w);
+                    }
                 }
             }
             const float il = den > 0.0f ? 1.0f / den : 0.0f;
@@ -266,6 +292,10 @@ cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t stream, bool pdl) {
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
+    if (p.nsplit > 8) {  // clusters of up to 16 CTAs are a non-portable size
+        e = cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)p.nsplit, (unsigned)p.Hkv, (unsigned)p.M);
     cfg.blockDim = dim3(kAttnThreads, 1, 1);
@@ -362,7 +392,7 @@ __global__ void rmsnorm_rows_kernel(const float* h, const float* w, int H, int l
 
 int choose_nsplit(int M, int Hkv, int max_pages, int num_sms) {
     // About one CTA per SM over the (sequence, KV head) pairs at the longest
-    // context, at least 8 pages per split there, at most one cluster (8) of splits.
+    // context, at least 8 pages per split there, at most one cluster (16) of splits.
     int pairs = M * Hkv;
     int ns = (num_sms + pairs - 1) / pairs;
     const int by_pages = (max_pages + 7) / 8;

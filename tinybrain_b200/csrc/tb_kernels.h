@@ -203,7 +203,7 @@ struct AttnParams {
     int* err;
 };
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
-constexpr int kMaxAttnSplits = 8;  // the splits of a (sequence, KV head) form one cluster
+constexpr int kMaxAttnSplits = 16;  // the splits of a (sequence, KV head) form one cluster
 int choose_nsplit(int M, int Hkv, int max_pages, int num_sms);
 
 // ----------------------------------------------------------------------------
