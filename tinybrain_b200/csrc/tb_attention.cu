@@ -51,8 +51,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kAttnStages;
     int* valid = reinterpret_cast<int*>(empty + kAttnStages);            // [stages]
-    float* S = reinterpret_cast<float*>(smem + kAttnHead);              // [2][G][16]
-    float* tiles = reinterpret_cast<float*>(smem + kAttnHead + ((2 * G * kPageTokens * 4 + 127) / 128) * 128);
+    float* S = reinterpret_cast<float*>(smem + kAttnHead);              // [2][G][16] scores / weights
+    float* Cb = S + 2 * G * kPageTokens;                                 // [2][G] running-max corrections
+    float* tiles = reinterpret_cast<float*>(smem + kAttnHead + (((2 * G * kPageTokens + 2 * G) * 4 + 127) / 128) * 128);
     float* cpart = tiles + kAttnStages * 2 * TILE;  // [G][D + 4]: acc, m, l of this split
 
     const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
@@ -125,6 +126,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         // q slice rotated by 4j (token j's start offset) so the 16 rows of a
         // page are read as conflict-spread float4s
         constexpr bool kVec = CHK % 4 == 0;
+        // softmax weights computed by the score threads (a head's 16 tokens
+        // within one warp) when G >= 4; otherwise by the PV threads
+        constexpr bool kSoftInScore = 16 * DP <= 32;
         const int rot = kVec ? (4 * j) % CHK : j % CHK;
         float qrot[CHK];
         {
@@ -173,10 +177,50 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 #pragma unroll
                 for (int o = DP / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
                 const int tok = (pg0 + i) * kPageTokens + j;
-                if (dp == 0) Sb[gq * kPageTokens + j] = (tok < Lq) ? __fmul_rn(dot, scale) : -INFINITY;
+                const float sc = (tok < Lq) ? __fmul_rn(dot, scale) : -INFINITY;
+                if constexpr (kSoftInScore) {
+                    // The 16 tokens of a head sit in 16 * DP consecutive lanes:
+                    // page max and the weights' sum by shuffles, the head's
+                    // running (m, l) in its first lane, one exp per token.
+                    float pm = sc;
+#pragma unroll
+                    for (int o = 8 * DP; o >= DP; o >>= 1) pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, o));
+                    const int leader = lane & ~(16 * DP - 1);
+                    const float mold = __shfl_sync(0xffffffffu, run_m, leader);
+                    const float mnew = fmaxf(mold, pm);
+                    const float corr = (mold == -INFINITY) ? 0.0f : expf(mold - mnew);
+                    const float e = (sc == -INFINITY) ? 0.0f : expf(sc - mnew);
+                    float ps = e;
+#pragma unroll
+                    for (int o = 8 * DP; o >= DP; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+                    if (lane == leader) {
+                        run_l = __fadd_rn(__fmul_rn(run_l, corr), ps);
+                        run_m = mnew;
+                        Cb[(i & 1) * G + gq] = corr;
+                    }
+                    if (dp == 0) Sb[gq * kPageTokens + j] = e;
+                } else {
+                    if (dp == 0) Sb[gq * kPageTokens + j] = sc;
+                }
             }
             named_bar_sync(1, 128);
-            if (pv) {
+            if (kSoftInScore && pv) {
+                const float* Sg = Sb + gv * kPageTokens;
+                const float corr = Cb[(i & 1) * G + gv];
+                float4 a = make_float4(acc.x * corr, acc.y * corr, acc.z * corr, acc.w * corr);
+                if (ok) {
+#pragma unroll
+                    for (int jj = 0; jj < kPageTokens; ++jj) {
+                        const float e = Sg[jj];
+                        const float4 v = *reinterpret_cast<const float4*>(Vt + jj * D + dv);
+                        a.x = fmaf(e, v.x, a.x);
+                        a.y = fmaf(e, v.y, a.y);
+                        a.z = fmaf(e, v.z, a.z);
+                        a.w = fmaf(e, v.w, a.w);
+                    }
+                }
+                acc = a;
+            } else if (pv) {
                 const float* Sg = Sb + gv * kPageTokens;
                 float pm = Sg[0];
 #pragma unroll
@@ -209,10 +253,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         if (pv) {
             float* cp = cpart + gv * (D + 4);
             *reinterpret_cast<float4*>(cp + dv) = acc;
-            if (dv == 0) {
+            if (!kSoftInScore && dv == 0) {
                 cp[D] = run_m;
                 cp[D + 1] = run_l;
             }
+        }
+        if (kSoftInScore && lane == (lane & ~(16 * DP - 1))) {  // head leaders hold (m, l)
+            float* cp = cpart + gq * (D + 4);
+            cp[D] = run_m;
+            cp[D + 1] = run_l;
         }
     }
     // Combine the splits (cluster ranks) in split order; CTA `split` produces
@@ -280,7 +329,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 
 template <int G, int D>
 size_t attn_smem() {
-    return kAttnHead + ((2 * G * kPageTokens * 4 + 127) / 128) * 128 + (size_t)attn_stages(D) * 2 * kPageTokens * D * 4 +
+    return kAttnHead + (((2 * G * kPageTokens + 2 * G) * 4 + 127) / 128) * 128 +
+           (size_t)attn_stages(D) * 2 * kPageTokens * D * 4 +
            (size_t)G * (D + 4) * 4;
 }
 
