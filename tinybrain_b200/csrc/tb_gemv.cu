@@ -77,14 +77,24 @@ constexpr int kGemvBarBytes = 512;  // mbarriers + tensor-memory address at the 
 __host__ __device__ constexpr int gemv_head_floats(int rb, int mb) { return rb * mb + 16 * mb + 2 * rb + 5 * mb; }
 __host__ __device__ constexpr int q4_dcols(int mb) { return q4_nb(mb) < 32 ? 32 : q4_nb(mb); }
 // INT4 CTAs add a tensor-core issue warp to the producer and 8 consumer warps.
-__host__ __device__ constexpr int gemv_threads(int prec) { return prec == 4 ? kGemvThreads + 32 : kGemvThreads; }
+// INT8 batches beyond 16 rows per CTA ("wide"): digits are built per unit
+// (B slots) instead of once for the CTA's k range.
+__host__ __device__ constexpr bool gemv_wide(int prec, int mb) { return prec == 8 && mb > 16; }
+constexpr int kWideSlots = 2;
+// wide B slots: 8-row core matrices 144 B apart (128 + 16 pad: conflict-free
+// digit stores), 16-k chunks NB / 8 core matrices apart
+constexpr uint32_t kWideSbo = 144;
+__host__ __device__ constexpr uint32_t wide_lbo(int nb) { return (uint32_t)(nb / 8) * kWideSbo; }
+__host__ __device__ constexpr int gemv_threads(int prec, int mb) {
+    return (prec == 4 || gemv_wide(prec, mb)) ? kGemvThreads + 32 : kGemvThreads;
+}
 // At most 256 columns: two CTAs of any GEMV variant fit one SM's 512 together,
 // so a CTA never waits in tcgen05.alloc for another one to finish.
 __host__ __device__ constexpr int q4_tmem_cols(int mb) { return 256; }
 // Batch rows handled by one CTA.
 inline int gemv_mb(int prec, int M) {
-    const int cap = prec == 8 ? 16 : 4;  // INT4: A slots + two accumulators fit 256 TMEM columns
-    const int mb = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16;
+    const int cap = prec == 8 ? 64 : 4;  // INT4: A slots + accumulator fit 256 TMEM columns
+    const int mb = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : M <= 16 ? 16 : 64;
     return std::min(mb, cap);
 }
 
@@ -101,7 +111,7 @@ __device__ __forceinline__ float gelu_ref(float x) {
 }
 
 template <int PREC, int RB, int MB>
-__global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const __grid_constant__ GemvParams p) {
     using Cfg = GemvCfg<PREC, RB>;
     static_assert(RB == kTcTileRows, "tensor-core tiles are 128 rows");
     constexpr int STAGES = Cfg::kStages;
@@ -149,8 +159,11 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
     //   [kQ4Slots][NB * 128], per-unit max |x| [nunits][MB], per-unit max
     //   |scale| [4][nunits], digit exponents [MB][4].
     const int kspan = ((L.slabs + P - 1) / P) * kTcUnitK;
-    float* xs = reinterpret_cast<float*>(PREC == 8 ? xbuf + (size_t)kspan * NB : xbuf);
-    float* wstage = xs + (size_t)MB * kspan;
+    constexpr bool WIDE = gemv_wide(PREC, MB);
+    // wide INT8: B slots [kWideSlots][NB * 128] at xbuf, norm weights after them, no x staging
+    float* xs = reinterpret_cast<float*>(
+        PREC == 8 ? xbuf + (WIDE ? (size_t)kWideSlots * wide_lbo(NB) * 8 : (size_t)kspan * NB) : xbuf);
+    float* wstage = WIDE ? xs : xs + (size_t)MB * kspan;
     uint8_t* bslots = reinterpret_cast<uint8_t*>(wstage + kspan);
     float* xmax = reinterpret_cast<float*>(bslots + kQ4Slots * NB * 128);
     float* smaxs = xmax + (size_t)(kspan / kTcUnitK) * MB;
@@ -168,7 +181,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
         mbar_init(&done[1], 1);
         for (int i = 0; i < kQ4Slots; ++i) {
             mbar_init(&a_ready[i], 4);
-            mbar_init(&b_ready[i], 4);
+            mbar_init(&b_ready[i], WIDE ? kGemvConsumerWarps : 4);
             mbar_init(&s_free[i], 1);
         }
         fence_barrier_init();
@@ -179,7 +192,30 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
     tc_fence_after();
     pdl_launch_dependents();
 
-    if (PREC == 4 && warp == kGemvConsumerWarps + 1) {
+    if (WIDE && warp == kGemvConsumerWarps + 1) {
+        // --------------------- wide INT8: tensor-core issue ---------------------
+        if (lane == 0) {
+            const uint32_t tmem = *tmem_slot;
+            for (int i = 0; i < nunits; ++i) {
+                const int st = i % STAGES;
+                const int sl = i % kWideSlots;
+                if (!mbar_wait(&full[st], (i / STAGES) & 1, p.err)) break;
+                if (!mbar_wait(&b_ready[sl], (uint32_t)(i / kWideSlots) & 1u, p.err)) break;
+                tc_fence_after();
+                const uint32_t a_s = smem_u32(stage_base + st * Cfg::kStageBytes);
+                const uint32_t b_s = smem_u32(xbuf + (size_t)sl * wide_lbo(NB) * 8);
+                const uint32_t idesc = tc_idesc_i8(NB);
+#pragma unroll
+                for (int s = 0; s < kTcUnitK / 32; ++s)
+                    tc_mma_i8(tmem, tc_sdesc(a_s + s * 256, 128, 1024),
+                              tc_sdesc(b_s + s * 2 * wide_lbo(NB), wide_lbo(NB), kWideSbo), idesc, i > 0 || s > 0);
+                tc_commit(&empty[st]);
+                tc_commit(&s_free[sl]);
+            }
+            tc_commit(&done[0]);
+        }
+        __syncwarp();
+    } else if (PREC == 4 && warp == kGemvConsumerWarps + 1) {
         // ------------------------- INT4 tensor-core issue -------------------------
         if (lane == 0) {
             const uint32_t tmem = *tmem_slot;
@@ -316,7 +352,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
                         a.z = k + 2 < L.K ? sr[k + 2] : 0.0f;
                         a.w = k + 3 < L.K ? sr[k + 3] : 0.0f;
                     }
-                    *reinterpret_cast<float4*>(xr + 4 * g) = a;
+                    if (!WIDE) *reinterpret_cast<float4*>(xr + 4 * g) = a;
                     if (PREC == 8) {
                         if (rms) {
                             const float4 w = *reinterpret_cast<const float4*>(wstage + 4 * g);
@@ -326,7 +362,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
                         mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
                     }
                 }
-            } else {
+            } else if (!WIDE) {
                 for (int g = sw * 32 + lane; g < kq; g += 32 * WPR)
                     *reinterpret_cast<float4*>(xr + 4 * g) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
@@ -367,7 +403,85 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
             return a;
         };
 
-        if constexpr (PREC == 8) {
+        if constexpr (WIDE) {
+            // ---- wide INT8: digits of each unit's 128 k for all rows, per B slot ----
+            // warp w: batch rows 8w + lane / 4; lane % 4 picks the 4-k word of
+            // each 16-k chunk (8 chunks per unit); x read from global, the next
+            // unit's values prefetched while this unit's digits are written
+            static_assert(MB == 64, "wide batches are 64 rows per CTA");
+            const int m = 8 * warp + (lane >> 2);
+            const int kw = lane & 3;
+            float4 xv[8];
+            const float* sr = m < Mloc ? srcrow(m) : nullptr;
+            auto load_unit = [&](int i) {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const int k = kbeg + i * kTcUnitK + 16 * c + 4 * kw;
+                    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (sr) {
+                        if (v4 && k + 3 < L.K) {
+                            a = *reinterpret_cast<const float4*>(sr + k);
+                        } else {
+                            a.x = k < L.K ? sr[k] : 0.0f;
+                            a.y = k + 1 < L.K ? sr[k + 1] : 0.0f;
+                            a.z = k + 2 < L.K ? sr[k + 2] : 0.0f;
+                            a.w = k + 3 < L.K ? sr[k + 3] : 0.0f;
+                        }
+                    }
+                    xv[c] = a;
+                }
+            };
+            const float iv = rowinv[m];
+            const float dscale = __int_as_float((127 - rowex[m]) << 23);
+            if (nunits > 0) load_unit(0);
+            for (int i = 0; i < nunits; ++i) {
+                const int sl = i % kWideSlots;
+                int ok = 1;
+                if (lane == 0 && i >= kWideSlots)
+                    ok = mbar_wait(&s_free[sl], (uint32_t)((i / kWideSlots) - 1) & 1u, p.err) ? 1 : 0;
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                float4 cur[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) cur[c] = xv[c];
+                if (i + 1 < nunits) load_unit(i + 1);
+                uint8_t* bs = xbuf + (size_t)sl * wide_lbo(NB) * 8;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    float4 a = cur[c];
+                    if (rms) {
+                        const float4 w = *reinterpret_cast<const float4*>(wstage + i * kTcUnitK + 16 * c + 4 * kw);
+                        a = make_float4(__fmul_rn(__fmul_rn(a.x, iv), w.x), __fmul_rn(__fmul_rn(a.y, iv), w.y),
+                                        __fmul_rn(__fmul_rn(a.z, iv), w.z), __fmul_rn(__fmul_rn(a.w, iv), w.w));
+                    }
+                    put_digits4_strided(bs, wide_lbo(NB), kWideSbo, 16 * c + 4 * kw, m, a, dscale);
+                }
+                fence_proxy_async_shared();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&b_ready[sl]);
+            }
+            if (ctid == 0) trace_max(p.trace, 3);
+            // epilogue: warps 0-3 read the accumulator, 32 columns (8 rows) at a time
+            if (warp < 4) {
+                const uint32_t tmem = *tmem_slot;
+                const bool okd = mbar_wait(&done[0], 0, p.err);
+                if (lane == 0) trace_max(p.trace, 4);
+                tc_fence_after();
+                const int row = 32 * warp + lane;
+#pragma unroll 1
+                for (int c = 0; c < NB / 32; ++c) {
+                    int d[32];
+                    tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(32 * c), d);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int m = 8 * c + u;
+                        red[row * MB + m] = okd ? combine_digits(d + kTcDigits * u, rowex[m]) : 0.0f;
+                    }
+                }
+                tc_fence_before();
+            }
+        } else if constexpr (PREC == 8) {
             // Digits of x[m][kbeg:kend) into the B operand, 4 consecutive k per thread.
             const int ngroups = (kend - kbeg) / 4;
             for (int g = ctid; g < ngroups; g += 256) {
@@ -600,21 +714,24 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
             if (p.bias) v = __fadd_rn(v, rowbias[i]);
             return v;
         };
-        unsigned long long best_local[MB];
-#pragma unroll
-        for (int m = 0; m < MB; ++m) best_local[m] = 0ull;
+        // Items it = ctid + 256 j map to batch row it % MB = ctid % MB (MB
+        // divides 256): one argmax key per thread.
+        static_assert(256 % MB == 0, "batch rows per CTA divide the consumer threads");
+        unsigned long long best_mine = 0ull;
 
-        // Two phases so that every global load of a thread's items is in flight
-        // together: (1) reduce, scale, issue the loads the stores need (RoPE
-        // table, the residual); (2) finish and store.
+        // Two phases per chunk of JC items, so that every global load of a
+        // chunk is in flight together: (1) reduce, scale, issue the loads the
+        // stores need (RoPE table, the residual); (2) finish and store.
         constexpr int JMAX = (RB * MB + 255) / 256;
-        float va[JMAX], vb[JMAX], old[JMAX];
-        float2 cs[JMAX];
+        constexpr int JC = JMAX < 4 ? JMAX : 4;
+        for (int jb = 0; jb < JMAX; jb += JC) {
+        float va[JC], vb[JC], old[JC];
+        float2 cs[JC];
 #pragma unroll
-        for (int j = 0; j < JMAX; ++j) {
+        for (int j = 0; j < JC; ++j) {
             va[j] = vb[j] = old[j] = 0.0f;
             cs[j] = make_float2(1.0f, 0.0f);
-            const int it = ctid + 256 * j;
+            const int it = ctid + 256 * (jb + j);
             if (it >= nitems) continue;
             const int m = it % MB;
             const int o = ob + it / MB;
@@ -641,8 +758,8 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
             }
         }
 #pragma unroll
-        for (int j = 0; j < JMAX; ++j) {
-            const int it = ctid + 256 * j;
+        for (int j = 0; j < JC; ++j) {
+            const int it = ctid + 256 * (jb + j);
             if (it >= nitems) continue;
             const int m = it % MB;
             const int o = ob + it / MB;
@@ -705,23 +822,21 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
                 } else {  // kEpiArgmax
                     if (p.logits) p.logits[(size_t)gm * L.N + n] = v;
                     const unsigned long long key = argmax_key(v, n);
-#pragma unroll
-                    for (int mm = 0; mm < MB; ++mm)
-                        if (mm == m && key > best_local[mm]) best_local[mm] = key;
+                    if (key > best_mine) best_mine = key;
                 }
             }
         }
+        }  // item chunks
         if (p.epilogue == kEpiArgmax) {
+            // lanes with the same batch row (lane % MB) combine, then one atomic per row and warp
+            unsigned long long b = best_mine;
 #pragma unroll
-            for (int m = 0; m < MB; ++m) {
-                unsigned long long b = best_local[m];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
-                    b = t > b ? t : b;
-                }
-                if (lane == 0 && b != 0ull && m < Mloc) atomicMax(&p.seq[m0 + m].best, b);
+            for (int o = 16; o >= MB; o >>= 1) {
+                unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+                b = t > b ? t : b;
             }
+            const int m = ctid % MB;
+            if (lane < MB && b != 0ull && m < Mloc) atomicMax(&p.seq[m0 + m].best, b);
             named_bar_sync(1, 256);
             if (ctid == 0) {
                 __threadfence();
@@ -754,6 +869,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC), 2) gemv_kernel(const __gri
 inline size_t gemv_xbytes(int prec, int mb, const QLayout& L, int P) {
     const size_t units = (size_t)((L.slabs + P - 1) / P);
     const size_t xw = units * kTcUnitK * (mb + 1) * 4;  // x and norm weights, fp32
+    if (gemv_wide(prec, mb)) return (size_t)kWideSlots * wide_lbo(tc_nb(mb)) * 8 + units * kTcUnitK * 4;
     if (prec == 8) return units * kTcUnitK * (size_t)tc_nb(mb) + xw;
     return xw + (size_t)kQ4Slots * q4_nb(mb) * 128 + units * (mb + kQ4Groups) * 4 + (size_t)mb * kQ4Groups * 4;
 }
@@ -778,7 +894,7 @@ cudaError_t launch_t(const GemvParams& p, cudaStream_t stream, bool pdl) {
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)(p.L.Np / RB * p.P), (unsigned)((p.M + MB - 1) / MB), 1);
-    cfg.blockDim = dim3(gemv_threads(PREC), 1, 1);
+    cfg.blockDim = dim3(gemv_threads(PREC, MB), 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attrs[2];
@@ -821,7 +937,7 @@ int choose_ksplit(const QLayout& L, int M, int num_sms) {
     // unit, measured; the SM's share of HBM bandwidth, ~44 KB/us, for the
     // units of all CTAs on that SM).
     constexpr double kWaveUs = 4.0, kSmKBperUs = 44.0;
-    const double unit_us = L.precision == 8 ? 0.15 : 0.42;
+    const double unit_us = gemv_wide(L.precision, mb) ? 0.5 : L.precision == 8 ? 0.15 : 0.42;
     const double unit_kb = (L.precision == 8 ? kTcUnitBytes : kQ4UnitBytes) / 1024.0;
     int best = 0;
     double best_cost = 0.0;
@@ -856,7 +972,8 @@ cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream, bool pdl) {
             case 2: return launch_t<8, 128, 2>(p, stream, pdl);
             case 4: return launch_t<8, 128, 4>(p, stream, pdl);
             case 8: return launch_t<8, 128, 8>(p, stream, pdl);
-            default: return launch_t<8, 128, 16>(p, stream, pdl);
+            case 16: return launch_t<8, 128, 16>(p, stream, pdl);
+            default: return launch_t<8, 128, 64>(p, stream, pdl);
         }
     }
     if (prec == 4) {

@@ -142,6 +142,16 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&v)[8]) {
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
                  : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld4(uint32_t taddr, int (&v)[4]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
@@ -178,6 +188,32 @@ __device__ __forceinline__ void put_digits4(uint8_t* xd, int nb, int k0_rel, int
         const uint32_t hi = prmt(__float_as_uint(t23.x), __float_as_uint(t23.y), 0x0040u);
         const int row = m * kTcDigits + j;
         *reinterpret_cast<uint32_t*>(base + ((row >> 3) * 128) + (row & 7) * 16) = prmt(lo, hi, 0x5410u);
+        if (j + 1 < kTcDigits) {
+            const float2 n01 = __ffma2_rn(t01, make_float2(-128.0f, -128.0f), make_float2(128.0f * kM, 128.0f * kM));
+            const float2 n23 = __ffma2_rn(t23, make_float2(-128.0f, -128.0f), make_float2(128.0f * kM, 128.0f * kM));
+            u01 = __ffma2_rn(u01, make_float2(128.0f, 128.0f), n01);
+            u23 = __ffma2_rn(u23, make_float2(128.0f, 128.0f), n23);
+        }
+    }
+}
+// put_digits4 into a B operand with explicit strides: `lbo` bytes between
+// 16-k chunks, `sbo` between 8-row core matrices (a padded sbo spreads the
+// stores of a warp over all banks).
+__device__ __forceinline__ void put_digits4_strided(uint8_t* xd, uint32_t lbo, uint32_t sbo, int k0_rel, int m,
+                                                    float4 v, float inv_scale) {
+    constexpr float kM = 12582912.0f;  // 1.5 * 2^23
+    const float2 sc = make_float2(inv_scale, inv_scale);
+    float2 u01 = __fmul2_rn(make_float2(v.x, v.y), sc);
+    float2 u23 = __fmul2_rn(make_float2(v.z, v.w), sc);
+    uint8_t* base = xd + (size_t)(k0_rel >> 4) * lbo + (k0_rel & 15);
+#pragma unroll
+    for (int j = 0; j < kTcDigits; ++j) {
+        const float2 t01 = __fadd2_rn(u01, make_float2(kM, kM));
+        const float2 t23 = __fadd2_rn(u23, make_float2(kM, kM));
+        const uint32_t lo = prmt(__float_as_uint(t01.x), __float_as_uint(t01.y), 0x0040u);
+        const uint32_t hi = prmt(__float_as_uint(t23.x), __float_as_uint(t23.y), 0x0040u);
+        const int row = m * kTcDigits + j;
+        *reinterpret_cast<uint32_t*>(base + (row >> 3) * sbo + (row & 7) * 16) = prmt(lo, hi, 0x5410u);
         if (j + 1 < kTcDigits) {
             const float2 n01 = __ffma2_rn(t01, make_float2(-128.0f, -128.0f), make_float2(128.0f * kM, 128.0f * kM));
             const float2 n23 = __ffma2_rn(t23, make_float2(-128.0f, -128.0f), make_float2(128.0f * kM, 128.0f * kM));
