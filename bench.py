@@ -460,7 +460,7 @@ def run_config4(args):
         "roofline": {"bound": "hbm", "achieved": db / (dms / 1000.0) / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": db / (dms / 1000.0) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs (burst copy)",
                      "kernel": "attn_decode_kernel (paged KV, all layers)" if dom == "attention" else
-                               "gemv_kernel<8,128,16> (all projections + LM head)",
+                               "gemv_kernel<8,128,64> (all projections + LM head, one CTA per 64-row batch)",
                      "bytes_per_launch": db / dn, "launches_per_step": dn, "ms_per_launch": dms / dn,
                      "traffic": None,
                      "gemv_ms_per_step": parts["gemv"][1], "attention_ms_per_step": parts["attention"][1]},

@@ -32,16 +32,12 @@ enum DeviceError : int {
 // a multiple of 128 with zero weights.  The fused gate/up matrix puts 64 gate
 // rows and the matching 64 up rows in each tile.
 //
-// INT4 (CUDA-core path, tb_unit.cuh): row blocks of RB = 32 rows (or 64 for the
-// fused gate/up matrix: 32 gate + 32 up rows), the reduction dimension cut in
-// slabs of 512 bytes per row (1024 int4 values; the last slab may be shorter);
-// unit = 32 rows x slab bytes, row-major.  Values stored biased (q + 8) two per
-// byte, low nibble = even k.  Group scales for the 32 rows of a group and the k
-// range of a slab are stored next to each other per unit, in the
-// lane-interleaved order the kernel reads them ([group][chunk c][lane][4
-// floats] for k = 32*lane + 4*c + i).
+// INT4 (tensor-core path, tb_tc.cuh): the same 128-row tiles and 128-k units,
+// 10 KB each: 8 KB of biased nibbles [4 k-chunks of 32][128 rows][16 bytes]
+// (word j of a chunk: byte i = k 8j+i low, k 8j+i+4 high), then the unit's
+// group scales [4 row groups of 32][128 k] fp32.  The scale buffer holds the
+// largest |scale| per (32-row group, unit).
 // ----------------------------------------------------------------------------
-constexpr int kSlabBytes = 512;
 constexpr int kGemvConsumerWarps = 8;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;  // + 1 producer warp
 constexpr int kMaxGemvBatch = 64;  // batch rows of one GEMV launch (grid y splits rows beyond a CTA's)
@@ -49,17 +45,17 @@ constexpr int kMaxGemvBatch = 64;  // batch rows of one GEMV launch (grid y spli
 struct QLayout {
     int precision;       // 8 or 4
     int K;               // logical reduction length
-    int Kp;              // K padded (INT8: multiple of 128, INT4: multiple of 32)
+    int Kp;              // K padded to a multiple of 128
     int N;               // logical output rows
     int Np;              // N padded to a multiple of RB
-    int RB;              // rows per row block (INT8: 128; INT4: 32, or 64 for gate/up)
+    int RB;              // rows per row block (128)
     int slabs;           // units along K per row block
-    int slab_k;          // k values per full unit (INT8 128, INT4 1024)
-    int slab_bytes;      // bytes per row of a full unit (INT8 128, INT4 512)
+    int slab_k;          // k values per unit (128)
+    int slab_bytes;      // bytes per row of a unit (INT8 128, INT4 64)
     int row_bytes;       // bytes per row (Kp or Kp/2)
     int fused_gu;        // 1: gate/up interleaved by half row blocks
-    size_t weight_bytes; // Np * row_bytes
-    size_t scale_floats; // INT8: Np ; INT4: (Np/32) * Kp
+    size_t weight_bytes; // INT8: Np * row_bytes; INT4: tiles * slabs * 10 KB (scales inline)
+    size_t scale_floats; // INT8: Np row scales; INT4: (Np/32) * slabs maxima
 };
 
 // GPU row of logical row n of a matrix placed at (row_offset, interleave) in a

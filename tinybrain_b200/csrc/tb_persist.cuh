@@ -39,8 +39,8 @@ __device__ __forceinline__ int att_floats(int G, int d, int Hkv, int A) {
     return max(G * d + 2 * d + 2 * G * kPageTokens, Hkv * G * A);
 }
 
-// Rows per streamed unit: INT8 128-row tiles, INT4 32-row units.
-__host__ __device__ constexpr int unit_rows(int prec) { return prec == 8 ? kTcTileRows : 32; }
+// Rows per streamed unit (128-row tiles).
+__host__ __device__ constexpr int unit_rows(int) { return kTcTileRows; }
 __host__ __device__ inline int phase_units(const QLayout& L) { return (L.Np / unit_rows(L.precision)) * L.slabs; }
 // Segment table bytes of a phase: [rb][kMaxTileSegs] unit indices + [rb] counts (16-byte rounded).
 __host__ __device__ inline int seg_table_bytes(const QLayout& L) {
@@ -109,43 +109,19 @@ struct Producer {
         cur.next(p.nslots);
     }
 
-    // Units [u0, u1) of a GEMV phase (row-block major, unit minor; an INT4
-    // 64-row gate/up block is two 32-row units).
+    // Units [u0, u1) of a GEMV phase: consecutive 16 KB INT8 tiles-units in memory.
     template <int PREC>
     __device__ void gemv(const QLayout& L, const uint8_t* w, const float* sc, int u0, int u1) {
-        if (u1 <= u0) return;
-        if (PREC == 8) {
-            // INT8 units are consecutive 16 KB blocks in memory.
-            for (int u = u0; u < u1 && !dead; ++u) {
-                int st;
-                uint8_t* dst = acquire(st);
-                if (!dst) return;
-                mbar_arrive_expect_tx(&sh.full[st], kTcUnitBytes);
-                bulk_g2s_stream(dst, w + (size_t)u * kTcUnitBytes, kTcUnitBytes, &sh.full[st], pol);
-                issued();
-            }
-            return;
-        }
-        const int hshift = L.RB == 64 ? 1 : 0;
-        int rb32 = u0 / L.slabs, s = u0 - rb32 * L.slabs;
+        static_assert(PREC == 8, "the persistent step streams INT8 units");
+        (void)L;
+        (void)sc;
         for (int u = u0; u < u1 && !dead; ++u) {
-            const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-            const int rbb = rb32 >> hshift, half = rb32 & hshift;
-            const uint8_t* src =
-                w + (size_t)rbb * L.RB * L.row_bytes + (size_t)s * L.RB * kSlabBytes + (size_t)half * 32 * sb;
             int st;
             uint8_t* dst = acquire(st);
             if (!dst) return;
-            const uint32_t wb = 32u * sb;
-            mbar_arrive_expect_tx(&sh.full[st], wb + 4096u);
-            bulk_g2s_stream(dst, src, wb, &sh.full[st], pol);
-            bulk_g2s_stream(dst + 16384, sc + (((size_t)rbb * L.slabs + s) * (L.RB / 32) + half) * 1024, 4096u,
-                            &sh.full[st], pol);
+            mbar_arrive_expect_tx(&sh.full[st], kTcUnitBytes);
+            bulk_g2s_stream(dst, w + (size_t)u * kTcUnitBytes, kTcUnitBytes, &sh.full[st], pol);
             issued();
-            if (++s == L.slabs) {
-                s = 0;
-                ++rb32;
-            }
         }
     }
 

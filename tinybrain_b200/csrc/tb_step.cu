@@ -241,24 +241,11 @@ struct Consumer {
         }
     }
 
-    // INT4: fp32 activation, lane-interleaved per slab, nibble-position scaled.
-    __device__ void put_x4(int k, float v) {
-        constexpr int SK = 2 * kSlabBytes;  // == L.slab_k
-        v *= int4_pos_scale(k & 7);
-        const int s = k / SK;
-        sh.xs[s * SK + xperm<32>(k - s * SK)] = v;
-    }
     // Four consecutive activations (k % 4 == 0) into the phase's operand.
     template <int PREC>
     __device__ __forceinline__ void put_x_group(int k, float4 v) {
-        if (PREC == 8) {
-            put_digits4(reinterpret_cast<uint8_t*>(sh.xs), 8, k, 0, v, __int_as_float((127 - xexp) << 23));
-        } else {
-            put_x4(k + 0, v.x);
-            put_x4(k + 1, v.y);
-            put_x4(k + 2, v.z);
-            put_x4(k + 3, v.w);
-        }
+        static_assert(PREC == 8, "the persistent step runs INT8 weights");
+        put_digits4(reinterpret_cast<uint8_t*>(sh.xs), 8, k, 0, v, __int_as_float((127 - xexp) << 23));
     }
     // Zero activations for k in [k0, Kp) (multiple-of-4 bounds).
     template <int PREC>
@@ -455,67 +442,10 @@ struct Consumer {
         rc.advance(u1 - u0, p.nslots);
     }
 
-    // INT4: 32-row units on the CUDA cores; each warp owns 4 rows of a unit.
-    __device__ void gemv_cc(const QLayout& L, float* part, const float* bias) {
-        trace(cur_phase, 2);
-        const int U = phase_units(L);
-        const int u0 = (int)((long long)c * U / C), u1 = (int)((long long)(c + 1) * U / C);
-        float2 acc[4][1];
-        int cur = -1, s_first = 0;
-        auto flush = [&](int rb32, int slab) {
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                float v = acc[r][0].x + acc[r][0].y;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                const int n = rb32 * 32 + warp * 4 + r;
-                if (lane == r) {
-                    if (bias && slab == 0) v = __fadd_rn(v, __ldg(bias + n));
-                    part[(size_t)slab * L.Np + n] = v;
-                }
-                acc[r][0] = make_float2(0.f, 0.f);
-            }
-        };
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r][0] = make_float2(0.f, 0.f);
-        const long long loop_c0 = (p.trace && ctid == 0) ? clock64() : 0;
-        const uint64_t loop_t0 = (p.trace && ctid == 0) ? global_timer_ns() : 0;
-        int rb32 = u0 / L.slabs, s = u0 - (u0 / L.slabs) * L.slabs;
-        for (int u = u0; u < u1; ++u, (++s == L.slabs ? (s = 0, ++rb32) : 0)) {
-            if (rb32 != cur) {
-                if (cur >= 0) flush(cur, s_first);
-                cur = rb32;
-                s_first = s;
-            }
-            int st;
-            const uint8_t* slot = wait_slot(st);
-            if (slot) {
-                const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-                const float* ssl = reinterpret_cast<const float*>(slot + 16384);
-                const long long td = (p.trace && ctid == 0) ? clock64() : 0;
-                unit_dot<4, 4, 1>(slot, sb, warp * 4, ssl, sh.xs + s * L.slab_k, 0, lane, acc);
-                if (p.trace && ctid == 0) {
-                    volatile float sink = acc[0][0].x + acc[1][0].x + acc[2][0].x + acc[3][0].x;
-                    (void)sink;
-                    dotted += clock64() - td;
-                }
-            }
-            release_slot(st, slot != nullptr);
-        }
-        if (p.trace && ctid == 0) {
-            unsigned long long* t = p.trace + ((size_t)c * nph + cur_phase) * 8;
-            t[6] = clock64() - loop_c0;
-            t[7] = global_timer_ns() - loop_t0;
-        }
-        if (cur >= 0) flush(cur, s_first);
-    }
-
     template <int PREC>
     __device__ void gemv_units(const QLayout& L, float* part, const float* sc, const float* bias) {
-        if (PREC == 8)
-            gemv_tc(L, part, sc, bias);
-        else
-            gemv_cc(L, part, bias);
+        static_assert(PREC == 8, "the persistent step runs INT8 weights");
+        gemv_tc(L, part, sc, bias);
     }
 
     // ---------------------------------------------------------------- attention
@@ -811,12 +741,8 @@ struct Consumer {
                 const float4 a = ok ? make_float4(__fmul_rn(silu_ref(g.x), u.x), __fmul_rn(silu_ref(g.y), u.y),
                                                   __fmul_rn(silu_ref(g.z), u.z), __fmul_rn(silu_ref(g.w), u.w))
                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-                if (PREC == 8) {
-                    *reinterpret_cast<float4*>(sh.hs + e0 + 4 * (ctid + kConsumers * j)) = a;
-                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
-                } else {
-                    put_x_group<PREC>(kk[j], a);
-                }
+                *reinterpret_cast<float4*>(sh.hs + e0 + 4 * (ctid + kConsumers * j)) = a;
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
             }
         }
         if (PREC == 8) {
@@ -906,54 +832,10 @@ struct Consumer {
         rc.advance((t1 - t0) * L.slabs, p.nslots);
     }
 
-    __device__ void lm_head_cc(unsigned long long* best_out) {
-        const QLayout& L = p.Llm;
-        const int nrb = L.Np / 32;
-        const int r0 = (int)((long long)c * nrb / C), r1 = (int)((long long)(c + 1) * nrb / C);
-        unsigned long long best = 0ull;
-        for (int rb = r0; rb < r1; ++rb) {
-            float2 acc[4][1];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) acc[r][0] = make_float2(0.f, 0.f);
-            for (int s = 0; s < L.slabs; ++s) {
-                int st;
-                const uint8_t* slot = wait_slot(st);
-                if (slot) {
-                    const int sb = min(kSlabBytes, L.row_bytes - s * kSlabBytes);
-                    const float* ssl = reinterpret_cast<const float*>(slot + 16384);
-                    unit_dot<4, 4, 1>(slot, sb, warp * 4, ssl, sh.xs + s * L.slab_k, 0, lane, acc);
-                }
-                release_slot(st, slot != nullptr);
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                float v = acc[r][0].x + acc[r][0].y;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                const int n = rb * 32 + warp * 4 + r;
-                if (lane == r && n < L.N && !*sh.abort) {
-                    float lv = v;
-                    if (p.lm_b) lv = __fadd_rn(lv, p.lm_b[n]);
-                    if (p.logits) p.logits[n] = lv;
-                    const unsigned long long key = argmax_key(lv, n);
-                    best = key > best ? key : best;
-                }
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
-            best = t > best ? t : best;
-        }
-        if (lane == 0 && best != 0ull) atomicMax(best_out, best);
-    }
-
     template <int PREC>
     __device__ void lm_head(unsigned long long* best_out) {
-        if (PREC == 8)
-            lm_head_tc(best_out);
-        else
-            lm_head_cc(best_out);
+        static_assert(PREC == 8, "the persistent step runs INT8 weights");
+        lm_head_tc(best_out);
     }
 };
 
@@ -1165,7 +1047,7 @@ size_t step_smem_bytes(const StepParams& p, int grid, int* nslots, int* slot_byt
             if (max_segments(*Ls[i], grid, false) > kMaxSegs) return 0;
         if (max_segments(p.Llm, grid, true) > kMaxSegs) return 0;
     }
-    const int slot = prec == 4 ? 16384 + 4096 : kTcUnitBytes;
+    const int slot = kTcUnitBytes;
     const int att_tile = 2 * kPageTokens * p.d * 4;
     const int sbytes = std::max(slot, att_tile);
     int kmax = 0;
