@@ -504,6 +504,12 @@ def run_config5(args):
                                shard=(rank, world) if world > 1 else None)
     dm = weights.upload(ctx, tp=(rank, world))
     runner = ModelRunner(dm, ctx, max_batch=1, max_positions=cfg.max_seq_len + 64)
+    peer = world > 1 and os.environ.get("TB_TP_ALLREDUCE", "peer") != "nccl"
+    if peer:  # the residual all-reduce through NVLink peer memory instead of NCCL
+        hs = [None] * world
+        dist.all_gather_object(hs, runner.tp_handle())
+        runner.tp_connect(hs)
+        dist.barrier()
     build_s = time.perf_counter() - t_build
     prompt = random_prompt(n_prompt, 32000, 5)
     W = args.warmup
@@ -575,8 +581,9 @@ def run_config5(args):
         "config": {"workload": "Llama-2-7B-shaped INT4-g32, batch 1, prompt 512, greedy decode (BASELINE config 5)",
                    "layers": 32, "hidden": 4096, "heads": "32 MHA", "intermediate": 11008, "vocab": 32000,
                    "prompt": len(prompt), "decode_tokens": total_new,
-                   "parallelism": f"tp{world} (column q/k/v, gate/up; row o_proj/down + NCCL all-reduce; "
-                                  "LM head replicated)",
+                   "parallelism": f"tp{world} (column q/k/v, gate/up; row o_proj/down + residual all-reduce "
+                                  + ("through NVLink peer memory fused into the GEMV launches" if peer else "by NCCL")
+                                  + "; LM head replicated)",
                    "prefill_s": round(prefill_s, 1),
                    "l2": "weights streamed per step per GPU exceed L2; no flush needed"},
         "e2e": {"value": e2e_value, "unit": UNIT,

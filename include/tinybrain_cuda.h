@@ -205,6 +205,17 @@ tb_status tb_model_free(tb_model *m);
 tb_status tb_tp_unique_id(uint8_t *id /* [128] */);
 tb_status tb_context_init_tp(tb_context *ctx, const uint8_t *id /* [128] */, int32_t rank, int32_t world);
 tb_status tb_model_set_tensor_parallel(tb_model *m, int32_t rank, int32_t world);
+/* Tensor parallel through peer memory (replaces the NCCL all-reduce of a
+ * runner; LLaMA models, batch <= 16).  Every rank exports its all-reduce
+ * buffer as a 64-byte CUDA IPC handle, the handles are shared out of band, and
+ * each rank maps the others' buffers.  The row-parallel o_proj / down_proj
+ * epilogues then write their partial rows into every rank's buffer over
+ * NVLink as 64-bit (value, step tag) words; the next launch that reads the
+ * residual stream spins (bounded, 2 s) until the words carry this step's tag
+ * and adds the ranks' partials in rank order, so all ranks hold identical
+ * bits.  No fences, counters or separate all-reduce launches. */
+tb_status tb_runner_tp_handle(tb_runner *r, uint8_t *handle /* [64] */);
+tb_status tb_runner_tp_connect(tb_runner *r, const uint8_t *handles /* [world][64], rank order */);
 tb_status tb_model_set_embedding(tb_model *m, const float *emb_host /* [vocab][hidden] */);
 tb_status tb_model_set_final_norm(tb_model *m, const float *w_host /* [hidden] */);
 tb_status tb_model_set_layer_norms(tb_model *m, int32_t layer, const float *input_norm_host,

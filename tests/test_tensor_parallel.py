@@ -137,8 +137,11 @@ TP_CFG = dict(num_layers=2, hidden_dim=256, num_heads=4, num_kv_heads=2, vocab_s
               max_seq_len=96)
 
 
-def _gpu_rank(rank, world, uid, mode, prompt, n_new, out):
+def _gpu_rank(rank, world, uid, mode, prompt, n_new, out, peer, port):
     try:
+        # torch first: its NCCL must be the process's libnccl.so.2 (the library
+        # binds whichever copy is already loaded)
+        import torch.distributed  # noqa: F401
         from tinybrain_b200.runtime import Context, ModelRunner
         cfg = ModelConfig(**TP_CFG)
         w = small_llama(cfg, seed=3, mode=mode)
@@ -146,6 +149,14 @@ def _gpu_rank(rank, world, uid, mode, prompt, n_new, out):
         ctx.init_tensor_parallel(uid, rank, world)
         dm = w.upload(ctx, tp=(rank, world))
         r = ModelRunner(dm, ctx)
+        if peer:  # all-reduce through peer memory: share the IPC handles over gloo
+            import torch.distributed as dist
+            os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+            dist.init_process_group("gloo", rank=rank, world_size=world)
+            hs = [None] * world
+            dist.all_gather_object(hs, r.tp_handle())
+            r.tp_connect(hs)
+            dist.barrier()
         toks = r.generate_batch([prompt], n_new)[0]
         out.put((rank, list(toks), None))
     except Exception as e:  # reported to the parent
@@ -154,7 +165,8 @@ def _gpu_rank(rank, world, uid, mode, prompt, n_new, out):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("mode", ["perChannel", "int4"])
-def test_tp2_greedy_matches_oracle(mode):
+@pytest.mark.parametrize("peer", [False, True], ids=["nccl", "peer_memory"])
+def test_tp2_greedy_matches_oracle(mode, peer):
     from tinybrain_b200.runtime import device_count, tp_unique_id
     if device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -166,7 +178,8 @@ def test_tp2_greedy_matches_oracle(mode):
     uid = tp_unique_id()
     ctxm = mp.get_context("spawn")
     out = ctxm.Queue()
-    procs = [ctxm.Process(target=_gpu_rank, args=(r, 2, uid, mode, prompt, n_new, out), daemon=True)
+    port = _free_port()
+    procs = [ctxm.Process(target=_gpu_rank, args=(r, 2, uid, mode, prompt, n_new, out, peer, port), daemon=True)
              for r in range(2)]
     for p in procs:
         p.start()

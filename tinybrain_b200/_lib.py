@@ -85,6 +85,8 @@ SIGNATURES = {
     "tb_context_init_tp": [_P, _P, _I32, _I32],
     "tb_model_set_tensor_parallel": [_P, _I32, _I32],
     "tb_runner_trace_launches": [_P, _P, _P, _P],
+    "tb_runner_tp_handle": [_P, _P],
+    "tb_runner_tp_connect": [_P, _P],
     "tb_model_set_embedding": [_P, _P],
     "tb_model_set_final_norm": [_P, _P],
     "tb_model_set_layer_norms": [_P, _I32, _P, _P],

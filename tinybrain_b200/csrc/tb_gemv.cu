@@ -281,6 +281,42 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             }
         if (!p.independent) pdl_wait();
         if (ctid == 0) trace_max(p.trace, 2);
+        // Tensor-parallel pull: the source is the residual stream plus the
+        // ranks' partials, in rank order; a word whose tag is not this step's
+        // has not arrived yet (bounded spin).
+        const bool pull = p.ar_world > 1 && p.ar_pull_slot >= 0;
+        const unsigned int ar_tag = (p.ar_world > 1 && p.ar_step) ? *p.ar_step + 1u : 0u;
+        auto pull4 = [&](int m, int k) -> float4 {
+            const size_t off = (size_t)(m0 + m) * p.ld_src + k;
+            float4 a = *reinterpret_cast<const float4*>(p.ar_hin + off);
+            const unsigned long long* base =
+                p.ar_local + (size_t)p.ar_pull_slot * p.ar_world * p.ar_slot_words + off;
+            for (int q = 0; q < p.ar_world; ++q) {
+                const unsigned long long* wq = base + (size_t)q * p.ar_slot_words;
+                unsigned long long w[4];
+                uint64_t t0 = 0;
+                while (true) {
+                    bool all = true;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        w[e] = ld_relaxed_sys_u64(wq + e);
+                        all = all && (uint32_t)(w[e] >> 32) == ar_tag;
+                    }
+                    if (all) break;
+                    if (t0 == 0) t0 = global_timer_ns();
+                    else if (global_timer_ns() - t0 > kWaitLimitNs) {
+                        record_error(p.err, kDevWaitTimeout);
+                        break;
+                    }
+                }
+                a = make_float4(__fadd_rn(a.x, __uint_as_float((uint32_t)w[0])),
+                                __fadd_rn(a.y, __uint_as_float((uint32_t)w[1])),
+                                __fadd_rn(a.z, __uint_as_float((uint32_t)w[2])),
+                                __fadd_rn(a.w, __uint_as_float((uint32_t)w[3])));
+            }
+            return a;
+        };
+        const bool hout = pull && p.ar_hout && blockIdx.x == 0 && blockIdx.y == 0;
         if (p.epilogue == kEpiQkv && ctid < Mloc) {
             const SeqState& sq = p.seq_ro[m0 + ctid];
             const int pos = sq.pos;
@@ -331,7 +367,8 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 if (rms) {
                     if (v4) {
                         for (int k = 4 * (sw * 32 + lane); k < L.K; k += 128 * WPR) {
-                            const float4 a = *reinterpret_cast<const float4*>(sr + k);
+                            const float4 a = pull ? pull4(m, k) : *reinterpret_cast<const float4*>(sr + k);
+                            if (hout) *reinterpret_cast<float4*>(p.ar_hout + (size_t)(m0 + m) * p.ld_src + k) = a;
                             ss = fmaf(a.x, a.x, ss);
                             ss = fmaf(a.y, a.y, ss);
                             ss = fmaf(a.z, a.z, ss);
@@ -345,7 +382,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                     const int k = kbeg + 4 * g;
                     float4 a;
                     if (v4 && k + 3 < L.K) {
-                        a = *reinterpret_cast<const float4*>(sr + k);
+                        a = pull ? pull4(m, k) : *reinterpret_cast<const float4*>(sr + k);
                     } else {
                         a.x = k < L.K ? sr[k] : 0.0f;
                         a.y = k + 1 < L.K ? sr[k + 1] : 0.0f;
@@ -714,6 +751,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             if (p.bias) v = __fadd_rn(v, rowbias[i]);
             return v;
         };
+        const unsigned int ar_tag_push = (p.epilogue == kEpiPush) ? *p.ar_step + 1u : 0u;
         // Items it = ctid + 256 j map to batch row it % MB = ctid % MB (MB
         // divides 256): one argmax key per thread.
         static_assert(256 % MB == 0, "batch rows per CTA divide the consumer threads");
@@ -815,6 +853,11 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 const float v = va[j];
                 if (p.epilogue == kEpiStore) {
                     p.out[(size_t)gm * p.ld_out + n] = v;
+                } else if (p.epilogue == kEpiPush) {
+                    const size_t off = ((size_t)p.ar_push_slot * p.ar_world + p.ar_rank) * p.ar_slot_words +
+                                       (size_t)gm * p.ld_out + n;
+                    const unsigned long long word = ((unsigned long long)ar_tag_push << 32) | __float_as_uint(v);
+                    for (int q = 0; q < p.ar_world; ++q) st_relaxed_sys_u64(p.ar_peers[q] + off, word);
                 } else if (p.epilogue == kEpiResidual) {
                     p.out[(size_t)gm * p.ld_out + n] = __fadd_rn(old[j], v);
                 } else if (p.epilogue == kEpiGelu) {
@@ -855,7 +898,10 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                     }
                     finish_sequence_step(sq, m, p.out_tokens, p.prompt, p.prompt_stride);
                 }
-                if (ctid == 0) *p.ticket = 0u;
+                if (ctid == 0) {
+                    *p.ticket = 0u;
+                    if (p.ar_step) *p.ar_step += 1u;  // tensor parallel: the step's pulls are done
+                }
             }
         }
     }
@@ -959,6 +1005,11 @@ int choose_ksplit(const QLayout& L, int M, int num_sms) {
         }
     }
     return best > 0 ? best : std::min(8, L.slabs);
+}
+
+int gemv_grid_ctas(const GemvParams& p) {
+    const int mb = gemv_mb(p.L.precision, p.M);
+    return (p.L.Np / p.L.RB) * p.P * ((p.M + mb - 1) / mb);
 }
 
 cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream, bool pdl) {

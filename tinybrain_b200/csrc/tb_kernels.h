@@ -85,6 +85,7 @@ enum GemvEpilogue : int {
     kEpiSiluMul = 3,   // RB 64: out[m][n] = silu(gate) * up
     kEpiGelu = 4,      // out[m][n] = gelu(v)
     kEpiArgmax = 5,    // logits (optional) + per-sequence argmax + step bookkeeping
+    kEpiPush = 6,      // tensor parallel: the partial rows go to every rank's all-reduce slot
 };
 
 // Per-sequence decode state living in device memory.
@@ -147,12 +148,30 @@ struct GemvParams {
     int prompt_stride;
     int vocab;
     int* err;                 // device error word
+    // Tensor-parallel all-reduce through peer memory (ar_world > 1).  Buffer of
+    // every rank: tagged words [slot][rank][ar_slot_words], each a 64-bit
+    // (fp32 value, u32 step + 1) pair written with one store, so a reader
+    // knows a value has arrived without fences or counters.  A pushing launch
+    // writes its output rows into every rank's [slot][own rank] region; a
+    // pulling launch reads its source as ar_hin + the ranks' partials (rank
+    // order), spinning (bounded) on words whose tag is not yet this step's,
+    // and its CTA (0, 0) stores that sum to ar_hout.
+    int ar_world, ar_rank;
+    int ar_push_slot, ar_pull_slot;  // -1: none
+    unsigned long long* const* ar_peers;  // [world] buffer bases (own included)
+    const unsigned long long* ar_local;   // own buffer base
+    long long ar_slot_words;              // words per (slot, rank): M * H
+    unsigned int* ar_step;                // step counter (the LM head's last CTA advances it)
+    const float* ar_hin;
+    float* ar_hout;
 };
 
 // Launch the GEMV described by p on `stream` (PDL + cluster attributes).
 cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream, bool pdl);
 // Pick the K-split (cluster size) for a layout and batch.
 int choose_ksplit(const QLayout& L, int M, int num_sms);
+// CTAs of the launch launch_gemv(p) makes.
+int gemv_grid_ctas(const GemvParams& p);
 
 // Repack reference-layout quantized weights (device copies of the host
 // arrays) into the GPU layout.  row_offset places the matrix at rows

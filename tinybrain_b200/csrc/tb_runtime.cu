@@ -220,6 +220,11 @@ struct tb_runner {
     int total_pages = 0;
     // device buffers
     DevBuf seq, ptab, kv, h, q, ctxv, act, logits, rope, prompt, out_tokens, ticket;
+    // tensor parallel through peer memory (tb_runner_tp_connect): the all-reduce
+    // buffer shared over CUDA IPC, the peers' mappings, a second residual buffer
+    DevBuf ar_buf, ar_peers_dev, ar_step, h2;
+    std::vector<void*> ar_peer_host;  // [world]; own buffer at the own rank
+    bool ar_on = false;
     int64_t h2d_bytes = 0, d2h_bytes = 0;  // host<->device traffic of the generate paths
     int prompt_stride = 0, max_out = 0;
     // host mirror
@@ -244,6 +249,8 @@ struct tb_runner {
     DevBuf obs_buf;   // observer outputs: attention weights, layer norms, final hidden
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     ~tb_runner() {
+        for (size_t q = 0; q < ar_peer_host.size(); ++q)
+            if (ar_peer_host[q] && ar_peer_host[q] != ar_buf.p) cudaIpcCloseMemHandle(ar_peer_host[q]);
         for (cudaEvent_t e : ptab_ev)
             if (e) cudaEventDestroy(e);
         if (graph) cudaGraphExecDestroy(graph);
@@ -1109,9 +1116,44 @@ static tb_status build_plan(tb_runner* r) {
     // in an all-reduce of the residual stream.  Rank 0 adds its partial to the
     // residual, the other ranks store theirs, so the sum is h + sum_r y_r.
     const bool tp = m->tp_world > 1;
-    const int row_epi = tp && m->tp_rank != 0 ? kEpiStore : kEpiResidual;
+    // Peer-memory all-reduce (after tb_runner_tp_connect): o_proj of layer l
+    // pushes into slot 2l, down_proj into slot 2l + 1; the next launch that
+    // reads the residual stream pulls the slot (residual + the ranks'
+    // partials, rank order) and, in its CTA (0, 0), stores the sum to the
+    // other residual buffer.  Otherwise NCCL: rank 0 adds its partial to the
+    // residual, the others store theirs, then an in-place all-reduce.
+    const bool ar = tp && r->ar_on;
+    const int row_epi = ar ? kEpiPush : (tp && m->tp_rank != 0 ? kEpiStore : kEpiResidual);
+    const int W = m->tp_world;
+    float* hres[2] = {r->h.as<float>(), ar ? r->h2.as<float>() : r->h.as<float>()};
+    int cur = 0;  // residual buffer holding the stream
+    auto ar_common = [&](GemvParams& p) {
+        p.ar_world = W;
+        p.ar_rank = m->tp_rank;
+        p.ar_push_slot = -1;
+        p.ar_pull_slot = -1;
+        p.ar_peers = r->ar_peers_dev.as<unsigned long long* const>();
+        p.ar_local = r->ar_buf.as<unsigned long long>();
+        p.ar_slot_words = (long long)B * H;
+        p.ar_step = r->ar_step.as<unsigned int>();
+    };
+    auto pull = [&](GemvParams& p, int slot, bool store) {
+        if (!ar) return;
+        ar_common(p);
+        p.ar_pull_slot = slot;
+        p.ar_hin = hres[cur];
+        p.ar_hout = store ? hres[cur ^ 1] : nullptr;
+        p.src = hres[cur];
+        if (store) cur ^= 1;
+    };
+    auto push = [&](GemvParams& p, int slot) {
+        if (!ar) return;
+        ar_common(p);
+        p.ar_push_slot = slot;
+        p.out = nullptr;
+    };
     auto push_allreduce = [&]() {
-        if (!tp) return;
+        if (!tp || ar) return;
         Launch ln{};
         ln.kind = 3;
         ln.bytes = (int64_t)B * H * 4;
@@ -1149,6 +1191,7 @@ static tb_status build_plan(tb_runner* r) {
             p.ptab_stride = r->ptab_stride;
             p.layer = l;
             p.num_layers = c.num_layers;
+            if (l > 0) pull(p, 2 * l - 1, true);
             ln.bytes = gemv_bytes(Ly.qkv.L, B) + (int64_t)B * 2 * kvd * 4;
             r->plan.push_back(ln);
         }
@@ -1187,6 +1230,7 @@ static tb_status build_plan(tb_runner* r) {
             p.epilogue = row_epi;
             p.out = r->h.as<float>();
             p.ld_out = H;
+            push(p, 2 * l);
             ln.bytes = gemv_bytes(Ly.o.L, B) + (int64_t)B * H * 4;
             r->plan.push_back(ln);
             push_allreduce();
@@ -1203,6 +1247,7 @@ static tb_status build_plan(tb_runner* r) {
             p.epilogue = llama ? kEpiSiluMul : kEpiGelu;
             p.out = r->act.as<float>();
             p.ld_out = c.intermediate_dim;
+            pull(p, 2 * l, true);
             ln.bytes = gemv_bytes(Ly.up.L, B);
             r->plan.push_back(ln);
         }
@@ -1217,6 +1262,7 @@ static tb_status build_plan(tb_runner* r) {
             p.epilogue = row_epi;
             p.out = r->h.as<float>();
             p.ld_out = H;
+            push(p, 2 * l + 1);
             ln.bytes = gemv_bytes(Ly.down.L, B) + (int64_t)B * H * 4;
             r->plan.push_back(ln);
             push_allreduce();
@@ -1238,6 +1284,7 @@ static tb_status build_plan(tb_runner* r) {
         p.out_tokens = r->out_tokens.as<int>();
         p.prompt = r->prompt.as<int>();
         p.prompt_stride = r->prompt_stride;
+        pull(p, 2 * c.num_layers - 1, false);
         ln.bytes = gemv_bytes(m->out.L, B);
         r->plan.push_back(ln);
     }
@@ -1533,6 +1580,63 @@ extern "C" tb_status tb_runner_create(tb_model* m, int32_t max_batch, int32_t ma
     }
     TB_CUDA(cudaDeviceSynchronize());
     *out = r.release();
+    return ok();
+}
+
+// ---------------------------------------------------------------------------
+// tensor parallel through peer memory
+// ---------------------------------------------------------------------------
+extern "C" tb_status tb_runner_tp_handle(tb_runner* r, uint8_t* handle) {
+    TB_CHECK(r && handle, "NULL argument");
+    tb_model* m = r->m;
+    TB_CHECK(m->tp_world > 1, "the model is not tensor parallel");
+    TB_CHECK(m->cfg.architecture == TB_ARCH_LLAMA && r->B <= 16 && m->cfg.hidden_dim % 4 == 0,
+             "peer-memory all-reduce: LLaMA models, batch <= 16");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    const size_t slots = (size_t)2 * m->cfg.num_layers, W = (size_t)m->tp_world;
+    const size_t bytes = slots * W * (size_t)r->B * m->cfg.hidden_dim * 8;  // tagged 64-bit words
+    if (!r->ar_buf.p) {
+        TB_CUDA(r->ar_buf.alloc(bytes));
+        TB_CUDA(cudaMemset(r->ar_buf.p, 0, bytes));
+        TB_CUDA(r->ar_step.alloc(64));
+        TB_CUDA(cudaMemset(r->ar_step.p, 0, 64));
+        TB_CUDA(r->h2.alloc((size_t)r->B * m->cfg.hidden_dim * 4));
+    }
+    cudaIpcMemHandle_t h;
+    TB_CUDA(cudaIpcGetMemHandle(&h, r->ar_buf.p));
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    memcpy(handle, &h, 64);
+    return ok();
+}
+
+extern "C" tb_status tb_runner_tp_connect(tb_runner* r, const uint8_t* handles) {
+    TB_CHECK(r && handles, "NULL argument");
+    TB_CHECK(r->ar_buf.p, "call tb_runner_tp_handle first");
+    TB_CHECK(!r->ar_on, "already connected");
+    tb_model* m = r->m;
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    const int W = m->tp_world;
+    r->ar_peer_host.assign(W, nullptr);
+    for (int q = 0; q < W; ++q) {
+        if (q == m->tp_rank) {
+            r->ar_peer_host[q] = r->ar_buf.p;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles + (size_t)q * 64, 64);
+        void* ptr = nullptr;
+        TB_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        r->ar_peer_host[q] = ptr;
+    }
+    TB_CUDA(r->ar_peers_dev.alloc((size_t)W * sizeof(void*)));
+    TB_CUDA(cudaMemcpy(r->ar_peers_dev.p, r->ar_peer_host.data(), (size_t)W * sizeof(void*), cudaMemcpyHostToDevice));
+    r->ar_on = true;
+    tb_status s = build_plan(r);
+    if (s != TB_OK) return s;
+    if (r->graph) {
+        cudaGraphExecDestroy(r->graph);
+        r->graph = nullptr;
+    }
     return ok();
 }
 

@@ -722,6 +722,23 @@ class ModelRunner:
         call("tb_runner_profile_step", self.handle, _ptr(t), _ptr(k), _ptr(b), C.byref(n))
         return t[:n.value].copy(), k[:n.value].copy(), b[:n.value].copy()
 
+    def tp_handle(self) -> bytes:
+        """Tensor parallel: this rank's all-reduce buffer as a 64-byte CUDA IPC
+        handle, to be shared with the other ranks (then tp_connect)."""
+        buf = (C.c_uint8 * 64)()
+        call("tb_runner_tp_handle", self.handle, buf)
+        return bytes(buf)
+
+    def tp_connect(self, handles: Sequence[bytes]):
+        """Map every rank's all-reduce buffer (handles in rank order); from then
+        on the residual all-reduce runs through peer memory inside the GEMV
+        launches instead of NCCL."""
+        blob = b"".join(handles)
+        if len(blob) != 64 * len(handles):
+            raise ValueError("handles must be 64 bytes each")
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        call("tb_runner_tp_connect", self.handle, buf)
+
     def trace_launches(self):
         """Device timeline of one decode step: (stamps [n][16], kinds [n])."""
         cap = 4096
