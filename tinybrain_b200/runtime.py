@@ -388,6 +388,17 @@ class ModelWeights:
     def upload(self, ctx: Optional[Context] = None, tp: Optional[tuple] = None) -> "DeviceModel":
         return DeviceModel(self, ctx, tp)
 
+    @staticmethod
+    def load(path: str) -> "ModelWeights":
+        """ModelWeights.load(from:) -- a .tbf file (ModelWeights.swift:496-798)."""
+        from . import tbf
+        return tbf.load(path)
+
+    def save(self, path: str) -> None:
+        """ModelWeights.save(to:) -- a .tbf file (ModelWeights.swift:260-490)."""
+        from . import tbf
+        tbf.save(self, path)
+
 
 # Which axis of each projection a tensor-parallel rank keeps: 1 = column
 # shard (heads / intermediate rows), 0 = row shard (partial sums).
