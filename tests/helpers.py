@@ -67,3 +67,13 @@ def rel_l2(a, b):
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def assert_same_tokens(got, want, gaps):
+    """Greedy tokens equal the oracle's; a divergence is accepted only at a step
+    whose oracle top-2 logit gap is below 1e-4 (an fp32 reordering can flip it)."""
+    for i, (a, b) in enumerate(zip(got, want)):
+        if a != b:
+            assert gaps[i] < 1e-4, f"token {i}: device {a} vs oracle {b} with top-2 gap {gaps[i]}"
+            return
+    assert len(got) == len(want)

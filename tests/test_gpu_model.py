@@ -8,19 +8,11 @@ import numpy as np
 import pytest
 
 import oracle
-from tests.helpers import rel_l2, small_llama, toy_model
+from tests.helpers import assert_same_tokens, rel_l2, small_llama, toy_model
 from tinybrain_b200.runtime import GenerationConfig, ModelConfig, ModelRunner, SamplerConfig
 
 pytestmark = pytest.mark.gpu
 RTOL_L2 = 1e-3
-
-
-def assert_same_tokens(got, want, gaps):
-    for i, (a, b) in enumerate(zip(got, want)):
-        if a != b:
-            assert gaps[i] < 1e-4, f"token {i}: device {a} vs oracle {b} with top-2 gap {gaps[i]}"
-            return
-    assert len(got) == len(want)
 
 
 def small_cfg(**kw):
