@@ -32,9 +32,9 @@ namespace {
 
 constexpr int kAttnConsumerWarps = 4;
 constexpr int kAttnThreads = (kAttnConsumerWarps + 1) * 32;
-// K/V ring depth: 96 KB (d = 64) or 128 KB (d = 128) of pages in flight per
-// CTA, enough for one or two CTAs to keep an SM's share of HBM busy.
-__host__ __device__ constexpr int attn_stages(int d) { return d >= 128 ? 8 : 12; }
+// K/V ring depth: 96 KB of pages in flight per CTA (12 pages at d = 64, 6 at
+// d = 128), so two CTAs share an SM and one wave holds MHA models' splits.
+__host__ __device__ constexpr int attn_stages(int d) { return d >= 128 ? 6 : 12; }
 constexpr int kAttnHead = 512;  // mbarriers + valid flags
 
 template <int G, int D>
