@@ -64,6 +64,9 @@ def load():
         "orc_runner_max_pages": ([P], I64),
         "orc_runner_page_status": ([P, I64, P], None),
         "orc_generate_greedy": ([P, P, I64, I64, P, P], I64),
+        "orc_lcg_next": ([P], C.c_uint64),
+        "orc_sample_detailed": ([P, I64, P, P, I64, P, P, P], I64),
+        "orc_generate_sampled": ([P, P, I64, I64, P, P, P, P, P], I64),
         "orc_set_threads": ([I32], None),
         "orc_get_threads": ([], I32),
     }
@@ -192,6 +195,30 @@ def attention(q, K, V, H, Hkv, d, want_probs=False):
     return (ctx, probs) if want_probs else ctx
 
 
+class _Sampler(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int32), ("has_top_p", C.c_int32),
+                ("top_p", C.c_float), ("repetition_penalty", C.c_float)]
+
+
+def _sampler(cfg):
+    """orc_sampler from an object with temperature, top_k, top_p, repetition_penalty."""
+    return _Sampler(float(cfg.temperature), int(cfg.top_k or 0), 0 if cfg.top_p is None else 1,
+                    float(cfg.top_p or 0.0), float(cfg.repetition_penalty))
+
+
+def sample_detailed(logits, cfg, history, rng_state):
+    """Sampler.sampleDetailed (Sampler.swift:401-473): (token, probability,
+    entropy, next rng state)."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    hist = np.ascontiguousarray(np.asarray(history, dtype=np.int64))
+    st = C.c_uint64(rng_state)
+    pr, en = C.c_float(0), C.c_float(0)
+    sc = _sampler(cfg)
+    tok = load().orc_sample_detailed(_p(logits), logits.size, C.byref(sc), _p(hist) if hist.size else None,
+                                     hist.size, C.byref(st), C.byref(pr), C.byref(en))
+    return int(tok), float(pr.value), float(en.value), int(st.value)
+
+
 def greedy(logits):
     logits = np.ascontiguousarray(logits, dtype=np.float32)
     return int(load().orc_greedy(_p(logits), logits.size))
@@ -277,6 +304,18 @@ class OracleModel:
         gap = np.zeros(max(1, max_tokens), dtype=np.float32)
         load().orc_generate_greedy(self.r, _p(pr), pr.size, max_tokens, _p(out), _p(gap))
         return out[:max_tokens].tolist(), gap[:max_tokens]
+
+    def generate_sampled(self, prompt, max_tokens, cfg, seed):
+        """generateStream with Sampler.sampleDetailed: (tokens, probabilities, entropies)."""
+        pr = np.ascontiguousarray(np.asarray(prompt, dtype=np.int64))
+        out = np.zeros(max(1, max_tokens), dtype=np.int64)
+        prob = np.zeros(max(1, max_tokens), dtype=np.float32)
+        ent = np.zeros(max(1, max_tokens), dtype=np.float32)
+        st = C.c_uint64(seed)
+        sc = _sampler(cfg)
+        load().orc_generate_sampled(self.r, _p(pr), pr.size, max_tokens, C.byref(sc), C.byref(st), _p(out),
+                                    _p(prob), _p(ent))
+        return out[:max_tokens].tolist(), prob[:max_tokens], ent[:max_tokens]
 
     def __del__(self):
         try:

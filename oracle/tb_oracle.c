@@ -638,6 +638,119 @@ void orc_runner_step(orc_runner *r, int64_t token, float *logits) {
     r->pos += 1;
 }
 
+/* Sampler.swift:369-381: LCG (Numerical Recipes constants). */
+uint64_t orc_lcg_next(uint64_t *state) {
+    *state = *state * 6364136223846793005ULL + 1442695040888963407ULL;
+    return *state;
+}
+
+/* Order of Swift's `sorted { $0.element > $1.element }` on (index, value)
+ * pairs: descending value; the reference's sort is not stable, so equal
+ * values keep ascending index here (a documented choice). */
+typedef struct { float v; int64_t i; } orc_kv;
+static int orc_kv_desc(const void *a, const void *b) {
+    const orc_kv *x = (const orc_kv *)a, *y = (const orc_kv *)b;
+    if (x->v > y->v) return -1;
+    if (x->v < y->v) return 1;
+    return x->i < y->i ? -1 : (x->i > y->i ? 1 : 0);
+}
+
+int64_t orc_sample_detailed(const float *logits, int64_t V, const orc_sampler *cfg, const int64_t *history,
+                            int64_t n_history, uint64_t *rng, float *prob, float *entropy) {
+    float *x = (float *)malloc(sizeof(float) * (size_t)V);
+    float *p = (float *)malloc(sizeof(float) * (size_t)V);
+    orc_kv *srt = (orc_kv *)malloc(sizeof(orc_kv) * (size_t)V);
+    memcpy(x, logits, sizeof(float) * (size_t)V);
+    /* 1. repetition penalty, sign-aware, once per history entry (Sampler.swift:409-421) */
+    if (cfg->repetition_penalty != 1.0f && n_history > 0) {
+        const float pen = cfg->repetition_penalty;
+        for (int64_t h = 0; h < n_history; ++h) {
+            const int64_t t = history[h];
+            if (t >= 0 && t < V) x[t] = x[t] > 0 ? x[t] / pen : x[t] * pen;
+        }
+    }
+    /* 2. top-k, else top-p (Sampler.swift:428-448) */
+    if (cfg->top_k > 0) {
+        for (int64_t i = 0; i < V; ++i) { srt[i].v = x[i]; srt[i].i = i; }
+        qsort(srt, (size_t)V, sizeof(orc_kv), orc_kv_desc);
+        char *keep = (char *)calloc((size_t)V, 1);
+        for (int64_t i = 0; i < cfg->top_k && i < V; ++i) keep[srt[i].i] = 1;
+        for (int64_t i = 0; i < V; ++i)
+            if (!keep[i]) x[i] = -INFINITY;
+        free(keep);
+    } else if (cfg->has_top_p) {
+        orc_softmax(x, V, p);
+        for (int64_t i = 0; i < V; ++i) { srt[i].v = p[i]; srt[i].i = i; }
+        qsort(srt, (size_t)V, sizeof(orc_kv), orc_kv_desc);
+        float cum = 0.0f;
+        int64_t cutoff = V;
+        for (int64_t i = 0; i < V; ++i) {
+            cum += srt[i].v;
+            if (cum >= cfg->top_p) { cutoff = i + 1; break; }
+        }
+        char *keep = (char *)calloc((size_t)V, 1);
+        for (int64_t i = 0; i < cutoff; ++i) keep[srt[i].i] = 1;
+        for (int64_t i = 0; i < V; ++i)
+            if (!keep[i]) x[i] = -INFINITY;
+        free(keep);
+    }
+    /* 3. temperature (Sampler.swift:451-458): below 0.01 the logits stay unscaled */
+    const float temp = cfg->temperature > 0 ? cfg->temperature : 0.0f;
+    if (!(temp < 0.01f))
+        for (int64_t i = 0; i < V; ++i) x[i] = x[i] / temp;
+    /* 4. final distribution and entropy (Sampler.swift:461-466) */
+    orc_softmax(x, V, p);
+    float ent = 0.0f;
+    for (int64_t i = 0; i < V; ++i)
+        if (p[i] > 0) ent -= p[i] * logf(p[i]);
+    /* 5. CDF draw (Sampler.swift:340-359) */
+    const float threshold = (float)orc_lcg_next(rng) / (float)UINT64_MAX;
+    float cum = 0.0f;
+    int64_t tok = V - 1;
+    for (int64_t i = 0; i < V; ++i) {
+        cum += p[i];
+        if (threshold <= cum) { tok = i; break; }
+    }
+    if (prob) *prob = p[tok];
+    if (entropy) *entropy = ent;
+    free(x);
+    free(p);
+    free(srt);
+    return tok;
+}
+
+/* ModelRunner.swift:227-298 with Sampler.sampleDetailed (history = prompt +
+ * generated tokens). */
+int64_t orc_generate_sampled(orc_runner *r, const int64_t *prompt, int64_t n_prompt, int64_t max_tokens,
+                             const orc_sampler *cfg, uint64_t *rng, int64_t *out_tokens, float *out_prob,
+                             float *out_entropy) {
+    const int64_t V = r->m->cfg.vocab;
+    float *logits = (float *)malloc(sizeof(float) * (size_t)V);
+    int64_t *hist = (int64_t *)malloc(sizeof(int64_t) * (size_t)(n_prompt + max_tokens + 1));
+    int64_t nh = 0, cur = 0;
+    for (int64_t i = 0; i < n_prompt; ++i) {
+        int64_t t = prompt[i] < 0 ? 0 : (prompt[i] > V - 1 ? V - 1 : prompt[i]);
+        hist[nh++] = t;
+        if (i + 1 < n_prompt)
+            orc_runner_step(r, t, logits);
+        else
+            cur = t;
+    }
+    for (int64_t g = 0; g < max_tokens; ++g) {
+        orc_runner_step(r, cur, logits);
+        float pr = 0.0f, en = 0.0f;
+        const int64_t tok = orc_sample_detailed(logits, V, cfg, hist, nh, rng, &pr, &en);
+        out_tokens[g] = tok;
+        if (out_prob) out_prob[g] = pr;
+        if (out_entropy) out_entropy[g] = en;
+        hist[nh++] = tok;
+        cur = tok;
+    }
+    free(logits);
+    free(hist);
+    return max_tokens;
+}
+
 /* ModelRunner.swift:227-298 with greedy sampling (Sampler.swift:126-138). */
 int64_t orc_generate_greedy(orc_runner *r, const int64_t *prompt, int64_t n_prompt,
                             int64_t max_tokens, int64_t *out_tokens, float *out_gap) {

@@ -67,6 +67,20 @@ void orc_rope(float *v, int64_t head_dim, int64_t num_heads, int64_t position,
 void orc_attention(const float *q, const float *K, const float *V, int64_t L,
                    int64_t H, int64_t Hkv, int64_t d, float *ctx, float *probs);
 int64_t orc_greedy(const float *logits, int64_t V);
+/* Sampler.sampleDetailed (Sampler.swift:401-473) with sampleFromDistribution
+ * (340-359) and the seeded LCG (369-381).  top_k <= 0: none; has_top_p = 0:
+ * none; history: prompt + generated tokens.  *rng advances once per call.
+ * Returns the token; *prob and *entropy as the reference reports them. */
+typedef struct {
+    float temperature;
+    int32_t top_k;        /* <= 0: no top-k filter */
+    int32_t has_top_p;
+    float top_p;
+    float repetition_penalty;
+} orc_sampler;
+uint64_t orc_lcg_next(uint64_t *state);
+int64_t orc_sample_detailed(const float *logits, int64_t V, const orc_sampler *cfg, const int64_t *history,
+                            int64_t n_history, uint64_t *rng, float *prob, float *entropy);
 
 /* ---- model + runner (ModelRunner.swift, KVCache.swift, PageAllocator.swift) ---- */
 typedef struct {
@@ -112,6 +126,11 @@ void orc_runner_page_status(const orc_runner *r, int64_t layer, uint8_t *status)
  * prompt ids are clamped, all but the last are prefilled, then max_tokens
  * steps each followed by argmax.  out_tokens[max_tokens]; out_gap (may be
  * NULL) receives the top-1 minus top-2 logit gap per generated token. */
+/* ModelRunner.swift:227-298 with Sampler.sampleDetailed: tokens, probabilities
+ * and entropies of max_tokens generated steps; *rng is the seeded state. */
+int64_t orc_generate_sampled(orc_runner *r, const int64_t *prompt, int64_t n_prompt, int64_t max_tokens,
+                             const orc_sampler *cfg, uint64_t *rng, int64_t *out_tokens, float *out_prob,
+                             float *out_entropy);
 int64_t orc_generate_greedy(orc_runner *r, const int64_t *prompt, int64_t n_prompt,
                             int64_t max_tokens, int64_t *out_tokens, float *out_gap);
 
