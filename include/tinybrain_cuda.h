@@ -290,6 +290,41 @@ tb_status tb_runner_generate(tb_runner *r, const int32_t *prompts, const int64_t
                              int32_t max_new_tokens, const int32_t *stop_tokens, int32_t n_stop,
                              int32_t *out_tokens, int32_t *out_counts, tb_token_callback cb, void *user);
 
+/* Sampler of tb_runner_generate (SamplerConfig, Sampler.swift:46-104;
+ * Sampler.sampleDetailed, Sampler.swift:401-473).  NULL restores greedy
+ * argmax decoding (the LM-head epilogue).  Otherwise every generated token is
+ * drawn on the device after the LM head: repetition penalty over prompt +
+ * generated tokens, top_k (> 0) else top_p (has_top_p), temperature (below
+ * 0.01: unscaled), softmax, then the reference's LCG (seeded with `seed`
+ * at the start of every generate call, each sequence alike; has_seed = 0
+ * draws a seed from the host).  The persistent step is off while a sampler
+ * is set; tb_runner_step then returns the drawn token as its argmax_out. */
+typedef struct tb_sampler_config {
+    float temperature;
+    int32_t top_k;
+    int32_t has_top_p;
+    float top_p;
+    float repetition_penalty;
+    int32_t has_seed;
+    uint64_t seed;
+} tb_sampler_config;
+tb_status tb_runner_set_sampler(tb_runner *r, const tb_sampler_config *cfg);
+/* Sampler.sampleDetailed (Sampler.swift:401-473) on one host logits row:
+ * the device sampler with `history` as the penalty history; *rng_state is the
+ * LCG state, advanced by the draw (cfg->seed is not read). */
+tb_status tb_sample_detailed(tb_context *ctx, const float *logits, int32_t vocab_size, const tb_sampler_config *cfg,
+                             const int32_t *history, int32_t n_history, uint64_t *rng_state, int32_t *token,
+                             float *prob, float *entropy);
+/* Per generated token of the last tb_runner_generate with a sampler: the
+ * probability of the drawn token and the entropy (nats) of the distribution
+ * it was drawn from (TokenOutput.probability / .entropy), [n_seqs][max_new]. */
+tb_status tb_runner_token_stats(tb_runner *r, int32_t n_seqs, int32_t max_new_tokens, float *prob, float *entropy);
+/* Penalty history (prompt + generated tokens, at most position + 1 of them)
+ * for the sampled draws of the following tb_runner_step / _observed calls,
+ * and the probability / entropy of the last such draw. */
+tb_status tb_runner_set_step_history(tb_runner *r, const int32_t *tokens, int32_t n);
+tb_status tb_runner_step_stats(tb_runner *r, float *prob, float *entropy);
+
 /* Timing hooks for benchmarks: run n decode steps from the current state
  * entirely on the device (inputs already resident), returning the elapsed
  * milliseconds measured with CUDA events on the runner's stream. */

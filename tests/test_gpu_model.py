@@ -139,14 +139,6 @@ def test_batched_eviction_parity(ctx):
         assert_same_tokens(gt, want, gaps)
 
 
-def test_unsupported_sampler_raises(ctx):
-    from tinybrain_b200._lib import TinyBrainError
-    w = small_llama(small_cfg(), seed=8)
-    r = ModelRunner(w, ctx)
-    with pytest.raises(TinyBrainError):
-        list(r.generate_stream([1, 2], GenerationConfig(max_tokens=3, sampler=SamplerConfig(temperature=0.8))))
-
-
 def test_persistent_available_for_batch1_llama_only(ctx):
     from tinybrain_b200._lib import TinyBrainError
     w = small_llama(small_cfg(), seed=9)

@@ -48,6 +48,13 @@ class ModelConfigC(C.Structure):
     ]
 
 
+class SamplerConfigC(C.Structure):
+    _fields_ = [
+        ("temperature", C.c_float), ("top_k", C.c_int32), ("has_top_p", C.c_int32), ("top_p", C.c_float),
+        ("repetition_penalty", C.c_float), ("has_seed", C.c_int32), ("seed", C.c_uint64),
+    ]
+
+
 TOKEN_CALLBACK = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.c_int32, C.c_int32, C.c_int32)
 
 _P = C.c_void_p
@@ -111,6 +118,11 @@ SIGNATURES = {
     "tb_runner_io_bytes": [_P, _PI64, _PI64, _I32],
     "tb_runner_set_persistent": [_P, _I32],
     "tb_runner_get_persistent": [_P, _PI32],
+    "tb_runner_set_sampler": [_P, _P],
+    "tb_sample_detailed": [_P, _P, _I32, _P, _P, _I32, _PU64, _PI32, _PF, _PF],
+    "tb_runner_token_stats": [_P, _I32, _I32, _P, _P],
+    "tb_runner_set_step_history": [_P, _P, _I32],
+    "tb_runner_step_stats": [_P, _PF, _PF],
     "tb_runner_debug_read": [_P, _I32, _P, _I64],
     "tb_runner_trace_step": [_P, _P, _I64, _PI32, _PI32],
 }

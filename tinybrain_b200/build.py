@@ -11,7 +11,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libtinybrain_cuda.so")
-SOURCES = ["tb_gemv.cu", "tb_attention.cu", "tb_quant.cu", "tb_step.cu", "tb_flow.cu", "tb_nccl.cu", "tb_runtime.cu"]
+SOURCES = ["tb_gemv.cu", "tb_attention.cu", "tb_quant.cu", "tb_step.cu", "tb_flow.cu", "tb_nccl.cu", "tb_sampler.cu", "tb_runtime.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -282,6 +282,30 @@ cudaError_t launch_decode_flow(const StepParams& p, int grid, size_t smem, cudaS
 // Phases per step of a launch (diagnostic trace rows).
 inline int step_phases(const StepParams& p) { return p.flow ? 7 * p.num_layers + 2 : 5 * p.num_layers + 1; }
 
+// Device sampler (Sampler.swift:401-473, sampleDetailed) after the LM head:
+// one CTA per sequence draws the next token from logits[m][V] and does the
+// step bookkeeping of finish_sequence_step.
+struct SampleParams {
+    const float* logits;      // [M][V] LM-head output
+    float* work;              // [M][V] working rows when V floats exceed shared memory, else nullptr
+    int V, M;
+    SeqState* seq;
+    const int* prompt;        // [M][prompt_stride]: penalty history, then next prompt tokens
+    int prompt_stride;
+    int* out_tokens;          // [M][max_out]
+    float* out_prob;          // [M][max_out] probability of the drawn token
+    float* out_entropy;       // [M][max_out] entropy (nats) of the final distribution
+    unsigned long long* rng;  // [M] LCG state per sequence
+    float temperature, top_p, repetition_penalty;
+    int top_k;                // <= 0: no top-k filter
+    int has_top_p;
+    unsigned int* ar_step;    // tensor parallel: step counter of the peer all-reduce (or nullptr)
+};
+// Dynamic shared memory of the sampler; *in_smem says whether the working
+// row fits there (else SampleParams::work is required).
+size_t sample_smem_bytes(int V, bool* in_smem);
+cudaError_t launch_sample(const SampleParams& p, cudaStream_t stream, bool pdl);
+
 // Record the calling thread's last-error message (tb_last_error); returns status.
 int report_error(int status, const char* fmt, ...);
 

@@ -24,6 +24,7 @@
 #include <memory>
 #include <string>
 #include <thread>
+#include <random>
 #include <vector>
 
 using namespace tb;
@@ -202,9 +203,11 @@ struct SeqKV {
 };
 
 struct Launch {
-    int kind;  // 0 gemv, 1 attention, 3 all-reduce of the residual stream over the tensor-parallel ranks
+    int kind;  // 0 gemv, 1 attention, 3 all-reduce of the residual stream over the tensor-parallel ranks,
+               // 5 sampler
     GemvParams g;
     AttnParams a;
+    SampleParams s;
     int64_t bytes;  // algorithmic bytes (weights + activations) for roofline
 };
 
@@ -225,6 +228,13 @@ struct tb_runner {
     DevBuf ar_buf, ar_peers_dev, ar_step, h2;
     std::vector<void*> ar_peer_host;  // [world]; own buffer at the own rank
     bool ar_on = false;
+    // device sampler (tb_runner_set_sampler): LCG states, per-token statistics,
+    // working rows for vocabularies beyond shared memory
+    bool sampling = false, persistent_before = false;
+    tb_sampler_config scfg{};
+    DevBuf rng, out_prob, out_ent, swork;
+    std::vector<int> step_hist;      // penalty history of tb_runner_step (sampled)
+    float last_prob = 0.0f, last_ent = 0.0f;
     int64_t h2d_bytes = 0, d2h_bytes = 0;  // host<->device traffic of the generate paths
     int prompt_stride = 0, max_out = 0;
     // host mirror
@@ -1106,6 +1116,29 @@ static int64_t gemv_bytes(const QLayout& L, int M) {
     return w + (int64_t)M * (L.K + L.N) * 4;
 }
 
+// Sampler launch parameters from the runner's current buffers and config.
+static void fill_sample(tb_runner* r, SampleParams& s) {
+    const int V = r->m->cfg.vocab_size;
+    bool in_smem = false;
+    sample_smem_bytes(V, &in_smem);
+    s.logits = r->logits.as<float>();
+    s.work = in_smem ? nullptr : r->swork.as<float>();
+    s.V = V;
+    s.M = r->B;
+    s.seq = r->seq.as<SeqState>();
+    s.prompt = r->prompt.as<int>();
+    s.prompt_stride = r->prompt_stride;
+    s.out_tokens = r->out_tokens.as<int>();
+    s.out_prob = r->out_prob.as<float>();
+    s.out_entropy = r->out_ent.as<float>();
+    s.rng = r->rng.as<unsigned long long>();
+    s.temperature = r->scfg.temperature;
+    s.top_p = r->scfg.top_p;
+    s.repetition_penalty = r->scfg.repetition_penalty;
+    s.top_k = r->scfg.top_k;
+    s.has_top_p = r->scfg.has_top_p;
+}
+
 static tb_status build_plan(tb_runner* r) {
     tb_model* m = r->m;
     const tb_model_config& c = m->cfg;
@@ -1277,15 +1310,29 @@ static tb_status build_plan(tb_runner* r) {
         p.src = r->h.as<float>();
         p.ld_src = H;
         p.norm_w = m->final_norm.as<float>();
-        p.epilogue = kEpiArgmax;
-        p.out = nullptr;
-        p.logits = r->logits.as<float>();
-        p.ticket = r->ticket.as<unsigned int>();
-        p.out_tokens = r->out_tokens.as<int>();
-        p.prompt = r->prompt.as<int>();
-        p.prompt_stride = r->prompt_stride;
+        if (r->sampling) {  // logits only; the sampler launch finishes the step
+            p.epilogue = kEpiStore;
+            p.out = r->logits.as<float>();
+            p.ld_out = c.vocab_size;
+        } else {
+            p.epilogue = kEpiArgmax;
+            p.out = nullptr;
+            p.logits = r->logits.as<float>();
+            p.ticket = r->ticket.as<unsigned int>();
+            p.out_tokens = r->out_tokens.as<int>();
+            p.prompt = r->prompt.as<int>();
+            p.prompt_stride = r->prompt_stride;
+        }
         pull(p, 2 * c.num_layers - 1, false);
         ln.bytes = gemv_bytes(m->out.L, B);
+        r->plan.push_back(ln);
+    }
+    if (r->sampling) {
+        Launch ln{};
+        ln.kind = 5;
+        fill_sample(r, ln.s);
+        ln.s.ar_step = ar ? r->ar_step.as<unsigned int>() : nullptr;
+        ln.bytes = (int64_t)B * c.vocab_size * 4;
         r->plan.push_back(ln);
     }
     return ok();
@@ -1298,6 +1345,11 @@ static tb_status launch_op(tb_runner* r, const Launch& ln, cudaStream_t st, bool
         std::string why;
         e = nccl_allreduce_sum_f32(r->ctx->comm, r->h.as<float>(), (size_t)r->B * r->m->cfg.hidden_dim, st, why);
         if (e != cudaSuccess) return fail(TB_ERR_CUDA, "tensor-parallel all-reduce: %s", why.c_str());
+        return ok();
+    }
+    if (ln.kind == 5) {
+        e = launch_sample(ln.s, st, pdl);
+        if (e != cudaSuccess) return cuda_fail(e, "launch_sample");
         return ok();
     }
     e = ln.kind == 0 ? launch_gemv(ln.g, st, pdl) : launch_attention(ln.a, st, pdl);
@@ -1563,6 +1615,10 @@ extern "C" tb_status tb_runner_create(tb_model* m, int32_t max_batch, int32_t ma
     r->max_out = 1;
     TB_CUDA(r->prompt.alloc((size_t)B * 4));
     TB_CUDA(r->out_tokens.alloc((size_t)B * 4));
+    TB_CUDA(r->out_prob.alloc((size_t)B * 4));
+    TB_CUDA(r->out_ent.alloc((size_t)B * 4));
+    TB_CUDA(r->rng.alloc((size_t)B * 8));
+    TB_CUDA(cudaMemset(r->rng.p, 0, (size_t)B * 8));
     TB_CUDA(cudaEventCreate(&r->ev0));
     TB_CUDA(cudaEventCreate(&r->ev1));
     if ((s = build_plan(r.get())) != TB_OK) return s;
@@ -1771,6 +1827,106 @@ static tb_status push_seq(tb_runner* r) {
     return ok();
 }
 
+// Every sequence's LCG starts from the configured seed (a generate call copies
+// the SamplerConfig, ModelRunner.swift:233); without one, from a host draw.
+static tb_status seed_sampler(tb_runner* r) {
+    uint64_t seed = r->scfg.seed;
+    if (!r->scfg.has_seed) {
+        std::random_device rd;
+        seed = ((uint64_t)rd() << 32) ^ (uint64_t)rd();
+    }
+    std::vector<uint64_t> v((size_t)r->B, seed);
+    TB_CUDA(cudaMemcpy(r->rng.p, v.data(), v.size() * 8, cudaMemcpyHostToDevice));
+    r->h2d_bytes += (int64_t)v.size() * 8;
+    return ok();
+}
+
+// Grow the prompt / output buffers to maxp prompt tokens and mo outputs per
+// sequence and point the plan's (and the persistent step's) launches at them.
+static tb_status ensure_io(tb_runner* r, int maxp, int mo) {
+    // (Re)size prompt/output buffers.
+    if (maxp > r->prompt_stride || r->B * (size_t)maxp * 4 > r->prompt.bytes) {
+        r->prompt_stride = maxp;
+        TB_CUDA(r->prompt.alloc((size_t)r->B * maxp * 4));
+    }
+    if (mo > r->max_out) {
+        r->max_out = mo;
+        TB_CUDA(r->out_tokens.alloc((size_t)r->B * mo * 4));
+        TB_CUDA(r->out_prob.alloc((size_t)r->B * mo * 4));
+        TB_CUDA(r->out_ent.alloc((size_t)r->B * mo * 4));
+        for (Launch& ln : r->plan)
+            if (ln.kind == 0 && ln.g.epilogue == kEpiArgmax) {
+                ln.g.out_tokens = r->out_tokens.as<int>();
+            }
+        if (r->graph) {
+            cudaGraphExecDestroy(r->graph);
+            r->graph = nullptr;
+        }
+    }
+    for (Launch& ln : r->plan)
+        if (ln.kind == 0 && ln.g.epilogue == kEpiArgmax && (ln.g.prompt != r->prompt.as<int>() ||
+                                                            ln.g.prompt_stride != r->prompt_stride)) {
+            ln.g.prompt = r->prompt.as<int>();
+            ln.g.prompt_stride = r->prompt_stride;
+            if (r->graph) {
+                cudaGraphExecDestroy(r->graph);
+                r->graph = nullptr;
+            }
+        }
+    for (Launch& ln : r->plan)
+        if (ln.kind == 5) {
+            SampleParams f = ln.s;
+            fill_sample(r, f);
+            if (f.prompt != ln.s.prompt || f.prompt_stride != ln.s.prompt_stride || f.out_tokens != ln.s.out_tokens ||
+                f.out_prob != ln.s.out_prob || f.out_entropy != ln.s.out_entropy) {
+                f.ar_step = ln.s.ar_step;
+                ln.s = f;
+                if (r->graph) {
+                    cudaGraphExecDestroy(r->graph);
+                    r->graph = nullptr;
+                }
+            }
+        }
+    if (r->persistent_ok &&
+        (r->sp.prompt != r->prompt.as<int>() || r->sp.prompt_stride != r->prompt_stride ||
+         r->sp.out_tokens != r->out_tokens.as<int>())) {
+        refresh_step_params(r);
+        if (r->persistent && r->graph) {
+            cudaGraphExecDestroy(r->graph);
+            r->graph = nullptr;
+        }
+    }
+    return ok();
+}
+
+// A single step (tb_runner_step / _observed) with a sampler draws from its
+// logits: the history of tb_runner_set_step_history stands in as the
+// sequence's prompt (at most pos + 1 tokens, so the step is a generation
+// step) and output slot 0 receives the draw.
+static tb_status step_sampler_state(tb_runner* r, SeqState* st) {
+    if (!r->sampling) return ok();
+    const int n = (int)r->step_hist.size();
+    TB_CHECK(n <= st->pos + 1, "step history holds %d tokens; at most position + 1 = %d", n, st->pos + 1);
+    tb_status e = ensure_io(r, std::max(1, n), 1);
+    if (e != TB_OK) return e;
+    if (n > 0) {
+        TB_CUDA(cudaMemcpy(r->prompt.p, r->step_hist.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+        r->h2d_bytes += (int64_t)n * 4;
+    }
+    st->n_prompt = n;
+    st->n_out = 0;
+    st->max_out = 1;
+    return ok();
+}
+
+// Probability and entropy of a single step's draw (read after the step).
+static tb_status step_sampler_stats(tb_runner* r) {
+    if (!r->sampling) return ok();
+    TB_CUDA(cudaMemcpyAsync(&r->last_prob, r->out_prob.p, 4, cudaMemcpyDeviceToHost, r->ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(&r->last_ent, r->out_ent.p, 4, cudaMemcpyDeviceToHost, r->ctx->stream));
+    return ok();
+}
+
 static tb_status launch_step(tb_runner* r) {
     tb_status s = capture_graph(r);
     if (s != TB_OK) return s;
@@ -1796,11 +1952,13 @@ extern "C" tb_status tb_runner_step(tb_runner* r, int32_t token, float* logits, 
     st->max_out = 0;
     st->active = 1;
     st->best = 0;
+    if ((s = step_sampler_state(r, st)) != TB_OK) return s;
     if ((s = push_seq(r)) != TB_OK) return s;
     if ((s = launch_step(r)) != TB_OK) return s;
     TB_CUDA(cudaMemcpyAsync(r->pin_seq.p, r->seq.p, sizeof(SeqState), cudaMemcpyDeviceToHost, r->ctx->stream));
     if (logits)
         TB_CUDA(cudaMemcpyAsync(logits, r->logits.p, (size_t)V * 4, cudaMemcpyDeviceToHost, r->ctx->stream));
+    if ((s = step_sampler_stats(r)) != TB_OK) return s;
     TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
     r->kvh[0].pos += 1;
     if (argmax_out) *argmax_out = r->pin_seq.as<SeqState>()->token;
@@ -1826,7 +1984,8 @@ extern "C" tb_status tb_runner_step_observed(tb_runner* r, int32_t token, float*
     const int64_t Lc = r->kvh[0].pos + 1;
     TB_CHECK(!attn_weights || attn_stride >= (int64_t)c.num_heads * Lc, "attn_stride %lld < num_heads * L = %lld",
              (long long)attn_stride, (long long)(c.num_heads * Lc));
-    TB_CHECK(r->plan.size() == (size_t)(5 * NL + 1), "observer needs the per-projection plan");
+    const size_t lm = (size_t)(5 * NL);  // the LM-head launch; the sampler (if set) follows it
+    TB_CHECK(r->plan.size() == lm + (r->sampling ? 2 : 1), "observer needs the per-projection plan");
     TB_CUDA(cudaSetDevice(r->ctx->device));
     tb_status s = kv_prepare(r, 0);
     if (s != TB_OK) return s;
@@ -1836,6 +1995,7 @@ extern "C" tb_status tb_runner_step_observed(tb_runner* r, int32_t token, float*
     st->pos = (int)r->kvh[0].pos;
     st->token = token;
     st->active = 1;
+    if ((s = step_sampler_state(r, st)) != TB_OK) return s;
     if ((s = push_seq(r)) != TB_OK) return s;
     const size_t probs_floats = (size_t)NL * c.num_heads * Lc;
     if (r->obs_buf.bytes < (probs_floats + NL + H) * 4) TB_CUDA(r->obs_buf.alloc((probs_floats + NL + H) * 4));
@@ -1846,15 +2006,16 @@ extern "C" tb_status tb_runner_step_observed(tb_runner* r, int32_t token, float*
     for (size_t i = 0; i < r->plan.size(); ++i) {
         const Launch& ln = r->plan[i];
         const int l = (int)(i / 5);
-        if (i + 1 == r->plan.size()) {
+        if (i == lm) {
             cudaError_t e = launch_rmsnorm_rows(r->h.as<float>(), m->has_final_norm ? m->final_norm.as<float>() : nullptr,
                                                 H, H, 1, c.rms_eps, d_final, sm);
             if (e != cudaSuccess) return cuda_fail(e, "launch_rmsnorm_rows");
         }
-        cudaError_t e = ln.kind == 0 ? launch_gemv(ln.g, sm, false) : launch_attention(ln.a, sm, false);
-        if (e != cudaSuccess) return cuda_fail(e, ln.kind == 0 ? "launch_gemv" : "launch_attention");
-        if (i + 1 < r->plan.size() && i % 5 == 0) e = launch_row_norm(r->h.as<float>(), H, H, 1, d_norms + l, sm);
-        if (i + 1 < r->plan.size() && i % 5 == 1)
+        tb_status ls = launch_op(r, ln, sm, false);
+        if (ls != TB_OK) return ls;
+        cudaError_t e = cudaSuccess;
+        if (i < lm && i % 5 == 0) e = launch_row_norm(r->h.as<float>(), H, H, 1, d_norms + l, sm);
+        if (i < lm && i % 5 == 1)
             e = launch_attention_probs(ln.a, d_probs + (size_t)l * c.num_heads * Lc, (int)Lc, sm);
         if (e != cudaSuccess) return cuda_fail(e, "observer kernel");
     }
@@ -1866,6 +2027,7 @@ extern "C" tb_status tb_runner_step_observed(tb_runner* r, int32_t token, float*
         for (int l = 0; l < NL; ++l)
             TB_CUDA(cudaMemcpyAsync(attn_weights + (size_t)l * attn_stride, d_probs + (size_t)l * c.num_heads * Lc,
                                     (size_t)c.num_heads * Lc * 4, cudaMemcpyDeviceToHost, sm));
+    if ((s = step_sampler_stats(r)) != TB_OK) return s;
     TB_CUDA(cudaStreamSynchronize(sm));
     r->kvh[0].pos += 1;
     if (argmax_out) *argmax_out = r->pin_seq.as<SeqState>()->token;
@@ -1898,42 +2060,12 @@ static tb_status gen_setup(tb_runner* r, const int32_t* prompts, const int64_t* 
         gp.n_prompt[s] = (int)n;
         maxp = std::max<int>(maxp, (int)n);
     }
-    // (Re)size prompt/output buffers.
-    if (maxp > r->prompt_stride || r->B * (size_t)maxp * 4 > r->prompt.bytes) {
-        r->prompt_stride = maxp;
-        TB_CUDA(r->prompt.alloc((size_t)r->B * maxp * 4));
-    }
     const int mo = std::max(1, max_new);
-    if (mo > r->max_out) {
-        r->max_out = mo;
-        TB_CUDA(r->out_tokens.alloc((size_t)r->B * mo * 4));
-        for (Launch& ln : r->plan)
-            if (ln.kind == 0 && ln.g.epilogue == kEpiArgmax) {
-                ln.g.out_tokens = r->out_tokens.as<int>();
-            }
-        if (r->graph) {
-            cudaGraphExecDestroy(r->graph);
-            r->graph = nullptr;
-        }
-    }
-    for (Launch& ln : r->plan)
-        if (ln.kind == 0 && ln.g.epilogue == kEpiArgmax && (ln.g.prompt != r->prompt.as<int>() ||
-                                                            ln.g.prompt_stride != r->prompt_stride)) {
-            ln.g.prompt = r->prompt.as<int>();
-            ln.g.prompt_stride = r->prompt_stride;
-            if (r->graph) {
-                cudaGraphExecDestroy(r->graph);
-                r->graph = nullptr;
-            }
-        }
-    if (r->persistent_ok &&
-        (r->sp.prompt != r->prompt.as<int>() || r->sp.prompt_stride != r->prompt_stride ||
-         r->sp.out_tokens != r->out_tokens.as<int>())) {
-        refresh_step_params(r);
-        if (r->persistent && r->graph) {
-            cudaGraphExecDestroy(r->graph);
-            r->graph = nullptr;
-        }
+    tb_status ie = ensure_io(r, maxp, mo);
+    if (ie != TB_OK) return ie;
+    if (r->sampling) {
+        tb_status e = seed_sampler(r);
+        if (e != TB_OK) return e;
     }
     TB_CUDA(r->pin_tokens.ensure((size_t)r->B * std::max(maxp, mo) * 4 + 64));
     int* pin = r->pin_tokens.as<int>();
@@ -2253,6 +2385,8 @@ extern "C" tb_status tb_runner_io_bytes(tb_runner* r, int64_t* h2d, int64_t* d2h
 extern "C" tb_status tb_runner_set_persistent(tb_runner* r, int32_t enable) {
     TB_CHECK(r, "NULL runner");
     const bool want = enable != 0;
+    if (want && r->sampling)
+        return fail(TB_ERR_UNSUPPORTED, "the persistent step decodes greedily; clear the sampler first");
     if (want && !r->persistent_ok)
         return fail(TB_ERR_UNSUPPORTED, "the persistent step needs batch 1, a LLaMA model with uniform layers "
                                         "and a supported head shape");
@@ -2263,6 +2397,131 @@ extern "C" tb_status tb_runner_set_persistent(tb_runner* r, int32_t enable) {
             r->graph = nullptr;
         }
     }
+    return ok();
+}
+
+// Sampler.sampleDetailed on one logits row from the host (the sampler kernel
+// with a single sequence; history = the penalty history).
+extern "C" tb_status tb_sample_detailed(tb_context* ctx, const float* logits, int32_t V, const tb_sampler_config* cfg,
+                                        const int32_t* history, int32_t n_history, uint64_t* rng_state,
+                                        int32_t* token, float* prob, float* entropy) {
+    TB_CHECK(ctx && logits && cfg && rng_state && token && prob && entropy, "NULL argument");
+    TB_CHECK(V >= 1 && n_history >= 0 && (history || n_history == 0), "bad size");
+    TB_CUDA(cudaSetDevice(ctx->device));
+    bool in_smem = false;
+    sample_smem_bytes(V, &in_smem);
+    const int nh = std::max(1, n_history);
+    DevBuf dl, dseq, dhist, dout, dwork;
+    TB_CUDA(dl.alloc((size_t)V * 4));
+    TB_CUDA(dseq.alloc(sizeof(SeqState)));
+    TB_CUDA(dhist.alloc((size_t)nh * 4));
+    TB_CUDA(dout.alloc(32));
+    if (!in_smem) TB_CUDA(dwork.alloc((size_t)V * 4));
+    SeqState st{};
+    st.pos = n_history;  // a generation step: pos >= n_prompt - 1
+    st.n_prompt = n_history;
+    st.max_out = 1;
+    st.active = 1;
+    cudaStream_t sm = ctx->stream;
+    TB_CUDA(cudaMemcpyAsync(dl.p, logits, (size_t)V * 4, cudaMemcpyHostToDevice, sm));
+    TB_CUDA(cudaMemcpyAsync(dseq.p, &st, sizeof st, cudaMemcpyHostToDevice, sm));
+    if (n_history > 0) TB_CUDA(cudaMemcpyAsync(dhist.p, history, (size_t)n_history * 4, cudaMemcpyHostToDevice, sm));
+    TB_CUDA(cudaMemcpyAsync(dout.as<char>() + 16, rng_state, 8, cudaMemcpyHostToDevice, sm));
+    SampleParams p{};
+    p.logits = dl.as<float>();
+    p.work = dwork.as<float>();
+    p.V = V;
+    p.M = 1;
+    p.seq = dseq.as<SeqState>();
+    p.prompt = dhist.as<int>();
+    p.prompt_stride = nh;
+    p.out_tokens = dout.as<int>();
+    p.out_prob = dout.as<float>() + 1;
+    p.out_entropy = dout.as<float>() + 2;
+    p.rng = reinterpret_cast<unsigned long long*>(dout.as<char>() + 16);
+    p.temperature = cfg->temperature;
+    p.top_p = cfg->top_p;
+    p.repetition_penalty = cfg->repetition_penalty;
+    p.top_k = cfg->top_k;
+    p.has_top_p = cfg->has_top_p;
+    cudaError_t e = launch_sample(p, sm, false);
+    if (e != cudaSuccess) return cuda_fail(e, "launch_sample");
+    unsigned char out[32];
+    TB_CUDA(cudaMemcpyAsync(out, dout.p, 32, cudaMemcpyDeviceToHost, sm));
+    TB_CUDA(cudaStreamSynchronize(sm));
+    memcpy(token, out, 4);
+    memcpy(prob, out + 4, 4);
+    memcpy(entropy, out + 8, 4);
+    memcpy(rng_state, out + 16, 8);
+    return tb_context_check_device(ctx);
+}
+
+extern "C" tb_status tb_runner_set_sampler(tb_runner* r, const tb_sampler_config* cfg) {
+    TB_CHECK(r, "NULL runner");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    if (cfg) {
+        TB_CHECK(std::isfinite(cfg->temperature), "temperature must be finite");
+        TB_CHECK(std::isfinite(cfg->repetition_penalty) && cfg->repetition_penalty > 0.0f,
+                 "repetition_penalty must be finite and > 0");
+        TB_CHECK(!cfg->has_top_p || std::isfinite(cfg->top_p), "top_p must be finite");
+    }
+    const bool want = cfg != nullptr;
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    if (want) {
+        const int V = r->m->cfg.vocab_size;
+        bool in_smem = false;
+        sample_smem_bytes(V, &in_smem);
+        if (!in_smem && r->swork.bytes < (size_t)r->B * V * 4) TB_CUDA(r->swork.alloc((size_t)r->B * V * 4));
+        if (!r->sampling) {
+            r->persistent_before = r->persistent;
+            r->persistent = false;
+        }
+        r->scfg = *cfg;
+        r->sampling = true;
+        tb_status e = seed_sampler(r);
+        if (e != TB_OK) return e;
+    } else if (r->sampling) {
+        r->sampling = false;
+        r->persistent = r->persistent_before;
+    }
+    tb_status e = build_plan(r);
+    if (e != TB_OK) return e;
+    if (r->graph) {
+        cudaGraphExecDestroy(r->graph);
+        r->graph = nullptr;
+    }
+    return ok();
+}
+
+extern "C" tb_status tb_runner_set_step_history(tb_runner* r, const int32_t* tokens, int32_t n) {
+    TB_CHECK(r && (tokens || n == 0) && n >= 0, "bad argument");
+    const int V = r->m->cfg.vocab_size;
+    r->step_hist.resize((size_t)n);
+    for (int i = 0; i < n; ++i) r->step_hist[i] = std::max(0, std::min(tokens[i], V - 1));
+    return ok();
+}
+
+extern "C" tb_status tb_runner_step_stats(tb_runner* r, float* prob, float* entropy) {
+    TB_CHECK(r && prob && entropy, "NULL argument");
+    TB_CHECK(r->sampling, "no sampler set: greedy steps draw nothing");
+    *prob = r->last_prob;
+    *entropy = r->last_ent;
+    return ok();
+}
+
+extern "C" tb_status tb_runner_token_stats(tb_runner* r, int32_t n_seqs, int32_t max_new, float* prob,
+                                           float* entropy) {
+    TB_CHECK(r && prob && entropy, "NULL argument");
+    TB_CHECK(n_seqs >= 1 && n_seqs <= r->B && max_new >= 0 && max_new <= r->max_out, "bad shape");
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    for (int s = 0; s < n_seqs; ++s) {
+        TB_CUDA(cudaMemcpy(prob + (size_t)s * max_new, r->out_prob.as<float>() + (size_t)s * r->max_out,
+                           (size_t)max_new * 4, cudaMemcpyDeviceToHost));
+        TB_CUDA(cudaMemcpy(entropy + (size_t)s * max_new, r->out_ent.as<float>() + (size_t)s * r->max_out,
+                           (size_t)max_new * 4, cudaMemcpyDeviceToHost));
+    }
+    r->d2h_bytes += (int64_t)n_seqs * max_new * 8;
     return ok();
 }
 

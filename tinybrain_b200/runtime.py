@@ -506,6 +506,28 @@ class SamplerConfig:
     def is_greedy(self) -> bool:
         return self.top_k == 1
 
+    def uses_argmax(self) -> bool:
+        """top_k = 1 without a penalty draws the argmax: the LM-head epilogue
+        decodes it without a sampler launch."""
+        return self.top_k == 1 and self.repetition_penalty == 1.0
+
+    def strategy(self) -> str:
+        """TokenOutput.strategy text (ModelRunner.swift:262-269)."""
+        parts = [f"temp={self.temperature:.2f}"]
+        if self.top_k is not None:
+            parts.append(f"topK={self.top_k}")
+        if self.top_p is not None:
+            parts.append(f"topP={self.top_p:.2f}")
+        if self.repetition_penalty != 1.0:
+            parts.append(f"penalty={self.repetition_penalty:.2f}")
+        return ", ".join(parts)
+
+    def to_c(self) -> "_lib.SamplerConfigC":
+        return _lib.SamplerConfigC(float(self.temperature), int(self.top_k) if self.top_k is not None else 0,
+                                   0 if self.top_p is None else 1, float(self.top_p or 0.0),
+                                   float(self.repetition_penalty), 0 if self.seed is None else 1,
+                                   int(self.seed or 0) & 0xFFFFFFFFFFFFFFFF)
+
 
 @dataclass
 class GenerationConfig:
@@ -525,6 +547,21 @@ class TokenOutput:
     entropy: float
     timestamp: float
     strategy: Optional[str] = None
+
+
+def sample_detailed(logits, sampler: SamplerConfig, history: Sequence[int] = (), rng_state: int = 0,
+                    ctx: Optional[Context] = None):
+    """Sampler.sampleDetailed (Sampler.swift:401-473) on the device for one
+    logits row: (token, probability, entropy, next LCG state)."""
+    ctx = ctx or Context.default()
+    lg = np.ascontiguousarray(np.asarray(logits, dtype=np.float32).reshape(-1))
+    h = np.ascontiguousarray(np.asarray(list(history), dtype=np.int32))
+    c = sampler.to_c()
+    st = C.c_uint64(int(rng_state) & 0xFFFFFFFFFFFFFFFF)
+    tok, pr, en = C.c_int32(0), C.c_float(0), C.c_float(0)
+    call("tb_sample_detailed", ctx.handle, _ptr(lg), lg.size, C.byref(c), _ptr(h) if h.size else None, int(h.size),
+         C.byref(st), C.byref(tok), C.byref(pr), C.byref(en))
+    return tok.value, pr.value, en.value, st.value
 
 
 def _greedy_topk1_stats():
@@ -646,42 +683,91 @@ class ModelRunner:
              _ptr(stops) if stops.size else None, int(stops.size), _ptr(out), _ptr(counts), cb, None)
         return [out[i, :counts[i]].tolist() for i in range(n)]
 
+    def set_sampler(self, sampler: Optional[SamplerConfig]):
+        """Device sampler for generate_batch / step (Sampler.sampleDetailed);
+        None restores greedy argmax decoding.  The LCG restarts from the
+        config's seed at every generate call."""
+        if sampler is None:
+            call("tb_runner_set_sampler", self.handle, None)
+        else:
+            c = sampler.to_c()
+            call("tb_runner_set_sampler", self.handle, C.byref(c))
+
+    def set_step_history(self, tokens: Sequence[int]):
+        """Penalty history (prompt + generated tokens) of the next sampled step()."""
+        h = np.ascontiguousarray(np.asarray(list(tokens), dtype=np.int32))
+        call("tb_runner_set_step_history", self.handle, _ptr(h) if h.size else None, int(h.size))
+
+    def step_stats(self):
+        """(probability, entropy) of the last sampled step()."""
+        p, e = C.c_float(0), C.c_float(0)
+        call("tb_runner_step_stats", self.handle, C.byref(p), C.byref(e))
+        return p.value, e.value
+
+    def token_stats(self, n_seqs: int, max_new_tokens: int):
+        """Per generated token of the last sampled generate: (probabilities, entropies), [n_seqs][max_new]."""
+        pr = np.zeros((n_seqs, max(1, max_new_tokens)), dtype=np.float32)
+        en = np.zeros_like(pr)
+        call("tb_runner_token_stats", self.handle, n_seqs, max_new_tokens, _ptr(pr), _ptr(en))
+        return pr[:, :max_new_tokens], en[:, :max_new_tokens]
+
     def generate_stream(self, prompt: Sequence[int], config: Optional[GenerationConfig] = None
                         ) -> Iterator[TokenOutput]:
-        """ModelRunner.generateStream (ModelRunner.swift:227-298), greedy sampler only."""
+        """ModelRunner.generateStream (ModelRunner.swift:227-298): every token is
+        drawn on the device -- by the LM-head argmax for top_k = 1 without a
+        penalty, else by the sampler kernel after the LM head."""
         config = config or GenerationConfig()
-        if not config.sampler.is_greedy():
-            raise TinyBrainError(4, "the device sampler implements greedy decoding (SamplerConfig(top_k=1)); "
-                                    "stochastic sampling is not available")
-        strategy = f"temp={config.sampler.temperature:.2f}, topK=1"
-        if config.sampler.repetition_penalty != 1.0:
-            raise TinyBrainError(4, "repetition penalty is not implemented by the device sampler")
-        p, ent = _greedy_topk1_stats()
+        sc = config.sampler
+        strategy = sc.strategy()
+        V = self.config.vocab_size
+        hist = [min(max(int(t), 0), V - 1) for t in prompt]  # ModelRunner.swift:236
+        stops = set(config.stop_tokens)
+        argmax = sc.uses_argmax()
         if self.observer is not None:
             # observed generation runs step by step so every step reports to the
             # observer (ModelRunner.swift:236-298: clamp, prefill all but the
             # last prompt token, then step + sample; a stop token is yielded)
-            V = self.config.vocab_size
-            ids = [min(max(int(t), 0), V - 1) for t in prompt] or [0]
+            ids = hist or [0]
             for t in ids[:-1]:
-                self.step(t)
+                self.step(t)  # prompt steps draw nothing (the sampler is set after them)
             cur = ids[-1]
-            stops = set(config.stop_tokens)
-            for _ in range(config.max_tokens):
-                _, nxt = self.step(cur)
-                yield TokenOutput(nxt, p, ent, time.time(), strategy)
-                if nxt in stops:
-                    break
-                cur = nxt
+            if not argmax:
+                self.set_sampler(sc)
+            try:
+                for _ in range(config.max_tokens):
+                    if not argmax:
+                        self.set_step_history(hist)
+                    _, nxt = self.step(cur)
+                    p, ent = _greedy_topk1_stats() if argmax else self.step_stats()
+                    yield TokenOutput(nxt, p, ent, time.time(), strategy)
+                    if nxt in stops:
+                        break
+                    hist.append(nxt)
+                    cur = nxt
+            finally:
+                if not argmax:
+                    self.set_sampler(None)
             return
-        toks: List[int] = []
+        if not argmax:
+            self.set_sampler(sc)
+        try:
+            toks: List[int] = []
 
-        def cb(seq, idx, tok):
-            toks.append(tok)
-            return False
+            def cb(seq, idx, tok):
+                toks.append(tok)
+                return False
 
-        self.generate_batch([list(prompt)], config.max_tokens, config.stop_tokens, cb)
-        for t in toks:
+            self.generate_batch([list(prompt)], config.max_tokens, config.stop_tokens, cb)
+            if argmax:
+                p, ent = _greedy_topk1_stats()
+                stats = [(p, ent)] * len(toks)
+            else:
+                pr, en = self.token_stats(1, config.max_tokens)
+                stats = [(float(pr[0, i]), float(en[0, i])) for i in range(len(toks))]
+        finally:
+            if not argmax:
+                self.set_sampler(None)
+        for t, (p, ent) in zip(toks, stats):
             yield TokenOutput(t, p, ent, time.time(), strategy)
 
     # -- benchmark hooks --
