@@ -115,6 +115,16 @@ typedef struct {
     int64_t num_zero_points;
 } tb_qtensor_desc;
 
+/* QuantizedTensor.dequantize (QuantizedTensor.swift:182-285) on the device:
+ * out_host[K*N] = (q - zero_point) * scale, per-channel INT8 or INT4 groups
+ * (zero points honoured when given). */
+tb_status tb_dequantize(tb_context *ctx, const tb_qtensor_desc *desc, float *out_host);
+/* PerplexityHarness.convertToINT4 (PerplexityHarness.swift:65-126) for one
+ * linear weight: dequantize, then tb_quantize_int4_group's quantizer with
+ * group_size, on the device; outputs as tb_quantize_int4_group. */
+tb_status tb_requantize_int4(tb_context *ctx, const tb_qtensor_desc *desc, int64_t group_size, uint8_t *packed_host,
+                             float *scales_host, int8_t *zero_points_host);
+
 /* Upload a quantized weight to HBM once (replaces MetalBackend's
  * cachedQuantizedBuffers / cachedINT4Buffers, MetalBackend.swift:1282-1359). */
 tb_status tb_qweight_upload(tb_context *ctx, const tb_qtensor_desc *desc, tb_qweight **out);
@@ -324,6 +334,15 @@ tb_status tb_runner_token_stats(tb_runner *r, int32_t n_seqs, int32_t max_new_to
  * and the probability / entropy of the last such draw. */
 tb_status tb_runner_set_step_history(tb_runner *r, const int32_t *tokens, int32_t n);
 tb_status tb_runner_step_stats(tb_runner *r, float *prob, float *entropy);
+
+/* PerplexityHarness.computePerplexity (PerplexityHarness.swift:141-193) for
+ * n_seqs token slices (tokens[offsets[s] .. offsets[s+1]), each >= 2 ids in
+ * [0, vocab)): teacher-forced steps over each slice on the device, which sums
+ * log P(tokens[i+1] | tokens[..i]) in fp64 (fp32 max, fp64 log-sum-exp).
+ * sum_logprob[s] and n_predictions[s] = length - 1; perplexity =
+ * exp(-sum / n).  No sampler may be set; the runner's sequences start fresh. */
+tb_status tb_runner_perplexity(tb_runner *r, const int32_t *tokens, const int64_t *offsets, int32_t n_seqs,
+                               double *sum_logprob, int64_t *n_predictions);
 
 /* Timing hooks for benchmarks: run n decode steps from the current state
  * entirely on the device (inputs already resident), returning the elapsed

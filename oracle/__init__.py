@@ -65,6 +65,7 @@ def load():
         "orc_runner_page_status": ([P, I64, P], None),
         "orc_generate_greedy": ([P, P, I64, I64, P, P], I64),
         "orc_lcg_next": ([P], C.c_uint64),
+        "orc_perplexity": ([P, P, I64, P], C.c_float),
         "orc_sample_detailed": ([P, I64, P, P, I64, P, P, P], I64),
         "orc_generate_sampled": ([P, P, I64, I64, P, P, P, P, P], I64),
         "orc_set_threads": ([I32], None),
@@ -304,6 +305,14 @@ class OracleModel:
         gap = np.zeros(max(1, max_tokens), dtype=np.float32)
         load().orc_generate_greedy(self.r, _p(pr), pr.size, max_tokens, _p(out), _p(gap))
         return out[:max_tokens].tolist(), gap[:max_tokens]
+
+    def perplexity(self, tokens):
+        """PerplexityHarness.computePerplexity from the current state (reset first):
+        (perplexity, sum of log-probabilities)."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int64))
+        s = C.c_double(0)
+        ppl = load().orc_perplexity(self.r, _p(t), t.size, C.byref(s))
+        return float(ppl), s.value
 
     def generate_sampled(self, prompt, max_tokens, cfg, seed):
         """generateStream with Sampler.sampleDetailed: (tokens, probabilities, entropies)."""

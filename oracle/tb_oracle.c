@@ -751,6 +751,28 @@ int64_t orc_generate_sampled(orc_runner *r, const int64_t *prompt, int64_t n_pro
     return max_tokens;
 }
 
+/* PerplexityHarness.swift:141-193 (computePerplexity): teacher forcing over
+ * tokens[0..n-2]; per step log P(tokens[i+1]) = logit - (log(sum exp(logit -
+ * max)) + max) with the max in fp32 and the sum in fp64; returns
+ * Float(exp(-mean)). */
+float orc_perplexity(orc_runner *r, const int64_t *tokens, int64_t n, double *sum_logprob) {
+    const int64_t V = r->m->cfg.vocab;
+    float *logits = (float *)malloc(sizeof(float) * (size_t)V);
+    double sum = 0.0;
+    for (int64_t i = 0; i + 1 < n; ++i) {
+        orc_runner_step(r, tokens[i], logits);
+        float mx = logits[0];
+        for (int64_t j = 1; j < V; ++j)
+            if (logits[j] > mx) mx = logits[j];
+        double se = 0.0;
+        for (int64_t j = 0; j < V; ++j) se += exp((double)logits[j] - (double)mx);
+        sum += (double)logits[tokens[i + 1]] - (log(se) + (double)mx);
+    }
+    free(logits);
+    if (sum_logprob) *sum_logprob = sum;
+    return n > 1 ? (float)exp(-sum / (double)(n - 1)) : 0.0f;
+}
+
 /* ModelRunner.swift:227-298 with greedy sampling (Sampler.swift:126-138). */
 int64_t orc_generate_greedy(orc_runner *r, const int64_t *prompt, int64_t n_prompt,
                             int64_t max_tokens, int64_t *out_tokens, float *out_gap) {

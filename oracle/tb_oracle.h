@@ -131,6 +131,7 @@ void orc_runner_page_status(const orc_runner *r, int64_t layer, uint8_t *status)
 int64_t orc_generate_sampled(orc_runner *r, const int64_t *prompt, int64_t n_prompt, int64_t max_tokens,
                              const orc_sampler *cfg, uint64_t *rng, int64_t *out_tokens, float *out_prob,
                              float *out_entropy);
+float orc_perplexity(orc_runner *r, const int64_t *tokens, int64_t n, double *sum_logprob);
 int64_t orc_generate_greedy(orc_runner *r, const int64_t *prompt, int64_t n_prompt,
                             int64_t max_tokens, int64_t *out_tokens, float *out_gap);
 

@@ -119,6 +119,9 @@ SIGNATURES = {
     "tb_runner_set_persistent": [_P, _I32],
     "tb_runner_get_persistent": [_P, _PI32],
     "tb_runner_set_sampler": [_P, _P],
+    "tb_runner_perplexity": [_P, _P, _P, _I32, _P, _P],
+    "tb_dequantize": [_P, _P, _P],
+    "tb_requantize_int4": [_P, _P, _I64, _P, _P, _P],
     "tb_sample_detailed": [_P, _P, _I32, _P, _P, _I32, _PU64, _PI32, _PF, _PF],
     "tb_runner_token_stats": [_P, _I32, _I32, _P, _P],
     "tb_runner_set_step_history": [_P, _P, _I32],

@@ -192,6 +192,10 @@ cudaError_t launch_repack(const RepackSrc& s, const QLayout& L, uint8_t* w_out, 
 // Device quantizers (bit-exact restatements of the reference quantizers).
 cudaError_t launch_quantize_int8_per_channel(const float* W, int64_t K, int64_t N, int8_t* Q, float* scales,
                                              cudaStream_t stream);
+// QuantizedTensor.dequantize on the device: prec 8 per-channel [K][N] (scales
+// per column), prec 4 flat groups of gs; zps may be nullptr.
+cudaError_t launch_dequantize(int prec, const uint8_t* data, const float* scales, const int8_t* zps, int64_t K,
+                              int64_t N, int64_t gs, float* out, cudaStream_t stream);
 cudaError_t launch_quantize_int4_group(const float* x, int64_t count, int64_t gs, uint8_t* packed,
                                        float* scales, int8_t* zp, cudaStream_t stream);
 
@@ -300,6 +304,7 @@ struct SampleParams {
     int top_k;                // <= 0: no top-k filter
     int has_top_p;
     unsigned int* ar_step;    // tensor parallel: step counter of the peer all-reduce (or nullptr)
+    double* logprob_acc;      // [M] teacher-forced scoring: prompt steps add log P(next prompt token)
 };
 // Dynamic shared memory of the sampler; *in_smem says whether the working
 // row fits there (else SampleParams::work is required).

@@ -6,6 +6,8 @@
 // integer conversion.  The repack converts the reference's [K in][N out]
 // row-major storage (INT8 per-column scales, INT4 flat groups packed high
 // nibble first) into the streamed layouts documented in tb_kernels.h.
+#include <algorithm>
+
 #include "tb_common.cuh"
 #include "tb_kernels.h"
 #include "tb_tc.cuh"
@@ -77,6 +79,31 @@ __global__ void q4_pack_kernel(const float* __restrict__ x, int64_t count, int64
 // INT8: one thread per (destination row, 16-value k chunk): 16 signed bytes
 // into the tensor-core operand layout of the row's 128-row tile.  Threads with
 // consecutive n read consecutive source bytes of row k.
+// QuantizedTensor.dequantize (QuantizedTensor.swift:182-285): perChannel
+// [K][N] with scales (and zero points) per output column; INT4 flat groups of
+// gs elements, even index = high nibble, nibbles sign-extended.
+// value = (q - zero_point) * scale, in fp32.
+__global__ void dequantize_kernel(int prec, const uint8_t* __restrict__ data, const float* __restrict__ scales,
+                                  const int8_t* __restrict__ zps, int64_t count, int64_t N, int64_t gs,
+                                  float* __restrict__ out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int q;
+        int64_t si;
+        if (prec == 8) {
+            q = (int)(int8_t)data[i];
+            si = i % N;
+        } else {
+            const uint8_t b = data[i >> 1];
+            const int raw = (i & 1) ? (b & 0x0F) : (b >> 4);
+            q = raw > 7 ? raw - 16 : raw;
+            si = i / gs;
+        }
+        const float zp = zps ? (float)zps[si] : 0.0f;
+        out[i] = __fmul_rn(__fsub_rn((float)q, zp), scales[si]);
+    }
+}
+
 __global__ void repack_q8_kernel(const int8_t* __restrict__ src, int K, int N, QLayout L, uint8_t* __restrict__ dst,
                                  int row_offset, int interleave) {
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
@@ -197,6 +224,16 @@ cudaError_t launch_quantize_int4_group(const float* x, int64_t count, int64_t gs
     q4_scales_kernel<<<(unsigned)((ng + 255) / 256), 256, 0, stream>>>(x, count, gs, scales, zp);
     const int64_t nb = (count + 1) / 2;
     q4_pack_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, stream>>>(x, count, gs, scales, packed);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(int prec, const uint8_t* data, const float* scales, const int8_t* zps, int64_t K,
+                              int64_t N, int64_t gs, float* out, cudaStream_t stream) {
+    const int64_t count = K * N;
+    if (count <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((count + 255) / 256, 148 * 16);
+    dequantize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(prec, data, scales, zps, count, N, gs > 0 ? gs : count,
+                                                           out);
     return cudaGetLastError();
 }
 

@@ -231,6 +231,8 @@ struct tb_runner {
     // device sampler (tb_runner_set_sampler): LCG states, per-token statistics,
     // working rows for vocabularies beyond shared memory
     bool sampling = false, persistent_before = false;
+    bool scoring = false;  // tb_runner_perplexity: the sampler launch scores prompt steps
+    DevBuf lp_acc;         // [B] fp64 sum of log P(target)
     tb_sampler_config scfg{};
     DevBuf rng, out_prob, out_ent, swork;
     std::vector<int> step_hist;      // penalty history of tb_runner_step (sampled)
@@ -490,6 +492,70 @@ extern "C" tb_status tb_quantize_int4_group(tb_context* ctx, const float* x, int
     TB_CUDA(cudaMemcpyAsync(packed, dp.p, nb, cudaMemcpyDeviceToHost, ctx->stream));
     TB_CUDA(cudaMemcpyAsync(s, ds.p, ng * 4, cudaMemcpyDeviceToHost, ctx->stream));
     if (zp) TB_CUDA(cudaMemcpyAsync(zp, dz.p, ng, cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return ok();
+}
+
+// QuantizedTensor.dequantize (QuantizedTensor.swift:182-285) of a host tensor:
+// per-channel INT8 or INT4 groups, zero points honoured; staged through HBM.
+static tb_status dequantize_to_device(tb_context* ctx, const tb_qtensor_desc* d, DevBuf& out) {
+    TB_CHECK(d && d->data && d->scales, "NULL argument");
+    TB_CHECK(d->precision == 8 || d->precision == 4, "precision must be 8 or 4 (got %d)", d->precision);
+    TB_CHECK(d->in_features > 0 && d->out_features > 0, "shape must be positive");
+    const int64_t cnt = d->in_features * d->out_features;
+    const int64_t gs = d->precision == 4 ? (d->group_size > 0 ? d->group_size : cnt) : 0;
+    const int64_t nb = d->precision == 8 ? cnt : (cnt + 1) / 2;
+    const int64_t ns = d->precision == 8 ? d->out_features : (cnt + gs - 1) / gs;
+    TB_CHECK(d->data_bytes == nb, "data must hold %lld bytes (got %lld)", (long long)nb, (long long)d->data_bytes);
+    TB_CHECK(d->num_scales == ns, "expected %lld scales (got %lld)", (long long)ns, (long long)d->num_scales);
+    TB_CHECK(!d->zero_points || d->num_zero_points == ns, "expected %lld zero points", (long long)ns);
+    DevBuf dd, ds, dz;
+    TB_CUDA(dd.alloc((size_t)nb));
+    TB_CUDA(ds.alloc((size_t)ns * 4));
+    TB_CUDA(out.alloc((size_t)cnt * 4));
+    TB_CUDA(cudaMemcpyAsync(dd.p, d->data, (size_t)nb, cudaMemcpyHostToDevice, ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(ds.p, d->scales, (size_t)ns * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (d->zero_points) {
+        TB_CUDA(dz.alloc((size_t)ns));
+        TB_CUDA(cudaMemcpyAsync(dz.p, d->zero_points, (size_t)ns, cudaMemcpyHostToDevice, ctx->stream));
+    }
+    TB_CUDA(launch_dequantize(d->precision, dd.as<uint8_t>(), ds.as<float>(), dz.as<int8_t>(), d->in_features,
+                              d->out_features, gs, out.as<float>(), ctx->stream));
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return ok();
+}
+
+extern "C" tb_status tb_dequantize(tb_context* ctx, const tb_qtensor_desc* d, float* out_host) {
+    TB_CHECK(ctx && out_host, "NULL argument");
+    TB_CUDA(cudaSetDevice(ctx->device));
+    DevBuf out;
+    tb_status s = dequantize_to_device(ctx, d, out);
+    if (s != TB_OK) return s;
+    TB_CUDA(cudaMemcpy(out_host, out.p, out.bytes, cudaMemcpyDeviceToHost));
+    return ok();
+}
+
+// PerplexityHarness.convertToINT4 (PerplexityHarness.swift:65-126) for one
+// linear weight: dequantize, then the INT4 group quantizer, both on the device.
+extern "C" tb_status tb_requantize_int4(tb_context* ctx, const tb_qtensor_desc* d, int64_t gs, uint8_t* packed,
+                                        float* scales, int8_t* zps) {
+    TB_CHECK(ctx && packed && scales, "NULL argument");
+    TB_CHECK(gs > 0, "group_size must be positive");
+    TB_CUDA(cudaSetDevice(ctx->device));
+    DevBuf w;
+    tb_status s = dequantize_to_device(ctx, d, w);
+    if (s != TB_OK) return s;
+    const int64_t cnt = d->in_features * d->out_features;
+    const size_t nb = (size_t)(cnt + 1) / 2, ng = (size_t)((cnt + gs - 1) / gs);
+    DevBuf dp, ds, dz;
+    TB_CUDA(dp.alloc(nb));
+    TB_CUDA(ds.alloc(ng * 4));
+    TB_CUDA(dz.alloc(ng));
+    TB_CUDA(launch_quantize_int4_group(w.as<float>(), cnt, gs, dp.as<uint8_t>(), ds.as<float>(), dz.as<int8_t>(),
+                                       ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(packed, dp.p, nb, cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA(cudaMemcpyAsync(scales, ds.p, ng * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (zps) TB_CUDA(cudaMemcpyAsync(zps, dz.p, ng, cudaMemcpyDeviceToHost, ctx->stream));
     TB_CUDA(cudaStreamSynchronize(ctx->stream));
     return ok();
 }
@@ -1137,6 +1203,7 @@ static void fill_sample(tb_runner* r, SampleParams& s) {
     s.repetition_penalty = r->scfg.repetition_penalty;
     s.top_k = r->scfg.top_k;
     s.has_top_p = r->scfg.has_top_p;
+    s.logprob_acc = r->scoring ? r->lp_acc.as<double>() : nullptr;
 }
 
 static tb_status build_plan(tb_runner* r) {
@@ -1310,7 +1377,7 @@ static tb_status build_plan(tb_runner* r) {
         p.src = r->h.as<float>();
         p.ld_src = H;
         p.norm_w = m->final_norm.as<float>();
-        if (r->sampling) {  // logits only; the sampler launch finishes the step
+        if (r->sampling || r->scoring) {  // logits only; the sampler launch finishes the step
             p.epilogue = kEpiStore;
             p.out = r->logits.as<float>();
             p.ld_out = c.vocab_size;
@@ -1327,7 +1394,7 @@ static tb_status build_plan(tb_runner* r) {
         ln.bytes = gemv_bytes(m->out.L, B);
         r->plan.push_back(ln);
     }
-    if (r->sampling) {
+    if (r->sampling || r->scoring) {
         Launch ln{};
         ln.kind = 5;
         fill_sample(r, ln.s);
@@ -2491,6 +2558,64 @@ extern "C" tb_status tb_runner_set_sampler(tb_runner* r, const tb_sampler_config
         r->graph = nullptr;
     }
     return ok();
+}
+
+// PerplexityHarness.computePerplexity (PerplexityHarness.swift:141-193) for
+// n_seqs token slices at once: every slice is fed teacher-forced (the slice is
+// the prompt: tokens[0..n-2] are stepped, each step scores tokens[i+1]) and
+// the device sums log P(target) per slice in fp64.  The runner's sequences
+// start fresh, as in generate.
+extern "C" tb_status tb_runner_perplexity(tb_runner* r, const int32_t* tokens, const int64_t* offs, int32_t n_seqs,
+                                          double* sum_logprob, int64_t* n_predictions) {
+    TB_CHECK(r && tokens && offs && sum_logprob && n_predictions, "NULL argument");
+    TB_CHECK(!r->sampling, "clear the sampler before scoring");
+    TB_CHECK(n_seqs >= 1 && n_seqs <= r->B, "n_seqs must be in [1, %d]", r->B);
+    const int V = r->m->cfg.vocab_size;
+    for (int s = 0; s < n_seqs; ++s) {
+        TB_CHECK(offs[s + 1] - offs[s] >= 2, "slice %d needs at least two tokens to have a prediction target", s);
+        for (int64_t i = offs[s]; i < offs[s + 1]; ++i)
+            TB_CHECK(tokens[i] >= 0 && tokens[i] < V, "token %d out of vocab range [0, %d)", tokens[i], V);
+    }
+    TB_CUDA(cudaSetDevice(r->ctx->device));
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    if (r->lp_acc.bytes < (size_t)r->B * 8) TB_CUDA(r->lp_acc.alloc((size_t)r->B * 8));
+    TB_CUDA(cudaMemset(r->lp_acc.p, 0, (size_t)r->B * 8));
+    const bool persistent = r->persistent;
+    r->persistent = false;
+    r->scoring = true;
+    auto restore = [&]() -> tb_status {
+        r->scoring = false;
+        r->persistent = persistent;
+        tb_status e = build_plan(r);
+        if (r->graph) {
+            cudaGraphExecDestroy(r->graph);
+            r->graph = nullptr;
+        }
+        return e;
+    };
+    tb_status e = build_plan(r);
+    if (r->graph) {
+        cudaGraphExecDestroy(r->graph);
+        r->graph = nullptr;
+    }
+    GenPlan gp;
+    if (e == TB_OK) e = gen_setup(r, tokens, offs, n_seqs, 0, gp);
+    if (e == TB_OK) e = gen_begin(r, gp);
+    if (e == TB_OK) {
+        std::vector<double> acc((size_t)r->B);
+        cudaError_t ce = cudaMemcpyAsync(acc.data(), r->lp_acc.p, (size_t)r->B * 8, cudaMemcpyDeviceToHost,
+                                         r->ctx->stream);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(r->ctx->stream);
+        if (ce != cudaSuccess) e = cuda_fail(ce, "perplexity read-back");
+        for (int s = 0; s < n_seqs && e == TB_OK; ++s) {
+            sum_logprob[s] = acc[s];
+            n_predictions[s] = offs[s + 1] - offs[s] - 1;
+        }
+    }
+    tb_status e2 = restore();
+    if (e != TB_OK) return e;
+    if (e2 != TB_OK) return e2;
+    return tb_context_check_device(r->ctx);
 }
 
 extern "C" tb_status tb_runner_set_step_history(tb_runner* r, const int32_t* tokens, int32_t n) {

@@ -72,6 +72,16 @@ __device__ __forceinline__ float block_sum(float v, double* red) {
     return s;
 }
 
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    double s = 0.0;
+    for (int w = 0; w < kSampWarps; ++w) s += red[w];
+    return s;
+}
+
 // Radix select over the descending order of (key, then index ascending) of
 // the members: the key T of the element at which the running weight first
 // reaches `target`.  Returns false when the members' total weight stays below
@@ -165,6 +175,22 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
     SeqState& sq = p.seq[m];
     const int active = sq.active, pos = sq.pos, n_prompt = sq.n_prompt, n_out = sq.n_out, max_out = sq.max_out;
     if (!active || pos < n_prompt - 1) {
+        if (active && p.logprob_acc) {
+            // PerplexityHarness.computePerplexity (PerplexityHarness.swift:155-186):
+            // log P(target) = logit[target] - (log(sum exp(logit - max)) + max),
+            // the max in fp32, the exponentials and their sum in fp64
+            const float* lg = p.logits + (size_t)m * V;
+            float lm = -INFINITY;
+            for (int i = tid; i < V; i += kSampThreads) lm = fmaxf(lm, lg[i]);
+            const float mx = block_max(lm, sh.red);
+            double ls = 0.0;
+            for (int i = tid; i < V; i += kSampThreads) ls += exp((double)lg[i] - (double)mx);
+            const double tot = block_sum_d(ls, sh.red);
+            if (tid == 0) {
+                const int tgt = p.prompt[(size_t)m * p.prompt_stride + pos + 1];
+                p.logprob_acc[m] += (double)lg[tgt] - (log(tot) + (double)mx);
+            }
+        }
         __syncthreads();
         if (tid == 0) {
             if (active) {  // prompt step: feed the next prompt token

@@ -167,9 +167,27 @@ class QuantizedTensor:
             d.num_zero_points = self.zero_points.size
         return d
 
-    def dequantize(self) -> np.ndarray:
-        raise TinyBrainError(4, "dequantize() is a host debugging helper in the reference; "
-                                "use the oracle in tests instead")
+    def dequantize(self, ctx: Optional[Context] = None) -> np.ndarray:
+        """QuantizedTensor.dequantize (QuantizedTensor.swift:182-285) on the
+        device: fp32 [K, N] = (q - zero_point) * scale."""
+        ctx = ctx or Context.default()
+        out = np.empty(self.shape, dtype=np.float32)
+        d = self.desc()
+        call("tb_dequantize", ctx.handle, C.byref(d), _ptr(out))
+        return out
+
+    def to_int4(self, group_size: int = 32, ctx: Optional[Context] = None) -> "QuantizedTensor":
+        """dequantize() then quantize(mode='int4') in one device pass
+        (the per-weight step of PerplexityHarness.convertToINT4)."""
+        ctx = ctx or Context.default()
+        cnt = int(self.shape[0]) * int(self.shape[1])
+        ng = (cnt + group_size - 1) // group_size
+        p = np.empty((cnt + 1) // 2, dtype=np.uint8)
+        sc = np.empty(ng, dtype=np.float32)
+        z = np.empty(ng, dtype=np.int8)
+        d = self.desc()
+        call("tb_requantize_int4", ctx.handle, C.byref(d), int(group_size), _ptr(p), _ptr(sc), _ptr(z))
+        return QuantizedTensor(tuple(self.shape), p, sc, "int4", group_size, z)
 
 
 def quantize(w: np.ndarray, mode: str = "perChannel", group_size: int = 32,
@@ -405,6 +423,21 @@ class ModelWeights:
 TP_AXIS = {"query": 1, "key": 1, "value": 1, "gate": 1, "up": 1, "output": 0, "down": 0}
 
 
+def convert_to_int4(weights: "ModelWeights", group_size: int = 32, ctx: Optional[Context] = None
+                    ) -> "ModelWeights":
+    """PerplexityHarness.convertToINT4 (PerplexityHarness.swift:65-126): every
+    linear weight re-quantized to INT4 groups on the device; embeddings, norms
+    and biases unchanged."""
+    def q4(lw):
+        return None if lw is None else LinearLayerWeights(lw.weights.to_int4(group_size, ctx), lw.bias)
+
+    layers = [TransformerLayerWeights(query=q4(ly.query), key=q4(ly.key), value=q4(ly.value), output=q4(ly.output),
+                                      up=q4(ly.up), down=q4(ly.down), gate=q4(ly.gate), input_norm=ly.input_norm,
+                                      post_attention_norm=ly.post_attention_norm) for ly in weights.layers]
+    return ModelWeights(weights.config, weights.token_embeddings, layers, q4(weights.output),
+                        final_norm=weights.final_norm)
+
+
 def shard_linear(lw: "LinearLayerWeights", axis: int, rank: int, world: int) -> "LinearLayerWeights":
     """Tensor-parallel slice of a projection; a row shard's bias stays on rank 0
     (the partial sums of all ranks are added up once)."""
@@ -572,6 +605,50 @@ def _greedy_topk1_stats():
     return float(p), float(ent)
 
 
+@dataclass
+class PerplexitySlice:
+    """PerplexitySlice (PerplexityHarness.swift:15-46): a pinned, pre-tokenized
+    slice; the first token is the BOS id."""
+
+    source: str
+    tokenizer: str
+    bos_token_id: int
+    seed: str
+    num_tokens: int
+    tokens: List[int]
+    notes: str = ""
+
+    @classmethod
+    def load(cls, path: str) -> "PerplexitySlice":
+        import json
+        with open(path) as f:
+            d = json.load(f)
+        return cls(d["source"], d["tokenizer"], int(d["bos_token_id"]), str(d["seed"]), int(d["num_tokens"]),
+                   [int(t) for t in d["tokens"]], d.get("notes", ""))
+
+
+@dataclass
+class PerplexityResult:
+    """PerplexityHarness.Result (PerplexityHarness.swift:127-133)."""
+
+    perplexity: float
+    num_predictions: int
+    elapsed_seconds: float
+    sum_log_prob: float = 0.0
+
+
+def compute_perplexity(weights, tokens, ctx: Optional[Context] = None) -> PerplexityResult:
+    """PerplexityHarness.computePerplexity (PerplexityHarness.swift:141-193):
+    a fresh runner, teacher-forced over the slice, fp64 log-probabilities
+    summed on the device; perplexity = Float(exp(-mean))."""
+    toks = tokens.tokens if isinstance(tokens, PerplexitySlice) else list(tokens)
+    r = ModelRunner(weights, ctx, max_batch=1, max_positions=max(len(toks), 1))
+    try:
+        return r.perplexity([toks])[0]
+    finally:
+        r.close()
+
+
 class KVCacheView:
     """The runner's KVCache as the reference exposes it (KVCache.swift:138-356)."""
 
@@ -682,6 +759,21 @@ class ModelRunner:
         call("tb_runner_generate", self.handle, _ptr(flat), _ptr(offs), n, max_new_tokens,
              _ptr(stops) if stops.size else None, int(stops.size), _ptr(out), _ptr(counts), cb, None)
         return [out[i, :counts[i]].tolist() for i in range(n)]
+
+    def perplexity(self, slices: Sequence[Sequence[int]]) -> List[PerplexityResult]:
+        """computePerplexity for up to max_batch slices decoded together (each
+        teacher-forced on its own sequence)."""
+        n = len(slices)
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(t, dtype=np.int32) for t in slices]))
+        offs = np.zeros(n + 1, dtype=np.int64)
+        offs[1:] = np.cumsum([len(t) for t in slices])
+        acc = np.zeros(n, dtype=np.float64)
+        cnt = np.zeros(n, dtype=np.int64)
+        t0 = time.perf_counter()
+        call("tb_runner_perplexity", self.handle, _ptr(flat), _ptr(offs), n, _ptr(acc), _ptr(cnt))
+        el = time.perf_counter() - t0
+        return [PerplexityResult(float(np.float32(np.exp(-acc[i] / cnt[i]))), int(cnt[i]), el, float(acc[i]))
+                for i in range(n)]
 
     def set_sampler(self, sampler: Optional[SamplerConfig]):
         """Device sampler for generate_batch / step (Sampler.sampleDetailed);
