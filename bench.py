@@ -210,7 +210,11 @@ def run_ours(args):
     total_new = W + K
 
     # ---- device-resident timing (value) ----
+    runner.ctx.synchronize()
+    t_pf = time.perf_counter()
     runner.prefill_device([prompt], total_new)
+    runner.ctx.synchronize()
+    prefill_s = time.perf_counter() - t_pf
     if W:
         runner.decode_device(W)
     clocks = ClockSampler(local)
@@ -304,6 +308,9 @@ def run_ours(args):
         "gpu_launches": int(len(kinds)) * K,
         "clocks": clk,
         "model_build_s": round(build_s, 1),
+        "prefill": {"tokens": len(prompt) - 1, "seconds": round(prefill_s, 4),
+                    "tok_s": round((len(prompt) - 1) / max(prefill_s, 1e-9), 1),
+                    "mode": "chunked (64 prompt tokens per pass of the layers)"},
     }
     if cpu:
         line["cpu_baseline"] = cpu

@@ -272,6 +272,13 @@ tb_status tb_runner_max_pages(const tb_runner *r, int64_t *n);
  * enable = 0, use one fused kernel per projection and attention. */
 tb_status tb_runner_set_persistent(tb_runner *r, int32_t enable);
 tb_status tb_runner_get_persistent(const tb_runner *r, int32_t *enabled);
+/* Prompt prefill of tb_runner_generate (default on): up to 64 prompt tokens
+ * (of one or several sequences) per pass of the layers, each token a row with
+ * its own position, so the weights stream once per chunk; the logits of prompt
+ * steps are not computed (the reference discards them).  Off, or for prompts
+ * that would evict KV pages, or under tensor parallelism, or while scoring,
+ * prompts are stepped one token at a time as ModelRunner.swift:240-244 does. */
+tb_status tb_runner_set_chunked_prefill(tb_runner *r, int32_t enable);
 /* Copy an internal fp32 buffer of the runner to the host (diagnostics):
  * 0 h_in, 1 h_mid (persistent step), 2-5 split-K partials (qkv, o, gate/up,
  * down), 6 attention split partials, 7 logits, 8 residual stream, 9 q,

@@ -229,3 +229,40 @@ def test_observer_generate_stream_same_tokens(ctx):
     assert seen == plain
     # one didComputeLogits per step: 7 prefill steps + 12 decode steps
     assert sum(1 for c in rec.calls if c[0] == "logits") == len(prompt) - 1 + 12
+
+
+@pytest.mark.parametrize("mode", ["perChannel", "int4"])
+def test_chunked_prefill_matches_oracle_and_token_by_token(ctx, mode):
+    from tinybrain_b200.runtime import KVCacheView
+    w = small_llama(small_cfg(max_seq_len=256), seed=12, mode=mode, std=0.05)
+    rng = np.random.default_rng(5)
+    # 150 tokens span three chunks; 70 + 2 + 1 share chunks with it
+    prompts = [rng.integers(0, 1024, n).tolist() for n in (150, 1, 70, 2)]
+    chunked = ModelRunner(w, ctx, max_batch=4)
+    stepped = ModelRunner(w, ctx, max_batch=4)
+    stepped.set_chunked_prefill(False)
+    a = chunked.generate_batch(prompts, 12)
+    b = stepped.generate_batch(prompts, 12)
+    for i, p in enumerate(prompts):
+        want, gaps = oracle.OracleModel(w, mode=1).generate_greedy(p, 12)
+        assert_same_tokens(a[i], want, gaps)
+        assert_same_tokens(b[i], want, gaps)
+        ka, kb = KVCacheView(chunked, i), KVCacheView(stepped, i)
+        assert ka.length == kb.length == len(p) - 1 + 12 if p else True
+        assert ka.page_allocation_status() == kb.page_allocation_status()
+
+
+def test_chunked_prefill_then_step_logits(ctx):
+    # the state a chunked prefill leaves (KV pages, positions) feeds later steps
+    w = small_llama(small_cfg(max_seq_len=256), seed=13)
+    prompt = np.random.default_rng(6).integers(0, 1024, 100).tolist()
+    r = ModelRunner(w, ctx)
+    r.generate_batch([prompt], 1)
+    o = oracle.OracleModel(w, mode=1)
+    for t in prompt:
+        o.step(t)
+    assert r.current_position == o.position
+    nxt = [5, 900, 17]
+    for t in nxt:
+        logits, _ = r.step(t)
+        assert rel_l2(logits, o.step(t)) <= RTOL_L2

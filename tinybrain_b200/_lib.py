@@ -118,6 +118,7 @@ SIGNATURES = {
     "tb_runner_io_bytes": [_P, _PI64, _PI64, _I32],
     "tb_runner_set_persistent": [_P, _I32],
     "tb_runner_get_persistent": [_P, _PI32],
+    "tb_runner_set_chunked_prefill": [_P, _I32],
     "tb_runner_set_sampler": [_P, _P],
     "tb_runner_perplexity": [_P, _P, _P, _I32, _P, _P],
     "tb_dequantize": [_P, _P, _P],

@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
                     if (!mbar_wait(&empty[st], ((i / kAttnStages) - 1) & 1, p.err)) break;
                 }
                 const int lp = pg0 + i;
-                if (lp == npages - 1 && !waited) {  // the page the preceding kernel appends to
+                if ((p.wait_first || lp == npages - 1) && !waited) {  // pages the preceding kernel appends to
                     pdl_wait();
                     waited = true;
                 }

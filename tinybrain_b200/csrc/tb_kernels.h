@@ -220,6 +220,10 @@ struct AttnParams {
     float* out;               // [M][H*d]
     int ld_out;
     int* err;
+    // 0: only the last page may be written by the preceding kernel (decode:
+    // earlier pages are fetched before the dependency wait); 1: any page may
+    // be (chunked prefill appends a whole chunk of positions), wait first
+    int wait_first;
 };
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
 constexpr int kMaxAttnSplits = 16;  // the splits of a (sequence, KV head) form one cluster

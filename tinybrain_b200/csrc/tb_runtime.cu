@@ -237,6 +237,14 @@ struct tb_runner {
     DevBuf rng, out_prob, out_ent, swork;
     std::vector<int> step_hist;      // penalty history of tb_runner_step (sampled)
     float last_prob = 0.0f, last_ent = 0.0f;
+    // chunked prefill: prompt tokens as the rows of a layers-only step plan
+    bool pf_ready = false, pf_enabled = true;
+    int pf_nsplit = 1;
+    std::vector<Launch> pf_plan;
+    cudaGraphExec_t pf_graph = nullptr;
+    DevBuf pf_h, pf_q, pf_ctx, pf_act, pf_seq, pf_ptab;
+    PinnedBuf pf_pin[2];
+    cudaEvent_t pf_ev[2] = {nullptr, nullptr};
     int64_t h2d_bytes = 0, d2h_bytes = 0;  // host<->device traffic of the generate paths
     int prompt_stride = 0, max_out = 0;
     // host mirror
@@ -266,6 +274,9 @@ struct tb_runner {
         for (cudaEvent_t e : ptab_ev)
             if (e) cudaEventDestroy(e);
         if (graph) cudaGraphExecDestroy(graph);
+        if (pf_graph) cudaGraphExecDestroy(pf_graph);
+        for (cudaEvent_t e : pf_ev)
+            if (e) cudaEventDestroy(e);
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
     }
@@ -1162,17 +1173,28 @@ extern "C" tb_status tb_model_weight_bytes(const tb_model* m, int64_t* bytes) {
 // ---------------------------------------------------------------------------
 // runner
 // ---------------------------------------------------------------------------
-static void fill_gemv_common(tb_runner* r, GemvParams& p, const FusedWeight& f) {
+// Buffers and rows of one step plan: the decode plan (the runner's batch) or
+// the chunked-prefill plan (prompt tokens as rows, layers only).
+struct PlanIO {
+    int B;
+    float *h, *h2, *q, *ctxv, *act;
+    SeqState* seq;
+    int* ptab;
+    int nsplit;
+    bool head;  // final norm + LM head (+ sampler)
+};
+
+static void fill_gemv_common(tb_runner* r, GemvParams& p, const FusedWeight& f, const PlanIO& io) {
     p.w = f.w.as<uint8_t>();
     p.scales = f.s.as<float>();
     p.bias = f.has_bias ? f.bias.as<float>() : nullptr;
     p.L = f.L;
-    p.M = r->B;
-    p.P = choose_ksplit(f.L, r->B, r->ctx->num_sms);
+    p.M = io.B;
+    p.P = choose_ksplit(f.L, io.B, r->ctx->num_sms);
     p.eps = r->m->cfg.rms_eps;
     p.vocab = r->m->cfg.vocab_size;
-    p.seq_ro = r->seq.as<SeqState>();
-    p.seq = r->seq.as<SeqState>();
+    p.seq_ro = io.seq;
+    p.seq = io.seq;
     p.err = r->ctx->err.as<int>();
 }
 
@@ -1206,10 +1228,10 @@ static void fill_sample(tb_runner* r, SampleParams& s) {
     s.logprob_acc = r->scoring ? r->lp_acc.as<double>() : nullptr;
 }
 
-static tb_status build_plan(tb_runner* r) {
+static tb_status build_plan_into(tb_runner* r, const PlanIO& io, std::vector<Launch>& plan) {
     tb_model* m = r->m;
     const tb_model_config& c = m->cfg;
-    const int H = c.hidden_dim, d = m->head_dim, kvd = m->kv_dim, qd = m->q_dim, B = r->B;
+    const int H = c.hidden_dim, d = m->head_dim, kvd = m->kv_dim, qd = m->q_dim, B = io.B;
     const bool llama = c.architecture == TB_ARCH_LLAMA;
     // Tensor parallel: QKV and gate/up are column shards (local heads, local
     // intermediate rows), o_proj and down row shards whose partial sums meet
@@ -1225,7 +1247,7 @@ static tb_status build_plan(tb_runner* r) {
     const bool ar = tp && r->ar_on;
     const int row_epi = ar ? kEpiPush : (tp && m->tp_rank != 0 ? kEpiStore : kEpiResidual);
     const int W = m->tp_world;
-    float* hres[2] = {r->h.as<float>(), ar ? r->h2.as<float>() : r->h.as<float>()};
+    float* hres[2] = {io.h, ar ? io.h2 : io.h};
     int cur = 0;  // residual buffer holding the stream
     auto ar_common = [&](GemvParams& p) {
         p.ar_world = W;
@@ -1257,9 +1279,9 @@ static tb_status build_plan(tb_runner* r) {
         Launch ln{};
         ln.kind = 3;
         ln.bytes = (int64_t)B * H * 4;
-        r->plan.push_back(ln);
+        plan.push_back(ln);
     };
-    r->plan.clear();
+    plan.clear();
     for (int l = 0; l < c.num_layers; ++l) {
         Layer& Ly = m->layers[l];
         const bool has_in = Ly.in_norm_d.p != nullptr, has_post = Ly.post_norm_d.p != nullptr;
@@ -1267,18 +1289,18 @@ static tb_status build_plan(tb_runner* r) {
             Launch ln{};
             ln.kind = 0;
             GemvParams& p = ln.g;
-            fill_gemv_common(r, p, Ly.qkv);
+            fill_gemv_common(r, p, Ly.qkv, io);
             if (l == 0)
                 p.prologue = has_in ? kProEmbedRms : kProEmbed;
             else
                 p.prologue = has_in ? kProRmsNorm : kProNone;
-            p.src = r->h.as<float>();
+            p.src = io.h;
             p.ld_src = H;
             p.norm_w = Ly.in_norm_d.as<float>();
             p.embedding = m->emb.as<float>();
-            p.resid = r->h.as<float>();
+            p.resid = io.h;
             p.epilogue = kEpiQkv;
-            p.out = r->q.as<float>();
+            p.out = io.q;
             p.ld_out = qd;
             p.H = qd;
             p.Hkv = c.num_kv_heads;
@@ -1287,24 +1309,24 @@ static tb_status build_plan(tb_runner* r) {
             p.rope = r->rope.as<float2>();
             p.rope_max_pos = r->max_positions;
             p.kv_pool = r->kv.as<float>();
-            p.page_table = r->ptab.as<int>();
+            p.page_table = io.ptab;
             p.ptab_stride = r->ptab_stride;
             p.layer = l;
             p.num_layers = c.num_layers;
             if (l > 0) pull(p, 2 * l - 1, true);
             ln.bytes = gemv_bytes(Ly.qkv.L, B) + (int64_t)B * 2 * kvd * 4;
-            r->plan.push_back(ln);
+            plan.push_back(ln);
         }
         {  // attention
             Launch ln{};
             ln.kind = 1;
             AttnParams& a = ln.a;
-            a.q = r->q.as<float>();
+            a.q = io.q;
             a.ld_q = qd;
             a.kv_pool = r->kv.as<float>();
-            a.page_table = r->ptab.as<int>();
+            a.page_table = io.ptab;
             a.ptab_stride = r->ptab_stride;
-            a.seq = r->seq.as<SeqState>();
+            a.seq = io.seq;
             a.lens = nullptr;
             a.layer = l;
             a.num_layers = c.num_layers;
@@ -1312,69 +1334,69 @@ static tb_status build_plan(tb_runner* r) {
             a.Hkv = c.num_kv_heads;
             a.d = d;
             a.M = B;
-            a.nsplit = r->nsplit;
-            a.out = r->ctxv.as<float>();
+            a.nsplit = io.nsplit;
+            a.out = io.ctxv;
             a.ld_out = qd;
             a.err = r->ctx->err.as<int>();
             ln.bytes = 0;  // depends on the context length; accounted by the caller
-            r->plan.push_back(ln);
+            plan.push_back(ln);
         }
         {  // o_proj + residual
             Launch ln{};
             ln.kind = 0;
             GemvParams& p = ln.g;
-            fill_gemv_common(r, p, Ly.o);
+            fill_gemv_common(r, p, Ly.o, io);
             p.prologue = kProNone;
-            p.src = r->ctxv.as<float>();
+            p.src = io.ctxv;
             p.ld_src = qd;
             p.epilogue = row_epi;
-            p.out = r->h.as<float>();
+            p.out = io.h;
             p.ld_out = H;
             push(p, 2 * l);
             ln.bytes = gemv_bytes(Ly.o.L, B) + (int64_t)B * H * 4;
-            r->plan.push_back(ln);
+            plan.push_back(ln);
             push_allreduce();
         }
         {  // gate/up (+ post-attention RMSNorm) + SiLU*up, or toy up + GELU
             Launch ln{};
             ln.kind = 0;
             GemvParams& p = ln.g;
-            fill_gemv_common(r, p, Ly.up);
+            fill_gemv_common(r, p, Ly.up, io);
             p.prologue = has_post ? kProRmsNorm : kProNone;
-            p.src = r->h.as<float>();
+            p.src = io.h;
             p.ld_src = H;
             p.norm_w = Ly.post_norm_d.as<float>();
             p.epilogue = llama ? kEpiSiluMul : kEpiGelu;
-            p.out = r->act.as<float>();
+            p.out = io.act;
             p.ld_out = c.intermediate_dim;
             pull(p, 2 * l, true);
             ln.bytes = gemv_bytes(Ly.up.L, B);
-            r->plan.push_back(ln);
+            plan.push_back(ln);
         }
         {  // down + residual
             Launch ln{};
             ln.kind = 0;
             GemvParams& p = ln.g;
-            fill_gemv_common(r, p, Ly.down);
+            fill_gemv_common(r, p, Ly.down, io);
             p.prologue = kProNone;
-            p.src = r->act.as<float>();
+            p.src = io.act;
             p.ld_src = c.intermediate_dim;
             p.epilogue = row_epi;
-            p.out = r->h.as<float>();
+            p.out = io.h;
             p.ld_out = H;
             push(p, 2 * l + 1);
             ln.bytes = gemv_bytes(Ly.down.L, B) + (int64_t)B * H * 4;
-            r->plan.push_back(ln);
+            plan.push_back(ln);
             push_allreduce();
         }
     }
-    {  // final norm + LM head + argmax + step bookkeeping
+    if (io.head) {  // final norm + LM head + argmax + step bookkeeping
         Launch ln{};
         ln.kind = 0;
         GemvParams& p = ln.g;
-        fill_gemv_common(r, p, m->out);
+        fill_gemv_common(r, p, m->out, io);
         p.prologue = m->has_final_norm ? kProRmsNorm : kProNone;
-        p.src = r->h.as<float>();
+        p.src = io.h;
         p.ld_src = H;
         p.norm_w = m->final_norm.as<float>();
         if (r->sampling || r->scoring) {  // logits only; the sampler launch finishes the step
@@ -1392,17 +1414,23 @@ static tb_status build_plan(tb_runner* r) {
         }
         pull(p, 2 * c.num_layers - 1, false);
         ln.bytes = gemv_bytes(m->out.L, B);
-        r->plan.push_back(ln);
+        plan.push_back(ln);
     }
-    if (r->sampling || r->scoring) {
+    if (io.head && (r->sampling || r->scoring)) {
         Launch ln{};
         ln.kind = 5;
         fill_sample(r, ln.s);
         ln.s.ar_step = ar ? r->ar_step.as<unsigned int>() : nullptr;
         ln.bytes = (int64_t)B * c.vocab_size * 4;
-        r->plan.push_back(ln);
+        plan.push_back(ln);
     }
     return ok();
+}
+
+static tb_status build_plan(tb_runner* r) {
+    PlanIO io{r->B, r->h.as<float>(), r->h2.as<float>(), r->q.as<float>(), r->ctxv.as<float>(), r->act.as<float>(),
+              r->seq.as<SeqState>(), r->ptab.as<int>(), r->nsplit, true};
+    return build_plan_into(r, io, r->plan);
 }
 
 // One launch of the plan on `st`.
@@ -2180,6 +2208,123 @@ static tb_status run_steps(tb_runner* r, int steps, const std::vector<char>& act
     return ok();
 }
 
+// Chunked prefill.  The reference steps every prompt token but the last one
+// at a time (ModelRunner.swift:240-244); here up to kPrefillRows prompt
+// tokens -- of one sequence or of several -- are the rows of one pass of the
+// layers: each row carries its own position and a copy of its sequence's page
+// table, so the QKV launch appends every row's K/V (RoPE at the row's
+// position) and the attention launch lets row i attend over positions
+// 0..pos_i, which includes the rows before it in the same chunk.  The weights
+// stream once per chunk instead of once per token.  The logits of prompt
+// steps are discarded by the reference, so the plan stops after the last layer.
+constexpr int kPrefillRows = kMaxGemvBatch;
+
+static tb_status pf_setup(tb_runner* r) {
+    if (r->pf_ready) return ok();
+    tb_model* m = r->m;
+    const tb_model_config& c = m->cfg;
+    const int C = kPrefillRows;
+    const int wq = std::max(c.hidden_dim, m->q_dim);
+    TB_CUDA(r->pf_h.alloc((size_t)C * c.hidden_dim * 4));
+    TB_CUDA(r->pf_q.alloc((size_t)C * wq * 4));
+    TB_CUDA(r->pf_ctx.alloc((size_t)C * wq * 4));
+    TB_CUDA(r->pf_act.alloc((size_t)C * c.intermediate_dim * 4));
+    TB_CUDA(r->pf_seq.alloc((size_t)C * sizeof(SeqState)));
+    TB_CUDA(r->pf_ptab.alloc((size_t)C * r->ptab_stride * 4));
+    r->pf_nsplit = choose_nsplit(C, c.num_kv_heads, r->ptab_stride, r->ctx->num_sms);
+    PlanIO io{C, r->pf_h.as<float>(), r->pf_h.as<float>(), r->pf_q.as<float>(), r->pf_ctx.as<float>(),
+              r->pf_act.as<float>(), r->pf_seq.as<SeqState>(), r->pf_ptab.as<int>(), r->pf_nsplit, false};
+    tb_status e = build_plan_into(r, io, r->pf_plan);
+    if (e != TB_OK) return e;
+    for (Launch& ln : r->pf_plan)
+        if (ln.kind == 1) ln.a.wait_first = 1;  // the chunk's QKV launch wrote any of the row's pages
+    const size_t slot = (size_t)C * sizeof(SeqState) + (size_t)C * r->ptab_stride * 4;
+    for (int i = 0; i < 2; ++i) {
+        TB_CUDA(r->pf_pin[i].ensure(slot));
+        TB_CUDA(cudaEventCreateWithFlags(&r->pf_ev[i], cudaEventDisableTiming));
+    }
+    cudaStream_t st = r->ctx->stream;
+    cudaGraph_t g = nullptr;
+    TB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    for (const Launch& ln : r->pf_plan) {
+        e = launch_op(r, ln, st, true);
+        if (e != TB_OK) break;
+    }
+    cudaError_t ce = cudaStreamEndCapture(st, &g);
+    if (e != TB_OK) {
+        if (g) cudaGraphDestroy(g);
+        return e;
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture (prefill)");
+    ce = cudaGraphInstantiate(&r->pf_graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate (prefill)");
+    r->pf_ready = true;
+    return ok();
+}
+
+// Whether every prompt's prefill fits the cache without eviction (eviction
+// reorders a sequence's pages mid-prompt; such prompts prefill token by token).
+static bool pf_eligible(tb_runner* r, const GenPlan& gp) {
+    if (!r->pf_enabled || r->m->tp_world > 1 || r->scoring) return false;
+    const int64_t cap = std::min<int64_t>(r->m->cfg.max_seq_len, (int64_t)r->max_pages_per_seq * kPageTokens);
+    int total = 0;
+    for (int s = 0; s < gp.n_seqs; ++s) {
+        if (gp.n_prompt[s] - 1 > cap || gp.n_prompt[s] - 1 > r->max_positions) return false;
+        total += std::max(0, gp.n_prompt[s] - 1);
+    }
+    return total >= 2;  // one token: the per-token plan is as good
+}
+
+static tb_status gen_prefill_chunked(tb_runner* r, const GenPlan& gp) {
+    tb_status e = pf_setup(r);
+    if (e != TB_OK) return e;
+    const int C = kPrefillRows, stride = r->ptab_stride;
+    const int* prompt = r->pin_tokens.as<int>();  // host copy of the clamped prompts, [B][prompt_stride]
+    std::vector<int> rows_s, rows_p;               // (sequence, position) of every prefill token
+    for (int s = 0; s < gp.n_seqs; ++s)
+        for (int p = 0; p < gp.n_prompt[s] - 1; ++p) {
+            rows_s.push_back(s);
+            rows_p.push_back(p);
+        }
+    const int n = (int)rows_s.size();
+    for (int c0 = 0, slot = 0; c0 < n; c0 += C, slot ^= 1) {
+        const int rows = std::min(C, n - c0);
+        // pages for every position of the chunk, in order
+        for (int i = 0; i < rows; ++i) {
+            const int s = rows_s[c0 + i];
+            if (r->kvh[s].pos != rows_p[c0 + i]) return fail(TB_ERR_INVALID_ARGUMENT, "prefill row out of order");
+            if ((e = kv_prepare(r, s)) != TB_OK) return e;
+            r->kvh[s].pos += 1;
+        }
+        TB_CUDA(cudaEventSynchronize(r->pf_ev[slot]));  // the slot's previous upload has been consumed
+        SeqState* st = r->pf_pin[slot].as<SeqState>();
+        int* pt = reinterpret_cast<int*>(st + C);
+        memset(st, 0, sizeof(SeqState) * C);
+        for (int i = 0; i < rows; ++i) {
+            const int s = rows_s[c0 + i], p = rows_p[c0 + i];
+            st[i].pos = p;
+            st[i].token = prompt[(size_t)s * r->prompt_stride + p];
+            st[i].active = 1;
+            memcpy(pt + (size_t)i * stride, r->ptab_host.data() + (size_t)s * stride, (size_t)stride * 4);
+        }
+        TB_CUDA(cudaMemcpyAsync(r->pf_seq.p, st, sizeof(SeqState) * C, cudaMemcpyHostToDevice, r->ctx->stream));
+        TB_CUDA(cudaMemcpyAsync(r->pf_ptab.p, pt, (size_t)rows * stride * 4, cudaMemcpyHostToDevice,
+                                r->ctx->stream));
+        r->h2d_bytes += (int64_t)sizeof(SeqState) * C + (int64_t)rows * stride * 4;
+        TB_CUDA(cudaEventRecord(r->pf_ev[slot], r->ctx->stream));
+        TB_CUDA(cudaGraphLaunch(r->pf_graph, r->ctx->stream));
+    }
+    // the decode loop starts at the last prompt token of every sequence
+    SeqState* sq = r->pin_seq.as<SeqState>();
+    for (int s = 0; s < gp.n_seqs; ++s) {
+        if (gp.n_prompt[s] <= 1) continue;
+        sq[s].pos = gp.n_prompt[s] - 1;
+        sq[s].token = prompt[(size_t)s * r->prompt_stride + gp.n_prompt[s] - 1];
+    }
+    return push_seq(r);
+}
+
 // Prefill: each sequence steps all but the last prompt token
 // (ModelRunner.swift:240-244).  Sequences with shorter prompts wait (inactive)
 // until every prompt is consumed, so the decode loop runs the whole batch.
@@ -2217,6 +2362,7 @@ static tb_status gen_begin(tb_runner* r, const GenPlan& gp) {
     // Push the initial state, then prefill.
     tb_status e = push_seq(r);
     if (e != TB_OK) return e;
+    if (pf_eligible(r, gp)) return gen_prefill_chunked(r, gp);
     return gen_prefill(r, gp);
 }
 
@@ -2647,6 +2793,12 @@ extern "C" tb_status tb_runner_token_stats(tb_runner* r, int32_t n_seqs, int32_t
                            (size_t)max_new * 4, cudaMemcpyDeviceToHost));
     }
     r->d2h_bytes += (int64_t)n_seqs * max_new * 8;
+    return ok();
+}
+
+extern "C" tb_status tb_runner_set_chunked_prefill(tb_runner* r, int32_t enable) {
+    TB_CHECK(r, "NULL runner");
+    r->pf_enabled = enable != 0;
     return ok();
 }
 

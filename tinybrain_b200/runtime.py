@@ -881,6 +881,11 @@ class ModelRunner:
         call("tb_runner_read_tokens", self.handle, _ptr(out), _ptr(counts))
         return [out[i, :counts[i]].tolist() for i in range(n_seqs)]
 
+    def set_chunked_prefill(self, enable: bool):
+        """Prefill prompts up to 64 tokens per pass of the layers (default) or
+        one token per step as the reference does."""
+        call("tb_runner_set_chunked_prefill", self.handle, int(bool(enable)))
+
     @property
     def persistent(self) -> bool:
         """True when each decode step is one persistent cooperative kernel."""
