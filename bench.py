@@ -64,9 +64,16 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return
+        # wait (bounded) for the first sample so that the sampler is running
+        # when the timed region starts; that pre-region sample is dropped
+        import select
+        r, _, _ = select.select([self.proc.stdout], [], [], 5.0)
+        if r:
+            self.proc.stdout.readline()
 
     def stop(self):
         if not self.proc:
