@@ -625,6 +625,64 @@ def run_config5(args):
     return 0
 
 
+def run_config6(args):
+    """The reference's only published figures for this path: the step rate of
+    its perplexity harness (PerplexityHarness.computePerplexity: 64 teacher-
+    forced single-token steps at context <= 65 on TinyLlama), 1.66 tok/s INT8
+    and 1.52 tok/s INT4-g32 on an M4 Max.  Same work here: a 65-token slice
+    (BOS 1 + 64 seeded uniform ids standing in for the reference's pinned
+    WikiText-2 slice), the INT8 model and its convertToINT4 re-quantization,
+    one teacher-forced step per prediction with the fp64 log-probability
+    summed on the device.  K timed harness calls after W warm-up calls; each
+    call resets the runner (host clock around the synchronous call: prompt
+    upload, every step, the sum's read-back)."""
+    import numpy as np
+    from tinybrain_b200.runtime import Context, ModelRunner, convert_to_int4
+    from tinybrain_b200.synthetic import random_prompt
+    ctx = Context(0)
+    w8 = build_model(ctx, mode="perChannel")
+    w4 = convert_to_int4(w8, 32, ctx)
+    slice_ids = [1] + [int(t) for t in random_prompt(64, 32000, 6)]
+    W, K = args.warmup, max(1, min(args.steps, 20))
+    out = {}
+    for name, w, published in (("int8", w8, 64 / 38.45), ("int4_g32", w4, 64 / 42.24)):
+        r = ModelRunner(w, ctx, max_batch=1, max_positions=len(slice_ids) + 8)
+        for _ in range(W):
+            r.perplexity([slice_ids])
+        clocks = ClockSampler(0)
+        clocks.start()
+        t0 = time.perf_counter()
+        for _ in range(K):
+            res = r.perplexity([slice_ids])[0]
+        dt = time.perf_counter() - t0
+        clk = clocks.stop()
+        rate = K * res.num_predictions / dt
+        out[name] = {"value": rate, "ms_per_call": 1000.0 * dt / K, "perplexity": res.perplexity,
+                     "published_tok_s": round(published, 3), "vs_published": rate / published, "clocks": clk}
+        r.close()
+    v = out["int8"]["value"]
+    line = {
+        "metric": "perplexity-harness step rate (teacher-forced TinyLlama steps/s, BASELINE.md section 1)",
+        "value": v, "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": out["int8"]["vs_published"],
+        "dtype": "int8 weights x fp32 activations; fp64 log-sum-exp",
+        "data": "synthetic (seeded LCG normal std 0.02 weights; slice = BOS + 64 seeded uniform ids)",
+        "config": {"workload": "PerplexityHarness.computePerplexity, TinyLlama-1.1B shape, 65-token slice "
+                               "(64 predictions), INT8 and convertToINT4 g32",
+                   "l2": "weights (1.04 GB INT8) exceed L2 every step"},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": round(4 * 65 / 64, 1),
+                "d2h_bytes_per_step": round(8 / 64, 2),
+                "api": "ModelRunner.perplexity (tb_runner_perplexity): host slice in, fp64 sum out"},
+        "int8": out["int8"], "int4_g32": out["int4_g32"],
+        "clocks": out["int8"]["clocks"],
+        # per harness call: 64 steps x (5 launches per layer + LM head + scoring launch)
+        "gpu_launches": K * 64 * (5 * 22 + 2),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -638,10 +696,11 @@ def main():
     ap.add_argument("--per-op", action="store_true", help="the default per-projection launch chain (kept for scripts)")
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
                     help="prompt length (default 128 = the config; shorter only for profiling captures)")
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5, 6],
                     help="BASELINE config: 2 = TinyLlama INT8 decode (default), 1 = single-GEMV HBM bandwidth, "
                          "3 = TinyLlama INT4-g32 decode at context ~2k, 4 = 64 sequences data-parallel, "
-                         "5 = 7B-shaped INT4 tensor-parallel")
+                         "5 = 7B-shaped INT4 tensor-parallel, 6 = perplexity-harness step rate (the reference's "
+                         "only published figures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -653,6 +712,8 @@ def main():
         return run_config4(args)
     if args.config == 5:
         return run_config5(args)
+    if args.config == 6:
+        return run_config6(args)
     return run_ours(args)
 
 
