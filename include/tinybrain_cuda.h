@@ -276,7 +276,7 @@ tb_status tb_runner_get_persistent(const tb_runner *r, int32_t *enabled);
  * (of one or several sequences) per pass of the layers, each token a row with
  * its own position, so the weights stream once per chunk; the logits of prompt
  * steps are not computed (the reference discards them).  Off, or for prompts
- * that would evict KV pages, or under tensor parallelism, or while scoring,
+ * that would evict KV pages, or under tensor parallelism,
  * prompts are stepped one token at a time as ModelRunner.swift:240-244 does. */
 tb_status tb_runner_set_chunked_prefill(tb_runner *r, int32_t enable);
 /* Copy an internal fp32 buffer of the runner to the host (diagnostics):
@@ -344,10 +344,13 @@ tb_status tb_runner_step_stats(tb_runner *r, float *prob, float *entropy);
 
 /* PerplexityHarness.computePerplexity (PerplexityHarness.swift:141-193) for
  * n_seqs token slices (tokens[offsets[s] .. offsets[s+1]), each >= 2 ids in
- * [0, vocab)): teacher-forced steps over each slice on the device, which sums
- * log P(tokens[i+1] | tokens[..i]) in fp64 (fp32 max, fp64 log-sum-exp).
- * sum_logprob[s] and n_predictions[s] = length - 1; perplexity =
- * exp(-sum / n).  No sampler may be set; the runner's sequences start fresh. */
+ * [0, vocab)): teacher-forced over each slice on the device, log
+ * P(tokens[i+1] | tokens[..i]) in fp64 (fp32 max, fp64 log-sum-exp), summed
+ * per slice in position order.  With chunked prefill on (the default) and no
+ * slice long enough to evict KV pages, up to 64 positions are scored per pass
+ * of the layers; otherwise one step per position.  sum_logprob[s] and
+ * n_predictions[s] = length - 1; perplexity = exp(-sum / n).  No sampler may
+ * be set; the runner's sequences start fresh. */
 tb_status tb_runner_perplexity(tb_runner *r, const int32_t *tokens, const int64_t *offsets, int32_t n_seqs,
                                double *sum_logprob, int64_t *n_predictions);
 

@@ -125,3 +125,17 @@ def test_batched_slices_match_single_and_errors(ctx):
     # the runner still generates greedily afterwards
     r1.reset()
     assert len(r1.generate_batch([[1, 2, 3]], 4)[0]) == 4
+
+
+@pytest.mark.gpu
+def test_chunked_scoring_matches_token_by_token(ctx):
+    from tinybrain_b200.runtime import ModelRunner
+    w = small_llama(_cfg(), seed=9, std=0.1)
+    slices = [_tokens(130, 1024, 7), _tokens(33, 1024, 8)]
+    chunked = ModelRunner(w, ctx, max_batch=2).perplexity(slices)
+    r = ModelRunner(w, ctx, max_batch=2)
+    r.set_chunked_prefill(False)
+    stepped = r.perplexity(slices)
+    for a, b in zip(chunked, stepped):
+        assert a.num_predictions == b.num_predictions
+        assert a.sum_log_prob == pytest.approx(b.sum_log_prob, rel=1e-4)

@@ -309,6 +309,8 @@ struct SampleParams {
     int has_top_p;
     unsigned int* ar_step;    // tensor parallel: step counter of the peer all-reduce (or nullptr)
     double* logprob_acc;      // [M] teacher-forced scoring: prompt steps add log P(next prompt token)
+    double* logprob_out;      // [M] chunked scoring: each row's log P(target) (instead of logprob_acc)
+    const int* target;        // [M] chunked scoring: each row's next token (instead of prompt)
 };
 // Dynamic shared memory of the sampler; *in_smem says whether the working
 // row fits there (else SampleParams::work is required).

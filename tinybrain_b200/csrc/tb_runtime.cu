@@ -245,6 +245,11 @@ struct tb_runner {
     DevBuf pf_h, pf_q, pf_ctx, pf_act, pf_seq, pf_ptab;
     PinnedBuf pf_pin[2];
     cudaEvent_t pf_ev[2] = {nullptr, nullptr};
+    // chunked scoring (tb_runner_perplexity): the prefill plan plus LM head and
+    // the scoring launch, one log-probability per row
+    std::vector<Launch> ps_plan;
+    cudaGraphExec_t ps_graph = nullptr;
+    DevBuf ps_logits, ps_lp, ps_target;
     int64_t h2d_bytes = 0, d2h_bytes = 0;  // host<->device traffic of the generate paths
     int prompt_stride = 0, max_out = 0;
     // host mirror
@@ -275,6 +280,7 @@ struct tb_runner {
             if (e) cudaEventDestroy(e);
         if (graph) cudaGraphExecDestroy(graph);
         if (pf_graph) cudaGraphExecDestroy(pf_graph);
+        if (ps_graph) cudaGraphExecDestroy(ps_graph);
         for (cudaEvent_t e : pf_ev)
             if (e) cudaEventDestroy(e);
         if (ev0) cudaEventDestroy(ev0);
@@ -1181,7 +1187,8 @@ struct PlanIO {
     SeqState* seq;
     int* ptab;
     int nsplit;
-    bool head;  // final norm + LM head (+ sampler)
+    bool head;      // final norm + LM head (+ sampler)
+    float* logits;  // [B][V] LM-head output
 };
 
 static void fill_gemv_common(tb_runner* r, GemvParams& p, const FusedWeight& f, const PlanIO& io) {
@@ -1401,7 +1408,7 @@ static tb_status build_plan_into(tb_runner* r, const PlanIO& io, std::vector<Lau
         p.norm_w = m->final_norm.as<float>();
         if (r->sampling || r->scoring) {  // logits only; the sampler launch finishes the step
             p.epilogue = kEpiStore;
-            p.out = r->logits.as<float>();
+            p.out = io.logits;
             p.ld_out = c.vocab_size;
         } else {
             p.epilogue = kEpiArgmax;
@@ -1429,7 +1436,7 @@ static tb_status build_plan_into(tb_runner* r, const PlanIO& io, std::vector<Lau
 
 static tb_status build_plan(tb_runner* r) {
     PlanIO io{r->B, r->h.as<float>(), r->h2.as<float>(), r->q.as<float>(), r->ctxv.as<float>(), r->act.as<float>(),
-              r->seq.as<SeqState>(), r->ptab.as<int>(), r->nsplit, true};
+              r->seq.as<SeqState>(), r->ptab.as<int>(), r->nsplit, true, r->logits.as<float>()};
     return build_plan_into(r, io, r->plan);
 }
 
@@ -2233,12 +2240,13 @@ static tb_status pf_setup(tb_runner* r) {
     TB_CUDA(r->pf_ptab.alloc((size_t)C * r->ptab_stride * 4));
     r->pf_nsplit = choose_nsplit(C, c.num_kv_heads, r->ptab_stride, r->ctx->num_sms);
     PlanIO io{C, r->pf_h.as<float>(), r->pf_h.as<float>(), r->pf_q.as<float>(), r->pf_ctx.as<float>(),
-              r->pf_act.as<float>(), r->pf_seq.as<SeqState>(), r->pf_ptab.as<int>(), r->pf_nsplit, false};
+              r->pf_act.as<float>(), r->pf_seq.as<SeqState>(), r->pf_ptab.as<int>(), r->pf_nsplit, false, nullptr};
     tb_status e = build_plan_into(r, io, r->pf_plan);
     if (e != TB_OK) return e;
     for (Launch& ln : r->pf_plan)
         if (ln.kind == 1) ln.a.wait_first = 1;  // the chunk's QKV launch wrote any of the row's pages
-    const size_t slot = (size_t)C * sizeof(SeqState) + (size_t)C * r->ptab_stride * 4;
+    // staging slot: SeqState rows, page-table rows, scoring targets
+    const size_t slot = (size_t)C * sizeof(SeqState) + (size_t)C * r->ptab_stride * 4 + (size_t)C * 4;
     for (int i = 0; i < 2; ++i) {
         TB_CUDA(r->pf_pin[i].ensure(slot));
         TB_CUDA(cudaEventCreateWithFlags(&r->pf_ev[i], cudaEventDisableTiming));
@@ -2260,6 +2268,113 @@ static tb_status pf_setup(tb_runner* r) {
     cudaGraphDestroy(g);
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate (prefill)");
     r->pf_ready = true;
+    return ok();
+}
+
+// Chunked scoring (tb_runner_perplexity): the prefill plan with the LM head and
+// the scoring launch; every row writes log P(its target) to ps_lp[row].
+static tb_status ps_setup(tb_runner* r) {
+    tb_status e = pf_setup(r);
+    if (e != TB_OK || r->ps_graph) return e;
+    const int C = kPrefillRows, V = r->m->cfg.vocab_size;
+    TB_CUDA(r->ps_logits.alloc((size_t)C * V * 4));
+    TB_CUDA(r->ps_lp.alloc((size_t)C * 8));
+    TB_CUDA(r->ps_target.alloc((size_t)C * 4));
+    PlanIO io{C, r->pf_h.as<float>(), r->pf_h.as<float>(), r->pf_q.as<float>(), r->pf_ctx.as<float>(),
+              r->pf_act.as<float>(), r->pf_seq.as<SeqState>(), r->pf_ptab.as<int>(), r->pf_nsplit, true,
+              r->ps_logits.as<float>()};
+    const bool scoring = r->scoring;
+    r->scoring = true;  // LM head stores logits; the sampler launch follows
+    e = build_plan_into(r, io, r->ps_plan);
+    r->scoring = scoring;
+    if (e != TB_OK) return e;
+    for (Launch& ln : r->ps_plan) {
+        if (ln.kind == 1) ln.a.wait_first = 1;
+        if (ln.kind == 5) {
+            SampleParams& sp = ln.s;
+            sp.logits = r->ps_logits.as<float>();
+            // rows are prompt steps only: the scoring branch reads the logits
+            // directly and never touches a working row, so any buffer serves
+            sp.work = r->ps_logits.as<float>();
+            sp.M = C;
+            sp.seq = r->pf_seq.as<SeqState>();
+            sp.logprob_acc = nullptr;
+            sp.logprob_out = r->ps_lp.as<double>();
+            sp.target = r->ps_target.as<int>();
+            sp.ar_step = nullptr;
+        }
+    }
+    cudaStream_t st = r->ctx->stream;
+    cudaGraph_t g = nullptr;
+    TB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    for (const Launch& ln : r->ps_plan) {
+        e = launch_op(r, ln, st, true);
+        if (e != TB_OK) break;
+    }
+    cudaError_t ce = cudaStreamEndCapture(st, &g);
+    if (e != TB_OK) {
+        if (g) cudaGraphDestroy(g);
+        return e;
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture (scoring)");
+    ce = cudaGraphInstantiate(&r->ps_graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate (scoring)");
+    return ok();
+}
+
+// Teacher-forced scoring of the slices in chunks of kPrefillRows positions:
+// lp[i] = log P(slice token i + 1 | tokens 0..i) for every (slice, position) in
+// slice order.  Slices must fit the cache without eviction.
+static tb_status score_chunked(tb_runner* r, const int32_t* tokens, const int64_t* offs, int32_t n_seqs,
+                               std::vector<double>& lp) {
+    tb_status e = ps_setup(r);
+    if (e != TB_OK) return e;
+    const int C = kPrefillRows, stride = r->ptab_stride;
+    for (int s = 0; s < r->B; ++s) kv_clear(r, s);
+    std::vector<int> rows_s, rows_p;
+    for (int s = 0; s < n_seqs; ++s)
+        for (int p = 0; p + 1 < (int)(offs[s + 1] - offs[s]); ++p) {
+            rows_s.push_back(s);
+            rows_p.push_back(p);
+        }
+    const int n = (int)rows_s.size();
+    lp.assign(n, 0.0);
+    PinnedBuf out;
+    TB_CUDA(out.ensure((size_t)std::max(1, n) * 8));
+    for (int c0 = 0, slot = 0; c0 < n; c0 += C, slot ^= 1) {
+        const int rows = std::min(C, n - c0);
+        for (int i = 0; i < rows; ++i) {
+            const int s = rows_s[c0 + i];
+            if ((e = kv_prepare(r, s)) != TB_OK) return e;
+            r->kvh[s].pos += 1;
+        }
+        TB_CUDA(cudaEventSynchronize(r->pf_ev[slot]));
+        SeqState* st = r->pf_pin[slot].as<SeqState>();
+        int* pt = reinterpret_cast<int*>(st + C);
+        int* tg = pt + (size_t)C * stride;
+        memset(st, 0, sizeof(SeqState) * C);
+        for (int i = 0; i < rows; ++i) {
+            const int s = rows_s[c0 + i], p = rows_p[c0 + i];
+            st[i].pos = p;
+            st[i].token = tokens[offs[s] + p];
+            st[i].n_prompt = p + 2;  // a prompt step: scored, never sampled
+            st[i].active = 1;
+            tg[i] = tokens[offs[s] + p + 1];
+            memcpy(pt + (size_t)i * stride, r->ptab_host.data() + (size_t)s * stride, (size_t)stride * 4);
+        }
+        cudaStream_t sm = r->ctx->stream;
+        TB_CUDA(cudaMemcpyAsync(r->pf_seq.p, st, sizeof(SeqState) * C, cudaMemcpyHostToDevice, sm));
+        TB_CUDA(cudaMemcpyAsync(r->pf_ptab.p, pt, (size_t)rows * stride * 4, cudaMemcpyHostToDevice, sm));
+        TB_CUDA(cudaMemcpyAsync(r->ps_target.p, tg, (size_t)C * 4, cudaMemcpyHostToDevice, sm));
+        r->h2d_bytes += (int64_t)sizeof(SeqState) * C + (int64_t)rows * stride * 4 + (int64_t)C * 4;
+        TB_CUDA(cudaEventRecord(r->pf_ev[slot], sm));
+        TB_CUDA(cudaGraphLaunch(r->ps_graph, sm));
+        TB_CUDA(cudaMemcpyAsync(out.as<double>() + c0, r->ps_lp.p, (size_t)rows * 8, cudaMemcpyDeviceToHost, sm));
+        r->d2h_bytes += (int64_t)rows * 8;
+    }
+    TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    memcpy(lp.data(), out.p, (size_t)n * 8);
     return ok();
 }
 
@@ -2724,6 +2839,28 @@ extern "C" tb_status tb_runner_perplexity(tb_runner* r, const int32_t* tokens, c
     }
     TB_CUDA(cudaSetDevice(r->ctx->device));
     TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
+    // Chunked: up to 64 positions (of one or several slices) per pass, when no
+    // slice would evict KV pages; the per-position log-probabilities come back
+    // and are summed per slice in position order, as the reference does.
+    bool chunk = r->pf_enabled && r->m->tp_world == 1;
+    const int64_t cap = std::min<int64_t>(r->m->cfg.max_seq_len, (int64_t)r->max_pages_per_seq * kPageTokens);
+    for (int s = 0; s < n_seqs && chunk; ++s)
+        chunk = offs[s + 1] - offs[s] - 1 <= std::min<int64_t>(cap, r->max_positions);
+    if (chunk) {
+        std::vector<double> lp;
+        tb_status e = score_chunked(r, tokens, offs, n_seqs, lp);
+        if (e != TB_OK) return e;
+        size_t i0 = 0;
+        for (int s = 0; s < n_seqs; ++s) {
+            const int64_t np = offs[s + 1] - offs[s] - 1;
+            double sum = 0.0;
+            for (int64_t i = 0; i < np; ++i) sum += lp[i0 + i];
+            i0 += (size_t)np;
+            sum_logprob[s] = sum;
+            n_predictions[s] = np;
+        }
+        return tb_context_check_device(r->ctx);
+    }
     if (r->lp_acc.bytes < (size_t)r->B * 8) TB_CUDA(r->lp_acc.alloc((size_t)r->B * 8));
     TB_CUDA(cudaMemset(r->lp_acc.p, 0, (size_t)r->B * 8));
     const bool persistent = r->persistent;

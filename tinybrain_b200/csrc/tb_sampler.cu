@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
     SeqState& sq = p.seq[m];
     const int active = sq.active, pos = sq.pos, n_prompt = sq.n_prompt, n_out = sq.n_out, max_out = sq.max_out;
     if (!active || pos < n_prompt - 1) {
-        if (active && p.logprob_acc) {
+        if (active && (p.logprob_acc || p.logprob_out)) {
             // PerplexityHarness.computePerplexity (PerplexityHarness.swift:155-186):
             // log P(target) = logit[target] - (log(sum exp(logit - max)) + max),
             // the max in fp32, the exponentials and their sum in fp64
@@ -187,14 +187,18 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
             for (int i = tid; i < V; i += kSampThreads) ls += exp((double)lg[i] - (double)mx);
             const double tot = block_sum_d(ls, sh.red);
             if (tid == 0) {
-                const int tgt = p.prompt[(size_t)m * p.prompt_stride + pos + 1];
-                p.logprob_acc[m] += (double)lg[tgt] - (log(tot) + (double)mx);
+                const int tgt = p.target ? p.target[m] : p.prompt[(size_t)m * p.prompt_stride + pos + 1];
+                const double lp = (double)lg[tgt] - (log(tot) + (double)mx);
+                if (p.logprob_out)
+                    p.logprob_out[m] = lp;
+                else
+                    p.logprob_acc[m] += lp;
             }
         }
         __syncthreads();
         if (tid == 0) {
             if (active) {  // prompt step: feed the next prompt token
-                sq.token = p.prompt[(size_t)m * p.prompt_stride + pos + 1];
+                sq.token = p.target ? p.target[m] : p.prompt[(size_t)m * p.prompt_stride + pos + 1];
                 sq.pos = pos + 1;
             }
             sq.best = 0ull;
