@@ -448,13 +448,14 @@ def run_config4(args):
         kinds, nbytes = k, b
     tmean = np.mean(np.stack(times[1:]), axis=0)
     peak, peak_kind = measured_peaks()
-    gm = kinds == 0
+    gm, am = kinds == 0, kinds == 1
+    dg = kinds == 6  # digit operand of each wide GEMV: counted in the GEMV time, not its bytes
     # attention reads every position's K and V rows once per layer (fp32, kv_dim
     # 256): context of the profiled steps = prompt + W + K + about 2
     kvd = 256
     att_bytes_layer = sum((len(p) + W + K + 2) * kvd * 2 * 4 for p in my_prompts)
-    parts = {"gemv": (float(nbytes[gm].sum()), float(tmean[gm].sum()), int(gm.sum())),
-             "attention": (float(att_bytes_layer * int((~gm).sum())), float(tmean[~gm].sum()), int((~gm).sum()))}
+    parts = {"gemv": (float(nbytes[gm].sum()), float(tmean[gm].sum() + tmean[dg].sum()), int(gm.sum())),
+             "attention": (float(att_bytes_layer * int(am.sum())), float(tmean[am].sum()), int(am.sum()))}
     dom = max(parts, key=lambda k: parts[k][1])
     db, dms, dn = parts[dom]
     if rank != 0:

@@ -160,6 +160,8 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
     //   |scale| [4][nunits], digit exponents [MB][4].
     const int kspan = ((L.slabs + P - 1) / P) * kTcUnitK;
     constexpr bool WIDE = gemv_wide(PREC, MB);
+    // wide with a precomputed digit operand (wide_digits): B streams in beside A
+    const bool pre = WIDE && p.bimg != nullptr;
     // wide INT8: B slots [kWideSlots][NB * 128] at xbuf, norm weights after them, no x staging
     float* xs = reinterpret_cast<float*>(
         PREC == 8 ? xbuf + (WIDE ? (size_t)kWideSlots * wide_lbo(NB) * 8 : (size_t)kspan * NB) : xbuf);
@@ -181,7 +183,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         mbar_init(&done[1], 1);
         for (int i = 0; i < kQ4Slots; ++i) {
             mbar_init(&a_ready[i], 4);
-            mbar_init(&b_ready[i], WIDE ? kGemvConsumerWarps : 4);
+            mbar_init(&b_ready[i], WIDE ? (pre ? 1 : kGemvConsumerWarps) : 4);
             mbar_init(&s_free[i], 1);
         }
         fence_barrier_init();
@@ -258,6 +260,19 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 uint8_t* dst = stage_base + st * Cfg::kStageBytes;
                 mbar_arrive_expect_tx(&full[st], Cfg::kStageBytes);
                 bulk_g2s_stream(dst, wrb + (size_t)(s0 + i) * Cfg::kStageBytes, Cfg::kStageBytes, &full[st], pol);
+            }
+        } else if (pre && lane == 1) {
+            // the digit operand of every unit, written by the preceding
+            // wide_digits launch: read only after the dependency wait
+            if (!p.independent) pdl_wait();
+            constexpr uint32_t kBBytes = wide_lbo(NB) * 8;
+            for (int i = 0; i < nunits; ++i) {
+                const int sl = i % kWideSlots;
+                if (i >= kWideSlots) {
+                    if (!mbar_wait(&s_free[sl], (uint32_t)((i / kWideSlots) - 1) & 1u, p.err)) break;
+                }
+                mbar_arrive_expect_tx(&b_ready[sl], kBBytes);
+                bulk_g2s(xbuf + (size_t)sl * kBBytes, p.bimg + (size_t)(s0 + i) * kBBytes, kBBytes, &b_ready[sl]);
             }
         }
     } else {
@@ -344,6 +359,16 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 for (int k = ctid; k < L.K; k += 256) p.resid[(size_t)(m0 + m) * p.ld_src + k] = sr[k];
             }
         }
+        // rows are read as float4 when K and the row stride allow it
+        const bool v4 = (L.K % 4 == 0) && (embed || p.ld_src % 4 == 0);
+        if (pre) {
+            // exponents from wide_digits (one per row over the whole K)
+            if (ctid < MB) {
+                rowinv[ctid] = 1.0f;
+                rowex[ctid] = ctid < Mloc ? p.rowex_g[m0 + ctid] : 0;
+            }
+            named_bar_sync(1, 256);
+        } else {
         // Tensor.swift:1538-1558: ss = sum x^2; inv = 1 / sqrt(ss/H + eps).  The
         // INT8 path also needs max |x| over this CTA's k range (digit scale).
         // One pass over the source, rows in parallel (WPR warps per row, each a
@@ -351,8 +376,6 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         // range staged into shared memory (zero past K), so the digit pass
         // reads no global memory.  Per-row 1/rms and digit exponents go to
         // shared memory (rowinv, rowex).
-        // rows are read as float4 when K and the row stride allow it
-        const bool v4 = (L.K % 4 == 0) && (embed || p.ld_src % 4 == 0);
         const int kq = kspan / 4;  // float4 groups of the staged range
         constexpr int WPR = MB >= 8 ? 1 : 8 / MB;
         constexpr int RS = 8 / WPR;  // rows in flight
@@ -427,6 +450,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             rowex[m] = digit_exponent(__fmul_rn(mx, iv) * 1.0000002f);
         }
         named_bar_sync(1, 256);
+        }
         // four consecutive staged k (g = (k - kbeg) / 4), normalised as the
         // reference does: (x * inv) * w
         auto xval4 = [&](int m, int g) -> float4 {
@@ -470,8 +494,8 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             };
             const float iv = rowinv[m];
             const float dscale = __int_as_float((127 - rowex[m]) << 23);
-            if (nunits > 0) load_unit(0);
-            for (int i = 0; i < nunits; ++i) {
+            if (!pre && nunits > 0) load_unit(0);
+            for (int i = 0; !pre && i < nunits; ++i) {
                 const int sl = i % kWideSlots;
                 int ok = 1;
                 if (lane == 0 && i >= kWideSlots)
@@ -910,6 +934,62 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
     if (P > 1) cluster_sync();
 }
 
+// Digit operand of a wide INT8 GEMV, once per launch: one CTA per batch row
+// runs the GEMV's prologue over the whole K (embedding gather or source row,
+// RMSNorm as Tensor.swift:1538-1558), takes one digit exponent for the row
+// and writes the row's four digit planes into every unit's B image, laid out
+// exactly as the GEMV's shared-memory B slot (so one bulk copy moves it).
+__global__ void __launch_bounds__(256) wide_digits_kernel(const __grid_constant__ GemvParams p) {
+    constexpr int NB = 256;  // tc_nb(64)
+    __shared__ float red[2][8];
+    const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const QLayout& L = p.L;
+    pdl_wait();
+    pdl_launch_dependents();
+    const bool embed = p.prologue == kProEmbed || p.prologue == kProEmbedRms;
+    const bool rms = p.prologue == kProRmsNorm || p.prologue == kProEmbedRms;
+    const float* sr;
+    if (embed) {
+        int tok = p.seq_ro[m].token;
+        if (tok < 0 || tok >= p.vocab) tok = 0;  // the GEMV records the error
+        sr = p.embedding + (size_t)tok * L.K;
+    } else {
+        sr = p.src + (size_t)m * p.ld_src;
+    }
+    float ss = 0.0f;
+    if (rms)
+        for (int k = tid; k < L.K; k += 256) ss = fmaf(sr[k], sr[k], ss);
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[0][warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int w = 0; w < 8; ++w) tot += red[0][w];
+    const float iv = rms ? __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)L.K), p.eps))) : 1.0f;
+    auto xval = [&](int k) -> float {
+        if (k >= L.K) return 0.0f;
+        float a = sr[k];
+        if (rms) a = __fmul_rn(__fmul_rn(a, iv), p.norm_w[k]);
+        return a;
+    };
+    float mx = 0.0f;
+    for (int k = tid; k < L.K; k += 256) mx = fmaxf(mx, fabsf(xval(k)));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[1][warp] = mx;
+    __syncthreads();
+    float bmax = 0.0f;
+    for (int w = 0; w < 8; ++w) bmax = fmaxf(bmax, red[1][w]);
+    const int ex = digit_exponent(bmax);
+    if (tid == 0) p.rowex_g[m] = ex;
+    const float dscale = __int_as_float((127 - ex) << 23);
+    constexpr uint32_t kBBytes = wide_lbo(NB) * 8;
+    for (int q = tid; q < L.Kp / 4; q += 256) {  // 4 consecutive k per step
+        const int k = 4 * q;
+        const float4 a = make_float4(xval(k), xval(k + 1), xval(k + 2), xval(k + 3));
+        put_digits4_strided(p.bimg + (size_t)(k / kTcUnitK) * kBBytes, wide_lbo(NB), kWideSbo, k % kTcUnitK, m, a,
+                            dscale);
+    }
+}
+
 // Staged activation bytes of a CTA: INT8 digits (NB per k); INT4 fp32 x,
 // B slots, per-unit maxima and exponents.
 inline size_t gemv_xbytes(int prec, int mb, const QLayout& L, int P) {
@@ -961,6 +1041,24 @@ cudaError_t launch_t(const GemvParams& p, cudaStream_t stream, bool pdl) {
 }
 
 }  // namespace
+
+bool gemv_uses_wide(int precision, int M) { return gemv_wide(precision, gemv_mb(precision, M)); }
+
+size_t wide_digits_bytes(const QLayout& L) { return (size_t)L.slabs * wide_lbo(tc_nb(64)) * 8; }
+
+cudaError_t launch_wide_digits(const GemvParams& p, cudaStream_t stream, bool pdl) {
+    if (!p.bimg || !p.rowex_g || !gemv_uses_wide(p.L.precision, p.M)) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)p.M);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, wide_digits_kernel, p);
+}
 
 int choose_ksplit(const QLayout& L, int M, int num_sms) {
     if (const char* e = getenv("TB_GEMV_P")) {  // tuning override: a fixed cluster size

@@ -164,10 +164,22 @@ struct GemvParams {
     unsigned int* ar_step;                // step counter (the LM head's last CTA advances it)
     const float* ar_hin;
     float* ar_hout;
+    // Batches over 16 rows (the "wide" INT8 path): when bimg is set, a
+    // preceding wide_digits launch has written the digit operand of every unit
+    // (bimg, wide_digits_bytes) and the rows' digit exponents (rowex_g [M]);
+    // the GEMV then streams B beside A instead of building it per CTA.
+    uint8_t* bimg;
+    int* rowex_g;
 };
 
 // Launch the GEMV described by p on `stream` (PDL + cluster attributes).
 cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream, bool pdl);
+// The digit operand of a wide INT8 GEMV (the GEMV's prologue: embedding
+// gather / RMSNorm, one exponent per row over the whole K), written once per
+// launch for all of its CTAs; p is the GEMV's own parameter block.
+cudaError_t launch_wide_digits(const GemvParams& p, cudaStream_t stream, bool pdl);
+size_t wide_digits_bytes(const QLayout& L);  // bimg bytes for a layout
+bool gemv_uses_wide(int precision, int M);
 // Pick the K-split (cluster size) for a layout and batch.
 int choose_ksplit(const QLayout& L, int M, int num_sms);
 // CTAs of the launch launch_gemv(p) makes.

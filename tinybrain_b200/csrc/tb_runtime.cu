@@ -204,7 +204,7 @@ struct SeqKV {
 
 struct Launch {
     int kind;  // 0 gemv, 1 attention, 3 all-reduce of the residual stream over the tensor-parallel ranks,
-               // 5 sampler
+               // 5 sampler, 6 digit operand of the following wide GEMV (g = that GEMV's parameters)
     GemvParams g;
     AttnParams a;
     SampleParams s;
@@ -250,6 +250,9 @@ struct tb_runner {
     std::vector<Launch> ps_plan;
     cudaGraphExec_t ps_graph = nullptr;
     DevBuf ps_logits, ps_lp, ps_target;
+    // wide GEMVs (batches over 16 rows): the digit operand written once per
+    // launch by a wide_digits launch, shared by the plan's launches in turn
+    DevBuf wide_b, wide_ex;
     int64_t h2d_bytes = 0, d2h_bytes = 0;  // host<->device traffic of the generate paths
     int prompt_stride = 0, max_out = 0;
     // host mirror
@@ -1431,6 +1434,32 @@ static tb_status build_plan_into(tb_runner* r, const PlanIO& io, std::vector<Lau
         ln.bytes = (int64_t)B * c.vocab_size * 4;
         plan.push_back(ln);
     }
+    // Wide GEMVs (over 16 batch rows) without a tensor-parallel pull get their
+    // digit operand from a wide_digits launch right before them.
+    size_t need = 0;
+    for (const Launch& ln : plan)
+        if (ln.kind == 0 && gemv_uses_wide(ln.g.L.precision, ln.g.M) &&
+            !(ln.g.ar_world > 1 && ln.g.ar_pull_slot >= 0))
+            need = std::max(need, wide_digits_bytes(ln.g.L));
+    if (need > 0) {
+        if (r->wide_b.bytes < need) TB_CUDA(r->wide_b.alloc(need));
+        if (r->wide_ex.bytes < (size_t)kMaxGemvBatch * 4) TB_CUDA(r->wide_ex.alloc((size_t)kMaxGemvBatch * 4));
+        std::vector<Launch> out;
+        out.reserve(plan.size() * 2);
+        for (Launch ln : plan) {
+            if (ln.kind == 0 && gemv_uses_wide(ln.g.L.precision, ln.g.M) &&
+            !(ln.g.ar_world > 1 && ln.g.ar_pull_slot >= 0)) {
+                ln.g.bimg = r->wide_b.as<uint8_t>();
+                ln.g.rowex_g = r->wide_ex.as<int>();
+                Launch d = ln;
+                d.kind = 6;
+                d.bytes = (int64_t)ln.g.M * ln.g.L.K * 4 + (int64_t)wide_digits_bytes(ln.g.L);
+                out.push_back(d);
+            }
+            out.push_back(ln);
+        }
+        plan.swap(out);
+    }
     return ok();
 }
 
@@ -1452,6 +1481,11 @@ static tb_status launch_op(tb_runner* r, const Launch& ln, cudaStream_t st, bool
     if (ln.kind == 5) {
         e = launch_sample(ln.s, st, pdl);
         if (e != cudaSuccess) return cuda_fail(e, "launch_sample");
+        return ok();
+    }
+    if (ln.kind == 6) {
+        e = launch_wide_digits(ln.g, st, pdl);
+        if (e != cudaSuccess) return cuda_fail(e, "launch_wide_digits");
         return ok();
     }
     e = ln.kind == 0 ? launch_gemv(ln.g, st, pdl) : launch_attention(ln.a, st, pdl);
