@@ -445,6 +445,11 @@ int choose_nsplit(int M, int Hkv, int max_pages, int num_sms) {
     // context, at least 8 pages per split there, at most one cluster (16) of splits.
     int pairs = M * Hkv;
     int ns = (num_sms + pairs - 1) / pairs;
+    // long contexts: at most ~64 pages per split, so that with many pairs the
+    // longest sequence does not serialise a launch (work then spreads over
+    // more CTAs than SMs, short sequences' splits finishing early)
+    const int balance = (max_pages + 63) / 64;
+    if (ns < balance) ns = balance;
     const int by_pages = (max_pages + 7) / 8;
     if (ns > by_pages) ns = by_pages;
     if (ns > kMaxAttnSplits) ns = kMaxAttnSplits;
