@@ -440,7 +440,7 @@ __global__ void rmsnorm_rows_kernel(const float* h, const float* w, int H, int l
 }  // namespace
 
 
-int choose_nsplit(int M, int Hkv, int max_pages, int num_sms) {
+int choose_nsplit(int M, int Hkv, int max_pages, int num_sms, bool balance_long) {
     // About one CTA per SM over the (sequence, KV head) pairs at the longest
     // context, at least 8 pages per split there, at most one cluster (16) of splits.
     int pairs = M * Hkv;
@@ -449,7 +449,7 @@ int choose_nsplit(int M, int Hkv, int max_pages, int num_sms) {
     // longest sequence does not serialise a launch (work then spreads over
     // more CTAs than SMs, short sequences' splits finishing early)
     const int balance = (max_pages + 63) / 64;
-    if (ns < balance) ns = balance;
+    if (balance_long && ns < balance) ns = balance;
     const int by_pages = (max_pages + 7) / 8;
     if (ns > by_pages) ns = by_pages;
     if (ns > kMaxAttnSplits) ns = kMaxAttnSplits;

@@ -239,7 +239,8 @@ struct AttnParams {
 };
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
 constexpr int kMaxAttnSplits = 16;  // the splits of a (sequence, KV head) form one cluster
-int choose_nsplit(int M, int Hkv, int max_pages, int num_sms);
+// balance: also split long contexts to at most ~64 pages per split
+int choose_nsplit(int M, int Hkv, int max_pages, int num_sms, bool balance = true);
 
 // ----------------------------------------------------------------------------
 // Persistent decode step (batch 1): one cooperative launch per token runs all

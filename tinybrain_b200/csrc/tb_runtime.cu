@@ -2272,7 +2272,10 @@ static tb_status pf_setup(tb_runner* r) {
     TB_CUDA(r->pf_act.alloc((size_t)C * c.intermediate_dim * 4));
     TB_CUDA(r->pf_seq.alloc((size_t)C * sizeof(SeqState)));
     TB_CUDA(r->pf_ptab.alloc((size_t)C * r->ptab_stride * 4));
-    r->pf_nsplit = choose_nsplit(C, c.num_kv_heads, r->ptab_stride, r->ctx->num_sms);
+    // chunks of 64 rows: one split per (row, KV head) pair unless the SMs
+    // would idle (rows of one chunk share their pages, and at short context
+    // extra splits are empty)
+    r->pf_nsplit = choose_nsplit(C, c.num_kv_heads, r->ptab_stride, r->ctx->num_sms, false);
     PlanIO io{C, r->pf_h.as<float>(), r->pf_h.as<float>(), r->pf_q.as<float>(), r->pf_ctx.as<float>(),
               r->pf_act.as<float>(), r->pf_seq.as<SeqState>(), r->pf_ptab.as<int>(), r->pf_nsplit, false, nullptr};
     tb_status e = build_plan_into(r, io, r->pf_plan);
