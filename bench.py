@@ -14,7 +14,9 @@ streams ~1.04 GB of weights, far more than the 126 MB L2, so no flush is needed.
 one token read back per step).  With N > 1 (torchrun) every GPU decodes its own
 sequence: replicas, weak scaling, no collective on the data path.
 `--impl reference` times the reference's CPU algorithm (the oracle restatement,
-reference-faithful mode) on the host cores instead.
+reference-faithful mode) on the host cores instead.  `--config 1..6` selects the
+other BASELINE workloads (6 = the perplexity harness, the only workload with
+published reference numbers).
 """
 import argparse
 import json
