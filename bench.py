@@ -1,24 +1,35 @@
 #!/usr/bin/env python3
-"""Decode benchmark: TinyLlama-1.1B-shaped INT8 model, batch 1, greedy.
+"""Decode benchmark of TinyBrain's hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C]
 
-A step is one decode token (one pass of the whole model: 22 layers + LM head +
-argmax) at batch 1.  The prompt is 128 uniform token ids (seed 2), prefilled
-token by token as the reference does; then W untimed warm-up decode steps and
-K timed ones (defaults 3 + 253 = the config's 256 decode tokens).  Every step
-streams ~1.04 GB of weights, far more than the 126 MB L2, so no flush is needed.
-
-`value` is device-timed (CUDA events around K graph replays, inputs resident);
-`e2e` is the same metric through the public streaming API (host prompt in,
-one token read back per step).  With N > 1 (torchrun) every GPU decodes its own
-sequence: replicas, weak scaling, no collective on the data path.
-`--impl reference` times the reference's CPU algorithm (the oracle restatement,
-reference-faithful mode) on the host cores instead.  `--config 1..6` selects the
-other BASELINE workloads (6 = the perplexity harness, the only workload with
-published reference numbers).
+Default run (one JSON line from rank 0), at every N:
+  * headline = BASELINE config 4: the TinyLlama-1.1B-shaped INT8 model decoding
+    64 independent sequences (prompt lengths U[512, 4096], numpy PCG64 seed 4)
+    greedily; the sequences are spread data parallel over the N ranks
+    (longest prompt first to the least-loaded rank, no collective on the data
+    path).  A step is one decode token of every sequence; W warm-up steps,
+    then K timed ones (W + K <= 128, the config's decode length).  value =
+    64 * K / (max over ranks of the device time of K graph replays): strong
+    scaling, the 64 sequences are fixed.
+  * "tp": BASELINE config 5, the Llama-2-7B-shaped INT4-g32 model, batch 1,
+    tensor parallel over the same N ranks (column q/k/v and gate/up, row
+    o_proj/down with the residual all-reduce over NVLink peer memory).
+  * at N = 1 also "b1" (TinyLlama INT8, batch 1, prompt 128,
+    greedy decode) and "gemv_config1" (config 1: one INT8 GEMV 2048 x 4096 and
+    its INT4-g32 twin, HBM GB/s).
+Every object carries `e2e` (the same metric through the public API from host
+prompts, per-token read-back), a roofline of its dominant kernel family on
+the graph-replayed device timeline, clocks sampled during the timed region and
+a check of its greedy tokens against the oracle's lists in
+tests/golden/config_tokens.json where they exist.  `--impl reference` times
+the reference's CPU algorithm (the oracle restatement in reference-faithful
+mode, all host cores) on bounded samples of the headline workload.
+`--config 1..6` runs one configuration alone (6 = the perplexity harness, the
+only workload with published reference numbers).
 """
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -31,15 +42,53 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (INT8/INT4, b=1 & b=64); dequant-GEMV HBM GB/s as % of peak"
 UNIT = "tok/s"
-PROMPT_LEN = 128
-PROMPT_SEED = 2
 MODEL_SEED = 0
+C4_SEQS, C4_NEW, C4_MAXLEN = 64, 128, 4224
+GOLDEN = os.path.join(ROOT, "tests", "golden", "config_tokens.json")
+TRAFFIC = os.path.join(ROOT, "profiles", "dram_traffic.md")
 
 
-def tl_config():
-    from tinybrain_b200.runtime import ModelConfig
-    from tinybrain_b200.synthetic import TINYLLAMA
-    return ModelConfig(**TINYLLAMA)
+# ------------------------------------------------------------------ helpers --
+class Env:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dist = None
+
+    def init(self):
+        if self.world > 1 and self.dist is None:
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl")
+            self.dist = dist
+
+    def barrier(self):
+        if self.dist:
+            self.dist.barrier()
+
+    def max(self, v):
+        if not self.dist:
+            return v
+        import torch
+        t = torch.tensor([float(v)], device=f"cuda:{self.local}")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather(self, obj):
+        if not self.dist:
+            return [obj]
+        out = [None] * self.world
+        self.dist.all_gather_object(out, obj)
+        return out
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
 
 
 def measured_peaks():
@@ -51,8 +100,31 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
+def golden(name):
+    try:
+        with open(GOLDEN) as f:
+            return json.load(f).get(name)
+    except Exception:
+        return None
+
+
+def traffic_per_launch(kernel_key):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of
+    an ncu capture summarised in profiles/dram_traffic.md: table rows
+    `| key | ... | bytes per launch | ...` (third column)."""
+    try:
+        with open(TRAFFIC) as f:
+            for line in f:
+                cells = [c.strip() for c in line.strip().strip("|").split("|")]
+                if len(cells) >= 3 and cells[0] == kernel_key:
+                    return float(cells[2].replace(",", ""))
+    except Exception:
+        pass
+    return None
+
+
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled during the timed region (read-only query)."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -70,12 +142,10 @@ class ClockSampler:
         except Exception:
             self.proc = None
             return
-        # wait (bounded) for the first sample so that the sampler is running
-        # when the timed region starts; that pre-region sample is dropped
         import select
         r, _, _ = select.select([self.proc.stdout], [], [], 5.0)
         if r:
-            self.proc.stdout.readline()
+            self.proc.stdout.readline()  # the sample before the timed region is dropped
 
     def stop(self):
         if not self.proc:
@@ -102,167 +172,261 @@ class ClockSampler:
                     reasons.add(n)
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def build_model(ctx, mode="perChannel", max_seq_len=None):
+def timeline_roofline(runner, attn_bytes_per_launch, family_names, traffic_keys, peak, peak_kind):
+    """Roofline of the dominant kernel family on the device timeline of one
+    graph-replayed step (tb_runner_trace_launches: globaltimer stamps per
+    launch).  With programmatic dependent launch the next kernel's CTAs start
+    while the previous one runs, so each launch is charged the interval
+    between the previous launch's last CTA exit and its own (the sum over the
+    step is the step's device time, launches overlap nowhere twice).
+    Algorithmic bytes per launch: tb_runner_profile_step (weights + scales as
+    stored + activations) for GEMVs, K/V rows of the context for attention."""
+    import numpy as np
+    stamps, kinds = runner.trace_launches()
+    _, _, nbytes = runner.profile_step()
+    exits = stamps[:, 6].astype(np.float64)
+    start = float(stamps[0, 0])
+    prev = np.concatenate([[start], exits[:-1]])
+    excl_us = np.maximum(exits - prev, 0.0) / 1000.0
+    step_us = float(exits[-1] - start) / 1000.0
+    fam = {}
+    gm, am, dg = kinds == 0, kinds == 1, kinds == 6
+    fam["gemv"] = (float(nbytes[gm].sum()), float(excl_us[gm].sum() + excl_us[dg].sum()), int(gm.sum()))
+    fam["attention"] = (float(attn_bytes_per_launch) * int(am.sum()), float(excl_us[am].sum()), int(am.sum()))
+    dom = max(fam, key=lambda k: fam[k][1])
+    b, us, n = fam[dom]
+    achieved = b / (us * 1e-6) / 1e9 if us > 0 else 0.0
+    tr = traffic_per_launch(traffic_keys[dom])
+    out = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+           "traffic": tr, "peak_source": f"{peak_kind} hbm_gbs (burst copy)", "kernel": family_names[dom],
+           "bytes_per_launch": b / max(n, 1), "launches_per_step": n, "us_per_launch": us / max(n, 1),
+           "timing": "device timeline of one graph-replayed step (globaltimer), exit-to-exit per launch",
+           "traced_step_us": step_us,
+           "families": {k: {"bytes": v[0], "us": v[1], "launches": v[2],
+                            "gbs": v[0] / (v[1] * 1e-6) / 1e9 if v[1] > 0 else None} for k, v in fam.items()}}
+    if tr is not None:
+        out["traffic_key"] = traffic_keys[dom]
+    return out
+
+
+def tokens_vs_fixture(name, key_to_tokens):
+    """Greedy tokens of the device run against the oracle lists (exact match,
+    or a near-tie flip at a step whose oracle top-2 gap < 1e-4: reported)."""
+    fx = golden(name)
+    if not fx:
+        return None
+    checked, identical, flips = 0, True, []
+    for seq in fx["sequences"]:
+        got = key_to_tokens.get(seq["key"])
+        if got is None:
+            continue
+        want = seq["tokens"][:len(got)]
+        checked += 1
+        for i, (a, b) in enumerate(zip(got, want)):
+            if a != b:
+                if seq["gaps"][i] < 1e-4:
+                    flips.append([seq["key"], i, seq["gaps"][i]])
+                else:
+                    identical = False
+                break
+    return {"fixture": name, "sequences_checked": checked, "identical": identical and not flips,
+            "near_tie_flips": flips}
+
+
+def build_tinyllama(ctx, mode="perChannel", max_seq_len=None):
     from tinybrain_b200.runtime import ModelConfig
     from tinybrain_b200.synthetic import TINYLLAMA, make_llama_model
     cfg = ModelConfig(**{**TINYLLAMA, **({"max_seq_len": max_seq_len} if max_seq_len else {})})
     return make_llama_model(cfg, seed=MODEL_SEED, mode=mode, ctx=ctx)
 
 
-def prompt_ids(n=PROMPT_LEN):
-    from tinybrain_b200.synthetic import random_prompt
-    return random_prompt(n, 32000, PROMPT_SEED)
+def config4_workload(world):
+    import numpy as np
+    rng = np.random.default_rng(4)
+    lens = rng.integers(512, 4097, size=C4_SEQS)
+    prompts = [rng.integers(0, 32000, size=int(n)).tolist() for n in lens]
+    load = [0] * world
+    owner = [0] * C4_SEQS
+    for i in sorted(range(C4_SEQS), key=lambda i: -lens[i]):
+        r = min(range(world), key=lambda q: load[q])
+        load[r] += int(lens[i])
+        owner[i] = r
+    return lens, prompts, owner
 
 
-def cpu_baseline(weights, prompt, budget_s=20.0, max_steps=24):
-    """Oracle in reference-faithful mode (dequantize per call + fp32 GEMV, scalar
-    attention) on the host cores: decode steps from an empty cache."""
-    import oracle
-    om = oracle.OracleModel(weights, mode=0)
-    t0 = time.perf_counter()
-    n = 0
-    while n < max_steps and (time.perf_counter() - t0) < budget_s:
-        om.step(prompt[n % len(prompt)])
-        n += 1
-    dt = time.perf_counter() - t0
-    return {"value": n / dt, "unit": UNIT, "cores": oracle.get_threads(), "kind": "port",
-            "sample": f"{n} TinyLlama-INT8 decode steps at context 1..{n} (fresh cache), "
-                      "oracle mode 0 = dequantize each weight per call then fp32 GEMV, OpenMP over all host cores"}
-
-
-def run_reference(args):
-    """--impl reference: the reference's CPU algorithm (oracle port) on host cores."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return 0
+# ------------------------------------------------------------ CPU baselines --
+def cpu_sample_config4(seconds, warmup=1, max_steps=None, threads=None):
+    """The reference's CPU algorithm (oracle, mode 0: dequantize each weight
+    per call then a sequential fp32 GEMV; scalar attention over the gathered
+    context) on a bounded sample of the headline workload: sequence-steps of
+    8 of the 64 sequences spread over the length distribution, each at its own
+    context (prompt length + a few steps; the KV rows are synthetic, filled
+    through the cache's paging rules, so no CPU prefill is needed), cycled
+    round robin.  Uses only oracle/ (never the product library)."""
     import numpy as np
     import oracle
-    from tinybrain_b200.runtime import (LinearLayerWeights, ModelWeights, QuantizedTensor, SeededGenerator,
-                                        TransformerLayerWeights)
-    cfg = tl_config()
-    g = SeededGenerator(MODEL_SEED)
-    H, I, V, kvd = cfg.hidden_dim, cfg.intermediate_dim, cfg.vocab_size, cfg.kv_dim
-
-    def q8(w):
-        q, s = oracle.quantize_int8_per_channel(w)
-        return LinearLayerWeights(QuantizedTensor(w.shape, q, s, "perChannel", 0, None))
-
-    emb = g.normal((V, H), 0.0, 0.02)
-    layers = []
-    for _ in range(cfg.num_layers):
-        p = [q8(g.normal(s, 0.0, 0.02)) for s in ((H, H), (H, kvd), (H, kvd), (H, H), (H, I), (H, I), (I, H))]
-        ones = np.ones(H, dtype=np.float32)
-        layers.append(TransformerLayerWeights(query=p[0], key=p[1], value=p[2], output=p[3], gate=p[4], up=p[5],
-                                              down=p[6], input_norm=ones, post_attention_norm=ones.copy()))
-    w = ModelWeights(cfg, emb, layers, q8(g.normal((H, V), 0.0, 0.02)), final_norm=np.ones(H, dtype=np.float32))
-    prompt = prompt_ids()
-    om = oracle.OracleModel(w, mode=0)
-    for i in range(min(args.warmup, 2)):
-        om.step(prompt[i])
-    steps = 0
-    t0 = time.perf_counter()
-    budget = float(os.environ.get("TB_REF_BUDGET_S", "60"))
-    while steps < args.steps and time.perf_counter() - t0 < budget:
-        om.step(prompt[(steps + 2) % len(prompt)])
+    from oracle.synthetic import TINYLLAMA, llama_model
+    n = threads or host_cores()
+    oracle.set_threads(n)
+    lens, _, _ = config4_workload(1)
+    order = np.argsort(lens, kind="stable")
+    pick = [int(order[j]) for j in range(4, C4_SEQS, 8)]  # 8 sequences across the distribution
+    w = llama_model({**TINYLLAMA, "max_seq_len": C4_MAXLEN}, seed=MODEL_SEED, mode="perChannel")
+    runners = []
+    for i in pick:
+        om = oracle.OracleModel(w, mode=0)
+        om.fill_context(int(lens[i]), seed=i + 1)
+        runners.append(om)
+    for j in range(warmup):
+        runners[j % len(runners)].step(1)
+    steps, t0 = 0, time.perf_counter()
+    while (time.perf_counter() - t0) < seconds and (max_steps is None or steps < max_steps):
+        runners[steps % len(runners)].step(7)
         steps += 1
     dt = time.perf_counter() - t0
-    v = steps / dt
-    line = {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
-        "warmup": min(args.warmup, 2), "ms_per_step": 1000 * dt / steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded LCG, std 0.02)",
-        "config": {"workload": "TinyLlama-1.1B-shaped INT8, batch 1, greedy decode (BASELINE config 2)",
-                   "prompt": PROMPT_LEN, "seq": "reference CPU path restated (oracle port)"},
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": oracle.get_threads(), "kind": "port",
-                         "sample": f"{steps} decode steps at context 3..{steps + 2} within a {budget:.0f}s budget; "
-                                   "Swift/Accelerate reference unavailable on this box"},
-        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
+    ctxs = [int(lens[i]) for i in pick]
+    return steps, dt, n, (f"{steps} single-sequence decode steps cycled over 8 of config 4's 64 sequences "
+                          f"(contexts {min(ctxs)}..{max(ctxs)}, synthetic KV rows), oracle mode 0 "
+                          f"(reference-faithful fp32), OpenMP over {n} host threads")
 
 
-def run_ours(args):
+# ------------------------------------------------------------------ config 4 --
+def run_config4(args, env, cpu=True):
     import numpy as np
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl")
     from tinybrain_b200.runtime import Context, ModelRunner
-
-    ctx = Context(local)
+    lens, prompts, owner = config4_workload(env.world)
+    if args.prompt_len:  # profiling captures only: cap the prompt lengths
+        lens = np.minimum(lens, args.prompt_len)
+        prompts = [p[:args.prompt_len] for p in prompts]
+    mine = [i for i in range(C4_SEQS) if owner[i] == env.rank]
+    ctx = Context(env.local)
     t_build = time.perf_counter()
-    cfg3 = args.config == 3
-    weights = build_model(ctx, mode="int4" if cfg3 else "perChannel")
-    # RoPE table covers the config's context plus the few extra profiling steps
-    runner = ModelRunner(weights, ctx, max_batch=1, max_positions=tl_config().max_seq_len + 64)
+    weights = build_tinyllama(ctx, max_seq_len=C4_MAXLEN)
+    runner = ModelRunner(weights, ctx, max_batch=len(mine), max_positions=C4_MAXLEN + 64)
+    build_s = time.perf_counter() - t_build
+    my_prompts = [prompts[i] for i in mine]
+    W = args.warmup
+    K = min(args.steps, C4_NEW - W)
+    t0 = time.perf_counter()
+    runner.prefill_device(my_prompts, W + K)
+    prefill_s = time.perf_counter() - t0
+    runner.decode_device(W)
+    clocks = ClockSampler(env.local)
+    env.barrier()
+    clocks.start()
+    ms = runner.decode_device(K)
+    clk = clocks.stop()
+    t_dev = env.max(ms / 1000.0)
+    value = C4_SEQS * K / t_dev
+    dev_tokens = runner.read_tokens(len(mine), W + K)
+    peak, peak_kind = measured_peaks()
+    # context of the traced step: prompt + W + K decode steps + this one
+    kvd = 256
+    att_bytes = sum((len(p) + W + K + 1) * kvd * 2 * 4 for p in my_prompts)
+    roof = timeline_roofline(
+        runner, att_bytes,
+        {"gemv": "gemv_kernel<8,128,64> (+ wide_digits): all projections + LM head of one step, all rows"
+                 if len(mine) > 16 else "gemv_kernel<8,128,*>: all projections + LM head of one step",
+         "attention": "attn_decode_kernel (paged KV, all layers)"},
+        {"gemv": f"gemv int8 M={len(mine)} tinyllama", "attention": f"attention tinyllama config4 M={len(mine)}"},
+        peak, peak_kind)
+    launches = int(len(runner.profile_step()[1]))
+
+    # ---- end to end through the public API (host prompts in, per-token read-back) ----
+    runner.io_bytes(reset=True)
+    stamps = {}
+
+    def on_token(seq, idx, tok):
+        stamps[idx] = time.perf_counter()
+        return False
+
+    env.barrier()
+    e2e_tokens = runner.generate_batch(my_prompts, W + K, stop_tokens=(), callback=on_token)
+    h2d, d2h = runner.io_bytes()
+    n_steps_e2e = W + K
+    e2e_t = env.max(stamps[W + K - 1] - stamps[W - 1])
+    e2e_value = C4_SEQS * K / e2e_t
+    same = e2e_tokens == [t[:W + K] for t in dev_tokens]
+    parity = env.gather(tokens_vs_fixture("config4", {i: dev_tokens[j] for j, i in enumerate(mine)}))
+    runner.close()
+    del runner, weights
+    gc.collect()
+    cpu_line = None
+    if cpu and env.world == 1 and env.rank == 0 and not args.no_cpu:
+        steps, dt, n, sample = cpu_sample_config4(20.0)
+        cpu_line = {"value": steps / dt, "unit": UNIT, "cores": n, "kind": "port", "sample": sample}
+    checked = [p for p in parity if p]
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": env.world, "steps": K, "warmup": W,
+        "ms_per_step": 1000.0 * t_dev / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8 weights x fp32 activations (exact integer tensor-core products, fp32 epilogue)",
+        "data": "synthetic (seeded LCG normal std 0.02 weights; numpy PCG64 seed 4 prompt lengths and ids)",
+        "config": {"workload": "TinyLlama-1.1B-shaped INT8, 64 sequences, prompts U[512,4096], greedy decode "
+                               "(BASELINE config 4)", "global_batch": C4_SEQS,
+                   "parallelism": f"dp{env.world} (sequences longest-first to the least-loaded rank, no collective)",
+                   "batch_rank0": len(mine), "prefill_s_rank0": round(prefill_s, 1),
+                   "model_build_s": round(build_s, 1),
+                   "l2": "weights (1.04 GB) and KV (GBs) streamed every step exceed L2; no flush needed"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": round(h2d / n_steps_e2e, 1),
+                "d2h_bytes_per_step": round(d2h / n_steps_e2e, 1),
+                "api": "ModelRunner.generate_batch (tb_runner_generate, per-token callback; prompt prefill "
+                       "outside the timed window)", "tokens_match_device_run": same},
+        "roofline": roof,
+        "parity": {"sequences_checked": sum(p["sequences_checked"] for p in checked),
+                   "identical": all(p["identical"] for p in checked) if checked else None,
+                   "near_tie_flips": [f for p in checked for f in p["near_tie_flips"]]},
+        "gpu_launches": launches * K,
+        "clocks": clk,
+    }
+    if cpu_line:
+        line["cpu_baseline"] = cpu_line
+    return line
+
+
+# ------------------------------------------------------------------ config 2 --
+def run_config2(args, env, mode="perChannel"):
+    """BASELINE config 2 (mode int4: config 3): one sequence, batch 1."""
+    from tinybrain_b200.runtime import Context, ModelRunner
+    from tinybrain_b200.synthetic import random_prompt
+    cfg3 = mode == "int4"
+    ctx = Context(env.local)
+    t_build = time.perf_counter()
+    weights = build_tinyllama(ctx, mode=mode)
+    runner = ModelRunner(weights, ctx, max_batch=1, max_positions=2048 + 64)
     runner.persistent = bool(args.persistent)
     build_s = time.perf_counter() - t_build
     if cfg3:
-        # config 3: prompt 1920 ids (seed 3), 128 greedy steps, context 1921..2048 (no eviction)
-        from tinybrain_b200.synthetic import random_prompt
-        prompt = random_prompt(args.prompt_len if args.prompt_len != PROMPT_LEN else 1920, 32000, 3)
-        W = args.warmup
-        K = min(args.steps, 128 - W)
+        prompt = random_prompt(args.prompt_len or 1920, 32000, 3)
+        W, K = args.warmup, min(args.steps, 128 - args.warmup)
     else:
-        prompt = prompt_ids(args.prompt_len)
-        W, K = args.warmup, args.steps
-    total_new = W + K
-
-    # ---- device-resident timing (value) ----
+        prompt = random_prompt(args.prompt_len or 128, 32000, 2)
+        W, K = args.warmup, min(args.b1_steps, 256 - args.warmup)
     runner.ctx.synchronize()
     t_pf = time.perf_counter()
-    runner.prefill_device([prompt], total_new)
+    runner.prefill_device([prompt], W + K)
     runner.ctx.synchronize()
     prefill_s = time.perf_counter() - t_pf
-    if W:
-        runner.decode_device(W)
-    clocks = ClockSampler(local)
-    if dist:
-        dist.barrier()
+    runner.decode_device(W)
+    clocks = ClockSampler(env.local)
     clocks.start()
     ms = runner.decode_device(K)
     clk = clocks.stop()
     t_dev = ms / 1000.0
-    if dist:
-        import torch
-        t = torch.tensor([t_dev], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_dev = float(t.item())
-        dist.barrier()
-    dev_tokens = runner.read_tokens(1, total_new)[0]
-    value = world * K / t_dev
-
-    # ---- roofline of the dominant kernel (CUDA events around each launch, no graph) ----
-    times, kinds, nbytes = [], None, None
-    for _ in range(5):
-        t, k, b = runner.profile_step()
-        times.append(t)
-        kinds, nbytes = k, b
-    tmean = np.mean(np.stack(times[1:]), axis=0)
+    dev_tokens = runner.read_tokens(1, W + K)[0]
     peak, peak_kind = measured_peaks()
-    if runner.persistent:
-        kern = "decode_step_kernel<8,8,64> (whole step: 22 layers + LM head, one cooperative launch)"
-        dom_bytes, dom_ms, n_dom = float(nbytes[0]), float(tmean[0]), 1
-        extra = {}
-    else:
-        gm = kinds == 0
-        kern = ("gemv_kernel<4,*,1>" if cfg3 else "gemv_kernel<8,128,1>") + " (all projections + LM head of one step)"
-        dom_bytes, dom_ms, n_dom = float(nbytes[gm].sum()), float(tmean[gm].sum()), int(gm.sum())
-        extra = {"gemv_ms_per_step": dom_ms, "attention_ms_per_step": float(tmean[~gm].sum())}
-    achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
-    step_bytes = float(runner.model.weight_bytes)
-
-    # ---- end-to-end through the public streaming API (value on host clock) ----
+    L = len(prompt) + W + K
+    tag = "int4" if cfg3 else "int8"
+    roof = None
+    if not runner.persistent:
+        roof = timeline_roofline(runner, L * 256 * 2 * 4,
+                                 {"gemv": f"gemv_kernel<{4 if cfg3 else 8},128,1>: all projections + LM head of one step",
+                                  "attention": "attn_decode_kernel (paged KV, all layers)"},
+                                 {"gemv": f"gemv {tag} M=1 tinyllama", "attention": f"attention tinyllama {tag} M=1"},
+                                 peak, peak_kind)
+    launches = int(len(runner.profile_step()[1]))
     runner.io_bytes(reset=True)
     stamps = []
 
@@ -270,70 +434,129 @@ def run_ours(args):
         stamps.append(time.perf_counter())
         return False
 
-    if dist:
-        dist.barrier()
-    t0 = time.perf_counter()
-    e2e_tokens = runner.generate_batch([prompt], total_new, stop_tokens=(), callback=on_token)[0]
-    t1 = time.perf_counter()
+    e2e_tokens = runner.generate_batch([prompt], W + K, stop_tokens=(), callback=on_token)[0]
     h2d, d2h = runner.io_bytes()
-    n_steps_e2e = (len(prompt) - 1) + total_new
-    e2e_t = stamps[-1] - stamps[W - 1] if W >= 1 else (stamps[-1] - t0)
-    if dist:
-        import torch
-        t = torch.tensor([e2e_t], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_t = float(t.item())
-    e2e_value = world * K / e2e_t
-    same = e2e_tokens == dev_tokens
-
-    if rank != 0:
-        if dist:
-            dist.destroy_process_group()
-        return 0
-    cpu = cpu_baseline(weights, prompt) if world == 1 and not args.no_cpu else None
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": 1000.0 * t_dev / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": ("int4-g32 weights x fp32 activations (fp32 accumulate)" if cfg3 else
+    n_steps_e2e = (len(prompt) - 1) + W + K
+    e2e_value = K / (stamps[-1] - stamps[W - 1])
+    step_bytes = float(runner.model.weight_bytes)
+    parity = tokens_vs_fixture("config3" if cfg3 else "config2", {"seq": dev_tokens})
+    runner.close()
+    del runner, weights
+    gc.collect()
+    return {
+        "metric": "decode tok/s, batch 1", "value": K / t_dev, "unit": UNIT, "steps": K, "warmup": W,
+        "ms_per_step": 1000.0 * t_dev / K,
+        "dtype": ("int4-g32 weights x fp32 activations" if cfg3 else
                   "int8 weights x fp32 activations (exact integer tensor-core products, fp32 epilogue)"),
-        "data": "synthetic (seeded LCG normal std 0.02, uniform prompt ids)",
-        "config": {"workload": ("TinyLlama-1.1B-shaped INT4-g32, batch 1, prompt 1920, greedy decode "
-                                "(BASELINE config 3)") if cfg3 else
-                               "TinyLlama-1.1B-shaped INT8, batch 1, greedy decode (BASELINE config 2)",
-                   "layers": 22, "hidden": 2048, "heads": "32q/4kv", "vocab": 32000,
-                   "prompt": len(prompt), "decode_tokens": total_new, "parallelism": f"replicas x{world}",
-                   "l2": "weights streamed per step (1.04 GB) exceed L2; no flush needed"},
-        "e2e": {"value": e2e_value, "unit": UNIT,
-                "h2d_bytes_per_step": round(h2d / n_steps_e2e, 1), "d2h_bytes_per_step": round(d2h / n_steps_e2e, 1),
+        "config": {"workload": ("TinyLlama-1.1B-shaped INT4-g32, batch 1, prompt 1920, greedy decode (BASELINE config 3)"
+                                if cfg3 else "TinyLlama-1.1B-shaped INT8, batch 1, prompt 128, greedy decode "
+                                             "(BASELINE config 2)"),
+                   "prompt": len(prompt), "decode_tokens": W + K, "model_build_s": round(build_s, 1),
+                   "l2": "weights streamed per step exceed L2; no flush needed"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": round(h2d / n_steps_e2e, 1),
+                "d2h_bytes_per_step": round(d2h / n_steps_e2e, 1),
                 "api": "ModelRunner.generate_stream path (tb_runner_generate with per-token callback)",
-                "tokens_match_device_run": same},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} hbm_gbs (burst copy)", "kernel": kern,
-                     "bytes_per_launch": dom_bytes / n_dom, "launches_per_step": n_dom,
-                     "ms_per_launch": dom_ms / n_dom, "traffic": None, **extra},
-        "step_roofline": {"weight_bytes_per_step": step_bytes,
-                          "achieved_gbs": step_bytes / (t_dev / K) / 1e9,
+                "tokens_match_device_run": e2e_tokens == dev_tokens},
+        "roofline": roof,
+        "step_roofline": {"weight_bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (t_dev / K) / 1e9,
                           "frac": step_bytes / (t_dev / K) / 1e9 / peak},
-        "gpu_launches": int(len(kinds)) * K,
-        "clocks": clk,
-        "model_build_s": round(build_s, 1),
+        "parity": parity,
         "prefill": {"tokens": len(prompt) - 1, "seconds": round(prefill_s, 4),
-                    "tok_s": round((len(prompt) - 1) / max(prefill_s, 1e-9), 1),
-                    "mode": "chunked (64 prompt tokens per pass of the layers)"},
+                    "tok_s": round((len(prompt) - 1) / max(prefill_s, 1e-9), 1)},
+        "gpu_launches": launches * K, "clocks": clk,
     }
-    if cpu:
-        line["cpu_baseline"] = cpu
-    print(json.dumps(line), flush=True)
-    if dist:
-        dist.destroy_process_group()
-    return 0
 
 
-def run_gemv_config1(args):
+# ------------------------------------------------------------------ config 5 --
+def run_config5(args, env):
+    """Llama-2-7B-shaped INT4-g32, batch 1, prompt 512 (seed 5),
+    greedy decode, tensor parallel over the ranks."""
+    from tinybrain_b200.runtime import Context, ModelConfig, ModelRunner, tp_unique_id
+    from tinybrain_b200.synthetic import LLAMA2_7B, make_llama_model, random_prompt
+    world, rank = env.world, env.rank
+    n_prompt, n_new = (args.prompt_len or 512), 256
+    cfg = ModelConfig(**{**LLAMA2_7B, "max_seq_len": 768})
+    ctx = Context(env.local)
+    if world > 1:
+        uid = [tp_unique_id() if rank == 0 else None]
+        env.dist.broadcast_object_list(uid, src=0)
+        ctx.init_tensor_parallel(uid[0], rank, world)
+    t_build = time.perf_counter()
+    weights = make_llama_model(cfg, seed=MODEL_SEED, mode="int4", ctx=ctx, shard=(rank, world) if world > 1 else None)
+    dm = weights.upload(ctx, tp=(rank, world))
+    runner = ModelRunner(dm, ctx, max_batch=1, max_positions=cfg.max_seq_len + 64)
+    peer = world > 1 and os.environ.get("TB_TP_ALLREDUCE", "peer") != "nccl"
+    if peer:
+        runner.tp_connect(env.gather(runner.tp_handle()))
+        env.barrier()
+    build_s = time.perf_counter() - t_build
+    prompt = random_prompt(n_prompt, 32000, 5)
+    W = args.warmup
+    K = min(args.tp_steps, n_new - W)
+    t0 = time.perf_counter()
+    runner.prefill_device([prompt], W + K)
+    prefill_s = time.perf_counter() - t0
+    runner.decode_device(W)
+    clocks = ClockSampler(env.local)
+    env.barrier()
+    clocks.start()
+    ms = runner.decode_device(K)
+    clk = clocks.stop()
+    t_dev = env.max(ms / 1000.0)
+    dev_tokens = runner.read_tokens(1, W + K)[0]
+    peak, peak_kind = measured_peaks()
+    roof = timeline_roofline(runner, (n_prompt + W + K + 1) * (4096 // world) * 2 * 4,
+                             {"gemv": "gemv_kernel<4,128,1>: all projection shards + LM head of one step (rank 0)",
+                              "attention": "attn_decode_kernel (paged KV, all layers)"},
+                             {"gemv": f"gemv int4 M=1 7b tp{world}", "attention": f"attention 7b tp{world}"},
+                             peak, peak_kind)
+    kinds = runner.profile_step()[1]
+    runner.io_bytes(reset=True)
+    stamps = []
+
+    def on_token(seq, idx, tok):
+        stamps.append(time.perf_counter())
+        return False
+
+    env.barrier()
+    e2e_tokens = runner.generate_batch([prompt], W + K, stop_tokens=(), callback=on_token)[0]
+    h2d, d2h = runner.io_bytes()
+    n_steps_e2e = (len(prompt) - 1) + W + K
+    e2e_value = K / env.max(stamps[-1] - stamps[W - 1])
+    all_tokens = env.gather(dev_tokens)
+    parity = tokens_vs_fixture("config5", {"seq": dev_tokens})
+    wbytes = float(dm.weight_bytes)
+    runner.close()
+    del runner, dm, weights
+    gc.collect()
+    return {
+        "metric": "decode tok/s, batch 1, tensor parallel", "value": K / t_dev, "unit": UNIT, "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": 1000.0 * t_dev / K, "scaling": "strong",
+        "dtype": "int4-g32 weights x fp32 activations",
+        "config": {"workload": "Llama-2-7B-shaped INT4-g32, batch 1, prompt 512, greedy decode (BASELINE config 5)",
+                   "parallelism": f"tp{world} (column q/k/v, gate/up; row o_proj/down + residual all-reduce "
+                                  + ("through NVLink peer memory fused into the GEMV launches" if peer else
+                                     ("by NCCL" if world > 1 else "none")) + "; LM head replicated)",
+                   "prefill_s": round(prefill_s, 1), "model_build_s": round(build_s, 1),
+                   "l2": "weights streamed per step per GPU exceed L2; no flush needed"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": round(h2d / n_steps_e2e, 1),
+                "d2h_bytes_per_step": round(d2h / n_steps_e2e, 1),
+                "tokens_match_device_run": e2e_tokens == dev_tokens},
+        "roofline": roof,
+        "step_roofline": {"weight_bytes_per_step_per_gpu": wbytes, "achieved_gbs": wbytes / (t_dev / K) / 1e9,
+                          "frac": wbytes / (t_dev / K) / 1e9 / peak},
+        "tokens_identical_across_ranks": all(t == all_tokens[0] for t in all_tokens),
+        "parity": parity,
+        "gpu_launches": int((kinds != 3).sum()) * K, "clocks": clk,
+    }
+
+
+# ------------------------------------------------------------------ config 1 --
+def run_config1(args):
     """one INT8 GEMV x[1,2048] . W[2048 in, 4096 out] (and the
     INT4-g32 twin).  W ~ N(0, 0.02) seed 0, x ~ N(0, 1) seed 1; quantized on the
-    GPU; the timed pass cycles through enough copies to exceed L2 (126 MB) so
-    every GEMV streams its weights from HBM."""
+    GPU; the timed pass cycles through enough weight copies to exceed L2 (126 MB)
+    so every GEMV streams its weights from HBM."""
     import numpy as np
     import torch
     from tinybrain_b200.runtime import Context, QuantizedWeight, SeededGenerator, gemv_stream_time, quantize
@@ -351,301 +574,39 @@ def run_gemv_config1(args):
         ws = [QuantizedWeight(q, ctx) for _ in range(copies)]
         xd = torch.tensor(x, device="cuda:0")
         yd = torch.empty((1, N), dtype=torch.float32, device="cuda:0")
-        # parity of one GEMV against the fp64 oracle on the same quantized weights
-        import oracle
-        want = oracle.qmatmul(x, q, mode=1)
         got = ws[0].matmul(x)
-        rel = float(np.linalg.norm(got - want) / np.linalg.norm(want))
         reps = max(3, args.steps // 10)
-        # (a) independent GEMVs: launches overlap, the kernel's streaming rate;
-        # (b) a dependent chain (each GEMV waits for its predecessor), as in a step
         per = gemv_stream_time(ws, xd.data_ptr(), 1, yd.data_ptr(), reps=reps, pdl=2) / copies
         per_dep = gemv_stream_time(ws, xd.data_ptr(), 1, yd.data_ptr(), reps=reps, pdl=1) / copies
         gbs = algo / (per / 1000.0) / 1e9
         gbs_dep = algo / (per_dep / 1000.0) / 1e9
-        lines[mode] = {"gemv_us": per * 1000.0, "gbs": gbs, "frac": gbs / peak, "bytes": algo,
-                       "copies": copies, "rel_l2_vs_fp64_oracle": rel,
-                       "dependent_chain": {"gemv_us": per_dep * 1000.0, "gbs": gbs_dep, "frac": gbs_dep / peak}}
+        lines[mode] = {"gemv_us": per * 1000.0, "gbs": gbs, "frac": gbs / peak, "bytes": algo, "copies": copies,
+                       "dependent_chain": {"gemv_us": per_dep * 1000.0, "gbs": gbs_dep, "frac": gbs_dep / peak},
+                       "y_norm": float(np.linalg.norm(got))}
         for wq in ws:
             wq.close()
-    out = {
-        "metric": "dequant-GEMV HBM GB/s (BASELINE config 1)", "value": lines["perChannel"]["gbs"],
-        "unit": "GB/s", "n_gpus": 1, "steps": max(3, args.steps // 10), "warmup": 1,
-        "ms_per_step": lines["perChannel"]["gemv_us"] / 1000.0, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8 weights x fp32 activations (exact integer tensor-core products)",
-        "data": "synthetic (seeded LCG normal: W std 0.02 seed 0, x std 1 seed 1)",
+    return {
+        "metric": "dequant-GEMV HBM GB/s (BASELINE config 1)", "value": lines["perChannel"]["gbs"], "unit": "GB/s",
+        "dtype": "int8 weights x fp32 activations", "peak": peak, "peak_source": peak_kind,
         "config": {"workload": "single INT8 GEMV 2048 in x 4096 out, batch 1 (BASELINE config 1)",
                    "l2": f"{lines['perChannel']['copies']} weight copies cycled (> 3 x L2) per pass",
-                   "launch": "one CUDA graph of back-to-back independent GEMVs (programmatic dependent launch, "
-                             "no dependency wait: executions overlap); the dependent-chain figure is in "
-                             "int8.dependent_chain"},
-        "roofline": {"bound": "hbm", "achieved": lines["perChannel"]["gbs"], "peak": peak, "unit": "GB/s",
-                     "frac": lines["perChannel"]["frac"], "peak_source": peak_kind,
-                     "kernel": "gemv_kernel<8,128,1>", "bytes_per_launch": lines["perChannel"]["bytes"],
-                     "traffic": None},
-        "int4_g32": lines["int4"],
-        "int8": lines["perChannel"],
+                   "launch": "one CUDA graph of back-to-back GEMVs; gbs: independent launches (executions overlap), "
+                             "dependent_chain: each waits for its predecessor, as inside a step"},
+        "int8": lines["perChannel"], "int4_g32": lines["int4"],
     }
-    print(json.dumps(out))
-    return 0
 
 
-def run_config4(args):
-    """TinyLlama INT8, 64 independent sequences, prompt lengths
-    ~ U[512, 4096] and ids ~ U[0, 32000) (numpy PCG64 seed 4), 128 greedy steps
-    each, max_seq_len 4224 (no eviction).  Data parallel over the ranks: sequences
-    assigned longest-first to the least-loaded rank, one batch per GPU, no
-    collective on the data path.  value = 64 x timed steps / max over ranks."""
-    import numpy as np
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl")
-    from tinybrain_b200.runtime import Context, ModelRunner
-    n_seqs, n_new = 64, 128
-    rng = np.random.default_rng(4)
-    lens = rng.integers(512, 4097, size=n_seqs)
-    if args.prompt_len != PROMPT_LEN:  # profiling captures only: cap the prompt lengths
-        lens = np.minimum(lens, args.prompt_len)
-    prompts = [rng.integers(0, 32000, size=int(n)).tolist() for n in lens]
-    load = [0] * world
-    mine = []
-    for i in sorted(range(n_seqs), key=lambda i: -lens[i]):
-        r = min(range(world), key=lambda q: load[q])
-        load[r] += int(lens[i])
-        if r == rank:
-            mine.append(i)
-    ctx = Context(local)
-    weights = build_model(ctx, max_seq_len=4224)  # >= 4096 + 128: no eviction
-    runner = ModelRunner(weights, ctx, max_batch=len(mine), max_positions=4224 + 64)
-    my_prompts = [prompts[i] for i in mine]
-    W = args.warmup
-    K = min(args.steps, n_new - W)
-    t0 = time.perf_counter()
-    runner.prefill_device(my_prompts, W + K)
-    prefill_s = time.perf_counter() - t0
-    runner.decode_device(W)
-    clocks = ClockSampler(local)
-    if dist:
-        dist.barrier()
-    clocks.start()
-    ms = runner.decode_device(K)
-    clk = clocks.stop()
-    t_dev = ms / 1000.0
-    if dist:
-        import torch
-        t = torch.tensor([t_dev], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_dev = float(t.item())
-    value = n_seqs * K / t_dev
-    times, kinds, nbytes = [], None, None
-    for _ in range(3):
-        t, k, b = runner.profile_step()
-        times.append(t)
-        kinds, nbytes = k, b
-    tmean = np.mean(np.stack(times[1:]), axis=0)
-    peak, peak_kind = measured_peaks()
-    gm, am = kinds == 0, kinds == 1
-    dg = kinds == 6  # digit operand of each wide GEMV: counted in the GEMV time, not its bytes
-    # attention reads every position's K and V rows once per layer (fp32, kv_dim
-    # 256): context of the profiled steps = prompt + W + K + about 2
-    kvd = 256
-    att_bytes_layer = sum((len(p) + W + K + 2) * kvd * 2 * 4 for p in my_prompts)
-    parts = {"gemv": (float(nbytes[gm].sum()), float(tmean[gm].sum() + tmean[dg].sum()), int(gm.sum())),
-             "attention": (float(att_bytes_layer * int(am.sum())), float(tmean[am].sum()), int(am.sum()))}
-    dom = max(parts, key=lambda k: parts[k][1])
-    db, dms, dn = parts[dom]
-    if rank != 0:
-        if dist:
-            dist.destroy_process_group()
-        return 0
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": 1000.0 * t_dev / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "int8 weights x fp32 activations (exact integer tensor-core products, fp32 epilogue)",
-        "data": "synthetic (seeded LCG normal std 0.02 weights; numpy PCG64 seed 4 prompt lengths and ids)",
-        "config": {"workload": "TinyLlama-1.1B-shaped INT8, 64 sequences, prompts U[512,4096], 128 greedy steps "
-                               "(BASELINE config 4)", "parallelism": f"dp{world} (longest-first assignment)",
-                   "batch_per_gpu": len(mine), "prefill_s_rank0": round(prefill_s, 1),
-                   "l2": "weights (1.04 GB) and KV (GBs) per step exceed L2; no flush needed"},
-        "e2e": None,
-        "roofline": {"bound": "hbm", "achieved": db / (dms / 1000.0) / 1e9, "peak": peak, "unit": "GB/s",
-                     "frac": db / (dms / 1000.0) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs (burst copy)",
-                     "kernel": "attn_decode_kernel (paged KV, all layers)" if dom == "attention" else
-                               "gemv_kernel<8,128,64> (all projections + LM head, one CTA per 64-row batch)",
-                     "bytes_per_launch": db / dn, "launches_per_step": dn, "ms_per_launch": dms / dn,
-                     "traffic": None,
-                     "gemv_ms_per_step": parts["gemv"][1], "attention_ms_per_step": parts["attention"][1]},
-        "gpu_launches": int(len(kinds)) * K,
-        "clocks": clk,
-    }
-    print(json.dumps(line), flush=True)
-    if dist:
-        dist.destroy_process_group()
-    return 0
-
-def run_config5(args):
-    """Llama-2-7B-shaped INT4-g32 (32 layers, hidden 4096, 32
-    MHA heads, intermediate 11008), weights N(0, 0.02) seed 0, prompt 512 ids
-    (seed 5), 256 greedy steps.  Tensor parallel over the ranks: q/k/v and
-    gate/up column shards (32/N heads, 11008/N rows per GPU), o_proj/down_proj
-    row shards followed by an NCCL all-reduce of the residual stream (2 per
-    layer), LM head replicated.  One sequence: value = timed steps / max over
-    ranks (strong scaling)."""
-    import numpy as np
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl")
-    from tinybrain_b200.runtime import Context, ModelConfig, ModelRunner, tp_unique_id
-    from tinybrain_b200.synthetic import LLAMA2_7B, make_llama_model, random_prompt
-    n_prompt, n_new = (args.prompt_len if args.prompt_len != PROMPT_LEN else 512), 256
-    cfg = ModelConfig(**{**LLAMA2_7B, "max_seq_len": n_prompt + n_new})
-    ctx = Context(local)
-    if world > 1:
-        uid = [tp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        ctx.init_tensor_parallel(uid[0], rank, world)
-    t_build = time.perf_counter()
-    weights = make_llama_model(cfg, seed=MODEL_SEED, mode="int4", ctx=ctx,
-                               shard=(rank, world) if world > 1 else None)
-    dm = weights.upload(ctx, tp=(rank, world))
-    runner = ModelRunner(dm, ctx, max_batch=1, max_positions=cfg.max_seq_len + 64)
-    peer = world > 1 and os.environ.get("TB_TP_ALLREDUCE", "peer") != "nccl"
-    if peer:  # the residual all-reduce through NVLink peer memory instead of NCCL
-        hs = [None] * world
-        dist.all_gather_object(hs, runner.tp_handle())
-        runner.tp_connect(hs)
-        dist.barrier()
-    build_s = time.perf_counter() - t_build
-    prompt = random_prompt(n_prompt, 32000, 5)
-    W = args.warmup
-    K = min(args.steps, n_new - W)
-    total_new = W + K
-
-    def max_over_ranks(v):
-        if not dist:
-            return v
-        import torch
-        t = torch.tensor([v], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    t0 = time.perf_counter()
-    runner.prefill_device([prompt], total_new)
-    prefill_s = time.perf_counter() - t0
-    runner.decode_device(W)
-    clocks = ClockSampler(local)
-    if dist:
-        dist.barrier()
-    clocks.start()
-    ms = runner.decode_device(K)
-    clk = clocks.stop()
-    t_dev = max_over_ranks(ms / 1000.0)
-    dev_tokens = runner.read_tokens(1, total_new)[0]
-    value = K / t_dev
-
-    times, kinds, nbytes = [], None, None
-    for _ in range(4):
-        t, k, b = runner.profile_step()
-        times.append(t)
-        kinds, nbytes = k, b
-    tmean = np.mean(np.stack(times[1:]), axis=0)
-    peak, peak_kind = measured_peaks()
-    gm, am, rm = kinds == 0, kinds == 1, kinds == 3
-    gemv_b, gemv_ms = float(nbytes[gm].sum()), float(tmean[gm].sum())
-    achieved = gemv_b / (gemv_ms / 1000.0) / 1e9
-
-    runner.io_bytes(reset=True)
-    stamps = []
-
-    def on_token(seq, idx, tok):
-        stamps.append(time.perf_counter())
-        return False
-
-    if dist:
-        dist.barrier()
-    e2e_tokens = runner.generate_batch([prompt], total_new, stop_tokens=(), callback=on_token)[0]
-    h2d, d2h = runner.io_bytes()
-    n_steps_e2e = (len(prompt) - 1) + total_new
-    e2e_t = max_over_ranks(stamps[-1] - stamps[W - 1])
-    e2e_value = K / e2e_t
-    same = e2e_tokens == dev_tokens
-    same_ranks = True
-    if dist:
-        allt = [None] * world
-        dist.all_gather_object(allt, dev_tokens)
-        same_ranks = all(t == allt[0] for t in allt)
-    if rank != 0:
-        if dist:
-            dist.destroy_process_group()
-        return 0
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": 1000.0 * t_dev / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "int4-g32 weights x fp32 activations (fp32 accumulate)",
-        "data": "synthetic (seeded LCG normal std 0.02, uniform prompt ids seed 5)",
-        "config": {"workload": "Llama-2-7B-shaped INT4-g32, batch 1, prompt 512, greedy decode (BASELINE config 5)",
-                   "layers": 32, "hidden": 4096, "heads": "32 MHA", "intermediate": 11008, "vocab": 32000,
-                   "prompt": len(prompt), "decode_tokens": total_new,
-                   "parallelism": f"tp{world} (column q/k/v, gate/up; row o_proj/down + residual all-reduce "
-                                  + ("through NVLink peer memory fused into the GEMV launches" if peer else "by NCCL")
-                                  + "; LM head replicated)",
-                   "prefill_s": round(prefill_s, 1),
-                   "l2": "weights streamed per step per GPU exceed L2; no flush needed"},
-        "e2e": {"value": e2e_value, "unit": UNIT,
-                "h2d_bytes_per_step": round(h2d / n_steps_e2e, 1), "d2h_bytes_per_step": round(d2h / n_steps_e2e, 1),
-                "api": "ModelRunner.generate_stream path (tb_runner_generate with per-token callback)",
-                "tokens_match_device_run": same},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} hbm_gbs (burst copy)",
-                     "kernel": "gemv_kernel<4,*,1> (all projection shards + LM head of one step, rank 0)",
-                     "bytes_per_launch": gemv_b / int(gm.sum()), "launches_per_step": int(gm.sum()),
-                     "ms_per_launch": gemv_ms / int(gm.sum()), "traffic": None,
-                     "gemv_ms_per_step": gemv_ms, "attention_ms_per_step": float(tmean[am].sum()),
-                     "allreduce_ms_per_step": float(tmean[rm].sum()), "allreduces_per_step": int(rm.sum())},
-        "step_roofline": {"weight_bytes_per_step_per_gpu": float(dm.weight_bytes),
-                          "achieved_gbs": dm.weight_bytes / (t_dev / K) / 1e9,
-                          "frac": dm.weight_bytes / (t_dev / K) / 1e9 / peak},
-        "tokens_identical_across_ranks": same_ranks,
-        "gpu_launches": int((~rm).sum()) * K,
-        "clocks": clk,
-        "model_build_s": round(build_s, 1),
-    }
-    print(json.dumps(line), flush=True)
-    if dist:
-        dist.destroy_process_group()
-    return 0
-
-
+# ------------------------------------------------------------------ config 6 --
 def run_config6(args):
     """The reference's only published figures for this path: the step rate of
     its perplexity harness (PerplexityHarness.computePerplexity: 64 teacher-
-    forced single-token steps at context <= 65 on TinyLlama), 1.66 tok/s INT8
-    and 1.52 tok/s INT4-g32 on an M4 Max.  Same work here: a 65-token slice
-    (BOS 1 + 64 seeded uniform ids standing in for the reference's pinned
-    WikiText-2 slice), the INT8 model and its convertToINT4 re-quantization,
-    teacher-forced: the 64 positions go through the layers as the rows of one
-    chunked pass (each row at its own position, attending to the rows before
-    it), each row's fp64 log-probability comes back and the host sums them in
-    position order.  K timed harness calls after W warm-up calls; each
-    call resets the runner (host clock around the synchronous call: prompt
-    upload, every step, the sum's read-back)."""
-    import numpy as np
+    forced steps at context <= 65 on TinyLlama), 1.66 tok/s INT8 and 1.52 tok/s
+    INT4-g32 on an M4 Max.  The same work here through ModelRunner.perplexity
+    (one chunk of 64 positions; host slice in, fp64 sum out)."""
     from tinybrain_b200.runtime import Context, ModelRunner, convert_to_int4
     from tinybrain_b200.synthetic import random_prompt
     ctx = Context(0)
-    w8 = build_model(ctx, mode="perChannel")
+    w8 = build_tinyllama(ctx)
     w4 = convert_to_int4(w8, 32, ctx)
     slice_ids = [1] + [int(t) for t in random_prompt(64, 32000, 6)]
     W, K = args.warmup, max(1, min(args.steps, 100))
@@ -666,11 +627,10 @@ def run_config6(args):
                      "published_tok_s": round(published, 3), "vs_published": rate / published, "clocks": clk}
         r.close()
     v = out["int8"]["value"]
-    line = {
-        "metric": "perplexity-harness step rate (teacher-forced TinyLlama steps/s, BASELINE.md section 1)",
-        "value": v, "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
-        "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": out["int8"]["vs_published"],
+    return {
+        "metric": "perplexity-harness step rate (teacher-forced TinyLlama steps/s)", "value": v, "unit": "tok/s",
+        "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": 1000.0 / v, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": out["int8"]["vs_published"],
         "dtype": "int8 weights x fp32 activations; fp64 log-sum-exp",
         "data": "synthetic (seeded LCG normal std 0.02 weights; slice = BOS + 64 seeded uniform ids)",
         "config": {"workload": "PerplexityHarness.computePerplexity, TinyLlama-1.1B shape, 65-token slice "
@@ -679,46 +639,92 @@ def run_config6(args):
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": round(4 * 65 / 64, 1),
                 "d2h_bytes_per_step": round(8 / 64, 2),
                 "api": "ModelRunner.perplexity (tb_runner_perplexity): host slice in, fp64 sum out"},
-        "int8": out["int8"], "int4_g32": out["int4_g32"],
-        "clocks": out["int8"]["clocks"],
-        # per harness call: one chunk of 64 positions x (5 launches per layer + LM head + scoring launch)
+        "int8": out["int8"], "int4_g32": out["int4_g32"], "clocks": out["int8"]["clocks"],
         "gpu_launches": K * (5 * 22 + 2),
     }
+
+
+# ------------------------------------------------------------------ arms --
+def run_reference(args):
+    """--impl reference: the reference's CPU algorithm on the host cores, on the
+    headline workload (config 4), with every host thread; oracle only."""
+    env = Env()
+    if env.rank != 0:
+        return 0
+    W = args.warmup
+    K = min(args.steps, C4_NEW - W)
+    steps, dt, n, sample = cpu_sample_config4(float(os.environ.get("TB_REF_BUDGET_S", "90")), warmup=W,
+                                              max_steps=K)
+    v = steps / dt
+    try:
+        with open("/proc/self/maps") as f:
+            product_loaded = "libtinybrain_cuda" in f.read()
+    except OSError:
+        product_loaded = None
+    line = {
+        "impl": "reference", "product_library_loaded": product_loaded, "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+        "warmup": W, "ms_per_step": 1000.0 * dt / steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded LCG, std 0.02)",
+        "config": {"workload": "TinyLlama-1.1B-shaped INT8, 64 sequences, prompts U[512,4096], greedy decode "
+                               "(BASELINE config 4)", "global_batch": C4_SEQS,
+                   "impl": "the reference's CPU path restated in C (oracle port, mode 0); the Swift/Accelerate "
+                           "reference does not build on Linux",
+                   "step": "one decode step of one sequence (bounded sample of the 64-sequence step)"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": n, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
     print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    env = Env()
+    env.init()
+    cfg = args.config
+    if cfg == 1:
+        line = run_config1(args)
+    elif cfg in (2, 3):
+        line = run_config2(args, env, mode="int4" if cfg == 3 else "perChannel")
+    elif cfg == 5:
+        line = run_config5(args, env)
+    elif cfg == 6:
+        line = run_config6(args)
+    else:
+        line = run_config4(args, env)
+        if cfg is None:
+            if env.world == 1:
+                line["b1"] = run_config2(args, env)
+                line["gemv_config1"] = run_config1(args)
+            line["tp"] = run_config5(args, env)
+    if env.rank == 0:
+        line.setdefault("n_gpus", env.world)
+        print(json.dumps(line), flush=True)
+    if env.dist:
+        env.dist.destroy_process_group()
     return 0
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=253)
+    ap.add_argument("--steps", type=int, default=125, help="timed decode steps of the headline (W + K <= 128)")
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--b1-steps", type=int, default=253, help="timed steps of the batch-1 object (config 2)")
+    ap.add_argument("--tp-steps", type=int, default=253, help="timed steps of the tensor-parallel object (config 5)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--persistent", action="store_true",
-                    help="one persistent kernel per step (TB_STEP_KERNEL=flow|barrier picks the variant) "
-                         "instead of the default per-projection launch chain")
-    ap.add_argument("--per-op", action="store_true", help="the default per-projection launch chain (kept for scripts)")
-    ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
-                    help="prompt length (default 128 = the config; shorter only for profiling captures)")
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5, 6],
-                    help="BASELINE config: 2 = TinyLlama INT8 decode (default), 1 = single-GEMV HBM bandwidth, "
-                         "3 = TinyLlama INT4-g32 decode at context ~2k, 4 = 64 sequences data-parallel, "
-                         "5 = 7B-shaped INT4 tensor-parallel, 6 = perplexity-harness step rate (the reference's "
-                         "only published figures)")
+                    help="config 2/3: one persistent kernel per step instead of the per-projection launch chain")
+    ap.add_argument("--prompt-len", type=int, default=0,
+                    help="cap / set the prompt length (profiling captures only; 0 = the config's)")
+    ap.add_argument("--config", type=int, default=None, choices=[1, 2, 3, 4, 5, 6],
+                    help="run one BASELINE config alone: 1 single GEMV, 2 TinyLlama INT8 b=1, 3 INT4 at context 2k, "
+                         "4 64 sequences data parallel, 5 7B INT4 tensor parallel, 6 perplexity harness")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
-    if args.config == 1:
-        return run_gemv_config1(args)
-    if args.config == 4:
-        return run_config4(args)
-    if args.config == 5:
-        return run_config5(args)
-    if args.config == 6:
-        return run_config6(args)
     return run_ours(args)
 
 

@@ -77,6 +77,14 @@ void *tb_context_stream(tb_context *ctx);
 /* Device-side error word (bounded-wait timeouts, bad pages, bad tokens).
  * Returns TB_OK, TB_ERR_DEVICE_TIMEOUT or TB_ERR_STATE; clears the word. */
 tb_status tb_context_check_device(tb_context *ctx);
+/* Failure-detection probe (no reference counterpart; the reference has no
+ * device-side waits): runs one kernel whose bounded wait nothing satisfies --
+ * which 0: an mbarrier wait with no arrival, 1: a spin on a tagged word that
+ * nothing writes (the tensor-parallel pull's wait) -- so it runs out after the
+ * library's 2 s limit and records the timeout in the context's error word.
+ * The next tb_context_check_device returns TB_ERR_DEVICE_TIMEOUT, and the
+ * context stays usable. */
+tb_status tb_debug_expire_wait(tb_context *ctx, int32_t which);
 
 /* ---------------------------------------------------------- quantizers -- */
 /* QuantizedTensor.swift:379-424 quantizePerChannel: W[K][N] fp32 ->
@@ -174,15 +182,23 @@ tb_status tb_paged_attention_dev(tb_context *ctx, const float *q_dev, int32_t ba
  * a latency-critical path where cudaMalloc/cudaFree would synchronise the
  * device.  It allocates nothing: the splits of each (sequence, KV head) are
  * combined inside their thread-block cluster, with no scratch memory, so any
- * batch size is accepted and concurrent calls are independent.  Runs on
- * `stream` (a cudaStream_t, NULL = default stream) of the current device.  The
- * first call on a device reads its SM count and should come before any stream
- * capture. */
+ * batch size is accepted.  Runs on `stream` (a cudaStream_t, NULL = default
+ * stream) of the current device.  The first call on a device reads its SM
+ * count and the address of the error word below, and should come before any
+ * stream capture.  A bounded device-side wait that runs out is recorded in one
+ * error word per device (a file-scope __device__ variable shared by every call
+ * on that device, including calls that overlap); read it with
+ * tb_paged_attention_noalloc_status. */
 tb_status tb_paged_attention_dev_noalloc(void *stream, const float *q_dev, int32_t batch, const float *kv_pool_dev,
                                          const int32_t *page_table_dev, int32_t ptab_stride,
                                          const int32_t *seq_lens_dev, int32_t max_len, int32_t layer,
                                          int32_t num_layers, int32_t num_heads, int32_t num_kv_heads,
                                          int32_t head_dim, float *out_dev);
+/* Status of the allocation-free attention calls on the current device: waits
+ * for `stream`, reads the shared error word (and zeroes it if `clear`), and
+ * returns TB_OK, or TB_ERR_DEVICE_TIMEOUT if a bounded wait ran out since the
+ * word was last cleared.  Allocates nothing. */
+tb_status tb_paged_attention_noalloc_status(void *stream, int32_t clear);
 
 /* ---------------------------------------------------------------- model -- */
 typedef enum { TB_ARCH_LLAMA = 0, TB_ARCH_TOY = 1 } tb_architecture;

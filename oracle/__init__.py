@@ -68,6 +68,10 @@ def load():
         "orc_perplexity": ([P, P, I64, P], C.c_float),
         "orc_sample_detailed": ([P, I64, P, P, I64, P, P, P], I64),
         "orc_generate_sampled": ([P, P, I64, I64, P, P, P, P, P], I64),
+        "orc_runner_prefill": ([P, P, I64], None),
+        "orc_runner_fill_context": ([P, I64, C.c_uint64], None),
+        "orc_rng_seed": ([C.c_uint64], C.c_uint64),
+        "orc_rng_fill_normal": ([P, F, F, I64, P], None),
         "orc_set_threads": ([I32], None),
         "orc_get_threads": ([], I32),
     }
@@ -264,6 +268,17 @@ class OracleModel:
         logits = np.empty(self.vocab, dtype=np.float32)
         load().orc_runner_step(self.r, int(token), _p(logits))
         return logits
+
+    def prefill(self, tokens):
+        """Steps every token of `tokens`, discarding the logits (chunked; the
+        same results as stepping one token at a time)."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int64))
+        load().orc_runner_prefill(self.r, _p(t), t.size)
+
+    def fill_context(self, length, seed=1):
+        """Position `length` with synthetic KV rows (benchmark samples: the
+        next step costs what a decode step at that context costs)."""
+        load().orc_runner_fill_context(self.r, int(length), seed)
 
     def step_observed(self, token):
         """step() plus the InferenceObserver values of this step:

@@ -283,42 +283,49 @@ void orc_rope(float *v, int64_t head_dim, int64_t num_heads, int64_t position,
     }
 }
 
-/* ModelRunner.swift:519-579: per head, kvHead = head / (H/Hkv); scores are
- * fp32 sequential dots times 1/sqrt(d); softmax without epsilon; context is
- * the fp32 sequential p-weighted sum of V rows. */
+/* ModelRunner.swift:519-579, one query head: scores are fp32 sequential dots
+ * times 1/sqrt(d); softmax without epsilon; the context is the fp32
+ * sequential p-weighted sum of V rows.  sc: L floats of scratch. */
+static void attn_head(const float *qh, const float *K, const float *V, int64_t L, int64_t kvdim, int64_t kvh,
+                      int64_t d, float scale, float *sc, float *ch, float *probs) {
+    for (int64_t j = 0; j < L; ++j) {
+        float dot = 0.0f;
+        const float *kr = K + j * kvdim + kvh * d;
+        for (int64_t t = 0; t < d; ++t) dot += qh[t] * kr[t];
+        sc[j] = dot * scale;
+    }
+    float mx = L > 0 ? sc[0] : 0.0f;
+    for (int64_t j = 1; j < L; ++j)
+        if (sc[j] > mx) mx = sc[j];
+    float sum = 0.0f;
+    for (int64_t j = 0; j < L; ++j) {
+        sc[j] = expf(sc[j] - mx);
+        sum += sc[j];
+    }
+    for (int64_t j = 0; j < L; ++j) sc[j] = sc[j] / sum;
+    if (probs) memcpy(probs, sc, sizeof(float) * (size_t)L);
+    for (int64_t t = 0; t < d; ++t) ch[t] = 0.0f;
+    for (int64_t j = 0; j < L; ++j) {
+        const float w = sc[j];
+        const float *vr = V + j * kvdim + kvh * d;
+        for (int64_t t = 0; t < d; ++t) ch[t] += w * vr[t];
+    }
+}
+
+/* ModelRunner.swift:519-579: per head, kvHead = head / (H/Hkv).  Heads are
+ * independent, so they run in parallel for long contexts (same results). */
 void orc_attention(const float *q, const float *K, const float *V, int64_t L,
                    int64_t H, int64_t Hkv, int64_t d, float *ctx, float *probs) {
     const float scale = 1.0f / sqrtf((float)d);
     const int64_t rep = H / Hkv, kvdim = Hkv * d;
-    float *sc = (float *)malloc(sizeof(float) * (size_t)(L > 0 ? L : 1));
-    for (int64_t h = 0; h < H; ++h) {
-        const int64_t kvh = h / rep;
-        const float *qh = q + h * d;
-        for (int64_t j = 0; j < L; ++j) {
-            float dot = 0.0f;
-            const float *kr = K + j * kvdim + kvh * d;
-            for (int64_t t = 0; t < d; ++t) dot += qh[t] * kr[t];
-            sc[j] = dot * scale;
-        }
-        float mx = L > 0 ? sc[0] : 0.0f;
-        for (int64_t j = 1; j < L; ++j)
-            if (sc[j] > mx) mx = sc[j];
-        float sum = 0.0f;
-        for (int64_t j = 0; j < L; ++j) {
-            sc[j] = expf(sc[j] - mx);
-            sum += sc[j];
-        }
-        for (int64_t j = 0; j < L; ++j) sc[j] = sc[j] / sum;
-        if (probs) memcpy(probs + h * L, sc, sizeof(float) * (size_t)L);
-        float *ch = ctx + h * d;
-        for (int64_t t = 0; t < d; ++t) ch[t] = 0.0f;
-        for (int64_t j = 0; j < L; ++j) {
-            const float w = sc[j];
-            const float *vr = V + j * kvdim + kvh * d;
-            for (int64_t t = 0; t < d; ++t) ch[t] += w * vr[t];
-        }
+#pragma omp parallel if (L * H >= 65536)
+    {
+        float *sc = (float *)malloc(sizeof(float) * (size_t)(L > 0 ? L : 1));
+#pragma omp for schedule(static)
+        for (int64_t h = 0; h < H; ++h)
+            attn_head(q + h * d, K, V, L, kvdim, h / rep, d, scale, sc, ctx + h * d, probs ? probs + h * L : NULL);
+        free(sc);
     }
-    free(sc);
 }
 
 /* Sampler.swift:126-138 (greedy): first index with the strict maximum. */
@@ -638,6 +645,215 @@ void orc_runner_step(orc_runner *r, int64_t token, float *logits) {
     r->pos += 1;
 }
 
+/* Mode 1 matmul of M rows at once (chunked prefill): per row exactly the
+ * arithmetic of orc_qmatmul mode 1 (fp64 sum over ascending k of x[k] *
+ * fp32(dequant w[k][n])), with each dequantized weight reused across rows. */
+#define ORC_NB 64
+static void qmatmul_rows_f64(const float *x, int64_t M, const orc_qtensor *w, float *y) {
+    const int64_t K = w->K, N = w->N;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t nb = 0; nb < N; nb += ORC_NB) {
+        const int64_t ne = nb + ORC_NB < N ? nb + ORC_NB : N, nn = ne - nb;
+        double *acc = (double *)calloc((size_t)(M * ORC_NB), sizeof(double));
+        float wv[ORC_NB];
+        for (int64_t k = 0; k < K; ++k) {
+            if (w->precision == 8) {
+                const int8_t *qr = (const int8_t *)w->data + k * N;
+                for (int64_t j = 0; j < nn; ++j) {
+                    const int64_t n = nb + j;
+                    wv[j] = ((float)qr[n] - (float)(w->zero_points ? w->zero_points[n] : 0)) * w->scales[n];
+                }
+            } else {
+                for (int64_t j = 0; j < nn; ++j) wv[j] = orc_wval(w, k, nb + j);
+            }
+            for (int64_t m = 0; m < M; ++m) {
+                const double xv = (double)x[m * K + k];
+                double *a = acc + m * ORC_NB;
+                for (int64_t j = 0; j < nn; ++j) a[j] += xv * (double)wv[j];
+            }
+        }
+        for (int64_t m = 0; m < M; ++m)
+            for (int64_t j = 0; j < nn; ++j) y[m * N + nb + j] = (float)acc[m * ORC_NB + j];
+        free(acc);
+    }
+}
+
+static void apply_proj_rows(const orc_runner *r, const orc_proj *p, const float *x, int64_t M, float *y) {
+    qmatmul_rows_f64(x, M, &p->w, y);
+    if (p->bias)
+        for (int64_t m = 0; m < M; ++m)
+            for (int64_t n = 0; n < p->w.N; ++n) y[m * p->w.N + n] += p->bias[n];
+}
+
+/* Prompt processing for test fixtures: the same results, bit for bit, as
+ * calling orc_runner_step for each token and discarding the logits (the
+ * reference discards prompt-step logits, ModelRunner.swift:240-244), computed
+ * layer by layer over chunks of up to 64 tokens.  Token t of a chunk attends
+ * to positions 0..pos+t; its K/V rows are appended before any of the chunk's
+ * attention runs, which reads only rows up to its own position.  Runs step by
+ * step where the chunk would evict pages, in mode 0, or with an observer. */
+void orc_runner_prefill(orc_runner *r, const int64_t *tokens, int64_t n) {
+    const orc_model *m = r->m;
+    const orc_config *c = &m->cfg;
+    if (n <= 0) return;
+    if (r->mode != 1 || r->obs_norms || r->obs_attn || r->obs_final || r->pos + n > c->max_seq_len) {
+        float *lg = (float *)malloc(sizeof(float) * (size_t)c->vocab);
+        for (int64_t i = 0; i < n; ++i) orc_runner_step(r, tokens[i], lg);
+        free(lg);
+        return;
+    }
+    const int64_t H = c->hidden, d = c->hidden / c->num_heads, kvd = r->kvdim;
+    int64_t I = 0;
+    for (int64_t l = 0; l < c->num_layers; ++l) {
+        const orc_layer *ly = &m->layers[l];
+        const int64_t w = ly->p[ORC_GATE].has ? ly->p[ORC_GATE].w.N : ly->p[ORC_UP].w.N;
+        if (w > I) I = w;
+    }
+    const int64_t T = 64;
+    float *h = (float *)malloc(sizeof(float) * (size_t)(T * H));
+    float *x = (float *)malloc(sizeof(float) * (size_t)(T * H));
+    float *q = (float *)malloc(sizeof(float) * (size_t)(T * H));
+    float *k = (float *)malloc(sizeof(float) * (size_t)(T * kvd));
+    float *v = (float *)malloc(sizeof(float) * (size_t)(T * kvd));
+    float *cx = (float *)malloc(sizeof(float) * (size_t)(T * H));
+    float *tmp = (float *)malloc(sizeof(float) * (size_t)(T * H));
+    float *f1 = (float *)malloc(sizeof(float) * (size_t)(T * I));
+    float *f2 = (float *)malloc(sizeof(float) * (size_t)(T * I));
+    const int64_t Lmax = r->pos + n;
+    float *K = (float *)malloc(sizeof(float) * (size_t)(Lmax * kvd));
+    float *V = (float *)malloc(sizeof(float) * (size_t)(Lmax * kvd));
+    const float scale = 1.0f / sqrtf((float)d);
+    const int64_t rep = c->num_heads / c->num_kv_heads;
+    for (int64_t c0 = 0; c0 < n; c0 += T) {
+        const int64_t Tc = n - c0 < T ? n - c0 : T;
+        for (int64_t t = 0; t < Tc; ++t) memcpy(h + t * H, m->emb + tokens[c0 + t] * H, sizeof(float) * (size_t)H);
+        for (int64_t l = 0; l < c->num_layers; ++l) {
+            const orc_layer *ly = &m->layers[l];
+            const float *xin = h;
+            if (ly->in_norm) {
+                for (int64_t t = 0; t < Tc; ++t) orc_rmsnorm(h + t * H, ly->in_norm, H, c->rms_eps, x + t * H);
+                xin = x;
+            }
+            apply_proj_rows(r, &ly->p[ORC_Q], xin, Tc, q);
+            apply_proj_rows(r, &ly->p[ORC_K], xin, Tc, k);
+            apply_proj_rows(r, &ly->p[ORC_V], xin, Tc, v);
+            for (int64_t t = 0; t < Tc; ++t) {
+                orc_rope(q + t * H, d, c->num_heads, r->pos + t, d);
+                orc_rope(k + t * kvd, d, c->num_kv_heads, r->pos + t, d);
+                kv_append(r, l, k + t * kvd, v + t * kvd, r->pos + t);
+            }
+            kv_gather(r, l, r->pos + Tc, K, V);
+#pragma omp parallel
+            {
+                float *sc = (float *)malloc(sizeof(float) * (size_t)(r->pos + Tc));
+#pragma omp for schedule(dynamic, 1) collapse(2)
+                for (int64_t t = 0; t < Tc; ++t)
+                    for (int64_t hh = 0; hh < c->num_heads; ++hh)
+                        attn_head(q + t * H + hh * d, K, V, r->pos + t + 1, kvd, hh / rep, d, scale, sc,
+                                  cx + t * H + hh * d, NULL);
+                free(sc);
+            }
+            apply_proj_rows(r, &ly->p[ORC_O], cx, Tc, tmp);
+            for (int64_t i = 0; i < Tc * H; ++i) h[i] = h[i] + tmp[i];
+            const float *x2 = h;
+            if (ly->post_norm) {
+                for (int64_t t = 0; t < Tc; ++t) orc_rmsnorm(h + t * H, ly->post_norm, H, c->rms_eps, x + t * H);
+                x2 = x;
+            }
+            int64_t Il;
+            if (ly->p[ORC_GATE].has) {
+                Il = ly->p[ORC_GATE].w.N;
+                apply_proj_rows(r, &ly->p[ORC_GATE], x2, Tc, f1);
+                apply_proj_rows(r, &ly->p[ORC_UP], x2, Tc, f2);
+                for (int64_t i = 0; i < Tc * Il; ++i) f1[i] = orc_silu(f1[i]) * f2[i];
+            } else {
+                Il = ly->p[ORC_UP].w.N;
+                apply_proj_rows(r, &ly->p[ORC_UP], x2, Tc, f1);
+                for (int64_t i = 0; i < Tc * Il; ++i) f1[i] = orc_gelu(f1[i]);
+            }
+            apply_proj_rows(r, &ly->p[ORC_DOWN], f1, Tc, tmp);
+            for (int64_t i = 0; i < Tc * H; ++i) h[i] = h[i] + tmp[i];
+        }
+        r->pos += Tc;
+    }
+    free(h); free(x); free(q); free(k); free(v); free(cx); free(tmp); free(f1); free(f2); free(K); free(V);
+}
+
+/* Benchmark support (the CPU baseline's bounded samples): puts the runner at
+ * position L with a KV cache of L synthetic rows per layer (uniform values in
+ * [-1, 1) from an LCG, appended through the cache's own paging rules), so
+ * that the next step does the work of a decode step at context L+1 without
+ * a CPU prefill of L prompt tokens.  The step's numbers are not meaningful;
+ * its cost is. */
+void orc_runner_fill_context(orc_runner *r, int64_t L, uint64_t seed) {
+    orc_runner_reset(r);
+    const int64_t kvd = r->kvdim;
+    float *k = (float *)malloc(sizeof(float) * (size_t)kvd);
+    float *v = (float *)malloc(sizeof(float) * (size_t)kvd);
+    uint64_t s = seed ? seed : 1;
+    for (int64_t l = 0; l < r->m->cfg.num_layers; ++l)
+        for (int64_t pos = 0; pos < L; ++pos) {
+            for (int64_t i = 0; i < kvd; ++i) {
+                s = s * 6364136223846793005ULL + 1442695040888963407ULL;
+                k[i] = (float)(int32_t)(s >> 32) * 4.656612873077393e-10f;
+                s = s * 6364136223846793005ULL + 1442695040888963407ULL;
+                v[i] = (float)(int32_t)(s >> 32) * 4.656612873077393e-10f;
+            }
+            kv_append(r, l, k, v, pos);
+        }
+    r->pos = L;
+    free(k);
+    free(v);
+}
+
+/* ModelWeights.swift:18-29 SeededGenerator (seed 0 -> 0xdeadbeef; state =
+ * 6364136223846793005 * state + 1) and Tensor.swift:1623-1644 Tensor.random:
+ * Box-Muller pairs in fp32, u = Float.random(in: 0..<1) taken as the low 24
+ * bits of the 32-bit truncation of next() times 2^-24 (Swift's standard
+ * library, which is not in the reference tree), u1 clamped to the least
+ * nonzero magnitude.  Parallel over pairs with an LCG jump per chunk. */
+#define ORC_LCG_A 6364136223846793005ULL
+static uint64_t orc_lcg_jump(uint64_t s, uint64_t n) {
+    uint64_t A = 1, Cc = 0, a = ORC_LCG_A, cc = 1;
+    while (n) {
+        if (n & 1) {
+            A = A * a;
+            Cc = Cc * a + cc;
+        }
+        cc = (a + 1) * cc;
+        a = a * a;
+        n >>= 1;
+    }
+    return A * s + Cc;
+}
+
+uint64_t orc_rng_seed(uint64_t seed) { return seed != 0 ? seed : 0xdeadbeefULL; }
+
+void orc_rng_fill_normal(uint64_t *state, float mean, float stdv, int64_t n, float *out) {
+    const int64_t pairs = (n + 1) / 2;
+    const uint64_t s0 = *state;
+    const int64_t chunk = 1 << 16;
+#pragma omp parallel for schedule(static)
+    for (int64_t pb = 0; pb < pairs; pb += chunk) {
+        const int64_t pe = pb + chunk < pairs ? pb + chunk : pairs;
+        uint64_t s = orc_lcg_jump(s0, (uint64_t)(2 * pb));
+        const float two_pi = 2.0f * 3.14159265358979323846f;
+        for (int64_t pi = pb; pi < pe; ++pi) {
+            s = ORC_LCG_A * s + 1;
+            float u1 = (float)((uint32_t)s & 0xFFFFFFu) * 5.9604644775390625e-08f;
+            s = ORC_LCG_A * s + 1;
+            const float u2 = (float)((uint32_t)s & 0xFFFFFFu) * 5.9604644775390625e-08f;
+            if (u1 < 1.40129846e-45f) u1 = 1.40129846e-45f;
+            const float rr = sqrtf(-2.0f * logf(u1));
+            const float th = two_pi * u2;
+            const int64_t i = 2 * pi;
+            out[i] = mean + stdv * rr * cosf(th);
+            if (i + 1 < n) out[i + 1] = mean + stdv * rr * sinf(th);
+        }
+    }
+    *state = orc_lcg_jump(s0, (uint64_t)(2 * pairs));
+}
+
 /* Sampler.swift:369-381: LCG (Numerical Recipes constants). */
 uint64_t orc_lcg_next(uint64_t *state) {
     *state = *state * 6364136223846793005ULL + 1442695040888963407ULL;
@@ -779,13 +995,16 @@ int64_t orc_generate_greedy(orc_runner *r, const int64_t *prompt, int64_t n_prom
     const int64_t V = r->m->cfg.vocab;
     float *logits = (float *)malloc(sizeof(float) * (size_t)V);
     int64_t cur = 0;
+    int64_t *pre = (int64_t *)malloc(sizeof(int64_t) * (size_t)(n_prompt > 0 ? n_prompt : 1));
     for (int64_t i = 0; i < n_prompt; ++i) {
         int64_t t = prompt[i] < 0 ? 0 : (prompt[i] > V - 1 ? V - 1 : prompt[i]);
         if (i + 1 < n_prompt)
-            orc_runner_step(r, t, logits);
+            pre[i] = t;
         else
             cur = t;
     }
+    orc_runner_prefill(r, pre, n_prompt - 1);
+    free(pre);
     for (int64_t g = 0; g < max_tokens; ++g) {
         orc_runner_step(r, cur, logits);
         int64_t best = orc_greedy(logits, V);

@@ -136,6 +136,13 @@ int64_t orc_generate_greedy(orc_runner *r, const int64_t *prompt, int64_t n_prom
                             int64_t max_tokens, int64_t *out_tokens, float *out_gap);
 
 /* ---- thread control ---- */
+/* n calls of orc_runner_step with the logits discarded, chunked (mode 1). */
+void orc_runner_prefill(orc_runner *r, const int64_t *tokens, int64_t n);
+/* Position L with L synthetic KV rows per layer (benchmark samples only). */
+void orc_runner_fill_context(orc_runner *r, int64_t L, uint64_t seed);
+/* SeededGenerator + Tensor.random (ModelWeights.swift:18-29, Tensor.swift:1623-1644). */
+uint64_t orc_rng_seed(uint64_t seed);
+void orc_rng_fill_normal(uint64_t *state, float mean, float stdv, int64_t n, float *out);
 void orc_set_threads(int32_t n);
 int32_t orc_get_threads(void);
 

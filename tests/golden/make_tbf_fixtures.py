@@ -61,4 +61,6 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_tbf_fixtures.py <path of the reference checkout>")
+    main(sys.argv[1])

@@ -1,5 +1,7 @@
 """Shared builders for tests: small seeded models quantized by the oracle (CPU)
 or by the library (GPU), over identical fp32 weights."""
+import warnings
+
 import numpy as np
 
 import oracle
@@ -69,11 +71,46 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def assert_same_tokens(got, want, gaps):
-    """Greedy tokens equal the oracle's; a divergence is accepted only at a step
-    whose oracle top-2 logit gap is below 1e-4 (an fp32 reordering can flip it)."""
-    for i, (a, b) in enumerate(zip(got, want)):
+def teacher_forced(weights, prompt, got, mode=1):
+    """The oracle's greedy choice and top-2 logit gap at every decode step when
+    each step's input is the DEVICE's previous token (teacher forcing on the
+    device's run; the prompt is processed as in ModelRunner.swift:236-244)."""
+    o = oracle.OracleModel(weights, mode=mode)
+    o.prefill([int(t) for t in prompt[:-1]])
+    cur = int(prompt[-1])
+    am, gaps = [], []
+    for tok in got:
+        lg = o.step(cur)
+        b = int(np.argmax(lg))  # first index of the maximum (Sampler.swift:126-138)
+        second = float(np.max(np.delete(lg, b)))
+        am.append(b)
+        gaps.append(float(lg[b]) - second)
+        cur = int(tok)
+    return am, gaps
+
+
+def assert_same_tokens(got, want, gaps, weights=None, prompt=None, teacher=None, tol=1e-4):
+    """Greedy tokens equal the oracle's.  A divergence is tolerated only at a
+    step whose oracle top-2 logit gap is below `tol` (an fp32 reordering can
+    flip such a near-tie); after it, every later device token is checked
+    against the oracle teacher-forced on the device's own tokens (weights +
+    prompt, or a `teacher(got) -> (argmaxes, gaps)` callable), where again only
+    near-ties may differ.  Returns the tolerated flips [(step, gap)], which are
+    also reported as warnings."""
+    assert len(got) == len(want), f"device produced {len(got)} tokens, oracle {len(want)}"
+    first = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
+    if first is None:
+        return []
+    assert gaps[first] < tol, f"token {first}: device {got[first]} vs oracle {want[first]} with top-2 gap {gaps[first]}"
+    if teacher is None:
+        assert weights is not None and prompt is not None, \
+            f"tolerated flip at token {first} (gap {gaps[first]}): the rest needs a teacher-forced check"
+        teacher = lambda g: teacher_forced(weights, prompt, g)  # noqa: E731
+    t_tok, t_gap = teacher(got)
+    flips = []
+    for i, (a, b) in enumerate(zip(got, t_tok)):
         if a != b:
-            assert gaps[i] < 1e-4, f"token {i}: device {a} vs oracle {b} with top-2 gap {gaps[i]}"
-            return
-    assert len(got) == len(want)
+            assert t_gap[i] < tol, f"token {i}: device {a} vs teacher-forced oracle {b}, top-2 gap {t_gap[i]}"
+            flips.append((i, float(t_gap[i])))
+    warnings.warn(f"tolerated greedy near-tie flips (step, oracle top-2 gap): {flips}")
+    return flips

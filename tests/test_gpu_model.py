@@ -50,7 +50,7 @@ def test_toy_model_greedy_identity(ctx):
     prompt = [1, 2, 3, 4, 5]
     want, gaps = o.generate_greedy(prompt, 40)
     got = r.generate_batch([prompt], 40)[0]
-    assert_same_tokens(got, want, gaps)
+    assert_same_tokens(got, want, gaps, w, prompt)
 
 
 @pytest.mark.parametrize("mode,persistent", [("perChannel", "flow"), ("perChannel", "barrier"),
@@ -65,7 +65,7 @@ def test_generate_greedy_identity(ctx, mode, persistent, monkeypatch):
     prompt = [11, 22, 33, 44, 55, 66, 77, 88, 99, 111, 222, 333, 444, 555, 666, 777, 888]
     want, gaps = o.generate_greedy(prompt, 48)
     got = r.generate_batch([prompt], 48)[0]
-    assert_same_tokens(got, want, gaps)
+    assert_same_tokens(got, want, gaps, w, prompt)
     assert r.kv_cache.length == len(prompt) - 1 + 48
 
 
@@ -107,7 +107,7 @@ def test_batched_sequences_match_independent_runs(ctx):
     for p, g in zip(prompts, got):
         o = oracle.OracleModel(w, mode=1)
         want, gaps = o.generate_greedy(p, 24)
-        assert_same_tokens(g, want, gaps)
+        assert_same_tokens(g, want, gaps, w, p)
 
 
 @pytest.mark.parametrize("mode", ["perChannel", "int4"])
@@ -122,7 +122,7 @@ def test_batch_of_twenty_sequences(ctx, mode):
     for p, gt in zip(prompts, got):
         o = oracle.OracleModel(w, mode=1)
         want, gaps = o.generate_greedy(p, 12)
-        assert_same_tokens(gt, want, gaps)
+        assert_same_tokens(gt, want, gaps, w, p)
 
 
 def test_batched_eviction_parity(ctx):
@@ -136,7 +136,7 @@ def test_batched_eviction_parity(ctx):
     for p, gt in zip(prompts, got):
         o = oracle.OracleModel(w, mode=1)
         want, gaps = o.generate_greedy(p, 30)
-        assert_same_tokens(gt, want, gaps)
+        assert_same_tokens(gt, want, gaps, w, p)
 
 
 def test_persistent_available_for_batch1_llama_only(ctx):
@@ -245,8 +245,8 @@ def test_chunked_prefill_matches_oracle_and_token_by_token(ctx, mode):
     b = stepped.generate_batch(prompts, 12)
     for i, p in enumerate(prompts):
         want, gaps = oracle.OracleModel(w, mode=1).generate_greedy(p, 12)
-        assert_same_tokens(a[i], want, gaps)
-        assert_same_tokens(b[i], want, gaps)
+        assert_same_tokens(a[i], want, gaps, w, p)
+        assert_same_tokens(b[i], want, gaps, w, p)
         ka, kb = KVCacheView(chunked, i), KVCacheView(stepped, i)
         assert ka.length == kb.length == len(p) - 1 + 12 if p else True
         assert ka.page_allocation_status() == kb.page_allocation_status()

@@ -76,3 +76,50 @@ def test_generate_is_deterministic_and_modes_agree():
         if x != y:
             assert gap[i] < 1e-3
             break
+
+
+def test_chunked_prefill_equals_stepping_bit_for_bit():
+    # orc_runner_prefill (used by generate_greedy and the config fixtures)
+    # must leave exactly the state n single steps leave: next logits bitwise
+    for mode in ("perChannel", "int4"):
+        cfg = ModelConfig(2, 128, 4, 256, max_seq_len=160, num_kv_heads=2, intermediate_dim=256)
+        w = small_llama(cfg, seed=6, mode=mode)
+        a, b = oracle.OracleModel(w, mode=1), oracle.OracleModel(w, mode=1)
+        toks = [int(t) for t in np.random.default_rng(1).integers(0, 256, 150)]
+        for t in toks:
+            a.step(t)
+        b.prefill(toks)
+        assert a.position == b.position == 150 and a.page_status() == b.page_status()
+        assert np.array_equal(a.step(7), b.step(7)), mode
+
+
+def test_oracle_generator_matches_product_generator():
+    # the oracle-only model builder (bench reference arm, fixture scripts)
+    # draws the same numbers as the product's tb_rng_fill_normal
+    from oracle.synthetic import Generator, random_prompt
+    from tinybrain_b200.runtime import SeededGenerator
+    from tinybrain_b200.synthetic import random_prompt as product_prompt
+    for seed, n in ((0, 5), (7, 200003), (3, 1)):
+        assert np.array_equal(Generator(seed).normal((n,), 0.0, 0.02), SeededGenerator(seed).normal((n,), 0.0, 0.02))
+    assert random_prompt(64, 32000, 2) == product_prompt(64, 32000, 2)
+
+
+def test_assert_same_tokens_checks_the_whole_run():
+    import pytest
+    from tests.helpers import assert_same_tokens
+    want = [1, 2, 3, 4, 5]
+    gaps = [1.0, 5e-5, 1.0, 1.0, 1.0]
+    assert assert_same_tokens(want, want, gaps) == []
+    with pytest.raises(AssertionError):  # a flip at a clear gap
+        assert_same_tokens([1, 9, 3, 4, 5], want, [1.0] * 5, teacher=lambda g: (want, [1.0] * 5))
+    with pytest.raises(AssertionError):  # length mismatch
+        assert_same_tokens([1, 2, 3, 4], want, gaps)
+    # a tolerated near-tie, then the device continues on its own tokens: the
+    # teacher-forced oracle agrees with the rest -> accepted and reported
+    got = [1, 9, 8, 7, 6]
+    with pytest.warns(UserWarning):
+        flips = assert_same_tokens(got, want, gaps, teacher=lambda g: ([1, 2, 8, 7, 6], [1.0, 5e-5, 1, 1, 1]))
+    assert flips == [(1, 5e-5)]
+    # a second divergence after the tolerated one at a clear gap -> fails
+    with pytest.raises(AssertionError):
+        assert_same_tokens(got, want, gaps, teacher=lambda g: ([1, 2, 8, 0, 6], [1.0, 5e-5, 1, 1, 1]))

@@ -116,4 +116,38 @@ def test_tbf_model_decodes_like_oracle(ctx, mode):
     w = ModelWeights.load(os.path.join(GOLD, f"tiny_{mode}.tbf"))
     got = ModelRunner(w, ctx).generate_batch([[1, 2, 3, 4, 5]], 20)[0]
     want, gaps = oracle.OracleModel(w, mode=1).generate_greedy([1, 2, 3, 4, 5], 20)
-    assert_same_tokens(got, want, gaps)
+    assert_same_tokens(got, want, gaps, w, [1, 2, 3, 4, 5])
+
+
+def test_converter_int4_files_are_flagged():
+    from tinybrain_b200 import tbf
+    w8 = ModelWeights.load(os.path.join(GOLD, "tiny_int8.tbf"))
+    assert w8.tbf_info["writer"] == "convert_model.py" and not w8.tbf_info["converter_int4"]
+    with pytest.warns(tbf.ConverterInt4Warning):
+        w4 = ModelWeights.load(os.path.join(GOLD, "tiny_int4.tbf"))
+    assert w4.tbf_info["converter_int4"] and len(w4.tbf_info["int4_tensors"]) == 2 * 7 + 1
+    with pytest.raises(TinyBrainError, match="convert_model"):
+        ModelWeights.load(os.path.join(GOLD, "tiny_int4.tbf"), int4_layout="reject")
+
+
+def test_files_written_by_save_are_not_flagged(tmp_path):
+    w4 = ModelWeights.load(os.path.join(GOLD, "tiny_int4.tbf"))
+    path = str(tmp_path / "saved.tbf")
+    w4.save(path)
+    v = ModelWeights.load(path, int4_layout="reject")  # compact JSON header: ModelWeights.save
+    assert v.tbf_info["writer"] == "ModelWeights.save" and not v.tbf_info["converter_int4"]
+
+
+@pytest.mark.gpu
+def test_converter_int4_requantize_rebuilds_the_converted_matrix(ctx):
+    # int4_layout="requantize": each INT4 tensor becomes the runtime-layout
+    # quantization of the matrix the converter was given ([in, out] = W.T)
+    w = ModelWeights.load(os.path.join(GOLD, "tiny_int4.tbf"), int4_layout="requantize", ctx=ctx)
+    src = weights(7)
+    qt = w.layers[0].query.weights
+    assert qt.shape == (CFG["hidden_dim"], CFG["hidden_dim"]) and qt.mode == "int4"
+    deq = qt.dequantize(ctx)
+    t = src["layers"][0]["q_proj"].T  # [in, out]
+    # two roundings (converter groups, then runtime groups): within ~2 steps of 1/7 of the group max
+    assert np.max(np.abs(deq - t)) <= 2.0 * np.abs(t).max() / 7.0
+    assert np.corrcoef(deq.ravel(), t.ravel())[0, 1] > 0.95

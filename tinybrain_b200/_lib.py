@@ -74,6 +74,7 @@ SIGNATURES = {
     "tb_context_synchronize": [_P],
     "tb_context_stream": [_P],
     "tb_context_check_device": [_P],
+    "tb_debug_expire_wait": [_P, _I32],
     "tb_quantize_int8_per_channel": [_P, _P, _I64, _I64, _P, _P],
     "tb_quantize_int4_group": [_P, _P, _I64, _I64, _P, _P, _P],
     "tb_quantize_int8_per_channel_dev": [_P, _P, _I64, _I64, _P, _P],
@@ -86,6 +87,7 @@ SIGNATURES = {
     "tb_attention_decode": [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _P],
     "tb_paged_attention_dev": [_P, _P, _I32, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P],
     "tb_paged_attention_dev_noalloc": [_P, _P, _I32, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P],
+    "tb_paged_attention_noalloc_status": [_P, _I32],
     "tb_model_create": [_P, C.POINTER(ModelConfigC), C.POINTER(_P)],
     "tb_model_free": [_P],
     "tb_tp_unique_id": [_P],

@@ -501,6 +501,23 @@ cudaError_t launch_attention_probs(const AttnParams& p, float* probs, int L, cud
     return cudaGetLastError();
 }
 
+__global__ void wait_probe_kernel(int which, const unsigned long long* word, int* err) {
+    __shared__ uint64_t bar;
+    if (which == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        mbar_wait(&bar, 0, err);  // no thread arrives: runs out after kWaitLimitNs
+    } else {
+        unsigned long long w[1];
+        wait_tagged<1>(word, 1u, w, err);  // the word stays zero: runs out
+    }
+}
+
+cudaError_t launch_wait_probe(int which, const unsigned long long* word, int* err, cudaStream_t stream) {
+    wait_probe_kernel<<<1, 1, 0, stream>>>(which, word, err);
+    return cudaGetLastError();
+}
+
 }  // namespace tb
 
 // ---------------------------------------------------------------------------
@@ -511,22 +528,56 @@ cudaError_t launch_attention_probs(const AttnParams& p, float* probs, int L, cud
 // latency-critical path where cudaMalloc / cudaFree would synchronise the
 // device.  tb_paged_attention_dev_noalloc serves them: the split partials are
 // combined inside each CTA cluster through distributed shared memory, so the
-// kernel needs no global scratch; the entry point only caches the SM count.
+// kernel needs no global scratch.  Its only device state is one error word
+// in a file-scope __device__ variable (every GPU that loads the library holds
+// it until exit): a bounded wait that runs out inside the kernel records
+// kDevWaitTimeout there, and tb_paged_attention_noalloc_status reads it.  In
+// host code the variable's name is only a host-side stand-in, so its device
+// address is taken once per device with cudaGetSymbolAddress.
 // ---------------------------------------------------------------------------
+static __device__ int g_noalloc_err;
+
 namespace tb {
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 int g_noalloc_sms[kMaxDevices] = {};
+int* g_noalloc_err_dev[kMaxDevices] = {};
 
+// SM count and the error word's device address of the current device `dev`
+// (called with `dev` current).
 cudaError_t noalloc_setup(int dev) {
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     if (g_noalloc_sms[dev]) return cudaSuccess;
     int sms = 0;
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_err);
+    if (e != cudaSuccess) return e;
+    g_noalloc_err_dev[dev] = static_cast<int*>(ptr);
     g_noalloc_sms[dev] = sms;
     return cudaSuccess;
+}
+
+int noalloc_device(tb_status* st) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *st = (tb_status)report_error(TB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    if (dev < 0 || dev >= kMaxDevices) {
+        *st = (tb_status)report_error(TB_ERR_UNSUPPORTED, "device index %d is beyond the %d devices supported", dev,
+                                      kMaxDevices);
+        return -1;
+    }
+    e = noalloc_setup(dev);
+    if (e != cudaSuccess) {
+        *st = (tb_status)report_error(TB_ERR_CUDA, "allocation-free attention set-up: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return dev;
 }
 }  // namespace
 
@@ -542,16 +593,11 @@ extern "C" tb_status tb_paged_attention_dev_noalloc(void* stream, const float* q
     if (batch < 1 || max_len < 1 || layer < 0 || layer >= num_layers || H <= 0 || Hkv <= 0 || d <= 0 ||
         H % Hkv != 0)
         return (tb_status)report_error(TB_ERR_INVALID_ARGUMENT, "bad batch / length / layer / head arguments");
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-        return (tb_status)report_error(TB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
-    e = noalloc_setup(dev);
-    if (e != cudaSuccess)
-        return (tb_status)report_error(TB_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+    tb_status st = TB_OK;
+    const int dev = noalloc_device(&st);
+    if (dev < 0) return st;
     const int max_pages = (max_len + kPageTokens - 1) / kPageTokens;
     const int ns = choose_nsplit(batch, Hkv, max_pages, g_noalloc_sms[dev]);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     AttnParams a{};
     a.q = q;
     a.ld_q = H * d;
@@ -569,10 +615,28 @@ extern "C" tb_status tb_paged_attention_dev_noalloc(void* stream, const float* q
     a.nsplit = ns;
     a.out = out;
     a.ld_out = H * d;
-    a.err = nullptr;
-    e = launch_attention(a, st, false);
+    a.err = g_noalloc_err_dev[dev];
+    cudaError_t e = launch_attention(a, static_cast<cudaStream_t>(stream), false);
     if (e != cudaSuccess)
         return (tb_status)report_error(e == cudaErrorNotSupported ? TB_ERR_UNSUPPORTED : TB_ERR_CUDA,
                                        "attention launch: %s", cudaGetErrorString(e));
     return TB_OK;
+}
+
+extern "C" tb_status tb_paged_attention_noalloc_status(void* stream, int32_t clear) {
+    using namespace tb;
+    tb_status st = TB_OK;
+    const int dev = noalloc_device(&st);
+    if (dev < 0) return st;
+    cudaStream_t sm = static_cast<cudaStream_t>(stream);
+    int v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, g_noalloc_err_dev[dev], sizeof(int), cudaMemcpyDeviceToHost, sm);
+    if (e == cudaSuccess && clear) e = cudaMemsetAsync(g_noalloc_err_dev[dev], 0, sizeof(int), sm);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(sm);
+    if (e != cudaSuccess)
+        return (tb_status)report_error(TB_ERR_CUDA, "reading the device error word: %s", cudaGetErrorString(e));
+    if (v == 0) return TB_OK;
+    if (v == kDevWaitTimeout)
+        return (tb_status)report_error(TB_ERR_DEVICE_TIMEOUT, "a device-side wait exceeded its time limit");
+    return (tb_status)report_error(TB_ERR_STATE, "device error code %d", v);
 }

@@ -96,6 +96,30 @@ __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsign
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+// Bounded spin until the N consecutive tagged words at p (64-bit: fp32 value
+// low, u32 tag high) all carry `tag`; their values end up in w.  Gives up
+// after kWaitLimitNs, records kDevWaitTimeout and returns false.
+template <int N>
+__device__ __forceinline__ bool wait_tagged(const unsigned long long* p, uint32_t tag, unsigned long long* w,
+                                            int* err) {
+    uint64_t t0 = 0;
+    while (true) {
+        bool all = true;
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+            w[e] = ld_relaxed_sys_u64(p + e);
+            all = all && (uint32_t)(w[e] >> 32) == tag;
+        }
+        if (all) return true;
+        if (t0 == 0) {
+            t0 = global_timer_ns();
+        } else if (global_timer_ns() - t0 > kWaitLimitNs) {
+            record_error(err, kDevWaitTimeout);
+            return false;
+        }
+    }
+}
+
 // ---- 1-D bulk copy global -> shared (TMA, no tensor map) ----
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

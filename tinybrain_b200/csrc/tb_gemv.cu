@@ -309,21 +309,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             for (int q = 0; q < p.ar_world; ++q) {
                 const unsigned long long* wq = base + (size_t)q * p.ar_slot_words;
                 unsigned long long w[4];
-                uint64_t t0 = 0;
-                while (true) {
-                    bool all = true;
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        w[e] = ld_relaxed_sys_u64(wq + e);
-                        all = all && (uint32_t)(w[e] >> 32) == ar_tag;
-                    }
-                    if (all) break;
-                    if (t0 == 0) t0 = global_timer_ns();
-                    else if (global_timer_ns() - t0 > kWaitLimitNs) {
-                        record_error(p.err, kDevWaitTimeout);
-                        break;
-                    }
-                }
+                wait_tagged<4>(wq, ar_tag, w, p.err);
                 a = make_float4(__fadd_rn(a.x, __uint_as_float((uint32_t)w[0])),
                                 __fadd_rn(a.y, __uint_as_float((uint32_t)w[1])),
                                 __fadd_rn(a.z, __uint_as_float((uint32_t)w[2])),

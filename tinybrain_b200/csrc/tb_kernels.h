@@ -330,6 +330,13 @@ struct SampleParams {
 size_t sample_smem_bytes(int V, bool* in_smem);
 cudaError_t launch_sample(const SampleParams& p, cudaStream_t stream, bool pdl);
 
+// Failure-detection probe: one thread runs a bounded wait that nothing will
+// satisfy -- which 0: an mbarrier wait with no arrival (mbar_wait), 1: a spin
+// on a tagged word that nothing writes (wait_tagged, the tensor-parallel pull)
+// -- so the wait runs out and records kDevWaitTimeout in *err.  `word` is one
+// zeroed 64-bit device word.
+cudaError_t launch_wait_probe(int which, const unsigned long long* word, int* err, cudaStream_t stream);
+
 // Record the calling thread's last-error message (tb_last_error); returns status.
 int report_error(int status, const char* fmt, ...);
 

@@ -228,6 +228,9 @@ struct tb_runner {
     DevBuf ar_buf, ar_peers_dev, ar_step, h2;
     std::vector<void*> ar_peer_host;  // [world]; own buffer at the own rank
     bool ar_on = false;
+    // sequences and decode capacity of the last tb_runner_prefill_device, read
+    // by decode_device / read_tokens / trace_launches / profile_step
+    int last_n_seqs = 0, last_max_new = 0;
     // device sampler (tb_runner_set_sampler): LCG states, per-token statistics,
     // working rows for vocabularies beyond shared memory
     bool sampling = false, persistent_before = false;
@@ -448,6 +451,18 @@ extern "C" tb_status tb_context_check_device(tb_context* ctx) {
     if (v == kDevBadPage) return fail(TB_ERR_STATE, "KV append found no page mapped for the position");
     if (v == kDevBadToken) return fail(TB_ERR_STATE, "token id outside the vocabulary");
     return fail(TB_ERR_STATE, "device error code %d", v);
+}
+
+extern "C" tb_status tb_debug_expire_wait(tb_context* ctx, int32_t which) {
+    TB_CHECK(ctx, "ctx is NULL");
+    TB_CHECK(which == 0 || which == 1, "which must be 0 (mbarrier) or 1 (tagged word)");
+    TB_CUDA(cudaSetDevice(ctx->device));
+    DevBuf word;
+    TB_CUDA(word.alloc(8));
+    TB_CUDA(cudaMemsetAsync(word.p, 0, 8, ctx->stream));
+    TB_CUDA(launch_wait_probe(which, word.as<unsigned long long>(), ctx->err.as<int>(), ctx->stream));
+    TB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return ok();
 }
 
 static tb_status ensure(DevBuf& b, size_t bytes) {
@@ -2527,8 +2542,6 @@ static tb_status gen_activate_all(tb_runner* r, const GenPlan& gp) {
     return push_seq(r);
 }
 
-static GenPlan g_last_plan;  // for the split timing entry points (single-threaded benchmark use)
-
 extern "C" tb_status tb_runner_generate(tb_runner* r, const int32_t* prompts, const int64_t* offs, int32_t n_seqs,
                                         int32_t max_new, const int32_t* stop, int32_t n_stop, int32_t* out_tokens,
                                         int32_t* out_counts, tb_token_callback cb, void* user) {
@@ -2596,10 +2609,13 @@ extern "C" tb_status tb_runner_prefill_device(tb_runner* r, const int32_t* promp
                                               int32_t n_seqs, int32_t max_new) {
     TB_CHECK(r, "NULL runner");
     TB_CUDA(cudaSetDevice(r->ctx->device));
-    tb_status e = gen_setup(r, prompts, offs, n_seqs, max_new, g_last_plan);
+    GenPlan gp;
+    tb_status e = gen_setup(r, prompts, offs, n_seqs, max_new, gp);
     if (e != TB_OK) return e;
-    if ((e = gen_begin(r, g_last_plan)) != TB_OK) return e;
-    if ((e = gen_activate_all(r, g_last_plan)) != TB_OK) return e;
+    r->last_n_seqs = gp.n_seqs;
+    r->last_max_new = gp.max_new;
+    if ((e = gen_begin(r, gp)) != TB_OK) return e;
+    if ((e = gen_activate_all(r, gp)) != TB_OK) return e;
     if ((e = capture_graph(r)) != TB_OK) return e;
     TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
     return tb_context_check_device(r->ctx);
@@ -2609,7 +2625,7 @@ extern "C" tb_status tb_runner_decode_device(tb_runner* r, int32_t n_steps, floa
     TB_CHECK(r && n_steps >= 0, "bad argument");
     TB_CUDA(cudaSetDevice(r->ctx->device));
     std::vector<char> act(r->B, 0);
-    for (int s = 0; s < g_last_plan.n_seqs; ++s) act[s] = 1;
+    for (int s = 0; s < r->last_n_seqs; ++s) act[s] = 1;
     // Pre-map the pages these steps touch so the timed loop is pure graph replays.
     TB_CUDA(cudaEventRecord(r->ev0, r->ctx->stream));
     tb_status e = run_steps(r, n_steps, act);
@@ -2646,7 +2662,7 @@ extern "C" tb_status tb_runner_trace_launches(tb_runner* r, uint64_t* stamps, in
         r->graph = nullptr;
     };
     std::vector<char> act(r->B, 0);
-    for (int s = 0; s < std::max(1, g_last_plan.n_seqs); ++s) act[s] = 1;
+    for (int s = 0; s < std::max(1, r->last_n_seqs); ++s) act[s] = 1;
     set(true);
     tb_status e = run_steps(r, 1, act);
     cudaError_t ce = cudaStreamSynchronize(r->ctx->stream);
@@ -2669,8 +2685,8 @@ extern "C" tb_status tb_runner_read_tokens(tb_runner* r, int32_t* out_tokens, in
     TB_CUDA(cudaStreamSynchronize(r->ctx->stream));
     const SeqState* st = r->pin_seq.as<SeqState>();
     const int* pt = r->pin_tokens.as<int>();
-    const int stride = std::max(1, g_last_plan.max_new);
-    for (int s = 0; s < g_last_plan.n_seqs; ++s) {
+    const int stride = std::max(1, r->last_max_new);
+    for (int s = 0; s < r->last_n_seqs; ++s) {
         const int n = std::min(std::min(st[s].n_out, r->max_out), stride);
         out_counts[s] = n;
         for (int i = 0; i < n; ++i) out_tokens[(size_t)s * stride + i] = pt[(size_t)s * r->max_out + i];
@@ -2685,7 +2701,7 @@ extern "C" tb_status tb_runner_profile_step(tb_runner* r, float* times_ms, int32
     const int cnt = (int)r->plan.size();
     TB_CHECK(*n >= cnt, "capacity %d < %d kernels", *n, cnt);
     std::vector<char> act(r->B, 0);
-    for (int s = 0; s < std::max(1, g_last_plan.n_seqs); ++s) act[s] = 1;
+    for (int s = 0; s < std::max(1, r->last_n_seqs); ++s) act[s] = 1;
     for (int s = 0; s < r->B; ++s)
         if (act[s]) {
             tb_status e = kv_prepare(r, s);

@@ -407,10 +407,12 @@ class ModelWeights:
         return DeviceModel(self, ctx, tp)
 
     @staticmethod
-    def load(path: str) -> "ModelWeights":
-        """ModelWeights.load(from:) -- a .tbf file (ModelWeights.swift:496-798)."""
+    def load(path: str, int4_layout: str = "runtime", ctx: Optional["Context"] = None) -> "ModelWeights":
+        """ModelWeights.load(from:) -- a .tbf file (ModelWeights.swift:496-798).
+        int4_layout: what to do with INT4 tensors of a file written by
+        Scripts/convert_model.py (see tbf.load)."""
         from . import tbf
-        return tbf.load(path)
+        return tbf.load(path, int4_layout=int4_layout, ctx=ctx)
 
     def save(self, path: str) -> None:
         """ModelWeights.save(to:) -- a .tbf file (ModelWeights.swift:260-490)."""

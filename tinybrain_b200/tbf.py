@@ -22,12 +22,30 @@ All integers little-endian.  Tensor names: "embeddings", "layer_{i}_attn_{q,k,v,
 
 The file is memory-mapped and tensors are views into it until uploaded (the
 reference reads the whole file; mmap gives the same bytes).
+
+Converter-written INT4 files.  Scripts/convert_model.py:489-502 quantizes an
+INT4 weight as the flattened PyTorch [out, in] tensor (groups of 32
+consecutive inputs of one output) without transposing the data, but records
+the shape as [in, out]; the runtime reads every INT4 tensor as row-major
+[in, out] (QuantizedTensor.swift:195-216, DequantINT4.metal:95-137), so such
+a file decodes to a different matrix than the one converted.  The writer is
+recognisable from the header: the converter writes the config with Python's
+json.dumps default separators (", " and ": ", convert_model.py:57-68) while
+Swift's JSONEncoder (ModelWeights.swift:273) writes compact JSON.  load()
+flags such files (ModelWeights.tbf_info["converter_int4"]) and, by
+`int4_layout`, keeps the reference's runtime reading ("runtime", the default:
+what the reference itself computes, with a warning), refuses the file
+("reject", TB_ERR_FORMAT), or rebuilds each INT4 tensor as the converted
+matrix ("requantize": dequantize in [out, in] order, transpose to [in, out],
+quantize again with the runtime's INT4 quantizer on the device -- a second
+rounding, since the two layouts group different elements).
 """
 from __future__ import annotations
 
 import json
 import mmap
 import struct
+import warnings
 from typing import Dict, List, Optional, Tuple
 
 import numpy as np
@@ -94,8 +112,22 @@ def _config_from_json(d: dict) -> ModelConfig:
                        architecture=arch)
 
 
-def load(path: str) -> ModelWeights:
-    """ModelWeights.load(from:) (ModelWeights.swift:496-798)."""
+class ConverterInt4Warning(UserWarning):
+    """An INT4 tensor of a converter-written file is read with the runtime's
+    [in, out] semantics, not as the matrix that was converted."""
+
+
+def written_by_converter(config_json: bytes) -> bool:
+    """True for a header written by Scripts/convert_model.py (json.dumps with
+    its default ", " / ": " separators); Swift's JSONEncoder writes none."""
+    return b'": ' in config_json or b'", "' in config_json
+
+
+def load(path: str, int4_layout: str = "runtime", ctx=None) -> ModelWeights:
+    """ModelWeights.load(from:) (ModelWeights.swift:496-798).  int4_layout is
+    "runtime", "reject" or "requantize" (module docstring)."""
+    if int4_layout not in ("runtime", "reject", "requantize"):
+        raise ValueError("int4_layout must be 'runtime', 'reject' or 'requantize'")
     f = open(path, "rb")
     try:
         buf = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
@@ -111,7 +143,9 @@ def load(path: str) -> ModelWeights:
     version = r.u32()
     if version != VERSION:
         raise TinyBrainError(_ERR_FORMAT, f"tbf: unsupported version {version}")
-    config = _config_from_json(json.loads(r.take(r.u32()).decode("utf-8")))
+    cj = r.take(r.u32())
+    config = _config_from_json(json.loads(cj.decode("utf-8")))
+    from_converter = written_by_converter(cj)
     r.align()
 
     meta: Dict[str, Tuple[int, int, int, np.ndarray, Optional[np.ndarray]]] = {}
@@ -154,8 +188,16 @@ def load(path: str) -> ModelWeights:
         if len(dims) != 2:
             raise TinyBrainError(_ERR_FORMAT, f"tbf: {name} is not a matrix")
         if precision == 2:  # INT4 per group (ModelWeights.swift:672-679)
-            return QuantizedTensor((dims[0], dims[1]), raw.copy(), scales, "int4", int(gs),
-                                   zps if zps is not None else np.zeros(scales.size, dtype=np.int8))
+            q = QuantizedTensor((dims[0], dims[1]), raw.copy(), scales, "int4", int(gs),
+                                zps if zps is not None else np.zeros(scales.size, dtype=np.int8))
+            if from_converter:
+                converter_int4.append(name)
+                if int4_layout == "reject":
+                    raise TinyBrainError(_ERR_FORMAT, f"tbf: {name} is an INT4 tensor written by convert_model.py "
+                                                      "([out, in] data recorded as [in, out])")
+                if int4_layout == "requantize":
+                    return _requantize_converter_int4(q, ctx)
+            return q
         if mode != 2:
             raise TinyBrainError(4, f"tbf: {name}: INT8 mode {mode} (symmetric) is outside the decode path")
         return QuantizedTensor((dims[0], dims[1]), raw.view(np.int8).copy(), scales, "perChannel", 0, zps)
@@ -163,6 +205,7 @@ def load(path: str) -> ModelWeights:
     def linear(name: str, bias: str) -> LinearLayerWeights:
         return LinearLayerWeights(quant(name), f32(bias))
 
+    converter_int4: List[str] = []
     emb = f32("embeddings")
     if emb is None:
         raise TinyBrainError(_ERR_FORMAT, "tbf: missing tensor embeddings")
@@ -179,7 +222,28 @@ def load(path: str) -> ModelWeights:
             input_norm=f32(p + "ln_input"), post_attention_norm=f32(p + "ln_post")))
     if f32("final_norm_bias") is not None:
         raise TinyBrainError(4, "tbf: LayerNorm biases (Phi-2) are outside the decode path")
-    return ModelWeights(config, emb, layers, linear("output", "output_bias"), final_norm=f32("final_norm"))
+    out = linear("output", "output_bias")
+    weights = ModelWeights(config, emb, layers, out, final_norm=f32("final_norm"))
+    weights.tbf_info = {"writer": "convert_model.py" if from_converter else "ModelWeights.save",
+                        "converter_int4": bool(converter_int4), "int4_layout": int4_layout,
+                        "int4_tensors": converter_int4}
+    if converter_int4 and int4_layout == "runtime":
+        warnings.warn(f"{path}: {len(converter_int4)} INT4 tensors written by convert_model.py are read with the "
+                      "runtime's [in, out] semantics, as the reference does (int4_layout='requantize' rebuilds "
+                      "the converted matrices)", ConverterInt4Warning, stacklevel=3)
+    return weights
+
+
+def _requantize_converter_int4(q: QuantizedTensor, ctx) -> QuantizedTensor:
+    """The converted matrix of a converter-written INT4 tensor: its flat data
+    is the PyTorch [out, in] weight, so dequantize flat, view as [out, in],
+    transpose to [in, out] and quantize with the runtime INT4 quantizer (same
+    group size) on the device."""
+    from .runtime import quantize
+    K, N = q.shape  # recorded [in, out]
+    flat = q.dequantize(ctx).reshape(-1)  # element order of the converter's flat [out, in] data
+    w = np.ascontiguousarray(flat.reshape(N, K).T)
+    return quantize(w, "int4", q.group_size, ctx)
 
 
 def save(weights: ModelWeights, path: str) -> None:
