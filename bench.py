@@ -188,6 +188,9 @@ def timeline_roofline(runner, attn_bytes_per_launch, family_names, traffic_keys,
     stamps, kinds = runner.trace_launches()
     _, _, nbytes = runner.profile_step()
     exits = stamps[:, 6].astype(np.float64)
+    for i in range(1, len(exits)):  # a launch without stamps inherits its predecessor's exit
+        if exits[i] <= 0:
+            exits[i] = exits[i - 1]
     start = float(stamps[0, 0])
     prev = np.concatenate([[start], exits[:-1]])
     excl_us = np.maximum(exits - prev, 0.0) / 1000.0

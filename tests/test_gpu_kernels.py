@@ -106,7 +106,7 @@ def test_gemv_rejects_unsupported_int4_layout(ctx):
 
 @pytest.mark.parametrize("H,Hkv,d,L", [(32, 4, 64, 1), (32, 4, 64, 15), (32, 4, 64, 16), (32, 4, 64, 17),
                                        (32, 4, 64, 384), (32, 4, 64, 2048), (32, 32, 128, 700),
-                                       (4, 4, 16, 32), (8, 2, 16, 33), (4, 4, 32, 4224)])
+                                       (4, 4, 16, 32), (8, 2, 16, 33), (4, 4, 32, 4224), (32, 4, 64, 4224)])
 def test_decode_attention(ctx, H, Hkv, d, L):
     g = SeededGenerator(H * 1000 + L)
     q = g.normal((H * d,))

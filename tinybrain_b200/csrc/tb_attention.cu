@@ -24,6 +24,7 @@
 #include "tb_common.cuh"
 #include "tb_kernels.h"
 
+#include <cstdlib>
 #include <mutex>
 
 namespace tb {
@@ -327,6 +328,352 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     if (threadIdx.x == 0) trace_max(p.trace, 6);
 }
 
+// ---------------------------------------------------------------------------
+// Grouped-query attention with 8 query heads per KV head and d = 64 (the
+// TinyLlama shape of the benchmark configurations).  Same grid, producer,
+// page ring and cluster combine as attn_decode_kernel, but the consumer
+// arithmetic is register-blocked so that each K and V element read from
+// shared memory serves all 8 heads:
+//   scores:  thread (token j, dim slice c) holds q of all 8 heads for its 8
+//            dims {4c..4c+3, 32+4c..32+4c+3} in registers, reads its 8 K
+//            values once (two conflict-free float4) and forms 8 partial dots;
+//            a reduce-scatter over the 8 slice lanes (4 + 2 + 1 shuffles)
+//            leaves lane c with head c's full dot for token j;
+//   softmax: per head, the page maximum over 16 tokens (two shuffles, then
+//            the four warps' maxima through shared memory), one exp per
+//            (token, head) and one per head for the running-max correction;
+//            each thread keeps a partial running sum of its tokens' weights;
+//   P.V:     thread (token pair tg, dim quad dc) keeps an 8-head x 4-dim
+//            accumulator, rescales it by the heads' corrections and adds its
+//            two tokens' weighted V rows (one float4 of V, two of weights,
+//            32 FMAs per token); the 8 token pairs' accumulators are summed
+//            once per CTA, in pair order, at the end.
+// Shared-memory reads per 8 KB page: ~16 KB (the generic kernel reads each
+// K / V tile once per head, 64 KB), which moved it off the shared-memory
+// pipe.  One consumer group of 4 warps and an 8-page ring per CTA, three
+// CTAs per SM.
+// ---------------------------------------------------------------------------
+constexpr int kGqaStages = 8;
+constexpr int kGqaThreads = (4 + 1) * 32;
+
+__global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __grid_constant__ AttnParams p) {
+    constexpr int G = 8, D = 64;
+    constexpr int TILE = kPageTokens * D;
+    static_assert(kGqaStages * 20 <= kAttnHead, "ring barriers exceed the header");
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kGqaStages;
+    int* valid = reinterpret_cast<int*>(empty + kGqaStages);  // [stages]
+    // scratch after the header: pm [2][G][4] page maxima per warp, Cs [2][G]
+    // corrections, Pw [2][16][G] weights, then the ring, then the combine area
+    float* pm = reinterpret_cast<float*>(smem + kAttnHead);
+    float* Cs = pm + 2 * G * 4;
+    float* Pw = Cs + 2 * G;
+    float* tiles = reinterpret_cast<float*>(smem + kAttnHead + 2048);
+    // [8 token pairs][G][D] accumulators, then l [16][G]: reuses the ring,
+    // which is idle once every page has been consumed
+    float* red = tiles;
+    float* cpart = tiles + kGqaStages * 2 * TILE;  // [G][D + 4]: acc, m, l of this split
+    static_assert(8 * G * D + 16 * G <= kGqaStages * 2 * TILE, "reduction area fits the ring");
+    static_assert((2 * G * 4 + 2 * G + 2 * 16 * G) * 4 <= 2048, "scratch");
+
+    const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kGqaStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 4);
+        }
+        fence_barrier_init();
+        trace_min(p.trace, 0);
+        trace_max(p.trace, 1);
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    const SeqState& sq = p.seq[m];
+    const bool active = p.lens ? true : (sq.active != 0);
+    const int Lq = p.lens ? p.lens[m] : sq.pos + 1;
+    const int npages = active ? (Lq + kPageTokens - 1) / kPageTokens : 0;
+    const int pps = (npages + p.nsplit - 1) / p.nsplit;
+    const int pg0 = min(npages, split * pps);
+    const int pg1 = min(npages, pg0 + pps);
+    const int nun = pg1 - pg0;
+
+    if (warp == 4) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            bool waited = false;
+            for (int i = 0; i < nun; ++i) {
+                const int st = i % kGqaStages;
+                if (i >= kGqaStages) {
+                    if (!mbar_wait(&empty[st], ((i / kGqaStages) - 1) & 1, p.err)) break;
+                }
+                const int lp = pg0 + i;
+                if ((p.wait_first || lp == npages - 1) && !waited) {  // pages the preceding kernel appends to
+                    pdl_wait();
+                    waited = true;
+                }
+                const int page = p.page_table[(size_t)m * p.ptab_stride + lp];
+                float* kd = tiles + st * 2 * TILE;
+                if (page >= 0) {
+                    valid[st] = 1;
+                    const size_t kbase =
+                        ((((size_t)page * p.num_layers + p.layer) * 2 + 0) * p.Hkv + kvh) * (size_t)TILE;
+                    const size_t vbase =
+                        ((((size_t)page * p.num_layers + p.layer) * 2 + 1) * p.Hkv + kvh) * (size_t)TILE;
+                    mbar_arrive_expect_tx(&full[st], 2u * TILE * 4u);
+                    bulk_g2s(kd, p.kv_pool + kbase, TILE * 4u, &full[st]);
+                    bulk_g2s(kd + TILE, p.kv_pool + vbase, TILE * 4u, &full[st]);
+                } else {
+                    valid[st] = 0;  // evicted page: rows read as zeros
+                    mbar_arrive(&full[st]);
+                }
+            }
+        }
+    } else {
+        // ------------------------------ consumers ------------------------------
+        pdl_wait();
+        if (threadIdx.x == 0) trace_max(p.trace, 2);
+        const int t = threadIdx.x;  // 0..127
+        // scores in base 2: (q.k) / sqrt(d) * log2(e), weights 2^(s - max) --
+        // the same softmax, one ex2 per weight
+        const float scale2 = __fmul_rn(__fdiv_rn(1.0f, __fsqrt_rn((float)D)), 1.4426950408889634f);
+        // score role: token j, dim slice c (dims 4c..4c+3 and 32+4c..32+4c+3)
+        const int j = t >> 3, c = t & 7;
+        float qr[G][8];
+        {
+            const float* qb = p.q + (size_t)m * p.ld_q + (size_t)kvh * G * D;
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float4 a = *reinterpret_cast<const float4*>(qb + h * D + 4 * c);
+                const float4 b = *reinterpret_cast<const float4*>(qb + h * D + 32 + 4 * c);
+                qr[h][0] = a.x; qr[h][1] = a.y; qr[h][2] = a.z; qr[h][3] = a.w;
+                qr[h][4] = b.x; qr[h][5] = b.y; qr[h][6] = b.z; qr[h][7] = b.w;
+            }
+        }
+        // P.V role: token pair tg (tokens 2tg, 2tg + 1), dims 4dc..4dc+3
+        const int tg = t >> 4, dc = t & 15;
+        float acc[G][4];
+#pragma unroll
+        for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
+        float run_m = -INFINITY, l_part = 0.0f;  // head c, this thread's tokens
+
+        bool bad = false;
+        for (int i = 0; i < nun; ++i) {
+            const int st = i % kGqaStages, b2 = i & 1;
+            if (!bad && !mbar_wait(&full[st], (i / kGqaStages) & 1, p.err)) bad = true;
+            const float* Kt = tiles + st * 2 * TILE;
+            const float* Vt = Kt + TILE;
+            const bool ok = !bad && valid[st] != 0;
+            // ---- scores of token j for the 8 heads ----
+            float s[G];
+#pragma unroll
+            for (int h = 0; h < G; ++h) s[h] = 0.0f;
+            if (ok) {
+                const float4 ka = *reinterpret_cast<const float4*>(Kt + j * D + 4 * c);
+                const float4 kb = *reinterpret_cast<const float4*>(Kt + j * D + 32 + 4 * c);
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    float d0 = qr[h][0] * ka.x;
+                    float d1 = qr[h][1] * ka.y;
+                    d0 = fmaf(qr[h][2], ka.z, d0);
+                    d1 = fmaf(qr[h][3], ka.w, d1);
+                    d0 = fmaf(qr[h][4], kb.x, d0);
+                    d1 = fmaf(qr[h][5], kb.y, d1);
+                    d0 = fmaf(qr[h][6], kb.z, d0);
+                    d1 = fmaf(qr[h][7], kb.w, d1);
+                    s[h] = d0 + d1;
+                }
+            }
+            // reduce-scatter over the 8 slice lanes: lane c ends with head c
+            float r4[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float mine = (c & 4) ? s[4 + k] : s[k];
+                const float other = (c & 4) ? s[k] : s[4 + k];
+                r4[k] = mine + __shfl_xor_sync(0xffffffffu, other, 4);
+            }
+            float r2[2];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const float mine = (c & 2) ? r4[2 + k] : r4[k];
+                const float other = (c & 2) ? r4[k] : r4[2 + k];
+                r2[k] = mine + __shfl_xor_sync(0xffffffffu, other, 2);
+            }
+            const float mine = (c & 1) ? r2[1] : r2[0];
+            const float other = (c & 1) ? r2[0] : r2[1];
+            const float dot = mine + __shfl_xor_sync(0xffffffffu, other, 1);
+            const int tok = (pg0 + i) * kPageTokens + j;
+            const float sc = (tok < Lq) ? __fmul_rn(dot, scale2) : -INFINITY;
+            // ---- page maximum of head c: the warp's 4 tokens, then the 4 warps ----
+            float wm = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 8));
+            wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 16));
+            if (lane < 8) pm[(b2 * G + c) * 4 + warp] = wm;
+            named_bar_sync(1, 128);
+            const float4 w4 = *reinterpret_cast<const float4*>(pm + (b2 * G + c) * 4);
+            const float mnew = fmaxf(run_m, fmaxf(fmaxf(w4.x, w4.y), fmaxf(w4.z, w4.w)));
+            const float e = (sc == -INFINITY) ? 0.0f : exp2f(sc - mnew);
+            if (j == 0) Cs[b2 * G + c] = (run_m == -INFINITY) ? 0.0f : exp2f(run_m - mnew);
+            run_m = mnew;
+            Pw[(b2 * 16 + j) * G + c] = e;
+            named_bar_sync(1, 128);
+            l_part = fmaf(l_part, Cs[b2 * G + c], e);
+            // ---- P.V for tokens 2tg, 2tg + 1 ----
+            {
+                const float4 ca = *reinterpret_cast<const float4*>(Cs + b2 * G);
+                const float4 cb = *reinterpret_cast<const float4*>(Cs + b2 * G + 4);
+                const float cr[G] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    acc[h][0] *= cr[h];
+                    acc[h][1] *= cr[h];
+                    acc[h][2] *= cr[h];
+                    acc[h][3] *= cr[h];
+                }
+                if (ok) {
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int jj = 2 * tg + u;
+                        const float4 v = *reinterpret_cast<const float4*>(Vt + jj * D + 4 * dc);
+                        const float4 pa = *reinterpret_cast<const float4*>(Pw + (b2 * 16 + jj) * G);
+                        const float4 pb = *reinterpret_cast<const float4*>(Pw + (b2 * 16 + jj) * G + 4);
+                        const float pw[G] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+                        for (int h = 0; h < G; ++h) {
+                            acc[h][0] = fmaf(pw[h], v.x, acc[h][0]);
+                            acc[h][1] = fmaf(pw[h], v.y, acc[h][1]);
+                            acc[h][2] = fmaf(pw[h], v.z, acc[h][2]);
+                            acc[h][3] = fmaf(pw[h], v.w, acc[h][3]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        // ---- this split's (acc, m, l): token pairs summed in pair order ----
+        named_bar_sync(1, 128);  // every warp is done with the ring
+#pragma unroll
+        for (int h = 0; h < G; ++h)
+            *reinterpret_cast<float4*>(red + (tg * G + h) * D + 4 * dc) =
+                make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+        red[8 * G * D + j * G + c] = l_part;
+        named_bar_sync(1, 128);
+        {
+            // thread t: head t / 16, dims 4 (t % 16) .. +3
+            const int h = t >> 4, d4 = 4 * (t & 15);
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 v = *reinterpret_cast<const float4*>(red + (q * G + h) * D + d4);
+                a.x += v.x;
+                a.y += v.y;
+                a.z += v.z;
+                a.w += v.w;
+            }
+            *reinterpret_cast<float4*>(cpart + h * (D + 4) + d4) = a;
+        }
+        if (t < G) {  // head t: running max (identical in every thread of the head), sum of the 16 tokens' sums
+            float l = 0.0f;
+            for (int q = 0; q < 16; ++q) l += red[8 * G * D + q * G + t];
+            cpart[t * (D + 4) + D] = __shfl_sync(0x000000ffu, run_m, t);  // lane t holds head t (j = 0)
+            cpart[t * (D + 4) + D + 1] = l;
+        }
+    }
+    // Combine the splits (cluster ranks) in split order, as attn_decode_kernel.
+    const int ns = p.nsplit;
+    if (ns > 1) cluster_sync();
+    else __syncthreads();
+    {
+        constexpr int Q = G * (D / 4);
+        const int t = threadIdx.x;
+        const int i0 = split * Q / ns, i1 = (split + 1) * Q / ns;
+        if (t < 128 && i0 + t < i1) {
+            const int item = i0 + t;
+            const int g = item / (D / 4), d4 = (item % (D / 4)) * 4;
+            float* out = p.out + (size_t)m * p.ld_out + (size_t)(kvh * G + g) * D + d4;
+            float mq[kMaxAttnSplits];
+#pragma unroll
+            for (int q = 0; q < kMaxAttnSplits; ++q)
+                mq[q] = q < ns ? dsmem_ld_f32(dsmem_map(cpart + g * (D + 4) + D, (uint32_t)q)) : -INFINITY;
+            float M = -INFINITY;
+#pragma unroll
+            for (int q = 0; q < kMaxAttnSplits; ++q) M = fmaxf(M, mq[q]);
+            float den = 0.0f;
+            float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (M != -INFINITY) {
+#pragma unroll
+                for (int q0 = 0; q0 < kMaxAttnSplits; q0 += 8) {
+                    if (q0 >= ns) break;
+                    float lq[8];
+                    float4 aq[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int q = q0 + u;
+                        if (q < ns) {
+                            const uint32_t base = dsmem_map(cpart + g * (D + 4), (uint32_t)q);
+                            lq[u] = dsmem_ld_f32(base + (D + 1) * 4);
+                            aq[u] = dsmem_ld_f32x4(base + d4 * 4);
+                        } else {
+                            lq[u] = 0.0f;
+                            aq[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int q = q0 + u;
+                        if (q >= ns) continue;
+                        const float w = (mq[q] == -INFINITY) ? 0.0f : exp2f(mq[q] - M);  // base-2 maxima
+                        den = fmaf(w, lq[u], den);
+                        num.x = fmaf(w, aq[u].x, num.x);
+                        num.y = fmaf(w, aq[u].y, num.y);
+                        num.z = fmaf(w, aq[u].z, num.z);
+                        num.w = fmaf(w, aq[u].w, num.w);
+                    }
+                }
+            }
+            const float il = den > 0.0f ? 1.0f / den : 0.0f;
+            *reinterpret_cast<float4*>(out) = make_float4(num.x * il, num.y * il, num.z * il, num.w * il);
+        }
+    }
+    if (ns > 1) cluster_sync();  // partials stay readable until every rank has combined
+    if (threadIdx.x == 0) trace_max(p.trace, 6);
+}
+
+size_t attn_gqa8_smem() {
+    return kAttnHead + 2048 + (size_t)kGqaStages * 2 * kPageTokens * 64 * 4 + (size_t)8 * (64 + 4) * 4;
+}
+
+cudaError_t launch_attn_gqa8(const AttnParams& p, cudaStream_t stream, bool pdl) {
+    const size_t smem = attn_gqa8_smem();
+    auto kfn = attn_gqa8_d64_kernel;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    if (p.nsplit > 8) {
+        e = cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
+    if (p.nsplit < 1 || p.nsplit > kMaxAttnSplits) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)p.nsplit, (unsigned)p.Hkv, (unsigned)p.M);
+    cfg.blockDim = dim3(kGqaThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.nsplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kfn, p);
+}
+
 template <int G, int D>
 size_t attn_smem() {
     return kAttnHead + (((2 * G * kPageTokens + 2 * G) * 4 + 127) / 128) * 128 +
@@ -459,6 +806,7 @@ int choose_nsplit(int M, int Hkv, int max_pages, int num_sms, bool balance_long)
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
     const int G = p.H / p.Hkv;
     if (p.H % p.Hkv != 0) return cudaErrorInvalidValue;
+    if (G == 8 && p.d == 64 && !getenv("TB_ATTN_GENERIC")) return launch_attn_gqa8(p, stream, pdl);
 #define TB_ATTN_CASE(g, dd) \
     if (G == g && p.d == dd) return launch_attn_t<g, dd>(p, stream, pdl);
     TB_ATTN_CASE(1, 16)

@@ -28,6 +28,9 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 namespace tb {
 
@@ -73,8 +76,14 @@ __host__ __device__ constexpr int q4_nb(int mb) { return 16 * mb; }
 // and B operands in shared memory, then one accumulator of NB columns.
 constexpr int kQ4Slots = 4;
 constexpr int kGemvBarBytes = 512;  // mbarriers + tensor-memory address at the start of shared memory
-// red [RB][MB], misc [16 MB], row scales and biases [2 RB], seqinfo [3 MB], rowinv / rowex [2 MB]
-__host__ __device__ constexpr int gemv_head_floats(int rb, int mb) { return rb * mb + 16 * mb + 2 * rb + 5 * mb; }
+// Row stride of the partial sums red[row][m]: one float of padding past a
+// single batch row, so the epilogue warps (one tile row per lane) write
+// 32 different banks.
+__host__ __device__ constexpr int red_stride(int mb) { return mb == 1 ? 1 : mb + 1; }
+// red [RB][red_stride], misc [16 MB], row scales and biases [2 RB], seqinfo [3 MB], rowinv / rowex [2 MB]
+__host__ __device__ constexpr int gemv_head_floats(int rb, int mb) {
+    return rb * red_stride(mb) + 16 * mb + 2 * rb + 5 * mb;
+}
 __host__ __device__ constexpr int q4_dcols(int mb) { return q4_nb(mb) < 32 ? 32 : q4_nb(mb); }
 // INT4 CTAs add a tensor-core issue warp to the producer and 8 consumer warps.
 // INT8 batches beyond 16 rows per CTA ("wide"): digits are built per unit
@@ -131,8 +140,9 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
     uint64_t* s_free = b_ready + kQ4Slots;                                // INT4: [kQ4Slots] products done
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + kQ4Slots);
     static_assert((2 * STAGES + 2 + 3 * kQ4Slots) * 8 + 4 <= kGemvBarBytes, "barrier region");
-    float* red = reinterpret_cast<float*>(smem + kGemvBarBytes);          // [RB][MB]
-    float* misc = red + RB * MB;                                          // [2][MB][8]
+    constexpr int RS = red_stride(MB);
+    float* red = reinterpret_cast<float*>(smem + kGemvBarBytes);          // [RB][RS]
+    float* misc = red + RB * RS;                                          // [2][MB][8]
     float* rowsc = misc + 16 * MB;                                        // [RB] row scales (1 for INT4)
     float* rowbias = rowsc + RB;                                          // [RB] row biases (0 if none)
     int* seqinfo = reinterpret_cast<int*>(rowbias + RB);                  // [3][MB] pos, active, page
@@ -174,6 +184,10 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
     if (threadIdx.x == 0) {
         trace_min(p.trace, 0);
         trace_max(p.trace, 1);
+        if (PREC == 8 && p.trace && blockIdx.x == 0 && blockIdx.y == 0) {  // launch shape (diagnostics)
+            p.trace[14] = (unsigned long long)P;
+            p.trace[15] = (unsigned long long)(gridDim.x * gridDim.y);
+        }
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&full[i], 1);
             // INT8: released by tcgen05.commit; INT4: by the 8 consumer warps after reading it
@@ -287,7 +301,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         const int kbeg = s0 * L.slab_k;
         const int kend = min(s1 * L.slab_k, L.Kp);
         const bool rms = p.prologue == kProRmsNorm || p.prologue == kProEmbedRms;
-        if (rms)  // RMSNorm weights of the CTA's k range (zero past K)
+        if (rms && !pre)  // RMSNorm weights of the CTA's k range (zero past K)
             for (int k = ctid; k < kspan; k += 256) wstage[k] = kbeg + k < L.K ? __ldg(p.norm_w + kbeg + k) : 0.0f;
         if (PREC == 4)
             for (int i = ctid; i < kQ4Groups * nunits; i += 256) {
@@ -508,22 +522,25 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 if (lane == 0) mbar_arrive(&b_ready[sl]);
             }
             if (ctid == 0) trace_max(p.trace, 3);
-            // epilogue: warps 0-3 read the accumulator, 32 columns (8 rows) at a time
-            if (warp < 4) {
+            // epilogue: all 8 warps read the accumulator, 32 columns (8 batch
+            // rows) at a time; warps w and w + 4 share TMEM lanes 32 (w % 4)..
+            // and take alternate column chunks
+            {
                 const uint32_t tmem = *tmem_slot;
                 const bool okd = mbar_wait(&done[0], 0, p.err);
                 if (lane == 0) trace_max(p.trace, 4);
                 tc_fence_after();
-                const int row = 32 * warp + lane;
+                const int wq = warp & 3;
+                const int row = 32 * wq + lane;
 #pragma unroll 1
-                for (int c = 0; c < NB / 32; ++c) {
+                for (int c = warp >> 2; c < NB / 32; c += 2) {
                     int d[32];
-                    tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(32 * c), d);
+                    tmem_ld32(tmem + ((uint32_t)(32 * wq) << 16) + (uint32_t)(32 * c), d);
                     tmem_ld_wait();
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
                         const int m = 8 * c + u;
-                        red[row * MB + m] = okd ? combine_digits(d + kTcDigits * u, rowex[m]) : 0.0f;
+                        red[row * RS + m] = okd ? combine_digits(d + kTcDigits * u, rowex[m]) : 0.0f;
                     }
                 }
                 tc_fence_before();
@@ -577,7 +594,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 tmem_ld_wait();
                 const int row = 32 * (warp - 4) + lane;
 #pragma unroll
-                for (int m = 0; m < MB; ++m) red[row * MB + m] = okd ? combine_digits(d + kTcDigits * m, rowex[m]) : 0.0f;
+                for (int m = 0; m < MB; ++m) red[row * RS + m] = okd ? combine_digits(d + kTcDigits * m, rowex[m]) : 0.0f;
                 tc_fence_before();
             }
         } else {
@@ -713,7 +730,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                     if (nunits > 0)
                         tmem_ld4(tmem + lane_base + (uint32_t)(kQ4Slots * 32 + (m * kQ4Groups + wq) * kTcDigits), d);
                     tmem_ld_wait();
-                    red[row * MB + m] = okd ? combine_digits(d, ex4[m * kQ4Groups + wq]) : 0.0f;
+                    red[row * RS + m] = okd ? combine_digits(d, ex4[m * kQ4Groups + wq]) : 0.0f;
                 }
                 tc_fence_before();
             }
@@ -745,10 +762,10 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         // Partial sums of a row from every rank: all loads issued before the
         // first add (one DSMEM round trip), then summed in rank order.
         auto rowsum = [&](int row, int m) -> float {
-            if (P == 1) return red[row * MB + m];
+            if (P == 1) return red[row * RS + m];
             float v[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) v[q] = q < P ? dsmem_ld_f32(rbase[q] + (uint32_t)((row * MB + m) * 4)) : 0.0f;
+            for (int q = 0; q < 8; ++q) v[q] = q < P ? dsmem_ld_f32(rbase[q] + (uint32_t)((row * RS + m) * 4)) : 0.0f;
             float s = 0.0f;
 #pragma unroll
             for (int q = 0; q < 8; ++q)
@@ -762,33 +779,86 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             return v;
         };
         const unsigned int ar_tag_push = (p.epilogue == kEpiPush) ? *p.ar_step + 1u : 0u;
-        // Items it = ctid + 256 j map to batch row it % MB = ctid % MB (MB
-        // divides 256): one argmax key per thread.
+        // Item order.  Up to 8 batch rows per CTA: it = ctid + 256 j maps to
+        // batch row it % MB = ctid % MB (MB divides 256), one argmax key per
+        // thread.  From 16 rows on ("row-major" items): batch row it / nr,
+        // tile row it % nr (nr = rows of this rank), so a warp's stores go to
+        // consecutive outputs of one batch row; the argmax is reduced per
+        // item over the lanes that share a batch row.
         static_assert(256 % MB == 0, "batch rows per CTA divide the consumer threads");
+        constexpr bool RMAJ = MB >= 16;
+        const int nr = oe - ob;
+        auto item_m = [&](int it) -> int { return RMAJ ? it / nr : it % MB; };
+        auto item_o = [&](int it) -> int { return ob + (RMAJ ? it - (it / nr) * nr : it / MB); };
         unsigned long long best_mine = 0ull;
+        // Row-major batches first gather every finished row value of this
+        // rank into shared memory in batch-row-minor order (consecutive lanes
+        // read consecutive partial sums of every rank: coalesced DSMEM
+        // requests), then the item loop below reads them back row-major (its
+        // global loads and stores coalesce).  Staging [MB][SR] reuses the
+        // weight ring, idle once the accumulators are complete.
+        const bool pairs = p.epilogue == kEpiQkv || p.epilogue == kEpiSiluMul;
+        const int nloc = pairs ? 2 * nr : nr;  // tile rows of this rank
+        const int SR = nloc + 1;
+        float* stg = reinterpret_cast<float*>(stage_base);
+        auto loc_row = [&](int li) -> int {  // tile row of local index li
+            if (p.epilogue == kEpiQkv) return 2 * ob + li;
+            if (p.epilogue == kEpiSiluMul) return li < nr ? ob + li : HALF + ob + (li - nr);
+            return ob + li;
+        };
+        if constexpr (RMAJ) {
+            static_assert(!RMAJ || MB * (RB + 1) * 4 <= STAGES * Cfg::kStageBytes, "staging fits the ring");
+            // (a plain loop: this kernel is large and instruction-fetch bound
+            // when its epilogue loops are unrolled)
+#pragma unroll 1
+            for (int it = ctid; it < nloc * MB; it += 256) {
+                const int m = it % MB, li = it / MB;
+                const int row = loc_row(li);
+                stg[m * SR + li] = finish(rb * RB + row, rowsum(row, m));
+            }
+            named_bar_sync(1, 256);
+            if (PREC == 8 && ctid == 0) trace_max(p.trace, 8);
+        }
+        // finished value of tile row `row`, batch row m
+        auto rowval = [&](int row, int m) -> float {
+            if constexpr (RMAJ) {
+                int li;
+                if (p.epilogue == kEpiQkv) li = row - 2 * ob;
+                else if (p.epilogue == kEpiSiluMul) li = row < HALF ? row - ob : nr + (row - HALF - ob);
+                else li = row - ob;
+                return stg[m * SR + li];
+            } else {
+                return finish(rb * RB + row, rowsum(row, m));
+            }
+        };
 
         // Two phases per chunk of JC items, so that every global load of a
         // chunk is in flight together: (1) reduce, scale, issue the loads the
         // stores need (RoPE table, the residual); (2) finish and store.
         constexpr int JMAX = (RB * MB + 255) / 256;
-        constexpr int JC = JMAX < 4 ? JMAX : 4;
+        constexpr int JC = JMAX < (RMAJ ? 2 : 4) ? JMAX : (RMAJ ? 2 : 4);
+#pragma unroll 1
         for (int jb = 0; jb < JMAX; jb += JC) {
         float va[JC], vb[JC], old[JC];
         float2 cs[JC];
+        unsigned long long keyj[JC];
+        int keym[JC];
 #pragma unroll
         for (int j = 0; j < JC; ++j) {
+            keyj[j] = 0ull;
+            keym[j] = -1;
             va[j] = vb[j] = old[j] = 0.0f;
             cs[j] = make_float2(1.0f, 0.0f);
             const int it = ctid + 256 * (jb + j);
             if (it >= nitems) continue;
-            const int m = it % MB;
-            const int o = ob + it / MB;
+            const int m = item_m(it);
+            const int o = item_o(it);
             if (m >= Mloc) continue;
             if (p.epilogue == kEpiQkv) {
                 const int n0 = rb * RB + 2 * o;
                 if (n0 >= L.N) continue;
-                va[j] = finish(n0, rowsum(2 * o, m));
-                vb[j] = finish(n0 + 1, rowsum(2 * o + 1, m));
+                va[j] = rowval(2 * o, m);
+                vb[j] = rowval(2 * o + 1, m);
                 const int pos = seqinfo[m];
                 if (seqinfo[MB + m] && n0 < p.H + p.kv_dim && pos < p.rope_max_pos) {
                     const int i = (n0 < p.H ? n0 : n0 - p.H) % p.head_dim;
@@ -796,12 +866,12 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 }
             } else if (p.epilogue == kEpiSiluMul) {
                 if (rb * HALF + o >= L.N) continue;
-                va[j] = finish(rb * RB + o, rowsum(o, m));
-                vb[j] = finish(rb * RB + HALF + o, rowsum(HALF + o, m));
+                va[j] = rowval(o, m);
+                vb[j] = rowval(HALF + o, m);
             } else {
                 const int n = rb * RB + o;
                 if (n >= L.N) continue;
-                va[j] = finish(n, rowsum(o, m));
+                va[j] = rowval(o, m);
                 if (p.epilogue == kEpiResidual) old[j] = p.out[(size_t)(m0 + m) * p.ld_out + n];
             }
         }
@@ -809,8 +879,8 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         for (int j = 0; j < JC; ++j) {
             const int it = ctid + 256 * (jb + j);
             if (it >= nitems) continue;
-            const int m = it % MB;
-            const int o = ob + it / MB;
+            const int m = item_m(it);
+            const int o = item_o(it);
             if (m >= Mloc) continue;
             const int gm = m0 + m;  // batch row
             if (p.epilogue == kEpiQkv) {
@@ -875,21 +945,49 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 } else {  // kEpiArgmax
                     if (p.logits) p.logits[(size_t)gm * L.N + n] = v;
                     const unsigned long long key = argmax_key(v, n);
-                    if (key > best_mine) best_mine = key;
+                    if (RMAJ) {
+                        keyj[j] = key;
+                        keym[j] = m;
+                    } else if (key > best_mine) {
+                        best_mine = key;
+                    }
+                }
+            }
+        }
+        if (RMAJ && p.epilogue == kEpiArgmax) {
+            // lanes of one batch row are contiguous: per distinct row in the
+            // warp, a full-warp max over its lanes' keys, one atomic
+#pragma unroll
+            for (int j = 0; j < JC; ++j) {
+                unsigned pending = __ballot_sync(0xffffffffu, keym[j] >= 0);
+                while (pending) {
+                    const int leader = __ffs(pending) - 1;
+                    const int target = __shfl_sync(0xffffffffu, keym[j], leader);
+                    unsigned long long v = keym[j] == target ? keyj[j] : 0ull;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const unsigned long long t = __shfl_xor_sync(0xffffffffu, v, o);
+                        v = t > v ? t : v;
+                    }
+                    if (lane == leader && v != 0ull) atomicMax(&p.seq[m0 + target].best, v);
+                    pending &= ~__ballot_sync(0xffffffffu, keym[j] == target);
                 }
             }
         }
         }  // item chunks
+        if (PREC == 8 && ctid == 0) trace_max(p.trace, 9);
         if (p.epilogue == kEpiArgmax) {
             // lanes with the same batch row (lane % MB) combine, then one atomic per row and warp
-            unsigned long long b = best_mine;
+            if (!RMAJ) {
+                unsigned long long b = best_mine;
 #pragma unroll
-            for (int o = 16; o >= MB; o >>= 1) {
-                unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
-                b = t > b ? t : b;
+                for (int o = 16; o >= MB; o >>= 1) {
+                    unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+                    b = t > b ? t : b;
+                }
+                const int m = ctid % MB;
+                if (lane < MB && b != 0ull && m < Mloc) atomicMax(&p.seq[m0 + m].best, b);
             }
-            const int m = ctid % MB;
-            if (lane < MB && b != 0ull && m < Mloc) atomicMax(&p.seq[m0 + m].best, b);
             named_bar_sync(1, 256);
             if (ctid == 0) {
                 __threadfence();
@@ -930,8 +1028,13 @@ __global__ void __launch_bounds__(256) wide_digits_kernel(const __grid_constant_
     __shared__ float red[2][8];
     const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const QLayout& L = p.L;
+    if (tid == 0) {
+        trace_min(p.trace, 0);
+        trace_max(p.trace, 1);
+    }
     pdl_wait();
     pdl_launch_dependents();
+    if (tid == 0) trace_max(p.trace, 2);
     const bool embed = p.prologue == kProEmbed || p.prologue == kProEmbedRms;
     const bool rms = p.prologue == kProRmsNorm || p.prologue == kProEmbedRms;
     const float* sr;
@@ -974,6 +1077,8 @@ __global__ void __launch_bounds__(256) wide_digits_kernel(const __grid_constant_
         put_digits4_strided(p.bimg + (size_t)(k / kTcUnitK) * kBBytes, wide_lbo(NB), kWideSbo, k % kTcUnitK, m, a,
                             dscale);
     }
+    __syncthreads();
+    if (tid == 0) trace_max(p.trace, 6);
 }
 
 // Staged activation bytes of a CTA: INT8 digits (NB per k); INT4 fp32 x,
@@ -1024,6 +1129,63 @@ cudaError_t launch_t(const GemvParams& p, cudaStream_t stream, bool pdl) {
     cfg.attrs = attrs;
     cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, kfn, p);
+}
+
+// Clusters of P CTAs (one launch configuration of this kernel variant) that
+// can be resident at once: a cluster needs P SMs of one GPC with room, so
+// large clusters of large CTAs leave SMs unused; the occupancy API counts it.
+template <int PREC, int RB, int MB>
+int max_clusters_t(int P, size_t smem) {
+    auto kfn = gemv_kernel<PREC, RB, MB>;
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess) return 0;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)P, 1, 1);
+    cfg.blockDim = dim3(gemv_threads(PREC, MB), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute a[1];
+    a[0].id = cudaLaunchAttributeClusterDimension;
+    a[0].val.clusterDim.x = (unsigned)P;
+    a[0].val.clusterDim.y = 1;
+    a[0].val.clusterDim.z = 1;
+    cfg.attrs = a;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+int max_clusters(int prec, int mb, int P, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int, int, size_t>, int> cache;
+    int dev = 0;
+    (void)cudaGetDevice(&dev);
+    const auto key = std::make_tuple(dev, prec, mb, P, smem);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    if (prec == 8) {
+        switch (mb) {
+            case 1: n = max_clusters_t<8, 128, 1>(P, smem); break;
+            case 2: n = max_clusters_t<8, 128, 2>(P, smem); break;
+            case 4: n = max_clusters_t<8, 128, 4>(P, smem); break;
+            case 8: n = max_clusters_t<8, 128, 8>(P, smem); break;
+            case 16: n = max_clusters_t<8, 128, 16>(P, smem); break;
+            default: n = max_clusters_t<8, 128, 64>(P, smem); break;
+        }
+    } else {
+        switch (mb) {
+            case 1: n = max_clusters_t<4, 128, 1>(P, smem); break;
+            case 2: n = max_clusters_t<4, 128, 2>(P, smem); break;
+            default: n = max_clusters_t<4, 128, 4>(P, smem); break;
+        }
+    }
+    cache[key] = n;
+    return n;
 }
 
 }  // namespace
@@ -1078,11 +1240,21 @@ int choose_ksplit(const QLayout& L, int M, int num_sms) {
         const int occ = (int)std::min<size_t>(2, kSmPerSm / (smem + 1024));  // TMEM and registers: at most 2
         if (occ < 1) continue;
         const long long ctas = (long long)nrb * P * splits;
-        const long long cap = (long long)occ * num_sms;
+        // one CTA per SM (the wide variant): a cluster needs P free SMs of one
+        // GPC, so count co-resident clusters; at two per SM the plain count
+        // matched the measured launches better
+        const int clusters = occ == 1 ? max_clusters(L.precision, mb, P, smem) : 0;
+        const long long cap = clusters > 0 ? (long long)clusters * P : (long long)occ * num_sms;
         const long long waves = (ctas + cap - 1) / cap;
         const long long per_sm = (ctas + num_sms - 1) / num_sms;
         const int units = (L.slabs + P - 1) / P;
-        const double cost = waves * (kWaveUs + std::max(units * unit_us, (double)per_sm * units * unit_kb / kSmKBperUs));
+        // + the epilogue, serial in each CTA: ~0.5 ns per output item (row x batch row)
+        const double epi_us = (double)L.RB * mb / P * 0.0005;
+        const double cost =
+            waves * (kWaveUs + epi_us + std::max(units * unit_us, (double)per_sm * units * unit_kb / kSmKBperUs));
+        if (getenv("TB_GEMV_DEBUG"))
+            fprintf(stderr, "ksplit K=%d N=%d M=%d P=%d smem=%zu occ=%d clusters=%d ctas=%lld cap=%lld cost=%.2f\n",
+                    L.K, L.N, M, P, smem, occ, clusters, ctas, cap, cost);
         if (best == 0 || cost < best_cost) {
             best = P;
             best_cost = cost;

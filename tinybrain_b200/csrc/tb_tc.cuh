@@ -225,7 +225,11 @@ __device__ __forceinline__ void put_digits4_strided(uint8_t* xd, uint32_t lbo, u
 // Combined accumulator of one batch row: digits at columns 4m .. 4m+3.
 __device__ __forceinline__ float combine_digits(const int* d, int e) {
     const long long v = ((long long)d[0] << 21) + ((long long)d[1] << 14) + ((long long)d[2] << 7) + (long long)d[3];
-    return ldexpf(__ll2float_rn(v), e - 21);
+    const int k = e - 21;
+    // one rounding (int64 -> fp32), then an exact power-of-two scaling; the
+    // bit-pattern power of two covers the normal range, ldexpf the rest
+    const float f = __ll2float_rn(v);
+    return (k >= -126 && k <= 127) ? f * __int_as_float((k + 127) << 23) : ldexpf(f, k);
 }
 
 }  // namespace tb
