@@ -86,19 +86,25 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     const int nun = pg1 - pg0;
 
     if (warp == kAttnConsumerWarps) {
-        if (lane == 0) {
-            bool waited = false;
-            for (int i = 0; i < nun; ++i) {
-                const int st = i % kAttnStages;
-                if (i >= kAttnStages) {
-                    if (!mbar_wait(&empty[st], ((i / kAttnStages) - 1) & 1, p.err)) break;
-                }
-                const int lp = pg0 + i;
-                if ((p.wait_first || lp == npages - 1) && !waited) {  // pages the preceding kernel appends to
-                    pdl_wait();
-                    waited = true;
-                }
-                const int page = p.page_table[(size_t)m * p.ptab_stride + lp];
+        // The whole warp walks the pages: 32 page-table entries are loaded at
+        // a time, one per lane, so the copies are not serialised behind one
+        // dependent global load each; lane 0 waits and issues.
+        bool waited = false;
+        int pt = -1;
+        for (int i = 0; i < nun; ++i) {
+            const int st = i % kAttnStages;
+            if ((i & 31) == 0)
+                pt = i + lane < nun ? p.page_table[(size_t)m * p.ptab_stride + pg0 + i + lane] : -1;
+            const int page = __shfl_sync(0xffffffffu, pt, i & 31);
+            int ok = 1;
+            if (lane == 0 && i >= kAttnStages) ok = mbar_wait(&empty[st], ((i / kAttnStages) - 1) & 1, p.err);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            const int lp = pg0 + i;
+            if ((p.wait_first || lp == npages - 1) && !waited) {  // pages the preceding kernel appends to
+                pdl_wait();
+                waited = true;
+            }
+            if (lane == 0) {
                 float* kd = tiles + st * 2 * TILE;
                 if (page >= 0) {
                     valid[st] = 1;
@@ -330,57 +336,52 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 
 // ---------------------------------------------------------------------------
 // Grouped-query attention with 8 query heads per KV head and d = 64 (the
-// TinyLlama shape of the benchmark configurations).  Same grid, producer,
-// page ring and cluster combine as attn_decode_kernel, but the consumer
-// arithmetic is register-blocked so that each K and V element read from
-// shared memory serves all 8 heads:
-//   scores:  thread (token j, dim slice c) holds q of all 8 heads for its 8
-//            dims {4c..4c+3, 32+4c..32+4c+3} in registers, reads its 8 K
-//            values once (two conflict-free float4) and forms 8 partial dots;
-//            a reduce-scatter over the 8 slice lanes (4 + 2 + 1 shuffles)
-//            leaves lane c with head c's full dot for token j;
-//   softmax: per head, the page maximum over 16 tokens (two shuffles, then
-//            the four warps' maxima through shared memory), one exp per
-//            (token, head) and one per head for the running-max correction;
-//            each thread keeps a partial running sum of its tokens' weights;
-//   P.V:     thread (token pair tg, dim quad dc) keeps an 8-head x 4-dim
-//            accumulator, rescales it by the heads' corrections and adds its
-//            two tokens' weighted V rows (one float4 of V, two of weights,
-//            32 FMAs per token); the 8 token pairs' accumulators are summed
-//            once per CTA, in pair order, at the end.
-// Shared-memory reads per 8 KB page: ~16 KB (the generic kernel reads each
-// K / V tile once per head, 64 KB), which moved it off the shared-memory
-// pipe.  One consumer group of 4 warps and an 8-page ring per CTA, three
-// CTAs per SM.
+// TinyLlama shape of the benchmark configurations).  Same grid, cluster
+// combine and page table walk as attn_decode_kernel, but each split runs two
+// passes over its pages instead of an online softmax, so no page waits on
+// another page's softmax:
+//   pass 1 (K tiles): thread (token j, head h) holds head h's 64 query values
+//     in registers (rotated by 4j, so the four tokens of a warp read four
+//     different bank groups) and forms the full dot product from 16 float4
+//     reads of K row j that the 8 heads' lanes share (one broadcast each);
+//     the scores go to shared memory, S[page][token][head];
+//   the split's maximum per head (shuffles and four warp values), then
+//     weights 2^(s - max) in place and each thread's partial sum of them;
+//   pass 2 (V tiles): thread (token pair tg, dims 4dc..4dc+3) accumulates the
+//     8 heads' weighted V rows of its two tokens (one float4 of V, two of
+//     weights, 16 packed FFMA2 per token); the 8 token pairs' accumulators
+//     are summed once, in pair order.
+// The producer streams every page's K tile, then every page's V tile, through
+// one ring of 4 KB tiles; each byte of K and V is read from HBM once, as in the
+// one-pass kernel.  Scores are kept in base 2 (q.k / sqrt(d) * log2 e), the
+// same softmax.  A split covers at most kGqaMaxPages pages (launch_attn_gqa8
+// raises the split count for longer contexts; beyond 16 splits the generic
+// kernel runs).
 // ---------------------------------------------------------------------------
-constexpr int kGqaStages = 8;
+constexpr int kGqaRing = 12;      // 4 KB tiles in flight per CTA
+constexpr int kGqaMaxPages = 32;  // pages per split (scores: 16 KB)
 constexpr int kGqaThreads = (4 + 1) * 32;
 
 __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __grid_constant__ AttnParams p) {
     constexpr int G = 8, D = 64;
-    constexpr int TILE = kPageTokens * D;
-    static_assert(kGqaStages * 20 <= kAttnHead, "ring barriers exceed the header");
+    constexpr int TILE = kPageTokens * D;  // floats per K or V tile
+    static_assert(kGqaRing * 20 <= kAttnHead, "ring barriers exceed the header");
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kGqaStages;
-    int* valid = reinterpret_cast<int*>(empty + kGqaStages);  // [stages]
-    // scratch after the header: pm [2][G][4] page maxima per warp, Cs [2][G]
-    // corrections, Pw [2][16][G] weights, then the ring, then the combine area
-    float* pm = reinterpret_cast<float*>(smem + kAttnHead);
-    float* Cs = pm + 2 * G * 4;
-    float* Pw = Cs + 2 * G;
-    float* tiles = reinterpret_cast<float*>(smem + kAttnHead + 2048);
-    // [8 token pairs][G][D] accumulators, then l [16][G]: reuses the ring,
-    // which is idle once every page has been consumed
+    uint64_t* empty = full + kGqaRing;
+    int* valid = reinterpret_cast<int*>(empty + kGqaRing);  // [ring]
+    float* wmax = reinterpret_cast<float*>(smem + kAttnHead);    // [4 warps][G]
+    float* tiles = reinterpret_cast<float*>(smem + kAttnHead + 512);
+    float* S = tiles + kGqaRing * TILE;                          // [kGqaMaxPages][16][G]
+    float* cpart = S + kGqaMaxPages * kPageTokens * G;           // [G][D + 4]: acc, m, l of this split
+    // after pass 2: [8 token pairs][G][D] accumulators and l [16][G] reuse the ring
     float* red = tiles;
-    float* cpart = tiles + kGqaStages * 2 * TILE;  // [G][D + 4]: acc, m, l of this split
-    static_assert(8 * G * D + 16 * G <= kGqaStages * 2 * TILE, "reduction area fits the ring");
-    static_assert((2 * G * 4 + 2 * G + 2 * 16 * G) * 4 <= 2048, "scratch");
+    static_assert(8 * G * D + 16 * G <= kGqaRing * TILE, "reduction area fits the ring");
 
     const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kGqaStages; ++i) {
+        for (int i = 0; i < kGqaRing; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 4);
         }
@@ -398,33 +399,34 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
     const int pps = (npages + p.nsplit - 1) / p.nsplit;
     const int pg0 = min(npages, split * pps);
     const int pg1 = min(npages, pg0 + pps);
-    const int nun = pg1 - pg0;
+    const int nun = min(pg1 - pg0, kGqaMaxPages);  // the launcher keeps pps <= kGqaMaxPages
 
     if (warp == 4) {
-        // ------------------------------ producer ------------------------------
-        if (lane == 0) {
-            bool waited = false;
-            for (int i = 0; i < nun; ++i) {
-                const int st = i % kGqaStages;
-                if (i >= kGqaStages) {
-                    if (!mbar_wait(&empty[st], ((i / kGqaStages) - 1) & 1, p.err)) break;
-                }
-                const int lp = pg0 + i;
-                if ((p.wait_first || lp == npages - 1) && !waited) {  // pages the preceding kernel appends to
-                    pdl_wait();
-                    waited = true;
-                }
-                const int page = p.page_table[(size_t)m * p.ptab_stride + lp];
-                float* kd = tiles + st * 2 * TILE;
+        // --------- producer: K tiles of the split's pages, then V tiles ---------
+        // (the split's page-table entries are loaded once, one per lane, so no
+        // copy waits behind a dependent global load; lane 0 waits and issues)
+        bool waited = false;
+        const int pt = lane < nun ? p.page_table[(size_t)m * p.ptab_stride + pg0 + lane] : -1;
+        for (int i = 0; i < 2 * nun; ++i) {
+            const int st = i % kGqaRing;
+            const int kv = i < nun ? 0 : 1;
+            const int li = i < nun ? i : i - nun;
+            const int page = __shfl_sync(0xffffffffu, pt, li);
+            int ok = 1;
+            if (lane == 0 && i >= kGqaRing) ok = mbar_wait(&empty[st], ((i / kGqaRing) - 1) & 1, p.err);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            const int lp = pg0 + li;
+            if ((p.wait_first || lp == npages - 1) && !waited) {  // pages the preceding kernel appends to
+                pdl_wait();
+                waited = true;
+            }
+            if (lane == 0) {
                 if (page >= 0) {
                     valid[st] = 1;
-                    const size_t kbase =
-                        ((((size_t)page * p.num_layers + p.layer) * 2 + 0) * p.Hkv + kvh) * (size_t)TILE;
-                    const size_t vbase =
-                        ((((size_t)page * p.num_layers + p.layer) * 2 + 1) * p.Hkv + kvh) * (size_t)TILE;
-                    mbar_arrive_expect_tx(&full[st], 2u * TILE * 4u);
-                    bulk_g2s(kd, p.kv_pool + kbase, TILE * 4u, &full[st]);
-                    bulk_g2s(kd + TILE, p.kv_pool + vbase, TILE * 4u, &full[st]);
+                    const size_t base =
+                        ((((size_t)page * p.num_layers + p.layer) * 2 + kv) * p.Hkv + kvh) * (size_t)TILE;
+                    mbar_arrive_expect_tx(&full[st], TILE * 4u);
+                    bulk_g2s(tiles + st * TILE, p.kv_pool + base, TILE * 4u, &full[st]);
                 } else {
                     valid[st] = 0;  // evicted page: rows read as zeros
                     mbar_arrive(&full[st]);
@@ -436,116 +438,106 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
         pdl_wait();
         if (threadIdx.x == 0) trace_max(p.trace, 2);
         const int t = threadIdx.x;  // 0..127
-        // scores in base 2: (q.k) / sqrt(d) * log2(e), weights 2^(s - max) --
-        // the same softmax, one ex2 per weight
         const float scale2 = __fmul_rn(__fdiv_rn(1.0f, __fsqrt_rn((float)D)), 1.4426950408889634f);
-        // score role: token j, dim slice c (dims 4c..4c+3 and 32+4c..32+4c+3)
-        const int j = t >> 3, c = t & 7;
-        float qr[G][8];
+        // pass-1 role: lane bits [c:2][hs:1][token:2] -- token j = 4 warp +
+        // (lane >> 3), dim quarter c (16 dims), heads 4 hs..4 hs+3.  The four
+        // float4 of a quarter are read in the order (e + j) & 3, so the 16
+        // addresses of a warp load fall in 8 bank groups (two wavefronts, the
+        // minimum).  After a reduce-scatter over the 4 quarters the lane holds
+        // the full dot of token j, head h = 4 hs + c.
+        const int c = lane & 3, hs = (lane >> 2) & 1;
+        const int j = 4 * warp + (lane >> 3), h = 4 * hs + c;
+        float2 qr[4][4][2];  // [head of the half][float4 e][pair]
         {
-            const float* qb = p.q + (size_t)m * p.ld_q + (size_t)kvh * G * D;
+            const float* qb = p.q + (size_t)m * p.ld_q + (size_t)(kvh * G + 4 * hs) * D + 16 * c;
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-                const float4 a = *reinterpret_cast<const float4*>(qb + h * D + 4 * c);
-                const float4 b = *reinterpret_cast<const float4*>(qb + h * D + 32 + 4 * c);
-                qr[h][0] = a.x; qr[h][1] = a.y; qr[h][2] = a.z; qr[h][3] = a.w;
-                qr[h][4] = b.x; qr[h][5] = b.y; qr[h][6] = b.z; qr[h][7] = b.w;
-            }
+            for (int hh = 0; hh < 4; ++hh)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float4 a = *reinterpret_cast<const float4*>(qb + hh * D + 4 * ((e + j) & 3));
+                    qr[hh][e][0] = make_float2(a.x, a.y);
+                    qr[hh][e][1] = make_float2(a.z, a.w);
+                }
         }
-        // P.V role: token pair tg (tokens 2tg, 2tg + 1), dims 4dc..4dc+3
-        const int tg = t >> 4, dc = t & 15;
-        float acc[G][4];
-#pragma unroll
-        for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
-        float run_m = -INFINITY, l_part = 0.0f;  // head c, this thread's tokens
-
         bool bad = false;
+        float mt = -INFINITY;  // this thread's maximum score (head h)
         for (int i = 0; i < nun; ++i) {
-            const int st = i % kGqaStages, b2 = i & 1;
-            if (!bad && !mbar_wait(&full[st], (i / kGqaStages) & 1, p.err)) bad = true;
-            const float* Kt = tiles + st * 2 * TILE;
-            const float* Vt = Kt + TILE;
-            const bool ok = !bad && valid[st] != 0;
-            // ---- scores of token j for the 8 heads ----
-            float s[G];
+            const int st = i % kGqaRing;
+            if (!bad && !mbar_wait(&full[st], (i / kGqaRing) & 1, p.err)) bad = true;
+            const float* Kr = tiles + st * TILE + j * D + 16 * c;
+            float part[4] = {0.f, 0.f, 0.f, 0.f};
+            if (!bad && valid[st]) {
+                float4 kv[4];
 #pragma unroll
-            for (int h = 0; h < G; ++h) s[h] = 0.0f;
-            if (ok) {
-                const float4 ka = *reinterpret_cast<const float4*>(Kt + j * D + 4 * c);
-                const float4 kb = *reinterpret_cast<const float4*>(Kt + j * D + 32 + 4 * c);
+                for (int e = 0; e < 4; ++e) kv[e] = *reinterpret_cast<const float4*>(Kr + 4 * ((e + j) & 3));
 #pragma unroll
-                for (int h = 0; h < G; ++h) {
-                    float d0 = qr[h][0] * ka.x;
-                    float d1 = qr[h][1] * ka.y;
-                    d0 = fmaf(qr[h][2], ka.z, d0);
-                    d1 = fmaf(qr[h][3], ka.w, d1);
-                    d0 = fmaf(qr[h][4], kb.x, d0);
-                    d1 = fmaf(qr[h][5], kb.y, d1);
-                    d0 = fmaf(qr[h][6], kb.z, d0);
-                    d1 = fmaf(qr[h][7], kb.w, d1);
-                    s[h] = d0 + d1;
+                for (int hh = 0; hh < 4; ++hh) {
+                    float2 d = __fmul2_rn(qr[hh][0][0], make_float2(kv[0].x, kv[0].y));
+                    d = __ffma2_rn(qr[hh][0][1], make_float2(kv[0].z, kv[0].w), d);
+#pragma unroll
+                    for (int e = 1; e < 4; ++e) {
+                        d = __ffma2_rn(qr[hh][e][0], make_float2(kv[e].x, kv[e].y), d);
+                        d = __ffma2_rn(qr[hh][e][1], make_float2(kv[e].z, kv[e].w), d);
+                    }
+                    part[hh] = d.x + d.y;
                 }
             }
-            // reduce-scatter over the 8 slice lanes: lane c ends with head c
-            float r4[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float mine = (c & 4) ? s[4 + k] : s[k];
-                const float other = (c & 4) ? s[k] : s[4 + k];
-                r4[k] = mine + __shfl_xor_sync(0xffffffffu, other, 4);
-            }
+            // reduce-scatter over the quarters (lane bits 0-1): lane c keeps head c
             float r2[2];
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                const float mine = (c & 2) ? r4[2 + k] : r4[k];
-                const float other = (c & 2) ? r4[k] : r4[2 + k];
-                r2[k] = mine + __shfl_xor_sync(0xffffffffu, other, 2);
+            for (int u = 0; u < 2; ++u) {
+                const float mine = (c & 2) ? part[2 + u] : part[u];
+                const float other = (c & 2) ? part[u] : part[2 + u];
+                r2[u] = mine + __shfl_xor_sync(0xffffffffu, other, 2);
             }
             const float mine = (c & 1) ? r2[1] : r2[0];
             const float other = (c & 1) ? r2[0] : r2[1];
             const float dot = mine + __shfl_xor_sync(0xffffffffu, other, 1);
             const int tok = (pg0 + i) * kPageTokens + j;
             const float sc = (tok < Lq) ? __fmul_rn(dot, scale2) : -INFINITY;
-            // ---- page maximum of head c: the warp's 4 tokens, then the 4 warps ----
-            float wm = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 8));
-            wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 16));
-            if (lane < 8) pm[(b2 * G + c) * 4 + warp] = wm;
-            named_bar_sync(1, 128);
-            const float4 w4 = *reinterpret_cast<const float4*>(pm + (b2 * G + c) * 4);
-            const float mnew = fmaxf(run_m, fmaxf(fmaxf(w4.x, w4.y), fmaxf(w4.z, w4.w)));
-            const float e = (sc == -INFINITY) ? 0.0f : exp2f(sc - mnew);
-            if (j == 0) Cs[b2 * G + c] = (run_m == -INFINITY) ? 0.0f : exp2f(run_m - mnew);
-            run_m = mnew;
-            Pw[(b2 * 16 + j) * G + c] = e;
-            named_bar_sync(1, 128);
-            l_part = fmaf(l_part, Cs[b2 * G + c], e);
-            // ---- P.V for tokens 2tg, 2tg + 1 ----
-            {
-                const float4 ca = *reinterpret_cast<const float4*>(Cs + b2 * G);
-                const float4 cb = *reinterpret_cast<const float4*>(Cs + b2 * G + 4);
-                const float cr[G] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+            S[(i * kPageTokens + j) * G + h] = sc;
+            mt = fmaxf(mt, sc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        // the split's maximum of head h: the 4 tokens of the warp, then the 4 warps
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+        if (lane < 8) wmax[warp * G + h] = mt;  // lanes 0-7: h = 4 hs + c covers 0..7
+        named_bar_sync(1, 128);
+        const float M = fmaxf(fmaxf(wmax[h], wmax[G + h]), fmaxf(wmax[2 * G + h], wmax[3 * G + h]));
+        // weights of this thread's own scores (no barrier needed) and their sum
+        float l_part = 0.0f;
+        for (int i = 0; i < nun; ++i) {
+            float* sp = S + (i * kPageTokens + j) * G + h;
+            const float e = (*sp == -INFINITY) ? 0.0f : exp2f(*sp - M);
+            *sp = e;
+            l_part += e;
+        }
+        named_bar_sync(1, 128);
+        // pass 2: P.V for tokens 2tg, 2tg + 1 of every page
+        const int tg = t >> 4, dc = t & 15;
+        float2 acc[G][2];
 #pragma unroll
-                for (int h = 0; h < G; ++h) {
-                    acc[h][0] *= cr[h];
-                    acc[h][1] *= cr[h];
-                    acc[h][2] *= cr[h];
-                    acc[h][3] *= cr[h];
-                }
-                if (ok) {
+        for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = make_float2(0.0f, 0.0f);
+        for (int i = 0; i < nun; ++i) {
+            const int q = nun + i, st = q % kGqaRing;
+            if (!bad && !mbar_wait(&full[st], (q / kGqaRing) & 1, p.err)) bad = true;
+            if (!bad && valid[st]) {
+                const float* Vt = tiles + st * TILE;
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int jj = 2 * tg + u;
-                        const float4 v = *reinterpret_cast<const float4*>(Vt + jj * D + 4 * dc);
-                        const float4 pa = *reinterpret_cast<const float4*>(Pw + (b2 * 16 + jj) * G);
-                        const float4 pb = *reinterpret_cast<const float4*>(Pw + (b2 * 16 + jj) * G + 4);
-                        const float pw[G] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+                for (int u = 0; u < 2; ++u) {
+                    const int jj = 2 * tg + u;
+                    const float4 v = *reinterpret_cast<const float4*>(Vt + jj * D + 4 * dc);
+                    const float4 pa = *reinterpret_cast<const float4*>(S + (i * kPageTokens + jj) * G);
+                    const float4 pb = *reinterpret_cast<const float4*>(S + (i * kPageTokens + jj) * G + 4);
+                    const float pw[G] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+                    const float2 v01 = make_float2(v.x, v.y), v23 = make_float2(v.z, v.w);
 #pragma unroll
-                        for (int h = 0; h < G; ++h) {
-                            acc[h][0] = fmaf(pw[h], v.x, acc[h][0]);
-                            acc[h][1] = fmaf(pw[h], v.y, acc[h][1]);
-                            acc[h][2] = fmaf(pw[h], v.z, acc[h][2]);
-                            acc[h][3] = fmaf(pw[h], v.w, acc[h][3]);
-                        }
+                    for (int g = 0; g < G; ++g) {
+                        const float2 w2 = make_float2(pw[g], pw[g]);
+                        acc[g][0] = __ffma2_rn(w2, v01, acc[g][0]);
+                        acc[g][1] = __ffma2_rn(w2, v23, acc[g][1]);
                     }
                 }
             }
@@ -555,33 +547,32 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
         // ---- this split's (acc, m, l): token pairs summed in pair order ----
         named_bar_sync(1, 128);  // every warp is done with the ring
 #pragma unroll
-        for (int h = 0; h < G; ++h)
-            *reinterpret_cast<float4*>(red + (tg * G + h) * D + 4 * dc) =
-                make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-        red[8 * G * D + j * G + c] = l_part;
+        for (int g = 0; g < G; ++g)
+            *reinterpret_cast<float4*>(red + (tg * G + g) * D + 4 * dc) =
+                make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
+        red[8 * G * D + j * G + h] = l_part;
         named_bar_sync(1, 128);
         {
-            // thread t: head t / 16, dims 4 (t % 16) .. +3
-            const int h = t >> 4, d4 = 4 * (t & 15);
+            const int g = t >> 4, d4 = 4 * (t & 15);
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-                const float4 v = *reinterpret_cast<const float4*>(red + (q * G + h) * D + d4);
+                const float4 v = *reinterpret_cast<const float4*>(red + (q * G + g) * D + d4);
                 a.x += v.x;
                 a.y += v.y;
                 a.z += v.z;
                 a.w += v.w;
             }
-            *reinterpret_cast<float4*>(cpart + h * (D + 4) + d4) = a;
+            *reinterpret_cast<float4*>(cpart + g * (D + 4) + d4) = a;
         }
-        if (t < G) {  // head t: running max (identical in every thread of the head), sum of the 16 tokens' sums
+        if (t < G) {  // head h of lanes 0-7 of warp 0: the split's maximum and the 16 tokens' sums
             float l = 0.0f;
-            for (int q = 0; q < 16; ++q) l += red[8 * G * D + q * G + t];
-            cpart[t * (D + 4) + D] = __shfl_sync(0x000000ffu, run_m, t);  // lane t holds head t (j = 0)
-            cpart[t * (D + 4) + D + 1] = l;
+            for (int q = 0; q < 16; ++q) l += red[8 * G * D + q * G + h];
+            cpart[h * (D + 4) + D] = M;
+            cpart[h * (D + 4) + D + 1] = l;
         }
     }
-    // Combine the splits (cluster ranks) in split order, as attn_decode_kernel.
+    // Combine the splits (cluster ranks) in split order (maxima in base 2).
     const int ns = p.nsplit;
     if (ns > 1) cluster_sync();
     else __syncthreads();
@@ -597,12 +588,12 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
 #pragma unroll
             for (int q = 0; q < kMaxAttnSplits; ++q)
                 mq[q] = q < ns ? dsmem_ld_f32(dsmem_map(cpart + g * (D + 4) + D, (uint32_t)q)) : -INFINITY;
-            float M = -INFINITY;
+            float Mx = -INFINITY;
 #pragma unroll
-            for (int q = 0; q < kMaxAttnSplits; ++q) M = fmaxf(M, mq[q]);
+            for (int q = 0; q < kMaxAttnSplits; ++q) Mx = fmaxf(Mx, mq[q]);
             float den = 0.0f;
             float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (M != -INFINITY) {
+            if (Mx != -INFINITY) {
 #pragma unroll
                 for (int q0 = 0; q0 < kMaxAttnSplits; q0 += 8) {
                     if (q0 >= ns) break;
@@ -624,7 +615,7 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
                     for (int u = 0; u < 8; ++u) {
                         const int q = q0 + u;
                         if (q >= ns) continue;
-                        const float w = (mq[q] == -INFINITY) ? 0.0f : exp2f(mq[q] - M);  // base-2 maxima
+                        const float w = (mq[q] == -INFINITY) ? 0.0f : exp2f(mq[q] - Mx);
                         den = fmaf(w, lq[u], den);
                         num.x = fmaf(w, aq[u].x, num.x);
                         num.y = fmaf(w, aq[u].y, num.y);
@@ -642,7 +633,8 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
 }
 
 size_t attn_gqa8_smem() {
-    return kAttnHead + 2048 + (size_t)kGqaStages * 2 * kPageTokens * 64 * 4 + (size_t)8 * (64 + 4) * 4;
+    return kAttnHead + 512 + (size_t)kGqaRing * kPageTokens * 64 * 4 + (size_t)kGqaMaxPages * kPageTokens * 8 * 4 +
+           (size_t)8 * (64 + 4) * 4;
 }
 
 cudaError_t launch_attn_gqa8(const AttnParams& p, cudaStream_t stream, bool pdl) {
@@ -806,7 +798,14 @@ int choose_nsplit(int M, int Hkv, int max_pages, int num_sms, bool balance_long)
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
     const int G = p.H / p.Hkv;
     if (p.H % p.Hkv != 0) return cudaErrorInvalidValue;
-    if (G == 8 && p.d == 64 && !getenv("TB_ATTN_GENERIC")) return launch_attn_gqa8(p, stream, pdl);
+    if (G == 8 && p.d == 64 && !getenv("TB_ATTN_GENERIC")) {
+        // at most kGqaMaxPages pages per split; the page table's width bounds
+        // a sequence's pages, so raise the split count to cover it
+        const int need = (p.ptab_stride + kGqaMaxPages - 1) / kGqaMaxPages;
+        AttnParams q = p;
+        if (need > q.nsplit) q.nsplit = need;
+        if (q.nsplit <= kMaxAttnSplits) return launch_attn_gqa8(q, stream, pdl);
+    }
 #define TB_ATTN_CASE(g, dd) \
     if (G == g && p.d == dd) return launch_attn_t<g, dd>(p, stream, pdl);
     TB_ATTN_CASE(1, 16)

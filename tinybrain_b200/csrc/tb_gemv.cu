@@ -1028,6 +1028,10 @@ __global__ void __launch_bounds__(256) wide_digits_kernel(const __grid_constant_
     __shared__ float red[2][8];
     const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const QLayout& L = p.L;
+    // CTA (m, c) writes the digit planes of units [u0, u1); every CTA of a row
+    // reduces the whole row (the same sums in the same order, so all chunks
+    // agree on the row's exponent)
+    const int u0 = blockIdx.y * L.slabs / gridDim.y, u1 = (blockIdx.y + 1) * L.slabs / gridDim.y;
     if (tid == 0) {
         trace_min(p.trace, 0);
         trace_max(p.trace, 1);
@@ -1068,10 +1072,10 @@ __global__ void __launch_bounds__(256) wide_digits_kernel(const __grid_constant_
     float bmax = 0.0f;
     for (int w = 0; w < 8; ++w) bmax = fmaxf(bmax, red[1][w]);
     const int ex = digit_exponent(bmax);
-    if (tid == 0) p.rowex_g[m] = ex;
+    if (tid == 0 && blockIdx.y == 0) p.rowex_g[m] = ex;
     const float dscale = __int_as_float((127 - ex) << 23);
     constexpr uint32_t kBBytes = wide_lbo(NB) * 8;
-    for (int q = tid; q < L.Kp / 4; q += 256) {  // 4 consecutive k per step
+    for (int q = u0 * (kTcUnitK / 4) + tid; q < u1 * (kTcUnitK / 4); q += 256) {  // 4 consecutive k per step
         const int k = 4 * q;
         const float4 a = make_float4(xval(k), xval(k + 1), xval(k + 2), xval(k + 3));
         put_digits4_strided(p.bimg + (size_t)(k / kTcUnitK) * kBBytes, wide_lbo(NB), kWideSbo, k % kTcUnitK, m, a,
@@ -1197,7 +1201,7 @@ size_t wide_digits_bytes(const QLayout& L) { return (size_t)L.slabs * wide_lbo(t
 cudaError_t launch_wide_digits(const GemvParams& p, cudaStream_t stream, bool pdl) {
     if (!p.bimg || !p.rowex_g || !gemv_uses_wide(p.L.precision, p.M)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)p.M);
+    cfg.gridDim = dim3((unsigned)p.M, (unsigned)std::min(8, p.L.slabs));
     cfg.blockDim = dim3(256);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -1240,10 +1244,10 @@ int choose_ksplit(const QLayout& L, int M, int num_sms) {
         const int occ = (int)std::min<size_t>(2, kSmPerSm / (smem + 1024));  // TMEM and registers: at most 2
         if (occ < 1) continue;
         const long long ctas = (long long)nrb * P * splits;
-        // one CTA per SM (the wide variant): a cluster needs P free SMs of one
-        // GPC, so count co-resident clusters; at two per SM the plain count
-        // matched the measured launches better
-        const int clusters = occ == 1 ? max_clusters(L.precision, mb, P, smem) : 0;
+        // A cluster needs P free SMs of one GPC: with one CTA per SM (the wide
+        // variant) or clusters beyond 4 CTAs, count the co-resident clusters;
+        // small clusters at two CTAs per SM were measured to fit as counted
+        const int clusters = (occ == 1 || P > 4) ? max_clusters(L.precision, mb, P, smem) : 0;
         const long long cap = clusters > 0 ? (long long)clusters * P : (long long)occ * num_sms;
         const long long waves = (ctas + cap - 1) / cap;
         const long long per_sm = (ctas + num_sms - 1) / num_sms;
