@@ -282,10 +282,12 @@ tb_status tb_runner_kv_length(const tb_runner *r, int32_t seq, int64_t *length);
 tb_status tb_runner_page_status(const tb_runner *r, int32_t seq, uint8_t *status, int64_t n);
 tb_status tb_runner_max_pages(const tb_runner *r, int64_t *n);
 
-/* Execution mode of a runner's decode step.  Batch-1 LLaMA runners default to
- * the persistent single-kernel step (one cooperative launch per token streams
- * every layer's weights through a shared-memory ring); other runners, or
- * enable = 0, use one fused kernel per projection and attention. */
+/* Execution mode of a runner's decode step.  Default (enable = 0): one fused
+ * kernel per projection and attention, the step captured as one CUDA graph.
+ * enable = 1 (batch-1 INT8 LLaMA runners): the persistent single-kernel step
+ * (one cooperative launch per token streams every layer's weights through a
+ * shared-memory ring); measured slower than the per-projection chain, kept as
+ * an option. */
 tb_status tb_runner_set_persistent(tb_runner *r, int32_t enable);
 tb_status tb_runner_get_persistent(const tb_runner *r, int32_t *enabled);
 /* Prompt prefill of tb_runner_generate (default on): up to 64 prompt tokens

@@ -82,3 +82,22 @@ def test_context_without_device_reports_error():
     st = _lib.load().tb_context_create(0, C.byref(h))
     assert st == 7  # TB_ERR_NO_DEVICE
     assert _lib.last_error()
+
+
+def test_swift_binding_calls_only_exported_symbols():
+    # The Swift target (Sources/TinyBrainCUDA) binds the header through the
+    # module map; every tb_* function it calls must be declared and exported.
+    src = os.path.join(ROOT, "Sources", "TinyBrainCUDA")
+    used = set()
+    for f in glob.glob(os.path.join(src, "*.swift")):
+        used |= set(re.findall(r"\b(tb_[a-z0-9_]+)\(", open(f).read()))
+    types = {"tb_model_config", "tb_sampler_config", "tb_qtensor_desc", "tb_status", "tb_projection",
+             "tb_token_callback"}
+    calls = used - types
+    assert {"tb_matmul_quantized", "tb_runner_generate", "tb_runner_set_sampler", "tb_qweight_upload"} <= calls
+    declared = set(declared_functions())
+    assert calls <= declared, calls - declared
+    lib = C.CDLL(_lib.LIB_PATH)
+    assert all(hasattr(lib, n) for n in calls)
+    mm = open(os.path.join(ROOT, "Sources", "CTinyBrainCUDA", "module.modulemap")).read()
+    assert 'link "tinybrain_cuda"' in mm and "tinybrain_cuda.h" in mm
