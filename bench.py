@@ -328,8 +328,10 @@ def run_config4(args, env, cpu=True):
     mine = [i for i in range(C4_SEQS) if owner[i] == env.rank]
     ctx = Context(env.local)
     t_build = time.perf_counter()
-    weights = build_tinyllama(ctx, max_seq_len=C4_MAXLEN)
-    runner = ModelRunner(weights, ctx, max_batch=len(mine), max_positions=C4_MAXLEN + 64)
+    # profiling captures (--prompt-len) size the KV pool for the capped prompts
+    maxlen = C4_MAXLEN if not args.prompt_len else args.prompt_len + C4_NEW + 64
+    weights = build_tinyllama(ctx, max_seq_len=maxlen)
+    runner = ModelRunner(weights, ctx, max_batch=len(mine), max_positions=maxlen + 64)
     build_s = time.perf_counter() - t_build
     my_prompts = [prompts[i] for i in mine]
     W = args.warmup
@@ -412,8 +414,9 @@ def run_config4(args, env, cpu=True):
 
 
 # ------------------------------------------------------------------ config 2 --
-def run_config2(args, env, mode="perChannel"):
-    """BASELINE config 2 (mode int4: config 3): one sequence, batch 1."""
+def run_config2(args, env, mode="perChannel", steps=None):
+    """BASELINE config 2 (mode int4: config 3): one sequence, batch 1.
+    steps: timed steps (default --steps when run alone, --b1-steps nested)."""
     from tinybrain_b200.runtime import Context, ModelRunner
     from tinybrain_b200.synthetic import random_prompt
     cfg3 = mode == "int4"
@@ -428,7 +431,7 @@ def run_config2(args, env, mode="perChannel"):
         W, K = args.warmup, min(args.steps, 128 - args.warmup)
     else:
         prompt = random_prompt(args.prompt_len or 128, 32000, 2)
-        W, K = args.warmup, min(args.b1_steps, 256 - args.warmup)
+        W, K = args.warmup, min(steps or args.steps, 256 - args.warmup)
     runner.ctx.synchronize()
     t_pf = time.perf_counter()
     runner.prefill_device([prompt], W + K)
@@ -494,7 +497,7 @@ def run_config2(args, env, mode="perChannel"):
 
 
 # ------------------------------------------------------------------ config 5 --
-def run_config5(args, env):
+def run_config5(args, env, steps=None):
     """Llama-2-7B-shaped INT4-g32, batch 1, prompt 512 (seed 5),
     greedy decode, tensor parallel over the ranks."""
     from tinybrain_b200.runtime import Context, ModelConfig, ModelRunner, tp_unique_id
@@ -518,7 +521,7 @@ def run_config5(args, env):
     build_s = time.perf_counter() - t_build
     prompt = random_prompt(n_prompt, 32000, 5)
     W = args.warmup
-    K = min(args.tp_steps, n_new - W)
+    K = min(steps or args.steps, n_new - W)
     t0 = time.perf_counter()
     runner.prefill_device([prompt], W + K)
     prefill_s = time.perf_counter() - t0
@@ -670,6 +673,72 @@ def run_config6(args):
     }
 
 
+# ------------------------------------------------- standalone attention --
+def run_attention_kernel(args):
+    """--kernel attention: the paged decode attention of one layer at the
+    headline shape (64 sequences, contexts = config 4's prompt lengths + 128,
+    32 query / 4 KV heads, d 64, scattered pages), through
+    tb_paged_attention_dev, CUDA events over `--steps` launches on the
+    context's stream.  K/V bytes per launch: every context position's K and V
+    row of its KV head, once."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    from tinybrain_b200 import _lib
+    from tinybrain_b200.runtime import Context
+    ctx = Context(0)
+    lens = [int(n) + C4_NEW for n in config4_workload(1)[0]]
+    H, Hkv, d = 32, 4, 64
+    pages = [(n + 15) // 16 for n in lens]
+    stride, total = max(pages), sum(pages)
+    perm = np.random.default_rng(1).permutation(total)
+    ptab = np.full((len(lens), stride), -1, dtype=np.int32)
+    k = 0
+    for s_, n in enumerate(pages):
+        ptab[s_, :n] = perm[k:k + n]
+        k += n
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    pool = torch.randn(total, 1, 2, Hkv, 16, d, device=dev, generator=g)
+    q = torch.randn(len(lens), H * d, device=dev, generator=g)
+    out = torch.zeros(len(lens), H * d, device=dev)
+    pt = torch.tensor(ptab, device=dev)
+    ln = torch.tensor(lens, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+
+    def launch():
+        _lib.check(lib.tb_paged_attention_dev(ctx.handle, P(q), len(lens), P(pool), P(pt), stride, P(ln), max(lens),
+                                              0, 1, H, Hkv, d, P(out)))
+
+    for _ in range(args.warmup):
+        launch()
+    ctx.synchronize()
+    st = torch.cuda.ExternalStream(lib.tb_context_stream(ctx.handle))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    K = max(1, args.steps)
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0.record(st)
+    for _ in range(K):
+        launch()
+    e1.record(st)
+    e1.synchronize()
+    clk = clocks.stop()
+    ctx.check_device()
+    us = e0.elapsed_time(e1) * 1000.0 / K
+    nbytes = sum(lens) * Hkv * d * 2 * 4
+    peak, kind = measured_peaks()
+    print(json.dumps({"metric": "paged decode attention HBM GB/s (one layer, config 4 shape)",
+                      "value": nbytes / (us * 1e-6) / 1e9, "unit": "GB/s", "us_per_launch": us,
+                      "bytes_per_launch": nbytes, "frac": nbytes / (us * 1e-6) / 1e9 / peak,
+                      "peak": peak, "peak_source": kind, "launches": K, "warmup": args.warmup,
+                      "config": {"sequences": len(lens), "tokens": sum(lens), "heads": "32q/4kv", "head_dim": d,
+                                 "l2": "K/V of one launch (350 MB) exceed L2"},
+                      "clocks": clk}), flush=True)
+    return 0
+
+
 # ------------------------------------------------------------------ arms --
 def run_reference(args):
     """--impl reference: the reference's CPU algorithm on the host cores, on the
@@ -719,9 +788,9 @@ def run_ours(args):
         line = run_config4(args, env)
         if cfg is None:
             if env.world == 1:
-                line["b1"] = run_config2(args, env)
+                line["b1"] = run_config2(args, env, steps=args.b1_steps)
                 line["gemv_config1"] = run_config1(args)
-            line["tp"] = run_config5(args, env)
+            line["tp"] = run_config5(args, env, steps=args.tp_steps)
     if env.rank == 0:
         line.setdefault("n_gpus", env.world)
         print(json.dumps(line), flush=True)
@@ -746,11 +815,15 @@ def main():
     ap.add_argument("--config", type=int, default=None, choices=[1, 2, 3, 4, 5, 6],
                     help="run one BASELINE config alone: 1 single GEMV, 2 TinyLlama INT8 b=1, 3 INT4 at context 2k, "
                          "4 64 sequences data parallel, 5 7B INT4 tensor parallel, 6 perplexity harness")
+    ap.add_argument("--kernel", default=None, choices=["attention"],
+                    help="time one kernel alone at the headline shape (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.kernel == "attention":
+        return run_attention_kernel(args)
     return run_ours(args)
 
 
