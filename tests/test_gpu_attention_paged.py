@@ -82,3 +82,26 @@ def test_generic_kernel_paged_batch(ctx, H, Hkv, d):
     torch = pytest.importorskip("torch")
     c = _case(torch, H + d, [1000, 3, 64, 129], H, Hkv, d)
     assert rel_l2(_device(torch, ctx, c), _numpy(c)) <= 1e-5
+
+
+@pytest.mark.parametrize("mode", ["perChannel", "int4"])
+def test_runner_persistent_attention_matches_cluster_kernel_and_oracle(ctx, monkeypatch, mode):
+    # GQA-8 / d 64 runners use the persistent chunked attention (chunk
+    # partials merged by the last chunk of each (row, KV head)); contexts of
+    # 1 to 40 pages, some rows a single chunk; the same batch through the
+    # cluster kernel (TB_ATTN_CLUSTER=1) and the oracle must agree
+    import oracle
+    from tests.helpers import assert_same_tokens, small_llama
+    from tinybrain_b200.runtime import ModelConfig, ModelRunner
+    cfg = ModelConfig(num_layers=2, hidden_dim=512, num_heads=8, vocab_size=512, max_seq_len=700, num_kv_heads=1,
+                      intermediate_dim=512)
+    w = small_llama(cfg, seed=21, mode=mode)
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, 512, n).tolist() for n in (640, 1, 17, 300, 33, 129)]
+    flat = ModelRunner(w, ctx, max_batch=len(prompts), max_positions=760).generate_batch(prompts, 10)
+    monkeypatch.setenv("TB_ATTN_CLUSTER", "1")
+    clus = ModelRunner(w, ctx, max_batch=len(prompts), max_positions=760).generate_batch(prompts, 10)
+    for p, a, b in zip(prompts, flat, clus):
+        want, gaps = oracle.OracleModel(w, mode=1).generate_greedy(p, 10)
+        assert_same_tokens(a, want, gaps, w, p)
+        assert_same_tokens(b, want, gaps, w, p)

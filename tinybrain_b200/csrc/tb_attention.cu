@@ -632,6 +632,471 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
     if (threadIdx.x == 0) trace_max(p.trace, 6);
 }
 
+// ---------------------------------------------------------------------------
+// Persistent chunked GQA-8 attention (runner plans; d = 64, 8 query heads per
+// KV head, up to kFlatMaxRows rows).  The cluster kernel above gives every
+// (sequence, KV head) the same number of splits, so with ragged contexts its
+// CTAs differ in length and run in ~5 short waves, each CTA paying its own
+// start (q load, first page) and end (cluster combine).  Here the work is cut
+// into chunks of chunk_pages pages per (sequence, KV head) -- equal except the
+// last of each -- and a fixed grid of 3 CTAs per SM walks them round robin;
+// the producer streams the next chunk's tiles while the consumers finish the
+// current one, so HBM streaming does not stop between chunks.  Chunk order:
+// every non-final chunk of every sequence first, then the final ones (which
+// hold the page the preceding QKV kernel appends to), so a CTA fetches its
+// first chunks before the programmatic-dependent-launch wait.  Each chunk runs
+// the two passes of attn_gqa8_d64_kernel and writes its partial (acc, m, l) to
+// `part`; the CTA that completes the last chunk of a (sequence, KV head)
+// (a ticket counter) merges the partials in chunk order -- deterministic --
+// writes the output and resets the ticket.  A single-chunk pair writes its
+// output directly.
+// ---------------------------------------------------------------------------
+constexpr int kFlatRing = 12;       // 4 KB tiles in flight per CTA
+constexpr int kFlatMaxPages = 16;   // pages per chunk at most
+constexpr int kFlatMaxRows = 64;    // sequences (rows) per launch
+constexpr int kFlatThreads = (4 + 1) * 32;
+
+struct FlatChunk {
+    int s, kvh, ci, p0, np, nch, L;
+    bool tail;
+};
+
+__global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const __grid_constant__ AttnParams p) {
+    constexpr int G = 8, D = 64;
+    constexpr int TILE = kPageTokens * D;
+    static_assert(kFlatRing * 20 <= kAttnHead, "ring barriers exceed the header");
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kFlatRing;
+    int* valid = reinterpret_cast<int*>(empty + kFlatRing);              // [ring]
+    int* nchk = reinterpret_cast<int*>(smem + kAttnHead);                // [rows] chunks of each row
+    int* pre_nt = nchk + kFlatMaxRows;                                   // [rows + 1] prefix of non-final chunks
+    int* pre_t = pre_nt + kFlatMaxRows + 1;                              // [rows + 1] prefix of rows with pages
+    int* lens = pre_t + kFlatMaxRows + 1;                                // [rows] context lengths
+    int* misc = lens + kFlatMaxRows;                                     // [4]
+    float* wmax = reinterpret_cast<float*>(misc + 4);                    // [4 warps][G]
+    float* tiles = reinterpret_cast<float*>(smem + kAttnHead + 2048);    // [ring][TILE]
+    float* S = tiles + kFlatRing * TILE;                                 // [kFlatMaxPages][16][G]
+    float* red = S + kFlatMaxPages * kPageTokens * G;                    // [4 warps][G][D] + l [16][G]
+    float* qs = red + 4 * G * D + 16 * G;                                // [2][G][D] query slots
+    static_assert((3 * kFlatMaxRows + 2 + 4 + 4 * G) * 4 <= 2048, "row tables");
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int M = p.M, Hkv = p.Hkv, CP = p.chunk_pages;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kFlatRing; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 4);
+        }
+        fence_barrier_init();
+        trace_min(p.trace, 0);
+        trace_max(p.trace, 1);
+    }
+    // rows: context length and chunk count (sequence state and page tables
+    // are written before the step starts: readable before the dependency wait)
+    for (int s = threadIdx.x; s < M; s += blockDim.x) {
+        const bool act = p.lens ? true : (p.seq[s].active != 0);
+        const int L = p.lens ? p.lens[s] : p.seq[s].pos + 1;
+        const int np = act ? (L + kPageTokens - 1) / kPageTokens : 0;
+        lens[s] = L;
+        nchk[s] = (np + CP - 1) / CP;
+    }
+    __syncthreads();
+    if (warp == 0) {  // two exclusive prefix sums over <= 64 rows (2 per lane)
+        const int a0 = 2 * lane < M ? nchk[2 * lane] : 0, a1 = 2 * lane + 1 < M ? nchk[2 * lane + 1] : 0;
+        const int nt0 = a0 > 0 ? a0 - 1 : 0, nt1 = a1 > 0 ? a1 - 1 : 0;
+        const int t0 = a0 > 0, t1 = a1 > 0;
+        int x = nt0 + nt1, y = t0 + t1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int xo = __shfl_up_sync(0xffffffffu, x, o), yo = __shfl_up_sync(0xffffffffu, y, o);
+            if (lane >= o) {
+                x += xo;
+                y += yo;
+            }
+        }
+        const int xe = x - nt0 - nt1, ye = y - t0 - t1;  // exclusive
+        if (2 * lane <= M) {
+            pre_nt[2 * lane] = xe;
+            pre_t[2 * lane] = ye;
+        }
+        if (2 * lane + 1 <= M) {
+            pre_nt[2 * lane + 1] = xe + nt0;
+            pre_t[2 * lane + 1] = ye + t0;
+        }
+        if (lane == 31) {  // the totals (index M; at M = 64 no lane above reaches it)
+            pre_nt[M] = x;
+            pre_t[M] = y;
+        }
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    const int total_nt = pre_nt[M], total_t = pre_t[M];
+    const int nchunks = Hkv * (total_nt + total_t);
+    // chunk c -> (row, KV head, chunk index); non-final chunks first
+    auto chunk = [&](int c) -> FlatChunk {
+        FlatChunk k{};
+        int unit;
+        bool tail = c >= Hkv * total_nt;
+        if (!tail) {
+            unit = c / Hkv;
+            k.kvh = c - unit * Hkv;
+            int lo = 0, hi = M - 1;  // last row with pre_nt[row] <= unit
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (pre_nt[mid] <= unit) lo = mid; else hi = mid - 1;
+            }
+            k.s = lo;
+            k.ci = unit - pre_nt[lo];
+        } else {
+            const int c2 = c - Hkv * total_nt;
+            unit = c2 / Hkv;
+            k.kvh = c2 - unit * Hkv;
+            int lo = 0, hi = M - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (pre_t[mid] <= unit) lo = mid; else hi = mid - 1;
+            }
+            k.s = lo;
+            k.ci = nchk[lo] - 1;
+        }
+        k.tail = tail;
+        k.nch = nchk[k.s];
+        k.L = lens[k.s];
+        const int npg = (k.L + kPageTokens - 1) / kPageTokens;
+        k.p0 = k.ci * CP;
+        k.np = min(CP, npg - k.p0);
+        return k;
+    };
+
+    if (warp == 4) {
+        // ------------- producer: every chunk's K tiles, then its V tiles -------------
+        bool waited = p.wait_first == 0 ? false : (pdl_wait(), true);
+        int ring = 0;
+        bool stop = false;
+        for (int c = blockIdx.x; c < nchunks && !stop; c += gridDim.x) {
+            const FlatChunk k = chunk(c);
+            const int pt = lane < k.np ? p.page_table[(size_t)k.s * p.ptab_stride + k.p0 + lane] : -1;
+            if (k.tail && !waited) {  // holds the page the preceding QKV kernel appends to
+                pdl_wait();
+                waited = true;
+            }
+            for (int i = 0; i < 2 * k.np; ++i, ++ring) {
+                const int st = ring % kFlatRing;
+                const int kv = i < k.np ? 0 : 1;
+                const int page = __shfl_sync(0xffffffffu, pt, i < k.np ? i : i - k.np);
+                int ok = 1;
+                if (lane == 0 && ring >= kFlatRing) ok = mbar_wait(&empty[st], ((ring / kFlatRing) - 1) & 1, p.err);
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    stop = true;
+                    break;
+                }
+                if (lane == 0) {
+                    if (page >= 0) {
+                        valid[st] = 1;
+                        const size_t base =
+                            ((((size_t)page * p.num_layers + p.layer) * 2 + kv) * p.Hkv + k.kvh) * (size_t)TILE;
+                        mbar_arrive_expect_tx(&full[st], TILE * 4u);
+                        bulk_g2s(tiles + st * TILE, p.kv_pool + base, TILE * 4u, &full[st]);
+                    } else {
+                        valid[st] = 0;  // evicted page: rows read as zeros
+                        mbar_arrive(&full[st]);
+                    }
+                }
+            }
+        }
+    } else {
+        // ------------------------------ consumers ------------------------------
+        pdl_wait();
+        if (threadIdx.x == 0) trace_max(p.trace, 2);
+        const int t = threadIdx.x;  // 0..127
+        const float scale2 = __fmul_rn(__fdiv_rn(1.0f, __fsqrt_rn((float)D)), 1.4426950408889634f);
+        const int c4 = lane & 3, hs = (lane >> 2) & 1;
+        const int j = 4 * warp + (lane >> 3), h = 4 * hs + c4;
+        const int tg = t >> 4, dc = t & 15;
+        bool bad = false;
+        int ring = 0, slot = 0;
+        // diagnostics (launch tracing): SM cycles of consumer warp 0, summed
+        // over CTAs: [8] pass-1 waits, [9] pass-1 math, [10] between passes,
+        // [11] pass-2 waits, [12] pass-2 math, [13] partial / merge, [14] chunks
+        unsigned long long* prb = (p.trace && t == 0) ? p.trace : nullptr;
+        long long cy = prb ? clock64() : 0;
+        auto lap = [&](int slotid) {
+            if (prb) {
+                const long long n = clock64();
+                atomicAdd(prb + slotid, (unsigned long long)(n - cy));
+                cy = n;
+            }
+        };
+        // query of a chunk -> shared slot (one 16-byte async copy per thread)
+        auto fetch_q = [&](const FlatChunk& k, int sl) {
+            const float* src = p.q + (size_t)k.s * p.ld_q + (size_t)k.kvh * G * D + 4 * t;
+            const uint32_t dst = smem_u32(qs + sl * G * D + 4 * t);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+        // deferred merge of the previous multi-chunk pair (thread 0 holds its ticket)
+        int tk = 0, pend_pair = -1, pend_nch = 0, pend_s = 0, pend_kvh = 0;
+        auto merge = [&]() {  // every chunk of the pending pair is in: merge them in chunk order
+            const int og = t >> 4, od = 4 * (t & 15);
+            const float* pb = p.part + (size_t)pend_pair * p.maxch * kAttnPartFloats;
+            float Mg = -INFINITY;
+            for (int q0 = 0; q0 < pend_nch; q0 += 8) {  // 8 independent loads at a time, bypassing L1
+                float mv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    mv[u] = q0 + u < pend_nch ? __ldcg(pb + (q0 + u) * kAttnPartFloats + 8 * D + og) : -INFINITY;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) Mg = fmaxf(Mg, mv[u]);
+            }
+            float den = 0.0f;
+            float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q0 = 0; q0 < pend_nch; q0 += 8) {
+                float mv[8], lv[8];
+                float4 av[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const bool in = q0 + u < pend_nch;
+                    const float* pq = pb + (q0 + u) * kAttnPartFloats;
+                    mv[u] = in ? __ldcg(pq + 8 * D + og) : -INFINITY;
+                    lv[u] = in ? __ldcg(pq + 8 * D + 8 + og) : 0.0f;
+                    av[u] = in ? __ldcg(reinterpret_cast<const float4*>(pq + og * D + od))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const float w = mv[u] == -INFINITY ? 0.0f : exp2f(mv[u] - Mg);
+                    den = fmaf(w, lv[u], den);
+                    num.x = fmaf(w, av[u].x, num.x);
+                    num.y = fmaf(w, av[u].y, num.y);
+                    num.z = fmaf(w, av[u].z, num.z);
+                    num.w = fmaf(w, av[u].w, num.w);
+                }
+            }
+            const float il = den > 0.0f ? 1.0f / den : 0.0f;
+            float* out = p.out + (size_t)pend_s * p.ld_out + (size_t)(pend_kvh * G + og) * D + od;
+            *reinterpret_cast<float4*>(out) = make_float4(num.x * il, num.y * il, num.z * il, num.w * il);
+            if (t == 0) p.ticket[pend_pair] = 0;  // ready for the next launch
+        };
+        int c = blockIdx.x;
+        FlatChunk k{};
+        if (c < nchunks) {
+            k = chunk(c);
+            fetch_q(k, 0);
+        }
+        if (p.probe) {  // streaming alone: wait for every tile, release it
+            for (; c < nchunks; c += gridDim.x) {
+                const FlatChunk kk = chunk(c);
+                for (int i = 0; i < 2 * kk.np; ++i, ++ring) {
+                    const int st = ring % kFlatRing;
+                    if (!bad && !mbar_wait(&full[st], (ring / kFlatRing) & 1, p.err)) bad = true;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[st]);
+                }
+            }
+        }
+        for (; c < nchunks; c += gridDim.x) {
+            const int cn = c + (int)gridDim.x;
+            FlatChunk kn{};
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+            named_bar_sync(1, 128);  // this chunk's query is in its slot; the other slot is free
+            if (cn < nchunks) {
+                kn = chunk(cn);
+                fetch_q(kn, slot ^ 1);  // the next chunk's query, behind this chunk's work
+            }
+            float2 qr[4][4][2];
+            {
+                const float* qb = qs + slot * G * D + 4 * hs * D + 16 * c4;
+#pragma unroll
+                for (int hh = 0; hh < 4; ++hh)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float4 a = *reinterpret_cast<const float4*>(qb + hh * D + 4 * ((e + j) & 3));
+                        qr[hh][e][0] = make_float2(a.x, a.y);
+                        qr[hh][e][1] = make_float2(a.z, a.w);
+                    }
+            }
+            // pass 1: scores of the chunk's pages
+            float mt = -INFINITY;
+            lap(14);
+            for (int i = 0; i < k.np; ++i, ++ring) {
+                const int st = ring % kFlatRing;
+                if (!bad && !mbar_wait(&full[st], (ring / kFlatRing) & 1, p.err)) bad = true;
+                                const float* Kr = tiles + st * TILE + j * D + 16 * c4;
+                float part[4] = {0.f, 0.f, 0.f, 0.f};
+                if (!bad && valid[st]) {
+                    float4 kv[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) kv[e] = *reinterpret_cast<const float4*>(Kr + 4 * ((e + j) & 3));
+#pragma unroll
+                    for (int hh = 0; hh < 4; ++hh) {
+                        float2 d = __fmul2_rn(qr[hh][0][0], make_float2(kv[0].x, kv[0].y));
+                        d = __ffma2_rn(qr[hh][0][1], make_float2(kv[0].z, kv[0].w), d);
+#pragma unroll
+                        for (int e = 1; e < 4; ++e) {
+                            d = __ffma2_rn(qr[hh][e][0], make_float2(kv[e].x, kv[e].y), d);
+                            d = __ffma2_rn(qr[hh][e][1], make_float2(kv[e].z, kv[e].w), d);
+                        }
+                        part[hh] = d.x + d.y;
+                    }
+                }
+                float r2[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const float mine = (c4 & 2) ? part[2 + u] : part[u];
+                    const float other = (c4 & 2) ? part[u] : part[2 + u];
+                    r2[u] = mine + __shfl_xor_sync(0xffffffffu, other, 2);
+                }
+                const float mine = (c4 & 1) ? r2[1] : r2[0];
+                const float other = (c4 & 1) ? r2[0] : r2[1];
+                const float dot = mine + __shfl_xor_sync(0xffffffffu, other, 1);
+                const int tok = (k.p0 + i) * kPageTokens + j;
+                const float sc = (tok < k.L) ? __fmul_rn(dot, scale2) : -INFINITY;
+                S[(i * kPageTokens + j) * G + h] = sc;
+                mt = fmaxf(mt, sc);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);
+            }
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+            if (lane < 8) wmax[warp * G + h] = mt;
+            if (t == 0) misc[1] = tk;  // the pending pair's ticket (its atomic has long completed)
+            named_bar_sync(1, 128);
+            const float Mx = fmaxf(fmaxf(wmax[h], wmax[G + h]), fmaxf(wmax[2 * G + h], wmax[3 * G + h]));
+            if (pend_pair >= 0) {  // (the query registers are dead here)
+                if (misc[1] == pend_nch - 1) merge();
+                pend_pair = -1;
+            }
+            float l_part = 0.0f;
+            for (int i = 0; i < k.np; ++i) {
+                float* sp = S + (i * kPageTokens + j) * G + h;
+                const float e = (*sp == -INFINITY) ? 0.0f : exp2f(*sp - Mx);
+                *sp = e;
+                l_part += e;
+            }
+            named_bar_sync(1, 128);
+            lap(10);
+            // pass 2: weighted V rows
+            float2 acc[G][2];
+#pragma unroll
+            for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = make_float2(0.0f, 0.0f);
+            for (int i = 0; i < k.np; ++i, ++ring) {
+                const int st = ring % kFlatRing;
+                if (!bad && !mbar_wait(&full[st], (ring / kFlatRing) & 1, p.err)) bad = true;
+                if (!bad && valid[st]) {
+                    const float* Vt = tiles + st * TILE;
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int jj = 2 * tg + u;
+                        const float4 v = *reinterpret_cast<const float4*>(Vt + jj * D + 4 * dc);
+                        const float4 pa = *reinterpret_cast<const float4*>(S + (i * kPageTokens + jj) * G);
+                        const float4 pb = *reinterpret_cast<const float4*>(S + (i * kPageTokens + jj) * G + 4);
+                        const float pw[G] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+                        const float2 v01 = make_float2(v.x, v.y), v23 = make_float2(v.z, v.w);
+#pragma unroll
+                        for (int g = 0; g < G; ++g) {
+                            const float2 w2 = make_float2(pw[g], pw[g]);
+                            acc[g][0] = __ffma2_rn(w2, v01, acc[g][0]);
+                            acc[g][1] = __ffma2_rn(w2, v23, acc[g][1]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);
+            }
+            lap(9);
+            if (prb) atomicAdd(prb + 15, 1ull);
+            // token pairs' accumulators (pairs 2w, 2w + 1 of warp w added by a
+            // shuffle, then the warps in order) and the tokens' sums
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float4 v = make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
+                v.x += __shfl_xor_sync(0xffffffffu, v.x, 16);
+                v.y += __shfl_xor_sync(0xffffffffu, v.y, 16);
+                v.z += __shfl_xor_sync(0xffffffffu, v.z, 16);
+                v.w += __shfl_xor_sync(0xffffffffu, v.w, 16);
+                if (lane < 16) *reinterpret_cast<float4*>(red + (warp * G + g) * D + 4 * dc) = v;
+            }
+            red[4 * G * D + j * G + h] = l_part;
+            named_bar_sync(1, 128);
+            const int og = t >> 4, od = 4 * (t & 15);  // output item: head og, dims od..od+3
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 v = *reinterpret_cast<const float4*>(red + (q * G + og) * D + od);
+                a.x += v.x;
+                a.y += v.y;
+                a.z += v.z;
+                a.w += v.w;
+            }
+            float lsum = 0.0f;
+            for (int q = 0; q < 16; ++q) lsum += red[4 * G * D + q * G + og];
+            const float mchunk = fmaxf(fmaxf(wmax[og], wmax[G + og]), fmaxf(wmax[2 * G + og], wmax[3 * G + og]));
+            lap(11);
+            const int pair = k.s * Hkv + k.kvh;
+            if (k.nch == 1) {
+                float* out = p.out + (size_t)k.s * p.ld_out + (size_t)(k.kvh * G + og) * D + od;
+                const float il = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+                *reinterpret_cast<float4*>(out) = make_float4(a.x * il, a.y * il, a.z * il, a.w * il);
+            } else {
+                float* pp = p.part + ((size_t)pair * p.maxch + k.ci) * kAttnPartFloats;
+                *reinterpret_cast<float4*>(pp + og * D + od) = a;
+                if ((t & 15) == 0) {
+                    pp[8 * D + og] = mchunk;
+                    pp[8 * D + 8 + og] = lsum;
+                }
+                // the barrier orders every thread's partial stores before thread
+                // 0's release increment of the ticket (cumulative); its result is
+                // read one chunk later, so the round trip overlaps the next chunk
+                named_bar_sync(1, 128);
+                if (t == 0)
+                    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(tk) : "l"(p.ticket + pair)
+                                 : "memory");
+                pend_pair = pair;
+                pend_nch = k.nch;
+                pend_s = k.s;
+                pend_kvh = k.kvh;
+            }
+            lap(12);
+            lap(13);
+            slot ^= 1;
+            k = kn;
+        }
+        if (pend_pair >= 0) {
+            if (t == 0) misc[1] = tk;
+            named_bar_sync(1, 128);
+            if (misc[1] == pend_nch - 1) merge();
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) trace_max(p.trace, 6);
+}
+
+size_t attn_flat_smem() {
+    return kAttnHead + 2048 + (size_t)kFlatRing * kPageTokens * 64 * 4 + (size_t)kFlatMaxPages * kPageTokens * 8 * 4 +
+           (size_t)(4 * 8 * 64 + 16 * 8) * 4 + (size_t)2 * 8 * 64 * 4;
+}
+
+cudaError_t launch_attn_flat(const AttnParams& p, cudaStream_t stream, bool pdl, int grid) {
+    const size_t smem = attn_flat_smem();
+    auto kfn = attn_flat_gqa8_kernel;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
+    cfg.blockDim = dim3(kFlatThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kfn, p);
+}
+
 size_t attn_gqa8_smem() {
     return kAttnHead + 512 + (size_t)kGqaRing * kPageTokens * 64 * 4 + (size_t)kGqaMaxPages * kPageTokens * 8 * 4 +
            (size_t)8 * (64 + 4) * 4;
@@ -795,9 +1260,34 @@ int choose_nsplit(int M, int Hkv, int max_pages, int num_sms, bool balance_long)
     return ns < 1 ? 1 : ns;
 }
 
+int attn_flat_grid(int num_sms) { return 3 * num_sms; }
+
+bool attn_flat_supported(int H, int Hkv, int d, int M) {
+    // from 64 (row, KV head) pairs on (measured: at 32 pairs the cluster
+    // kernel's DSMEM combine is cheaper than chunk partials)
+    return Hkv > 0 && H == 8 * Hkv && d == 64 && M <= kFlatMaxRows && M * Hkv >= 64;
+}
+
+int attn_flat_chunk_pages(int M, int Hkv, int max_pages, int num_sms) {
+    // the largest chunk (fewest partials) that still gives every CTA of the
+    // grid a couple of chunks at the longest context
+    for (int cp = kFlatMaxPages; cp > 2; cp /= 2)
+        if ((long long)M * Hkv * ((max_pages + cp - 1) / cp) >= 2LL * attn_flat_grid(num_sms)) return cp;
+    return 2;
+}
+
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
     const int G = p.H / p.Hkv;
     if (p.H % p.Hkv != 0) return cudaErrorInvalidValue;
+    if (p.part && attn_flat_supported(p.H, p.Hkv, p.d, p.M) && p.chunk_pages >= 1 &&
+        p.chunk_pages <= kFlatMaxPages && !getenv("TB_ATTN_GENERIC")) {
+        int sms = 148;
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        AttnParams q = p;
+        q.probe = getenv("TB_ATTN_PROBE") != nullptr;
+        return launch_attn_flat(q, stream, pdl, attn_flat_grid(sms));
+    }
     if (G == 8 && p.d == 64 && !getenv("TB_ATTN_GENERIC")) {
         // at most kGqaMaxPages pages per split; the page table's width bounds
         // a sequence's pages, so raise the split count to cover it

@@ -1049,14 +1049,46 @@ __global__ void __launch_bounds__(256) wide_digits_kernel(const __grid_constant_
     } else {
         sr = p.src + (size_t)m * p.ld_src;
     }
-    float ss = 0.0f;
-    if (rms)
-        for (int k = tid; k < L.K; k += 256) ss = fmaf(sr[k], sr[k], ss);
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[0][warp] = ss;
+    // one pass over the row: sum of squares and max |x * w| (the digit bound:
+    // |(x * inv) * w| <= max |x * w| * inv up to two roundings, covered by the
+    // margin below)
+    float ss = 0.0f, mw = 0.0f;
+    const bool v4 = (L.K % 4 == 0) && (embed || p.ld_src % 4 == 0);
+    if (v4) {
+        for (int q = tid; q < L.K / 4; q += 256) {
+            const float4 a = *reinterpret_cast<const float4*>(sr + 4 * q);
+            ss = fmaf(a.x, a.x, ss);
+            ss = fmaf(a.y, a.y, ss);
+            ss = fmaf(a.z, a.z, ss);
+            ss = fmaf(a.w, a.w, ss);
+            float4 b = a;
+            if (rms) {
+                const float4 w = *reinterpret_cast<const float4*>(p.norm_w + 4 * q);
+                b = make_float4(__fmul_rn(a.x, w.x), __fmul_rn(a.y, w.y), __fmul_rn(a.z, w.z), __fmul_rn(a.w, w.w));
+            }
+            mw = fmaxf(mw, fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+        }
+    } else {
+        for (int k = tid; k < L.K; k += 256) {
+            const float a = sr[k];
+            ss = fmaf(a, a, ss);
+            mw = fmaxf(mw, fabsf(rms ? __fmul_rn(a, p.norm_w[k]) : a));
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, o));
+    }
+    if (lane == 0) {
+        red[0][warp] = ss;
+        red[1][warp] = mw;
+    }
     __syncthreads();
-    float tot = 0.0f;
-    for (int w = 0; w < 8; ++w) tot += red[0][w];
+    float tot = 0.0f, bw = 0.0f;
+    for (int w = 0; w < 8; ++w) {
+        tot += red[0][w];
+        bw = fmaxf(bw, red[1][w]);
+    }
     const float iv = rms ? __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)L.K), p.eps))) : 1.0f;
     auto xval = [&](int k) -> float {
         if (k >= L.K) return 0.0f;
@@ -1064,20 +1096,24 @@ __global__ void __launch_bounds__(256) wide_digits_kernel(const __grid_constant_
         if (rms) a = __fmul_rn(__fmul_rn(a, iv), p.norm_w[k]);
         return a;
     };
-    float mx = 0.0f;
-    for (int k = tid; k < L.K; k += 256) mx = fmaxf(mx, fabsf(xval(k)));
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[1][warp] = mx;
-    __syncthreads();
-    float bmax = 0.0f;
-    for (int w = 0; w < 8; ++w) bmax = fmaxf(bmax, red[1][w]);
+    const float bmax = rms ? __fmul_rn(bw, iv) * 1.0000004f : bw;
     const int ex = digit_exponent(bmax);
     if (tid == 0 && blockIdx.y == 0) p.rowex_g[m] = ex;
     const float dscale = __int_as_float((127 - ex) << 23);
     constexpr uint32_t kBBytes = wide_lbo(NB) * 8;
     for (int q = u0 * (kTcUnitK / 4) + tid; q < u1 * (kTcUnitK / 4); q += 256) {  // 4 consecutive k per step
         const int k = 4 * q;
-        const float4 a = make_float4(xval(k), xval(k + 1), xval(k + 2), xval(k + 3));
+        float4 a;
+        if (v4 && k + 3 < L.K) {
+            a = *reinterpret_cast<const float4*>(sr + k);
+            if (rms) {
+                const float4 w = *reinterpret_cast<const float4*>(p.norm_w + k);
+                a = make_float4(__fmul_rn(__fmul_rn(a.x, iv), w.x), __fmul_rn(__fmul_rn(a.y, iv), w.y),
+                                __fmul_rn(__fmul_rn(a.z, iv), w.z), __fmul_rn(__fmul_rn(a.w, iv), w.w));
+            }
+        } else {
+            a = make_float4(xval(k), xval(k + 1), xval(k + 2), xval(k + 3));
+        }
         put_digits4_strided(p.bimg + (size_t)(k / kTcUnitK) * kBBytes, wide_lbo(NB), kWideSbo, k % kTcUnitK, m, a,
                             dscale);
     }

@@ -236,7 +236,22 @@ struct AttnParams {
     // earlier pages are fetched before the dependency wait); 1: any page may
     // be (chunked prefill appends a whole chunk of positions), wait first
     int wait_first;
+    // Persistent chunked variant (G = 8, d = 64, set by the runner): work is
+    // cut into chunks of chunk_pages pages per (sequence, KV head), spread
+    // over a fixed grid; chunk partials [M * Hkv][maxch][kAttnPartFloats] go
+    // to `part` and the last chunk of a (sequence, KV head) to finish (ticket
+    // [M * Hkv], zero between launches) combines them.  nullptr: cluster kernel.
+    float* part;
+    int* ticket;
+    int chunk_pages;
+    int maxch;
+    int probe;  // diagnostics (TB_ATTN_PROBE): consumers only release the pages
 };
+constexpr int kAttnPartFloats = 8 * 64 + 16;  // acc [8 heads][64], m [8], l [8]
+// Grid of the persistent chunked attention launch and its chunk size.
+int attn_flat_grid(int num_sms);
+int attn_flat_chunk_pages(int M, int Hkv, int max_pages, int num_sms);
+bool attn_flat_supported(int H, int Hkv, int d, int M);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
 constexpr int kMaxAttnSplits = 16;  // the splits of a (sequence, KV head) form one cluster
 // balance: also split long contexts to at most ~64 pages per split

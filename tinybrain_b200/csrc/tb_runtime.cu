@@ -223,6 +223,10 @@ struct tb_runner {
     int total_pages = 0;
     // device buffers
     DevBuf seq, ptab, kv, h, q, ctxv, act, logits, rope, prompt, out_tokens, ticket;
+    // persistent chunked attention (GQA-8, d 64): chunk partials and per
+    // (row, KV head) tickets, shared by the decode and prefill plans (they
+    // never run at the same time; the tickets return to zero after each launch)
+    DevBuf attn_part, attn_ticket;
     // tensor parallel through peer memory (tb_runner_tp_connect): the all-reduce
     // buffer shared over CUDA IPC, the peers' mappings, a second residual buffer
     DevBuf ar_buf, ar_peers_dev, ar_step, h2;
@@ -1363,6 +1367,12 @@ static tb_status build_plan_into(tb_runner* r, const PlanIO& io, std::vector<Lau
             a.out = io.ctxv;
             a.ld_out = qd;
             a.err = r->ctx->err.as<int>();
+            if (r->attn_part.p && attn_flat_supported(a.H, a.Hkv, a.d, a.M) && !getenv("TB_ATTN_CLUSTER")) {
+                a.part = r->attn_part.as<float>();
+                a.ticket = r->attn_ticket.as<int>();
+                a.chunk_pages = attn_flat_chunk_pages(a.M, a.Hkv, r->ptab_stride, r->ctx->num_sms);
+                a.maxch = (r->ptab_stride + a.chunk_pages - 1) / a.chunk_pages;
+            }
             ln.bytes = 0;  // depends on the context length; accounted by the caller
             plan.push_back(ln);
         }
@@ -1760,6 +1770,19 @@ extern "C" tb_status tb_runner_create(tb_model* m, int32_t max_batch, int32_t ma
     TB_CUDA(r->pin_seq.ensure(sizeof(SeqState) * B));
     // Attention splits per (sequence, KV head), sized for the longest context.
     r->nsplit = choose_nsplit(B, c.num_kv_heads, r->ptab_stride, ctx->num_sms);
+    {
+        // chunk partials for the persistent attention: rows up to the larger
+        // of the batch and the prefill chunk, chunks of at least 2 pages
+        const int d = c.hidden_dim / c.num_heads;
+        const int rows = std::max(B, (int)kMaxGemvBatch);  // the prefill plan has kMaxGemvBatch rows
+        if (attn_flat_supported(c.num_heads, c.num_kv_heads, d, rows)) {
+            const size_t pairs = (size_t)rows * c.num_kv_heads;
+            const size_t maxch = (size_t)(r->ptab_stride + 1) / 2;
+            TB_CUDA(r->attn_part.alloc(pairs * maxch * kAttnPartFloats * 4));
+            TB_CUDA(r->attn_ticket.alloc(pairs * 4));
+            TB_CUDA(cudaMemset(r->attn_ticket.p, 0, pairs * 4));
+        }
+    }
     tb_status s = TB_OK;
     // Prompt / output buffers start small and grow in generate.
     r->prompt_stride = 1;
