@@ -93,11 +93,13 @@ def test_runner_persistent_attention_matches_cluster_kernel_and_oracle(ctx, monk
     import oracle
     from tests.helpers import assert_same_tokens, small_llama
     from tinybrain_b200.runtime import ModelConfig, ModelRunner
-    cfg = ModelConfig(num_layers=2, hidden_dim=512, num_heads=8, vocab_size=512, max_seq_len=700, num_kv_heads=1,
+    # 32 rows x 2 KV heads = 64 (row, KV head) pairs: the persistent kernel's range
+    cfg = ModelConfig(num_layers=2, hidden_dim=1024, num_heads=16, vocab_size=512, max_seq_len=700, num_kv_heads=2,
                       intermediate_dim=512)
     w = small_llama(cfg, seed=21, mode=mode)
     rng = np.random.default_rng(3)
-    prompts = [rng.integers(0, 512, n).tolist() for n in (640, 1, 17, 300, 33, 129)]
+    lens = [640, 1, 17, 300, 33, 129] + [int(n) for n in rng.integers(1, 600, 26)]
+    prompts = [rng.integers(0, 512, n).tolist() for n in lens]
     flat = ModelRunner(w, ctx, max_batch=len(prompts), max_positions=760).generate_batch(prompts, 10)
     monkeypatch.setenv("TB_ATTN_CLUSTER", "1")
     clus = ModelRunner(w, ctx, max_batch=len(prompts), max_positions=760).generate_batch(prompts, 10)
