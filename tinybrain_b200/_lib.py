@@ -8,7 +8,8 @@ import ctypes as C
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libtinybrain_cuda.so")
+# TB_LIBRARY: load another in-tree build of the library (experiments)
+LIB_PATH = os.environ.get("TB_LIBRARY") or os.path.join(_HERE, "libtinybrain_cuda.so")
 
 TB_OK = 0
 STATUS_NAMES = {
