@@ -152,7 +152,8 @@ tb_status tb_matmul_quantized_dev(tb_context *ctx, const float *x_dev, int64_t M
  * plain stream order; 1: programmatic dependent launch, each GEMV waits for
  * the previous one to finish before reading x (a dependent chain, as inside a
  * decode step); 2: the GEMVs are treated as independent (no wait), so their
- * executions overlap the way independent projections can.
+ * executions overlap the way independent projections can, and each runs with
+ * whole rows per CTA (no K split: the throughput choice when launches overlap).
  * Measurement helper for the single-GEMV HBM benchmark (
  * cycle through more weight copies than fit in L2). */
 tb_status tb_qgemv_stream_time(tb_context *ctx, const tb_qweight *const *ws, int32_t n, const float *x_dev,

@@ -1303,6 +1303,17 @@ int choose_ksplit(const QLayout& L, int M, int num_sms) {
     return best > 0 ? best : std::min(8, L.slabs);
 }
 
+int choose_ksplit_stream(const QLayout& L, int M) {
+    // Independent GEMVs overlap their launches, so the grid need not fill the
+    // GPU by itself: whole rows per CTA (no K split, no partial-sum combine)
+    // stream the most bytes per fixed CTA cost.  The smallest split whose
+    // activation staging fits.
+    const int mb = gemv_mb(L.precision, M);
+    for (int P = 1; P <= std::min(8, L.slabs); ++P)
+        if (gemv_xbytes(L.precision, mb, L, P) <= 96 * 1024) return P;
+    return std::min(8, L.slabs);
+}
+
 int gemv_grid_ctas(const GemvParams& p) {
     const int mb = gemv_mb(p.L.precision, p.M);
     return (p.L.Np / p.L.RB) * p.P * ((p.M + mb - 1) / mb);

@@ -182,6 +182,8 @@ size_t wide_digits_bytes(const QLayout& L);  // bimg bytes for a layout
 bool gemv_uses_wide(int precision, int M);
 // Pick the K-split (cluster size) for a layout and batch.
 int choose_ksplit(const QLayout& L, int M, int num_sms);
+// The split for GEMVs whose launches overlap (independent of each other).
+int choose_ksplit_stream(const QLayout& L, int M);
 // CTAs of the launch launch_gemv(p) makes.
 int gemv_grid_ctas(const GemvParams& p);
 

@@ -744,6 +744,7 @@ extern "C" tb_status tb_qgemv_stream_time(tb_context* ctx, const tb_qweight* con
         p.src = x;
         p.out = y;
         p.independent = pdl == 2 ? 1 : 0;  // independent GEMVs overlap their launches
+        if (pdl == 2 && !getenv("TB_GEMV_P")) p.P = choose_ksplit_stream(ws[i]->L, (int)M);
         le = launch_gemv(p, st, pdl != 0 && i > 0);
     }
     cudaError_t ce = cudaStreamEndCapture(st, &g);
