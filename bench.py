@@ -357,7 +357,8 @@ def run_config4(args, env, cpu=True):
         runner, att_bytes,
         {"gemv": "gemv_kernel<8,128,64> (+ wide_digits): all projections + LM head of one step, all rows"
                  if len(mine) > 16 else "gemv_kernel<8,128,*>: all projections + LM head of one step",
-         "attention": "attn_decode_kernel (paged KV, all layers)"},
+         "attention": ("attn_flat_gqa8_kernel (persistent chunked paged attention, all layers)" if len(mine) * 4 >= 64
+                       else "attn_gqa8_d64_kernel (cluster-split paged attention, all layers)")},
         {"gemv": f"gemv int8 M={len(mine)} tinyllama", "attention": f"attention tinyllama config4 M={len(mine)}"},
         peak, peak_kind)
     launches = int(len(runner.profile_step()[1]))
