@@ -661,6 +661,22 @@ struct FlatChunk {
     bool tail;
 };
 
+// tf32 of x, rounded to nearest (ties away), as the 32-bit operand pattern.
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+// d (16 x 8, fp32) += a (16 x 8, tf32, row major) x b (8 x 8, tf32, column major), one warp.
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+template <bool MMA>
 __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const __grid_constant__ AttnParams p) {
     constexpr int G = 8, D = 64;
     constexpr int TILE = kPageTokens * D;
@@ -686,7 +702,7 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
     if (threadIdx.x == 0) {
         for (int i = 0; i < kFlatRing; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 4);
+            mbar_init(&empty[i], MMA ? 1 : 4);  // MMA: one warp consumes a tile
         }
         fence_barrier_init();
         trace_min(p.trace, 0);
@@ -891,7 +907,7 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                     const int st = ring % kFlatRing;
                     if (!bad && !mbar_wait(&full[st], (ring / kFlatRing) & 1, p.err)) bad = true;
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[st]);
+                    if (lane == 0 && (!MMA || warp == 0)) mbar_arrive(&empty[st]);
                 }
             }
         }
@@ -904,6 +920,178 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                 kn = chunk(cn);
                 fetch_q(kn, slot ^ 1);  // the next chunk's query, behind this chunk's work
             }
+            const int og = t >> 4, od = 4 * (t & 15);  // output item: head og, dims od..od+3
+            float4 a;
+            float lsum, mchunk;
+            if constexpr (MMA) {
+            // ---- tensor cores (mma.sync m16n8k8, tf32 split in three products
+            // hi*hi + hi*lo + lo*hi ~ fp32 accuracy).  Warp w takes the
+            // chunk's pages i = w, w + 4, ... in both passes.
+            // lane = (g = lane / 4, t = lane % 4).  Scores: A = K tile rows
+            // (tokens) g / g + 8, B = query^T (head g); dims of k-step (b, s):
+            // k = t -> 16b + 4t + 2s, k = t + 4 -> 16b + 4t + 2s + 1, so each
+            // thread loads 4 consecutive dims of a row at once.
+            const int gq = lane >> 2, tq = lane & 3;
+            uint32_t qh[4][2][2], ql[4][2][2];  // [16-dim block][k-step][b0 / b1]
+            {
+                const float* qg = qs + slot * G * D + gq * D;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const float4 v = *reinterpret_cast<const float4*>(qg + 16 * b + 4 * tq);
+                    const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const uint32_t h32 = tf32_rna(e[u]);
+                        qh[b][u >> 1][u & 1] = h32;
+                        ql[b][u >> 1][u & 1] = __float_as_uint(e[u] - __uint_as_float(h32));
+                    }
+                }
+            }
+            float mth[2] = {-INFINITY, -INFINITY};  // this lane's max of heads 2t, 2t + 1
+            for (int i = warp; i < k.np; i += 4) {
+                const int st = (ring + i) % kFlatRing;
+                if (!bad && !mbar_wait(&full[st], ((ring + i) / kFlatRing) & 1, p.err)) bad = true;
+                float c[4] = {0.f, 0.f, 0.f, 0.f};
+                if (!bad && valid[st]) {
+                    const float* Kt = tiles + st * TILE;
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const float4 r0 = *reinterpret_cast<const float4*>(Kt + gq * D + 16 * b + 4 * tq);
+                        const float4 r1 = *reinterpret_cast<const float4*>(Kt + (gq + 8) * D + 16 * b + 4 * tq);
+                        const float e0[4] = {r0.x, r0.y, r0.z, r0.w}, e1[4] = {r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+                        for (int sstep = 0; sstep < 2; ++sstep) {
+                            uint32_t ah[4], al[4];
+                            const float av[4] = {e0[2 * sstep], e1[2 * sstep], e0[2 * sstep + 1], e1[2 * sstep + 1]};
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                ah[u] = tf32_rna(av[u]);
+                                al[u] = __float_as_uint(av[u] - __uint_as_float(ah[u]));
+                            }
+                            mma_tf32(c, ah, qh[b][sstep]);
+                            mma_tf32(c, ah, ql[b][sstep]);
+                            mma_tf32(c, al, qh[b][sstep]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);
+                // c0 (token g, head 2t), c1 (g, 2t + 1), c2 (g + 8, 2t), c3 (g + 8, 2t + 1)
+                const int tok0 = (k.p0 + i) * kPageTokens + gq;
+                const float s0 = tok0 < k.L ? __fmul_rn(c[0], scale2) : -INFINITY;
+                const float s1 = tok0 < k.L ? __fmul_rn(c[1], scale2) : -INFINITY;
+                const float s2 = tok0 + 8 < k.L ? __fmul_rn(c[2], scale2) : -INFINITY;
+                const float s3 = tok0 + 8 < k.L ? __fmul_rn(c[3], scale2) : -INFINITY;
+                float* Sp = S + (i * kPageTokens) * G;
+                *reinterpret_cast<float2*>(Sp + gq * G + 2 * tq) = make_float2(s0, s1);
+                *reinterpret_cast<float2*>(Sp + (gq + 8) * G + 2 * tq) = make_float2(s2, s3);
+                mth[0] = fmaxf(mth[0], fmaxf(s0, s2));
+                mth[1] = fmaxf(mth[1], fmaxf(s1, s3));
+            }
+            // per head: the lanes of equal t, then the 4 warps
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                mth[0] = fmaxf(mth[0], __shfl_xor_sync(0xffffffffu, mth[0], o));
+                mth[1] = fmaxf(mth[1], __shfl_xor_sync(0xffffffffu, mth[1], o));
+            }
+            if (lane < 4) {
+                wmax[warp * G + 2 * tq] = mth[0];
+                wmax[warp * G + 2 * tq + 1] = mth[1];
+            }
+            if (t == 0) misc[1] = tk;  // the pending pair's ticket (its atomic has long completed)
+            named_bar_sync(1, 128);
+            float Mh[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int hh = 2 * tq + u;
+                Mh[u] = fmaxf(fmaxf(wmax[hh], wmax[G + hh]), fmaxf(wmax[2 * G + hh], wmax[3 * G + hh]));
+            }
+            if (pend_pair >= 0) {
+                if (misc[1] == pend_nch - 1) merge();
+                pend_pair = -1;
+            }
+            // weights of this warp's own pages, in place (no other warp reads them)
+            float lh[2] = {0.f, 0.f};
+            for (int i = warp; i < k.np; i += 4) {
+                float* Sp = S + (i * kPageTokens) * G;
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    float2* e2 = reinterpret_cast<float2*>(Sp + (gq + 8 * r) * G + 2 * tq);
+                    float2 v = *e2;
+                    v.x = v.x == -INFINITY ? 0.0f : exp2f(v.x - Mh[0]);
+                    v.y = v.y == -INFINITY ? 0.0f : exp2f(v.y - Mh[1]);
+                    lh[0] += v.x;
+                    lh[1] += v.y;
+                    *e2 = v;
+                }
+            }
+            __syncwarp();
+            // pass 2: O^(rows) = A (rows 0-7: P hi of head g, rows 8-15: P lo) x V;
+            // k-step s: k = t -> token 8s + t, k = t + 4 -> token 8s + t + 4;
+            // n-block v: dims 8v .. 8v + 7 (column g)
+            float dacc[8][4];
+#pragma unroll
+            for (int v = 0; v < 8; ++v) dacc[v][0] = dacc[v][1] = dacc[v][2] = dacc[v][3] = 0.0f;
+            for (int i = warp; i < k.np; i += 4) {
+                const int q2 = k.np + i, st = (ring + q2) % kFlatRing;
+                if (!bad && !mbar_wait(&full[st], ((ring + q2) / kFlatRing) & 1, p.err)) bad = true;
+                if (!bad && valid[st]) {
+                    const float* Vt = tiles + st * TILE;
+                    const float* Sp = S + (i * kPageTokens) * G;
+#pragma unroll
+                    for (int sstep = 0; sstep < 2; ++sstep) {
+                        const float pa = Sp[(8 * sstep + tq) * G + gq], pb = Sp[(8 * sstep + tq + 4) * G + gq];
+                        uint32_t a[4];
+                        a[0] = tf32_rna(pa);
+                        a[2] = tf32_rna(pb);
+                        a[1] = __float_as_uint(pa - __uint_as_float(a[0]));
+                        a[3] = __float_as_uint(pb - __uint_as_float(a[2]));
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) {
+                            const float b0 = Vt[(8 * sstep + tq) * D + 8 * v + gq];
+                            const float b1 = Vt[(8 * sstep + tq + 4) * D + 8 * v + gq];
+                            uint32_t bh[2], bl[2];
+                            bh[0] = tf32_rna(b0);
+                            bh[1] = tf32_rna(b1);
+                            bl[0] = __float_as_uint(b0 - __uint_as_float(bh[0]));
+                            bl[1] = __float_as_uint(b1 - __uint_as_float(bh[1]));
+                            mma_tf32(dacc[v], a, bh);
+                            mma_tf32(dacc[v], a, bl);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);
+            }
+            ring += 2 * k.np;
+            // this warp's O[head g][dims 8v + 2t, +1] = rows g + rows g + 8 -> red[warp][head][dim]
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+                *reinterpret_cast<float2*>(red + (warp * G + gq) * D + 8 * v + 2 * tq) =
+                    make_float2(dacc[v][0] + dacc[v][2], dacc[v][1] + dacc[v][3]);
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                lh[0] += __shfl_xor_sync(0xffffffffu, lh[0], o);
+                lh[1] += __shfl_xor_sync(0xffffffffu, lh[1], o);
+            }
+            if (lane < 4) {
+                red[4 * G * D + warp * G + 2 * tq] = lh[0];
+                red[4 * G * D + warp * G + 2 * tq + 1] = lh[1];
+            }
+            named_bar_sync(1, 128);
+            a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 v = *reinterpret_cast<const float4*>(red + (q * G + og) * D + od);
+                a.x += v.x;
+                a.y += v.y;
+                a.z += v.z;
+                a.w += v.w;
+            }
+            lsum = 0.0f;
+            for (int q = 0; q < 4; ++q) lsum += red[4 * G * D + q * G + og];
+            mchunk = fmaxf(fmaxf(wmax[og], wmax[G + og]), fmaxf(wmax[2 * G + og], wmax[3 * G + og]));
+            } else {
             float2 qr[4][4][2];
             {
                 const float* qb = qs + slot * G * D + 4 * hs * D + 16 * c4;
@@ -1019,8 +1207,7 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
             }
             red[4 * G * D + j * G + h] = l_part;
             named_bar_sync(1, 128);
-            const int og = t >> 4, od = 4 * (t & 15);  // output item: head og, dims od..od+3
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            a = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const float4 v = *reinterpret_cast<const float4*>(red + (q * G + og) * D + od);
@@ -1029,9 +1216,10 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                 a.z += v.z;
                 a.w += v.w;
             }
-            float lsum = 0.0f;
+            lsum = 0.0f;
             for (int q = 0; q < 16; ++q) lsum += red[4 * G * D + q * G + og];
-            const float mchunk = fmaxf(fmaxf(wmax[og], wmax[G + og]), fmaxf(wmax[2 * G + og], wmax[3 * G + og]));
+            mchunk = fmaxf(fmaxf(wmax[og], wmax[G + og]), fmaxf(wmax[2 * G + og], wmax[3 * G + og]));
+            }
             lap(11);
             const int pair = k.s * Hkv + k.kvh;
             if (k.nch == 1) {
@@ -1079,7 +1267,7 @@ size_t attn_flat_smem() {
 
 cudaError_t launch_attn_flat(const AttnParams& p, cudaStream_t stream, bool pdl, int grid) {
     const size_t smem = attn_flat_smem();
-    auto kfn = attn_flat_gqa8_kernel;
+    auto kfn = getenv("TB_ATTN_CUDACORE") ? attn_flat_gqa8_kernel<false> : attn_flat_gqa8_kernel<true>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
