@@ -31,6 +31,7 @@
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <type_traits>
 
 namespace tb {
 
@@ -751,9 +752,17 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
     if (warp < kGemvConsumerWarps) {
         const int ctid = threadIdx.x;
         if (ctid == 0) trace_max(p.trace, 5);
+        unsigned long long best_mine = 0ull;
+        constexpr bool RMAJ = MB >= 16;  // row-major items (below)
+        // The item loops below are instantiated once per epilogue kind (EPI a
+        // compile-time constant): each loop then holds only its own kind's
+        // code, small enough to stay in the instruction cache.  With one
+        // loop for every kind the warps stalled on instruction fetch.
+        auto epilogue_items = [&](auto epi_kind) {
+        constexpr int EPI = decltype(epi_kind)::value;
         // Output items handled by this rank: a contiguous chunk.
         constexpr int HALF = RB / 2;  // fused gate/up: gate rows [0, HALF), up rows [HALF, RB)
-        const int nout = (p.epilogue == kEpiQkv || p.epilogue == kEpiSiluMul) ? HALF : RB;
+        const int nout = (EPI == kEpiQkv || EPI == kEpiSiluMul) ? HALF : RB;
         const int ob = rank * nout / P, oe = (rank + 1) * nout / P;
         const int nitems = (oe - ob) * MB;
         uint32_t rbase[8];
@@ -778,7 +787,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             if (p.bias) v = __fadd_rn(v, rowbias[i]);
             return v;
         };
-        const unsigned int ar_tag_push = (p.epilogue == kEpiPush) ? *p.ar_step + 1u : 0u;
+        const unsigned int ar_tag_push = (EPI == kEpiPush) ? *p.ar_step + 1u : 0u;
         // Item order.  Up to 8 batch rows per CTA: it = ctid + 256 j maps to
         // batch row it % MB = ctid % MB (MB divides 256), one argmax key per
         // thread.  From 16 rows on ("row-major" items): batch row it / nr,
@@ -786,30 +795,37 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         // consecutive outputs of one batch row; the argmax is reduced per
         // item over the lanes that share a batch row.
         static_assert(256 % MB == 0, "batch rows per CTA divide the consumer threads");
-        constexpr bool RMAJ = MB >= 16;
         const int nr = oe - ob;
-        auto item_m = [&](int it) -> int { return RMAJ ? it / nr : it % MB; };
-        auto item_o = [&](int it) -> int { return ob + (RMAJ ? it - (it / nr) * nr : it / MB); };
-        unsigned long long best_mine = 0ull;
+        // (batch row, tile-row offset) of item it = ctid + 256 j, stepped by
+        // 256 items at a time without divisions
+        const int step_m = RMAJ ? 256 / nr : 0, step_o = RMAJ ? 256 % nr : 256 / MB;
+        auto item_next = [&](int& m, int& o) {
+            o += step_o;
+            m += step_m;
+            if (RMAJ && o >= nr) {
+                o -= nr;
+                ++m;
+            }
+        };
         // Row-major batches first gather every finished row value of this
         // rank into shared memory in batch-row-minor order (consecutive lanes
         // read consecutive partial sums of every rank: coalesced DSMEM
         // requests), then the item loop below reads them back row-major (its
         // global loads and stores coalesce).  Staging [MB][SR] reuses the
         // weight ring, idle once the accumulators are complete.
-        const bool pairs = p.epilogue == kEpiQkv || p.epilogue == kEpiSiluMul;
+        const bool pairs = EPI == kEpiQkv || EPI == kEpiSiluMul;
         const int nloc = pairs ? 2 * nr : nr;  // tile rows of this rank
         const int SR = nloc + 1;
         float* stg = reinterpret_cast<float*>(stage_base);
         auto loc_row = [&](int li) -> int {  // tile row of local index li
-            if (p.epilogue == kEpiQkv) return 2 * ob + li;
-            if (p.epilogue == kEpiSiluMul) return li < nr ? ob + li : HALF + ob + (li - nr);
+            if (EPI == kEpiQkv) return 2 * ob + li;
+            if (EPI == kEpiSiluMul) return li < nr ? ob + li : HALF + ob + (li - nr);
             return ob + li;
         };
         if constexpr (RMAJ) {
             static_assert(!RMAJ || MB * (RB + 1) * 4 <= STAGES * Cfg::kStageBytes, "staging fits the ring");
-            // (a plain loop: this kernel is large and instruction-fetch bound
-            // when its epilogue loops are unrolled)
+            // (a plain loop: unrolling it was measured slower, instruction
+            // fetch of a large straight-line body)
 #pragma unroll 1
             for (int it = ctid; it < nloc * MB; it += 256) {
                 const int m = it % MB, li = it / MB;
@@ -823,8 +839,8 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         auto rowval = [&](int row, int m) -> float {
             if constexpr (RMAJ) {
                 int li;
-                if (p.epilogue == kEpiQkv) li = row - 2 * ob;
-                else if (p.epilogue == kEpiSiluMul) li = row < HALF ? row - ob : nr + (row - HALF - ob);
+                if (EPI == kEpiQkv) li = row - 2 * ob;
+                else if (EPI == kEpiSiluMul) li = row < HALF ? row - ob : nr + (row - HALF - ob);
                 else li = row - ob;
                 return stg[m * SR + li];
             } else {
@@ -836,25 +852,30 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         // chunk is in flight together: (1) reduce, scale, issue the loads the
         // stores need (RoPE table, the residual); (2) finish and store.
         constexpr int JMAX = (RB * MB + 255) / 256;
-        constexpr int JC = JMAX < (RMAJ ? 2 : 4) ? JMAX : (RMAJ ? 2 : 4);
+        constexpr int JC = JMAX < 4 ? JMAX : 4;
+        int cm = RMAJ ? ctid / nr : ctid % MB, co = RMAJ ? ctid % nr : ctid / MB;
 #pragma unroll 1
         for (int jb = 0; jb < JMAX; jb += JC) {
+        if ((ctid & ~31) + 256 * jb >= nitems) break;  // warp-uniform: the argmax below uses whole warps
         float va[JC], vb[JC], old[JC];
         float2 cs[JC];
         unsigned long long keyj[JC];
-        int keym[JC];
+        int keym[JC], mj[JC], oj[JC];
 #pragma unroll
         for (int j = 0; j < JC; ++j) {
             keyj[j] = 0ull;
             keym[j] = -1;
             va[j] = vb[j] = old[j] = 0.0f;
             cs[j] = make_float2(1.0f, 0.0f);
+            mj[j] = cm;
+            oj[j] = ob + co;
+            item_next(cm, co);
             const int it = ctid + 256 * (jb + j);
             if (it >= nitems) continue;
-            const int m = item_m(it);
-            const int o = item_o(it);
+            const int m = mj[j];
+            const int o = oj[j];
             if (m >= Mloc) continue;
-            if (p.epilogue == kEpiQkv) {
+            if (EPI == kEpiQkv) {
                 const int n0 = rb * RB + 2 * o;
                 if (n0 >= L.N) continue;
                 va[j] = rowval(2 * o, m);
@@ -864,7 +885,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                     const int i = (n0 < p.H ? n0 : n0 - p.H) % p.head_dim;
                     cs[j] = p.rope[(size_t)pos * (p.head_dim / 2) + i / 2];
                 }
-            } else if (p.epilogue == kEpiSiluMul) {
+            } else if (EPI == kEpiSiluMul) {
                 if (rb * HALF + o >= L.N) continue;
                 va[j] = rowval(o, m);
                 vb[j] = rowval(HALF + o, m);
@@ -872,18 +893,18 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 const int n = rb * RB + o;
                 if (n >= L.N) continue;
                 va[j] = rowval(o, m);
-                if (p.epilogue == kEpiResidual) old[j] = p.out[(size_t)(m0 + m) * p.ld_out + n];
+                if (EPI == kEpiResidual) old[j] = p.out[(size_t)(m0 + m) * p.ld_out + n];
             }
         }
 #pragma unroll
         for (int j = 0; j < JC; ++j) {
             const int it = ctid + 256 * (jb + j);
             if (it >= nitems) continue;
-            const int m = item_m(it);
-            const int o = item_o(it);
+            const int m = mj[j];
+            const int o = oj[j];
             if (m >= Mloc) continue;
             const int gm = m0 + m;  // batch row
-            if (p.epilogue == kEpiQkv) {
+            if (EPI == kEpiQkv) {
                 const int n0 = rb * RB + 2 * o;
                 if (n0 >= L.N || !seqinfo[MB + m]) continue;
                 const int pos = seqinfo[m];
@@ -923,7 +944,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                     p.kv_pool[base * d + jj % d] = v0;
                     p.kv_pool[base * d + jj % d + 1] = v1;
                 }
-            } else if (p.epilogue == kEpiSiluMul) {
+            } else if (EPI == kEpiSiluMul) {
                 const int n = rb * HALF + o;
                 if (n >= L.N) continue;
                 p.out[(size_t)gm * p.ld_out + n] = __fmul_rn(silu_ref(va[j]), vb[j]);
@@ -931,16 +952,16 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 const int n = rb * RB + o;
                 if (n >= L.N) continue;
                 const float v = va[j];
-                if (p.epilogue == kEpiStore) {
+                if (EPI == kEpiStore) {
                     p.out[(size_t)gm * p.ld_out + n] = v;
-                } else if (p.epilogue == kEpiPush) {
+                } else if (EPI == kEpiPush) {
                     const size_t off = ((size_t)p.ar_push_slot * p.ar_world + p.ar_rank) * p.ar_slot_words +
                                        (size_t)gm * p.ld_out + n;
                     const unsigned long long word = ((unsigned long long)ar_tag_push << 32) | __float_as_uint(v);
                     for (int q = 0; q < p.ar_world; ++q) st_relaxed_sys_u64(p.ar_peers[q] + off, word);
-                } else if (p.epilogue == kEpiResidual) {
+                } else if (EPI == kEpiResidual) {
                     p.out[(size_t)gm * p.ld_out + n] = __fadd_rn(old[j], v);
-                } else if (p.epilogue == kEpiGelu) {
+                } else if (EPI == kEpiGelu) {
                     p.out[(size_t)gm * p.ld_out + n] = gelu_ref(v);
                 } else {  // kEpiArgmax
                     if (p.logits) p.logits[(size_t)gm * L.N + n] = v;
@@ -954,7 +975,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 }
             }
         }
-        if (RMAJ && p.epilogue == kEpiArgmax) {
+        if (RMAJ && EPI == kEpiArgmax) {
             // lanes of one batch row are contiguous: per distinct row in the
             // warp, a full-warp max over its lanes' keys, one atomic
 #pragma unroll
@@ -975,6 +996,17 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             }
         }
         }  // item chunks
+        };
+        switch (p.epilogue) {
+            case kEpiStore: epilogue_items(std::integral_constant<int, kEpiStore>{}); break;
+            case kEpiResidual: epilogue_items(std::integral_constant<int, kEpiResidual>{}); break;
+            case kEpiQkv: epilogue_items(std::integral_constant<int, kEpiQkv>{}); break;
+            case kEpiSiluMul: epilogue_items(std::integral_constant<int, kEpiSiluMul>{}); break;
+            case kEpiGelu: epilogue_items(std::integral_constant<int, kEpiGelu>{}); break;
+            case kEpiArgmax: epilogue_items(std::integral_constant<int, kEpiArgmax>{}); break;
+            case kEpiPush: epilogue_items(std::integral_constant<int, kEpiPush>{}); break;
+            default: break;  // the host passes only the kinds above
+        }
         if (PREC == 8 && ctid == 0) trace_max(p.trace, 9);
         if (p.epilogue == kEpiArgmax) {
             // lanes with the same batch row (lane % MB) combine, then one atomic per row and warp
