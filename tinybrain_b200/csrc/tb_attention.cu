@@ -651,7 +651,8 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
 // writes the output and resets the ticket.  A single-chunk pair writes its
 // output directly.
 // ---------------------------------------------------------------------------
-constexpr int kFlatRing = 12;       // 4 KB tiles in flight per CTA
+constexpr int kFlatCtas = 4;        // CTAs per SM
+constexpr int kFlatRing = kFlatCtas == 4 ? 8 : kFlatCtas == 3 ? 12 : 20;  // 4 KB tiles in flight per CTA
 constexpr int kFlatMaxPages = 16;   // pages per chunk at most
 constexpr int kFlatMaxRows = 64;    // sequences (rows) per launch
 constexpr int kFlatThreads = (4 + 1) * 32;
@@ -676,8 +677,7 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-template <bool MMA>
-__global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel(const __grid_constant__ AttnParams p) {
     constexpr int G = 8, D = 64;
     constexpr int TILE = kPageTokens * D;
     static_assert(kFlatRing * 20 <= kAttnHead, "ring barriers exceed the header");
@@ -702,7 +702,7 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
     if (threadIdx.x == 0) {
         for (int i = 0; i < kFlatRing; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], MMA ? 1 : 4);  // MMA: one warp consumes a tile
+            mbar_init(&empty[i], 1);  // one consumer warp reads a tile
         }
         fence_barrier_init();
         trace_min(p.trace, 0);
@@ -807,17 +807,17 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                     stop = true;
                     break;
                 }
-                if (lane == 0) {
-                    if (page >= 0) {
+                if (page >= 0) {
+                    if (lane == 0) {
                         valid[st] = 1;
                         const size_t base =
                             ((((size_t)page * p.num_layers + p.layer) * 2 + kv) * p.Hkv + k.kvh) * (size_t)TILE;
                         mbar_arrive_expect_tx(&full[st], TILE * 4u);
                         bulk_g2s(tiles + st * TILE, p.kv_pool + base, TILE * 4u, &full[st]);
-                    } else {
-                        valid[st] = 0;  // evicted page: rows read as zeros
-                        mbar_arrive(&full[st]);
                     }
+                } else if (lane == 0) {
+                    valid[st] = 0;  // evicted page: rows read as zeros
+                    mbar_arrive(&full[st]);
                 }
             }
         }
@@ -827,14 +827,12 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
         if (threadIdx.x == 0) trace_max(p.trace, 2);
         const int t = threadIdx.x;  // 0..127
         const float scale2 = __fmul_rn(__fdiv_rn(1.0f, __fsqrt_rn((float)D)), 1.4426950408889634f);
-        const int c4 = lane & 3, hs = (lane >> 2) & 1;
-        const int j = 4 * warp + (lane >> 3), h = 4 * hs + c4;
-        const int tg = t >> 4, dc = t & 15;
         bool bad = false;
         int ring = 0, slot = 0;
         // diagnostics (launch tracing): SM cycles of consumer warp 0, summed
-        // over CTAs: [8] pass-1 waits, [9] pass-1 math, [10] between passes,
-        // [11] pass-2 waits, [12] pass-2 math, [13] partial / merge, [14] chunks
+        // over CTAs: [14] chunk start, [8] pass 1, [9] between the passes,
+        // [10] pass 2, [11] warp reduction, [12] partial and ticket, [13]
+        // tile waits (within the passes), [15] chunks
         unsigned long long* prb = (p.trace && t == 0) ? p.trace : nullptr;
         long long cy = prb ? clock64() : 0;
         auto lap = [&](int slotid) {
@@ -852,7 +850,12 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
             asm volatile("cp.async.commit_group;" ::: "memory");
         };
         // deferred merge of the previous multi-chunk pair (thread 0 holds its ticket)
+        // Two pairs in flight: A (pend_*) has its ticket increment issued,
+        // its result read one chunk later; B (pb_*) has its partial stored,
+        // its increment issued at the next chunk's mid-point, when the stores
+        // have long completed (so the release costs no wait).
         int tk = 0, pend_pair = -1, pend_nch = 0, pend_s = 0, pend_kvh = 0;
+        int pb_pair = -1, pb_nch = 0, pb_s = 0, pb_kvh = 0;
         auto merge = [&]() {  // every chunk of the pending pair is in: merge them in chunk order
             const int og = t >> 4, od = 4 * (t & 15);
             const float* pb = p.part + (size_t)pend_pair * p.maxch * kAttnPartFloats;
@@ -867,11 +870,11 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
             }
             float den = 0.0f;
             float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int q0 = 0; q0 < pend_nch; q0 += 8) {
-                float mv[8], lv[8];
-                float4 av[8];
+            for (int q0 = 0; q0 < pend_nch; q0 += 4) {  // 4 partials' loads in flight
+                float mv[4], lv[4];
+                float4 av[4];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int u = 0; u < 4; ++u) {
                     const bool in = q0 + u < pend_nch;
                     const float* pq = pb + (q0 + u) * kAttnPartFloats;
                     mv[u] = in ? __ldcg(pq + 8 * D + og) : -INFINITY;
@@ -880,7 +883,7 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                                : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int u = 0; u < 4; ++u) {
                     const float w = mv[u] == -INFINITY ? 0.0f : exp2f(mv[u] - Mg);
                     den = fmaf(w, lv[u], den);
                     num.x = fmaf(w, av[u].x, num.x);
@@ -907,7 +910,7 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                     const int st = ring % kFlatRing;
                     if (!bad && !mbar_wait(&full[st], (ring / kFlatRing) & 1, p.err)) bad = true;
                     __syncwarp();
-                    if (lane == 0 && (!MMA || warp == 0)) mbar_arrive(&empty[st]);
+                    if (lane == 0 && warp == 0) mbar_arrive(&empty[st]);
                 }
             }
         }
@@ -923,7 +926,7 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
             const int og = t >> 4, od = 4 * (t & 15);  // output item: head og, dims od..od+3
             float4 a;
             float lsum, mchunk;
-            if constexpr (MMA) {
+            {
             // ---- tensor cores (mma.sync m16n8k8, tf32 split in three products
             // hi*hi + hi*lo + lo*hi ~ fp32 accuracy).  Warp w takes the
             // chunk's pages i = w, w + 4, ... in both passes.
@@ -931,6 +934,8 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
             // (tokens) g / g + 8, B = query^T (head g); dims of k-step (b, s):
             // k = t -> 16b + 4t + 2s, k = t + 4 -> 16b + 4t + 2s + 1, so each
             // thread loads 4 consecutive dims of a row at once.
+            lap(14);
+            if (prb) atomicAdd(prb + 15, 1ull);
             const int gq = lane >> 2, tq = lane & 3;
             uint32_t qh[4][2][2], ql[4][2][2];  // [16-dim block][k-step][b0 / b1]
             {
@@ -950,8 +955,15 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
             float mth[2] = {-INFINITY, -INFINITY};  // this lane's max of heads 2t, 2t + 1
             for (int i = warp; i < k.np; i += 4) {
                 const int st = (ring + i) % kFlatRing;
+                const long long w0 = prb ? clock64() : 0;
                 if (!bad && !mbar_wait(&full[st], ((ring + i) / kFlatRing) & 1, p.err)) bad = true;
+                if (prb) atomicAdd(prb + 13, (unsigned long long)(clock64() - w0));
                 float c[4] = {0.f, 0.f, 0.f, 0.f};
+                // two independent accumulators (block parity): dependent
+                // chains of 12 products instead of 24
+                float cacc[2][4];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) cacc[u][0] = cacc[u][1] = cacc[u][2] = cacc[u][3] = 0.0f;
                 if (!bad && valid[st]) {
                     const float* Kt = tiles + st * TILE;
 #pragma unroll
@@ -968,11 +980,13 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                                 ah[u] = tf32_rna(av[u]);
                                 al[u] = __float_as_uint(av[u] - __uint_as_float(ah[u]));
                             }
-                            mma_tf32(c, ah, qh[b][sstep]);
-                            mma_tf32(c, ah, ql[b][sstep]);
-                            mma_tf32(c, al, qh[b][sstep]);
+                            mma_tf32(cacc[b & 1], al, qh[b][sstep]);
+                            mma_tf32(cacc[b & 1], ah, ql[b][sstep]);
+                            mma_tf32(cacc[b & 1], ah, qh[b][sstep]);
                         }
                     }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) c[u] = cacc[0][u] + cacc[1][u];
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[st]);
@@ -988,6 +1002,7 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                 mth[0] = fmaxf(mth[0], fmaxf(s0, s2));
                 mth[1] = fmaxf(mth[1], fmaxf(s1, s3));
             }
+            lap(8);
             // per head: the lanes of equal t, then the 4 warps
 #pragma unroll
             for (int o = 4; o < 32; o <<= 1) {
@@ -998,7 +1013,14 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                 wmax[warp * G + 2 * tq] = mth[0];
                 wmax[warp * G + 2 * tq + 1] = mth[1];
             }
-            if (t == 0) misc[1] = tk;  // the pending pair's ticket (its atomic has long completed)
+            if (t == 0) {
+                misc[1] = tk;  // pair A's ticket (its atomic has long completed)
+                // pair B: the barrier at this chunk's start ordered every
+                // thread's partial stores before this release increment
+                if (pb_pair >= 0)
+                    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(tk) : "l"(p.ticket + pb_pair)
+                                 : "memory");
+            }
             named_bar_sync(1, 128);
             float Mh[2];
 #pragma unroll
@@ -1006,10 +1028,12 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                 const int hh = 2 * tq + u;
                 Mh[u] = fmaxf(fmaxf(wmax[hh], wmax[G + hh]), fmaxf(wmax[2 * G + hh], wmax[3 * G + hh]));
             }
-            if (pend_pair >= 0) {
-                if (misc[1] == pend_nch - 1) merge();
-                pend_pair = -1;
-            }
+            if (pend_pair >= 0 && misc[1] == pend_nch - 1) merge();
+            pend_pair = pb_pair;
+            pend_nch = pb_nch;
+            pend_s = pb_s;
+            pend_kvh = pb_kvh;
+            pb_pair = -1;
             // weights of this warp's own pages, in place (no other warp reads them)
             float lh[2] = {0.f, 0.f};
             for (int i = warp; i < k.np; i += 4) {
@@ -1032,9 +1056,12 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
             float dacc[8][4];
 #pragma unroll
             for (int v = 0; v < 8; ++v) dacc[v][0] = dacc[v][1] = dacc[v][2] = dacc[v][3] = 0.0f;
+            lap(9);
             for (int i = warp; i < k.np; i += 4) {
                 const int q2 = k.np + i, st = (ring + q2) % kFlatRing;
+                const long long w0 = prb ? clock64() : 0;
                 if (!bad && !mbar_wait(&full[st], ((ring + q2) / kFlatRing) & 1, p.err)) bad = true;
+                if (prb) atomicAdd(prb + 13, (unsigned long long)(clock64() - w0));
                 if (!bad && valid[st]) {
                     const float* Vt = tiles + st * TILE;
                     const float* Sp = S + (i * kPageTokens) * G;
@@ -1064,6 +1091,7 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                 if (lane == 0) mbar_arrive(&empty[st]);
             }
             ring += 2 * k.np;
+            lap(10);
             // this warp's O[head g][dims 8v + 2t, +1] = rows g + rows g + 8 -> red[warp][head][dim]
 #pragma unroll
             for (int v = 0; v < 8; ++v)
@@ -1091,134 +1119,6 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
             lsum = 0.0f;
             for (int q = 0; q < 4; ++q) lsum += red[4 * G * D + q * G + og];
             mchunk = fmaxf(fmaxf(wmax[og], wmax[G + og]), fmaxf(wmax[2 * G + og], wmax[3 * G + og]));
-            } else {
-            float2 qr[4][4][2];
-            {
-                const float* qb = qs + slot * G * D + 4 * hs * D + 16 * c4;
-#pragma unroll
-                for (int hh = 0; hh < 4; ++hh)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float4 a = *reinterpret_cast<const float4*>(qb + hh * D + 4 * ((e + j) & 3));
-                        qr[hh][e][0] = make_float2(a.x, a.y);
-                        qr[hh][e][1] = make_float2(a.z, a.w);
-                    }
-            }
-            // pass 1: scores of the chunk's pages
-            float mt = -INFINITY;
-            lap(14);
-            for (int i = 0; i < k.np; ++i, ++ring) {
-                const int st = ring % kFlatRing;
-                if (!bad && !mbar_wait(&full[st], (ring / kFlatRing) & 1, p.err)) bad = true;
-                                const float* Kr = tiles + st * TILE + j * D + 16 * c4;
-                float part[4] = {0.f, 0.f, 0.f, 0.f};
-                if (!bad && valid[st]) {
-                    float4 kv[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) kv[e] = *reinterpret_cast<const float4*>(Kr + 4 * ((e + j) & 3));
-#pragma unroll
-                    for (int hh = 0; hh < 4; ++hh) {
-                        float2 d = __fmul2_rn(qr[hh][0][0], make_float2(kv[0].x, kv[0].y));
-                        d = __ffma2_rn(qr[hh][0][1], make_float2(kv[0].z, kv[0].w), d);
-#pragma unroll
-                        for (int e = 1; e < 4; ++e) {
-                            d = __ffma2_rn(qr[hh][e][0], make_float2(kv[e].x, kv[e].y), d);
-                            d = __ffma2_rn(qr[hh][e][1], make_float2(kv[e].z, kv[e].w), d);
-                        }
-                        part[hh] = d.x + d.y;
-                    }
-                }
-                float r2[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const float mine = (c4 & 2) ? part[2 + u] : part[u];
-                    const float other = (c4 & 2) ? part[u] : part[2 + u];
-                    r2[u] = mine + __shfl_xor_sync(0xffffffffu, other, 2);
-                }
-                const float mine = (c4 & 1) ? r2[1] : r2[0];
-                const float other = (c4 & 1) ? r2[0] : r2[1];
-                const float dot = mine + __shfl_xor_sync(0xffffffffu, other, 1);
-                const int tok = (k.p0 + i) * kPageTokens + j;
-                const float sc = (tok < k.L) ? __fmul_rn(dot, scale2) : -INFINITY;
-                S[(i * kPageTokens + j) * G + h] = sc;
-                mt = fmaxf(mt, sc);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[st]);
-            }
-            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
-            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
-            if (lane < 8) wmax[warp * G + h] = mt;
-            if (t == 0) misc[1] = tk;  // the pending pair's ticket (its atomic has long completed)
-            named_bar_sync(1, 128);
-            const float Mx = fmaxf(fmaxf(wmax[h], wmax[G + h]), fmaxf(wmax[2 * G + h], wmax[3 * G + h]));
-            if (pend_pair >= 0) {  // (the query registers are dead here)
-                if (misc[1] == pend_nch - 1) merge();
-                pend_pair = -1;
-            }
-            float l_part = 0.0f;
-            for (int i = 0; i < k.np; ++i) {
-                float* sp = S + (i * kPageTokens + j) * G + h;
-                const float e = (*sp == -INFINITY) ? 0.0f : exp2f(*sp - Mx);
-                *sp = e;
-                l_part += e;
-            }
-            named_bar_sync(1, 128);
-            lap(10);
-            // pass 2: weighted V rows
-            float2 acc[G][2];
-#pragma unroll
-            for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = make_float2(0.0f, 0.0f);
-            for (int i = 0; i < k.np; ++i, ++ring) {
-                const int st = ring % kFlatRing;
-                if (!bad && !mbar_wait(&full[st], (ring / kFlatRing) & 1, p.err)) bad = true;
-                if (!bad && valid[st]) {
-                    const float* Vt = tiles + st * TILE;
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int jj = 2 * tg + u;
-                        const float4 v = *reinterpret_cast<const float4*>(Vt + jj * D + 4 * dc);
-                        const float4 pa = *reinterpret_cast<const float4*>(S + (i * kPageTokens + jj) * G);
-                        const float4 pb = *reinterpret_cast<const float4*>(S + (i * kPageTokens + jj) * G + 4);
-                        const float pw[G] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-                        const float2 v01 = make_float2(v.x, v.y), v23 = make_float2(v.z, v.w);
-#pragma unroll
-                        for (int g = 0; g < G; ++g) {
-                            const float2 w2 = make_float2(pw[g], pw[g]);
-                            acc[g][0] = __ffma2_rn(w2, v01, acc[g][0]);
-                            acc[g][1] = __ffma2_rn(w2, v23, acc[g][1]);
-                        }
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[st]);
-            }
-            lap(9);
-            if (prb) atomicAdd(prb + 15, 1ull);
-            // token pairs' accumulators (pairs 2w, 2w + 1 of warp w added by a
-            // shuffle, then the warps in order) and the tokens' sums
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float4 v = make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
-                v.x += __shfl_xor_sync(0xffffffffu, v.x, 16);
-                v.y += __shfl_xor_sync(0xffffffffu, v.y, 16);
-                v.z += __shfl_xor_sync(0xffffffffu, v.z, 16);
-                v.w += __shfl_xor_sync(0xffffffffu, v.w, 16);
-                if (lane < 16) *reinterpret_cast<float4*>(red + (warp * G + g) * D + 4 * dc) = v;
-            }
-            red[4 * G * D + j * G + h] = l_part;
-            named_bar_sync(1, 128);
-            a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float4 v = *reinterpret_cast<const float4*>(red + (q * G + og) * D + od);
-                a.x += v.x;
-                a.y += v.y;
-                a.z += v.z;
-                a.w += v.w;
-            }
-            lsum = 0.0f;
-            for (int q = 0; q < 16; ++q) lsum += red[4 * G * D + q * G + og];
-            mchunk = fmaxf(fmaxf(wmax[og], wmax[G + og]), fmaxf(wmax[2 * G + og], wmax[3 * G + og]));
             }
             lap(11);
             const int pair = k.s * Hkv + k.kvh;
@@ -1233,27 +1133,32 @@ __global__ void __launch_bounds__(kFlatThreads, 3) attn_flat_gqa8_kernel(const _
                     pp[8 * D + og] = mchunk;
                     pp[8 * D + 8 + og] = lsum;
                 }
-                // the barrier orders every thread's partial stores before thread
-                // 0's release increment of the ticket (cumulative); its result is
-                // read one chunk later, so the round trip overlaps the next chunk
-                named_bar_sync(1, 128);
-                if (t == 0)
-                    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(tk) : "l"(p.ticket + pair)
-                                 : "memory");
-                pend_pair = pair;
-                pend_nch = k.nch;
-                pend_s = k.s;
-                pend_kvh = k.kvh;
+                pb_pair = pair;
+                pb_nch = k.nch;
+                pb_s = k.s;
+                pb_kvh = k.kvh;
             }
             lap(12);
-            lap(13);
             slot ^= 1;
             k = kn;
         }
-        if (pend_pair >= 0) {
-            if (t == 0) misc[1] = tk;
+        if (pend_pair >= 0 || pb_pair >= 0) {  // drain both pending pairs
+            named_bar_sync(1, 128);  // B's partial stores before thread 0's increment
+            if (t == 0) {
+                misc[1] = tk;
+                if (pb_pair >= 0)
+                    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(misc[2]) : "l"(p.ticket + pb_pair)
+                                 : "memory");
+            }
             named_bar_sync(1, 128);
-            if (misc[1] == pend_nch - 1) merge();
+            if (pend_pair >= 0 && misc[1] == pend_nch - 1) merge();
+            if (pb_pair >= 0) {
+                pend_pair = pb_pair;
+                pend_nch = pb_nch;
+                pend_s = pb_s;
+                pend_kvh = pb_kvh;
+                if (misc[2] == pend_nch - 1) merge();
+            }
         }
     }
     __syncthreads();
@@ -1267,7 +1172,7 @@ size_t attn_flat_smem() {
 
 cudaError_t launch_attn_flat(const AttnParams& p, cudaStream_t stream, bool pdl, int grid) {
     const size_t smem = attn_flat_smem();
-    auto kfn = getenv("TB_ATTN_CUDACORE") ? attn_flat_gqa8_kernel<false> : attn_flat_gqa8_kernel<true>;
+    auto kfn = attn_flat_gqa8_kernel;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
@@ -1448,7 +1353,7 @@ int choose_nsplit(int M, int Hkv, int max_pages, int num_sms, bool balance_long)
     return ns < 1 ? 1 : ns;
 }
 
-int attn_flat_grid(int num_sms) { return 3 * num_sms; }
+int attn_flat_grid(int num_sms) { return kFlatCtas * num_sms; }
 
 bool attn_flat_supported(int H, int Hkv, int d, int M) {
     // from 64 (row, KV head) pairs on (measured: at 32 pairs the cluster
