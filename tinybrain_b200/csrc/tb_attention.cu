@@ -652,7 +652,8 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
 // output directly.
 // ---------------------------------------------------------------------------
 constexpr int kFlatCtas = 4;        // CTAs per SM
-constexpr int kFlatRing = kFlatCtas == 4 ? 8 : kFlatCtas == 3 ? 12 : 20;  // 4 KB tiles in flight per CTA
+constexpr int kFlatRing = kFlatCtas == 4 ? 10 : kFlatCtas == 3 ? 12 : 20;
+constexpr int kFlatSRed = 4 * 8 * 64 + 16 * 8;  // floats of the scores / reduction region  // 4 KB tiles in flight per CTA
 constexpr int kFlatMaxPages = 16;   // pages per chunk at most
 constexpr int kFlatMaxRows = 64;    // sequences (rows) per launch
 constexpr int kFlatThreads = (4 + 1) * 32;
@@ -662,12 +663,9 @@ struct FlatChunk {
     bool tail;
 };
 
-// tf32 of x, rounded to nearest (ties away), as the 32-bit operand pattern.
-__device__ __forceinline__ uint32_t tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
-}
+// High tf32 part of x (the top 19 bits, low 13 cleared) as the 32-bit
+// operand pattern: one logic op instead of a conversion; x - hi is exact.
+__device__ __forceinline__ uint32_t tf32_hi(float x) { return __float_as_uint(x) & 0xffffe000u; }
 // d (16 x 8, fp32) += a (16 x 8, tf32, row major) x b (8 x 8, tf32, column major), one warp.
 __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
     asm volatile(
@@ -693,8 +691,13 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
     float* wmax = reinterpret_cast<float*>(misc + 4);                    // [4 warps][G]
     float* tiles = reinterpret_cast<float*>(smem + kAttnHead + 2048);    // [ring][TILE]
     float* S = tiles + kFlatRing * TILE;                                 // [kFlatMaxPages][16][G]
-    float* red = S + kFlatMaxPages * kPageTokens * G;                    // [4 warps][G][D] + l [16][G]
-    float* qs = red + 4 * G * D + 16 * G;                                // [2][G][D] query slots
+    // red [4 warps][G][D] + l [16][G] shares its storage with S: it is
+    // written once every warp has finished pass 2 (S is dead until the next
+    // chunk's pass 1, which follows a later barrier)
+    float* red = S;
+    static_assert(kFlatMaxPages * kPageTokens * G <= kFlatSRed, "S fits the shared region");
+    static_assert(4 * G * D + 16 * G <= kFlatSRed, "red fits the shared region");
+    float* qs = S + kFlatSRed;                                           // [2][G][D] query slots
     static_assert((3 * kFlatMaxRows + 2 + 4 + 4 * G) * 4 <= 2048, "row tables");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -946,7 +949,7 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                     const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const uint32_t h32 = tf32_rna(e[u]);
+                        const uint32_t h32 = tf32_hi(e[u]);
                         qh[b][u >> 1][u & 1] = h32;
                         ql[b][u >> 1][u & 1] = __float_as_uint(e[u] - __uint_as_float(h32));
                     }
@@ -977,7 +980,7 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                             const float av[4] = {e0[2 * sstep], e1[2 * sstep], e0[2 * sstep + 1], e1[2 * sstep + 1]};
 #pragma unroll
                             for (int u = 0; u < 4; ++u) {
-                                ah[u] = tf32_rna(av[u]);
+                                ah[u] = tf32_hi(av[u]);
                                 al[u] = __float_as_uint(av[u] - __uint_as_float(ah[u]));
                             }
                             mma_tf32(cacc[b & 1], al, qh[b][sstep]);
@@ -1069,8 +1072,8 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                     for (int sstep = 0; sstep < 2; ++sstep) {
                         const float pa = Sp[(8 * sstep + tq) * G + gq], pb = Sp[(8 * sstep + tq + 4) * G + gq];
                         uint32_t a[4];
-                        a[0] = tf32_rna(pa);
-                        a[2] = tf32_rna(pb);
+                        a[0] = tf32_hi(pa);
+                        a[2] = tf32_hi(pb);
                         a[1] = __float_as_uint(pa - __uint_as_float(a[0]));
                         a[3] = __float_as_uint(pb - __uint_as_float(a[2]));
 #pragma unroll
@@ -1078,8 +1081,8 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                             const float b0 = Vt[(8 * sstep + tq) * D + 8 * v + gq];
                             const float b1 = Vt[(8 * sstep + tq + 4) * D + 8 * v + gq];
                             uint32_t bh[2], bl[2];
-                            bh[0] = tf32_rna(b0);
-                            bh[1] = tf32_rna(b1);
+                            bh[0] = tf32_hi(b0);
+                            bh[1] = tf32_hi(b1);
                             bl[0] = __float_as_uint(b0 - __uint_as_float(bh[0]));
                             bl[1] = __float_as_uint(b1 - __uint_as_float(bh[1]));
                             mma_tf32(dacc[v], a, bh);
@@ -1092,6 +1095,7 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
             }
             ring += 2 * k.np;
             lap(10);
+            named_bar_sync(1, 128);  // every warp is past pass 2: S may be overwritten by red
             // this warp's O[head g][dims 8v + 2t, +1] = rows g + rows g + 8 -> red[warp][head][dim]
 #pragma unroll
             for (int v = 0; v < 8; ++v)
@@ -1166,8 +1170,8 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
 }
 
 size_t attn_flat_smem() {
-    return kAttnHead + 2048 + (size_t)kFlatRing * kPageTokens * 64 * 4 + (size_t)kFlatMaxPages * kPageTokens * 8 * 4 +
-           (size_t)(4 * 8 * 64 + 16 * 8) * 4 + (size_t)2 * 8 * 64 * 4;
+    return kAttnHead + 2048 + (size_t)kFlatRing * kPageTokens * 64 * 4 + (size_t)kFlatSRed * 4 +
+           (size_t)2 * 8 * 64 * 4;
 }
 
 cudaError_t launch_attn_flat(const AttnParams& p, cudaStream_t stream, bool pdl, int grid) {
