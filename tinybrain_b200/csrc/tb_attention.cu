@@ -678,10 +678,18 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
 __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel(const __grid_constant__ AttnParams p) {
     constexpr int G = 8, D = 64;
     constexpr int TILE = kPageTokens * D;
-    static_assert(kFlatRing * 20 <= kAttnHead, "ring barriers exceed the header");
+    static_assert(kFlatRing * 28 <= kAttnHead, "ring barriers exceed the header");
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kFlatRing;
+    // Tile j lands in data slot j % R (R = kFlatRing) and completes full
+    // barrier j % 2R.  Two full barriers per slot: a consumer warp may start
+    // waiting on tile j while tile j - R (same slot) is still in flight
+    // (chunks hold more pages than the ring, and the 4 warps take every 4th
+    // page), and a parity wait on a single barrier would then mistake the
+    // earlier tile's completed phase for tile j.  Tile j - 2R has always
+    // completed by then (the waiting warp consumed tile j - 4, whose
+    // production needed tile j - 4 - R released), so 2R barriers decide it.
+    uint64_t* empty = full + 2 * kFlatRing;
     int* valid = reinterpret_cast<int*>(empty + kFlatRing);              // [ring]
     int* nchk = reinterpret_cast<int*>(smem + kAttnHead);                // [rows] chunks of each row
     int* pre_nt = nchk + kFlatMaxRows;                                   // [rows + 1] prefix of non-final chunks
@@ -705,6 +713,7 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
     if (threadIdx.x == 0) {
         for (int i = 0; i < kFlatRing; ++i) {
             mbar_init(&full[i], 1);
+            mbar_init(&full[kFlatRing + i], 1);
             mbar_init(&empty[i], 1);  // one consumer warp reads a tile
         }
         fence_barrier_init();
@@ -815,12 +824,12 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                         valid[st] = 1;
                         const size_t base =
                             ((((size_t)page * p.num_layers + p.layer) * 2 + kv) * p.Hkv + k.kvh) * (size_t)TILE;
-                        mbar_arrive_expect_tx(&full[st], TILE * 4u);
-                        bulk_g2s(tiles + st * TILE, p.kv_pool + base, TILE * 4u, &full[st]);
+                        mbar_arrive_expect_tx(&full[ring % (2 * kFlatRing)], TILE * 4u);
+                        bulk_g2s(tiles + st * TILE, p.kv_pool + base, TILE * 4u, &full[ring % (2 * kFlatRing)]);
                     }
                 } else if (lane == 0) {
                     valid[st] = 0;  // evicted page: rows read as zeros
-                    mbar_arrive(&full[st]);
+                    mbar_arrive(&full[ring % (2 * kFlatRing)]);
                 }
             }
         }
@@ -911,7 +920,7 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                 const FlatChunk kk = chunk(c);
                 for (int i = 0; i < 2 * kk.np; ++i, ++ring) {
                     const int st = ring % kFlatRing;
-                    if (!bad && !mbar_wait(&full[st], (ring / kFlatRing) & 1, p.err)) bad = true;
+                    if (!bad && !mbar_wait(&full[ring % (2 * kFlatRing)], (ring / (2 * kFlatRing)) & 1, p.err)) bad = true;
                     __syncwarp();
                     if (lane == 0 && warp == 0) mbar_arrive(&empty[st]);
                 }
@@ -959,7 +968,8 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
             for (int i = warp; i < k.np; i += 4) {
                 const int st = (ring + i) % kFlatRing;
                 const long long w0 = prb ? clock64() : 0;
-                if (!bad && !mbar_wait(&full[st], ((ring + i) / kFlatRing) & 1, p.err)) bad = true;
+                if (!bad && !mbar_wait(&full[(ring + i) % (2 * kFlatRing)], ((ring + i) / (2 * kFlatRing)) & 1, p.err))
+                    bad = true;
                 if (prb) atomicAdd(prb + 13, (unsigned long long)(clock64() - w0));
                 float c[4] = {0.f, 0.f, 0.f, 0.f};
                 // two independent accumulators (block parity): dependent
@@ -1063,7 +1073,8 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
             for (int i = warp; i < k.np; i += 4) {
                 const int q2 = k.np + i, st = (ring + q2) % kFlatRing;
                 const long long w0 = prb ? clock64() : 0;
-                if (!bad && !mbar_wait(&full[st], ((ring + q2) / kFlatRing) & 1, p.err)) bad = true;
+                if (!bad && !mbar_wait(&full[(ring + q2) % (2 * kFlatRing)], ((ring + q2) / (2 * kFlatRing)) & 1, p.err))
+                    bad = true;
                 if (prb) atomicAdd(prb + 13, (unsigned long long)(clock64() - w0));
                 if (!bad && valid[st]) {
                     const float* Vt = tiles + st * TILE;
