@@ -24,6 +24,9 @@
 #include "tb_common.cuh"
 #include "tb_kernels.h"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cstdlib>
 #include <mutex>
 
@@ -654,6 +657,8 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
 constexpr int kFlatCtas = 4;        // CTAs per SM
 constexpr int kFlatRing = kFlatCtas == 4 ? 10 : kFlatCtas == 3 ? 12 : 20;
 constexpr int kFlatSRed = 4 * 8 * 64 + 16 * 8;  // floats of the scores / reduction region  // 4 KB tiles in flight per CTA
+// Ring tiles start on a 1 KB boundary (128-byte swizzle atoms of the tensor loads).
+constexpr int kFlatTilesOff = (kAttnHead + 2048 + 1023) / 1024 * 1024;
 constexpr int kFlatMaxPages = 16;   // pages per chunk at most
 constexpr int kFlatMaxRows = 64;    // sequences (rows) per launch
 constexpr int kFlatThreads = (4 + 1) * 32;
@@ -666,6 +671,20 @@ struct FlatChunk {
 // High tf32 part of x (the top 19 bits, low 13 cleared) as the 32-bit
 // operand pattern: one logic op instead of a conversion; x - hi is exact.
 __device__ __forceinline__ uint32_t tf32_hi(float x) { return __float_as_uint(x) & 0xffffe000u; }
+// One 2-D tile of a tensor map -> shared memory (TMA), completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+// Float offset of (token t, dimension dd) in a ring tile: two 16 x 32 halves
+// (dimensions 0-31, 32-63), each row's 16-byte chunks swizzled by the row
+// (chunk ^ (t % 8)), as the 128-byte-swizzle tensor load writes them.
+__device__ __forceinline__ int flat_tile_off(int t, int dd) {
+    return (dd >> 5) * (kPageTokens * 32) + t * 32 + ((((dd & 31) >> 2) ^ (t & 7)) << 2) + (dd & 3);
+}
 // d (16 x 8, fp32) += a (16 x 8, tf32, row major) x b (8 x 8, tf32, column major), one warp.
 __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
     asm volatile(
@@ -675,7 +694,8 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-__global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel(const __grid_constant__ AttnParams p,
+                                                                                const __grid_constant__ CUtensorMap kvmap) {
     constexpr int G = 8, D = 64;
     constexpr int TILE = kPageTokens * D;
     static_assert(kFlatRing * 28 <= kAttnHead, "ring barriers exceed the header");
@@ -697,7 +717,7 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
     int* lens = pre_t + kFlatMaxRows + 1;                                // [rows] context lengths
     int* misc = lens + kFlatMaxRows;                                     // [4]
     float* wmax = reinterpret_cast<float*>(misc + 4);                    // [4 warps][G]
-    float* tiles = reinterpret_cast<float*>(smem + kAttnHead + 2048);    // [ring][TILE]
+    float* tiles = reinterpret_cast<float*>(smem + kFlatTilesOff);       // [ring][TILE], swizzled halves
     float* S = tiles + kFlatRing * TILE;                                 // [kFlatMaxPages][16][G]
     // red [4 warps][G][D] + l [16][G] shares its storage with S: it is
     // written once every warp has finished pass 2 (S is dead until the next
@@ -708,6 +728,10 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
     float* qs = S + kFlatSRed;                                           // [2][G][D] query slots
     static_assert((3 * kFlatMaxRows + 2 + 4 + 4 * G) * 4 <= 2048, "row tables");
 
+    if (smem_u32(tiles) & 1023u) {  // the swizzled tensor loads need 1 KB-aligned tiles: do nothing
+        if (threadIdx.x == 0) record_error(p.err, kDevBadSmem);
+        return;
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int M = p.M, Hkv = p.Hkv, CP = p.chunk_pages;
     if (threadIdx.x == 0) {
@@ -822,10 +846,13 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                 if (page >= 0) {
                     if (lane == 0) {
                         valid[st] = 1;
-                        const size_t base =
-                            ((((size_t)page * p.num_layers + p.layer) * 2 + kv) * p.Hkv + k.kvh) * (size_t)TILE;
-                        mbar_arrive_expect_tx(&full[ring % (2 * kFlatRing)], TILE * 4u);
-                        bulk_g2s(tiles + st * TILE, p.kv_pool + base, TILE * 4u, &full[ring % (2 * kFlatRing)]);
+                        // first pool row of the tile (a row = 64 floats)
+                        const int row0 =
+                            (int)((((size_t)page * p.num_layers + p.layer) * 2 + kv) * p.Hkv + k.kvh) * kPageTokens;
+                        uint64_t* fb = &full[ring % (2 * kFlatRing)];
+                        mbar_arrive_expect_tx(fb, TILE * 4u);
+                        tma_load_2d(tiles + st * TILE, &kvmap, 0, row0, fb);
+                        tma_load_2d(tiles + st * TILE + kPageTokens * 32, &kvmap, 32, row0, fb);
                     }
                 } else if (lane == 0) {
                     valid[st] = 0;  // evicted page: rows read as zeros
@@ -943,9 +970,12 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
             // hi*hi + hi*lo + lo*hi ~ fp32 accuracy).  Warp w takes the
             // chunk's pages i = w, w + 4, ... in both passes.
             // lane = (g = lane / 4, t = lane % 4).  Scores: A = K tile rows
-            // (tokens) g / g + 8, B = query^T (head g); dims of k-step (b, s):
-            // k = t -> 16b + 4t + 2s, k = t + 4 -> 16b + 4t + 2s + 1, so each
-            // thread loads 4 consecutive dims of a row at once.
+            // (tokens) g / g + 8, B = query^T (head g); block b covers 16-byte
+            // chunk 2t + (b & 1) of dimension half b / 2 for lane t, and k-step
+            // s uses its dims 2s (k = t) and 2s + 1 (k = t + 4): each thread
+            // loads 4 consecutive dims of a row at once, and with the tile's
+            // chunk swizzle (chunk ^ row % 8) the 8 lanes of a quarter warp
+            // (two rows, 4 chunks of equal parity) hit 8 different chunks.
             lap(14);
             if (prb) atomicAdd(prb + 15, 1ull);
             const int gq = lane >> 2, tq = lane & 3;
@@ -954,7 +984,7 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                 const float* qg = qs + slot * G * D + gq * D;
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
-                    const float4 v = *reinterpret_cast<const float4*>(qg + 16 * b + 4 * tq);
+                    const float4 v = *reinterpret_cast<const float4*>(qg + 32 * (b >> 1) + 4 * (2 * tq + (b & 1)));
                     const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
@@ -981,8 +1011,9 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                     const float* Kt = tiles + st * TILE;
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {
-                        const float4 r0 = *reinterpret_cast<const float4*>(Kt + gq * D + 16 * b + 4 * tq);
-                        const float4 r1 = *reinterpret_cast<const float4*>(Kt + (gq + 8) * D + 16 * b + 4 * tq);
+                        const int dd = 32 * (b >> 1) + 4 * (2 * tq + (b & 1));
+                        const float4 r0 = *reinterpret_cast<const float4*>(Kt + flat_tile_off(gq, dd));
+                        const float4 r1 = *reinterpret_cast<const float4*>(Kt + flat_tile_off(gq + 8, dd));
                         const float e0[4] = {r0.x, r0.y, r0.z, r0.w}, e1[4] = {r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
                         for (int sstep = 0; sstep < 2; ++sstep) {
@@ -1064,7 +1095,9 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
             }
             __syncwarp();
             // pass 2: O^(rows) = A (rows 0-7: P hi of head g, rows 8-15: P lo) x V;
-            // k-step s: k = t -> token 8s + t, k = t + 4 -> token 8s + t + 4;
+            // k-step s: k = t -> token 8s + 2t, k = t + 4 -> token 8s + 2t + 1
+            // (row % 8 of the 4 t lanes then differs in its upper two bits, so
+            // with the chunk swizzle a warp's 32 fragment loads hit 32 banks);
             // n-block v: dims 8v .. 8v + 7 (column g)
             float dacc[8][4];
 #pragma unroll
@@ -1081,7 +1114,7 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                     const float* Sp = S + (i * kPageTokens) * G;
 #pragma unroll
                     for (int sstep = 0; sstep < 2; ++sstep) {
-                        const float pa = Sp[(8 * sstep + tq) * G + gq], pb = Sp[(8 * sstep + tq + 4) * G + gq];
+                        const float pa = Sp[(8 * sstep + 2 * tq) * G + gq], pb = Sp[(8 * sstep + 2 * tq + 1) * G + gq];
                         uint32_t a[4];
                         a[0] = tf32_hi(pa);
                         a[2] = tf32_hi(pb);
@@ -1089,8 +1122,8 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                         a[3] = __float_as_uint(pb - __uint_as_float(a[2]));
 #pragma unroll
                         for (int v = 0; v < 8; ++v) {
-                            const float b0 = Vt[(8 * sstep + tq) * D + 8 * v + gq];
-                            const float b1 = Vt[(8 * sstep + tq + 4) * D + 8 * v + gq];
+                            const float b0 = Vt[flat_tile_off(8 * sstep + 2 * tq, 8 * v + gq)];
+                            const float b1 = Vt[flat_tile_off(8 * sstep + 2 * tq + 1, 8 * v + gq)];
                             uint32_t bh[2], bl[2];
                             bh[0] = tf32_hi(b0);
                             bh[1] = tf32_hi(b1);
@@ -1181,12 +1214,40 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
 }
 
 size_t attn_flat_smem() {
-    return kAttnHead + 2048 + (size_t)kFlatRing * kPageTokens * 64 * 4 + (size_t)kFlatSRed * 4 +
-           (size_t)2 * 8 * 64 * 4;
+    return kFlatTilesOff + (size_t)kFlatRing * kPageTokens * 64 * 4 + (size_t)kFlatSRed * 4 + (size_t)2 * 8 * 64 * 4;
+}
+
+// The driver's tensor-map encoder, fetched once through the runtime (no link
+// against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
 }
 
 cudaError_t launch_attn_flat(const AttnParams& p, cudaStream_t stream, bool pdl, int grid) {
     const size_t smem = attn_flat_smem();
+    // The KV pool as a 2-D fp32 tensor [rows][64] (a row = one token of one
+    // (page, layer, K|V, KV head) tile); a box is 16 rows x 32 floats (one
+    // half tile, 2 KB), landing 128-byte swizzled.
+    auto encode = tensor_map_encoder();
+    if (!encode || p.kv_floats < 64) return cudaErrorInvalidValue;
+    CUtensorMap kvmap;
+    const cuuint64_t dims[2] = {64, (cuuint64_t)(p.kv_floats / 64)};
+    const cuuint64_t strides[1] = {64 * sizeof(float)};
+    const cuuint32_t box[2] = {32, kPageTokens};
+    const cuuint32_t estr[2] = {1, 1};
+    if (encode(&kvmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p.kv_pool), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
     auto kfn = attn_flat_gqa8_kernel;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -1202,7 +1263,7 @@ cudaError_t launch_attn_flat(const AttnParams& p, cudaStream_t stream, bool pdl,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kfn, p);
+    return cudaLaunchKernelEx(&cfg, kfn, p, kvmap);
 }
 
 size_t attn_gqa8_smem() {
@@ -1387,7 +1448,7 @@ int attn_flat_chunk_pages(int M, int Hkv, int max_pages, int num_sms) {
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
     const int G = p.H / p.Hkv;
     if (p.H % p.Hkv != 0) return cudaErrorInvalidValue;
-    if (p.part && attn_flat_supported(p.H, p.Hkv, p.d, p.M) && p.chunk_pages >= 1 &&
+    if (p.part && p.kv_floats >= 64 && attn_flat_supported(p.H, p.Hkv, p.d, p.M) && p.chunk_pages >= 1 &&
         p.chunk_pages <= kFlatMaxPages && !getenv("TB_ATTN_GENERIC")) {
         int sms = 148;
         int dev = 0;

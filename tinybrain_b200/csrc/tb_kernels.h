@@ -15,6 +15,7 @@ enum DeviceError : int {
     kDevWaitTimeout = 1,      // an mbarrier wait exceeded its time limit
     kDevBadPage = 2,          // KV append found no page mapped for a position
     kDevBadToken = 3,         // token id outside [0, vocab)
+    kDevBadSmem = 4,          // a shared-memory buffer is not aligned as its layout requires
 };
 
 // ----------------------------------------------------------------------------
@@ -248,6 +249,9 @@ struct AttnParams {
     int chunk_pages;
     int maxch;
     int probe;  // diagnostics (TB_ATTN_PROBE): consumers only release the pages
+    // floats in kv_pool (the persistent variant loads its tiles through a
+    // tensor map over the pool, which needs the extent)
+    long long kv_floats;
 };
 constexpr int kAttnPartFloats = 8 * 64 + 16;  // acc [8 heads][64], m [8], l [8]
 // Grid of the persistent chunked attention launch and its chunk size.

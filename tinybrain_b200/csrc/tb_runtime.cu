@@ -454,6 +454,7 @@ extern "C" tb_status tb_context_check_device(tb_context* ctx) {
     if (v == kDevWaitTimeout) return fail(TB_ERR_DEVICE_TIMEOUT, "a device-side wait exceeded its time limit");
     if (v == kDevBadPage) return fail(TB_ERR_STATE, "KV append found no page mapped for the position");
     if (v == kDevBadToken) return fail(TB_ERR_STATE, "token id outside the vocabulary");
+    if (v == kDevBadSmem) return fail(TB_ERR_STATE, "a kernel's shared-memory layout was misaligned (no work done)");
     return fail(TB_ERR_STATE, "device error code %d", v);
 }
 
@@ -1373,6 +1374,7 @@ static tb_status build_plan_into(tb_runner* r, const PlanIO& io, std::vector<Lau
                 a.ticket = r->attn_ticket.as<int>();
                 a.chunk_pages = attn_flat_chunk_pages(a.M, a.Hkv, r->ptab_stride, r->ctx->num_sms);
                 a.maxch = (r->ptab_stride + a.chunk_pages - 1) / a.chunk_pages;
+                a.kv_floats = (long long)(r->kv.bytes / 4);
             }
             ln.bytes = 0;  // depends on the context length; accounted by the caller
             plan.push_back(ln);
