@@ -171,7 +171,8 @@ tb_status tb_attention_decode(tb_context *ctx, const float *q_host, const float 
  *   kv_pool_dev  [pages][num_layers][2 (K,V)][Hkv][16 tokens][d] fp32
  *   page_table_dev [batch][ptab_stride] int32 (logical page -> pool page, -1 = evicted)
  *   seq_lens_dev [batch] int32 context lengths, q_dev [batch][H*d], out_dev [batch][H*d].
- * Scratch for the split-K partials is owned by the context. */
+ * The splits of a (sequence, KV head) combine inside their thread-block
+ * cluster through distributed shared memory: no scratch memory is used. */
 tb_status tb_paged_attention_dev(tb_context *ctx, const float *q_dev, int32_t batch, const float *kv_pool_dev,
                                  const int32_t *page_table_dev, int32_t ptab_stride, const int32_t *seq_lens_dev,
                                  int32_t max_len, int32_t layer, int32_t num_layers, int32_t num_heads,
