@@ -656,7 +656,7 @@ __global__ void __launch_bounds__(kGqaThreads, 3) attn_gqa8_d64_kernel(const __g
 // ---------------------------------------------------------------------------
 constexpr int kFlatCtas = 4;        // CTAs per SM
 constexpr int kFlatRing = kFlatCtas == 4 ? 10 : kFlatCtas == 3 ? 12 : 20;
-constexpr int kFlatSRed = 4 * 8 * 64 + 16 * 8;  // floats of the scores / reduction region  // 4 KB tiles in flight per CTA
+constexpr int kFlatSRed = 4 * 8 * 64 + 16 * 8;  // floats of the region shared by the scores and the reduction
 // Ring tiles start on a 1 KB boundary (128-byte swizzle atoms of the tensor loads).
 constexpr int kFlatTilesOff = (kAttnHead + 2048 + 1023) / 1024 * 1024;
 constexpr int kFlatMaxPages = 16;   // pages per chunk at most
