@@ -817,6 +817,8 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         const int nloc = pairs ? 2 * nr : nr;  // tile rows of this rank
         const int SR = nloc + 1;
         float* stg = reinterpret_cast<float*>(stage_base);
+        (void)SR;  // (unused by the batch-minor item order)
+        (void)stg;
         auto loc_row = [&](int li) -> int {  // tile row of local index li
             if (EPI == kEpiQkv) return 2 * ob + li;
             if (EPI == kEpiSiluMul) return li < nr ? ob + li : HALF + ob + (li - nr);
