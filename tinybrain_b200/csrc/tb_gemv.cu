@@ -749,7 +749,11 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         tmem_dealloc(*tmem_slot, kTmemCols);
     }
 
-    if (warp < kGemvConsumerWarps) {
+    // Epilogue threads: the 8 consumer warps, and in the wide variant also the
+    // producer and tensor-core issue warps, idle once the products are done.
+    constexpr int ET = WIDE ? (kGemvConsumerWarps + 2) * 32 : 256;
+    static_assert(!WIDE || ET == gemv_threads(PREC, MB), "wide epilogue uses every warp");
+    if (warp < ET / 32) {
         const int ctid = threadIdx.x;
         if (ctid == 0) trace_max(p.trace, 5);
         unsigned long long best_mine = 0ull;
@@ -788,17 +792,17 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             return v;
         };
         const unsigned int ar_tag_push = (EPI == kEpiPush) ? *p.ar_step + 1u : 0u;
-        // Item order.  Up to 8 batch rows per CTA: it = ctid + 256 j maps to
-        // batch row it % MB = ctid % MB (MB divides 256), one argmax key per
+        // Item order.  Up to 8 batch rows per CTA: it = ctid + ET j maps to
+        // batch row it % MB = ctid % MB (MB divides ET), one argmax key per
         // thread.  From 16 rows on ("row-major" items): batch row it / nr,
         // tile row it % nr (nr = rows of this rank), so a warp's stores go to
         // consecutive outputs of one batch row; the argmax is reduced per
         // item over the lanes that share a batch row.
-        static_assert(256 % MB == 0, "batch rows per CTA divide the consumer threads");
+        static_assert(ET % MB == 0, "batch rows per CTA divide the epilogue threads");
         const int nr = oe - ob;
-        // (batch row, tile-row offset) of item it = ctid + 256 j, stepped by
-        // 256 items at a time without divisions
-        const int step_m = RMAJ ? 256 / nr : 0, step_o = RMAJ ? 256 % nr : 256 / MB;
+        // (batch row, tile-row offset) of item it = ctid + ET j, stepped by
+        // ET items at a time without divisions
+        const int step_m = RMAJ ? ET / nr : 0, step_o = RMAJ ? ET % nr : ET / MB;
         auto item_next = [&](int& m, int& o) {
             o += step_o;
             m += step_m;
@@ -829,12 +833,12 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             // (a plain loop: unrolling it was measured slower, instruction
             // fetch of a large straight-line body)
 #pragma unroll 1
-            for (int it = ctid; it < nloc * MB; it += 256) {
+            for (int it = ctid; it < nloc * MB; it += ET) {
                 const int m = it % MB, li = it / MB;
                 const int row = loc_row(li);
                 stg[m * SR + li] = finish(rb * RB + row, rowsum(row, m));
             }
-            named_bar_sync(1, 256);
+            named_bar_sync(1, ET);
             if (PREC == 8 && ctid == 0) trace_max(p.trace, 8);
         }
         // finished value of tile row `row`, batch row m
@@ -853,12 +857,12 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         // Two phases per chunk of JC items, so that every global load of a
         // chunk is in flight together: (1) reduce, scale, issue the loads the
         // stores need (RoPE table, the residual); (2) finish and store.
-        constexpr int JMAX = (RB * MB + 255) / 256;
+        constexpr int JMAX = (RB * MB + ET - 1) / ET;
         constexpr int JC = JMAX < 4 ? JMAX : 4;
         int cm = RMAJ ? ctid / nr : ctid % MB, co = RMAJ ? ctid % nr : ctid / MB;
 #pragma unroll 1
         for (int jb = 0; jb < JMAX; jb += JC) {
-        if ((ctid & ~31) + 256 * jb >= nitems) break;  // warp-uniform: the argmax below uses whole warps
+        if ((ctid & ~31) + ET * jb >= nitems) break;  // warp-uniform: the argmax below uses whole warps
         float va[JC], vb[JC], old[JC];
         float2 cs[JC];
         unsigned long long keyj[JC];
@@ -872,7 +876,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             mj[j] = cm;
             oj[j] = ob + co;
             item_next(cm, co);
-            const int it = ctid + 256 * (jb + j);
+            const int it = ctid + ET * (jb + j);
             if (it >= nitems) continue;
             const int m = mj[j];
             const int o = oj[j];
@@ -900,7 +904,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         }
 #pragma unroll
         for (int j = 0; j < JC; ++j) {
-            const int it = ctid + 256 * (jb + j);
+            const int it = ctid + ET * (jb + j);
             if (it >= nitems) continue;
             const int m = mj[j];
             const int o = oj[j];
@@ -1022,17 +1026,17 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
                 const int m = ctid % MB;
                 if (lane < MB && b != 0ull && m < Mloc) atomicMax(&p.seq[m0 + m].best, b);
             }
-            named_bar_sync(1, 256);
+            named_bar_sync(1, ET);
             if (ctid == 0) {
                 __threadfence();
                 const unsigned int t = atomicAdd(p.ticket, 1u);
                 misc[0] = __int_as_float(t == gridDim.x * gridDim.y - 1 ? 1 : 0);
             }
-            named_bar_sync(1, 256);
+            named_bar_sync(1, ET);
             if (__float_as_int(misc[0]) == 1) {
                 // Last CTA: finish the step for every sequence (ModelRunner.swift:251-292).
                 __threadfence();
-                for (int m = ctid; m < p.M; m += 256) {
+                for (int m = ctid; m < p.M; m += ET) {
                     SeqState& sq = p.seq[m];
                     if (!sq.active) {
                         sq.best = 0ull;  // paused slot: drop this step's argmax
