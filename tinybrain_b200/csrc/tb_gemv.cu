@@ -858,7 +858,7 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
         // chunk is in flight together: (1) reduce, scale, issue the loads the
         // stores need (RoPE table, the residual); (2) finish and store.
         constexpr int JMAX = (RB * MB + ET - 1) / ET;
-        constexpr int JC = JMAX < 4 ? JMAX : 4;
+        constexpr int JC = JMAX < 2 ? JMAX : 2;
         int cm = RMAJ ? ctid / nr : ctid % MB, co = RMAJ ? ctid % nr : ctid / MB;
 #pragma unroll 1
         for (int jb = 0; jb < JMAX; jb += JC) {
