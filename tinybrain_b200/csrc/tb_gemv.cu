@@ -353,12 +353,18 @@ __global__ void __launch_bounds__(gemv_threads(PREC, MB), 2) gemv_kernel(const _
             }
             return p.src + (size_t)(m0 + m) * p.ld_src;
         };
-        // Embedding prologue: CTA 0 materialises the residual stream h.
-        if (embed && blockIdx.x == 0) {
-            for (int m = 0; m < Mloc; ++m) {
-                const float* sr = srcrow(m);
-                for (int k = ctid; k < L.K; k += 256) p.resid[(size_t)(m0 + m) * p.ld_src + k] = sr[k];
-            }
+        // Embedding prologue: the residual stream h of the CTA's batch rows is
+        // materialised by all CTAs of its grid row, each a slice of K (one CTA
+        // copying 64 rows alone took ~100 us).
+        if (embed) {
+            const int k0 = (int)((long long)blockIdx.x * L.K / gridDim.x);
+            const int k1 = (int)((long long)(blockIdx.x + 1) * L.K / gridDim.x);
+            const int w = k1 - k0;
+            if (w > 0)
+                for (int e = ctid; e < Mloc * w; e += 256) {  // independent elements: loads overlap
+                    const int m = e / w, k = k0 + (e - m * w);
+                    p.resid[(size_t)(m0 + m) * p.ld_src + k] = srcrow(m)[k];
+                }
         }
         // rows are read as float4 when K and the row stride allow it
         const bool v4 = (L.K % 4 == 0) && (embed || p.ld_src % 4 == 0);
