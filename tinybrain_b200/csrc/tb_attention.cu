@@ -847,8 +847,8 @@ __global__ void __launch_bounds__(kFlatThreads, kFlatCtas) attn_flat_gqa8_kernel
                     if (lane == 0) {
                         valid[st] = 1;
                         // first pool row of the tile (a row = 64 floats)
-                        const int row0 =
-                            (int)((((size_t)page * p.num_layers + p.layer) * 2 + kv) * p.Hkv + k.kvh) * kPageTokens;
+                        const int row0 = (int)(((((size_t)page * p.num_layers + p.layer) * 2 + kv) * p.Hkv + k.kvh) *
+                                               (size_t)kPageTokens);
                         uint64_t* fb = &full[ring % (2 * kFlatRing)];
                         mbar_arrive_expect_tx(fb, TILE * 4u);
                         tma_load_2d(tiles + st * TILE, &kvmap, 0, row0, fb);
@@ -1448,7 +1448,8 @@ int attn_flat_chunk_pages(int M, int Hkv, int max_pages, int num_sms) {
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
     const int G = p.H / p.Hkv;
     if (p.H % p.Hkv != 0) return cudaErrorInvalidValue;
-    if (p.part && p.kv_floats >= 64 && attn_flat_supported(p.H, p.Hkv, p.d, p.M) && p.chunk_pages >= 1 &&
+    if (p.part && p.kv_floats >= 64 && p.kv_floats / 64 < (1ll << 31) && tensor_map_encoder() != nullptr &&
+        attn_flat_supported(p.H, p.Hkv, p.d, p.M) && p.chunk_pages >= 1 &&
         p.chunk_pages <= kFlatMaxPages && !getenv("TB_ATTN_GENERIC")) {
         int sms = 148;
         int dev = 0;
